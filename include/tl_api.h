@@ -1,0 +1,260 @@
+/*
+ * tl_api.h -- C ABI of the B200 TinyLlama INT8 engine.
+ *
+ * Plain C: integer status codes, host/device pointers and sizes; no C++ or
+ * torch types. Two layers of entry points:
+ *
+ *  1. Runtime contract (host buffers). Replaces the FPGA's launch/status
+ *     register interface and its three controllers:
+ *       rtl/control/prefill_decode_controller.sv:39-198  (prefill -> LM head ->
+ *           token -> decode loop, bad-descriptor check, prefill-only launch)
+ *       rtl/control/layer_controller.sv:25-195           (per-layer block order)
+ *       rtl/control/stop_condition_unit.sv:19-37         (abort > EOS > max)
+ *     and the Python driver model/tinyllama_gemm_int8.py:629-685 (run_generate).
+ *
+ *  2. Operator entry points (caller-owned device buffers plus a CUDA stream),
+ *     one per reference operator, for parity checks and for callers that drive
+ *     their own loop:
+ *       quantize_int8      model/tinyllama_gemm_int8.py:36-42
+ *       quantized_linear   model/tinyllama_gemm_int8.py:59-88
+ *       shared GEMM        rtl/compute/shared_gemm_engine.sv:127-168
+ *       requantize         rtl/compute/requantize_unit.sv:39-93
+ *       rms_norm           model/tinyllama.py:45-50
+ *       LM head + argmax   rtl/compute/argmax_reduction.sv:47-131,
+ *                          model/tinyllama_gemm_int8.py:463-467,671
+ *
+ * Weight layout at this boundary is the reference's: W[in][out] row-major so
+ * that y = x @ W (model/tinyllama.py:106-110, :339-364). Device-side operator
+ * entry points take the engine's device layout instead, W^T[out][in] (each
+ * output channel's inputs contiguous, the K-major operand of the tensor
+ * cores); tl_transpose_i8 converts.
+ *
+ * Threading: calls on one engine are serialized by the caller (the RTL
+ * accepts START only when idle). tl_abort() is the one thread-safe call; the
+ * runtime samples it between decode steps.
+ */
+#ifndef TL_API_H
+#define TL_API_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TL_API __attribute__((visibility("default")))
+#else
+#define TL_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. 0..7 mirror error_code_e (rtl/common/tinyllama_pkg.sv:260-269);
+ * 16.. are engine conditions with no RTL counterpart. */
+typedef enum tl_status {
+  TL_OK = 0,
+  TL_ERR_BAD_DESCRIPTOR = 1,   /* empty prompt in prefill mode (prefill_decode_controller.sv:85-88) */
+  TL_ERR_HBM_READ = 2,
+  TL_ERR_HBM_WRITE = 3,
+  TL_ERR_SCALE_METADATA = 4,
+  TL_ERR_DEBUG_OVERFLOW = 5,
+  TL_ERR_UNSUPPORTED_MODE = 6,
+  TL_ERR_INTERNAL = 7,
+  TL_ERR_INVALID_ARGUMENT = 16, /* null pointer, bad shape or alignment */
+  TL_ERR_OUT_OF_RANGE = 17,     /* position would exceed max_positions, batch > max_batch */
+  TL_ERR_CUDA = 18,
+  TL_ERR_NCCL = 19,
+  TL_ERR_TIMEOUT = 20,
+  TL_ERR_NOT_LOADED = 21,       /* weights not loaded */
+  TL_ERR_UNIMPLEMENTED = 22
+} tl_status;
+
+/* stop_reason_e (rtl/common/tinyllama_pkg.sv:252-258). */
+typedef enum tl_stop_reason {
+  TL_STOP_NONE = 0,
+  TL_STOP_EOS = 1,
+  TL_STOP_MAX_TOKENS = 2,
+  TL_STOP_HOST_ABORT = 3,
+  TL_STOP_INTERNAL_ERR = 4
+} tl_stop_reason;
+
+/* Launch modes (runtime_mode_e, rtl/common/tinyllama_pkg.sv:177-180). */
+enum { TL_MODE_PREFILL = 0, TL_MODE_DECODE = 1 };
+
+typedef struct tl_config {
+  int32_t hidden_size;        /* 2048 */
+  int32_t intermediate_size;  /* 5632 */
+  int32_t num_layers;         /* 22 */
+  int32_t num_heads;          /* 32 */
+  int32_t num_kv_heads;       /* 4 */
+  int32_t head_dim;           /* 64 (only 64 is supported) */
+  int32_t vocab_size;         /* 32000 */
+  int32_t max_positions;      /* 2048 */
+  float rms_norm_eps;         /* 1e-5 */
+  float rope_theta;           /* 10000 */
+  int32_t max_batch;          /* sequences held at once (KV slots) */
+  int32_t max_prefill_tokens; /* rows of one batched prefill (sum of prompt lengths) */
+} tl_config;
+
+/* One projection: int8 W[in][out] row-major plus one float64 scale per output
+ * channel (a per-tensor scale is passed broadcast). */
+typedef struct tl_linear_view {
+  const int8_t* w;
+  const double* scale;
+} tl_linear_view;
+
+typedef struct tl_layer_view {
+  tl_linear_view q, k, v, o, gate, up, down;
+  const float* input_norm;    /* [hidden] */
+  const float* post_norm;     /* [hidden] */
+} tl_layer_view;
+
+/* Host view of a whole quantized model (TinyLlamaWeights key schema,
+ * model/tinyllama.py:240-267). rope_cos/rope_sin are the float32 tables of
+ * model/tinyllama.py:59-66, [max_positions][head_dim]. */
+typedef struct tl_weights_view {
+  const float* embed;         /* [vocab][hidden] */
+  const float* final_norm;    /* [hidden] */
+  tl_linear_view lm_head;     /* W[hidden][vocab] */
+  const tl_layer_view* layers;/* [num_layers] */
+  const float* rope_cos;
+  const float* rope_sin;
+} tl_weights_view;
+
+/* Host-visible run status (STATUS register and status beat,
+ * rtl/common/tinyllama_pkg.sv:128-133, 159-166). */
+typedef struct tl_run_status {
+  uint32_t status_word;      /* bit0 busy, bit1 done, bit2 error, bit3 stop_valid,
+                                bits[6:4] stop_reason, bits[11:8] error_code */
+  uint32_t generated_count;
+  uint32_t last_token;
+  uint32_t current_layer;
+  uint32_t current_block;
+  int32_t stop_reason;       /* tl_stop_reason */
+  int32_t error_code;        /* tl_status */
+  uint32_t position;         /* tokens held in this sequence's KV cache */
+} tl_run_status;
+
+typedef struct tl_engine tl_engine;
+
+/* ---------------------------------------------------------------- runtime */
+TL_API const char* tl_status_string(int32_t status);
+TL_API int32_t tl_version(void);
+
+TL_API tl_status tl_create(const tl_config* cfg, int32_t device, tl_engine** out);
+TL_API tl_status tl_destroy(tl_engine* eng);
+/* Copies (and lays out) the host weights into the engine's device arena. */
+TL_API tl_status tl_load_weights(tl_engine* eng, const tl_weights_view* w);
+/* Random INT8 weights drawn on the device (benchmarks of the full model
+ * without a host archive): int8 uniform in [-127,127], per-channel scale
+ * 0.02/73.3 (the uniform int8 std), so each matrix has std ~0.02.
+ * Norm gains 1, embeddings N(0, 0.02) via a counter-based hash. */
+TL_API tl_status tl_init_random_weights(tl_engine* eng, uint64_t seed);
+
+/* Greedy generation for one sequence held in KV slot 0.
+ * mode TL_MODE_PREFILL: resets the slot, prefills prompt[0..n), then decodes.
+ *   n == 0 -> TL_ERR_BAD_DESCRIPTOR; max_new_tokens == 0 -> prefill only.
+ * mode TL_MODE_DECODE: continues the slot's cache; feeds prompt[0..n) as
+ *   decode steps, or the pending last token when n == 0; max_new_tokens == 0
+ *   means no limit other than out_cap and max_positions.
+ * Tokens are written to out_ids[0..generated_count). */
+TL_API tl_status tl_generate(tl_engine* eng, const uint32_t* prompt, uint32_t n_prompt,
+                      uint32_t max_new_tokens, uint32_t eos_id, uint32_t mode,
+                      uint32_t* out_ids, uint32_t out_cap, tl_run_status* st);
+
+/* Batched generation of n_seqs independent sequences (slots 0..n_seqs), all
+ * prompts of equal length n_prompt (prompts is [n_seqs][n_prompt]). Each
+ * sequence stops on its own (EOS / max / abort); out_ids is [n_seqs][out_cap],
+ * st is [n_seqs]. */
+TL_API tl_status tl_generate_batch(tl_engine* eng, uint32_t n_seqs, const uint32_t* prompts,
+                            uint32_t n_prompt, uint32_t max_new_tokens, uint32_t eos_id,
+                            uint32_t* out_ids, uint32_t out_cap, tl_run_status* st);
+
+/* Host abort request (CONTROL.ABORT_REQ): thread-safe, sampled between steps. */
+TL_API tl_status tl_abort(tl_engine* eng);
+
+/* Teacher-forced access for parity checks.
+ * tl_prefill_logits: prefill slot `slot` with ids[0..n) and return the last
+ *   row's float32 logits [vocab] (host).
+ * tl_decode_logits: feed one token to slot `slot` at its current position and
+ *   return the float32 logits [vocab] (host). */
+TL_API tl_status tl_prefill_logits(tl_engine* eng, uint32_t slot, const uint32_t* ids, uint32_t n,
+                            float* logits_out);
+TL_API tl_status tl_decode_logits(tl_engine* eng, uint32_t slot, uint32_t token, float* logits_out);
+/* Copies one (slot, layer) of the INT8 KV cache to host: k/v [kv_heads][n_pos][head_dim],
+ * scales [kv_heads]. */
+TL_API tl_status tl_read_kv(tl_engine* eng, uint32_t slot, uint32_t layer, uint32_t n_pos,
+                     int8_t* k_out, int8_t* v_out, float* k_scale_out, float* v_scale_out);
+TL_API tl_status tl_get_position(tl_engine* eng, uint32_t slot, uint32_t* pos);
+
+/* Device-resident decode step for benchmarks: runs `steps` captured decode
+ * steps of the first n_seqs slots (greedy feedback on the device) and
+ * returns without copying tokens to the host. */
+TL_API tl_status tl_decode_steps_device(tl_engine* eng, uint32_t n_seqs, uint32_t steps);
+TL_API tl_status tl_prefill_batch_device(tl_engine* eng, uint32_t n_seqs, const uint32_t* prompts,
+                                  uint32_t n_prompt);
+/* Rewinds rows 0..n_seqs-1 to `position` (KV rows at and beyond it will be
+ * overwritten), re-arms them (active, zero emitted count, no stop) and keeps
+ * each row's current input token. Lets a benchmark replay the same decode
+ * span from one prefilled prompt state. Enqueued on the engine stream. */
+TL_API tl_status tl_decode_rewind(tl_engine* eng, uint32_t n_seqs, uint32_t position);
+TL_API tl_status tl_synchronize(tl_engine* eng);
+/* Times each decode-step kernel kind in isolation on the engine stream with
+ * CUDA events: [0] norm+QKV GEMV, [1] attention (+RoPE, KV append),
+ * [2] O GEMV + residual, [3] norm+gate/up GEMV + SiLU*up, [4] down GEMV +
+ * residual, [5] final norm + LM head + argmax. Layers are cycled so weights
+ * come from HBM as in a real step; the LM head (one matrix) is preceded by an
+ * L2 flush outside the timed interval. avg_ms_out receives 6 averages. The
+ * rows must have been prefilled (tl_prefill_batch_device). */
+TL_API tl_status tl_profile_decode_kernels(tl_engine* eng, uint32_t n_seqs, uint32_t iters,
+                                           float* avg_ms_out);
+/* Number of kernels one decode step launches (for launch accounting). */
+TL_API int32_t tl_decode_step_kernel_count(tl_engine* eng);
+TL_API void* tl_engine_stream(tl_engine* eng);
+
+/* ------------------------------------------------------------- operators */
+/* All operator entry points: device pointers, `stream` is a cudaStream_t
+ * (NULL = legacy default stream). Shapes must satisfy K % 16 == 0 and
+ * 16-byte aligned int8 rows. */
+
+/* int8 W[K][N] -> W^T[N][K] (device to device). */
+TL_API tl_status tl_transpose_i8(const int8_t* w_kn, int8_t* w_nk, int32_t K, int32_t N, void* stream);
+
+/* quantize_int8 over groups of rows: rows [g*rows_per_group, (g+1)*rows_per_group)
+ * share one scale. out_absmax[g] receives max|x| of the group (float32);
+ * the scale is absmax/127 in float64 (1.0 when absmax == 0). */
+TL_API tl_status tl_quantize_int8(const float* x, int32_t rows, int32_t cols, int32_t rows_per_group,
+                           int8_t* out_q, float* out_absmax, void* stream);
+
+/* shared GEMM: C[M][N] = A[M][K] (int8) x B (int8, given as W^T[N][K]) in int32. */
+TL_API tl_status tl_gemm_i8(const int8_t* a, const int8_t* w_nk, int32_t* c, int32_t M, int32_t N,
+                     int32_t K, void* stream);
+
+/* shared GEMM + requantize_unit: out = clamp(RNE((acc * scale_q16) >> 16)).
+ * scale_q16 has N entries when per_column != 0, else 1 entry. */
+TL_API tl_status tl_gemm_i8_requant(const int8_t* a, const int8_t* w_nk, const uint32_t* scale_q16,
+                             int32_t per_column, int32_t nonnegative_only, int8_t* out,
+                             int32_t M, int32_t N, int32_t K, void* stream);
+
+/* quantized_linear: quantize x per tensor (all M rows), int8 GEMM, dequantize
+ * with float32(s_x * w_scale[n]). out[M][N] float32. acc_out (optional) int32. */
+TL_API tl_status tl_quantized_linear(const float* x, const int8_t* w_nk, const double* w_scale,
+                              float* out, int32_t* acc_out, int32_t M, int32_t N, int32_t K,
+                              void* stream);
+
+/* rms_norm, bit-exact with NumPy's float32 reduction order. */
+TL_API tl_status tl_rmsnorm(const float* x, const float* gamma, float eps, float* out, int32_t rows,
+                     int32_t cols, void* stream);
+
+/* Final RMSNorm + per-row INT8 quantization + LM-head GEMV + argmax for `rows`
+ * rows: token_out[r] = argmax (lowest id on ties); logits_out optional
+ * [rows][vocab]. Each call allocates (and frees) its own reduction scratch. */
+TL_API tl_status tl_lmhead_argmax(const float* x, const float* gamma, float eps, const int8_t* w_nk,
+                           const double* w_scale, int32_t rows, int32_t vocab, int32_t hidden,
+                           int32_t* token_out, float* logits_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TL_API_H */

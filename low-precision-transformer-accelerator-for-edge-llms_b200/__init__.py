@@ -1,0 +1,16 @@
+"""B200-native TinyLlama INT8 engine: the reference's INT8 inference hot path
+(shared INT8 GEMM + requantize, INT8 KV cache, RMSNorm/RoPE/softmax/SiLU,
+LM head + argmax, prefill/decode/stop controllers) as sm_100a CUDA kernels
+behind the C ABI in include/tl_api.h.
+
+The directory name is not a Python identifier; load it with
+``importlib.util.spec_from_file_location`` (tests/conftest.py does this) under
+any module name. The compute lives in ``libtl_b200.so``; ``shim`` is its
+ctypes binding and mirrors the reference's Python operator API.
+"""
+
+from . import shim  # noqa: F401
+from .shim import (  # noqa: F401
+    Engine, Linear, Layer, Model, TLError, forward_mixed, from_tinyllama_weights, load_library,
+    quantize_int8, quantize_weight, quantized_linear, rms_norm, rope_tables,
+)

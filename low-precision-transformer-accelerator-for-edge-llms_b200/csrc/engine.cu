@@ -1,0 +1,963 @@
+// engine.cu -- host runtime behind include/tl_api.h.
+//
+// Replaces the FPGA control plane on the hot path:
+//  * prefill_decode_controller.sv:39-198 -> tl_generate / tl_generate_batch:
+//    bad-descriptor check, prefill, LM head, token emission, decode loop,
+//    prefill-only launch (max_new_tokens == 0), decode-mode continuation.
+//  * layer_controller.sv:25-195 -> enqueue_decode_step / enqueue_prefill:
+//    the per-layer kernel sequence (norm+QKV, RoPE+KV append+attention,
+//    O+residual, norm+gate/up+SiLU*up, down+residual), 22 layers, LM head.
+//    The decode step is captured once per batch size into a CUDA graph and
+//    replayed with all per-step state (token, position, stop flags) held on
+//    the device.
+//  * stop_condition_unit.sv:19-37 -> step_finalize kernel (EOS, max tokens)
+//    plus the host abort flag sampled between graph replays.
+// Device memory layout:
+//  * weight arena: per layer W^T int8 [out][in] for QKV (fused rows q|k|v),
+//    O, gate/up (interleaved rows gate_j, up_j), down; float64 per-channel
+//    scales; float32 norm gains; float32 embedding [V][D]; LM head W^T [V][D].
+//  * KV cache: int8 [slot][layer][kv_head][max_pos][64] for K and for V
+//    (kv_cache_manager.sv:43-47 layout per slot), float32 scales
+//    [slot][layer][kv_head].
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/tl_api.h"
+#include "kernels.cuh"
+
+using namespace tl;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+#define TL_CU(call)                                                                     \
+  do {                                                                                  \
+    cudaError_t _e = (call);                                                            \
+    if (_e != cudaSuccess) {                                                            \
+      g_last_error = std::string(#call) + ": " + cudaGetErrorString(_e);                \
+      return TL_ERR_CUDA;                                                               \
+    }                                                                                   \
+  } while (0)
+
+#define TL_TRY(call)                      \
+  do {                                    \
+    tl_status _s = (call);                \
+    if (_s != TL_OK) return _s;           \
+  } while (0)
+
+template <typename T>
+tl_status dmalloc(T** p, size_t count) {
+  *p = nullptr;
+  if (count == 0) return TL_OK;
+  TL_CU(cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T)));
+  return TL_OK;
+}
+
+struct Layer {
+  int8_t* wqkv = nullptr;
+  double* sqkv = nullptr;
+  int8_t* wo = nullptr;
+  double* so = nullptr;
+  int8_t* wgu = nullptr;
+  double* sgu = nullptr;
+  int8_t* wd = nullptr;
+  double* sd = nullptr;
+  float* g1 = nullptr;
+  float* g2 = nullptr;
+};
+
+struct DecodeBufs {
+  int rows = 0;
+  float *x = nullptr, *qkv = nullptr, *att = nullptr, *hid = nullptr;
+  int *tokens = nullptr, *pos = nullptr, *slots = nullptr, *active = nullptr;
+  int *count = nullptr, *stop = nullptr, *out_ids = nullptr, *run = nullptr;
+  int32_t* argmax = nullptr;
+  unsigned long long* am_partial = nullptr;
+  unsigned int* am_counter = nullptr;
+  float* logits = nullptr;  // [rows][V], teacher-forced calls only
+};
+
+struct PrefillBufs {
+  size_t rows = 0;
+  int n_seq_cap = 0;
+  int* ids = nullptr;
+  float *x = nullptr, *h = nullptr, *qkv = nullptr, *att = nullptr, *hid = nullptr;
+  int8_t* xq = nullptr;
+  float* amax = nullptr;     // [L][4][n_seq] + [n_seq] (final norm)
+  float* kvamax = nullptr;   // [L][n_seq][2][Hkv]
+};
+
+}  // namespace
+
+struct tl_engine {
+  tl_config cfg{};
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int D = 0, F = 0, H = 0, Hkv = 0, Dq = 0, Dkv = 0, Nqkv = 0, V = 0, L = 0, P = 0, B = 0;
+  std::vector<Layer> layers;
+  float *embed = nullptr, *gfinal = nullptr, *cosT = nullptr, *sinT = nullptr;
+  int8_t* wlm = nullptr;
+  double* slm = nullptr;
+  bool loaded = false;
+  int8_t *kc = nullptr, *vc = nullptr;
+  float *ks = nullptr, *vs = nullptr;
+  DecodeBufs dec;
+  PrefillBufs pf;
+  std::map<int, cudaGraphExec_t> graphs;
+  std::atomic<int> abort_req{0};
+  std::vector<int> slot_pos;       // host mirror: tokens held per slot
+  std::vector<int> slot_pending;   // emitted token not yet fed (-1 = none)
+  int* h_pinned = nullptr;         // pinned staging
+  size_t h_pinned_ints = 0;
+  bool use_pdl = true;
+};
+
+namespace {
+
+tl_status check_cfg(const tl_config* c) {
+  if (!c) return TL_ERR_INVALID_ARGUMENT;
+  if (c->head_dim != 64) return TL_ERR_INVALID_ARGUMENT;
+  if (c->num_heads <= 0 || c->num_kv_heads <= 0 || c->num_heads % c->num_kv_heads) return TL_ERR_INVALID_ARGUMENT;
+  const int G = c->num_heads / c->num_kv_heads;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return TL_ERR_INVALID_ARGUMENT;
+  if (c->hidden_size % 64 || c->intermediate_size % 16 || c->hidden_size != c->num_heads * 64)
+    return TL_ERR_INVALID_ARGUMENT;
+  if (c->num_layers <= 0 || c->vocab_size <= 0 || c->max_positions <= 0 || c->max_batch <= 0)
+    return TL_ERR_INVALID_ARGUMENT;
+  return TL_OK;
+}
+
+// The pinned staging buffer is written by the host and read by async copies
+// on the engine stream; every user waits for the stream first so no earlier
+// copy can still be reading it.
+tl_status ensure_pinned(tl_engine* e, size_t ints) {
+  TL_CU(cudaStreamSynchronize(e->stream));
+  if (e->h_pinned_ints >= ints) return TL_OK;
+  if (e->h_pinned) cudaFreeHost(e->h_pinned);
+  e->h_pinned = nullptr;
+  TL_CU(cudaMallocHost(reinterpret_cast<void**>(&e->h_pinned), ints * sizeof(int)));
+  e->h_pinned_ints = ints;
+  return TL_OK;
+}
+
+tl_status alloc_decode(tl_engine* e) {
+  DecodeBufs& d = e->dec;
+  const int B = e->B;
+  d.rows = B;
+  TL_TRY(dmalloc(&d.x, static_cast<size_t>(B) * e->D));
+  TL_TRY(dmalloc(&d.qkv, static_cast<size_t>(B) * e->Nqkv));
+  TL_TRY(dmalloc(&d.att, static_cast<size_t>(B) * e->Dq));
+  TL_TRY(dmalloc(&d.hid, static_cast<size_t>(B) * e->F));
+  TL_TRY(dmalloc(&d.tokens, B));
+  TL_TRY(dmalloc(&d.pos, B));
+  TL_TRY(dmalloc(&d.slots, B));
+  TL_TRY(dmalloc(&d.active, B));
+  TL_TRY(dmalloc(&d.count, B));
+  TL_TRY(dmalloc(&d.stop, B));
+  TL_TRY(dmalloc(&d.out_ids, static_cast<size_t>(B) * e->P));
+  TL_TRY(dmalloc(&d.run, 4));
+  TL_TRY(dmalloc(&d.argmax, B));
+  TL_TRY(dmalloc(&d.am_partial, gemv_argmax_partials(B, e->V)));
+  TL_TRY(dmalloc(&d.am_counter, gemv_argmax_row_blocks(B) + 1));
+  TL_CU(cudaMemset(d.am_counter, 0, (gemv_argmax_row_blocks(B) + 1) * sizeof(unsigned int)));
+  TL_CU(cudaMemset(d.active, 0, B * sizeof(int)));
+  TL_CU(cudaMemset(d.stop, 0, B * sizeof(int)));
+  TL_CU(cudaMemset(d.pos, 0, B * sizeof(int)));
+  std::vector<int> slots(B);
+  for (int i = 0; i < B; ++i) slots[i] = i;
+  TL_CU(cudaMemcpy(d.slots, slots.data(), B * sizeof(int), cudaMemcpyHostToDevice));
+  return TL_OK;
+}
+
+tl_status ensure_prefill(tl_engine* e, size_t rows, int n_seq) {
+  PrefillBufs& p = e->pf;
+  if (p.rows >= rows && p.n_seq_cap >= n_seq) return TL_OK;
+  rows = std::max(rows, p.rows);
+  n_seq = std::max(n_seq, p.n_seq_cap);
+  cudaFree(p.ids); cudaFree(p.x); cudaFree(p.h); cudaFree(p.qkv); cudaFree(p.att);
+  cudaFree(p.hid); cudaFree(p.xq); cudaFree(p.amax); cudaFree(p.kvamax);
+  p = PrefillBufs{};
+  TL_TRY(dmalloc(&p.ids, rows));
+  TL_TRY(dmalloc(&p.x, rows * e->D));
+  TL_TRY(dmalloc(&p.h, rows * e->D));
+  TL_TRY(dmalloc(&p.qkv, rows * e->Nqkv));
+  TL_TRY(dmalloc(&p.att, rows * e->Dq));
+  TL_TRY(dmalloc(&p.hid, rows * e->F));
+  TL_TRY(dmalloc(&p.xq, rows * std::max(e->F, e->D)));
+  TL_TRY(dmalloc(&p.amax, static_cast<size_t>(e->L) * 4 * n_seq + n_seq));
+  TL_TRY(dmalloc(&p.kvamax, static_cast<size_t>(e->L) * n_seq * 2 * e->Hkv));
+  p.rows = rows;
+  p.n_seq_cap = n_seq;
+  return TL_OK;
+}
+
+void invalidate_graphs(tl_engine* e) {
+  for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+  e->graphs.clear();
+}
+
+// ------------------------------------------------------------- decode step
+// One decode step for rows 0..M-1 (row m uses KV slot dec.slots[m]). All
+// inputs (token, position, active) come from device memory, so the sequence
+// is graph-capturable.
+tl_status enqueue_decode_step(tl_engine* e, int M, float* logits, bool finalize) {
+  DecodeBufs& d = e->dec;
+  cudaStream_t s = e->stream;
+  const bool pdl = e->use_pdl;
+  TL_CU(launch_embed(e->embed, d.tokens, d.x, M, e->D, e->V, s, pdl));
+  for (int l = 0; l < e->L; ++l) {
+    const Layer& ly = e->layers[l];
+    GemvArgs q;
+    q.x_f32 = d.x; q.gamma = ly.g1; q.eps = e->cfg.rms_norm_eps;
+    q.w = ly.wqkv; q.w_scale = ly.sqkv; q.M = M; q.N = e->Nqkv; q.K = e->D; q.out_f32 = d.qkv;
+    TL_CU(launch_gemv(PRO_NORM, EPI_F32, q, s, pdl));
+
+    AttnDecodeArgs at;
+    at.qkv = d.qkv; at.ld = e->Nqkv; at.pos = d.pos; at.slot = d.slots; at.active = d.active;
+    at.kc = e->kc; at.vc = e->vc; at.ks = e->ks; at.vs = e->vs;
+    at.layer = l; at.L = e->L; at.H = e->H; at.Hkv = e->Hkv; at.P = e->P; at.M = M;
+    at.cos = e->cosT; at.sin = e->sinT; at.out = d.att;
+    TL_CU(launch_attn_decode(at, s, pdl));
+
+    GemvArgs o;
+    o.x_f32 = d.att; o.w = ly.wo; o.w_scale = ly.so; o.M = M; o.N = e->D; o.K = e->Dq;
+    o.out_f32 = d.x; o.resid = d.x;
+    TL_CU(launch_gemv(PRO_F32, EPI_RESID, o, s, pdl));
+
+    GemvArgs gu;
+    gu.x_f32 = d.x; gu.gamma = ly.g2; gu.eps = e->cfg.rms_norm_eps;
+    gu.w = ly.wgu; gu.w_scale = ly.sgu; gu.M = M; gu.N = 2 * e->F; gu.K = e->D; gu.out_f32 = d.hid;
+    TL_CU(launch_gemv(PRO_NORM, EPI_SILU, gu, s, pdl));
+
+    GemvArgs dn;
+    dn.x_f32 = d.hid; dn.w = ly.wd; dn.w_scale = ly.sd; dn.M = M; dn.N = e->D; dn.K = e->F;
+    dn.out_f32 = d.x; dn.resid = d.x;
+    TL_CU(launch_gemv(PRO_F32, EPI_RESID, dn, s, pdl));
+  }
+  GemvArgs lm;
+  lm.x_f32 = d.x; lm.gamma = e->gfinal; lm.eps = e->cfg.rms_norm_eps;
+  lm.w = e->wlm; lm.w_scale = e->slm; lm.M = M; lm.N = e->V; lm.K = e->D;
+  lm.logits = logits; lm.am_partial = d.am_partial; lm.am_counter = d.am_counter; lm.am_token = d.argmax;
+  TL_CU(launch_gemv(PRO_NORM, EPI_ARGMAX, lm, s, pdl));
+  if (finalize) {
+    StepArgs st;
+    st.M = M; st.argmax = d.argmax; st.tokens = d.tokens; st.pos = d.pos; st.active = d.active;
+    st.count = d.count; st.stop = d.stop; st.out_ids = d.out_ids; st.out_stride = e->P;
+    st.run = d.run; st.P = e->P;
+    TL_CU(launch_step_finalize(st, s, pdl));
+  }
+  return TL_OK;
+}
+
+tl_status get_graph(tl_engine* e, int M, cudaGraphExec_t* out) {
+  auto it = e->graphs.find(M);
+  if (it != e->graphs.end()) {
+    *out = it->second;
+    return TL_OK;
+  }
+  cudaGraph_t g = nullptr;
+  TL_CU(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+  tl_status st = enqueue_decode_step(e, M, nullptr, true);
+  cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
+  if (st != TL_OK) {
+    if (g) cudaGraphDestroy(g);
+    return st;
+  }
+  TL_CU(ce);
+  cudaGraphExec_t ex = nullptr;
+  cudaError_t ie = cudaGraphInstantiate(&ex, g, 0);
+  cudaGraphDestroy(g);
+  TL_CU(ie);
+  e->graphs[M] = ex;
+  *out = ex;
+  return TL_OK;
+}
+
+// ------------------------------------------------------------------ prefill
+// n_seq sequences of S tokens each, token ids already in pf.ids; slots
+// slot_base..slot_base+n_seq-1. Leaves the first greedy token of each
+// sequence in dec.argmax[0..n_seq) when `head` is set.
+tl_status enqueue_prefill(tl_engine* e, int n_seq, int S, int slot_base, bool head, float* logits) {
+  PrefillBufs& p = e->pf;
+  cudaStream_t s = e->stream;
+  const int R = n_seq * S;
+  const float eps = e->cfg.rms_norm_eps;
+  TL_CU(cudaMemsetAsync(p.amax, 0, (static_cast<size_t>(e->L) * 4 * n_seq + n_seq) * sizeof(float), s));
+  TL_CU(cudaMemsetAsync(p.kvamax, 0, static_cast<size_t>(e->L) * n_seq * 2 * e->Hkv * sizeof(float), s));
+  TL_CU(launch_embed(e->embed, p.ids, p.x, R, e->D, e->V, s, false));
+  for (int l = 0; l < e->L; ++l) {
+    const Layer& ly = e->layers[l];
+    float* am = p.amax + static_cast<size_t>(l) * 4 * n_seq;
+    float* kva = p.kvamax + static_cast<size_t>(l) * n_seq * 2 * e->Hkv;
+    // attention block
+    TL_CU(launch_rmsnorm_rows(p.x, ly.g1, eps, p.h, am, R, e->D, S, s));
+    TL_CU(launch_quantize_rows(p.h, am, R, e->D, S, p.xq, s));
+    GemvArgs q;
+    q.x_q = p.xq; q.in_absmax = am; q.rows_per_group = S;
+    q.w = ly.wqkv; q.w_scale = ly.sqkv; q.M = R; q.N = e->Nqkv; q.K = e->D; q.out_f32 = p.qkv;
+    TL_CU(launch_gemv(PRO_Q8, EPI_F32, q, s, false));
+    TL_CU(launch_rope_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->cosT, e->sinT, kva, s));
+    TL_CU(launch_kv_write_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, kva, e->kc, e->vc, e->ks, e->vs,
+                                  slot_base, l, e->L, e->P, s));
+    TL_CU(launch_attn_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->kc, e->vc, e->ks, e->vs, slot_base,
+                              l, e->L, e->P, p.att, am + n_seq, s));
+    TL_CU(launch_quantize_rows(p.att, am + n_seq, R, e->Dq, S, p.xq, s));
+    GemvArgs o;
+    o.x_q = p.xq; o.in_absmax = am + n_seq; o.rows_per_group = S;
+    o.w = ly.wo; o.w_scale = ly.so; o.M = R; o.N = e->D; o.K = e->Dq; o.out_f32 = p.x; o.resid = p.x;
+    TL_CU(launch_gemv(PRO_Q8, EPI_RESID, o, s, false));
+    // feed-forward block
+    TL_CU(launch_rmsnorm_rows(p.x, ly.g2, eps, p.h, am + 2 * n_seq, R, e->D, S, s));
+    TL_CU(launch_quantize_rows(p.h, am + 2 * n_seq, R, e->D, S, p.xq, s));
+    GemvArgs gu;
+    gu.x_q = p.xq; gu.in_absmax = am + 2 * n_seq; gu.rows_per_group = S;
+    gu.w = ly.wgu; gu.w_scale = ly.sgu; gu.M = R; gu.N = 2 * e->F; gu.K = e->D; gu.out_f32 = p.hid;
+    gu.out_absmax = am + 3 * n_seq;
+    TL_CU(launch_gemv(PRO_Q8, EPI_SILU, gu, s, false));
+    TL_CU(launch_quantize_rows(p.hid, am + 3 * n_seq, R, e->F, S, p.xq, s));
+    GemvArgs dn;
+    dn.x_q = p.xq; dn.in_absmax = am + 3 * n_seq; dn.rows_per_group = S;
+    dn.w = ly.wd; dn.w_scale = ly.sd; dn.M = R; dn.N = e->D; dn.K = e->F; dn.out_f32 = p.x; dn.resid = p.x;
+    TL_CU(launch_gemv(PRO_Q8, EPI_RESID, dn, s, false));
+  }
+  if (!head) return TL_OK;
+  float* amf = p.amax + static_cast<size_t>(e->L) * 4 * n_seq;
+  TL_CU(launch_rmsnorm_rows(p.x, e->gfinal, eps, p.h, amf, R, e->D, S, s));
+  GemvArgs lm;
+  lm.x_f32 = p.h; lm.x_row_offset = S - 1; lm.x_row_step = S;
+  lm.in_absmax = amf; lm.rows_per_group = 1;
+  lm.w = e->wlm; lm.w_scale = e->slm; lm.M = n_seq; lm.N = e->V; lm.K = e->D;
+  lm.logits = logits; lm.am_partial = e->dec.am_partial; lm.am_counter = e->dec.am_counter;
+  lm.am_token = e->dec.argmax;
+  TL_CU(launch_gemv(PRO_F32_GIVEN, EPI_ARGMAX, lm, s, false));
+  return TL_OK;
+}
+
+void fill_status(tl_run_status* st, int count, int last, int stop, int err, int pos) {
+  if (!st) return;
+  st->generated_count = static_cast<uint32_t>(count);
+  st->last_token = static_cast<uint32_t>(last);
+  st->current_layer = 0;
+  st->current_block = 0;
+  st->stop_reason = stop;
+  st->error_code = err;
+  st->position = static_cast<uint32_t>(pos);
+  const bool error = err != TL_OK;
+  const bool stop_valid = stop != TL_STOP_NONE;
+  st->status_word = (1u << 1) | (error ? (1u << 2) : 0u) | (stop_valid ? (1u << 3) : 0u) |
+                    ((static_cast<uint32_t>(stop) & 7u) << 4) |
+                    ((static_cast<uint32_t>(err) & 0xFu) << 8);
+}
+
+// Runs decode steps for rows 0..M-1 until every row stopped (or abort).
+// Rows must be set up (tokens, pos, active, count, stop, run params).
+tl_status run_decode_loop(tl_engine* e, int M, int budget, bool* aborted) {
+  *aborted = false;
+  cudaGraphExec_t g = nullptr;
+  TL_TRY(get_graph(e, M, &g));
+  TL_TRY(ensure_pinned(e, 2 * M + 8));
+  int done = 0;
+  while (done < budget) {
+    if (e->abort_req.load()) {
+      *aborted = true;
+      break;
+    }
+    const int chunk = std::min(8, budget - done);
+    for (int i = 0; i < chunk; ++i) TL_CU(cudaGraphLaunch(g, e->stream));
+    done += chunk;
+    TL_CU(cudaMemcpyAsync(e->h_pinned, e->dec.active, M * sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+    TL_CU(cudaStreamSynchronize(e->stream));
+    bool any = false;
+    for (int m = 0; m < M; ++m) any |= e->h_pinned[m] != 0;
+    if (!any) break;
+  }
+  return TL_OK;
+}
+
+tl_status setup_rows_after_prefill(tl_engine* e, int n_seq, int S, uint32_t max_new, uint32_t eos,
+                                   uint32_t out_cap) {
+  DecodeBufs& d = e->dec;
+  TL_TRY(ensure_pinned(e, 8 * static_cast<size_t>(n_seq) + 8));
+  int* h = e->h_pinned;
+  for (int m = 0; m < n_seq; ++m) {
+    h[m] = S - 1;          // finalize advances it to S
+    h[n_seq + m] = 1;      // active
+  }
+  TL_CU(cudaMemcpyAsync(d.pos, h, n_seq * sizeof(int), cudaMemcpyHostToDevice, e->stream));
+  TL_CU(cudaMemcpyAsync(d.active, h + n_seq, n_seq * sizeof(int), cudaMemcpyHostToDevice, e->stream));
+  TL_CU(cudaMemsetAsync(d.count, 0, n_seq * sizeof(int), e->stream));
+  TL_CU(cudaMemsetAsync(d.stop, 0, n_seq * sizeof(int), e->stream));
+  int run[4] = {static_cast<int>(max_new), static_cast<int>(eos), static_cast<int>(std::min<uint32_t>(out_cap, e->P)), 0};
+  std::memcpy(h + 2 * n_seq, run, sizeof(run));
+  TL_CU(cudaMemcpyAsync(d.run, h + 2 * n_seq, sizeof(run), cudaMemcpyHostToDevice, e->stream));
+  StepArgs st;
+  st.M = n_seq; st.argmax = d.argmax; st.tokens = d.tokens; st.pos = d.pos; st.active = d.active;
+  st.count = d.count; st.stop = d.stop; st.out_ids = d.out_ids; st.out_stride = e->P; st.run = d.run;
+  st.P = e->P;
+  TL_CU(launch_step_finalize(st, e->stream, false));
+  return TL_OK;
+}
+
+tl_status collect_rows(tl_engine* e, int n_seq, uint32_t* out_ids, uint32_t out_cap, tl_run_status* st,
+                       bool aborted) {
+  DecodeBufs& d = e->dec;
+  TL_TRY(ensure_pinned(e, 4 * static_cast<size_t>(n_seq)));
+  int* h = e->h_pinned;
+  TL_CU(cudaMemcpyAsync(h, d.count, n_seq * sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+  TL_CU(cudaMemcpyAsync(h + n_seq, d.stop, n_seq * sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+  TL_CU(cudaMemcpyAsync(h + 2 * n_seq, d.pos, n_seq * sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+  TL_CU(cudaStreamSynchronize(e->stream));
+  std::vector<int> cnt(h, h + n_seq), stp(h + n_seq, h + 2 * n_seq), pos(h + 2 * n_seq, h + 3 * n_seq);
+  for (int m = 0; m < n_seq; ++m) {
+    const int c = std::min<int>(cnt[m], static_cast<int>(out_cap));
+    if (c > 0)
+      TL_CU(cudaMemcpy2D(out_ids + static_cast<size_t>(m) * out_cap, out_cap * sizeof(uint32_t),
+                         d.out_ids + static_cast<size_t>(m) * e->P, e->P * sizeof(int), c * sizeof(int), 1,
+                         cudaMemcpyDeviceToHost));
+    int stop = stp[m], err = TL_OK;
+    if (stop == 0 && aborted) stop = TL_STOP_HOST_ABORT;
+    if (stop == 4) err = TL_ERR_OUT_OF_RANGE;
+    const int last = c > 0 ? static_cast<int>(out_ids[static_cast<size_t>(m) * out_cap + c - 1]) : 0;
+    fill_status(st ? st + m : nullptr, c, last, stop, err, pos[m]);
+    e->slot_pos[m] = pos[m];
+    e->slot_pending[m] = c > 0 ? last : -1;
+  }
+  return TL_OK;
+}
+
+}  // namespace
+
+// ============================================================== public API
+extern "C" {
+
+const char* tl_status_string(int32_t s) {
+  switch (s) {
+    case TL_OK: return "ok";
+    case TL_ERR_BAD_DESCRIPTOR: return "bad descriptor";
+    case TL_ERR_UNSUPPORTED_MODE: return "unsupported mode";
+    case TL_ERR_INTERNAL: return "internal error";
+    case TL_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case TL_ERR_OUT_OF_RANGE: return "out of range";
+    case TL_ERR_CUDA: return g_last_error.empty() ? "cuda error" : g_last_error.c_str();
+    case TL_ERR_NCCL: return "nccl error";
+    case TL_ERR_TIMEOUT: return "timeout";
+    case TL_ERR_NOT_LOADED: return "weights not loaded";
+    case TL_ERR_UNIMPLEMENTED: return "unimplemented";
+    default: return "error";
+  }
+}
+
+int32_t tl_version(void) { return 0x00010000; }
+
+tl_status tl_create(const tl_config* cfg, int32_t device, tl_engine** out) {
+  if (!out) return TL_ERR_INVALID_ARGUMENT;
+  *out = nullptr;
+  TL_TRY(check_cfg(cfg));
+  TL_CU(cudaSetDevice(device));
+  tl_engine* e = new tl_engine();
+  e->cfg = *cfg;
+  e->device = device;
+  e->D = cfg->hidden_size; e->F = cfg->intermediate_size; e->H = cfg->num_heads; e->Hkv = cfg->num_kv_heads;
+  e->Dq = e->H * 64; e->Dkv = e->Hkv * 64; e->Nqkv = e->Dq + 2 * e->Dkv; e->V = cfg->vocab_size;
+  e->L = cfg->num_layers; e->P = cfg->max_positions; e->B = cfg->max_batch;
+  auto fail = [&](tl_status s) { tl_destroy(e); return s; };
+  cudaError_t ce = prepare_kernels(std::max(e->F, e->D));
+  if (ce == cudaSuccess) ce = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
+  if (ce != cudaSuccess) { g_last_error = cudaGetErrorString(ce); return fail(TL_ERR_CUDA); }
+  e->layers.resize(e->L);
+  for (auto& ly : e->layers) {
+    tl_status s;
+    if ((s = dmalloc(&ly.wqkv, static_cast<size_t>(e->Nqkv) * e->D)) != TL_OK) return fail(s);
+    if ((s = dmalloc(&ly.sqkv, e->Nqkv)) != TL_OK) return fail(s);
+    if ((s = dmalloc(&ly.wo, static_cast<size_t>(e->D) * e->Dq)) != TL_OK) return fail(s);
+    if ((s = dmalloc(&ly.so, e->D)) != TL_OK) return fail(s);
+    if ((s = dmalloc(&ly.wgu, static_cast<size_t>(2) * e->F * e->D)) != TL_OK) return fail(s);
+    if ((s = dmalloc(&ly.sgu, 2 * e->F)) != TL_OK) return fail(s);
+    if ((s = dmalloc(&ly.wd, static_cast<size_t>(e->D) * e->F)) != TL_OK) return fail(s);
+    if ((s = dmalloc(&ly.sd, e->D)) != TL_OK) return fail(s);
+    if ((s = dmalloc(&ly.g1, e->D)) != TL_OK) return fail(s);
+    if ((s = dmalloc(&ly.g2, e->D)) != TL_OK) return fail(s);
+  }
+  tl_status s;
+  if ((s = dmalloc(&e->embed, static_cast<size_t>(e->V) * e->D)) != TL_OK) return fail(s);
+  if ((s = dmalloc(&e->gfinal, e->D)) != TL_OK) return fail(s);
+  if ((s = dmalloc(&e->wlm, static_cast<size_t>(e->V) * e->D)) != TL_OK) return fail(s);
+  if ((s = dmalloc(&e->slm, e->V)) != TL_OK) return fail(s);
+  if ((s = dmalloc(&e->cosT, static_cast<size_t>(e->P) * 64)) != TL_OK) return fail(s);
+  if ((s = dmalloc(&e->sinT, static_cast<size_t>(e->P) * 64)) != TL_OK) return fail(s);
+  const size_t kv = static_cast<size_t>(e->B) * e->L * e->Hkv * e->P * 64;
+  if ((s = dmalloc(&e->kc, kv)) != TL_OK) return fail(s);
+  if ((s = dmalloc(&e->vc, kv)) != TL_OK) return fail(s);
+  if ((s = dmalloc(&e->ks, static_cast<size_t>(e->B) * e->L * e->Hkv)) != TL_OK) return fail(s);
+  if ((s = dmalloc(&e->vs, static_cast<size_t>(e->B) * e->L * e->Hkv)) != TL_OK) return fail(s);
+  if ((s = alloc_decode(e)) != TL_OK) return fail(s);
+  const size_t pf_rows = cfg->max_prefill_tokens > 0 ? cfg->max_prefill_tokens : e->P;
+  if ((s = ensure_prefill(e, pf_rows, e->B)) != TL_OK) return fail(s);
+  e->slot_pos.assign(e->B, 0);
+  e->slot_pending.assign(e->B, -1);
+  *out = e;
+  return TL_OK;
+}
+
+tl_status tl_destroy(tl_engine* e) {
+  if (!e) return TL_OK;
+  cudaSetDevice(e->device);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  invalidate_graphs(e);
+  for (auto& ly : e->layers) {
+    cudaFree(ly.wqkv); cudaFree(ly.sqkv); cudaFree(ly.wo); cudaFree(ly.so); cudaFree(ly.wgu);
+    cudaFree(ly.sgu); cudaFree(ly.wd); cudaFree(ly.sd); cudaFree(ly.g1); cudaFree(ly.g2);
+  }
+  cudaFree(e->embed); cudaFree(e->gfinal); cudaFree(e->wlm); cudaFree(e->slm);
+  cudaFree(e->cosT); cudaFree(e->sinT); cudaFree(e->kc); cudaFree(e->vc); cudaFree(e->ks); cudaFree(e->vs);
+  DecodeBufs& d = e->dec;
+  cudaFree(d.x); cudaFree(d.qkv); cudaFree(d.att); cudaFree(d.hid); cudaFree(d.tokens); cudaFree(d.pos);
+  cudaFree(d.slots); cudaFree(d.active); cudaFree(d.count); cudaFree(d.stop); cudaFree(d.out_ids);
+  cudaFree(d.run); cudaFree(d.argmax); cudaFree(d.am_partial); cudaFree(d.am_counter); cudaFree(d.logits);
+  PrefillBufs& p = e->pf;
+  cudaFree(p.ids); cudaFree(p.x); cudaFree(p.h); cudaFree(p.qkv); cudaFree(p.att); cudaFree(p.hid);
+  cudaFree(p.xq); cudaFree(p.amax); cudaFree(p.kvamax);
+  if (e->h_pinned) cudaFreeHost(e->h_pinned);
+  if (e->stream) cudaStreamDestroy(e->stream);
+  delete e;
+  return TL_OK;
+}
+
+static tl_status upload_transposed(tl_engine* e, int8_t* tmp, const int8_t* host_kn, int K, int N,
+                                   int8_t* dst_nk) {
+  TL_CU(cudaMemcpyAsync(tmp, host_kn, static_cast<size_t>(K) * N, cudaMemcpyHostToDevice, e->stream));
+  TL_CU(launch_transpose_i8(tmp, dst_nk, K, N, e->stream));
+  return TL_OK;
+}
+
+tl_status tl_load_weights(tl_engine* e, const tl_weights_view* w) {
+  if (!e || !w || !w->embed || !w->final_norm || !w->lm_head.w || !w->lm_head.scale || !w->layers)
+    return TL_ERR_INVALID_ARGUMENT;
+  TL_CU(cudaSetDevice(e->device));
+  const int D = e->D, F = e->F, Dq = e->Dq, Dkv = e->Dkv, V = e->V;
+  const size_t tmp_bytes = std::max<size_t>(static_cast<size_t>(V) * D, 2 * static_cast<size_t>(F) * D);
+  int8_t* tmp = nullptr;
+  TL_TRY(dmalloc(&tmp, tmp_bytes));
+  auto body = [&]() -> tl_status {
+    for (int l = 0; l < e->L; ++l) {
+      const tl_layer_view& lv = w->layers[l];
+      const tl_linear_view* all[7] = {&lv.q, &lv.k, &lv.v, &lv.o, &lv.gate, &lv.up, &lv.down};
+      for (auto* p : all)
+        if (!p->w || !p->scale) return TL_ERR_INVALID_ARGUMENT;
+      if (!lv.input_norm || !lv.post_norm) return TL_ERR_INVALID_ARGUMENT;
+      Layer& ly = e->layers[l];
+      TL_TRY(upload_transposed(e, tmp, lv.q.w, D, Dq, ly.wqkv));
+      TL_TRY(upload_transposed(e, tmp, lv.k.w, D, Dkv, ly.wqkv + static_cast<size_t>(Dq) * D));
+      TL_TRY(upload_transposed(e, tmp, lv.v.w, D, Dkv, ly.wqkv + static_cast<size_t>(Dq + Dkv) * D));
+      TL_CU(cudaMemcpyAsync(ly.sqkv, lv.q.scale, Dq * sizeof(double), cudaMemcpyHostToDevice, e->stream));
+      TL_CU(cudaMemcpyAsync(ly.sqkv + Dq, lv.k.scale, Dkv * sizeof(double), cudaMemcpyHostToDevice, e->stream));
+      TL_CU(cudaMemcpyAsync(ly.sqkv + Dq + Dkv, lv.v.scale, Dkv * sizeof(double), cudaMemcpyHostToDevice, e->stream));
+      TL_TRY(upload_transposed(e, tmp, lv.o.w, Dq, D, ly.wo));
+      TL_CU(cudaMemcpyAsync(ly.so, lv.o.scale, D * sizeof(double), cudaMemcpyHostToDevice, e->stream));
+      TL_CU(cudaMemcpyAsync(tmp, lv.gate.w, static_cast<size_t>(D) * F, cudaMemcpyHostToDevice, e->stream));
+      TL_CU(cudaMemcpyAsync(tmp + static_cast<size_t>(D) * F, lv.up.w, static_cast<size_t>(D) * F,
+                            cudaMemcpyHostToDevice, e->stream));
+      TL_CU(launch_interleave_gate_up(tmp, tmp + static_cast<size_t>(D) * F, ly.wgu, D, F, e->stream));
+      std::vector<double> sgu(2 * static_cast<size_t>(F));
+      for (int j = 0; j < F; ++j) {
+        sgu[2 * j] = lv.gate.scale[j];
+        sgu[2 * j + 1] = lv.up.scale[j];
+      }
+      TL_CU(cudaMemcpyAsync(ly.sgu, sgu.data(), sgu.size() * sizeof(double), cudaMemcpyHostToDevice, e->stream));
+      TL_CU(cudaStreamSynchronize(e->stream));  // sgu is a host temporary
+      TL_TRY(upload_transposed(e, tmp, lv.down.w, F, D, ly.wd));
+      TL_CU(cudaMemcpyAsync(ly.sd, lv.down.scale, D * sizeof(double), cudaMemcpyHostToDevice, e->stream));
+      TL_CU(cudaMemcpyAsync(ly.g1, lv.input_norm, D * sizeof(float), cudaMemcpyHostToDevice, e->stream));
+      TL_CU(cudaMemcpyAsync(ly.g2, lv.post_norm, D * sizeof(float), cudaMemcpyHostToDevice, e->stream));
+    }
+    TL_CU(cudaMemcpyAsync(e->embed, w->embed, static_cast<size_t>(V) * D * sizeof(float), cudaMemcpyHostToDevice, e->stream));
+    TL_CU(cudaMemcpyAsync(e->gfinal, w->final_norm, D * sizeof(float), cudaMemcpyHostToDevice, e->stream));
+    TL_TRY(upload_transposed(e, tmp, w->lm_head.w, D, V, e->wlm));
+    TL_CU(cudaMemcpyAsync(e->slm, w->lm_head.scale, V * sizeof(double), cudaMemcpyHostToDevice, e->stream));
+    std::vector<float> c(static_cast<size_t>(e->P) * 64), sn(static_cast<size_t>(e->P) * 64);
+    if (w->rope_cos && w->rope_sin) {
+      std::memcpy(c.data(), w->rope_cos, c.size() * sizeof(float));
+      std::memcpy(sn.data(), w->rope_sin, sn.size() * sizeof(float));
+    } else {
+      for (int p = 0; p < e->P; ++p)
+        for (int i = 0; i < 32; ++i) {
+          const double f = 1.0 / std::pow(static_cast<double>(e->cfg.rope_theta), (2.0 * i) / 64.0);
+          const double a = p * f;
+          c[p * 64 + i] = c[p * 64 + i + 32] = static_cast<float>(std::cos(a));
+          sn[p * 64 + i] = sn[p * 64 + i + 32] = static_cast<float>(std::sin(a));
+        }
+    }
+    TL_CU(cudaMemcpyAsync(e->cosT, c.data(), c.size() * sizeof(float), cudaMemcpyHostToDevice, e->stream));
+    TL_CU(cudaMemcpyAsync(e->sinT, sn.data(), sn.size() * sizeof(float), cudaMemcpyHostToDevice, e->stream));
+    TL_CU(cudaStreamSynchronize(e->stream));
+    return TL_OK;
+  };
+  tl_status st = body();
+  cudaStreamSynchronize(e->stream);
+  cudaFree(tmp);
+  if (st == TL_OK) e->loaded = true;
+  return st;
+}
+
+tl_status tl_init_random_weights(tl_engine* e, uint64_t seed) {
+  if (!e) return TL_ERR_INVALID_ARGUMENT;
+  TL_CU(cudaSetDevice(e->device));
+  cudaStream_t s = e->stream;
+  const double wscale = 0.02 / 73.3;  // int8 uniform[-127,127] has std ~73.3
+  uint64_t k = seed * 1000003ull;
+  for (auto& ly : e->layers) {
+    TL_CU(launch_random_i8(ly.wqkv, static_cast<size_t>(e->Nqkv) * e->D, ++k, s));
+    TL_CU(launch_random_i8(ly.wo, static_cast<size_t>(e->D) * e->Dq, ++k, s));
+    TL_CU(launch_random_i8(ly.wgu, static_cast<size_t>(2) * e->F * e->D, ++k, s));
+    TL_CU(launch_random_i8(ly.wd, static_cast<size_t>(e->D) * e->F, ++k, s));
+    TL_CU(launch_fill_f64(ly.sqkv, e->Nqkv, wscale, s));
+    TL_CU(launch_fill_f64(ly.so, e->D, wscale, s));
+    TL_CU(launch_fill_f64(ly.sgu, 2 * e->F, wscale, s));
+    TL_CU(launch_fill_f64(ly.sd, e->D, wscale, s));
+    TL_CU(launch_fill_f32(ly.g1, e->D, 1.0f, s));
+    TL_CU(launch_fill_f32(ly.g2, e->D, 1.0f, s));
+  }
+  TL_CU(launch_random_normal_f32(e->embed, static_cast<size_t>(e->V) * e->D, 0.02f, ++k, s));
+  TL_CU(launch_fill_f32(e->gfinal, e->D, 1.0f, s));
+  TL_CU(launch_random_i8(e->wlm, static_cast<size_t>(e->V) * e->D, ++k, s));
+  TL_CU(launch_fill_f64(e->slm, e->V, wscale, s));
+  std::vector<float> c(static_cast<size_t>(e->P) * 64), sn(static_cast<size_t>(e->P) * 64);
+  for (int p = 0; p < e->P; ++p)
+    for (int i = 0; i < 32; ++i) {
+      const double f = 1.0 / std::pow(static_cast<double>(e->cfg.rope_theta), (2.0 * i) / 64.0);
+      c[p * 64 + i] = c[p * 64 + i + 32] = static_cast<float>(std::cos(p * f));
+      sn[p * 64 + i] = sn[p * 64 + i + 32] = static_cast<float>(std::sin(p * f));
+    }
+  TL_CU(cudaMemcpyAsync(e->cosT, c.data(), c.size() * sizeof(float), cudaMemcpyHostToDevice, s));
+  TL_CU(cudaMemcpyAsync(e->sinT, sn.data(), sn.size() * sizeof(float), cudaMemcpyHostToDevice, s));
+  TL_CU(cudaStreamSynchronize(s));
+  e->loaded = true;
+  return TL_OK;
+}
+
+static tl_status prefill_common(tl_engine* e, uint32_t n_seq, const uint32_t* prompts, uint32_t S,
+                                bool head, float* logits) {
+  if (S == 0) return TL_ERR_BAD_DESCRIPTOR;
+  if (S > static_cast<uint32_t>(e->P)) return TL_ERR_OUT_OF_RANGE;
+  if (n_seq == 0 || n_seq > static_cast<uint32_t>(e->B)) return TL_ERR_OUT_OF_RANGE;
+  const size_t R = static_cast<size_t>(n_seq) * S;
+  TL_TRY(ensure_prefill(e, R, static_cast<int>(n_seq)));
+  TL_TRY(ensure_pinned(e, R));
+  for (size_t i = 0; i < R; ++i) e->h_pinned[i] = static_cast<int>(prompts[i]);
+  TL_CU(cudaMemcpyAsync(e->pf.ids, e->h_pinned, R * sizeof(int), cudaMemcpyHostToDevice, e->stream));
+  TL_TRY(enqueue_prefill(e, static_cast<int>(n_seq), static_cast<int>(S), 0, head, logits));
+  return TL_OK;
+}
+
+tl_status tl_generate_batch(tl_engine* e, uint32_t n_seqs, const uint32_t* prompts, uint32_t n_prompt,
+                            uint32_t max_new, uint32_t eos, uint32_t* out_ids, uint32_t out_cap,
+                            tl_run_status* st) {
+  if (!e || !prompts || (!out_ids && out_cap)) return TL_ERR_INVALID_ARGUMENT;
+  if (!e->loaded) return TL_ERR_NOT_LOADED;
+  TL_CU(cudaSetDevice(e->device));
+  e->abort_req.store(0);
+  if (n_prompt == 0) {
+    for (uint32_t m = 0; st && m < n_seqs; ++m) fill_status(st + m, 0, 0, TL_STOP_NONE, TL_ERR_BAD_DESCRIPTOR, 0);
+    return TL_ERR_BAD_DESCRIPTOR;
+  }
+  TL_TRY(prefill_common(e, n_seqs, prompts, n_prompt, max_new != 0, nullptr));
+  const int M = static_cast<int>(n_seqs);
+  if (max_new == 0) {  // prefill-only launch
+    TL_CU(cudaStreamSynchronize(e->stream));
+    for (int m = 0; m < M; ++m) {
+      e->slot_pos[m] = static_cast<int>(n_prompt);
+      e->slot_pending[m] = -1;
+      fill_status(st ? st + m : nullptr, 0, 0, TL_STOP_NONE, TL_OK, static_cast<int>(n_prompt));
+    }
+    return TL_OK;
+  }
+  TL_TRY(setup_rows_after_prefill(e, M, static_cast<int>(n_prompt), max_new, eos, out_cap));
+  bool aborted = false;
+  const int budget = static_cast<int>(std::min<uint32_t>(max_new ? max_new : out_cap, out_cap));
+  if (e->abort_req.load()) aborted = true;
+  else TL_TRY(run_decode_loop(e, M, std::max(0, budget - 1), &aborted));
+  return collect_rows(e, M, out_ids, out_cap, st, aborted);
+}
+
+tl_status tl_generate(tl_engine* e, const uint32_t* prompt, uint32_t n, uint32_t max_new, uint32_t eos,
+                      uint32_t mode, uint32_t* out_ids, uint32_t out_cap, tl_run_status* st) {
+  if (!e) return TL_ERR_INVALID_ARGUMENT;
+  if (!e->loaded) return TL_ERR_NOT_LOADED;
+  if (mode == TL_MODE_PREFILL) {
+    if (n == 0) {
+      fill_status(st, 0, 0, TL_STOP_NONE, TL_ERR_BAD_DESCRIPTOR, 0);
+      return TL_ERR_BAD_DESCRIPTOR;
+    }
+    if (!prompt) return TL_ERR_INVALID_ARGUMENT;
+    if (n > static_cast<uint32_t>(e->P)) {
+      fill_status(st, 0, 0, TL_STOP_INTERNAL_ERR, TL_ERR_OUT_OF_RANGE, 0);
+      return TL_ERR_OUT_OF_RANGE;
+    }
+    return tl_generate_batch(e, 1, prompt, n, max_new, eos, out_ids, out_cap, st);
+  }
+  if (mode != TL_MODE_DECODE) {
+    fill_status(st, 0, 0, TL_STOP_NONE, TL_ERR_UNSUPPORTED_MODE, 0);
+    return TL_ERR_UNSUPPORTED_MODE;
+  }
+  // decode-mode continuation of slot 0: feed prompt tokens (or the pending
+  // token) one decode step at a time, then generate.
+  TL_CU(cudaSetDevice(e->device));
+  e->abort_req.store(0);
+  std::vector<uint32_t> feed(prompt, prompt + n);
+  if (feed.empty()) {
+    if (e->slot_pending[0] < 0) {
+      fill_status(st, 0, 0, TL_STOP_NONE, TL_ERR_BAD_DESCRIPTOR, e->slot_pos[0]);
+      return TL_ERR_BAD_DESCRIPTOR;
+    }
+    feed.push_back(static_cast<uint32_t>(e->slot_pending[0]));
+  }
+  int pos = e->slot_pos[0];
+  if (pos + static_cast<int>(feed.size()) > e->P) {
+    fill_status(st, 0, 0, TL_STOP_INTERNAL_ERR, TL_ERR_OUT_OF_RANGE, pos);
+    return TL_ERR_OUT_OF_RANGE;
+  }
+  DecodeBufs& d = e->dec;
+  const uint32_t cap = std::min<uint32_t>(out_cap, static_cast<uint32_t>(e->P));
+  int run[4] = {static_cast<int>(max_new), static_cast<int>(eos), static_cast<int>(cap), 0};
+  TL_TRY(ensure_pinned(e, 16));
+  // feed all but the last token without emitting (teacher forcing)
+  for (size_t i = 0; i < feed.size(); ++i) {
+    int* h = e->h_pinned;
+    h[0] = static_cast<int>(feed[i]);
+    h[1] = pos;
+    h[2] = 1;
+    TL_CU(cudaMemcpyAsync(d.tokens, h, sizeof(int), cudaMemcpyHostToDevice, e->stream));
+    TL_CU(cudaMemcpyAsync(d.pos, h + 1, sizeof(int), cudaMemcpyHostToDevice, e->stream));
+    TL_CU(cudaMemcpyAsync(d.active, h + 2, sizeof(int), cudaMemcpyHostToDevice, e->stream));
+    const bool last = i + 1 == feed.size();
+    if (!last) {
+      TL_TRY(enqueue_decode_step(e, 1, nullptr, false));
+      TL_CU(cudaStreamSynchronize(e->stream));
+      ++pos;
+    } else {
+      // the last fed token's step emits the first new token through finalize
+      h[3] = 0;
+      TL_CU(cudaMemsetAsync(d.count, 0, sizeof(int), e->stream));
+      TL_CU(cudaMemsetAsync(d.stop, 0, sizeof(int), e->stream));
+      std::memcpy(h + 4, run, sizeof(run));
+      TL_CU(cudaMemcpyAsync(d.run, h + 4, sizeof(run), cudaMemcpyHostToDevice, e->stream));
+      TL_CU(cudaStreamSynchronize(e->stream));
+    }
+  }
+  bool aborted = false;
+  const int budget = static_cast<int>(max_new ? std::min(max_new, cap) : cap);
+  TL_TRY(run_decode_loop(e, 1, budget, &aborted));
+  return collect_rows(e, 1, out_ids, out_cap, st, aborted);
+}
+
+tl_status tl_abort(tl_engine* e) {
+  if (!e) return TL_ERR_INVALID_ARGUMENT;
+  e->abort_req.store(1);
+  return TL_OK;
+}
+
+tl_status tl_prefill_logits(tl_engine* e, uint32_t slot, const uint32_t* ids, uint32_t n, float* logits_out) {
+  if (!e || !ids || !logits_out) return TL_ERR_INVALID_ARGUMENT;
+  if (!e->loaded) return TL_ERR_NOT_LOADED;
+  if (slot != 0) return TL_ERR_UNIMPLEMENTED;
+  TL_CU(cudaSetDevice(e->device));
+  if (!e->dec.logits) TL_TRY(dmalloc(&e->dec.logits, static_cast<size_t>(e->B) * e->V));
+  TL_TRY(prefill_common(e, 1, ids, n, true, e->dec.logits));
+  TL_CU(cudaMemcpyAsync(logits_out, e->dec.logits, e->V * sizeof(float), cudaMemcpyDeviceToHost, e->stream));
+  TL_CU(cudaStreamSynchronize(e->stream));
+  e->slot_pos[0] = static_cast<int>(n);
+  e->slot_pending[0] = -1;
+  return TL_OK;
+}
+
+tl_status tl_decode_logits(tl_engine* e, uint32_t slot, uint32_t token, float* logits_out) {
+  if (!e || !logits_out) return TL_ERR_INVALID_ARGUMENT;
+  if (!e->loaded) return TL_ERR_NOT_LOADED;
+  if (slot >= static_cast<uint32_t>(e->B)) return TL_ERR_OUT_OF_RANGE;
+  TL_CU(cudaSetDevice(e->device));
+  const int pos = e->slot_pos[slot];
+  if (pos >= e->P) return TL_ERR_OUT_OF_RANGE;
+  if (!e->dec.logits) TL_TRY(dmalloc(&e->dec.logits, static_cast<size_t>(e->B) * e->V));
+  TL_TRY(ensure_pinned(e, 8));
+  int* h = e->h_pinned;
+  h[0] = static_cast<int>(token); h[1] = pos; h[2] = 1; h[3] = static_cast<int>(slot);
+  DecodeBufs& d = e->dec;
+  TL_CU(cudaMemcpyAsync(d.tokens, h, sizeof(int), cudaMemcpyHostToDevice, e->stream));
+  TL_CU(cudaMemcpyAsync(d.pos, h + 1, sizeof(int), cudaMemcpyHostToDevice, e->stream));
+  TL_CU(cudaMemcpyAsync(d.active, h + 2, sizeof(int), cudaMemcpyHostToDevice, e->stream));
+  TL_CU(cudaMemcpyAsync(d.slots, h + 3, sizeof(int), cudaMemcpyHostToDevice, e->stream));
+  tl_status st = enqueue_decode_step(e, 1, d.logits, false);
+  h[4] = 0;
+  TL_CU(cudaMemcpyAsync(d.slots, h + 4, sizeof(int), cudaMemcpyHostToDevice, e->stream));
+  TL_TRY(st);
+  TL_CU(cudaMemcpyAsync(logits_out, d.logits, e->V * sizeof(float), cudaMemcpyDeviceToHost, e->stream));
+  TL_CU(cudaStreamSynchronize(e->stream));
+  e->slot_pos[slot] = pos + 1;
+  e->slot_pending[slot] = -1;
+  return TL_OK;
+}
+
+tl_status tl_read_kv(tl_engine* e, uint32_t slot, uint32_t layer, uint32_t n_pos, int8_t* k_out,
+                     int8_t* v_out, float* ks_out, float* vs_out) {
+  if (!e || !k_out || !v_out || !ks_out || !vs_out) return TL_ERR_INVALID_ARGUMENT;
+  if (slot >= static_cast<uint32_t>(e->B) || layer >= static_cast<uint32_t>(e->L) || n_pos > static_cast<uint32_t>(e->P))
+    return TL_ERR_OUT_OF_RANGE;
+  TL_CU(cudaSetDevice(e->device));
+  TL_CU(cudaStreamSynchronize(e->stream));
+  for (int h = 0; h < e->Hkv; ++h) {
+    const size_t sidx = (static_cast<size_t>(slot) * e->L + layer) * e->Hkv + h;
+    TL_CU(cudaMemcpy(k_out + static_cast<size_t>(h) * n_pos * 64, e->kc + sidx * e->P * 64,
+                     static_cast<size_t>(n_pos) * 64, cudaMemcpyDeviceToHost));
+    TL_CU(cudaMemcpy(v_out + static_cast<size_t>(h) * n_pos * 64, e->vc + sidx * e->P * 64,
+                     static_cast<size_t>(n_pos) * 64, cudaMemcpyDeviceToHost));
+    TL_CU(cudaMemcpy(ks_out + h, e->ks + sidx, sizeof(float), cudaMemcpyDeviceToHost));
+    TL_CU(cudaMemcpy(vs_out + h, e->vs + sidx, sizeof(float), cudaMemcpyDeviceToHost));
+  }
+  return TL_OK;
+}
+
+tl_status tl_get_position(tl_engine* e, uint32_t slot, uint32_t* pos) {
+  if (!e || !pos || slot >= static_cast<uint32_t>(e->B)) return TL_ERR_INVALID_ARGUMENT;
+  *pos = static_cast<uint32_t>(e->slot_pos[slot]);
+  return TL_OK;
+}
+
+tl_status tl_prefill_batch_device(tl_engine* e, uint32_t n_seqs, const uint32_t* prompts, uint32_t n_prompt) {
+  if (!e || !prompts) return TL_ERR_INVALID_ARGUMENT;
+  if (!e->loaded) return TL_ERR_NOT_LOADED;
+  TL_CU(cudaSetDevice(e->device));
+  TL_TRY(prefill_common(e, n_seqs, prompts, n_prompt, true, nullptr));
+  // rows ready for device-resident decode: no stop limit except capacity
+  TL_TRY(setup_rows_after_prefill(e, static_cast<int>(n_seqs), static_cast<int>(n_prompt), 0, 0xFFFFFFFFu,
+                                  static_cast<uint32_t>(e->P)));
+  for (uint32_t m = 0; m < n_seqs; ++m) e->slot_pos[m] = static_cast<int>(n_prompt) + 1;
+  return TL_OK;
+}
+
+tl_status tl_decode_steps_device(tl_engine* e, uint32_t n_seqs, uint32_t steps) {
+  if (!e) return TL_ERR_INVALID_ARGUMENT;
+  if (!e->loaded) return TL_ERR_NOT_LOADED;
+  if (n_seqs == 0 || n_seqs > static_cast<uint32_t>(e->B)) return TL_ERR_OUT_OF_RANGE;
+  TL_CU(cudaSetDevice(e->device));
+  cudaGraphExec_t g = nullptr;
+  TL_TRY(get_graph(e, static_cast<int>(n_seqs), &g));
+  for (uint32_t i = 0; i < steps; ++i) TL_CU(cudaGraphLaunch(g, e->stream));
+  return TL_OK;
+}
+
+tl_status tl_decode_rewind(tl_engine* e, uint32_t n_seqs, uint32_t position) {
+  if (!e) return TL_ERR_INVALID_ARGUMENT;
+  if (n_seqs == 0 || n_seqs > static_cast<uint32_t>(e->B) || position >= static_cast<uint32_t>(e->P))
+    return TL_ERR_OUT_OF_RANGE;
+  TL_CU(cudaSetDevice(e->device));
+  DecodeBufs& d = e->dec;
+  TL_CU(launch_rows_rewind(d.pos, d.active, d.count, d.stop, static_cast<int>(n_seqs),
+                           static_cast<int>(position), e->stream));
+  return TL_OK;
+}
+
+tl_status tl_synchronize(tl_engine* e) {
+  if (!e) return TL_ERR_INVALID_ARGUMENT;
+  TL_CU(cudaStreamSynchronize(e->stream));
+  TL_CU(cudaGetLastError());
+  return TL_OK;
+}
+
+tl_status tl_profile_decode_kernels(tl_engine* e, uint32_t n_seqs, uint32_t iters, float* avg_ms_out) {
+  if (!e || !avg_ms_out || iters == 0) return TL_ERR_INVALID_ARGUMENT;
+  if (!e->loaded) return TL_ERR_NOT_LOADED;
+  if (n_seqs == 0 || n_seqs > static_cast<uint32_t>(e->B)) return TL_ERR_OUT_OF_RANGE;
+  TL_CU(cudaSetDevice(e->device));
+  const int M = static_cast<int>(n_seqs);
+  DecodeBufs& d = e->dec;
+  cudaStream_t s = e->stream;
+  const size_t flush_bytes = 256ull << 20;
+  void* flush = nullptr;
+  TL_CU(cudaMallocAsync(&flush, flush_bytes, s));
+  std::vector<cudaEvent_t> ev(2 * iters);
+  for (auto& x : ev) TL_CU(cudaEventCreate(&x));
+  tl_status result = TL_OK;
+  for (int kind = 0; kind < 6 && result == TL_OK; ++kind) {
+    for (uint32_t it = 0; it < iters; ++it) {
+      const int l = static_cast<int>(it % e->L);
+      const Layer& ly = e->layers[l];
+      if (kind == 5) TL_CU(cudaMemsetAsync(flush, it & 0xff, flush_bytes, s));
+      TL_CU(cudaEventRecord(ev[2 * it], s));
+      cudaError_t ce = cudaSuccess;
+      GemvArgs g;
+      g.M = M;
+      g.eps = e->cfg.rms_norm_eps;
+      switch (kind) {
+        case 0:
+          g.x_f32 = d.x; g.gamma = ly.g1; g.w = ly.wqkv; g.w_scale = ly.sqkv; g.N = e->Nqkv; g.K = e->D;
+          g.out_f32 = d.qkv;
+          ce = launch_gemv(PRO_NORM, EPI_F32, g, s, false);
+          break;
+        case 1: {
+          AttnDecodeArgs at;
+          at.qkv = d.qkv; at.ld = e->Nqkv; at.pos = d.pos; at.slot = d.slots; at.active = nullptr;
+          at.kc = e->kc; at.vc = e->vc; at.ks = e->ks; at.vs = e->vs; at.layer = l; at.L = e->L;
+          at.H = e->H; at.Hkv = e->Hkv; at.P = e->P; at.M = M; at.cos = e->cosT; at.sin = e->sinT;
+          at.out = d.att;
+          // profile the read side only: no KV append, row p is read as stored
+          at.active = d.stop;  // stop[] is 0 for running rows -> append disabled
+          ce = launch_attn_decode(at, s, false);
+          break;
+        }
+        case 2:
+          g.x_f32 = d.att; g.w = ly.wo; g.w_scale = ly.so; g.N = e->D; g.K = e->Dq; g.out_f32 = d.hid;
+          g.resid = d.hid;
+          ce = launch_gemv(PRO_F32, EPI_RESID, g, s, false);
+          break;
+        case 3:
+          g.x_f32 = d.x; g.gamma = ly.g2; g.w = ly.wgu; g.w_scale = ly.sgu; g.N = 2 * e->F; g.K = e->D;
+          g.out_f32 = d.hid;
+          ce = launch_gemv(PRO_NORM, EPI_SILU, g, s, false);
+          break;
+        case 4:
+          g.x_f32 = d.hid; g.w = ly.wd; g.w_scale = ly.sd; g.N = e->D; g.K = e->F; g.out_f32 = d.att;
+          g.resid = d.att;
+          ce = launch_gemv(PRO_F32, EPI_RESID, g, s, false);
+          break;
+        case 5:
+          g.x_f32 = d.x; g.gamma = e->gfinal; g.w = e->wlm; g.w_scale = e->slm; g.N = e->V; g.K = e->D;
+          g.am_partial = d.am_partial; g.am_counter = d.am_counter; g.am_token = d.argmax;
+          ce = launch_gemv(PRO_NORM, EPI_ARGMAX, g, s, false);
+          break;
+      }
+      if (ce != cudaSuccess) {
+        g_last_error = cudaGetErrorString(ce);
+        result = TL_ERR_CUDA;
+        break;
+      }
+      TL_CU(cudaEventRecord(ev[2 * it + 1], s));
+    }
+    if (result != TL_OK) break;
+    TL_CU(cudaStreamSynchronize(s));
+    double tot = 0.0;
+    for (uint32_t it = 0; it < iters; ++it) {
+      float ms = 0.f;
+      TL_CU(cudaEventElapsedTime(&ms, ev[2 * it], ev[2 * it + 1]));
+      tot += ms;
+    }
+    avg_ms_out[kind] = static_cast<float>(tot / iters);
+  }
+  for (auto& x : ev) cudaEventDestroy(x);
+  cudaFreeAsync(flush, s);
+  cudaStreamSynchronize(s);
+  return result;
+}
+
+int32_t tl_decode_step_kernel_count(tl_engine* e) { return e ? 1 + 5 * e->L + 2 : 0; }
+
+void* tl_engine_stream(tl_engine* e) { return e ? static_cast<void*>(e->stream) : nullptr; }
+
+}  // extern "C"

@@ -1,0 +1,990 @@
+// kernels.cu -- sm_100a CUDA-core kernels of the TinyLlama INT8 hot path.
+//
+//  * gemv_kernel: the decode-path INT8 GEMV (M <= 8 rows per CTA row block),
+//    128-bit streaming weight loads, dp4a, warp-shuffle reduction, with a
+//    fused activation prologue (RMSNorm + per-row INT8 quantization) and fused
+//    epilogues (dequant, residual add, SiLU*up, Q16.16 requant, LM-head
+//    argmax). Reference units: shared_gemm_engine.sv:127-168,
+//    requantize_unit.sv:39-93, residual_add.sv:92-96, elementwise_mul.sv:112-119,
+//    argmax_reduction.sv:47-131; numerics of quantized_linear
+//    (model/tinyllama_gemm_int8.py:59-88).
+//  * attn_decode_kernel: GQA decode attention over the INT8 KV cache with the
+//    new row's RoPE, quantization and in-place append fused in
+//    (rope_unit.sv, causal_mask_unit.sv:49-54, gqa_router.sv:25-31,
+//    kv_cache_manager.sv:43-47).
+//  * prefill helpers: RMSNorm rows, quantize rows, RoPE + KV calibration, KV
+//    write, causal attention.
+#include <cfloat>
+#include <cmath>
+#include <cstdio>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace tl {
+
+// ============================================================== RMSNorm row
+// Leaf of NumPy's pairwise sum over squares v[i]*v[i]; called by all 32 lanes
+// of a warp together (8-lane groups, one leaf per group).
+TL_DEV float pw_leaf_sq(const float* v, int n, int j) {
+  const unsigned full_mask = 0xffffffffu;
+  const bool big = n >= 8;
+  const int full = n - (n % 8);
+  float r = 0.0f;
+  if (big) {
+    r = __fmul_rn(v[j], v[j]);
+    for (int i = 8 + j; i < full; i += 8) r = __fadd_rn(r, __fmul_rn(v[i], v[i]));
+  }
+  float r1 = __shfl_down_sync(full_mask, r, 1, 8);
+  float s01 = __fadd_rn(r, r1);
+  float s23 = __shfl_down_sync(full_mask, s01, 2, 8);
+  float s0123 = __fadd_rn(s01, s23);
+  float s4567 = __shfl_down_sync(full_mask, s0123, 4, 8);
+  float res = __fadd_rn(s0123, s4567);
+  if (j == 0) {
+    if (big) {
+      for (int i = full; i < n; ++i) res = __fadd_rn(res, __fmul_rn(v[i], v[i]));
+    } else {
+      res = 0.0f;
+      for (int i = 0; i < n; ++i) res = __fadd_rn(res, __fmul_rn(v[i], v[i]));
+    }
+  }
+  return res;
+}
+
+struct RowScratch {
+  PwPlan plan;
+  float leaf[kPwMaxLeaves];
+  float red[32];
+  double d;
+};
+
+// In-place RMSNorm of buf[0..K) by the whole block (blockDim multiple of 32):
+// buf = (buf * (1/sqrt(mean(buf^2) + eps))) * gamma  (model/tinyllama.py:45-50).
+// rs.plan must hold the leaf plan for K.
+TL_DEV void block_rmsnorm(float* buf, int K, const float* gamma, float eps, RowScratch& rs) {
+  const int tid = threadIdx.x;
+  const int groups = blockDim.x / 8;
+  for (int base = 0; base < rs.plan.n_leaves; base += groups) {
+    int l = base + tid / 8;
+    bool ok = l < rs.plan.n_leaves;
+    float s = pw_leaf_sq(buf + (ok ? rs.plan.start[l] : 0), ok ? rs.plan.len[l] : 0, tid & 7);
+    if (ok && (tid & 7) == 0) rs.leaf[l] = s;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int idx = 0;
+    float tot = pw_fold_rec(rs.leaf, idx, K);
+    float mean = __fdiv_rn(tot, static_cast<float>(K));
+    float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    rs.red[0] = inv;
+  }
+  __syncthreads();
+  const float inv = rs.red[0];
+  for (int i = tid; i < K; i += blockDim.x) buf[i] = __fmul_rn(__fmul_rn(buf[i], inv), gamma[i]);
+  __syncthreads();
+}
+
+TL_DEV float block_absmax(const float* buf, int K, RowScratch& rs) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float m = 0.0f;
+  for (int i = tid; i < K; i += blockDim.x) m = fmaxf(m, fabsf(buf[i]));
+  m = warp_max(m);
+  if (lane == 0) rs.red[warp] = m;
+  __syncthreads();
+  if (warp == 0) {
+    float v = lane < (int)(blockDim.x >> 5) ? rs.red[lane] : 0.0f;
+    v = warp_max(v);
+    if (lane == 0) rs.red[0] = v;
+  }
+  __syncthreads();
+  float r = rs.red[0];
+  __syncthreads();
+  return r;
+}
+
+// ================================================================ the GEMV
+constexpr int kGemvThreads = 256;
+constexpr int kGemvWarps = kGemvThreads / 32;
+constexpr int kGemvRW = 2;   // weight rows per warp
+constexpr int kGemvU = 4;    // 16-byte chunks per lane per row in flight
+
+TL_DEV unsigned long long argmax_key(float v, int idx) {
+  unsigned int b = __float_as_uint(v);
+  unsigned int ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return (static_cast<unsigned long long>(ord) << 32) |
+         static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<unsigned int>(idx));
+}
+TL_DEV int argmax_key_index(unsigned long long k) {
+  return static_cast<int>(0xFFFFFFFFu - static_cast<unsigned int>(k & 0xFFFFFFFFull));
+}
+
+TL_DEV float silu_mul(float g, float u) {
+  // model/tinyllama.py:159-161: x / (1 + exp(-clip(x, -60, 60))), then * up
+  float c = fminf(fmaxf(g, -60.0f), 60.0f);
+  float den = __fadd_rn(1.0f, expf(-c));
+  return __fmul_rn(__fdiv_rn(g, den), u);
+}
+
+template <int PRO, int EPI, int MR>
+__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int K = a.K, N = a.N, M = a.M;
+  int8_t* xs = reinterpret_cast<int8_t*>(smem);                       // [MR][K]
+  double* sx64 = reinterpret_cast<double*>(smem + MR * K);            // [MR]
+  float* fbuf = reinterpret_cast<float*>(smem + MR * K + 8 * MR);     // [K]
+  RowScratch* rs = reinterpret_cast<RowScratch*>(fbuf + K);
+  unsigned long long* am = reinterpret_cast<unsigned long long*>(rs + 1);  // [warps][MR]
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int m0 = blockIdx.y * MR;
+  const int mr = min(MR, M - m0);
+  const int K16 = K >> 4;
+  const int nrow0 = (blockIdx.x * kGemvWarps + warp) * kGemvRW;
+
+  // ---- 1. start streaming this warp's weight rows before anything else
+  const int4* wp[kGemvRW];
+  bool rv[kGemvRW];
+#pragma unroll
+  for (int i = 0; i < kGemvRW; ++i) {
+    rv[i] = nrow0 + i < N;
+    wp[i] = reinterpret_cast<const int4*>(a.w + static_cast<size_t>(rv[i] ? nrow0 + i : 0) * K);
+  }
+  int4 wv[kGemvU][kGemvRW];
+  auto load_chunk = [&](int cbase) {
+#pragma unroll
+    for (int u = 0; u < kGemvU; ++u) {
+      const int c = cbase + lane + 32 * u;
+#pragma unroll
+      for (int i = 0; i < kGemvRW; ++i)
+        wv[u][i] = (rv[i] && c < K16) ? ld_stream_v4(wp[i] + c) : make_int4(0, 0, 0, 0);
+    }
+  };
+  load_chunk(0);
+
+  // ---- 2. activation prologue (depends on the previous kernel)
+  pdl_wait();
+  if (PRO == PRO_NORM && tid == 0) {
+    rs->plan.n_leaves = 0;
+    pw_plan_rec(rs->plan, 0, K);
+  }
+  if (PRO == PRO_Q8) {
+    for (int r = 0; r < MR; ++r) {
+      int4* dst = reinterpret_cast<int4*>(xs + r * K);
+      if (r < mr) {
+        const int4* src = reinterpret_cast<const int4*>(a.x_q + static_cast<size_t>(m0 + r) * K);
+        for (int c = tid; c < K16; c += kGemvThreads) dst[c] = src[c];
+      } else {
+        for (int c = tid; c < K16; c += kGemvThreads) dst[c] = make_int4(0, 0, 0, 0);
+      }
+      if (tid == 0)
+        sx64[r] = quant_scale64((r < mr && a.in_absmax) ? a.in_absmax[(m0 + r) / a.rows_per_group] : 0.0f);
+    }
+  } else {
+    __syncthreads();
+    for (int r = 0; r < MR; ++r) {
+      if (r >= mr) {
+        int4* dst = reinterpret_cast<int4*>(xs + r * K);
+        for (int c = tid; c < K16; c += kGemvThreads) dst[c] = make_int4(0, 0, 0, 0);
+        if (tid == 0) sx64[r] = 1.0;
+        continue;
+      }
+      const float* src =
+          a.x_f32 + (static_cast<size_t>(a.x_row_offset) + static_cast<size_t>(m0 + r) * a.x_row_step) * K;
+      for (int i = tid; i < K; i += kGemvThreads) fbuf[i] = src[i];
+      __syncthreads();
+      if (PRO == PRO_NORM) block_rmsnorm(fbuf, K, a.gamma, a.eps, *rs);
+      float amax;
+      if (PRO == PRO_F32_GIVEN) amax = a.in_absmax[(m0 + r) / a.rows_per_group];
+      else amax = block_absmax(fbuf, K, *rs);
+      const double s64 = quant_scale64(amax);
+      const float sf = static_cast<float>(s64);
+      int8_t* dst = xs + r * K;
+      for (int i = tid; i < K; i += kGemvThreads) dst[i] = static_cast<int8_t>(quantize_one(fbuf[i], sf));
+      if (tid == 0) sx64[r] = s64;
+      __syncthreads();
+    }
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  // ---- 3. dot products
+  int acc[kGemvRW][MR];
+#pragma unroll
+  for (int i = 0; i < kGemvRW; ++i)
+#pragma unroll
+    for (int m = 0; m < MR; ++m) acc[i][m] = 0;
+
+  for (int cbase = 0; cbase < K16; cbase += 32 * kGemvU) {
+    if (cbase) load_chunk(cbase);
+#pragma unroll
+    for (int u = 0; u < kGemvU; ++u) {
+      const int c = cbase + lane + 32 * u;
+      if (c < K16) {
+#pragma unroll
+        for (int m = 0; m < MR; ++m) {
+          const int4 xv = reinterpret_cast<const int4*>(xs + m * K)[c];
+#pragma unroll
+          for (int i = 0; i < kGemvRW; ++i) {
+            int t = acc[i][m];
+            t = dp4a(wv[u][i].x, xv.x, t);
+            t = dp4a(wv[u][i].y, xv.y, t);
+            t = dp4a(wv[u][i].z, xv.z, t);
+            t = dp4a(wv[u][i].w, xv.w, t);
+            acc[i][m] = t;
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kGemvRW; ++i)
+#pragma unroll
+    for (int m = 0; m < MR; ++m) acc[i][m] = warp_sum_i(acc[i][m]);
+
+  // ---- 4. epilogue
+  if (EPI == EPI_ARGMAX) {
+    unsigned long long best[MR];
+#pragma unroll
+    for (int m = 0; m < MR; ++m) best[m] = 0ull;
+    if (lane == 0) {
+#pragma unroll
+      for (int i = 0; i < kGemvRW; ++i) {
+        const int n = nrow0 + i;
+        if (n >= N) continue;
+        const double sw = a.w_scale[n];
+#pragma unroll
+        for (int m = 0; m < MR; ++m) {
+          if (m >= mr) continue;
+          const float y = dequant(acc[i][m], sx64[m], sw);
+          if (a.logits) a.logits[static_cast<size_t>(m0 + m) * N + n] = y;
+          const unsigned long long k = argmax_key(y, n);
+          best[m] = k > best[m] ? k : best[m];
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < MR; ++m) am[warp * MR + m] = best[m];
+    }
+    __syncthreads();
+    if (tid < mr) {
+      unsigned long long b = 0ull;
+      for (int w = 0; w < kGemvWarps; ++w) b = am[w * MR + tid] > b ? am[w * MR + tid] : b;
+      a.am_partial[static_cast<size_t>(blockIdx.x) * M + m0 + tid] = b;
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ int is_last;
+    if (tid == 0) {
+      unsigned int prev = atomicAdd(a.am_counter + blockIdx.y, 1u);
+      is_last = (prev == gridDim.x - 1);
+    }
+    __syncthreads();
+    if (is_last) {
+      __threadfence();
+      if (tid < mr) {
+        unsigned long long b = 0ull;
+        for (unsigned int bx = 0; bx < gridDim.x; ++bx) {
+          const unsigned long long v =
+              *reinterpret_cast<volatile unsigned long long*>(a.am_partial + static_cast<size_t>(bx) * M + m0 + tid);
+          b = v > b ? v : b;
+        }
+        a.am_token[m0 + tid] = argmax_key_index(b);
+      }
+      if (tid == 0) a.am_counter[blockIdx.y] = 0u;
+    }
+    return;
+  }
+
+  if (lane != 0) return;
+  if (EPI == EPI_SILU) {
+    const int n = nrow0;  // even: (gate_j, up_j) rows
+    if (n >= N) return;
+    const int j = n >> 1;
+    const int Nh = N >> 1;
+    const double sg = a.w_scale[n], su = a.w_scale[n + 1];
+    float local_max = 0.0f;
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+      if (m >= mr) continue;
+      const float g = dequant(acc[0][m], sx64[m], sg);
+      const float u = dequant(acc[1][m], sx64[m], su);
+      const float hv = silu_mul(g, u);
+      a.out_f32[static_cast<size_t>(m0 + m) * Nh + j] = hv;
+      if (a.out_absmax) atomic_max_nonneg(a.out_absmax + (m0 + m) / a.rows_per_group, fabsf(hv));
+      (void)local_max;
+    }
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < kGemvRW; ++i) {
+    const int n = nrow0 + i;
+    if (n >= N) continue;
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+      if (m >= mr) continue;
+      const size_t o = static_cast<size_t>(m0 + m) * N + n;
+      if (EPI == EPI_I32) {
+        a.out_i32[o] = acc[i][m];
+      } else if (EPI == EPI_REQ) {
+        const uint32_t sc = a.req_scale[a.req_per_col ? n : 0];
+        a.out_i8[o] = static_cast<int8_t>(requant_q16(acc[i][m], sc, a.req_nonneg != 0));
+      } else {
+        const float y = dequant(acc[i][m], sx64[m], a.w_scale[n]);
+        const float v = (EPI == EPI_RESID) ? __fadd_rn(a.resid[o], y) : y;
+        a.out_f32[o] = v;
+        if (EPI == EPI_F32 && a.out_absmax)
+          atomic_max_nonneg(a.out_absmax + (m0 + m) / a.rows_per_group, fabsf(v));
+      }
+    }
+  }
+}
+
+static size_t gemv_smem_bytes(int MR, int K) {
+  return static_cast<size_t>(MR) * K + 8 * MR + 4 * static_cast<size_t>(K) + sizeof(RowScratch) +
+         8 * kGemvWarps * MR + 64;
+}
+
+size_t gemv_argmax_partials(int M, int N) {
+  const int rows_per_cta = kGemvWarps * kGemvRW;
+  return static_cast<size_t>((N + rows_per_cta - 1) / rows_per_cta) * M;
+}
+int gemv_argmax_row_blocks(int M) { return (M + 7) / 8; }
+
+template <int PRO, int EPI, int MR>
+static cudaError_t launch_gemv_t(const GemvArgs& a, cudaStream_t s, bool pdl) {
+  const size_t smem = gemv_smem_bytes(MR, a.K);
+  auto kfn = gemv_kernel<PRO, EPI, MR>;
+  const int rows_per_cta = kGemvWarps * kGemvRW;
+  dim3 grid((a.N + rows_per_cta - 1) / rows_per_cta, (a.M + MR - 1) / MR);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kGemvThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kfn, a);
+}
+
+template <int PRO, int EPI, int MR>
+static cudaError_t prepare_gemv_t(int max_k) {
+  return cudaFuncSetAttribute(gemv_kernel<PRO, EPI, MR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(gemv_smem_bytes(MR, max_k)));
+}
+
+template <int PRO, int EPI>
+static cudaError_t launch_gemv_mr(const GemvArgs& a, cudaStream_t s, bool pdl) {
+  if (a.M <= 1) return launch_gemv_t<PRO, EPI, 1>(a, s, pdl);
+  if (a.M <= 2) return launch_gemv_t<PRO, EPI, 2>(a, s, pdl);
+  if (a.M <= 4) return launch_gemv_t<PRO, EPI, 4>(a, s, pdl);
+  return launch_gemv_t<PRO, EPI, 8>(a, s, pdl);
+}
+
+template <int PRO, int EPI>
+static cudaError_t prepare_gemv_mr(int max_k) {
+  cudaError_t e;
+  if ((e = prepare_gemv_t<PRO, EPI, 1>(max_k)) != cudaSuccess) return e;
+  if ((e = prepare_gemv_t<PRO, EPI, 2>(max_k)) != cudaSuccess) return e;
+  if ((e = prepare_gemv_t<PRO, EPI, 4>(max_k)) != cudaSuccess) return e;
+  return prepare_gemv_t<PRO, EPI, 8>(max_k);
+}
+
+#define TL_GEMV_VARIANTS(X)        \
+  X(PRO_Q8, EPI_I32)               \
+  X(PRO_Q8, EPI_F32)               \
+  X(PRO_Q8, EPI_RESID)             \
+  X(PRO_Q8, EPI_SILU)              \
+  X(PRO_Q8, EPI_REQ)               \
+  X(PRO_NORM, EPI_F32)             \
+  X(PRO_NORM, EPI_SILU)            \
+  X(PRO_NORM, EPI_ARGMAX)          \
+  X(PRO_F32, EPI_RESID)            \
+  X(PRO_F32, EPI_F32)              \
+  X(PRO_F32_GIVEN, EPI_ARGMAX)
+
+cudaError_t launch_gemv(int pro, int epi, const GemvArgs& a, cudaStream_t s, bool pdl) {
+  if (a.K % 16 != 0 || a.K <= 0 || a.N <= 0 || a.M <= 0) return cudaErrorInvalidValue;
+  if (epi == EPI_SILU && (a.N % 2 != 0)) return cudaErrorInvalidValue;
+#define TL_GEMV_CASE(P, E) \
+  if (pro == P && epi == E) return launch_gemv_mr<P, E>(a, s, pdl);
+  TL_GEMV_VARIANTS(TL_GEMV_CASE)
+#undef TL_GEMV_CASE
+  return cudaErrorInvalidValue;
+}
+
+static size_t rmsnorm_rows_smem(int D);
+__global__ void rmsnorm_rows_kernel(const float*, const float*, float, float*, float*, int, int);
+
+cudaError_t prepare_kernels(int max_k) {
+  static int prepared_k[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (max_k <= prepared_k[dev]) return cudaSuccess;
+#define TL_GEMV_PREP(P, E) \
+  if ((e = prepare_gemv_mr<P, E>(max_k)) != cudaSuccess) return e;
+  TL_GEMV_VARIANTS(TL_GEMV_PREP)
+#undef TL_GEMV_PREP
+  e = cudaFuncSetAttribute(rmsnorm_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(rmsnorm_rows_smem(max_k)));
+  if (e != cudaSuccess) return e;
+  prepared_k[dev] = max_k;
+  return cudaSuccess;
+}
+
+// ====================================================== decode attention
+// One CTA per (kv head, sequence row); one warp per query head of the group.
+template <int G>
+__global__ void __launch_bounds__(32 * G) attn_decode_kernel(AttnDecodeArgs a) {
+  constexpr int CH = 128;
+  constexpr int KSTRIDE = 68;  // 17 words: conflict-free per-lane row reads
+  __shared__ __align__(16) int8_t k_sm[CH * KSTRIDE];
+  __shared__ __align__(16) int8_t v_sm[CH * 64];
+  __shared__ float q_sm[G][64];
+  __shared__ float p_sm[G][CH];
+  const int h = blockIdx.x, m = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int Dq = a.H * 64;
+  pdl_wait();
+  const int p = a.pos[m];
+  float* out = a.out + static_cast<size_t>(m) * Dq + (h * G + warp) * 64;
+  if (p < 0 || p >= a.P) {
+    out[lane] = 0.0f;
+    out[lane + 32] = 0.0f;
+    return;
+  }
+  const int slot = a.slot[m];
+  const bool act = a.active ? (a.active[m] != 0) : true;
+  const size_t sidx = (static_cast<size_t>(slot) * a.L + a.layer) * a.Hkv + h;
+  const float sK = a.ks[sidx], sV = a.vs[sidx];
+  int8_t* kbase = a.kc + sidx * static_cast<size_t>(a.P) * 64;
+  int8_t* vbase = a.vc + sidx * static_cast<size_t>(a.P) * 64;
+  const float* row = a.qkv + static_cast<size_t>(m) * a.ld;
+  const float* cs = a.cos + static_cast<size_t>(p) * 64;
+  const float* sn = a.sin + static_cast<size_t>(p) * 64;
+
+  if (warp == 0 && act) {
+    // new K row: RoPE (model/tinyllama.py:74-80), quantize with the frozen
+    // per-(layer, kv head) scale, append at position p.
+    const float* kr = row + Dq + h * 64;
+    const float* vr = row + Dq + a.Hkv * 64 + h * 64;
+    const float k0 = kr[lane], k1 = kr[lane + 32];
+    const float r0 = __fadd_rn(__fmul_rn(k0, cs[lane]), __fmul_rn(-k1, sn[lane]));
+    const float r1 = __fadd_rn(__fmul_rn(k1, cs[lane + 32]), __fmul_rn(k0, sn[lane + 32]));
+    kbase[static_cast<size_t>(p) * 64 + lane] = static_cast<int8_t>(quantize_one(r0, sK));
+    kbase[static_cast<size_t>(p) * 64 + lane + 32] = static_cast<int8_t>(quantize_one(r1, sK));
+    vbase[static_cast<size_t>(p) * 64 + lane] = static_cast<int8_t>(quantize_one(vr[lane], sV));
+    vbase[static_cast<size_t>(p) * 64 + lane + 32] = static_cast<int8_t>(quantize_one(vr[lane + 32], sV));
+  }
+  {
+    const float* qr = row + (h * G + warp) * 64;
+    const float q0 = qr[lane], q1 = qr[lane + 32];
+    q_sm[warp][lane] = __fadd_rn(__fmul_rn(q0, cs[lane]), __fmul_rn(-q1, sn[lane]));
+    q_sm[warp][lane + 32] = __fadd_rn(__fmul_rn(q1, cs[lane + 32]), __fmul_rn(q0, sn[lane + 32]));
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  const float score_scale = sK * 0.125f;
+  float m_run = -INFINITY, l_run = 0.0f, acc0 = 0.0f, acc1 = 0.0f;
+  const int ntot = p + 1;
+  for (int t0 = 0; t0 < ntot; t0 += CH) {
+    const int n = min(CH, ntot - t0);
+    for (int wi = tid; wi < n * 16; wi += 32 * G) {
+      const int r = wi >> 4, c = wi & 15;
+      reinterpret_cast<int*>(k_sm + r * KSTRIDE)[c] =
+          reinterpret_cast<const int*>(kbase + static_cast<size_t>(t0 + r) * 64)[c];
+    }
+    for (int wi = tid; wi < n * 4; wi += 32 * G) {
+      const int r = wi >> 2, c = wi & 3;
+      reinterpret_cast<int4*>(v_sm + r * 64)[c] =
+          reinterpret_cast<const int4*>(vbase + static_cast<size_t>(t0 + r) * 64)[c];
+    }
+    __syncthreads();
+    float cmax = -INFINITY;
+    for (int tt = lane; tt < n; tt += 32) {
+      const int* kw = reinterpret_cast<const int*>(k_sm + tt * KSTRIDE);
+      float s = 0.0f;
+#pragma unroll
+      for (int w4 = 0; w4 < 16; ++w4) {
+        const int v = kw[w4];
+        s += static_cast<float>(static_cast<int8_t>(v & 0xff)) * q_sm[warp][4 * w4];
+        s += static_cast<float>(static_cast<int8_t>((v >> 8) & 0xff)) * q_sm[warp][4 * w4 + 1];
+        s += static_cast<float>(static_cast<int8_t>((v >> 16) & 0xff)) * q_sm[warp][4 * w4 + 2];
+        s += static_cast<float>(static_cast<int8_t>((v >> 24) & 0xff)) * q_sm[warp][4 * w4 + 3];
+      }
+      s *= score_scale;
+      p_sm[warp][tt] = s;
+      cmax = fmaxf(cmax, s);
+    }
+    cmax = warp_max(cmax);
+    const float m_new = fmaxf(m_run, cmax);
+    const float corr = expf(m_run - m_new);
+    l_run *= corr;
+    acc0 *= corr;
+    acc1 *= corr;
+    __syncwarp();
+    float lsum = 0.0f;
+    for (int tt = lane; tt < n; tt += 32) {
+      const float e = expf(p_sm[warp][tt] - m_new);
+      p_sm[warp][tt] = e;
+      lsum += e;
+    }
+    l_run += warp_sum(lsum);
+    m_run = m_new;
+    __syncwarp();
+    for (int tt = 0; tt < n; ++tt) {
+      const float e = p_sm[warp][tt];
+      acc0 += e * static_cast<float>(v_sm[tt * 64 + lane]);
+      acc1 += e * static_cast<float>(v_sm[tt * 64 + lane + 32]);
+    }
+    __syncthreads();
+  }
+  const float inv = sV / l_run;
+  out[lane] = acc0 * inv;
+  out[lane + 32] = acc1 * inv;
+}
+
+cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) {
+  const int G = a.H / a.Hkv;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.Hkv, a.M);
+  cfg.blockDim = dim3(32 * G);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  switch (G) {
+    case 1: return cudaLaunchKernelEx(&cfg, attn_decode_kernel<1>, a);
+    case 2: return cudaLaunchKernelEx(&cfg, attn_decode_kernel<2>, a);
+    case 4: return cudaLaunchKernelEx(&cfg, attn_decode_kernel<4>, a);
+    case 8: return cudaLaunchKernelEx(&cfg, attn_decode_kernel<8>, a);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// ================================================================= prefill
+__global__ void embed_kernel(const float* table, const int* ids, float* x, int D, int vocab) {
+  pdl_wait();
+  const int r = blockIdx.x;
+  int id = ids[r];
+  id = id < 0 ? 0 : (id >= vocab ? vocab - 1 : id);
+  const float4* src = reinterpret_cast<const float4*>(table + static_cast<size_t>(id) * D);
+  float4* dst = reinterpret_cast<float4*>(x + static_cast<size_t>(r) * D);
+  for (int i = threadIdx.x; i < D / 4; i += blockDim.x) dst[i] = src[i];
+  pdl_launch_dependents();
+}
+
+cudaError_t launch_embed(const float* table, const int* ids, float* x, int rows, int D, int vocab,
+                         cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(rows);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, embed_kernel, table, ids, x, D, vocab);
+}
+
+static size_t rmsnorm_rows_smem(int D) { return 4 * static_cast<size_t>(D) + sizeof(RowScratch) + 16; }
+
+__global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float* x, const float* gamma,
+                                                           float eps, float* out, float* absmax,
+                                                           int D, int rows_per_group) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* buf = reinterpret_cast<float*>(smem);
+  RowScratch* rs = reinterpret_cast<RowScratch*>(buf + D);
+  const int r = blockIdx.x;
+  if (threadIdx.x == 0) {
+    rs->plan.n_leaves = 0;
+    pw_plan_rec(rs->plan, 0, D);
+  }
+  const float* src = x + static_cast<size_t>(r) * D;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) buf[i] = src[i];
+  __syncthreads();
+  block_rmsnorm(buf, D, gamma, eps, *rs);
+  float* dst = out + static_cast<size_t>(r) * D;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) dst[i] = buf[i];
+  if (absmax) {
+    const float m = block_absmax(buf, D, *rs);
+    if (threadIdx.x == 0) atomic_max_nonneg(absmax + r / rows_per_group, m);
+  }
+}
+
+cudaError_t launch_rmsnorm_rows(const float* x, const float* gamma, float eps, float* out,
+                                float* absmax_groups, int rows, int D, int rows_per_group,
+                                cudaStream_t s) {
+  const size_t smem = rmsnorm_rows_smem(D);
+  rmsnorm_rows_kernel<<<rows, 256, smem, s>>>(x, gamma, eps, out, absmax_groups, D, rows_per_group);
+  return cudaGetLastError();
+}
+
+__global__ void absmax_rows_kernel(const float* x, int K, int rows_per_group, float* absmax) {
+  const int r = blockIdx.x;
+  const float* src = x + static_cast<size_t>(r) * K;
+  float m = 0.0f;
+  for (int i = threadIdx.x; i < K; i += blockDim.x) m = fmaxf(m, fabsf(src[i]));
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) atomic_max_nonneg(absmax + r / rows_per_group, m);
+}
+
+cudaError_t launch_absmax_rows(const float* x, int rows, int K, int rows_per_group, float* absmax,
+                               cudaStream_t s) {
+  absmax_rows_kernel<<<rows, 256, 0, s>>>(x, K, rows_per_group, absmax);
+  return cudaGetLastError();
+}
+
+__global__ void quantize_rows_kernel(const float* x, const float* absmax, int K, int rows_per_group,
+                                     int8_t* out) {
+  const int r = blockIdx.x;
+  const float sf = static_cast<float>(quant_scale64(absmax[r / rows_per_group]));
+  const float* src = x + static_cast<size_t>(r) * K;
+  int8_t* dst = out + static_cast<size_t>(r) * K;
+  for (int i = threadIdx.x; i < K; i += blockDim.x) dst[i] = static_cast<int8_t>(quantize_one(src[i], sf));
+}
+
+cudaError_t launch_quantize_rows(const float* x, const float* absmax_groups, int rows, int K,
+                                 int rows_per_group, int8_t* out, cudaStream_t s) {
+  quantize_rows_kernel<<<rows, 256, 0, s>>>(x, absmax_groups, K, rows_per_group, out);
+  return cudaGetLastError();
+}
+
+// RoPE in place on all q and k heads of one row; absmax of rotated K and of V
+// per (sequence, kv head). One warp per head, lane = pair index.
+__global__ void rope_prefill_kernel(float* qkv, int ld, int seq_len, int H, int Hkv,
+                                    const float* cos, const float* sin, float* kv_absmax) {
+  const int r = blockIdx.x;
+  const int t = r % seq_len, seq = r / seq_len;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  float* row = qkv + static_cast<size_t>(r) * ld;
+  const float* cs = cos + static_cast<size_t>(t) * 64;
+  const float* sn = sin + static_cast<size_t>(t) * 64;
+  for (int hh = warp; hh < H + 2 * Hkv; hh += nw) {
+    if (hh < H + Hkv) {
+      float* x = row + hh * 64;  // q heads then k heads are contiguous
+      const float a0 = x[lane], a1 = x[lane + 32];
+      const float r0 = __fadd_rn(__fmul_rn(a0, cs[lane]), __fmul_rn(-a1, sn[lane]));
+      const float r1 = __fadd_rn(__fmul_rn(a1, cs[lane + 32]), __fmul_rn(a0, sn[lane + 32]));
+      x[lane] = r0;
+      x[lane + 32] = r1;
+      if (hh >= H) {
+        const float m = warp_max(fmaxf(fabsf(r0), fabsf(r1)));
+        if (lane == 0) atomic_max_nonneg(kv_absmax + (seq * 2 + 0) * Hkv + (hh - H), m);
+      }
+    } else {
+      const int vh = hh - H - Hkv;
+      const float* x = row + (H + Hkv) * 64 + vh * 64;
+      const float m = warp_max(fmaxf(fabsf(x[lane]), fabsf(x[lane + 32])));
+      if (lane == 0) atomic_max_nonneg(kv_absmax + (seq * 2 + 1) * Hkv + vh, m);
+    }
+  }
+}
+
+cudaError_t launch_rope_prefill(float* qkv, int ld, int rows, int seq_len, int H, int Hkv,
+                                const float* cos, const float* sin, float* kv_absmax,
+                                cudaStream_t s) {
+  rope_prefill_kernel<<<rows, 256, 0, s>>>(qkv, ld, seq_len, H, Hkv, cos, sin, kv_absmax);
+  return cudaGetLastError();
+}
+
+__global__ void kv_write_prefill_kernel(const float* qkv, int ld, int seq_len, int H, int Hkv,
+                                        const float* kv_absmax, int8_t* kc, int8_t* vc, float* ks,
+                                        float* vs, int slot_base, int layer, int L, int P) {
+  const int r = blockIdx.x;
+  const int t = r % seq_len, seq = r / seq_len;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const float* row = qkv + static_cast<size_t>(r) * ld;
+  for (int hh = warp; hh < 2 * Hkv; hh += nw) {
+    const int kind = hh / Hkv, h = hh % Hkv;  // 0 = K, 1 = V
+    const double s64 = quant_scale64(kv_absmax[(seq * 2 + kind) * Hkv + h]);
+    const float sf = static_cast<float>(s64);
+    const float* x = row + (H + kind * Hkv + h) * 64;
+    const size_t sidx = (static_cast<size_t>(slot_base + seq) * L + layer) * Hkv + h;
+    int8_t* dst = (kind == 0 ? kc : vc) + (sidx * P + t) * 64;
+    dst[lane] = static_cast<int8_t>(quantize_one(x[lane], sf));
+    dst[lane + 32] = static_cast<int8_t>(quantize_one(x[lane + 32], sf));
+    if (t == 0 && lane == 0) (kind == 0 ? ks : vs)[sidx] = sf;
+  }
+}
+
+cudaError_t launch_kv_write_prefill(const float* qkv, int ld, int rows, int seq_len, int H,
+                                    int Hkv, const float* kv_absmax, int8_t* kc, int8_t* vc,
+                                    float* ks, float* vs, int slot_base, int layer, int L, int P,
+                                    cudaStream_t s) {
+  kv_write_prefill_kernel<<<rows, 256, 0, s>>>(qkv, ld, seq_len, H, Hkv, kv_absmax, kc, vc, ks, vs,
+                                               slot_base, layer, L, P);
+  return cudaGetLastError();
+}
+
+// Causal prefill attention on CUDA cores: CTA = (head, 16-query tile, seq),
+// 4 warps x 4 query rows, keys streamed in 64-row chunks through shared memory.
+__global__ void __launch_bounds__(128) attn_prefill_kernel(
+    const float* qkv, int ld, int seq_len, int H, int Hkv, const int8_t* kc, const int8_t* vc,
+    const float* ks, const float* vs, int slot_base, int layer, int L, int P, float* out,
+    float* out_absmax) {
+  constexpr int QT = 16, RPW = 4, CH = 64, KSTRIDE = 68;
+  __shared__ __align__(16) int8_t k_sm[CH * KSTRIDE];
+  __shared__ __align__(16) int8_t v_sm[CH * 64];
+  __shared__ float q_sm[QT][64];
+  __shared__ float p_sm[4][RPW][CH];
+  const int g = blockIdx.x, qt0 = blockIdx.y * QT, seq = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = H / Hkv, h = g / G;
+  const int Dq = H * 64;
+  const size_t sidx = (static_cast<size_t>(slot_base + seq) * L + layer) * Hkv + h;
+  const float sK = ks[sidx], sV = vs[sidx];
+  const int8_t* kbase = kc + sidx * static_cast<size_t>(P) * 64;
+  const int8_t* vbase = vc + sidx * static_cast<size_t>(P) * 64;
+  for (int i = tid; i < QT * 64; i += 128) {
+    const int qi = i >> 6, d = i & 63;
+    const int t = qt0 + qi;
+    q_sm[qi][d] = t < seq_len ? qkv[static_cast<size_t>(seq * seq_len + t) * ld + g * 64 + d] : 0.0f;
+  }
+  float m_run[RPW], l_run[RPW], acc0[RPW], acc1[RPW];
+#pragma unroll
+  for (int i = 0; i < RPW; ++i) {
+    m_run[i] = -INFINITY;
+    l_run[i] = 0.0f;
+    acc0[i] = 0.0f;
+    acc1[i] = 0.0f;
+  }
+  const float score_scale = sK * 0.125f;
+  const int last_q = min(qt0 + QT, seq_len) - 1;
+  __syncthreads();
+  for (int t0 = 0; t0 <= last_q; t0 += CH) {
+    const int n = min(CH, last_q + 1 - t0);
+    for (int wi = tid; wi < n * 16; wi += 128) {
+      const int r = wi >> 4, c = wi & 15;
+      reinterpret_cast<int*>(k_sm + r * KSTRIDE)[c] =
+          reinterpret_cast<const int*>(kbase + static_cast<size_t>(t0 + r) * 64)[c];
+    }
+    for (int wi = tid; wi < n * 4; wi += 128) {
+      const int r = wi >> 2, c = wi & 3;
+      reinterpret_cast<int4*>(v_sm + r * 64)[c] =
+          reinterpret_cast<const int4*>(vbase + static_cast<size_t>(t0 + r) * 64)[c];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+      const int qi = warp * RPW + i;
+      const int tq = qt0 + qi;
+      float cmax = -INFINITY;
+      for (int tt = lane; tt < CH; tt += 32) {
+        float s = -INFINITY;
+        if (tt < n && t0 + tt <= tq) {
+          const int* kw = reinterpret_cast<const int*>(k_sm + tt * KSTRIDE);
+          float a = 0.0f;
+#pragma unroll
+          for (int w4 = 0; w4 < 16; ++w4) {
+            const int v = kw[w4];
+            a += static_cast<float>(static_cast<int8_t>(v & 0xff)) * q_sm[qi][4 * w4];
+            a += static_cast<float>(static_cast<int8_t>((v >> 8) & 0xff)) * q_sm[qi][4 * w4 + 1];
+            a += static_cast<float>(static_cast<int8_t>((v >> 16) & 0xff)) * q_sm[qi][4 * w4 + 2];
+            a += static_cast<float>(static_cast<int8_t>((v >> 24) & 0xff)) * q_sm[qi][4 * w4 + 3];
+          }
+          s = a * score_scale;
+        }
+        p_sm[warp][i][tt] = s;
+        cmax = fmaxf(cmax, s);
+      }
+      cmax = warp_max(cmax);
+      if (cmax == -INFINITY) continue;  // no visible key in this chunk (tq < t0)
+      const float m_new = fmaxf(m_run[i], cmax);
+      const float corr = expf(m_run[i] - m_new);
+      l_run[i] *= corr;
+      acc0[i] *= corr;
+      acc1[i] *= corr;
+      __syncwarp();
+      float lsum = 0.0f;
+      for (int tt = lane; tt < CH; tt += 32) {
+        const float e = expf(p_sm[warp][i][tt] - m_new);
+        p_sm[warp][i][tt] = e;
+        lsum += e;
+      }
+      l_run[i] += warp_sum(lsum);
+      m_run[i] = m_new;
+      __syncwarp();
+      for (int tt = 0; tt < n; ++tt) {
+        const float e = p_sm[warp][i][tt];
+        acc0[i] += e * static_cast<float>(v_sm[tt * 64 + lane]);
+        acc1[i] += e * static_cast<float>(v_sm[tt * 64 + lane + 32]);
+      }
+    }
+    __syncthreads();
+  }
+  float local_max = 0.0f;
+#pragma unroll
+  for (int i = 0; i < RPW; ++i) {
+    const int tq = qt0 + warp * RPW + i;
+    if (tq >= seq_len) continue;
+    const float inv = sV / l_run[i];
+    const float o0 = acc0[i] * inv, o1 = acc1[i] * inv;
+    float* o = out + static_cast<size_t>(seq * seq_len + tq) * Dq + g * 64;
+    o[lane] = o0;
+    o[lane + 32] = o1;
+    local_max = fmaxf(local_max, fmaxf(fabsf(o0), fabsf(o1)));
+  }
+  if (out_absmax) {
+    local_max = warp_max(local_max);
+    if (lane == 0) atomic_max_nonneg(out_absmax + seq, local_max);
+  }
+}
+
+cudaError_t launch_attn_prefill(const float* qkv, int ld, int rows, int seq_len, int H, int Hkv,
+                                const int8_t* kc, const int8_t* vc, const float* ks,
+                                const float* vs, int slot_base, int layer, int L, int P,
+                                float* out, float* out_absmax, cudaStream_t s) {
+  const int nseq = rows / seq_len;
+  dim3 grid(H, (seq_len + 15) / 16, nseq);
+  attn_prefill_kernel<<<grid, 128, 0, s>>>(qkv, ld, seq_len, H, Hkv, kc, vc, ks, vs, slot_base,
+                                           layer, L, P, out, out_absmax);
+  return cudaGetLastError();
+}
+
+// ==================================================================== misc
+// dst[n * dst_ld + k] = src[k * N + n]
+__global__ void transpose_i8_kernel(const int8_t* src, int8_t* dst, int K, int N, int dst_ld) {
+  __shared__ int8_t tile[32][33];
+  const int n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+  for (int j = ty; j < 32; j += 8) {
+    const int k = k0 + j, n = n0 + tx;
+    tile[j][tx] = (k < K && n < N) ? src[static_cast<size_t>(k) * N + n] : 0;
+  }
+  __syncthreads();
+  for (int j = ty; j < 32; j += 8) {
+    const int n = n0 + j, k = k0 + tx;
+    if (n < N && k < K) dst[static_cast<size_t>(n) * dst_ld + k] = tile[tx][j];
+  }
+}
+
+cudaError_t launch_transpose_i8(const int8_t* src_kn, int8_t* dst_nk, int K, int N, cudaStream_t s) {
+  dim3 grid((N + 31) / 32, (K + 31) / 32);
+  transpose_i8_kernel<<<grid, dim3(32, 8), 0, s>>>(src_kn, dst_nk, K, N, K);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_interleave_gate_up(const int8_t* gate_kn, const int8_t* up_kn, int8_t* dst,
+                                      int K, int F, cudaStream_t s) {
+  dim3 grid((F + 31) / 32, (K + 31) / 32);
+  transpose_i8_kernel<<<grid, dim3(32, 8), 0, s>>>(gate_kn, dst, K, F, 2 * K);
+  transpose_i8_kernel<<<grid, dim3(32, 8), 0, s>>>(up_kn, dst + K, K, F, 2 * K);
+  return cudaGetLastError();
+}
+
+TL_DEV uint64_t splitmix64(uint64_t x) {
+  x += 0x9E3779B97F4A7C15ull;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  return x ^ (x >> 31);
+}
+
+__global__ void random_i8_kernel(int8_t* dst, size_t n, uint64_t seed) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const uint64_t h = splitmix64(seed ^ (i * 0xD1B54A32D192ED03ull));
+    dst[i] = static_cast<int8_t>(static_cast<int>(h % 255ull) - 127);
+  }
+}
+
+__global__ void random_normal_kernel(float* dst, size_t n, float std, uint64_t seed) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const uint64_t h = splitmix64(seed ^ (i * 0xD1B54A32D192ED03ull));
+    const float u1 = (static_cast<float>(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
+    const float u2 = static_cast<float>((h >> 16) & 0xFFFFFFull) * (1.0f / 16777216.0f);
+    dst[i] = std * sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+  }
+}
+
+__global__ void fill_f32_kernel(float* dst, size_t n, float v) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    dst[i] = v;
+}
+__global__ void fill_f64_kernel(double* dst, size_t n, double v) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    dst[i] = v;
+}
+
+cudaError_t launch_random_i8(int8_t* dst, size_t n, uint64_t seed, cudaStream_t s) {
+  random_i8_kernel<<<148 * 8, 256, 0, s>>>(dst, n, seed);
+  return cudaGetLastError();
+}
+cudaError_t launch_random_normal_f32(float* dst, size_t n, float std, uint64_t seed, cudaStream_t s) {
+  random_normal_kernel<<<148 * 8, 256, 0, s>>>(dst, n, std, seed);
+  return cudaGetLastError();
+}
+cudaError_t launch_fill_f32(float* dst, size_t n, float v, cudaStream_t s) {
+  fill_f32_kernel<<<148 * 4, 256, 0, s>>>(dst, n, v);
+  return cudaGetLastError();
+}
+cudaError_t launch_fill_f64(double* dst, size_t n, double v, cudaStream_t s) {
+  fill_f64_kernel<<<148 * 4, 256, 0, s>>>(dst, n, v);
+  return cudaGetLastError();
+}
+
+// Decode-step bookkeeping: emit the argmax token, apply the stop rules of
+// stop_condition_unit.sv:19-37 (EOS before MAX_TOKENS; abort is host-side),
+// advance the position.
+__global__ void step_finalize_kernel(StepArgs a) {
+  pdl_wait();
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= a.M) return;
+  if (a.stop[m] != 0 || !a.active[m]) return;
+  const int max_new = a.run[0], eos = a.run[1], out_cap = a.run[2];
+  const int tok = a.argmax[m];
+  const int c = a.count[m];
+  if (c < out_cap) a.out_ids[static_cast<size_t>(m) * a.out_stride + c] = tok;
+  a.count[m] = c + 1;
+  a.pos[m] += 1;  // the token just processed now sits in the cache
+  a.tokens[m] = tok;
+  int stop = 0;
+  if (tok == eos) stop = 1;
+  else if ((max_new != 0 && c + 1 >= max_new) || c + 1 >= out_cap) stop = 2;
+  else if (a.pos[m] >= a.P) stop = 4;  // next feed would exceed the cache
+  if (stop) {
+    a.stop[m] = stop;
+    a.active[m] = 0;
+  }
+}
+
+cudaError_t launch_step_finalize(const StepArgs& a, cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.M + 127) / 128);
+  cfg.blockDim = dim3(128);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, step_finalize_kernel, a);
+}
+
+__global__ void rows_rewind_kernel(int* pos, int* active, int* count, int* stop, int M, int position) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= M) return;
+  pos[m] = position;
+  active[m] = 1;
+  count[m] = 0;
+  stop[m] = 0;
+}
+
+cudaError_t launch_rows_rewind(int* pos, int* active, int* count, int* stop, int M, int position,
+                               cudaStream_t s) {
+  rows_rewind_kernel<<<(M + 127) / 128, 128, 0, s>>>(pos, active, count, stop, M, position);
+  return cudaGetLastError();
+}
+
+}  // namespace tl

@@ -1,0 +1,140 @@
+// kernels.cuh -- launch interface of the sm_100a kernels (internal to the
+// library; the public boundary is include/tl_api.h).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace tl {
+
+// Activation prologue of the fused GEMV/GEMM (how the int8 operand is made).
+enum Prologue : int {
+  PRO_Q8 = 0,        // int8 rows given + per-group absmax (scale = absmax/127)
+  PRO_F32 = 1,       // float rows; per-row absmax computed in the kernel
+  PRO_NORM = 2,      // float rows; RMSNorm(gamma) then per-row absmax
+  PRO_F32_GIVEN = 3  // float rows; per-group absmax given
+};
+
+// Epilogue: what is done with each INT32 accumulator.
+enum Epilogue : int {
+  EPI_I32 = 0,     // raw accumulator
+  EPI_F32 = 1,     // float32(acc) * float32(s_x * s_w[n])
+  EPI_RESID = 2,   // resid + dequant (may alias the output)
+  EPI_SILU = 3,    // rows (2j, 2j+1) = (gate_j, up_j): silu(gate) * up
+  EPI_REQ = 4,     // Q16.16 requantize to int8 (requantize_unit.sv)
+  EPI_ARGMAX = 5   // dequant, optional logits, argmax over N per row
+};
+
+struct GemvArgs {
+  const float* x_f32 = nullptr;
+  const int8_t* x_q = nullptr;
+  const float* gamma = nullptr;
+  float eps = 1e-5f;
+  const float* in_absmax = nullptr;  // [groups]
+  int rows_per_group = 1;
+  const int8_t* w = nullptr;         // [N][K]
+  const double* w_scale = nullptr;   // [N]
+  int M = 0, N = 0, K = 0;
+  int32_t* out_i32 = nullptr;
+  float* out_f32 = nullptr;
+  const float* resid = nullptr;
+  int8_t* out_i8 = nullptr;
+  const uint32_t* req_scale = nullptr;
+  int req_per_col = 0, req_nonneg = 0;
+  float* out_absmax = nullptr;       // optional atomic max of |out| per group
+  float* logits = nullptr;           // EPI_ARGMAX optional [M][N]
+  unsigned long long* am_partial = nullptr;  // [gridDim.x][M]
+  unsigned int* am_counter = nullptr;        // [gridDim.y]
+  int32_t* am_token = nullptr;               // [M]
+  int x_row_offset = 0;              // float rows: source row of m is offset + m * step
+  int x_row_step = 1;                // (prefill LM head: last row of each sequence)
+};
+
+// Raises the dynamic shared-memory limit of every kernel variant for rows of
+// up to max_k elements. Called once per process/device before any launch (in
+// particular before stream capture, where attribute changes are not wanted).
+cudaError_t prepare_kernels(int max_k);
+
+// Picks the tile shape and launches; `pdl` enables programmatic dependent
+// launch (the kernel prefetches weights before waiting on its predecessor).
+cudaError_t launch_gemv(int pro, int epi, const GemvArgs& a, cudaStream_t s, bool pdl);
+// Scratch the argmax epilogue needs for a given shape.
+size_t gemv_argmax_partials(int M, int N);
+int gemv_argmax_row_blocks(int M);
+
+struct AttnDecodeArgs {
+  const float* qkv = nullptr;   // [M][ld]; q at 0, k at H*64, v at H*64 + Hkv*64
+  int ld = 0;
+  const int* pos = nullptr;     // [M]
+  const int* slot = nullptr;    // [M]
+  const int* active = nullptr;  // [M] (null = all rows active)
+  int8_t* kc = nullptr;
+  int8_t* vc = nullptr;
+  const float* ks = nullptr;    // [slots][L][Hkv]
+  const float* vs = nullptr;
+  int layer = 0, L = 0, H = 0, Hkv = 0, P = 0, M = 0;
+  const float* cos = nullptr;   // [P][64]
+  const float* sin = nullptr;
+  float* out = nullptr;         // [M][H*64]
+};
+cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);
+
+// ---- prefill helpers (rows of n_seq sequences of seq_len tokens each)
+cudaError_t launch_embed(const float* table, const int* ids, float* x, int rows, int D,
+                         int vocab, cudaStream_t s, bool pdl);
+cudaError_t launch_rmsnorm_rows(const float* x, const float* gamma, float eps, float* out,
+                                float* absmax_groups, int rows, int D, int rows_per_group,
+                                cudaStream_t s);
+cudaError_t launch_quantize_rows(const float* x, const float* absmax_groups, int rows, int K,
+                                 int rows_per_group, int8_t* out, cudaStream_t s);
+cudaError_t launch_absmax_rows(const float* x, int rows, int K, int rows_per_group, float* absmax,
+                               cudaStream_t s);
+// RoPE on q and k of qkv [rows][ld] in place (positions t = row % seq_len) and
+// per (seq, kv head) absmax of rotated K and of V -> kv_absmax[seq][2][Hkv].
+cudaError_t launch_rope_prefill(float* qkv, int ld, int rows, int seq_len, int H, int Hkv,
+                                const float* cos, const float* sin, float* kv_absmax,
+                                cudaStream_t s);
+// Quantize K/V of qkv with the calibrated per-head scales into the cache and
+// store the float32 scales.
+cudaError_t launch_kv_write_prefill(const float* qkv, int ld, int rows, int seq_len, int H,
+                                    int Hkv, const float* kv_absmax, int8_t* kc, int8_t* vc,
+                                    float* ks, float* vs, int slot_base, int layer, int L, int P,
+                                    cudaStream_t s);
+// Causal attention of a prefilled batch: q from qkv (rotated), K/V from cache.
+cudaError_t launch_attn_prefill(const float* qkv, int ld, int rows, int seq_len, int H, int Hkv,
+                                const int8_t* kc, const int8_t* vc, const float* ks,
+                                const float* vs, int slot_base, int layer, int L, int P,
+                                float* out, float* out_absmax, cudaStream_t s);
+
+// ---- misc
+cudaError_t launch_transpose_i8(const int8_t* src_kn, int8_t* dst_nk, int K, int N,
+                                cudaStream_t s);
+// gate [K][F] and up [K][F] (reference layout) -> interleaved W^T [2F][K]
+cudaError_t launch_interleave_gate_up(const int8_t* gate_kn, const int8_t* up_kn, int8_t* dst,
+                                      int K, int F, cudaStream_t s);
+cudaError_t launch_random_i8(int8_t* dst, size_t n, uint64_t seed, cudaStream_t s);
+cudaError_t launch_random_normal_f32(float* dst, size_t n, float std, uint64_t seed,
+                                     cudaStream_t s);
+cudaError_t launch_fill_f32(float* dst, size_t n, float v, cudaStream_t s);
+cudaError_t launch_fill_f64(double* dst, size_t n, double v, cudaStream_t s);
+
+// Decode-step bookkeeping on the device (after the LM-head argmax).
+struct StepArgs {
+  int M = 0;
+  const int32_t* argmax = nullptr;  // [M]
+  int* tokens = nullptr;            // [M] next input token
+  int* pos = nullptr;               // [M]
+  int* active = nullptr;            // [M]
+  int* count = nullptr;             // [M] emitted tokens
+  int* stop = nullptr;              // [M] stop reason (0 = running)
+  int* out_ids = nullptr;           // [M][out_stride]
+  int out_stride = 0;
+  const int* run = nullptr;         // device {max_new (0 = no limit), eos, out_cap}
+  int P = 0;
+};
+cudaError_t launch_step_finalize(const StepArgs& a, cudaStream_t s, bool pdl);
+// rows 0..M-1: pos = position, active = 1, count = 0, stop = 0
+cudaError_t launch_rows_rewind(int* pos, int* active, int* count, int* stop, int M, int position,
+                               cudaStream_t s);
+
+}  // namespace tl

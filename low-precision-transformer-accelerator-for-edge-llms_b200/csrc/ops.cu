@@ -1,0 +1,131 @@
+// ops.cu -- operator-level C ABI (caller-owned device buffers + stream).
+// Each entry point maps one reference operator onto the sm_100a kernels; see
+// include/tl_api.h for the reference lines each one replaces.
+#include <algorithm>
+#include <string>
+
+#include "../../include/tl_api.h"
+#include "kernels.cuh"
+
+using namespace tl;
+
+namespace {
+
+tl_status cu(cudaError_t e) { return e == cudaSuccess ? TL_OK : TL_ERR_CUDA; }
+
+#define TL_OPS_TRY(expr)          \
+  do {                            \
+    tl_status _s = (expr);        \
+    if (_s != TL_OK) return _s;   \
+  } while (0)
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+tl_status check_gemm(const void* a, const void* w, int M, int N, int K) {
+  if (!a || !w) return TL_ERR_INVALID_ARGUMENT;
+  if (M <= 0 || N <= 0 || K <= 0 || K % 16) return TL_ERR_INVALID_ARGUMENT;
+  if (!aligned16(a) || !aligned16(w)) return TL_ERR_INVALID_ARGUMENT;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return TL_ERR_CUDA;
+  return cu(prepare_kernels(K));
+}
+
+}  // namespace
+
+extern "C" {
+
+tl_status tl_transpose_i8(const int8_t* w_kn, int8_t* w_nk, int32_t K, int32_t N, void* stream) {
+  if (!w_kn || !w_nk || K <= 0 || N <= 0) return TL_ERR_INVALID_ARGUMENT;
+  return cu(launch_transpose_i8(w_kn, w_nk, K, N, static_cast<cudaStream_t>(stream)));
+}
+
+tl_status tl_quantize_int8(const float* x, int32_t rows, int32_t cols, int32_t rows_per_group,
+                           int8_t* out_q, float* out_absmax, void* stream) {
+  if (!x || !out_q || !out_absmax || rows <= 0 || cols <= 0 || rows_per_group <= 0)
+    return TL_ERR_INVALID_ARGUMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int groups = (rows + rows_per_group - 1) / rows_per_group;
+  TL_OPS_TRY(cu(cudaMemsetAsync(out_absmax, 0, groups * sizeof(float), s)));
+  TL_OPS_TRY(cu(launch_absmax_rows(x, rows, cols, rows_per_group, out_absmax, s)));
+  return cu(launch_quantize_rows(x, out_absmax, rows, cols, rows_per_group, out_q, s));
+}
+
+tl_status tl_gemm_i8(const int8_t* a, const int8_t* w_nk, int32_t* c, int32_t M, int32_t N, int32_t K,
+                     void* stream) {
+  if (!c) return TL_ERR_INVALID_ARGUMENT;
+  TL_OPS_TRY(check_gemm(a, w_nk, M, N, K));
+  GemvArgs g;
+  g.x_q = a; g.w = w_nk; g.M = M; g.N = N; g.K = K; g.out_i32 = c;
+  return cu(launch_gemv(PRO_Q8, EPI_I32, g, static_cast<cudaStream_t>(stream), false));
+}
+
+tl_status tl_gemm_i8_requant(const int8_t* a, const int8_t* w_nk, const uint32_t* scale_q16,
+                             int32_t per_column, int32_t nonnegative_only, int8_t* out, int32_t M,
+                             int32_t N, int32_t K, void* stream) {
+  if (!out || !scale_q16) return TL_ERR_INVALID_ARGUMENT;
+  TL_OPS_TRY(check_gemm(a, w_nk, M, N, K));
+  GemvArgs g;
+  g.x_q = a; g.w = w_nk; g.M = M; g.N = N; g.K = K; g.out_i8 = out;
+  g.req_scale = scale_q16; g.req_per_col = per_column ? 1 : 0; g.req_nonneg = nonnegative_only ? 1 : 0;
+  return cu(launch_gemv(PRO_Q8, EPI_REQ, g, static_cast<cudaStream_t>(stream), false));
+}
+
+tl_status tl_quantized_linear(const float* x, const int8_t* w_nk, const double* w_scale, float* out,
+                              int32_t* acc_out, int32_t M, int32_t N, int32_t K, void* stream) {
+  if (!out || !w_scale) return TL_ERR_INVALID_ARGUMENT;
+  TL_OPS_TRY(check_gemm(x, w_nk, M, N, K));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int8_t* xq = nullptr;
+  float* amax = nullptr;
+  TL_OPS_TRY(cu(cudaMallocAsync(reinterpret_cast<void**>(&xq), static_cast<size_t>(M) * K, s)));
+  tl_status st = cu(cudaMallocAsync(reinterpret_cast<void**>(&amax), sizeof(float), s));
+  if (st == TL_OK) st = tl_quantize_int8(x, M, K, M, xq, amax, stream);
+  if (st == TL_OK) {
+    GemvArgs g;
+    g.x_q = xq; g.in_absmax = amax; g.rows_per_group = M;
+    g.w = w_nk; g.w_scale = w_scale; g.M = M; g.N = N; g.K = K; g.out_f32 = out;
+    st = cu(launch_gemv(PRO_Q8, EPI_F32, g, s, false));
+  }
+  if (st == TL_OK && acc_out) {
+    GemvArgs g;
+    g.x_q = xq; g.w = w_nk; g.M = M; g.N = N; g.K = K; g.out_i32 = acc_out;
+    st = cu(launch_gemv(PRO_Q8, EPI_I32, g, s, false));
+  }
+  if (xq) cudaFreeAsync(xq, s);
+  if (amax) cudaFreeAsync(amax, s);
+  return st;
+}
+
+tl_status tl_rmsnorm(const float* x, const float* gamma, float eps, float* out, int32_t rows, int32_t cols,
+                     void* stream) {
+  if (!x || !gamma || !out || rows <= 0 || cols <= 0) return TL_ERR_INVALID_ARGUMENT;
+  TL_OPS_TRY(cu(prepare_kernels(cols)));
+  return cu(launch_rmsnorm_rows(x, gamma, eps, out, nullptr, rows, cols, 1, static_cast<cudaStream_t>(stream)));
+}
+
+tl_status tl_lmhead_argmax(const float* x, const float* gamma, float eps, const int8_t* w_nk,
+                           const double* w_scale, int32_t rows, int32_t vocab, int32_t hidden,
+                           int32_t* token_out, float* logits_out, void* stream) {
+  if (!gamma || !w_scale || !token_out) return TL_ERR_INVALID_ARGUMENT;
+  TL_OPS_TRY(check_gemm(x, w_nk, rows, vocab, hidden));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  unsigned long long* partial = nullptr;
+  unsigned int* counter = nullptr;
+  const size_t n_part = gemv_argmax_partials(rows, vocab);
+  const int n_cnt = gemv_argmax_row_blocks(rows);
+  TL_OPS_TRY(cu(cudaMallocAsync(reinterpret_cast<void**>(&partial), n_part * sizeof(unsigned long long), s)));
+  tl_status st = cu(cudaMallocAsync(reinterpret_cast<void**>(&counter), n_cnt * sizeof(unsigned int), s));
+  if (st == TL_OK) st = cu(cudaMemsetAsync(counter, 0, n_cnt * sizeof(unsigned int), s));
+  if (st == TL_OK) {
+    GemvArgs g;
+    g.x_f32 = x; g.gamma = gamma; g.eps = eps; g.w = w_nk; g.w_scale = w_scale;
+    g.M = rows; g.N = vocab; g.K = hidden; g.logits = logits_out;
+    g.am_partial = partial; g.am_counter = counter; g.am_token = token_out;
+    st = cu(launch_gemv(PRO_NORM, EPI_ARGMAX, g, s, false));
+  }
+  if (partial) cudaFreeAsync(partial, s);
+  if (counter) cudaFreeAsync(counter, s);
+  return st;
+}
+
+}  // extern "C"

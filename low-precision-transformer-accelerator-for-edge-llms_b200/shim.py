@@ -1,0 +1,491 @@
+"""ctypes binding of ``libtl_b200.so`` (include/tl_api.h) and a Python surface
+that mirrors the reference's own operator API.
+
+Reference entry points mirrored here (same names, same argument meaning, same
+error behaviour where the reference has one):
+
+* ``quantized_linear(x, w, b=None, capture_arrays=False)``
+  model/tinyllama_gemm_int8.py:59-88 -> returns ``(out, debug)`` with the
+  same debug keys (``input_q``, ``weight_q``, ``accum_int32``,
+  ``input_scale``, ``weight_scale``).
+* ``quantize_int8(t)``           model/tinyllama_gemm_int8.py:36-42
+* ``rms_norm(x, w, eps)``        model/tinyllama.py:45-50
+* ``forward_mixed(token_ids, weights, cos, sin, layer_count, quantize_lm_head)``
+  model/tinyllama_gemm_int8.py:437-467 (last row of logits; see its docstring)
+* ``Engine.generate`` / ``generate_batch``: run_generate
+  (model/tinyllama_gemm_int8.py:629-685) with the RTL launch/stop contract
+  (rtl/control/prefill_decode_controller.sv, stop_condition_unit.sv).
+
+Every computation runs in the CUDA library; there is no CPU path. If the
+library is missing or no GPU is visible, calls raise.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+from pathlib import Path
+
+import numpy as np
+
+LIB_PATH = Path(__file__).resolve().parent / "libtl_b200.so"
+
+TL_OK = 0
+STATUS_NAMES = {
+    0: "TL_OK", 1: "TL_ERR_BAD_DESCRIPTOR", 2: "TL_ERR_HBM_READ", 3: "TL_ERR_HBM_WRITE",
+    4: "TL_ERR_SCALE_METADATA", 5: "TL_ERR_DEBUG_OVERFLOW", 6: "TL_ERR_UNSUPPORTED_MODE",
+    7: "TL_ERR_INTERNAL", 16: "TL_ERR_INVALID_ARGUMENT", 17: "TL_ERR_OUT_OF_RANGE",
+    18: "TL_ERR_CUDA", 19: "TL_ERR_NCCL", 20: "TL_ERR_TIMEOUT", 21: "TL_ERR_NOT_LOADED",
+    22: "TL_ERR_UNIMPLEMENTED",
+}
+STOP_NONE, STOP_EOS, STOP_MAX_TOKENS, STOP_HOST_ABORT, STOP_INTERNAL_ERR = 0, 1, 2, 3, 4
+MODE_PREFILL, MODE_DECODE = 0, 1
+
+# Every symbol the header declares (checked by the CPU tests).
+EXPORTS = (
+    "tl_status_string", "tl_version", "tl_create", "tl_destroy", "tl_load_weights",
+    "tl_init_random_weights", "tl_generate", "tl_generate_batch", "tl_abort",
+    "tl_prefill_logits", "tl_decode_logits", "tl_read_kv", "tl_get_position",
+    "tl_decode_steps_device", "tl_prefill_batch_device", "tl_decode_rewind", "tl_synchronize",
+    "tl_decode_step_kernel_count", "tl_engine_stream", "tl_profile_decode_kernels", "tl_transpose_i8", "tl_quantize_int8",
+    "tl_gemm_i8", "tl_gemm_i8_requant", "tl_quantized_linear", "tl_rmsnorm", "tl_lmhead_argmax",
+)
+
+
+class TLError(RuntimeError):
+    def __init__(self, code: int, what: str, detail: str = ""):
+        self.code = code
+        super().__init__(f"{what}: {STATUS_NAMES.get(code, code)} {detail}".rstrip())
+
+
+class Config(C.Structure):
+    _fields_ = [("hidden_size", C.c_int32), ("intermediate_size", C.c_int32),
+                ("num_layers", C.c_int32), ("num_heads", C.c_int32), ("num_kv_heads", C.c_int32),
+                ("head_dim", C.c_int32), ("vocab_size", C.c_int32), ("max_positions", C.c_int32),
+                ("rms_norm_eps", C.c_float), ("rope_theta", C.c_float), ("max_batch", C.c_int32),
+                ("max_prefill_tokens", C.c_int32)]
+
+
+class LinearView(C.Structure):
+    _fields_ = [("w", C.c_void_p), ("scale", C.c_void_p)]
+
+
+class LayerView(C.Structure):
+    _fields_ = [("q", LinearView), ("k", LinearView), ("v", LinearView), ("o", LinearView),
+                ("gate", LinearView), ("up", LinearView), ("down", LinearView),
+                ("input_norm", C.c_void_p), ("post_norm", C.c_void_p)]
+
+
+class WeightsView(C.Structure):
+    _fields_ = [("embed", C.c_void_p), ("final_norm", C.c_void_p), ("lm_head", LinearView),
+                ("layers", C.POINTER(LayerView)), ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p)]
+
+
+class RunStatus(C.Structure):
+    _fields_ = [("status_word", C.c_uint32), ("generated_count", C.c_uint32),
+                ("last_token", C.c_uint32), ("current_layer", C.c_uint32),
+                ("current_block", C.c_uint32), ("stop_reason", C.c_int32),
+                ("error_code", C.c_int32), ("position", C.c_uint32)]
+
+    def as_dict(self) -> dict:
+        return {f: getattr(self, f) for f, _ in self._fields_}
+
+
+_LIB = None
+
+
+def load_library(path: Path | str | None = None):
+    """Load libtl_b200.so (built in-tree by build.py). Raises if it is missing."""
+    global _LIB
+    if _LIB is not None and path is None:
+        return _LIB
+    p = Path(path) if path else LIB_PATH
+    if not p.exists():
+        raise ImportError(f"{p} not found: build it with build.py (nvcc, sm_100a); "
+                          "there is no CPU fallback")
+    lib = C.CDLL(str(p))
+    vp, i32, u32, u64 = C.c_void_p, C.c_int32, C.c_uint32, C.c_uint64
+    sig = {
+        "tl_status_string": (C.c_char_p, [i32]),
+        "tl_version": (i32, []),
+        "tl_create": (i32, [C.POINTER(Config), i32, C.POINTER(vp)]),
+        "tl_destroy": (i32, [vp]),
+        "tl_load_weights": (i32, [vp, C.POINTER(WeightsView)]),
+        "tl_init_random_weights": (i32, [vp, u64]),
+        "tl_generate": (i32, [vp, vp, u32, u32, u32, u32, vp, u32, C.POINTER(RunStatus)]),
+        "tl_generate_batch": (i32, [vp, u32, vp, u32, u32, u32, vp, u32, vp]),
+        "tl_abort": (i32, [vp]),
+        "tl_prefill_logits": (i32, [vp, u32, vp, u32, vp]),
+        "tl_decode_logits": (i32, [vp, u32, u32, vp]),
+        "tl_read_kv": (i32, [vp, u32, u32, u32, vp, vp, vp, vp]),
+        "tl_get_position": (i32, [vp, u32, C.POINTER(u32)]),
+        "tl_decode_steps_device": (i32, [vp, u32, u32]),
+        "tl_prefill_batch_device": (i32, [vp, u32, vp, u32]),
+        "tl_decode_rewind": (i32, [vp, u32, u32]),
+        "tl_synchronize": (i32, [vp]),
+        "tl_decode_step_kernel_count": (i32, [vp]),
+        "tl_engine_stream": (vp, [vp]),
+        "tl_profile_decode_kernels": (i32, [vp, u32, u32, vp]),
+        "tl_transpose_i8": (i32, [vp, vp, i32, i32, vp]),
+        "tl_quantize_int8": (i32, [vp, i32, i32, i32, vp, vp, vp]),
+        "tl_gemm_i8": (i32, [vp, vp, vp, i32, i32, i32, vp]),
+        "tl_gemm_i8_requant": (i32, [vp, vp, vp, i32, i32, vp, i32, i32, i32, vp]),
+        "tl_quantized_linear": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, vp]),
+        "tl_rmsnorm": (i32, [vp, vp, C.c_float, vp, i32, i32, vp]),
+        "tl_lmhead_argmax": (i32, [vp, vp, C.c_float, vp, vp, i32, i32, i32, vp, vp, vp]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if path is None:
+        _LIB = lib
+    return lib
+
+
+def check(code: int, what: str):
+    if code != TL_OK:
+        detail = ""
+        try:
+            detail = load_library().tl_status_string(code).decode()
+        except Exception:
+            pass
+        raise TLError(code, what, detail)
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+# --------------------------------------------------------------------------
+# Host-side model container (reference key schema, quantized)
+# --------------------------------------------------------------------------
+@dataclass
+class Linear:
+    w: np.ndarray       # int8 [in, out]
+    scale: np.ndarray   # float64 [out]
+
+
+@dataclass
+class Layer:
+    q: Linear
+    k: Linear
+    v: Linear
+    o: Linear
+    gate: Linear
+    up: Linear
+    down: Linear
+    input_norm: np.ndarray
+    post_norm: np.ndarray
+
+
+@dataclass
+class Model:
+    cfg: dict
+    embed: np.ndarray
+    final_norm: np.ndarray
+    lm_head: Linear
+    layers: list = field(default_factory=list)
+
+
+def quantize_weight(w: np.ndarray, granularity: str = "tensor") -> Linear:
+    """INT8 weight with a float64 scale per output channel. ``tensor`` is the
+    reference bridge's per-call rule (model/tinyllama_gemm_int8.py:36-42, 69),
+    ``channel`` applies the same rule per output column."""
+    w = np.asarray(w, dtype=np.float32)
+    if granularity == "tensor":
+        peak = float(np.max(np.abs(w))) if w.size else 0.0
+        s = 1.0 if peak == 0.0 else peak / 127.0
+        q = np.clip(np.round(w / s), -127, 127).astype(np.int8)
+        return Linear(q, np.full(w.shape[1], s, dtype=np.float64))
+    peak = np.max(np.abs(w), axis=0).astype(np.float64)
+    s = np.where(peak == 0.0, 1.0, peak / 127.0)
+    q = np.clip(np.round(w / s.astype(np.float32)[None, :]), -127, 127).astype(np.int8)
+    return Linear(q, s)
+
+
+def from_tinyllama_weights(weights, layer_count: int | None = None, granularity: str = "tensor") -> Model:
+    """Quantize a reference ``TinyLlamaWeights``-like object (``cfg`` dict,
+    ``layer(i)`` dict with ``q_w``.. ``down_w`` [in, out], norms, ``embed``,
+    ``final_norm_w()``, ``lm_head_w()``; model/tinyllama.py:198-267)."""
+    cfg = dict(weights.cfg)
+    n = cfg["num_hidden_layers"] if layer_count is None else layer_count
+    layers = []
+    for i in range(n):
+        d = weights.layer(i)
+        layers.append(Layer(*(quantize_weight(d[f"{p}_w"], granularity)
+                               for p in ("q", "k", "v", "o", "gate", "up", "down")),
+                            input_norm=np.asarray(d["input_norm_w"], np.float32),
+                            post_norm=np.asarray(d["post_norm_w"], np.float32)))
+    emb = weights._array("embed_w") if hasattr(weights, "_array") else weights.embed_w
+    cfg["num_hidden_layers"] = n
+    return Model(cfg, np.asarray(emb, np.float32), np.asarray(weights.final_norm_w(), np.float32),
+                 quantize_weight(weights.lm_head_w(), granularity), layers)
+
+
+def rope_tables(n_pos: int, head_dim: int, theta: float) -> tuple[np.ndarray, np.ndarray]:
+    """float32 RoPE tables with the reference's NumPy arithmetic
+    (model/tinyllama.py:59-66), so the device sees identical cos/sin."""
+    inv_freq = 1.0 / (theta ** (np.arange(0, head_dim, 2, dtype=np.float32) / head_dim))
+    ang = np.outer(np.arange(n_pos, dtype=np.float32), inv_freq)
+    ang = np.concatenate([ang, ang], axis=-1)
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+# --------------------------------------------------------------------------
+# Engine (runtime contract)
+# --------------------------------------------------------------------------
+class Engine:
+    """One engine per GPU: weights arena, INT8 KV cache for ``max_batch``
+    sequences, captured decode graphs."""
+
+    def __init__(self, cfg: dict, max_batch: int = 1, device: int = 0,
+                 max_prefill_tokens: int | None = None):
+        self.lib = load_library()
+        self.cfg = dict(cfg)
+        c = Config(hidden_size=cfg["hidden_size"], intermediate_size=cfg["intermediate_size"],
+                   num_layers=cfg["num_hidden_layers"], num_heads=cfg["num_attention_heads"],
+                   num_kv_heads=cfg["num_key_value_heads"], head_dim=cfg["head_dim"],
+                   vocab_size=cfg["vocab_size"], max_positions=cfg["max_position_embeddings"],
+                   rms_norm_eps=cfg["rms_norm_eps"], rope_theta=cfg["rope_theta"],
+                   max_batch=max_batch,
+                   max_prefill_tokens=max_prefill_tokens or cfg["max_position_embeddings"])
+        h = C.c_void_p()
+        check(self.lib.tl_create(C.byref(c), device, C.byref(h)), "tl_create")
+        self.h = h
+        self.max_batch = max_batch
+        self._keep = []
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.tl_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ----------------------------------------------------------- weights
+    def load(self, model: Model):
+        cfg = model.cfg
+        cos, sin = rope_tables(cfg["max_position_embeddings"], cfg["head_dim"], cfg["rope_theta"])
+        keep = [cos, sin]
+
+        def lin(l: Linear) -> LinearView:
+            w = np.ascontiguousarray(l.w, dtype=np.int8)
+            s = np.ascontiguousarray(l.scale, dtype=np.float64)
+            keep.extend([w, s])
+            return LinearView(_ptr(w), _ptr(s))
+
+        def arr(a) -> int:
+            a = np.ascontiguousarray(a, dtype=np.float32)
+            keep.append(a)
+            return _ptr(a)
+
+        layers = (LayerView * len(model.layers))()
+        for i, ly in enumerate(model.layers):
+            layers[i] = LayerView(lin(ly.q), lin(ly.k), lin(ly.v), lin(ly.o), lin(ly.gate), lin(ly.up),
+                                  lin(ly.down), arr(ly.input_norm), arr(ly.post_norm))
+        view = WeightsView(arr(model.embed), arr(model.final_norm), lin(model.lm_head), layers,
+                           _ptr(cos), _ptr(sin))
+        check(self.lib.tl_load_weights(self.h, C.byref(view)), "tl_load_weights")
+
+    def init_random(self, seed: int = 0):
+        check(self.lib.tl_init_random_weights(self.h, seed), "tl_init_random_weights")
+
+    # ----------------------------------------------------------- runtime
+    def generate(self, prompt, max_new_tokens: int, eos_id: int = 0xFFFFFFFF, mode: int = MODE_PREFILL,
+                 out_cap: int | None = None, raise_on_error: bool = True):
+        """Greedy generation in slot 0. Returns (tokens, status dict)."""
+        ids = np.ascontiguousarray(np.asarray(list(prompt), dtype=np.uint32))
+        cap = out_cap if out_cap is not None else max(1, max_new_tokens or self.cfg["max_position_embeddings"])
+        out = np.zeros(cap, dtype=np.uint32)
+        st = RunStatus()
+        code = self.lib.tl_generate(self.h, _ptr(ids) if ids.size else None, ids.size, max_new_tokens,
+                                    eos_id & 0xFFFFFFFF, mode, _ptr(out), cap, C.byref(st))
+        if raise_on_error and code not in (TL_OK,):
+            check(code, "tl_generate")
+        d = st.as_dict()
+        d["return_code"] = code
+        return [int(t) for t in out[:st.generated_count]], d
+
+    def generate_batch(self, prompts: np.ndarray, max_new_tokens: int, eos_id: int = 0xFFFFFFFF,
+                       out_cap: int | None = None):
+        p = np.ascontiguousarray(np.asarray(prompts, dtype=np.uint32))
+        n, s = p.shape
+        cap = out_cap if out_cap is not None else max(1, max_new_tokens)
+        out = np.zeros((n, cap), dtype=np.uint32)
+        st = (RunStatus * n)()
+        check(self.lib.tl_generate_batch(self.h, n, _ptr(p), s, max_new_tokens, eos_id & 0xFFFFFFFF,
+                                         _ptr(out), cap, st), "tl_generate_batch")
+        return [[int(t) for t in out[i, :st[i].generated_count]] for i in range(n)], [x.as_dict() for x in st]
+
+    def abort(self):
+        check(self.lib.tl_abort(self.h), "tl_abort")
+
+    def prefill_logits(self, ids) -> np.ndarray:
+        ids = np.ascontiguousarray(np.asarray(list(ids), dtype=np.uint32))
+        out = np.zeros(self.cfg["vocab_size"], dtype=np.float32)
+        check(self.lib.tl_prefill_logits(self.h, 0, _ptr(ids), ids.size, _ptr(out)), "tl_prefill_logits")
+        return out
+
+    def decode_logits(self, token: int, slot: int = 0) -> np.ndarray:
+        out = np.zeros(self.cfg["vocab_size"], dtype=np.float32)
+        check(self.lib.tl_decode_logits(self.h, slot, int(token), _ptr(out)), "tl_decode_logits")
+        return out
+
+    def read_kv(self, layer: int, n_pos: int, slot: int = 0):
+        hkv = self.cfg["num_key_value_heads"]
+        k = np.zeros((hkv, n_pos, 64), np.int8)
+        v = np.zeros((hkv, n_pos, 64), np.int8)
+        ks = np.zeros(hkv, np.float32)
+        vs = np.zeros(hkv, np.float32)
+        check(self.lib.tl_read_kv(self.h, slot, layer, n_pos, _ptr(k), _ptr(v), _ptr(ks), _ptr(vs)),
+              "tl_read_kv")
+        return k, v, ks, vs
+
+    def position(self, slot: int = 0) -> int:
+        p = C.c_uint32()
+        check(self.lib.tl_get_position(self.h, slot, C.byref(p)), "tl_get_position")
+        return p.value
+
+    # ------------------------------------------------ device-resident (bench)
+    def prefill_batch_device(self, prompts: np.ndarray):
+        p = np.ascontiguousarray(np.asarray(prompts, dtype=np.uint32))
+        check(self.lib.tl_prefill_batch_device(self.h, p.shape[0], _ptr(p), p.shape[1]),
+              "tl_prefill_batch_device")
+
+    def decode_steps_device(self, n_seqs: int, steps: int):
+        check(self.lib.tl_decode_steps_device(self.h, n_seqs, steps), "tl_decode_steps_device")
+
+    def decode_rewind(self, n_seqs: int, position: int):
+        check(self.lib.tl_decode_rewind(self.h, n_seqs, position), "tl_decode_rewind")
+
+    def synchronize(self):
+        check(self.lib.tl_synchronize(self.h), "tl_synchronize")
+
+    def stream_handle(self) -> int:
+        return self.lib.tl_engine_stream(self.h) or 0
+
+    def profile_decode_kernels(self, n_seqs: int, iters: int = 44) -> np.ndarray:
+        """Average device time (ms) of each decode kernel kind, see
+        tl_profile_decode_kernels: [qkv, attn, o, gate_up, down, lm_head]."""
+        out = np.zeros(6, dtype=np.float32)
+        check(self.lib.tl_profile_decode_kernels(self.h, n_seqs, iters, _ptr(out)),
+              "tl_profile_decode_kernels")
+        return out
+
+    def decode_step_kernel_count(self) -> int:
+        return int(self.lib.tl_decode_step_kernel_count(self.h))
+
+
+# --------------------------------------------------------------------------
+# Operator API (device tensors via torch for buffers; compute in the library)
+# --------------------------------------------------------------------------
+def _torch():
+    import torch
+    if not torch.cuda.is_available():
+        raise RuntimeError("no CUDA device visible: the operator API runs only on the GPU")
+    return torch
+
+
+def _stream(torch):
+    return torch.cuda.current_stream().cuda_stream
+
+
+def quantize_int8(t: np.ndarray):
+    """GPU ``quantize_int8`` (model/tinyllama_gemm_int8.py:36-42): returns
+    (int8 array, scale as a Python float)."""
+    torch = _torch()
+    lib = load_library()
+    x = np.ascontiguousarray(np.asarray(t, dtype=np.float32))
+    flat = x.reshape(1, -1) if x.ndim != 2 else x
+    rows, cols = flat.shape
+    if x.ndim != 2:
+        rows, cols = 1, x.size
+    dx = torch.from_numpy(flat.reshape(rows, cols)).cuda()
+    q = torch.empty((rows, cols), dtype=torch.int8, device="cuda")
+    am = torch.empty(1, dtype=torch.float32, device="cuda")
+    check(lib.tl_quantize_int8(dx.data_ptr(), rows, cols, rows, q.data_ptr(), am.data_ptr(), _stream(torch)),
+          "tl_quantize_int8")
+    peak = float(am.item())
+    scale = 1.0 if peak == 0.0 else peak / 127.0
+    return q.cpu().numpy().reshape(x.shape), scale
+
+
+def quantized_linear(x: np.ndarray, w: np.ndarray, b: np.ndarray | None = None, capture_arrays: bool = False):
+    """GPU ``quantized_linear`` (model/tinyllama_gemm_int8.py:59-88): x [S,K]
+    float, w [K,N] float quantized per tensor, INT8 GEMM with INT32
+    accumulation, dequantized output [S,N] float32."""
+    torch = _torch()
+    lib = load_library()
+    x_fp = np.ascontiguousarray(np.asarray(x, dtype=np.float32))
+    w_fp = np.asarray(w, dtype=np.float32)
+    lw = quantize_weight(w_fp, "tensor")
+    m, k = x_fp.shape
+    n = w_fp.shape[1]
+    if k % 16:
+        raise ValueError("K must be a multiple of 16")
+    dx = torch.from_numpy(x_fp).cuda()
+    wkn = torch.from_numpy(np.ascontiguousarray(lw.w)).cuda()
+    wnk = torch.empty((n, k), dtype=torch.int8, device="cuda")
+    st = _stream(torch)
+    check(lib.tl_transpose_i8(wkn.data_ptr(), wnk.data_ptr(), k, n, st), "tl_transpose_i8")
+    ws = torch.from_numpy(lw.scale).cuda()
+    out = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    acc = torch.empty((m, n), dtype=torch.int32, device="cuda") if capture_arrays else None
+    check(lib.tl_quantized_linear(dx.data_ptr(), wnk.data_ptr(), ws.data_ptr(), out.data_ptr(),
+                                  acc.data_ptr() if acc is not None else None, m, n, k, st),
+          "tl_quantized_linear")
+    o = out.cpu().numpy()
+    if b is not None:
+        o = o + np.asarray(b, dtype=np.float32)
+    xq, sx = quantize_int8(x_fp)
+    dbg = {"input_scale": np.array([sx], dtype=np.float32),
+           "weight_scale": np.array([lw.scale[0]], dtype=np.float32)}
+    if capture_arrays:
+        dbg.update({"input_fp": x_fp, "input_q": xq, "weight_fp": w_fp, "weight_q": lw.w,
+                    "accum_int32": acc.cpu().numpy(), "output_fp": o.astype(np.float32)})
+    return o.astype(np.float32), dbg
+
+
+def rms_norm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    """GPU ``rms_norm`` (model/tinyllama.py:45-50), bit-exact with NumPy."""
+    torch = _torch()
+    lib = load_library()
+    xf = np.ascontiguousarray(np.asarray(x, dtype=np.float32))
+    shp = xf.shape
+    x2 = xf.reshape(-1, shp[-1])
+    dx = torch.from_numpy(x2).cuda()
+    g = torch.from_numpy(np.ascontiguousarray(np.asarray(w, np.float32))).cuda()
+    out = torch.empty_like(dx)
+    check(lib.tl_rmsnorm(dx.data_ptr(), g.data_ptr(), float(eps), out.data_ptr(), x2.shape[0], x2.shape[1],
+                         _stream(torch)), "tl_rmsnorm")
+    return out.cpu().numpy().reshape(shp)
+
+
+_ENGINE_CACHE: dict = {}
+
+
+def forward_mixed(token_ids, weights, cos=None, sin=None, layer_count: int | None = None,
+                  quantize_lm_head: bool = True) -> np.ndarray:
+    """GPU ``forward_mixed`` (model/tinyllama_gemm_int8.py:437-467) for a
+    ``TinyLlamaWeights``-like object. Only the INT8 LM head is supported
+    (``quantize_lm_head=True``). Returns the logits of the LAST row as an
+    array of shape [1, vocab] -- the only row the reference's callers read
+    (``logits[-1]``, :671). ``cos``/``sin`` are accepted for signature
+    compatibility; the engine uses the same float32 tables."""
+    if not quantize_lm_head:
+        raise NotImplementedError("the engine's LM head is INT8 (quantize_lm_head=True)")
+    key = (id(weights), layer_count)
+    eng = _ENGINE_CACHE.get(key)
+    if eng is None:
+        model = from_tinyllama_weights(weights, layer_count)
+        eng = Engine(model.cfg, max_batch=1)
+        eng.load(model)
+        _ENGINE_CACHE[key] = eng
+    if len(token_ids) > eng.cfg["max_position_embeddings"]:
+        raise ValueError("Sequence length exceeds max_position_embeddings")
+    return eng.prefill_logits(token_ids)[None, :]

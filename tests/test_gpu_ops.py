@@ -1,0 +1,161 @@
+"""Operator-level parity of the CUDA kernels against the oracle (GPU).
+
+Integer results (INT32 accumulators, INT8 quantization, Q16.16 requantize)
+must be bit-exact; RMSNorm is bit-exact as well because the kernel follows
+NumPy's float32 reduction order.
+"""
+
+import numpy as np
+import pytest
+
+from oracle import contract as C
+from oracle import golden as G
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def lib(pkg):
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    return pkg.load_library()
+
+
+def stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def gemm_gpu(lib, pkg, a, w_kn):
+    m, k = a.shape
+    n = w_kn.shape[1]
+    wnk = dev(np.ascontiguousarray(w_kn.T))
+    c = torch.empty((m, n), dtype=torch.int32, device="cuda")
+    pkg.shim.check(lib.tl_gemm_i8(dev(a).data_ptr(), wnk.data_ptr(), c.data_ptr(), m, n, k, stream()), "gemm")
+    return c.cpu().numpy()
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 64, 64), (1, 2048, 256), (3, 2048, 2048), (8, 5632, 2048),
+                                   (17, 2048, 320), (32, 5632, 256), (1, 2048, 32000), (5, 704, 96)])
+def test_gemm_i8_bit_exact(lib, pkg, m, k, n):
+    rng = np.random.default_rng(m * 131 + k + n)
+    a = rng.integers(-127, 128, (m, k)).astype(np.int8)
+    w = rng.integers(-127, 128, (k, n)).astype(np.int8)
+    np.testing.assert_array_equal(gemm_gpu(lib, pkg, a, w), G.int8_matmul(a, w))
+
+
+def test_gemm_extremes_and_kats(lib, pkg, golden):
+    a = np.full((2, 5632), -127, np.int8)
+    w = np.full((5632, 16), 127, np.int8)
+    np.testing.assert_array_equal(gemm_gpu(lib, pkg, a, w), G.int8_matmul(a, w))
+    d = golden["kat_sim"]
+    got = gemm_gpu(lib, pkg, d["gemv_x"][None, :], np.ascontiguousarray(d["gemv_w_nk"].T))[0]
+    np.testing.assert_array_equal(got, d["gemv_expected"])
+    for k in (16, 64):
+        y1 = gemm_gpu(lib, pkg, d[f"k{k}_x_q"][None, :], np.ascontiguousarray(d[f"k{k}_W1_q"].T))[0]
+        np.testing.assert_array_equal(y1, d[f"k{k}_y1_int"])
+        y = gemm_gpu(lib, pkg, d[f"k{k}_y2_q"][None, :], np.ascontiguousarray(d[f"k{k}_W2_q"].T))[0]
+        np.testing.assert_array_equal(y, d[f"k{k}_y_expected"])
+
+
+@pytest.mark.parametrize("per_col,nonneg", [(0, 0), (1, 0), (0, 1)])
+def test_gemm_requant_bit_exact(lib, pkg, per_col, nonneg):
+    rng = np.random.default_rng(10 + per_col + 2 * nonneg)
+    m, k, n = 6, 2048, 512
+    a = rng.integers(-127, 128, (m, k)).astype(np.int8)
+    w = rng.integers(-127, 128, (k, n)).astype(np.int8)
+    scales = rng.uniform(1e-4, 1e-2, n if per_col else 1)
+    sq = np.array([C.q16_16_from_float(s) for s in scales], dtype=np.uint32)
+    out = torch.empty((m, n), dtype=torch.int8, device="cuda")
+    pkg.shim.check(lib.tl_gemm_i8_requant(dev(a).data_ptr(), dev(np.ascontiguousarray(w.T)).data_ptr(),
+                                          dev(sq).data_ptr(), per_col, nonneg, out.data_ptr(), m, n, k,
+                                          stream()), "requant")
+    ref = C.requantize_q16(G.int8_matmul(a, w), sq[None, :] if per_col else sq[0], bool(nonneg))
+    np.testing.assert_array_equal(out.cpu().numpy(), ref)
+
+
+def test_quantize_int8_bit_exact(lib, pkg, golden):
+    d = golden["quant_cases"]
+    for key in ("q0", "q1", "q2", "q3", "q4", "qz", "qh"):
+        x = np.atleast_2d(d[f"{key}_x"])
+        q = torch.empty(x.shape, dtype=torch.int8, device="cuda")
+        am = torch.empty(1, dtype=torch.float32, device="cuda")
+        pkg.shim.check(lib.tl_quantize_int8(dev(x).data_ptr(), x.shape[0], x.shape[1], x.shape[0],
+                                            q.data_ptr(), am.data_ptr(), stream()), "quantize")
+        np.testing.assert_array_equal(q.cpu().numpy().reshape(d[f"{key}_q"].shape), d[f"{key}_q"], err_msg=key)
+        peak = float(am.item())
+        assert (1.0 if peak == 0.0 else peak / 127.0) == float(d[f"{key}_scale"]), key
+
+
+def test_quantized_linear_matches_reference_fixture(pkg, golden, lib):
+    d = golden["quant_cases"]
+    for i in range(4):
+        out, dbg = pkg.quantized_linear(d[f"l{i}_x"], d[f"l{i}_w"], capture_arrays=True)
+        np.testing.assert_array_equal(dbg["accum_int32"], d[f"l{i}_acc"])
+        np.testing.assert_array_equal(dbg["input_q"], d[f"l{i}_xq"])
+        np.testing.assert_array_equal(out, d[f"l{i}_out"])
+
+
+@pytest.mark.parametrize("rows,cols", [(3, 64), (7, 256), (5, 2048), (2, 5632), (1, 704)])
+def test_rmsnorm_bit_exact(pkg, lib, rows, cols):
+    rng = np.random.default_rng(rows * cols)
+    x = (rng.standard_normal((rows, cols), dtype=np.float32) * rng.uniform(0.01, 30)).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(cols, dtype=np.float32)).astype(np.float32)
+    np.testing.assert_array_equal(pkg.rms_norm(x, g, 1e-5), G.rms_norm(x, g, 1e-5))
+
+
+def test_rmsnorm_reference_fixture(pkg, golden, lib):
+    d = golden["small_model"]
+    np.testing.assert_array_equal(pkg.rms_norm(d["rms_x"], d["rms_g"], 1e-5), d["rms_out"])
+
+
+@pytest.mark.parametrize("rows,vocab,hidden", [(1, 32000, 2048), (3, 512, 256), (8, 1000, 2048)])
+def test_lmhead_argmax_bit_exact(pkg, lib, rows, vocab, hidden):
+    rng = np.random.default_rng(vocab + rows)
+    x = rng.standard_normal((rows, hidden), dtype=np.float32)
+    g = (1 + 0.1 * rng.standard_normal(hidden, dtype=np.float32)).astype(np.float32)
+    wf = (rng.standard_normal((hidden, vocab), dtype=np.float32) * 0.02).astype(np.float32)
+    lw = pkg.quantize_weight(wf, "channel")
+    tok = torch.empty(rows, dtype=torch.int32, device="cuda")
+    logits = torch.empty((rows, vocab), dtype=torch.float32, device="cuda")
+    pkg.shim.check(lib.tl_lmhead_argmax(dev(x).data_ptr(), dev(g).data_ptr(), 1e-5,
+                                        dev(np.ascontiguousarray(lw.w.T)).data_ptr(), dev(lw.scale).data_ptr(),
+                                        rows, vocab, hidden, tok.data_ptr(), logits.data_ptr(), stream()),
+                   "lmhead")
+    ref = []
+    for r in range(rows):
+        h = G.rms_norm(x[r:r + 1], g, 1e-5)
+        lg, _, _, _ = G.linear_q(h, lw.w, lw.scale)
+        ref.append(lg[0])
+    ref = np.array(ref)
+    np.testing.assert_array_equal(logits.cpu().numpy(), ref)
+    assert list(tok.cpu().numpy()) == [G.argmax_first(r) for r in ref]
+
+
+def test_argmax_tie_breaks_to_lowest_id(pkg, lib):
+    """Equal logits: the lower token id wins (argmax_reduction.sv:47-58)."""
+    hidden, vocab = 64, 300
+    x = np.ones((1, hidden), np.float32)
+    g = np.ones(hidden, np.float32)
+    w = np.zeros((hidden, vocab), np.int8)
+    w[:, 17] = 5
+    w[:, 230] = 5
+    w[:, 3] = 4
+    s = np.full(vocab, 0.01, np.float64)
+    tok = torch.empty(1, dtype=torch.int32, device="cuda")
+    pkg.shim.check(lib.tl_lmhead_argmax(dev(x).data_ptr(), dev(g).data_ptr(), 1e-5,
+                                        dev(np.ascontiguousarray(w.T)).data_ptr(), dev(s).data_ptr(),
+                                        1, vocab, hidden, tok.data_ptr(), None, stream()), "lmhead")
+    assert int(tok.item()) == 17
+
+
+def test_invalid_shapes_rejected(pkg, lib):
+    a = torch.zeros((1, 24), dtype=torch.int8, device="cuda")
+    c = torch.zeros((1, 8), dtype=torch.int32, device="cuda")
+    assert lib.tl_gemm_i8(a.data_ptr(), a.data_ptr(), c.data_ptr(), 1, 8, 24, stream()) == 16
+    assert lib.tl_gemm_i8(None, a.data_ptr(), c.data_ptr(), 1, 8, 16, stream()) == 16
