@@ -200,14 +200,18 @@ TL_API tl_status tl_prefill_batch_device(tl_engine* eng, uint32_t n_seqs, const 
 TL_API tl_status tl_decode_rewind(tl_engine* eng, uint32_t n_seqs, uint32_t position);
 TL_API tl_status tl_synchronize(tl_engine* eng);
 /* Times each decode-step kernel kind in isolation on the engine stream with
- * CUDA events: [0] norm+QKV GEMV, [1] attention (+RoPE, KV append),
- * [2] O GEMV + residual, [3] norm+gate/up GEMV + SiLU*up, [4] down GEMV +
- * residual, [5] final norm + LM head + argmax. Layers are cycled so weights
- * come from HBM as in a real step; the LM head (one matrix) is preceded by an
- * L2 flush outside the timed interval. avg_ms_out receives 6 averages. The
- * rows must have been prefilled (tl_prefill_batch_device). */
+ * CUDA events: [0] QKV projection, [1] attention (+RoPE), [2] O projection +
+ * residual, [3] gate/up + SiLU*up, [4] down + residual, [5] LM head + argmax,
+ * [6] RMSNorm+quantize rows, [7] quantize rows. For n_seqs < 16 the
+ * projections are the dp4a GEMVs with the RMSNorm/quantize prologue fused
+ * ([6], [7] = 0); for n_seqs >= 16 they are the tcgen05 GEMMs. Layers are
+ * cycled so weights come from HBM as in a real step; the LM head (one matrix)
+ * is preceded by an L2 flush outside the timed interval. avg_ms_out receives
+ * 8 averages. The rows must have been prefilled (tl_prefill_batch_device). */
 TL_API tl_status tl_profile_decode_kernels(tl_engine* eng, uint32_t n_seqs, uint32_t iters,
                                            float* avg_ms_out);
+/* Number of kernels one decode step of n_seqs rows launches. */
+TL_API int32_t tl_decode_step_kernel_count_rows(tl_engine* eng, uint32_t n_seqs);
 /* Number of kernels one decode step launches (for launch accounting). */
 TL_API int32_t tl_decode_step_kernel_count(tl_engine* eng);
 TL_API void* tl_engine_stream(tl_engine* eng);
@@ -216,6 +220,10 @@ TL_API void* tl_engine_stream(tl_engine* eng);
 /* All operator entry points: device pointers, `stream` is a cudaStream_t
  * (NULL = legacy default stream). Shapes must satisfy K % 16 == 0 and
  * 16-byte aligned int8 rows. */
+
+/* Waits for the device and reports TL_ERR_TIMEOUT if a tensor-core kernel
+ * gave up on a bounded pipeline wait since the last call (then clears it). */
+TL_API tl_status tl_device_error(void);
 
 /* int8 W[K][N] -> W^T[N][K] (device to device). */
 TL_API tl_status tl_transpose_i8(const int8_t* w_kn, int8_t* w_nk, int32_t K, int32_t N, void* stream);

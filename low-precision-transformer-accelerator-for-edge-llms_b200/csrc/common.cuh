@@ -89,62 +89,57 @@ TL_DEV int requant_q16(int acc, uint32_t scale_q16, bool nonneg) {
 // NumPy reduces a contiguous float32 row as: runs longer than 128 split at
 // n/2 rounded down to a multiple of 8; a run of 8..128 keeps eight running
 // sums over stride 8, folded ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)), then adds
-// the n%8 tail in order; a run shorter than 8 is a plain ordered sum.
-// pw_plan() lists the leaf runs in order (depth-first), pw_fold() adds leaf
-// sums back up the same binary tree.
-constexpr int kPwMaxLeaves = 128;
-
-struct PwPlan {
-  int n_leaves;
-  int start[kPwMaxLeaves];
-  int len[kPwMaxLeaves];
+// the n%8 tail in order. When every split is exact (n = 2^a * L, L <= 128,
+// L % 8 == 0 -- true for TinyLlama's hidden size 2048 = 16 x 128) the tree
+// is balanced: 2^a leaves of L elements, combined level by level
+// left + right. norm_plan() checks that shape on the host; the device side
+// (block_sumsq_numpy) evaluates exactly that tree.
+struct NormPlan {
+  int leaf_len;   // L
+  int n_leaves;   // 2^a
 };
 
-TL_DEV void pw_plan_rec(PwPlan& p, int start, int n) {
-  if (n <= 128) {
-    p.start[p.n_leaves] = start;
-    p.len[p.n_leaves] = n;
-    p.n_leaves++;
-    return;
+inline bool norm_plan(int n, NormPlan* p) {
+  int len = n;
+  int leaves = 1;
+  while (len > 128) {
+    int h = len / 2;
+    h -= h % 8;
+    if (h * 2 != len) return false;
+    len = h;
+    leaves *= 2;
   }
-  int h = n / 2;
-  h -= h % 8;
-  pw_plan_rec(p, start, h);
-  pw_plan_rec(p, start + h, n - h);
+  if (len < 8 || len % 8 != 0) return false;
+  p->leaf_len = len;
+  p->n_leaves = leaves;
+  return leaves <= 1024;
 }
 
-// Leaf sum of v[0..n) for n <= 128, sequential per lane group: lane j (0..7)
-// of an 8-lane group accumulates r[j]; lane 0 folds. Returns the value in
-// lane 0 of the group (others hold partials).
-TL_DEV float pw_leaf_group8(const float* v, int n, int j /*0..7*/, unsigned mask) {
-  if (n < 8) {
-    float acc = 0.0f;
-    if (j == 0)
-      for (int i = 0; i < n; ++i) acc = __fadd_rn(acc, v[i]);
-    return acc;
+// Sum of v[i]^2 over v[0..n) in NumPy's order; all threads of the block call
+// it; `part` is shared scratch of n_leaves*8 floats, `leaf` of n_leaves.
+// Returns the total in every thread.
+TL_DEV float block_sumsq_numpy(const float* v, NormPlan plan, float* part, float* leaf) {
+  const int tid = threadIdx.x, bs = blockDim.x;
+  const int L = plan.leaf_len, nl = plan.n_leaves;
+  for (int idx = tid; idx < nl * 8; idx += bs) {
+    const int l = idx >> 3, j = idx & 7;
+    const float* x = v + l * L;
+    float r = __fmul_rn(x[j], x[j]);
+    for (int i = 8 + j; i < L; i += 8) r = __fadd_rn(r, __fmul_rn(x[i], x[i]));
+    part[idx] = r;
   }
-  int full = n - (n % 8);
-  float r = v[j];
-  for (int i = 8 + j; i < full; i += 8) r = __fadd_rn(r, v[i]);
-  // fold ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) inside the 8-lane group
-  float r1 = __shfl_down_sync(mask, r, 1, 8);
-  float s01 = __fadd_rn(r, r1);                 // valid in even lanes
-  float s23 = __shfl_down_sync(mask, s01, 2, 8);
-  float s0123 = __fadd_rn(s01, s23);            // valid in lanes 0 and 4
-  float s4567 = __shfl_down_sync(mask, s0123, 4, 8);
-  float res = __fadd_rn(s0123, s4567);          // valid in lane 0
-  if (j == 0)
-    for (int i = full; i < n; ++i) res = __fadd_rn(res, v[i]);
-  return res;
-}
-
-TL_DEV float pw_fold_rec(const float* leaf_sum, int& idx, int n) {
-  if (n <= 128) return leaf_sum[idx++];
-  int h = n / 2;
-  h -= h % 8;
-  float a = pw_fold_rec(leaf_sum, idx, h);
-  float b = pw_fold_rec(leaf_sum, idx, n - h);
-  return __fadd_rn(a, b);
+  __syncthreads();
+  for (int l = tid; l < nl; l += bs) {
+    const float* q = part + l * 8;
+    leaf[l] = __fadd_rn(__fadd_rn(__fadd_rn(q[0], q[1]), __fadd_rn(q[2], q[3])),
+                        __fadd_rn(__fadd_rn(q[4], q[5]), __fadd_rn(q[6], q[7])));
+  }
+  __syncthreads();
+  for (int st = 1; st < nl; st *= 2) {
+    for (int l = tid * 2 * st; l < nl; l += bs * 2 * st) leaf[l] = __fadd_rn(leaf[l], leaf[l + st]);
+    __syncthreads();
+  }
+  return leaf[0];
 }
 
 }  // namespace tl

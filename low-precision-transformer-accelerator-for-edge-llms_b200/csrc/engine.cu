@@ -82,8 +82,14 @@ struct DecodeBufs {
   int32_t* argmax = nullptr;
   unsigned long long* am_partial = nullptr;
   unsigned int* am_counter = nullptr;
-  float* logits = nullptr;  // [rows][V], teacher-forced calls only
+  float* logits = nullptr;  // [rows][V]
+  int8_t* xq = nullptr;     // [rows][max(D, F)] int8 activations (tensor-core path)
+  float* amax = nullptr;    // [rows] per-row absmax of the activation in xq
 };
+
+// Batches of at least this many rows use the tcgen05 GEMM; smaller ones the
+// dp4a GEMV with the fused RMSNorm/quantize prologue.
+constexpr int kTcMinRows = 16;
 
 struct PrefillBufs {
   size_t rows = 0;
@@ -132,6 +138,8 @@ tl_status check_cfg(const tl_config* c) {
     return TL_ERR_INVALID_ARGUMENT;
   if (c->num_layers <= 0 || c->vocab_size <= 0 || c->max_positions <= 0 || c->max_batch <= 0)
     return TL_ERR_INVALID_ARGUMENT;
+  NormPlan plan;
+  if (!norm_plan(c->hidden_size, &plan)) return TL_ERR_INVALID_ARGUMENT;  // RMSNorm reduction tree
   return TL_OK;
 }
 
@@ -167,6 +175,9 @@ tl_status alloc_decode(tl_engine* e) {
   TL_TRY(dmalloc(&d.argmax, B));
   TL_TRY(dmalloc(&d.am_partial, gemv_argmax_partials(B, e->V)));
   TL_TRY(dmalloc(&d.am_counter, gemv_argmax_row_blocks(B) + 1));
+  TL_TRY(dmalloc(&d.logits, static_cast<size_t>(B) * e->V));
+  TL_TRY(dmalloc(&d.xq, static_cast<size_t>(B) * std::max(e->D, e->F)));
+  TL_TRY(dmalloc(&d.amax, B));
   TL_CU(cudaMemset(d.am_counter, 0, (gemv_argmax_row_blocks(B) + 1) * sizeof(unsigned int)));
   TL_CU(cudaMemset(d.active, 0, B * sizeof(int)));
   TL_CU(cudaMemset(d.stop, 0, B * sizeof(int)));
@@ -204,11 +215,73 @@ void invalidate_graphs(tl_engine* e) {
   e->graphs.clear();
 }
 
+// One tcgen05 GEMM: out = epi(X[M][K] . W^T[N][K]); plan (tensor maps, tile,
+// split-K) made on the host, so this is also safe inside stream capture.
+tl_status tc_gemm(tl_engine* e, const int8_t* w, int N, const int8_t* x, int M, int K, const TcArgs& args,
+                  bool pdl) {
+  TcPlan p;
+  TL_CU(tc_make_plan(&p, w, N, x, M, K, device_sm_count()));
+  TL_CU(launch_gemm_tc(p, args, e->stream, pdl));
+  return TL_OK;
+}
+
+// Batched decode step on the tensor cores (M >= kTcMinRows rows): per row
+// RMSNorm + INT8 quantization kernels feed tcgen05 GEMMs whose epilogues
+// dequantize, add the residual or apply SiLU*up.
+tl_status enqueue_decode_step_tc(tl_engine* e, int M, bool finalize) {
+  DecodeBufs& d = e->dec;
+  cudaStream_t s = e->stream;
+  const bool pdl = e->use_pdl;
+  const float eps = e->cfg.rms_norm_eps;
+  TL_CU(launch_embed(e->embed, d.tokens, d.x, M, e->D, e->V, s, pdl));
+  for (int l = 0; l < e->L; ++l) {
+    const Layer& ly = e->layers[l];
+    TL_CU(launch_norm_quant_rows(d.x, ly.g1, eps, M, e->D, d.xq, d.amax, s, pdl));
+    TcArgs q;
+    q.epi = EPI_F32; q.w_scale = ly.sqkv; q.in_absmax = d.amax; q.rows_per_group = 1; q.out_f32 = d.qkv;
+    TL_TRY(tc_gemm(e, ly.wqkv, e->Nqkv, d.xq, M, e->D, q, pdl));
+    AttnDecodeArgs at;
+    at.qkv = d.qkv; at.ld = e->Nqkv; at.pos = d.pos; at.slot = d.slots; at.active = d.active;
+    at.kc = e->kc; at.vc = e->vc; at.ks = e->ks; at.vs = e->vs;
+    at.layer = l; at.L = e->L; at.H = e->H; at.Hkv = e->Hkv; at.P = e->P; at.M = M;
+    at.cos = e->cosT; at.sin = e->sinT; at.out = d.att;
+    TL_CU(launch_attn_decode(at, s, pdl));
+    TL_CU(launch_quant_rows(d.att, M, e->Dq, d.xq, d.amax, s, pdl));
+    TcArgs o;
+    o.epi = EPI_RESID; o.w_scale = ly.so; o.in_absmax = d.amax; o.rows_per_group = 1; o.out_f32 = d.x;
+    o.resid = d.x;
+    TL_TRY(tc_gemm(e, ly.wo, e->D, d.xq, M, e->Dq, o, pdl));
+    TL_CU(launch_norm_quant_rows(d.x, ly.g2, eps, M, e->D, d.xq, d.amax, s, pdl));
+    TcArgs gu;
+    gu.epi = EPI_SILU; gu.w_scale = ly.sgu; gu.in_absmax = d.amax; gu.rows_per_group = 1; gu.out_f32 = d.hid;
+    TL_TRY(tc_gemm(e, ly.wgu, 2 * e->F, d.xq, M, e->D, gu, pdl));
+    TL_CU(launch_quant_rows(d.hid, M, e->F, d.xq, d.amax, s, pdl));
+    TcArgs dn;
+    dn.epi = EPI_RESID; dn.w_scale = ly.sd; dn.in_absmax = d.amax; dn.rows_per_group = 1; dn.out_f32 = d.x;
+    dn.resid = d.x;
+    TL_TRY(tc_gemm(e, ly.wd, e->D, d.xq, M, e->F, dn, pdl));
+  }
+  TL_CU(launch_norm_quant_rows(d.x, e->gfinal, eps, M, e->D, d.xq, d.amax, s, pdl));
+  TcArgs lm;
+  lm.epi = EPI_F32; lm.w_scale = e->slm; lm.in_absmax = d.amax; lm.rows_per_group = 1; lm.out_f32 = d.logits;
+  TL_TRY(tc_gemm(e, e->wlm, e->V, d.xq, M, e->D, lm, pdl));
+  TL_CU(launch_row_argmax(d.logits, M, e->V, d.argmax, s, pdl));
+  if (finalize) {
+    StepArgs st;
+    st.M = M; st.argmax = d.argmax; st.tokens = d.tokens; st.pos = d.pos; st.active = d.active;
+    st.count = d.count; st.stop = d.stop; st.out_ids = d.out_ids; st.out_stride = e->P;
+    st.run = d.run; st.P = e->P;
+    TL_CU(launch_step_finalize(st, s, pdl));
+  }
+  return TL_OK;
+}
+
 // ------------------------------------------------------------- decode step
 // One decode step for rows 0..M-1 (row m uses KV slot dec.slots[m]). All
 // inputs (token, position, active) come from device memory, so the sequence
 // is graph-capturable.
 tl_status enqueue_decode_step(tl_engine* e, int M, float* logits, bool finalize) {
+  if (M >= kTcMinRows && !logits) return enqueue_decode_step_tc(e, M, finalize);
   DecodeBufs& d = e->dec;
   cudaStream_t s = e->stream;
   const bool pdl = e->use_pdl;
@@ -282,6 +355,31 @@ tl_status get_graph(tl_engine* e, int M, cudaGraphExec_t* out) {
 }
 
 // ------------------------------------------------------------------ prefill
+// One prefill projection from pf.xq (rows grouped by sequence of S tokens):
+// tcgen05 for R >= kTcMinRows rows, else the dp4a GEMV. out_absmax (per
+// sequence) only where no split-K is used; otherwise a separate pass.
+tl_status prefill_gemm(tl_engine* e, const int8_t* w, const double* ws, int N, int K, int R, int S,
+                       const float* in_absmax, int epi, float* out, const float* resid, float* out_absmax) {
+  PrefillBufs& p = e->pf;
+  if (R >= kTcMinRows) {
+    TcPlan plan;
+    TL_CU(tc_make_plan(&plan, w, N, p.xq, R, K, device_sm_count()));
+    TcArgs a;
+    a.epi = epi; a.w_scale = ws; a.in_absmax = in_absmax; a.rows_per_group = S; a.out_f32 = out;
+    a.resid = resid;
+    a.out_absmax = plan.k_splits == 1 ? out_absmax : nullptr;
+    TL_CU(launch_gemm_tc(plan, a, e->stream, false));
+    if (out_absmax && plan.k_splits > 1)
+      TL_CU(launch_absmax_rows(out, R, epi == EPI_SILU ? N / 2 : N, S, out_absmax, e->stream));
+    return TL_OK;
+  }
+  GemvArgs g;
+  g.x_q = p.xq; g.in_absmax = in_absmax; g.rows_per_group = S;
+  g.w = w; g.w_scale = ws; g.M = R; g.N = N; g.K = K; g.out_f32 = out; g.resid = resid; g.out_absmax = out_absmax;
+  TL_CU(launch_gemv(PRO_Q8, epi, g, e->stream, false));
+  return TL_OK;
+}
+
 // n_seq sequences of S tokens each, token ids already in pf.ids; slots
 // slot_base..slot_base+n_seq-1. Leaves the first greedy token of each
 // sequence in dec.argmax[0..n_seq) when `head` is set.
@@ -300,33 +398,21 @@ tl_status enqueue_prefill(tl_engine* e, int n_seq, int S, int slot_base, bool he
     // attention block
     TL_CU(launch_rmsnorm_rows(p.x, ly.g1, eps, p.h, am, R, e->D, S, s));
     TL_CU(launch_quantize_rows(p.h, am, R, e->D, S, p.xq, s));
-    GemvArgs q;
-    q.x_q = p.xq; q.in_absmax = am; q.rows_per_group = S;
-    q.w = ly.wqkv; q.w_scale = ly.sqkv; q.M = R; q.N = e->Nqkv; q.K = e->D; q.out_f32 = p.qkv;
-    TL_CU(launch_gemv(PRO_Q8, EPI_F32, q, s, false));
+    TL_TRY(prefill_gemm(e, ly.wqkv, ly.sqkv, e->Nqkv, e->D, R, S, am, EPI_F32, p.qkv, nullptr, nullptr));
     TL_CU(launch_rope_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->cosT, e->sinT, kva, s));
     TL_CU(launch_kv_write_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, kva, e->kc, e->vc, e->ks, e->vs,
                                   slot_base, l, e->L, e->P, s));
     TL_CU(launch_attn_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->kc, e->vc, e->ks, e->vs, slot_base,
                               l, e->L, e->P, p.att, am + n_seq, s));
     TL_CU(launch_quantize_rows(p.att, am + n_seq, R, e->Dq, S, p.xq, s));
-    GemvArgs o;
-    o.x_q = p.xq; o.in_absmax = am + n_seq; o.rows_per_group = S;
-    o.w = ly.wo; o.w_scale = ly.so; o.M = R; o.N = e->D; o.K = e->Dq; o.out_f32 = p.x; o.resid = p.x;
-    TL_CU(launch_gemv(PRO_Q8, EPI_RESID, o, s, false));
+    TL_TRY(prefill_gemm(e, ly.wo, ly.so, e->D, e->Dq, R, S, am + n_seq, EPI_RESID, p.x, p.x, nullptr));
     // feed-forward block
     TL_CU(launch_rmsnorm_rows(p.x, ly.g2, eps, p.h, am + 2 * n_seq, R, e->D, S, s));
     TL_CU(launch_quantize_rows(p.h, am + 2 * n_seq, R, e->D, S, p.xq, s));
-    GemvArgs gu;
-    gu.x_q = p.xq; gu.in_absmax = am + 2 * n_seq; gu.rows_per_group = S;
-    gu.w = ly.wgu; gu.w_scale = ly.sgu; gu.M = R; gu.N = 2 * e->F; gu.K = e->D; gu.out_f32 = p.hid;
-    gu.out_absmax = am + 3 * n_seq;
-    TL_CU(launch_gemv(PRO_Q8, EPI_SILU, gu, s, false));
+    TL_TRY(prefill_gemm(e, ly.wgu, ly.sgu, 2 * e->F, e->D, R, S, am + 2 * n_seq, EPI_SILU, p.hid, nullptr,
+                        am + 3 * n_seq));
     TL_CU(launch_quantize_rows(p.hid, am + 3 * n_seq, R, e->F, S, p.xq, s));
-    GemvArgs dn;
-    dn.x_q = p.xq; dn.in_absmax = am + 3 * n_seq; dn.rows_per_group = S;
-    dn.w = ly.wd; dn.w_scale = ly.sd; dn.M = R; dn.N = e->D; dn.K = e->F; dn.out_f32 = p.x; dn.resid = p.x;
-    TL_CU(launch_gemv(PRO_Q8, EPI_RESID, dn, s, false));
+    TL_TRY(prefill_gemm(e, ly.wd, ly.sd, e->D, e->F, R, S, am + 3 * n_seq, EPI_RESID, p.x, p.x, nullptr));
   }
   if (!head) return TL_OK;
   float* amf = p.amax + static_cast<size_t>(e->L) * 4 * n_seq;
@@ -379,6 +465,9 @@ tl_status run_decode_loop(tl_engine* e, int M, int budget, bool* aborted) {
     for (int m = 0; m < M; ++m) any |= e->h_pinned[m] != 0;
     if (!any) break;
   }
+  unsigned int code = 0;
+  TL_CU(tc_read_error(&code));
+  if (code) return TL_ERR_TIMEOUT;
   return TL_OK;
 }
 
@@ -522,6 +611,7 @@ tl_status tl_destroy(tl_engine* e) {
   cudaFree(d.x); cudaFree(d.qkv); cudaFree(d.att); cudaFree(d.hid); cudaFree(d.tokens); cudaFree(d.pos);
   cudaFree(d.slots); cudaFree(d.active); cudaFree(d.count); cudaFree(d.stop); cudaFree(d.out_ids);
   cudaFree(d.run); cudaFree(d.argmax); cudaFree(d.am_partial); cudaFree(d.am_counter); cudaFree(d.logits);
+  cudaFree(d.xq); cudaFree(d.amax);
   PrefillBufs& p = e->pf;
   cudaFree(p.ids); cudaFree(p.x); cudaFree(p.h); cudaFree(p.qkv); cudaFree(p.att); cudaFree(p.hid);
   cudaFree(p.xq); cudaFree(p.amax); cudaFree(p.kvamax);
@@ -866,8 +956,15 @@ tl_status tl_decode_rewind(tl_engine* e, uint32_t n_seqs, uint32_t position) {
 
 tl_status tl_synchronize(tl_engine* e) {
   if (!e) return TL_ERR_INVALID_ARGUMENT;
+  TL_CU(cudaSetDevice(e->device));
   TL_CU(cudaStreamSynchronize(e->stream));
   TL_CU(cudaGetLastError());
+  unsigned int code = 0;
+  TL_CU(tc_read_error(&code));
+  if (code) {
+    g_last_error = "tensor-core pipeline wait expired (code " + std::to_string(code) + ")";
+    return TL_ERR_TIMEOUT;
+  }
   return TL_OK;
 }
 
@@ -877,6 +974,7 @@ tl_status tl_profile_decode_kernels(tl_engine* e, uint32_t n_seqs, uint32_t iter
   if (n_seqs == 0 || n_seqs > static_cast<uint32_t>(e->B)) return TL_ERR_OUT_OF_RANGE;
   TL_CU(cudaSetDevice(e->device));
   const int M = static_cast<int>(n_seqs);
+  const bool tc = M >= kTcMinRows;
   DecodeBufs& d = e->dec;
   cudaStream_t s = e->stream;
   const size_t flush_bytes = 256ull << 20;
@@ -885,57 +983,101 @@ tl_status tl_profile_decode_kernels(tl_engine* e, uint32_t n_seqs, uint32_t iter
   std::vector<cudaEvent_t> ev(2 * iters);
   for (auto& x : ev) TL_CU(cudaEventCreate(&x));
   tl_status result = TL_OK;
-  for (int kind = 0; kind < 6 && result == TL_OK; ++kind) {
+  const float eps = e->cfg.rms_norm_eps;
+  for (int kind = 0; kind < 8 && result == TL_OK; ++kind) {
+    if (!tc && kind >= 6) {
+      avg_ms_out[kind] = 0.0f;
+      continue;
+    }
     for (uint32_t it = 0; it < iters; ++it) {
       const int l = static_cast<int>(it % e->L);
       const Layer& ly = e->layers[l];
       if (kind == 5) TL_CU(cudaMemsetAsync(flush, it & 0xff, flush_bytes, s));
       TL_CU(cudaEventRecord(ev[2 * it], s));
       cudaError_t ce = cudaSuccess;
+      tl_status ts = TL_OK;
       GemvArgs g;
       g.M = M;
-      g.eps = e->cfg.rms_norm_eps;
+      g.eps = eps;
+      TcArgs t;
+      t.in_absmax = d.amax;
+      t.rows_per_group = 1;
       switch (kind) {
         case 0:
-          g.x_f32 = d.x; g.gamma = ly.g1; g.w = ly.wqkv; g.w_scale = ly.sqkv; g.N = e->Nqkv; g.K = e->D;
-          g.out_f32 = d.qkv;
-          ce = launch_gemv(PRO_NORM, EPI_F32, g, s, false);
+          if (tc) {
+            t.epi = EPI_F32; t.w_scale = ly.sqkv; t.out_f32 = d.qkv;
+            ts = tc_gemm(e, ly.wqkv, e->Nqkv, d.xq, M, e->D, t, false);
+          } else {
+            g.x_f32 = d.x; g.gamma = ly.g1; g.w = ly.wqkv; g.w_scale = ly.sqkv; g.N = e->Nqkv; g.K = e->D;
+            g.out_f32 = d.qkv;
+            ce = launch_gemv(PRO_NORM, EPI_F32, g, s, false);
+          }
           break;
         case 1: {
           AttnDecodeArgs at;
-          at.qkv = d.qkv; at.ld = e->Nqkv; at.pos = d.pos; at.slot = d.slots; at.active = nullptr;
+          at.qkv = d.qkv; at.ld = e->Nqkv; at.pos = d.pos; at.slot = d.slots;
           at.kc = e->kc; at.vc = e->vc; at.ks = e->ks; at.vs = e->vs; at.layer = l; at.L = e->L;
           at.H = e->H; at.Hkv = e->Hkv; at.P = e->P; at.M = M; at.cos = e->cosT; at.sin = e->sinT;
           at.out = d.att;
-          // profile the read side only: no KV append, row p is read as stored
-          at.active = d.stop;  // stop[] is 0 for running rows -> append disabled
+          at.active = d.stop;  // stop[] is 0 for running rows: read side only, no KV append
           ce = launch_attn_decode(at, s, false);
           break;
         }
         case 2:
-          g.x_f32 = d.att; g.w = ly.wo; g.w_scale = ly.so; g.N = e->D; g.K = e->Dq; g.out_f32 = d.hid;
-          g.resid = d.hid;
-          ce = launch_gemv(PRO_F32, EPI_RESID, g, s, false);
+          if (tc) {
+            t.epi = EPI_RESID; t.w_scale = ly.so; t.out_f32 = d.hid; t.resid = d.hid;
+            ts = tc_gemm(e, ly.wo, e->D, d.xq, M, e->Dq, t, false);
+          } else {
+            g.x_f32 = d.att; g.w = ly.wo; g.w_scale = ly.so; g.N = e->D; g.K = e->Dq; g.out_f32 = d.hid;
+            g.resid = d.hid;
+            ce = launch_gemv(PRO_F32, EPI_RESID, g, s, false);
+          }
           break;
         case 3:
-          g.x_f32 = d.x; g.gamma = ly.g2; g.w = ly.wgu; g.w_scale = ly.sgu; g.N = 2 * e->F; g.K = e->D;
-          g.out_f32 = d.hid;
-          ce = launch_gemv(PRO_NORM, EPI_SILU, g, s, false);
+          if (tc) {
+            t.epi = EPI_SILU; t.w_scale = ly.sgu; t.out_f32 = d.hid;
+            ts = tc_gemm(e, ly.wgu, 2 * e->F, d.xq, M, e->D, t, false);
+          } else {
+            g.x_f32 = d.x; g.gamma = ly.g2; g.w = ly.wgu; g.w_scale = ly.sgu; g.N = 2 * e->F; g.K = e->D;
+            g.out_f32 = d.hid;
+            ce = launch_gemv(PRO_NORM, EPI_SILU, g, s, false);
+          }
           break;
         case 4:
-          g.x_f32 = d.hid; g.w = ly.wd; g.w_scale = ly.sd; g.N = e->D; g.K = e->F; g.out_f32 = d.att;
-          g.resid = d.att;
-          ce = launch_gemv(PRO_F32, EPI_RESID, g, s, false);
+          if (tc) {
+            t.epi = EPI_RESID; t.w_scale = ly.sd; t.out_f32 = d.att; t.resid = d.att;
+            ts = tc_gemm(e, ly.wd, e->D, d.xq, M, e->F, t, false);
+          } else {
+            g.x_f32 = d.hid; g.w = ly.wd; g.w_scale = ly.sd; g.N = e->D; g.K = e->F; g.out_f32 = d.att;
+            g.resid = d.att;
+            ce = launch_gemv(PRO_F32, EPI_RESID, g, s, false);
+          }
           break;
         case 5:
-          g.x_f32 = d.x; g.gamma = e->gfinal; g.w = e->wlm; g.w_scale = e->slm; g.N = e->V; g.K = e->D;
-          g.am_partial = d.am_partial; g.am_counter = d.am_counter; g.am_token = d.argmax;
-          ce = launch_gemv(PRO_NORM, EPI_ARGMAX, g, s, false);
+          if (tc) {
+            t.epi = EPI_F32; t.w_scale = e->slm; t.out_f32 = d.logits;
+            ts = tc_gemm(e, e->wlm, e->V, d.xq, M, e->D, t, false);
+            if (ts == TL_OK) ce = launch_row_argmax(d.logits, M, e->V, d.argmax, s, false);
+          } else {
+            g.x_f32 = d.x; g.gamma = e->gfinal; g.w = e->wlm; g.w_scale = e->slm; g.N = e->V; g.K = e->D;
+            g.am_partial = d.am_partial; g.am_counter = d.am_counter; g.am_token = d.argmax;
+            ce = launch_gemv(PRO_NORM, EPI_ARGMAX, g, s, false);
+          }
+          break;
+        case 6:
+          ce = launch_norm_quant_rows(d.x, ly.g1, eps, M, e->D, d.xq, d.amax, s, false);
+          break;
+        case 7:
+          ce = launch_quant_rows(d.hid, M, e->F, d.xq, d.amax, s, false);
           break;
       }
       if (ce != cudaSuccess) {
         g_last_error = cudaGetErrorString(ce);
         result = TL_ERR_CUDA;
+        break;
+      }
+      if (ts != TL_OK) {
+        result = ts;
         break;
       }
       TL_CU(cudaEventRecord(ev[2 * it + 1], s));
@@ -957,6 +1099,12 @@ tl_status tl_profile_decode_kernels(tl_engine* e, uint32_t n_seqs, uint32_t iter
 }
 
 int32_t tl_decode_step_kernel_count(tl_engine* e) { return e ? 1 + 5 * e->L + 2 : 0; }
+
+int32_t tl_decode_step_kernel_count_rows(tl_engine* e, uint32_t n_seqs) {
+  if (!e) return 0;
+  if (static_cast<int>(n_seqs) >= kTcMinRows) return 1 + 8 * e->L + 3 + 1;
+  return 1 + 5 * e->L + 2;
+}
 
 void* tl_engine_stream(tl_engine* e) { return e ? static_cast<void*>(e->stream) : nullptr; }
 

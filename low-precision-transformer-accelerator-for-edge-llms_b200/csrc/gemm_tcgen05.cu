@@ -1,0 +1,488 @@
+// gemm_tcgen05.cu -- INT8 x INT8 -> INT32 GEMM on the 5th-generation tensor
+// cores (tcgen05.mma kind::i8), TMA-fed shared memory, TMEM accumulators.
+//
+// The reference reuses one shared INT8 GEMM engine for every projection
+// (rtl/compute/shared_gemm_engine.sv:127-168; numerics of quantized_linear,
+// model/tinyllama_gemm_int8.py:59-88). Here it is one kernel with the
+// engine's fused epilogues (dequantize, residual add, SiLU*up, Q16.16
+// requantize of rtl/compute/requantize_unit.sv:39-93, raw INT32).
+//
+// Orientation ("swap AB"): the weight tile is the MMA's A operand (128 output
+// channels per CTA, K-major W^T[N][K]) and the token tile is B (BN tokens,
+// K-major X[M][K]); the accumulator D[n][m] lives in TMEM as 128 lanes x BN
+// columns. Decode batches of 16..64 tokens then still fill the 128-row MMA,
+// and the epilogue thread that owns TMEM lane n writes out[m][n] for
+// consecutive n across a warp (coalesced).
+//
+// Pipeline per CTA (128 threads): warp 0 lane 0 issues TMA loads into a ring
+// of `stages` (A 16 KB + B BN*128 B, 128-byte swizzle); warp 1 lane 0 issues
+// four 128xBNx32 MMAs per stage and commits each stage back to its producer
+// barrier; all four warps then drain TMEM with tcgen05.ld. With k_splits > 1
+// the CTAs of one tile each reduce a K range and add their INT32 partials
+// into an L2-resident workspace (integer addition: exact, order-free); the
+// last CTA of the tile runs the epilogue and re-zeroes the workspace.
+//
+// No TMA multicast is used anywhere. Every mbarrier wait is bounded (about a
+// second of clock cycles); on expiry the kernel records an error code in
+// g_tc_error and skips ahead so that TMEM is still freed and the host sees
+// TL_ERR_TIMEOUT instead of a hung GPU.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdio>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace tl {
+
+__device__ unsigned int g_tc_error = 0;
+
+namespace {
+
+constexpr int kTcThreads = 128;
+constexpr int kTileN = 128;      // weight rows per CTA (MMA M)
+constexpr int kTileK = 128;      // bytes of K per stage (one 128-byte swizzle row)
+constexpr int kABytes = kTileN * kTileK;
+constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at 1.9 GHz
+
+TL_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+TL_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+TL_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+TL_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false (and the error word set) if the phase never completes.
+TL_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned code) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitCycles) {
+      atomicCAS(&g_tc_error, 0u, code);
+      return false;
+    }
+  }
+  return true;
+}
+
+TL_DEV void tma_load_2d(void* dst, const CUtensorMap* tm, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor, K-major tile of 128-byte rows with the
+// 128-byte swizzle: start>>4, leading offset 1 (16 B, unused for this
+// layout), stride offset 1024 B (8 rows), version 1, layout SWIZZLE_128B.
+TL_DEV uint64_t smem_desc_sw128(uint32_t addr) {
+  return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
+         (2ull << 61);
+}
+
+// Instruction descriptor, kind::i8: S32 accumulate, signed A and B, both
+// K-major, N>>3 at bit 17, M>>4 at bit 24.
+__host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+TL_DEV void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+TL_DEV void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+TL_DEV void tmem_ld16(uint32_t taddr, int* v) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+TL_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+TL_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+TL_DEV void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+TL_DEV uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+TL_DEV int ld_dsmem_s32(uint32_t local_addr, uint32_t peer) {
+  uint32_t remote;
+  int v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(peer));
+  asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(remote) : "memory");
+  return v;
+}
+
+TL_DEV float silu_mul_tc(float g, float u) {
+  float c = fminf(fmaxf(g, -60.0f), 60.0f);
+  float den = __fadd_rn(1.0f, expf(-c));
+  return __fmul_rn(__fdiv_rn(g, den), u);
+}
+
+// Epilogue of one group of 16 accumulators (columns m0c..m0c+15) of TMEM
+// lane n. Every lane of the warp calls it (the SiLU pairing shuffles).
+TL_DEV void tc_epilogue16(const TcArgs& a, int n, int m0c, const int* v) {
+  const bool n_ok = n < a.N;
+  if (a.epi == EPI_I32) {
+    if (!n_ok) return;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int m = m0c + j;
+      if (m < a.M) a.out_i32[static_cast<size_t>(m) * a.N + n] = v[j];
+    }
+    return;
+  }
+  if (a.epi == EPI_REQ) {
+    if (!n_ok) return;
+    const uint32_t sc = a.req_scale[a.req_per_col ? n : 0];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int m = m0c + j;
+      if (m < a.M) a.out_i8[static_cast<size_t>(m) * a.N + n] = static_cast<int8_t>(requant_q16(v[j], sc, a.req_nonneg != 0));
+    }
+    return;
+  }
+  const double sw = n_ok ? a.w_scale[n] : 0.0;
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int m = m0c + j;
+    const bool ok = n_ok && m < a.M;
+    const double sx = ok ? quant_scale64(a.in_absmax ? a.in_absmax[m / a.rows_per_group] : 0.0f) : 1.0;
+    const float y = ok ? dequant(v[j], sx, sw) : 0.0f;
+    float mag = 0.0f;
+    if (a.epi == EPI_SILU) {
+      const float partner = __shfl_xor_sync(0xffffffffu, y, 1);
+      if (ok && (lane & 1) == 0) {
+        const float h = silu_mul_tc(y, partner);
+        a.out_f32[static_cast<size_t>(m) * (a.N >> 1) + (n >> 1)] = h;
+        mag = fabsf(h);
+      }
+    } else if (ok) {
+      const size_t o = static_cast<size_t>(m) * a.N + n;
+      const float r = (a.epi == EPI_RESID) ? __fadd_rn(a.resid[o], y) : y;
+      a.out_f32[o] = r;
+      mag = fabsf(r);
+    }
+    if (a.out_absmax) {
+      mag = warp_max(mag);
+      if (lane == 0 && m < a.M) atomic_max_nonneg(a.out_absmax + m / a.rows_per_group, mag);
+    }
+  }
+}
+
+// Epilogue of a single accumulator (split-K path). The SiLU pairing of rows
+// (2j, 2j+1) uses the neighbouring lane, which owns row n^1 for the same m.
+TL_DEV void tc_epilogue1(const TcArgs& a, int n, int m, int acc) {
+  const bool ok = n < a.N && m < a.M;
+  if (a.epi == EPI_I32) {
+    if (ok) a.out_i32[static_cast<size_t>(m) * a.N + n] = acc;
+    return;
+  }
+  if (a.epi == EPI_REQ) {
+    if (ok) a.out_i8[static_cast<size_t>(m) * a.N + n] =
+        static_cast<int8_t>(requant_q16(acc, a.req_scale[a.req_per_col ? n : 0], a.req_nonneg != 0));
+    return;
+  }
+  const double sw = ok ? a.w_scale[n] : 0.0;
+  const double sx = ok ? quant_scale64(a.in_absmax ? a.in_absmax[m / a.rows_per_group] : 0.0f) : 1.0;
+  const float y = ok ? dequant(acc, sx, sw) : 0.0f;
+  if (a.epi == EPI_SILU) {
+    const float partner = __shfl_xor_sync(0xffffffffu, y, 1);
+    if (ok && (n & 1) == 0) a.out_f32[static_cast<size_t>(m) * (a.N >> 1) + (n >> 1)] = silu_mul_tc(y, partner);
+    return;
+  }
+  if (!ok) return;
+  const size_t o = static_cast<size_t>(m) * a.N + n;
+  a.out_f32[o] = (a.epi == EPI_RESID) ? __fadd_rn(a.resid[o], y) : y;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, TcArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int kBBytes = BN * kTileK;
+  constexpr int kStage = kABytes + kBBytes;
+  constexpr int kTmemCols = BN < 32 ? 32 : BN;
+  const int stages = a.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * kStage);
+  uint64_t* empty = full + stages;
+  uint64_t* done = empty + stages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * kTileN, m0 = blockIdx.y * BN;
+  const int nkb = (a.K + kTileK - 1) / kTileK;
+  const int kb0 = static_cast<int>(static_cast<long long>(blockIdx.z) * nkb / a.k_splits);
+  const int kb1 = static_cast<int>(static_cast<long long>(blockIdx.z + 1) * nkb / a.k_splits);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    mbar_init(done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_w)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_x)) : "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  pdl_wait();  // activations come from the previous kernel
+
+  bool ok = true;
+  if (warp == 0 && lane == 0) {
+    for (int kb = kb0, i = 0; kb < kb1 && ok; ++kb, ++i) {
+      const int s = i % stages, round = i / stages;
+      if (round > 0) ok = mbar_wait(empty + s, (round - 1) & 1, 1u);
+      if (!ok) break;
+      mbar_arrive_expect_tx(full + s, kStage);
+      tma_load_2d(smem + s * kStage, &tm_w, kb * kTileK, n0, full + s);
+      tma_load_2d(smem + s * kStage + kABytes, &tm_x, kb * kTileK, m0, full + s);
+    }
+  } else if (warp == 1 && lane == 0) {
+    constexpr uint32_t idesc = idesc_i8(kTileN, BN);
+    for (int kb = kb0, i = 0; kb < kb1 && ok; ++kb, ++i) {
+      const int s = i % stages, round = i / stages;
+      ok = mbar_wait(full + s, round & 1, 2u);
+      if (!ok) break;
+      tc_fence_after();
+      const uint64_t ad = smem_desc_sw128(smem_u32(smem + s * kStage));
+      const uint64_t bd = smem_desc_sw128(smem_u32(smem + s * kStage + kABytes));
+#pragma unroll
+      for (int kk = 0; kk < kTileK / 32; ++kk)
+        mma_i8(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+      mma_commit(empty + s);
+    }
+    mma_commit(done);  // arrives once every MMA issued above has completed
+  }
+  __syncwarp();
+  // all threads: accumulator ready (uniform across the CTA)
+  const bool ready = __syncthreads_and(mbar_wait(done, 0, 3u) ? 1 : 0) != 0;
+  tc_fence_after();
+  pdl_launch_dependents();
+
+  const int n = n0 + warp * 32 + lane;
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  if (a.k_splits == 1) {
+    if (ready && kb1 > kb0) {
+      for (int c = 0; c < BN / 16; ++c) {
+        int v[16];
+        tmem_ld16(lane_base + c * 16, v);
+        tc_epilogue16(a, n, m0 + c * 16, v);
+      }
+    }
+  } else {
+    // Split-K across the CTAs of one cluster (cluster dims 1 x 1 x k_splits):
+    // each CTA parks its INT32 partial tile [128 n][BN m] in its own shared
+    // memory (the operand ring is idle now), then CTA `rank` sums rows
+    // [rank*R, (rank+1)*R) over all peers through distributed shared memory
+    // and runs the epilogue for those rows. Both cluster barriers are reached
+    // by every CTA whatever happened before, so none can wait forever.
+    int* part = reinterpret_cast<int*>(smem);
+    const int nl = warp * 32 + lane;
+    if (ready) {
+      for (int c = 0; c < BN / 16; ++c) {
+        int v[16];
+        tmem_ld16(lane_base + c * 16, v);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) part[nl * BN + c * 16 + j] = v[j];
+      }
+    }
+    cluster_sync();
+    const int ks = a.k_splits;
+    const int rank = static_cast<int>(cluster_rank());
+    const int R = kTileN / ks;                 // rows reduced by this CTA
+    const uint32_t base = smem_u32(part);
+    for (int e = threadIdx.x; e < R * BN; e += kTcThreads) {
+      const int r = e % R, m = e / R;          // consecutive threads: consecutive rows n
+      const int nloc = rank * R + r;
+      const uint32_t off = base + static_cast<uint32_t>((nloc * BN + m) * 4);
+      int acc = 0;
+      for (int p = 0; p < ks; ++p) acc += ld_dsmem_s32(off, static_cast<uint32_t>(p));
+      if (ready) tc_epilogue1(a, n0 + nloc, m0 + m, acc);
+    }
+    cluster_sync();  // peers keep their smem until every CTA has read it
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+cudaError_t get_encode() {
+  if (g_encode) return cudaSuccess;
+  cudaDriverEntryPointQueryResult q;
+  void* fn = nullptr;
+  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+  if (e != cudaSuccess) return e;
+  if (q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return cudaSuccess;
+}
+
+template <int BN>
+size_t tc_smem(int stages) {
+  return static_cast<size_t>(stages) * (kABytes + BN * kTileK) + 1024 + 16 * (2 * stages + 2);
+}
+
+template <int BN>
+cudaError_t launch_tc_t(const TcPlan& p, const TcArgs& a, cudaStream_t s, bool pdl) {
+  const size_t smem = tc_smem<BN>(a.stages);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.N + kTileN - 1) / kTileN, (a.M + BN - 1) / BN, a.k_splits);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeClusterDimension;
+  attr[na].val.clusterDim.x = 1;
+  attr[na].val.clusterDim.y = 1;
+  attr[na].val.clusterDim.z = a.k_splits;
+  ++na;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN>, p.tm_w, p.tm_x, a);
+}
+
+template <int BN>
+cudaError_t prepare_tc_t() {
+  return cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(tc_smem<BN>(tc_max_stages(BN))));
+}
+
+}  // namespace
+
+int tc_max_stages(int bn) {
+  const int stage = kABytes + bn * kTileK;
+  return std::max(2, std::min(8, (200 * 1024) / stage));
+}
+
+int tc_pick_bn(int M) {
+  if (M <= 32) return 32;
+  if (M <= 64) return 64;
+  if (M <= 128) return 128;
+  return 256;
+}
+
+cudaError_t tc_encode_operand(CUtensorMap* tm, const int8_t* base, int rows, int K, int box_rows) {
+  cudaError_t e = get_encode();
+  if (e != cudaSuccess) return e;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) || K % 16 || rows <= 0 || box_rows > 256) return cudaErrorInvalidValue;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kTileK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+cudaError_t tc_make_plan(TcPlan* p, const int8_t* w_nk, int N, const int8_t* x, int M, int K, int num_sms) {
+  p->bn = tc_pick_bn(M);
+  cudaError_t e = tc_encode_operand(&p->tm_w, w_nk, N, K, kTileN);
+  if (e != cudaSuccess) return e;
+  e = tc_encode_operand(&p->tm_x, x, M, K, p->bn);
+  if (e != cudaSuccess) return e;
+  const int nkb = (K + kTileK - 1) / kTileK;
+  const int tiles = ((N + kTileN - 1) / kTileN) * ((M + p->bn - 1) / p->bn);
+  const int want = num_sms > 0 ? num_sms : 148;
+  int ks = 1;
+  // split K over a cluster of 2/4/8 CTAs until the grid covers the SMs;
+  // only for tiles of <= 64 tokens (the partial tile must fit the ring)
+  while (p->bn <= 64 && ks < 8 && tiles * ks < want && 2 * ks <= nkb) ks *= 2;
+  p->k_splits = ks;
+  const int per = (nkb + ks - 1) / ks;
+  p->stages = std::max(2, std::min(tc_max_stages(p->bn), per));
+  // the split-K partial tile [128][bn] int32 is staged in the ring
+  while (ks > 1 && static_cast<size_t>(p->stages) * (kABytes + p->bn * kTileK) < static_cast<size_t>(kTileN) * p->bn * 4)
+    ++p->stages;
+  p->M = M;
+  p->N = N;
+  p->K = K;
+  return cudaSuccess;
+}
+
+cudaError_t launch_gemm_tc(const TcPlan& p, const TcArgs& a0, cudaStream_t s, bool pdl) {
+  TcArgs a = a0;
+  a.M = p.M;
+  a.N = p.N;
+  a.K = p.K;
+  a.k_splits = p.k_splits;
+  a.stages = p.stages;
+  if (a.epi == EPI_SILU && (a.N % 2)) return cudaErrorInvalidValue;
+  switch (p.bn) {
+    case 32: return launch_tc_t<32>(p, a, s, pdl);
+    case 64: return launch_tc_t<64>(p, a, s, pdl);
+    case 128: return launch_tc_t<128>(p, a, s, pdl);
+    case 256: return launch_tc_t<256>(p, a, s, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t prepare_tc() {
+  cudaError_t e;
+  if ((e = prepare_tc_t<32>()) != cudaSuccess) return e;
+  if ((e = prepare_tc_t<64>()) != cudaSuccess) return e;
+  if ((e = prepare_tc_t<128>()) != cudaSuccess) return e;
+  return prepare_tc_t<256>();
+}
+
+cudaError_t tc_read_error(unsigned int* code) {
+  cudaError_t e = cudaMemcpyFromSymbol(code, g_tc_error, sizeof(unsigned int));
+  if (e != cudaSuccess) return e;
+  if (*code) {
+    unsigned int zero = 0;
+    return cudaMemcpyToSymbol(g_tc_error, &zero, sizeof(unsigned int));
+  }
+  return cudaSuccess;
+}
+
+}  // namespace tl

@@ -14,6 +14,7 @@
 //    kv_cache_manager.sv:43-47).
 //  * prefill helpers: RMSNorm rows, quantize rows, RoPE + KV calibration, KV
 //    write, causal attention.
+#include <algorithm>
 #include <cfloat>
 #include <cmath>
 #include <cstdio>
@@ -23,91 +24,63 @@
 
 namespace tl {
 
-// ============================================================== RMSNorm row
-// Leaf of NumPy's pairwise sum over squares v[i]*v[i]; called by all 32 lanes
-// of a warp together (8-lane groups, one leaf per group).
-TL_DEV float pw_leaf_sq(const float* v, int n, int j) {
-  const unsigned full_mask = 0xffffffffu;
-  const bool big = n >= 8;
-  const int full = n - (n % 8);
-  float r = 0.0f;
-  if (big) {
-    r = __fmul_rn(v[j], v[j]);
-    for (int i = 8 + j; i < full; i += 8) r = __fadd_rn(r, __fmul_rn(v[i], v[i]));
-  }
-  float r1 = __shfl_down_sync(full_mask, r, 1, 8);
-  float s01 = __fadd_rn(r, r1);
-  float s23 = __shfl_down_sync(full_mask, s01, 2, 8);
-  float s0123 = __fadd_rn(s01, s23);
-  float s4567 = __shfl_down_sync(full_mask, s0123, 4, 8);
-  float res = __fadd_rn(s0123, s4567);
-  if (j == 0) {
-    if (big) {
-      for (int i = full; i < n; ++i) res = __fadd_rn(res, __fmul_rn(v[i], v[i]));
-    } else {
-      res = 0.0f;
-      for (int i = 0; i < n; ++i) res = __fadd_rn(res, __fmul_rn(v[i], v[i]));
-    }
-  }
-  return res;
-}
-
+// ============================================================ row helpers
 struct RowScratch {
-  PwPlan plan;
-  float leaf[kPwMaxLeaves];
+  float part[1024 * 8];
+  float leaf[1024];
   float red[32];
-  double d;
 };
+// Only the used prefix of RowScratch is allocated: n_leaves*8 + n_leaves + 32
+// floats (rs_floats()).
+static inline size_t rs_floats(const NormPlan& p) { return static_cast<size_t>(p.n_leaves) * 9 + 32; }
 
-// In-place RMSNorm of buf[0..K) by the whole block (blockDim multiple of 32):
-// buf = (buf * (1/sqrt(mean(buf^2) + eps))) * gamma  (model/tinyllama.py:45-50).
-// rs.plan must hold the leaf plan for K.
-TL_DEV void block_rmsnorm(float* buf, int K, const float* gamma, float eps, RowScratch& rs) {
-  const int tid = threadIdx.x;
-  const int groups = blockDim.x / 8;
-  for (int base = 0; base < rs.plan.n_leaves; base += groups) {
-    int l = base + tid / 8;
-    bool ok = l < rs.plan.n_leaves;
-    float s = pw_leaf_sq(buf + (ok ? rs.plan.start[l] : 0), ok ? rs.plan.len[l] : 0, tid & 7);
-    if (ok && (tid & 7) == 0) rs.leaf[l] = s;
-  }
-  __syncthreads();
-  if (tid == 0) {
-    int idx = 0;
-    float tot = pw_fold_rec(rs.leaf, idx, K);
-    float mean = __fdiv_rn(tot, static_cast<float>(K));
-    float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
-    rs.red[0] = inv;
-  }
-  __syncthreads();
-  const float inv = rs.red[0];
-  for (int i = tid; i < K; i += blockDim.x) buf[i] = __fmul_rn(__fmul_rn(buf[i], inv), gamma[i]);
+struct RowScratchView {
+  float* part;
+  float* leaf;
+  float* red;
+};
+TL_DEV RowScratchView rs_view(float* base, NormPlan p) {
+  return {base, base + p.n_leaves * 8, base + p.n_leaves * 9};
+}
+
+// In-place RMSNorm of buf[0..K) by the whole block:
+// buf = (buf * (1/sqrt(mean(buf^2) + eps))) * gamma  (model/tinyllama.py:45-50),
+// mean of squares in NumPy's float32 reduction order.
+TL_DEV void block_rmsnorm(float* buf, int K, const float* gamma, float eps, NormPlan plan,
+                          RowScratchView rs) {
+  const float tot = block_sumsq_numpy(buf, plan, rs.part, rs.leaf);
+  const float mean = __fdiv_rn(tot, static_cast<float>(K));
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+  for (int i = threadIdx.x; i < K; i += blockDim.x) buf[i] = __fmul_rn(__fmul_rn(buf[i], inv), gamma[i]);
   __syncthreads();
 }
 
-TL_DEV float block_absmax(const float* buf, int K, RowScratch& rs) {
+TL_DEV float block_absmax(const float* buf, int K, float* red) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float m = 0.0f;
   for (int i = tid; i < K; i += blockDim.x) m = fmaxf(m, fabsf(buf[i]));
   m = warp_max(m);
-  if (lane == 0) rs.red[warp] = m;
+  if (lane == 0) red[warp] = m;
   __syncthreads();
-  if (warp == 0) {
-    float v = lane < (int)(blockDim.x >> 5) ? rs.red[lane] : 0.0f;
-    v = warp_max(v);
-    if (lane == 0) rs.red[0] = v;
-  }
+  float v = lane < static_cast<int>(blockDim.x >> 5) ? red[lane] : 0.0f;
+  v = warp_max(v);
   __syncthreads();
-  float r = rs.red[0];
-  __syncthreads();
-  return r;
+  return v;
 }
 
 // ================================================================ the GEMV
+// Persistent over output-row groups: each warp owns kGemvRW weight rows at a
+// time and walks (row group, K chunk) work items with the next item's 16-byte
+// weight loads in flight while the current one is reduced. The first item's
+// loads are issued before griddepcontrol.wait, so under programmatic
+// dependent launch they overlap the previous kernel's tail. The activation
+// prologue (RMSNorm, per-row INT8 quantization) runs once per CTA.
 constexpr int kGemvThreads = 256;
 constexpr int kGemvWarps = kGemvThreads / 32;
-constexpr int kGemvRW = 2;   // weight rows per warp
-constexpr int kGemvU = 4;    // 16-byte chunks per lane per row in flight
+constexpr int kGemvRW = 2;   // weight rows per warp item
+constexpr int kGemvU = 4;    // 16-byte chunks per lane per row per item
+constexpr int kGemvMaxGrid = 1024;
+static int g_num_sms[64] = {0};
 
 TL_DEV unsigned long long argmax_key(float v, int idx) {
   unsigned int b = __float_as_uint(v);
@@ -126,77 +99,86 @@ TL_DEV float silu_mul(float g, float u) {
   return __fmul_rn(__fdiv_rn(g, den), u);
 }
 
+__host__ __device__ constexpr int align16(int x) { return (x + 15) & ~15; }
+__host__ __device__ constexpr int gemv_off_sx(int MR, int K) { return MR * K; }
+__host__ __device__ constexpr int gemv_off_am(int MR, int K) { return gemv_off_sx(MR, K) + align16(8 * MR); }
+__host__ __device__ constexpr int gemv_off_f(int MR, int K) {
+  return gemv_off_am(MR, K) + align16(8 * kGemvWarps * MR);
+}
+
+template <int MR>
+struct GemvItem {
+  int4 w[kGemvU][kGemvRW];
+};
+
 template <int PRO, int EPI, int MR>
 __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int K = a.K, N = a.N, M = a.M;
-  int8_t* xs = reinterpret_cast<int8_t*>(smem);                       // [MR][K]
-  double* sx64 = reinterpret_cast<double*>(smem + MR * K);            // [MR]
-  float* fbuf = reinterpret_cast<float*>(smem + MR * K + 8 * MR);     // [K]
-  RowScratch* rs = reinterpret_cast<RowScratch*>(fbuf + K);
-  unsigned long long* am = reinterpret_cast<unsigned long long*>(rs + 1);  // [warps][MR]
+  // 16-byte aligned carve-up: xs [MR][K] | sx64 [MR] | am [warps][MR] | fbuf [K] | norm scratch
+  int8_t* xs = reinterpret_cast<int8_t*>(smem);
+  double* sx64 = reinterpret_cast<double*>(smem + gemv_off_sx(MR, K));
+  unsigned long long* am = reinterpret_cast<unsigned long long*>(smem + gemv_off_am(MR, K));
+  float* fbuf = reinterpret_cast<float*>(smem + gemv_off_f(MR, K));
+  RowScratchView rs = rs_view(fbuf + K, a.norm);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int m0 = blockIdx.y * MR;
   const int mr = min(MR, M - m0);
   const int K16 = K >> 4;
-  const int nrow0 = (blockIdx.x * kGemvWarps + warp) * kGemvRW;
+  const int nch = (K16 + 32 * kGemvU - 1) / (32 * kGemvU);
+  const int groups = (N + kGemvRW - 1) / kGemvRW;
+  const int gstride = gridDim.x * kGemvWarps;
 
-  // ---- 1. start streaming this warp's weight rows before anything else
-  const int4* wp[kGemvRW];
-  bool rv[kGemvRW];
+  auto load_item = [&](GemvItem<MR>& it, int g, int c) {
 #pragma unroll
-  for (int i = 0; i < kGemvRW; ++i) {
-    rv[i] = nrow0 + i < N;
-    wp[i] = reinterpret_cast<const int4*>(a.w + static_cast<size_t>(rv[i] ? nrow0 + i : 0) * K);
-  }
-  int4 wv[kGemvU][kGemvRW];
-  auto load_chunk = [&](int cbase) {
+    for (int i = 0; i < kGemvRW; ++i) {
+      const int n = g * kGemvRW + i;
+      const int4* wp = reinterpret_cast<const int4*>(a.w + static_cast<size_t>(n < N ? n : 0) * K);
 #pragma unroll
-    for (int u = 0; u < kGemvU; ++u) {
-      const int c = cbase + lane + 32 * u;
-#pragma unroll
-      for (int i = 0; i < kGemvRW; ++i)
-        wv[u][i] = (rv[i] && c < K16) ? ld_stream_v4(wp[i] + c) : make_int4(0, 0, 0, 0);
+      for (int u = 0; u < kGemvU; ++u) {
+        const int col = c * 32 * kGemvU + lane + 32 * u;
+        it.w[u][i] = (n < N && col < K16) ? ld_stream_v4(wp + col) : make_int4(0, 0, 0, 0);
+      }
     }
   };
-  load_chunk(0);
+
+  // ---- 1. first work item's weights in flight before anything else
+  int g = blockIdx.x * kGemvWarps + warp;
+  int c = 0;
+  GemvItem<MR> cur, nxt;
+  if (g < groups) load_item(cur, g, 0);
 
   // ---- 2. activation prologue (depends on the previous kernel)
   pdl_wait();
-  if (PRO == PRO_NORM && tid == 0) {
-    rs->plan.n_leaves = 0;
-    pw_plan_rec(rs->plan, 0, K);
-  }
   if (PRO == PRO_Q8) {
     for (int r = 0; r < MR; ++r) {
       int4* dst = reinterpret_cast<int4*>(xs + r * K);
       if (r < mr) {
         const int4* src = reinterpret_cast<const int4*>(a.x_q + static_cast<size_t>(m0 + r) * K);
-        for (int c = tid; c < K16; c += kGemvThreads) dst[c] = src[c];
+        for (int q = tid; q < K16; q += kGemvThreads) dst[q] = src[q];
       } else {
-        for (int c = tid; c < K16; c += kGemvThreads) dst[c] = make_int4(0, 0, 0, 0);
+        for (int q = tid; q < K16; q += kGemvThreads) dst[q] = make_int4(0, 0, 0, 0);
       }
       if (tid == 0)
         sx64[r] = quant_scale64((r < mr && a.in_absmax) ? a.in_absmax[(m0 + r) / a.rows_per_group] : 0.0f);
     }
   } else {
-    __syncthreads();
     for (int r = 0; r < MR; ++r) {
       if (r >= mr) {
         int4* dst = reinterpret_cast<int4*>(xs + r * K);
-        for (int c = tid; c < K16; c += kGemvThreads) dst[c] = make_int4(0, 0, 0, 0);
+        for (int q = tid; q < K16; q += kGemvThreads) dst[q] = make_int4(0, 0, 0, 0);
         if (tid == 0) sx64[r] = 1.0;
         continue;
       }
-      const float* src =
-          a.x_f32 + (static_cast<size_t>(a.x_row_offset) + static_cast<size_t>(m0 + r) * a.x_row_step) * K;
-      for (int i = tid; i < K; i += kGemvThreads) fbuf[i] = src[i];
+      const float4* src = reinterpret_cast<const float4*>(
+          a.x_f32 + (static_cast<size_t>(a.x_row_offset) + static_cast<size_t>(m0 + r) * a.x_row_step) * K);
+      for (int q = tid; q < (K >> 2); q += kGemvThreads) reinterpret_cast<float4*>(fbuf)[q] = src[q];
       __syncthreads();
-      if (PRO == PRO_NORM) block_rmsnorm(fbuf, K, a.gamma, a.eps, *rs);
+      if (PRO == PRO_NORM) block_rmsnorm(fbuf, K, a.gamma, a.eps, a.norm, rs);
       float amax;
       if (PRO == PRO_F32_GIVEN) amax = a.in_absmax[(m0 + r) / a.rows_per_group];
-      else amax = block_absmax(fbuf, K, *rs);
+      else amax = block_absmax(fbuf, K, rs.red);
       const double s64 = quant_scale64(amax);
       const float sf = static_cast<float>(s64);
       int8_t* dst = xs + r * K;
@@ -208,60 +190,130 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
   __syncthreads();
   pdl_launch_dependents();
 
-  // ---- 3. dot products
+  // ---- 3. work items: dot products + epilogue per completed row group
   int acc[kGemvRW][MR];
 #pragma unroll
   for (int i = 0; i < kGemvRW; ++i)
 #pragma unroll
     for (int m = 0; m < MR; ++m) acc[i][m] = 0;
+  unsigned long long best[MR];
+#pragma unroll
+  for (int m = 0; m < MR; ++m) best[m] = 0ull;
 
-  for (int cbase = 0; cbase < K16; cbase += 32 * kGemvU) {
-    if (cbase) load_chunk(cbase);
+  auto compute = [&](const GemvItem<MR>& it, int cc) {
 #pragma unroll
     for (int u = 0; u < kGemvU; ++u) {
-      const int c = cbase + lane + 32 * u;
-      if (c < K16) {
+      const int col = cc * 32 * kGemvU + lane + 32 * u;
+      if (col < K16) {
 #pragma unroll
         for (int m = 0; m < MR; ++m) {
-          const int4 xv = reinterpret_cast<const int4*>(xs + m * K)[c];
+          const int4 xv = reinterpret_cast<const int4*>(xs + m * K)[col];
 #pragma unroll
           for (int i = 0; i < kGemvRW; ++i) {
             int t = acc[i][m];
-            t = dp4a(wv[u][i].x, xv.x, t);
-            t = dp4a(wv[u][i].y, xv.y, t);
-            t = dp4a(wv[u][i].z, xv.z, t);
-            t = dp4a(wv[u][i].w, xv.w, t);
+            t = dp4a(it.w[u][i].x, xv.x, t);
+            t = dp4a(it.w[u][i].y, xv.y, t);
+            t = dp4a(it.w[u][i].z, xv.z, t);
+            t = dp4a(it.w[u][i].w, xv.w, t);
             acc[i][m] = t;
           }
         }
       }
     }
-  }
-#pragma unroll
-  for (int i = 0; i < kGemvRW; ++i)
-#pragma unroll
-    for (int m = 0; m < MR; ++m) acc[i][m] = warp_sum_i(acc[i][m]);
+  };
 
-  // ---- 4. epilogue
-  if (EPI == EPI_ARGMAX) {
-    unsigned long long best[MR];
+  auto epilogue = [&](int gg) {
 #pragma unroll
-    for (int m = 0; m < MR; ++m) best[m] = 0ull;
+    for (int i = 0; i < kGemvRW; ++i)
+#pragma unroll
+      for (int m = 0; m < MR; ++m) acc[i][m] = warp_sum_i(acc[i][m]);
     if (lane == 0) {
+      const int n0 = gg * kGemvRW;
+      if (EPI == EPI_ARGMAX) {
 #pragma unroll
-      for (int i = 0; i < kGemvRW; ++i) {
-        const int n = nrow0 + i;
-        if (n >= N) continue;
-        const double sw = a.w_scale[n];
+        for (int i = 0; i < kGemvRW; ++i) {
+          const int n = n0 + i;
+          if (n >= N) continue;
+          const double sw = a.w_scale[n];
 #pragma unroll
-        for (int m = 0; m < MR; ++m) {
-          if (m >= mr) continue;
-          const float y = dequant(acc[i][m], sx64[m], sw);
-          if (a.logits) a.logits[static_cast<size_t>(m0 + m) * N + n] = y;
-          const unsigned long long k = argmax_key(y, n);
-          best[m] = k > best[m] ? k : best[m];
+          for (int m = 0; m < MR; ++m) {
+            if (m >= mr) continue;
+            const float y = dequant(acc[i][m], sx64[m], sw);
+            if (a.logits) a.logits[static_cast<size_t>(m0 + m) * N + n] = y;
+            const unsigned long long k = argmax_key(y, n);
+            best[m] = k > best[m] ? k : best[m];
+          }
+        }
+      } else if (EPI == EPI_SILU) {
+        if (n0 < N) {
+          const int j = n0 >> 1, Nh = N >> 1;
+          const double sg = a.w_scale[n0], su = a.w_scale[n0 + 1];
+#pragma unroll
+          for (int m = 0; m < MR; ++m) {
+            if (m >= mr) continue;
+            const float gv = dequant(acc[0][m], sx64[m], sg);
+            const float uv = dequant(acc[1][m], sx64[m], su);
+            const float hv = silu_mul(gv, uv);
+            a.out_f32[static_cast<size_t>(m0 + m) * Nh + j] = hv;
+            if (a.out_absmax) atomic_max_nonneg(a.out_absmax + (m0 + m) / a.rows_per_group, fabsf(hv));
+          }
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < kGemvRW; ++i) {
+          const int n = n0 + i;
+          if (n >= N) continue;
+#pragma unroll
+          for (int m = 0; m < MR; ++m) {
+            if (m >= mr) continue;
+            const size_t o = static_cast<size_t>(m0 + m) * N + n;
+            if (EPI == EPI_I32) {
+              a.out_i32[o] = acc[i][m];
+            } else if (EPI == EPI_REQ) {
+              const uint32_t sc = a.req_scale[a.req_per_col ? n : 0];
+              a.out_i8[o] = static_cast<int8_t>(requant_q16(acc[i][m], sc, a.req_nonneg != 0));
+            } else {
+              const float y = dequant(acc[i][m], sx64[m], a.w_scale[n]);
+              const float v = (EPI == EPI_RESID) ? __fadd_rn(a.resid[o], y) : y;
+              a.out_f32[o] = v;
+              if (EPI == EPI_F32 && a.out_absmax)
+                atomic_max_nonneg(a.out_absmax + (m0 + m) / a.rows_per_group, fabsf(v));
+            }
+          }
         }
       }
+    }
+#pragma unroll
+    for (int i = 0; i < kGemvRW; ++i)
+#pragma unroll
+      for (int m = 0; m < MR; ++m) acc[i][m] = 0;
+  };
+
+  // ping-pong between two register buffers, prefetching one item ahead
+  while (g < groups) {
+    {
+      int gn = g, cn = c + 1;
+      if (cn == nch) { cn = 0; gn = g + gstride; }
+      if (gn < groups) load_item(nxt, gn, cn);
+      compute(cur, c);
+      if (c == nch - 1) epilogue(g);
+      g = gn;
+      c = cn;
+    }
+    if (g >= groups) break;
+    {
+      int gn = g, cn = c + 1;
+      if (cn == nch) { cn = 0; gn = g + gstride; }
+      if (gn < groups) load_item(cur, gn, cn);
+      compute(nxt, c);
+      if (c == nch - 1) epilogue(g);
+      g = gn;
+      c = cn;
+    }
+  }
+
+  if (EPI == EPI_ARGMAX) {
+    if (lane == 0) {
 #pragma unroll
       for (int m = 0; m < MR; ++m) am[warp * MR + m] = best[m];
     }
@@ -284,78 +336,53 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
       if (tid < mr) {
         unsigned long long b = 0ull;
         for (unsigned int bx = 0; bx < gridDim.x; ++bx) {
-          const unsigned long long v =
-              *reinterpret_cast<volatile unsigned long long*>(a.am_partial + static_cast<size_t>(bx) * M + m0 + tid);
+          const unsigned long long v = *reinterpret_cast<volatile unsigned long long*>(
+              a.am_partial + static_cast<size_t>(bx) * M + m0 + tid);
           b = v > b ? v : b;
         }
         a.am_token[m0 + tid] = argmax_key_index(b);
       }
       if (tid == 0) a.am_counter[blockIdx.y] = 0u;
     }
-    return;
-  }
-
-  if (lane != 0) return;
-  if (EPI == EPI_SILU) {
-    const int n = nrow0;  // even: (gate_j, up_j) rows
-    if (n >= N) return;
-    const int j = n >> 1;
-    const int Nh = N >> 1;
-    const double sg = a.w_scale[n], su = a.w_scale[n + 1];
-    float local_max = 0.0f;
-#pragma unroll
-    for (int m = 0; m < MR; ++m) {
-      if (m >= mr) continue;
-      const float g = dequant(acc[0][m], sx64[m], sg);
-      const float u = dequant(acc[1][m], sx64[m], su);
-      const float hv = silu_mul(g, u);
-      a.out_f32[static_cast<size_t>(m0 + m) * Nh + j] = hv;
-      if (a.out_absmax) atomic_max_nonneg(a.out_absmax + (m0 + m) / a.rows_per_group, fabsf(hv));
-      (void)local_max;
-    }
-    return;
-  }
-#pragma unroll
-  for (int i = 0; i < kGemvRW; ++i) {
-    const int n = nrow0 + i;
-    if (n >= N) continue;
-#pragma unroll
-    for (int m = 0; m < MR; ++m) {
-      if (m >= mr) continue;
-      const size_t o = static_cast<size_t>(m0 + m) * N + n;
-      if (EPI == EPI_I32) {
-        a.out_i32[o] = acc[i][m];
-      } else if (EPI == EPI_REQ) {
-        const uint32_t sc = a.req_scale[a.req_per_col ? n : 0];
-        a.out_i8[o] = static_cast<int8_t>(requant_q16(acc[i][m], sc, a.req_nonneg != 0));
-      } else {
-        const float y = dequant(acc[i][m], sx64[m], a.w_scale[n]);
-        const float v = (EPI == EPI_RESID) ? __fadd_rn(a.resid[o], y) : y;
-        a.out_f32[o] = v;
-        if (EPI == EPI_F32 && a.out_absmax)
-          atomic_max_nonneg(a.out_absmax + (m0 + m) / a.rows_per_group, fabsf(v));
-      }
-    }
   }
 }
 
-static size_t gemv_smem_bytes(int MR, int K) {
-  return static_cast<size_t>(MR) * K + 8 * MR + 4 * static_cast<size_t>(K) + sizeof(RowScratch) +
-         8 * kGemvWarps * MR + 64;
+static size_t gemv_smem_bytes(int MR, int K, const NormPlan& plan) {
+  return static_cast<size_t>(gemv_off_f(MR, K)) + 4 * static_cast<size_t>(K) + 4 * rs_floats(plan) + 64;
+}
+static NormPlan plan_or_min(int K) {
+  NormPlan p{8, 1};
+  if (!norm_plan(K, &p)) p = NormPlan{8, 1};
+  return p;
+}
+
+static int gemv_grid_x(int N, int MR) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int sms = (dev >= 0 && dev < 64 && g_num_sms[dev] > 0) ? g_num_sms[dev] : 148;
+  const int groups = (N + kGemvRW - 1) / kGemvRW;
+  const int need = (groups + kGemvWarps - 1) / kGemvWarps;
+  const int per_sm = MR <= 2 ? 2 : 1;  // register-limited residency (ptxas: <=104 vs >=128 regs)
+  return std::max(1, std::min(std::min(need, per_sm * sms), kGemvMaxGrid));
 }
 
 size_t gemv_argmax_partials(int M, int N) {
-  const int rows_per_cta = kGemvWarps * kGemvRW;
-  return static_cast<size_t>((N + rows_per_cta - 1) / rows_per_cta) * M;
+  (void)N;
+  return static_cast<size_t>(kGemvMaxGrid) * M;
 }
 int gemv_argmax_row_blocks(int M) { return (M + 7) / 8; }
 
 template <int PRO, int EPI, int MR>
-static cudaError_t launch_gemv_t(const GemvArgs& a, cudaStream_t s, bool pdl) {
-  const size_t smem = gemv_smem_bytes(MR, a.K);
+static cudaError_t launch_gemv_t(const GemvArgs& a0, cudaStream_t s, bool pdl) {
+  GemvArgs a = a0;
+  if (PRO == PRO_NORM) {
+    if (!norm_plan(a.K, &a.norm)) return cudaErrorInvalidValue;
+  } else {
+    a.norm = plan_or_min(a.K);
+  }
+  const size_t smem = gemv_smem_bytes(MR, a.K, a.norm);
   auto kfn = gemv_kernel<PRO, EPI, MR>;
-  const int rows_per_cta = kGemvWarps * kGemvRW;
-  dim3 grid((a.N + rows_per_cta - 1) / rows_per_cta, (a.M + MR - 1) / MR);
+  dim3 grid(gemv_grid_x(a.N, MR), (a.M + MR - 1) / MR);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kGemvThreads);
@@ -372,7 +399,7 @@ static cudaError_t launch_gemv_t(const GemvArgs& a, cudaStream_t s, bool pdl) {
 template <int PRO, int EPI, int MR>
 static cudaError_t prepare_gemv_t(int max_k) {
   return cudaFuncSetAttribute(gemv_kernel<PRO, EPI, MR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(gemv_smem_bytes(MR, max_k)));
+                              static_cast<int>(gemv_smem_bytes(MR, max_k, NormPlan{128, 64})));
 }
 
 template <int PRO, int EPI>
@@ -415,8 +442,14 @@ cudaError_t launch_gemv(int pro, int epi, const GemvArgs& a, cudaStream_t s, boo
   return cudaErrorInvalidValue;
 }
 
+int device_sm_count() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return (dev >= 0 && dev < 64 && g_num_sms[dev] > 0) ? g_num_sms[dev] : 148;
+}
+
 static size_t rmsnorm_rows_smem(int D);
-__global__ void rmsnorm_rows_kernel(const float*, const float*, float, float*, float*, int, int);
+__global__ void rmsnorm_rows_kernel(const float*, const float*, float, float*, float*, int, int, NormPlan);
 
 cudaError_t prepare_kernels(int max_k) {
   static int prepared_k[64] = {0};
@@ -425,6 +458,10 @@ cudaError_t prepare_kernels(int max_k) {
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (max_k <= prepared_k[dev]) return cudaSuccess;
+  if (g_num_sms[dev] == 0) {
+    e = cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+  }
 #define TL_GEMV_PREP(P, E) \
   if ((e = prepare_gemv_mr<P, E>(max_k)) != cudaSuccess) return e;
   TL_GEMV_VARIANTS(TL_GEMV_PREP)
@@ -432,6 +469,7 @@ cudaError_t prepare_kernels(int max_k) {
   e = cudaFuncSetAttribute(rmsnorm_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(rmsnorm_rows_smem(max_k)));
   if (e != cudaSuccess) return e;
+  if ((e = prepare_tc()) != cudaSuccess) return e;
   prepared_k[dev] = max_k;
   return cudaSuccess;
 }
@@ -595,27 +633,25 @@ cudaError_t launch_embed(const float* table, const int* ids, float* x, int rows,
   return cudaLaunchKernelEx(&cfg, embed_kernel, table, ids, x, D, vocab);
 }
 
-static size_t rmsnorm_rows_smem(int D) { return 4 * static_cast<size_t>(D) + sizeof(RowScratch) + 16; }
+static size_t rmsnorm_rows_smem(int D) {
+  return 4 * static_cast<size_t>(D) + 4 * rs_floats(NormPlan{128, 64}) + 16;
+}
 
-__global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float* x, const float* gamma,
-                                                           float eps, float* out, float* absmax,
-                                                           int D, int rows_per_group) {
+__global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float* x, const float* gamma, float eps,
+                                                           float* out, float* absmax, int D,
+                                                           int rows_per_group, NormPlan plan) {
   extern __shared__ __align__(16) unsigned char smem[];
   float* buf = reinterpret_cast<float*>(smem);
-  RowScratch* rs = reinterpret_cast<RowScratch*>(buf + D);
+  RowScratchView rs = rs_view(buf + D, plan);
   const int r = blockIdx.x;
-  if (threadIdx.x == 0) {
-    rs->plan.n_leaves = 0;
-    pw_plan_rec(rs->plan, 0, D);
-  }
-  const float* src = x + static_cast<size_t>(r) * D;
-  for (int i = threadIdx.x; i < D; i += blockDim.x) buf[i] = src[i];
+  const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(r) * D);
+  for (int i = threadIdx.x; i < D / 4; i += blockDim.x) reinterpret_cast<float4*>(buf)[i] = src[i];
   __syncthreads();
-  block_rmsnorm(buf, D, gamma, eps, *rs);
-  float* dst = out + static_cast<size_t>(r) * D;
-  for (int i = threadIdx.x; i < D; i += blockDim.x) dst[i] = buf[i];
+  block_rmsnorm(buf, D, gamma, eps, plan, rs);
+  float4* dst = reinterpret_cast<float4*>(out + static_cast<size_t>(r) * D);
+  for (int i = threadIdx.x; i < D / 4; i += blockDim.x) dst[i] = reinterpret_cast<float4*>(buf)[i];
   if (absmax) {
-    const float m = block_absmax(buf, D, *rs);
+    const float m = block_absmax(buf, D, rs.red);
     if (threadIdx.x == 0) atomic_max_nonneg(absmax + r / rows_per_group, m);
   }
 }
@@ -623,9 +659,114 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float* x, const
 cudaError_t launch_rmsnorm_rows(const float* x, const float* gamma, float eps, float* out,
                                 float* absmax_groups, int rows, int D, int rows_per_group,
                                 cudaStream_t s) {
-  const size_t smem = rmsnorm_rows_smem(D);
-  rmsnorm_rows_kernel<<<rows, 256, smem, s>>>(x, gamma, eps, out, absmax_groups, D, rows_per_group);
+  NormPlan plan;
+  if (!norm_plan(D, &plan) || D % 4) return cudaErrorInvalidValue;
+  rmsnorm_rows_kernel<<<rows, 256, rmsnorm_rows_smem(D), s>>>(x, gamma, eps, out, absmax_groups, D,
+                                                                rows_per_group, plan);
   return cudaGetLastError();
+}
+
+static cudaLaunchConfig_t row_cfg(int rows, int threads, size_t smem, cudaStream_t s, bool pdl,
+                                   cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(rows);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cfg;
+}
+
+__global__ void __launch_bounds__(256) norm_quant_rows_kernel(const float* x, const float* gamma, float eps,
+                                                              int D, NormPlan plan, int8_t* out_q,
+                                                              float* out_absmax) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* buf = reinterpret_cast<float*>(smem);
+  RowScratchView rs = rs_view(buf + D, plan);
+  const int r = blockIdx.x;
+  pdl_wait();
+  const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(r) * D);
+  for (int i = threadIdx.x; i < D / 4; i += blockDim.x) reinterpret_cast<float4*>(buf)[i] = src[i];
+  __syncthreads();
+  block_rmsnorm(buf, D, gamma, eps, plan, rs);
+  const float amax = block_absmax(buf, D, rs.red);
+  pdl_launch_dependents();
+  const float sf = static_cast<float>(quant_scale64(amax));
+  int8_t* dst = out_q + static_cast<size_t>(r) * D;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) dst[i] = static_cast<int8_t>(quantize_one(buf[i], sf));
+  if (threadIdx.x == 0) out_absmax[r] = amax;
+}
+
+cudaError_t launch_norm_quant_rows(const float* x, const float* gamma, float eps, int rows, int D,
+                                   int8_t* out_q, float* out_absmax, cudaStream_t s, bool pdl) {
+  NormPlan plan;
+  if (!norm_plan(D, &plan) || D % 4) return cudaErrorInvalidValue;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = row_cfg(rows, 256, rmsnorm_rows_smem(D), s, pdl, attr);
+  return cudaLaunchKernelEx(&cfg, norm_quant_rows_kernel, x, gamma, eps, D, plan, out_q, out_absmax);
+}
+
+__global__ void __launch_bounds__(256) quant_rows_kernel(const float* x, int K, int8_t* out_q, float* out_absmax) {
+  __shared__ float red[32];
+  const int r = blockIdx.x;
+  pdl_wait();
+  const float* src = x + static_cast<size_t>(r) * K;
+  float m = 0.0f;
+  for (int i = threadIdx.x; i < K; i += blockDim.x) m = fmaxf(m, fabsf(src[i]));
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  float v = (threadIdx.x & 31) < static_cast<int>(blockDim.x >> 5) ? red[threadIdx.x & 31] : 0.0f;
+  v = warp_max(v);
+  pdl_launch_dependents();
+  const float sf = static_cast<float>(quant_scale64(v));
+  int8_t* dst = out_q + static_cast<size_t>(r) * K;
+  for (int i = threadIdx.x; i < K; i += blockDim.x) dst[i] = static_cast<int8_t>(quantize_one(src[i], sf));
+  if (threadIdx.x == 0) out_absmax[r] = v;
+}
+
+cudaError_t launch_quant_rows(const float* x, int rows, int K, int8_t* out_q, float* out_absmax,
+                              cudaStream_t s, bool pdl) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = row_cfg(rows, 256, 0, s, pdl, attr);
+  return cudaLaunchKernelEx(&cfg, quant_rows_kernel, x, K, out_q, out_absmax);
+}
+
+__global__ void __launch_bounds__(512) row_argmax_kernel(const float* logits, int V, int32_t* out) {
+  __shared__ unsigned long long red[32];
+  const int r = blockIdx.x;
+  pdl_wait();
+  const float* src = logits + static_cast<size_t>(r) * V;
+  unsigned long long best = 0ull;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const unsigned long long k = argmax_key(src[i], i);
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    unsigned long long b = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0ull;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, b, o);
+      b = other > b ? other : b;
+    }
+    if (threadIdx.x == 0) out[r] = argmax_key_index(b);
+  }
+}
+
+cudaError_t launch_row_argmax(const float* logits, int rows, int V, int32_t* out, cudaStream_t s, bool pdl) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = row_cfg(rows, 512, 0, s, pdl, attr);
+  return cudaLaunchKernelEx(&cfg, row_argmax_kernel, logits, V, out);
 }
 
 __global__ void absmax_rows_kernel(const float* x, int K, int rows_per_group, float* absmax) {

@@ -3,7 +3,10 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
+
+#include "common.cuh"
 
 namespace tl {
 
@@ -48,6 +51,7 @@ struct GemvArgs {
   int32_t* am_token = nullptr;               // [M]
   int x_row_offset = 0;              // float rows: source row of m is offset + m * step
   int x_row_step = 1;                // (prefill LM head: last row of each sequence)
+  NormPlan norm{8, 1};               // filled by launch_gemv from K
 };
 
 // Raises the dynamic shared-memory limit of every kernel variant for rows of
@@ -61,6 +65,38 @@ cudaError_t launch_gemv(int pro, int epi, const GemvArgs& a, cudaStream_t s, boo
 // Scratch the argmax epilogue needs for a given shape.
 size_t gemv_argmax_partials(int M, int N);
 int gemv_argmax_row_blocks(int M);
+
+// ---- tcgen05 INT8 GEMM (gemm_tcgen05.cu): out[m][n] = epi(sum_k X[m][k] W[n][k])
+struct TcArgs {
+  int M = 0, N = 0, K = 0;             // filled from the plan
+  int k_splits = 1, stages = 2;        // filled from the plan
+  int epi = EPI_F32;
+  const double* w_scale = nullptr;     // [N]
+  const float* in_absmax = nullptr;    // [groups]: scale of X row m is absmax[m / rows_per_group]/127
+  int rows_per_group = 1;
+  float* out_f32 = nullptr;
+  const float* resid = nullptr;
+  int32_t* out_i32 = nullptr;
+  int8_t* out_i8 = nullptr;
+  const uint32_t* req_scale = nullptr;
+  int req_per_col = 0, req_nonneg = 0;
+  float* out_absmax = nullptr;         // only without split-K
+};
+struct TcPlan {
+  CUtensorMap tm_w;                    // W^T [N][K], 128-row boxes
+  CUtensorMap tm_x;                    // X [M][K], bn-row boxes
+  int bn = 64, k_splits = 1, stages = 2, M = 0, N = 0, K = 0;
+};
+// Encodes the two operand tensor maps and picks tile/split/stage counts.
+cudaError_t tc_make_plan(TcPlan* p, const int8_t* w_nk, int N, const int8_t* x, int M, int K, int num_sms);
+cudaError_t launch_gemm_tc(const TcPlan& p, const TcArgs& a, cudaStream_t s, bool pdl);
+cudaError_t prepare_tc();
+int tc_max_stages(int bn);
+int tc_pick_bn(int M);
+// Reads (and clears) the device error word of the tensor-core kernels: 0 ok,
+// else the code of the bounded wait that expired.
+cudaError_t tc_read_error(unsigned int* code);
+int device_sm_count();
 
 struct AttnDecodeArgs {
   const float* qkv = nullptr;   // [M][ld]; q at 0, k at H*64, v at H*64 + Hkv*64
@@ -105,6 +141,16 @@ cudaError_t launch_attn_prefill(const float* qkv, int ld, int rows, int seq_len,
                                 const int8_t* kc, const int8_t* vc, const float* ks,
                                 const float* vs, int slot_base, int layer, int L, int P,
                                 float* out, float* out_absmax, cudaStream_t s);
+
+// ---- per-row (one sequence per row) activation prep for the batched path
+// out_q[r] = quantize(rmsnorm(x[r]) ), out_absmax[r] = max|rmsnorm(x[r])|
+cudaError_t launch_norm_quant_rows(const float* x, const float* gamma, float eps, int rows, int D,
+                                   int8_t* out_q, float* out_absmax, cudaStream_t s, bool pdl);
+// out_q[r] = quantize(x[r]) with the row's own absmax
+cudaError_t launch_quant_rows(const float* x, int rows, int K, int8_t* out_q, float* out_absmax,
+                              cudaStream_t s, bool pdl);
+// out[r] = argmax over logits[r][0..V) (lowest index on ties)
+cudaError_t launch_row_argmax(const float* logits, int rows, int V, int32_t* out, cudaStream_t s, bool pdl);
 
 // ---- misc
 cudaError_t launch_transpose_i8(const int8_t* src_kn, int8_t* dst_nk, int K, int N,

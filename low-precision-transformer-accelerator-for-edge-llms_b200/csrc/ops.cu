@@ -34,6 +34,13 @@ tl_status check_gemm(const void* a, const void* w, int M, int N, int K) {
 
 extern "C" {
 
+tl_status tl_device_error(void) {
+  unsigned int code = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess) return TL_ERR_CUDA;
+  if (tc_read_error(&code) != cudaSuccess) return TL_ERR_CUDA;
+  return code ? TL_ERR_TIMEOUT : TL_OK;
+}
+
 tl_status tl_transpose_i8(const int8_t* w_kn, int8_t* w_nk, int32_t K, int32_t N, void* stream) {
   if (!w_kn || !w_nk || K <= 0 || N <= 0) return TL_ERR_INVALID_ARGUMENT;
   return cu(launch_transpose_i8(w_kn, w_nk, K, N, static_cast<cudaStream_t>(stream)));
@@ -50,10 +57,25 @@ tl_status tl_quantize_int8(const float* x, int32_t rows, int32_t cols, int32_t r
   return cu(launch_quantize_rows(x, out_absmax, rows, cols, rows_per_group, out_q, s));
 }
 
+// Batches of >= 16 rows go to the tcgen05 GEMM, smaller ones to the GEMV.
+static constexpr int kOpsTcMinRows = 16;
+
+static tl_status tc_op(const int8_t* a, const int8_t* w_nk, int M, int N, int K, const TcArgs& args, cudaStream_t s) {
+  TcPlan p;
+  TL_OPS_TRY(cu(tc_make_plan(&p, w_nk, N, a, M, K, device_sm_count())));
+  return cu(launch_gemm_tc(p, args, s, false));
+}
+
 tl_status tl_gemm_i8(const int8_t* a, const int8_t* w_nk, int32_t* c, int32_t M, int32_t N, int32_t K,
                      void* stream) {
   if (!c) return TL_ERR_INVALID_ARGUMENT;
   TL_OPS_TRY(check_gemm(a, w_nk, M, N, K));
+  if (M >= kOpsTcMinRows) {
+    TcArgs t;
+    t.epi = EPI_I32;
+    t.out_i32 = c;
+    return tc_op(a, w_nk, M, N, K, t, static_cast<cudaStream_t>(stream));
+  }
   GemvArgs g;
   g.x_q = a; g.w = w_nk; g.M = M; g.N = N; g.K = K; g.out_i32 = c;
   return cu(launch_gemv(PRO_Q8, EPI_I32, g, static_cast<cudaStream_t>(stream), false));
@@ -64,6 +86,15 @@ tl_status tl_gemm_i8_requant(const int8_t* a, const int8_t* w_nk, const uint32_t
                              int32_t N, int32_t K, void* stream) {
   if (!out || !scale_q16) return TL_ERR_INVALID_ARGUMENT;
   TL_OPS_TRY(check_gemm(a, w_nk, M, N, K));
+  if (M >= kOpsTcMinRows) {
+    TcArgs t;
+    t.epi = EPI_REQ;
+    t.out_i8 = out;
+    t.req_scale = scale_q16;
+    t.req_per_col = per_column ? 1 : 0;
+    t.req_nonneg = nonnegative_only ? 1 : 0;
+    return tc_op(a, w_nk, M, N, K, t, static_cast<cudaStream_t>(stream));
+  }
   GemvArgs g;
   g.x_q = a; g.w = w_nk; g.M = M; g.N = N; g.K = K; g.out_i8 = out;
   g.req_scale = scale_q16; g.req_per_col = per_column ? 1 : 0; g.req_nonneg = nonnegative_only ? 1 : 0;
@@ -80,6 +111,20 @@ tl_status tl_quantized_linear(const float* x, const int8_t* w_nk, const double* 
   TL_OPS_TRY(cu(cudaMallocAsync(reinterpret_cast<void**>(&xq), static_cast<size_t>(M) * K, s)));
   tl_status st = cu(cudaMallocAsync(reinterpret_cast<void**>(&amax), sizeof(float), s));
   if (st == TL_OK) st = tl_quantize_int8(x, M, K, M, xq, amax, stream);
+  if (st == TL_OK && M >= kOpsTcMinRows) {
+    TcArgs t;
+    t.epi = EPI_F32; t.w_scale = w_scale; t.in_absmax = amax; t.rows_per_group = M; t.out_f32 = out;
+    st = tc_op(xq, w_nk, M, N, K, t, s);
+    if (st == TL_OK && acc_out) {
+      TcArgs t2;
+      t2.epi = EPI_I32;
+      t2.out_i32 = acc_out;
+      st = tc_op(xq, w_nk, M, N, K, t2, s);
+    }
+    cudaFreeAsync(xq, s);
+    cudaFreeAsync(amax, s);
+    return st;
+  }
   if (st == TL_OK) {
     GemvArgs g;
     g.x_q = xq; g.in_absmax = amax; g.rows_per_group = M;
@@ -98,7 +143,9 @@ tl_status tl_quantized_linear(const float* x, const int8_t* w_nk, const double* 
 
 tl_status tl_rmsnorm(const float* x, const float* gamma, float eps, float* out, int32_t rows, int32_t cols,
                      void* stream) {
-  if (!x || !gamma || !out || rows <= 0 || cols <= 0) return TL_ERR_INVALID_ARGUMENT;
+  if (!x || !gamma || !out || rows <= 0 || cols <= 0 || cols % 4) return TL_ERR_INVALID_ARGUMENT;
+  NormPlan plan;
+  if (!norm_plan(cols, &plan)) return TL_ERR_INVALID_ARGUMENT;
   TL_OPS_TRY(cu(prepare_kernels(cols)));
   return cu(launch_rmsnorm_rows(x, gamma, eps, out, nullptr, rows, cols, 1, static_cast<cudaStream_t>(stream)));
 }
@@ -107,6 +154,8 @@ tl_status tl_lmhead_argmax(const float* x, const float* gamma, float eps, const 
                            const double* w_scale, int32_t rows, int32_t vocab, int32_t hidden,
                            int32_t* token_out, float* logits_out, void* stream) {
   if (!gamma || !w_scale || !token_out) return TL_ERR_INVALID_ARGUMENT;
+  NormPlan plan;
+  if (!norm_plan(hidden, &plan)) return TL_ERR_INVALID_ARGUMENT;
   TL_OPS_TRY(check_gemm(x, w_nk, rows, vocab, hidden));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   unsigned long long* partial = nullptr;

@@ -47,7 +47,8 @@ EXPORTS = (
     "tl_init_random_weights", "tl_generate", "tl_generate_batch", "tl_abort",
     "tl_prefill_logits", "tl_decode_logits", "tl_read_kv", "tl_get_position",
     "tl_decode_steps_device", "tl_prefill_batch_device", "tl_decode_rewind", "tl_synchronize",
-    "tl_decode_step_kernel_count", "tl_engine_stream", "tl_profile_decode_kernels", "tl_transpose_i8", "tl_quantize_int8",
+    "tl_decode_step_kernel_count", "tl_decode_step_kernel_count_rows", "tl_engine_stream", "tl_profile_decode_kernels", "tl_device_error",
+    "tl_transpose_i8", "tl_quantize_int8",
     "tl_gemm_i8", "tl_gemm_i8_requant", "tl_quantized_linear", "tl_rmsnorm", "tl_lmhead_argmax",
 )
 
@@ -124,8 +125,10 @@ def load_library(path: Path | str | None = None):
         "tl_decode_rewind": (i32, [vp, u32, u32]),
         "tl_synchronize": (i32, [vp]),
         "tl_decode_step_kernel_count": (i32, [vp]),
+        "tl_decode_step_kernel_count_rows": (i32, [vp, u32]),
         "tl_engine_stream": (vp, [vp]),
         "tl_profile_decode_kernels": (i32, [vp, u32, u32, vp]),
+        "tl_device_error": (i32, []),
         "tl_transpose_i8": (i32, [vp, vp, i32, i32, vp]),
         "tl_quantize_int8": (i32, [vp, i32, i32, i32, vp, vp, vp]),
         "tl_gemm_i8": (i32, [vp, vp, vp, i32, i32, i32, vp]),
@@ -371,14 +374,15 @@ class Engine:
 
     def profile_decode_kernels(self, n_seqs: int, iters: int = 44) -> np.ndarray:
         """Average device time (ms) of each decode kernel kind, see
-        tl_profile_decode_kernels: [qkv, attn, o, gate_up, down, lm_head]."""
-        out = np.zeros(6, dtype=np.float32)
+        tl_profile_decode_kernels: [qkv, attn, o, gate_up, down, lm_head,
+        norm_quant_rows, quant_rows]."""
+        out = np.zeros(8, dtype=np.float32)
         check(self.lib.tl_profile_decode_kernels(self.h, n_seqs, iters, _ptr(out)),
               "tl_profile_decode_kernels")
         return out
 
-    def decode_step_kernel_count(self) -> int:
-        return int(self.lib.tl_decode_step_kernel_count(self.h))
+    def decode_step_kernel_count(self, n_seqs: int = 1) -> int:
+        return int(self.lib.tl_decode_step_kernel_count_rows(self.h, n_seqs))
 
 
 # --------------------------------------------------------------------------

@@ -103,6 +103,30 @@ def test_generate_batch_matches_single(small):
         assert sts[i]["stop_reason"] == 2
 
 
+def test_batched_tensor_core_path(pkg, gpu):
+    """20 sequences: prefill (140 rows) and every decode step run on the
+    tcgen05 GEMMs with split-K cluster reductions; each sequence must follow
+    its own oracle."""
+    qm = small_model(11, 2)
+    eng = pkg.Engine(qm.cfg, max_batch=20, max_prefill_tokens=20 * 7)
+    eng.load(to_engine_model(pkg, qm))
+    rng = np.random.default_rng(12)
+    prompts = rng.integers(0, qm.cfg["vocab_size"], (20, 7)).astype(np.uint32)
+    outs, sts = eng.generate_batch(prompts, 6)
+    assert pkg.shim.load_library().tl_device_error() == 0
+    mism = 0
+    for i in range(20):
+        ref, ref_logits, _ = oracle_generate(qm, list(prompts[i]), 6)
+        assert sts[i]["stop_reason"] == 2 and sts[i]["generated_count"] == 6
+        assert tokens_match_modulo_ties(outs[i], ref, ref_logits), (i, outs[i], ref)
+        mism += outs[i] != ref
+    k, _, _, _ = eng.read_kv(0, 7, slot=5)
+    ora = KVGolden(qm, kv="int8")
+    ora.prefill(list(prompts[5]))
+    np.testing.assert_array_equal(k, ora.k_cache[0, :, :7])
+    eng.close()
+
+
 def test_stop_contract(small):
     qm, eng = small
     prompt = list(np.random.default_rng(6).integers(0, qm.cfg["vocab_size"], 5))
@@ -197,8 +221,9 @@ def test_config0_full_size(pkg, gpu, golden):
 
 def test_reference_golden_first_token(pkg, gpu, golden):
     """Against the reference's own forward_mixed output (per-tensor weights,
-    fixture made by the reference): same first token, logits within the
-    INT8-KV quantization difference."""
+    fixture made by the reference): the engine equals the INT8-KV oracle to
+    1e-3, so its whole distance to the reference is the INT8 KV cache (which
+    the reference does not have); the greedy token is the reference's."""
     if "config0" not in golden:
         pytest.skip("config0 fixture missing")
     d = golden["config0"]
@@ -207,8 +232,10 @@ def test_reference_golden_first_token(pkg, gpu, golden):
     eng.load(to_engine_model(pkg, qm))
     prompt = [int(t) for t in d["prompt"]]
     lg = eng.prefill_logits(prompt)
+    ora = KVGolden(qm, kv="int8").prefill(prompt)
+    assert rel_err(lg, ora) <= FP_RTOL
     ref = d["first_logits"]
-    assert rel_err(lg, ref) < 0.05
+    assert abs(rel_err(lg, ref) - rel_err(ora, ref)) <= FP_RTOL
     top2 = np.sort(ref)[-2:]
     if top2[1] - top2[0] > FP_RTOL * abs(top2[1]):
         assert int(np.argmax(lg)) == int(d["recompute_tokens"][0])

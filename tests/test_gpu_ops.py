@@ -27,8 +27,23 @@ def stream():
     return torch.cuda.current_stream().cuda_stream
 
 
+_KEEP = []
+
+
 def dev(a):
-    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    """Device copy kept alive until the next test: passing a temporary's
+    data_ptr() would let the caching allocator hand its block to the next
+    argument before the kernel runs."""
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    _KEEP.append(t)
+    return t
+
+
+@pytest.fixture(autouse=True)
+def _release():
+    yield
+    torch.cuda.synchronize()
+    _KEEP.clear()
 
 
 def gemm_gpu(lib, pkg, a, w_kn):
@@ -41,7 +56,10 @@ def gemm_gpu(lib, pkg, a, w_kn):
 
 
 @pytest.mark.parametrize("m,k,n", [(1, 64, 64), (1, 2048, 256), (3, 2048, 2048), (8, 5632, 2048),
-                                   (17, 2048, 320), (32, 5632, 256), (1, 2048, 32000), (5, 704, 96)])
+                                   (17, 2048, 320), (32, 5632, 256), (1, 2048, 32000), (5, 704, 96),
+                                   # tcgen05 path (m >= 16): tails in m, n and k, split-K clusters
+                                   (16, 2048, 256), (64, 2048, 2560), (100, 704, 96), (300, 2048, 2048),
+                                   (64, 5632, 2048), (48, 2048, 11264), (257, 256, 130), (64, 256, 512)])
 def test_gemm_i8_bit_exact(lib, pkg, m, k, n):
     rng = np.random.default_rng(m * 131 + k + n)
     a = rng.integers(-127, 128, (m, k)).astype(np.int8)
@@ -159,3 +177,41 @@ def test_invalid_shapes_rejected(pkg, lib):
     c = torch.zeros((1, 8), dtype=torch.int32, device="cuda")
     assert lib.tl_gemm_i8(a.data_ptr(), a.data_ptr(), c.data_ptr(), 1, 8, 24, stream()) == 16
     assert lib.tl_gemm_i8(None, a.data_ptr(), c.data_ptr(), 1, 8, 16, stream()) == 16
+
+
+CONFIG1 = [(m, k, n) for m in (1, 32, 512, 4096) for k in (2048, 5632) for n in (256, 2048, 5632, 32000)]
+
+
+@pytest.mark.parametrize("m,k,n", CONFIG1)
+def test_config1_gemm_sweep_requant(lib, pkg, m, k, n):
+    """Benchmark config 1: INT8 x INT8 -> INT32 with per-tensor Q16.16
+    requantize to INT8, operands uniform in [-127,127], scale uniform in
+    [1e-4, 1e-2]. Bit-exact on 8 sampled rows (all rows for m <= 32)."""
+    rng = np.random.default_rng(m * 7 + k * 3 + n)
+    a = rng.integers(-127, 128, (m, k), dtype=np.int8)
+    w_nk = rng.integers(-127, 128, (n, k), dtype=np.int8)
+    scale = rng.uniform(1e-4, 1e-2)
+    sq = np.array([C.q16_16_from_float(scale)], dtype=np.uint32)
+    out = torch.empty((m, n), dtype=torch.int8, device="cuda")
+    acc = torch.empty((m, n), dtype=torch.int32, device="cuda")
+    da, dw = dev(a), dev(w_nk)
+    pkg.shim.check(lib.tl_gemm_i8_requant(da.data_ptr(), dw.data_ptr(), dev(sq).data_ptr(), 0, 0, out.data_ptr(),
+                                          m, n, k, stream()), "requant")
+    pkg.shim.check(lib.tl_gemm_i8(da.data_ptr(), dw.data_ptr(), acc.data_ptr(), m, n, k, stream()), "gemm")
+    rows = np.arange(m) if m <= 32 else np.sort(rng.choice(m, 8, replace=False))
+    ref_acc = G.int8_matmul(a[rows], np.ascontiguousarray(w_nk.T))
+    got_acc = acc.cpu().numpy()[rows]
+    np.testing.assert_array_equal(got_acc, ref_acc)
+    np.testing.assert_array_equal(out.cpu().numpy()[rows], C.requantize_q16(ref_acc, sq[0]))
+    assert pkg.shim.load_library().tl_device_error() == 0
+
+
+@pytest.mark.parametrize("m", [16, 40, 130])
+def test_quantized_linear_tc(pkg, lib, m):
+    rng = np.random.default_rng(m)
+    x = rng.standard_normal((m, 2048), dtype=np.float32)
+    w = (rng.standard_normal((2048, 384), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    out, dbg = pkg.quantized_linear(x, w, capture_arrays=True)
+    ref, rdbg = G.quantized_linear(x, w)
+    np.testing.assert_array_equal(dbg["accum_int32"], rdbg["accum_int32"])
+    np.testing.assert_array_equal(out, ref)
