@@ -261,6 +261,20 @@ TL_API tl_status tl_lmhead_argmax(const float* x, const float* gamma, float eps,
                            const double* w_scale, int32_t rows, int32_t vocab, int32_t hidden,
                            int32_t* token_out, float* logits_out, void* stream);
 
+/* Decode attention for `rows` sequences at one layer over the INT8 KV cache
+ * (device buffers): qkv [rows][(H + 2*Hkv)*64] float32 pre-RoPE q|k|v of the
+ * new token, pos[rows] its position, slot[rows] its KV slot; kc/vc int8
+ * [slots][L][Hkv][P][64], ks/vs float [slots][L][Hkv]; cos/sin [P][64].
+ * Appends the new K (after RoPE) and V rows (quantized with the cached
+ * scales) and writes out [rows][H*64]. Allocates its split scratch per call.
+ * Follows model/tinyllama_gemm_int8.py:154-163 with the cache layout of
+ * rtl/memory/kv_cache_manager.sv:43-47 and rtl/compute/gqa_router.sv:25-31. */
+TL_API tl_status tl_attn_decode(const float* qkv, const int32_t* pos, const int32_t* slot, int8_t* kc,
+                                int8_t* vc, const float* ks, const float* vs, const float* rope_cos,
+                                const float* rope_sin, int32_t layer, int32_t num_layers, int32_t heads,
+                                int32_t kv_heads, int32_t max_positions, int32_t rows, float* out,
+                                void* stream);
+
 #ifdef __cplusplus
 }
 #endif

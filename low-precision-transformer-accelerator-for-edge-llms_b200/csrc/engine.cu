@@ -23,6 +23,7 @@
 #include <atomic>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -85,6 +86,8 @@ struct DecodeBufs {
   float* logits = nullptr;  // [rows][V]
   int8_t* xq = nullptr;     // [rows][max(D, F)] int8 activations (tensor-core path)
   float* amax = nullptr;    // [rows] per-row absmax of the activation in xq
+  float* attn_part = nullptr;         // decode attention split partials
+  unsigned int* attn_cnt = nullptr;   // [rows][Hkv] merge tickets
 };
 
 // Batches of at least this many rows use the tcgen05 GEMM; smaller ones the
@@ -178,6 +181,11 @@ tl_status alloc_decode(tl_engine* e) {
   TL_TRY(dmalloc(&d.logits, static_cast<size_t>(B) * e->V));
   TL_TRY(dmalloc(&d.xq, static_cast<size_t>(B) * std::max(e->D, e->F)));
   TL_TRY(dmalloc(&d.amax, B));
+  // upper bound over both split lengths (64 positions below 16 rows, 128 above)
+  TL_TRY(dmalloc(&d.attn_part, std::max(attn_part_floats(B, e->Hkv, e->P),
+                                        attn_part_floats(std::min(B, 15), e->Hkv, e->P))));
+  TL_TRY(dmalloc(&d.attn_cnt, static_cast<size_t>(B) * e->Hkv));
+  TL_CU(cudaMemset(d.attn_cnt, 0, static_cast<size_t>(B) * e->Hkv * sizeof(unsigned int)));
   TL_CU(cudaMemset(d.am_counter, 0, (gemv_argmax_row_blocks(B) + 1) * sizeof(unsigned int)));
   TL_CU(cudaMemset(d.active, 0, B * sizeof(int)));
   TL_CU(cudaMemset(d.stop, 0, B * sizeof(int)));
@@ -245,6 +253,7 @@ tl_status enqueue_decode_step_tc(tl_engine* e, int M, bool finalize) {
     at.kc = e->kc; at.vc = e->vc; at.ks = e->ks; at.vs = e->vs;
     at.layer = l; at.L = e->L; at.H = e->H; at.Hkv = e->Hkv; at.P = e->P; at.M = M;
     at.cos = e->cosT; at.sin = e->sinT; at.out = d.att;
+    at.part = d.attn_part; at.counters = d.attn_cnt;
     TL_CU(launch_attn_decode(at, s, pdl));
     TL_CU(launch_quant_rows(d.att, M, e->Dq, d.xq, d.amax, s, pdl));
     TcArgs o;
@@ -298,6 +307,7 @@ tl_status enqueue_decode_step(tl_engine* e, int M, float* logits, bool finalize)
     at.kc = e->kc; at.vc = e->vc; at.ks = e->ks; at.vs = e->vs;
     at.layer = l; at.L = e->L; at.H = e->H; at.Hkv = e->Hkv; at.P = e->P; at.M = M;
     at.cos = e->cosT; at.sin = e->sinT; at.out = d.att;
+    at.part = d.attn_part; at.counters = d.attn_cnt;
     TL_CU(launch_attn_decode(at, s, pdl));
 
     GemvArgs o;
@@ -592,6 +602,9 @@ tl_status tl_create(const tl_config* cfg, int32_t device, tl_engine** out) {
   if ((s = ensure_prefill(e, pf_rows, e->B)) != TL_OK) return fail(s);
   e->slot_pos.assign(e->B, 0);
   e->slot_pending.assign(e->B, -1);
+  // TL_DISABLE_PDL=1 launches every kernel without programmatic dependent
+  // launch (plain stream order); a debugging aid, off by default.
+  if (const char* v = std::getenv("TL_DISABLE_PDL")) e->use_pdl = !(v[0] == '1');
   *out = e;
   return TL_OK;
 }
@@ -611,7 +624,7 @@ tl_status tl_destroy(tl_engine* e) {
   cudaFree(d.x); cudaFree(d.qkv); cudaFree(d.att); cudaFree(d.hid); cudaFree(d.tokens); cudaFree(d.pos);
   cudaFree(d.slots); cudaFree(d.active); cudaFree(d.count); cudaFree(d.stop); cudaFree(d.out_ids);
   cudaFree(d.run); cudaFree(d.argmax); cudaFree(d.am_partial); cudaFree(d.am_counter); cudaFree(d.logits);
-  cudaFree(d.xq); cudaFree(d.amax);
+  cudaFree(d.xq); cudaFree(d.amax); cudaFree(d.attn_part); cudaFree(d.attn_cnt);
   PrefillBufs& p = e->pf;
   cudaFree(p.ids); cudaFree(p.x); cudaFree(p.h); cudaFree(p.qkv); cudaFree(p.att); cudaFree(p.hid);
   cudaFree(p.xq); cudaFree(p.amax); cudaFree(p.kvamax);
@@ -1019,6 +1032,7 @@ tl_status tl_profile_decode_kernels(tl_engine* e, uint32_t n_seqs, uint32_t iter
           at.kc = e->kc; at.vc = e->vc; at.ks = e->ks; at.vs = e->vs; at.layer = l; at.L = e->L;
           at.H = e->H; at.Hkv = e->Hkv; at.P = e->P; at.M = M; at.cos = e->cosT; at.sin = e->sinT;
           at.out = d.att;
+          at.part = d.attn_part; at.counters = d.attn_cnt;
           at.active = d.stop;  // stop[] is 0 for running rows: read side only, no KV append
           ce = launch_attn_decode(at, s, false);
           break;

@@ -133,11 +133,13 @@ TL_DEV uint32_t cluster_rank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
-TL_DEV int ld_dsmem_s32(uint32_t local_addr, uint32_t peer) {
+TL_DEV int4 ld_dsmem_v4(uint32_t local_addr, uint32_t peer) {
   uint32_t remote;
-  int v;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(peer));
-  asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(remote) : "memory");
+  int4 v;
+  asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(peer));
+  asm volatile("ld.shared::cluster.v4.s32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(remote));
   return v;
 }
 
@@ -331,13 +333,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int rank = static_cast<int>(cluster_rank());
     const int R = kTileN / ks;                 // rows reduced by this CTA
     const uint32_t base = smem_u32(part);
-    for (int e = threadIdx.x; e < R * BN; e += kTcThreads) {
-      const int r = e % R, m = e / R;          // consecutive threads: consecutive rows n
+    // Work item = (row r, 4 consecutive tokens): one 16-byte DSMEM load per
+    // peer, all peers' loads issued before any add. Consecutive threads take
+    // consecutive rows n, so each output row m is written as a contiguous run.
+    const int quads = BN / 4;
+    for (int e = threadIdx.x; e < R * quads; e += kTcThreads) {
+      const int r = e % R, q = e / R;
       const int nloc = rank * R + r;
-      const uint32_t off = base + static_cast<uint32_t>((nloc * BN + m) * 4);
-      int acc = 0;
-      for (int p = 0; p < ks; ++p) acc += ld_dsmem_s32(off, static_cast<uint32_t>(p));
-      if (ready) tc_epilogue1(a, n0 + nloc, m0 + m, acc);
+      const uint32_t off = base + static_cast<uint32_t>((nloc * BN + q * 4) * 4);
+      int4 v[8];
+#pragma unroll
+      for (int p = 0; p < 8; ++p)
+        if (p < ks) v[p] = ld_dsmem_v4(off, static_cast<uint32_t>(p));
+      int4 acc = v[0];
+#pragma unroll
+      for (int p = 1; p < 8; ++p)
+        if (p < ks) {
+          acc.x += v[p].x;
+          acc.y += v[p].y;
+          acc.z += v[p].z;
+          acc.w += v[p].w;
+        }
+      if (ready) {
+        tc_epilogue1(a, n0 + nloc, m0 + q * 4 + 0, acc.x);
+        tc_epilogue1(a, n0 + nloc, m0 + q * 4 + 1, acc.y);
+        tc_epilogue1(a, n0 + nloc, m0 + q * 4 + 2, acc.z);
+        tc_epilogue1(a, n0 + nloc, m0 + q * 4 + 3, acc.w);
+      }
     }
     cluster_sync();  // peers keep their smem until every CTA has read it
   }

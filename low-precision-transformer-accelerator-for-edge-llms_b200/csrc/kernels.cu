@@ -8,10 +8,7 @@
 //    requantize_unit.sv:39-93, residual_add.sv:92-96, elementwise_mul.sv:112-119,
 //    argmax_reduction.sv:47-131; numerics of quantized_linear
 //    (model/tinyllama_gemm_int8.py:59-88).
-//  * attn_decode_kernel: GQA decode attention over the INT8 KV cache with the
-//    new row's RoPE, quantization and in-place append fused in
-//    (rope_unit.sv, causal_mask_unit.sv:49-54, gqa_router.sv:25-31,
-//    kv_cache_manager.sv:43-47).
+//  (decode attention on tensor cores lives in attention.cu)
 //  * prefill helpers: RMSNorm rows, quantize rows, RoPE + KV calibration, KV
 //    write, causal attention.
 #include <algorithm>
@@ -472,139 +469,6 @@ cudaError_t prepare_kernels(int max_k) {
   if ((e = prepare_tc()) != cudaSuccess) return e;
   prepared_k[dev] = max_k;
   return cudaSuccess;
-}
-
-// ====================================================== decode attention
-// One CTA per (kv head, sequence row); one warp per query head of the group.
-template <int G>
-__global__ void __launch_bounds__(32 * G) attn_decode_kernel(AttnDecodeArgs a) {
-  constexpr int CH = 128;
-  constexpr int KSTRIDE = 68;  // 17 words: conflict-free per-lane row reads
-  __shared__ __align__(16) int8_t k_sm[CH * KSTRIDE];
-  __shared__ __align__(16) int8_t v_sm[CH * 64];
-  __shared__ float q_sm[G][64];
-  __shared__ float p_sm[G][CH];
-  const int h = blockIdx.x, m = blockIdx.y;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int Dq = a.H * 64;
-  pdl_wait();
-  const int p = a.pos[m];
-  float* out = a.out + static_cast<size_t>(m) * Dq + (h * G + warp) * 64;
-  if (p < 0 || p >= a.P) {
-    out[lane] = 0.0f;
-    out[lane + 32] = 0.0f;
-    return;
-  }
-  const int slot = a.slot[m];
-  const bool act = a.active ? (a.active[m] != 0) : true;
-  const size_t sidx = (static_cast<size_t>(slot) * a.L + a.layer) * a.Hkv + h;
-  const float sK = a.ks[sidx], sV = a.vs[sidx];
-  int8_t* kbase = a.kc + sidx * static_cast<size_t>(a.P) * 64;
-  int8_t* vbase = a.vc + sidx * static_cast<size_t>(a.P) * 64;
-  const float* row = a.qkv + static_cast<size_t>(m) * a.ld;
-  const float* cs = a.cos + static_cast<size_t>(p) * 64;
-  const float* sn = a.sin + static_cast<size_t>(p) * 64;
-
-  if (warp == 0 && act) {
-    // new K row: RoPE (model/tinyllama.py:74-80), quantize with the frozen
-    // per-(layer, kv head) scale, append at position p.
-    const float* kr = row + Dq + h * 64;
-    const float* vr = row + Dq + a.Hkv * 64 + h * 64;
-    const float k0 = kr[lane], k1 = kr[lane + 32];
-    const float r0 = __fadd_rn(__fmul_rn(k0, cs[lane]), __fmul_rn(-k1, sn[lane]));
-    const float r1 = __fadd_rn(__fmul_rn(k1, cs[lane + 32]), __fmul_rn(k0, sn[lane + 32]));
-    kbase[static_cast<size_t>(p) * 64 + lane] = static_cast<int8_t>(quantize_one(r0, sK));
-    kbase[static_cast<size_t>(p) * 64 + lane + 32] = static_cast<int8_t>(quantize_one(r1, sK));
-    vbase[static_cast<size_t>(p) * 64 + lane] = static_cast<int8_t>(quantize_one(vr[lane], sV));
-    vbase[static_cast<size_t>(p) * 64 + lane + 32] = static_cast<int8_t>(quantize_one(vr[lane + 32], sV));
-  }
-  {
-    const float* qr = row + (h * G + warp) * 64;
-    const float q0 = qr[lane], q1 = qr[lane + 32];
-    q_sm[warp][lane] = __fadd_rn(__fmul_rn(q0, cs[lane]), __fmul_rn(-q1, sn[lane]));
-    q_sm[warp][lane + 32] = __fadd_rn(__fmul_rn(q1, cs[lane + 32]), __fmul_rn(q0, sn[lane + 32]));
-  }
-  __syncthreads();
-  pdl_launch_dependents();
-
-  const float score_scale = sK * 0.125f;
-  float m_run = -INFINITY, l_run = 0.0f, acc0 = 0.0f, acc1 = 0.0f;
-  const int ntot = p + 1;
-  for (int t0 = 0; t0 < ntot; t0 += CH) {
-    const int n = min(CH, ntot - t0);
-    for (int wi = tid; wi < n * 16; wi += 32 * G) {
-      const int r = wi >> 4, c = wi & 15;
-      reinterpret_cast<int*>(k_sm + r * KSTRIDE)[c] =
-          reinterpret_cast<const int*>(kbase + static_cast<size_t>(t0 + r) * 64)[c];
-    }
-    for (int wi = tid; wi < n * 4; wi += 32 * G) {
-      const int r = wi >> 2, c = wi & 3;
-      reinterpret_cast<int4*>(v_sm + r * 64)[c] =
-          reinterpret_cast<const int4*>(vbase + static_cast<size_t>(t0 + r) * 64)[c];
-    }
-    __syncthreads();
-    float cmax = -INFINITY;
-    for (int tt = lane; tt < n; tt += 32) {
-      const int* kw = reinterpret_cast<const int*>(k_sm + tt * KSTRIDE);
-      float s = 0.0f;
-#pragma unroll
-      for (int w4 = 0; w4 < 16; ++w4) {
-        const int v = kw[w4];
-        s += static_cast<float>(static_cast<int8_t>(v & 0xff)) * q_sm[warp][4 * w4];
-        s += static_cast<float>(static_cast<int8_t>((v >> 8) & 0xff)) * q_sm[warp][4 * w4 + 1];
-        s += static_cast<float>(static_cast<int8_t>((v >> 16) & 0xff)) * q_sm[warp][4 * w4 + 2];
-        s += static_cast<float>(static_cast<int8_t>((v >> 24) & 0xff)) * q_sm[warp][4 * w4 + 3];
-      }
-      s *= score_scale;
-      p_sm[warp][tt] = s;
-      cmax = fmaxf(cmax, s);
-    }
-    cmax = warp_max(cmax);
-    const float m_new = fmaxf(m_run, cmax);
-    const float corr = expf(m_run - m_new);
-    l_run *= corr;
-    acc0 *= corr;
-    acc1 *= corr;
-    __syncwarp();
-    float lsum = 0.0f;
-    for (int tt = lane; tt < n; tt += 32) {
-      const float e = expf(p_sm[warp][tt] - m_new);
-      p_sm[warp][tt] = e;
-      lsum += e;
-    }
-    l_run += warp_sum(lsum);
-    m_run = m_new;
-    __syncwarp();
-    for (int tt = 0; tt < n; ++tt) {
-      const float e = p_sm[warp][tt];
-      acc0 += e * static_cast<float>(v_sm[tt * 64 + lane]);
-      acc1 += e * static_cast<float>(v_sm[tt * 64 + lane + 32]);
-    }
-    __syncthreads();
-  }
-  const float inv = sV / l_run;
-  out[lane] = acc0 * inv;
-  out[lane + 32] = acc1 * inv;
-}
-
-cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) {
-  const int G = a.H / a.Hkv;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.Hkv, a.M);
-  cfg.blockDim = dim3(32 * G);
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  switch (G) {
-    case 1: return cudaLaunchKernelEx(&cfg, attn_decode_kernel<1>, a);
-    case 2: return cudaLaunchKernelEx(&cfg, attn_decode_kernel<2>, a);
-    case 4: return cudaLaunchKernelEx(&cfg, attn_decode_kernel<4>, a);
-    case 8: return cudaLaunchKernelEx(&cfg, attn_decode_kernel<8>, a);
-    default: return cudaErrorInvalidValue;
-  }
 }
 
 // ================================================================= prefill

@@ -112,8 +112,15 @@ struct AttnDecodeArgs {
   const float* cos = nullptr;   // [P][64]
   const float* sin = nullptr;
   float* out = nullptr;         // [M][H*64]
+  float* part = nullptr;        // split partials, attn_part_floats(M, Hkv, P)
+  unsigned int* counters = nullptr;  // [M][Hkv], zero on entry and on exit
+  int splits = 0;               // set by the launcher
 };
+constexpr int kAttnPartStride = 8 * 66;  // per split: 8 heads x (max, sum, 64 values)
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);
+int attn_split_len(int M);
+int attn_splits(int M, int P);
+size_t attn_part_floats(int M, int Hkv, int P);
 
 // ---- prefill helpers (rows of n_seq sequences of seq_len tokens each)
 cudaError_t launch_embed(const float* table, const int* ids, float* x, int rows, int D,

@@ -177,4 +177,33 @@ tl_status tl_lmhead_argmax(const float* x, const float* gamma, float eps, const 
   return st;
 }
 
+tl_status tl_attn_decode(const float* qkv, const int32_t* pos, const int32_t* slot, int8_t* kc, int8_t* vc,
+                         const float* ks, const float* vs, const float* rope_cos, const float* rope_sin,
+                         int32_t layer, int32_t num_layers, int32_t heads, int32_t kv_heads,
+                         int32_t max_positions, int32_t rows, float* out, void* stream) {
+  if (!qkv || !pos || !slot || !kc || !vc || !ks || !vs || !rope_cos || !rope_sin || !out)
+    return TL_ERR_INVALID_ARGUMENT;
+  if (rows <= 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads || heads / kv_heads > 8 ||
+      layer < 0 || layer >= num_layers || max_positions <= 0)
+    return TL_ERR_INVALID_ARGUMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* part = nullptr;
+  unsigned int* cnt = nullptr;
+  const size_t nparts = attn_part_floats(rows, kv_heads, max_positions);
+  TL_OPS_TRY(cu(cudaMallocAsync(reinterpret_cast<void**>(&part), nparts * sizeof(float), s)));
+  tl_status st = cu(cudaMallocAsync(reinterpret_cast<void**>(&cnt), static_cast<size_t>(rows) * kv_heads * 4, s));
+  if (st == TL_OK) st = cu(cudaMemsetAsync(cnt, 0, static_cast<size_t>(rows) * kv_heads * 4, s));
+  if (st == TL_OK) {
+    AttnDecodeArgs a;
+    a.qkv = qkv; a.ld = (heads + 2 * kv_heads) * 64; a.pos = pos; a.slot = slot; a.active = nullptr;
+    a.kc = kc; a.vc = vc; a.ks = ks; a.vs = vs; a.layer = layer; a.L = num_layers; a.H = heads;
+    a.Hkv = kv_heads; a.P = max_positions; a.M = rows; a.cos = rope_cos; a.sin = rope_sin; a.out = out;
+    a.part = part; a.counters = cnt;
+    st = cu(launch_attn_decode(a, s, false));
+  }
+  if (part) cudaFreeAsync(part, s);
+  if (cnt) cudaFreeAsync(cnt, s);
+  return st;
+}
+
 }  // extern "C"

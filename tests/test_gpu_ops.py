@@ -215,3 +215,57 @@ def test_quantized_linear_tc(pkg, lib, m):
     ref, rdbg = G.quantized_linear(x, w)
     np.testing.assert_array_equal(dbg["accum_int32"], rdbg["accum_int32"])
     np.testing.assert_array_equal(out, ref)
+
+
+def attn_reference(qkv, pos, slot, kc, vc, ks, vs, cos, sin, layer, H, Hkv):
+    """NumPy decode attention with the engine's INT8-cache semantics
+    (oracle/kv_golden.py): RoPE q/k, append quantized k/v at pos, attend over
+    0..pos with dequantized K/V (float64 scores as in the reference)."""
+    G = H // Hkv
+    out = np.zeros((len(pos), H * 64), np.float32)
+    kc, vc = kc.copy(), vc.copy()
+    for r, (p, s) in enumerate(zip(pos, slot)):
+        row = qkv[r]
+        q = row[:H * 64].reshape(H, 1, 64)
+        k = row[H * 64:(H + Hkv) * 64].reshape(Hkv, 1, 64)
+        v = row[(H + Hkv) * 64:].reshape(Hkv, 1, 64)
+        q = G_.rope(q, cos[p:p + 1], sin[p:p + 1])
+        k = G_.rope(k, cos[p:p + 1], sin[p:p + 1])
+        for h in range(Hkv):
+            kc[s, layer, h, p] = G_.quantize_with_scale(k[h, 0], float(ks[s, layer, h]))
+            vc[s, layer, h, p] = G_.quantize_with_scale(v[h, 0], float(vs[s, layer, h]))
+        kd = kc[s, layer, :, :p + 1].astype(np.float32) * ks[s, layer][:, None, None]
+        vd = vc[s, layer, :, :p + 1].astype(np.float32) * vs[s, layer][:, None, None]
+        out[r] = G_.attention_core(q, kd, vd, G, np.float64(0.125), False)[0]
+    return out, kc, vc
+
+
+G_ = G
+
+
+@pytest.mark.parametrize("rows,H,Hkv,positions", [(1, 32, 4, [5]), (1, 32, 4, [300]), (3, 4, 2, [0, 63, 64]),
+                                                  (2, 32, 4, [1023, 2047]), (20, 32, 4, list(range(0, 2000, 100)))])
+def test_attn_decode_matches_reference(pkg, lib, rows, H, Hkv, positions):
+    rng = np.random.default_rng(rows * 31 + H + positions[0])
+    L, P = 2, 2048
+    slots = rows + 1
+    kc = rng.integers(-127, 128, (slots, L, Hkv, P, 64), dtype=np.int8)
+    vc = rng.integers(-127, 128, (slots, L, Hkv, P, 64), dtype=np.int8)
+    ks = rng.uniform(0.005, 0.03, (slots, L, Hkv)).astype(np.float32)
+    vs = rng.uniform(0.005, 0.03, (slots, L, Hkv)).astype(np.float32)
+    qkv = rng.standard_normal((rows, (H + 2 * Hkv) * 64), dtype=np.float32)
+    pos = np.array(positions, np.int32)
+    slot = (np.arange(rows, dtype=np.int32) + 1) % slots
+    cos, sin = G.build_rope_cache(P, 64, 10000.0)
+    ref, kref, vref = attn_reference(qkv, pos, slot, kc, vc, ks, vs, cos, sin, 1, H, Hkv)
+    dkc, dvc = dev(kc), dev(vc)
+    out = torch.empty((rows, H * 64), dtype=torch.float32, device="cuda")
+    pkg.shim.check(lib.tl_attn_decode(dev(qkv).data_ptr(), dev(pos).data_ptr(), dev(slot).data_ptr(),
+                                      dkc.data_ptr(), dvc.data_ptr(), dev(ks).data_ptr(), dev(vs).data_ptr(),
+                                      dev(cos).data_ptr(), dev(sin).data_ptr(), 1, L, H, Hkv, P, rows,
+                                      out.data_ptr(), stream()), "attn")
+    got = out.cpu().numpy()
+    err = np.max(np.abs(got - ref)) / np.max(np.abs(ref))
+    assert err < 2e-6, err
+    np.testing.assert_array_equal(dkc.cpu().numpy(), kref)
+    np.testing.assert_array_equal(dvc.cpu().numpy(), vref)
