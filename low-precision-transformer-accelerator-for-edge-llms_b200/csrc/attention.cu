@@ -8,8 +8,8 @@
 // are quantized with the frozen per-(layer, kv head) scales and appended in
 // place (rtl/memory/kv_cache_manager.sv:43-47 layout).
 //
-// Mapping: one CTA per (kv head, sequence, context split of TS positions),
-// four warps. Each warp runs flash-attention tiles of 16 positions with
+// Mapping: a fixed number of CTAs per (kv head, sequence), each looping over
+// its share of TS-position context chunks, four warps. Each warp runs flash-attention tiles of 16 positions with
 // mma.sync m16n8k16 fp16: A = the group's query rows (8 heads, padded to 16)
 // for Q.K^T and the probabilities for P.V; B = INT8 K / V rows converted to
 // fp16, which is exact for |v| <= 127. To keep fp32-level accuracy the fp32
@@ -21,9 +21,10 @@
 // float error visible as rounding flips, so attention has to be as accurate
 // as fp32 arithmetic.) Warps merge in shared memory; splits merge via a
 // per-(sequence, kv head) partial buffer, the last CTA to arrive (atomic
-// ticket) producing the output. Splits beyond the context exit at once.
+// ticket) producing the output. CTAs with no chunk exit at once.
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cmath>
 
 #include "common.cuh"
@@ -96,10 +97,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_mma_kernel(AttnDecod
     return;
   }
   const int T = p + 1;
-  const int t_begin = sp * TS;
-  if (t_begin >= T) return;  // no work for this split (not counted in the merge)
-  const int n_act = (T + TS - 1) / TS;
-  const int n = min(TS, T - t_begin);
+  const int nz = gridDim.z;
+  const int n_chunks = (T + TS - 1) / TS;
+  if (sp >= n_chunks) return;  // no work for this CTA (not counted in the merge)
+  const int n_act = min(nz, n_chunks);
   const int slot = a.slot[m];
   const bool act = a.active ? (a.active[m] != 0) : true;
   const size_t sidx = (static_cast<size_t>(slot) * a.L + a.layer) * a.Hkv + h;
@@ -110,20 +111,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_mma_kernel(AttnDecod
   const float* cs = a.cos + static_cast<size_t>(p) * 64;
   const float* sn = a.sin + static_cast<size_t>(p) * 64;
 
-  // ---- stage this split's K/V rows (zero past the context)
-  for (int i = tid; i < TS * 4; i += kAttnThreads) {
-    const int r = i >> 2, c = i & 3;
-    int4 v = make_int4(0, 0, 0, 0);
-    if (r < n) v = reinterpret_cast<const int4*>(kbase + static_cast<size_t>(t_begin + r) * 64)[c];
-    *reinterpret_cast<int4*>(k_sm + r * kKStride + c * 16) = v;
-  }
-  for (int i = tid; i < TS * 8; i += kAttnThreads) {
-    const int r = i >> 3, c = i & 7;
-    uint2 v = make_uint2(0u, 0u);
-    if (r < n) v = reinterpret_cast<const uint2*>(vbase + static_cast<size_t>(t_begin + r) * 64)[c];
-    *reinterpret_cast<uint2*>(v_sm + r * kVStride + c * 8) = v;
-  }
-  // ---- rotated queries of the group (rows >= G stay zero)
+  // ---- rotated queries of the group (rows >= G stay zero), power-of-two scaled
   for (int g = warp; g < 8; g += kAttnWarps) {
     float r0 = 0.0f, r1 = 0.0f;
     if (g < G) {
@@ -136,29 +124,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_mma_kernel(AttnDecod
     q_sm[g][lane] = r0 * qs;
     q_sm[g][lane + 32] = r1 * qs;
     if (lane == 0) q_scale[g] = qs;
-  }
-  __syncthreads();
-  // ---- the new position's K (RoPE) and V: quantize, append, and use
-  if (warp == 0 && p >= t_begin && p < t_begin + n) {
-    const float* kr = row + Dq + h * 64;
-    const float* vr = row + Dq + a.Hkv * 64 + h * 64;
-    const float k0 = kr[lane], k1 = kr[lane + 32];
-    const float r0 = __fadd_rn(__fmul_rn(k0, cs[lane]), __fmul_rn(-k1, sn[lane]));
-    const float r1 = __fadd_rn(__fmul_rn(k1, cs[lane + 32]), __fmul_rn(k0, sn[lane + 32]));
-    const int8_t qk0 = static_cast<int8_t>(quantize_one(r0, sK)), qk1 = static_cast<int8_t>(quantize_one(r1, sK));
-    const int8_t qv0 = static_cast<int8_t>(quantize_one(vr[lane], sV));
-    const int8_t qv1 = static_cast<int8_t>(quantize_one(vr[lane + 32], sV));
-    const int rl = p - t_begin;
-    k_sm[rl * kKStride + lane] = qk0;
-    k_sm[rl * kKStride + lane + 32] = qk1;
-    v_sm[rl * kVStride + lane] = qv0;
-    v_sm[rl * kVStride + lane + 32] = qv1;
-    if (act) {
-      kbase[static_cast<size_t>(p) * 64 + lane] = qk0;
-      kbase[static_cast<size_t>(p) * 64 + lane + 32] = qk1;
-      vbase[static_cast<size_t>(p) * 64 + lane] = qv0;
-      vbase[static_cast<size_t>(p) * 64 + lane + 32] = qv1;
-    }
   }
   __syncthreads();
 
@@ -178,56 +143,100 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_mma_kernel(AttnDecod
 #pragma unroll
   for (int dt = 0; dt < 8; ++dt) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.0f;
 
-  for (int t0 = warp * 16; t0 < n; t0 += kAttnWarps * 16) {
-    float s[2][4];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
-      const int8_t* kr = k_sm + (t0 + nt * 8 + g) * kKStride + q4 * 2;
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        const uint32_t b0 = pack_i8(kr[ks * 16], kr[ks * 16 + 1]);
-        const uint32_t b1 = pack_i8(kr[ks * 16 + 8], kr[ks * 16 + 9]);
-        mma16816(s[nt], qa_hi[ks][0], qa_hi[ks][1], b0, b1);
-        mma16816(s[nt], qa_lo[ks][0], qa_lo[ks][1], b0, b1);
+  // This CTA owns chunks sp, sp + nz, ... of TS positions; the online
+  // softmax state of each warp carries across them.
+  for (int chunk = sp; chunk < n_chunks; chunk += nz) {
+    const int t_begin = chunk * TS;
+    const int n = min(TS, T - t_begin);
+    __syncthreads();  // previous chunk fully consumed
+    for (int i = tid; i < TS * 4; i += kAttnThreads) {
+      const int r = i >> 2, c = i & 3;
+      int4 v = make_int4(0, 0, 0, 0);
+      if (r < n) v = reinterpret_cast<const int4*>(kbase + static_cast<size_t>(t_begin + r) * 64)[c];
+      *reinterpret_cast<int4*>(k_sm + r * kKStride + c * 16) = v;
+    }
+    for (int i = tid; i < TS * 8; i += kAttnThreads) {
+      const int r = i >> 3, c = i & 7;
+      uint2 v = make_uint2(0u, 0u);
+      if (r < n) v = reinterpret_cast<const uint2*>(vbase + static_cast<size_t>(t_begin + r) * 64)[c];
+      *reinterpret_cast<uint2*>(v_sm + r * kVStride + c * 8) = v;
+    }
+    __syncthreads();
+    // the new position's K (RoPE) and V: quantize, append, and use
+    if (warp == 0 && p >= t_begin && p < t_begin + n) {
+      const float* kr = row + Dq + h * 64;
+      const float* vr = row + Dq + a.Hkv * 64 + h * 64;
+      const float k0 = kr[lane], k1 = kr[lane + 32];
+      const float r0 = __fadd_rn(__fmul_rn(k0, cs[lane]), __fmul_rn(-k1, sn[lane]));
+      const float r1 = __fadd_rn(__fmul_rn(k1, cs[lane + 32]), __fmul_rn(k0, sn[lane + 32]));
+      const int8_t qk0 = static_cast<int8_t>(quantize_one(r0, sK)), qk1 = static_cast<int8_t>(quantize_one(r1, sK));
+      const int8_t qv0 = static_cast<int8_t>(quantize_one(vr[lane], sV));
+      const int8_t qv1 = static_cast<int8_t>(quantize_one(vr[lane + 32], sV));
+      const int rl = p - t_begin;
+      k_sm[rl * kKStride + lane] = qk0;
+      k_sm[rl * kKStride + lane + 32] = qk1;
+      v_sm[rl * kVStride + lane] = qv0;
+      v_sm[rl * kVStride + lane + 32] = qv1;
+      if (act) {
+        kbase[static_cast<size_t>(p) * 64 + lane] = qk0;
+        kbase[static_cast<size_t>(p) * 64 + lane + 32] = qk1;
+        vbase[static_cast<size_t>(p) * 64 + lane] = qv0;
+        vbase[static_cast<size_t>(p) * 64 + lane + 32] = qv1;
       }
     }
-    float v4[4];
-    float mx = -INFINITY;
+    __syncthreads();
+
+    for (int t0 = warp * 16; t0 < n; t0 += kAttnWarps * 16) {
+      float s[2][4];
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
+      for (int nt = 0; nt < 2; ++nt) {
+        s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
+        const int8_t* kr = k_sm + (t0 + nt * 8 + g) * kKStride + q4 * 2;
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int tl = t0 + nt * 8 + q4 * 2 + j;
-        const float val = tl < n ? s[nt][j] * score_scale : -INFINITY;
-        v4[nt * 2 + j] = val;
-        mx = fmaxf(mx, val);
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint32_t b0 = pack_i8(kr[ks * 16], kr[ks * 16 + 1]);
+          const uint32_t b1 = pack_i8(kr[ks * 16 + 8], kr[ks * 16 + 9]);
+          mma16816(s[nt], qa_hi[ks][0], qa_hi[ks][1], b0, b1);
+          mma16816(s[nt], qa_lo[ks][0], qa_lo[ks][1], b0, b1);
+        }
       }
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    const float m_new = fmaxf(m_run, mx);
-    const float corr = expf(m_run - m_new);
-    float pv[4];
+      float v4[4];
+      float mx = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) pv[j] = expf(v4[j] - m_new);
-    l_part = l_part * corr + (pv[0] + pv[1] + pv[2] + pv[3]);
+      for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-    for (int dt = 0; dt < 8; ++dt) {
-      o[dt][0] *= corr;
-      o[dt][1] *= corr;
-    }
-    m_run = m_new;
-    uint32_t pa_hi0, pa_lo0, pa_hi2, pa_lo2;
-    split2(pv[0] * kPScale, pv[1] * kPScale, pa_hi0, pa_lo0);
-    split2(pv[2] * kPScale, pv[3] * kPScale, pa_hi2, pa_lo2);
-    const int8_t* vr = v_sm + (t0 + q4 * 2) * kVStride + g;
+        for (int j = 0; j < 2; ++j) {
+          const int tl = t0 + nt * 8 + q4 * 2 + j;
+          const float val = tl < n ? s[nt][j] * score_scale : -INFINITY;
+          v4[nt * 2 + j] = val;
+          mx = fmaxf(mx, val);
+        }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_new = fmaxf(m_run, mx);
+      const float corr = expf(m_run - m_new);
+      float pv[4];
 #pragma unroll
-    for (int dt = 0; dt < 8; ++dt) {
-      const int8_t* vc = vr + dt * 8;
-      const uint32_t b0 = pack_i8(vc[0], vc[kVStride]);
-      const uint32_t b1 = pack_i8(vc[8 * kVStride], vc[9 * kVStride]);
-      mma16816(o[dt], pa_hi0, pa_hi2, b0, b1);
-      mma16816(o[dt], pa_lo0, pa_lo2, b0, b1);
+      for (int j = 0; j < 4; ++j) pv[j] = expf(v4[j] - m_new);
+      l_part = l_part * corr + (pv[0] + pv[1] + pv[2] + pv[3]);
+#pragma unroll
+      for (int dt = 0; dt < 8; ++dt) {
+        o[dt][0] *= corr;
+        o[dt][1] *= corr;
+      }
+      m_run = m_new;
+      uint32_t pa_hi0, pa_lo0, pa_hi2, pa_lo2;
+      split2(pv[0] * kPScale, pv[1] * kPScale, pa_hi0, pa_lo0);
+      split2(pv[2] * kPScale, pv[3] * kPScale, pa_hi2, pa_lo2);
+      const int8_t* vr = v_sm + (t0 + q4 * 2) * kVStride + g;
+#pragma unroll
+      for (int dt = 0; dt < 8; ++dt) {
+        const int8_t* vc = vr + dt * 8;
+        const uint32_t b0 = pack_i8(vc[0], vc[kVStride]);
+        const uint32_t b1 = pack_i8(vc[8 * kVStride], vc[9 * kVStride]);
+        mma16816(o[dt], pa_hi0, pa_hi2, b0, b1);
+        mma16816(o[dt], pa_lo0, pa_lo2, b0, b1);
+      }
     }
   }
   pdl_launch_dependents();
@@ -296,10 +305,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_mma_kernel(AttnDecod
 
 }  // namespace
 
+// Chunk length and CTAs per (row, kv head): batched decode has many rows, so
+// few CTAs per row; a single sequence spreads its context over more CTAs.
 int attn_split_len(int M) { return M >= 16 ? 128 : 64; }
 int attn_splits(int M, int P) {
   const int ts = attn_split_len(M);
-  return (P + ts - 1) / ts;
+  const int most = (P + ts - 1) / ts;
+  return std::min(most, M >= 16 ? 4 : 16);
 }
 
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a0, cudaStream_t s, bool pdl) {

@@ -149,9 +149,11 @@ TL_DEV float silu_mul_tc(float g, float u) {
   return __fmul_rn(__fdiv_rn(g, den), u);
 }
 
-// Epilogue of one group of 16 accumulators (columns m0c..m0c+15) of TMEM
-// lane n. Every lane of the warp calls it (the SiLU pairing shuffles).
-TL_DEV void tc_epilogue16(const TcArgs& a, int n, int m0c, const int* v) {
+// Epilogue of one group of 16 accumulators (tokens m0c..m0c+15) of TMEM lane
+// (output channel) n; sx[j] is the float64 activation scale of token m0c+j.
+// Every lane of the warp calls it (the SiLU pairing shuffles). Residual reads
+// are all issued before the first store (out may alias resid).
+TL_DEV void tc_epilogue16(const TcArgs& a, int n, int m0c, const int* v, const double* sx) {
   const bool n_ok = n < a.N;
   if (a.epi == EPI_I32) {
     if (!n_ok) return;
@@ -174,25 +176,34 @@ TL_DEV void tc_epilogue16(const TcArgs& a, int n, int m0c, const int* v) {
   }
   const double sw = n_ok ? a.w_scale[n] : 0.0;
   const int lane = threadIdx.x & 31;
+  float y[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) y[j] = dequant(v[j], sx[j], sw);
+  if (a.epi == EPI_RESID) {
+    float r[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int m = m0c + j;
+      r[j] = (n_ok && m < a.M) ? a.resid[static_cast<size_t>(m) * a.N + n] : 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) y[j] = __fadd_rn(r[j], y[j]);
+  }
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
     const int m = m0c + j;
     const bool ok = n_ok && m < a.M;
-    const double sx = ok ? quant_scale64(a.in_absmax ? a.in_absmax[m / a.rows_per_group] : 0.0f) : 1.0;
-    const float y = ok ? dequant(v[j], sx, sw) : 0.0f;
     float mag = 0.0f;
     if (a.epi == EPI_SILU) {
-      const float partner = __shfl_xor_sync(0xffffffffu, y, 1);
+      const float partner = __shfl_xor_sync(0xffffffffu, y[j], 1);
       if (ok && (lane & 1) == 0) {
-        const float h = silu_mul_tc(y, partner);
+        const float h = silu_mul_tc(y[j], partner);
         a.out_f32[static_cast<size_t>(m) * (a.N >> 1) + (n >> 1)] = h;
         mag = fabsf(h);
       }
     } else if (ok) {
-      const size_t o = static_cast<size_t>(m) * a.N + n;
-      const float r = (a.epi == EPI_RESID) ? __fadd_rn(a.resid[o], y) : y;
-      a.out_f32[o] = r;
-      mag = fabsf(r);
+      a.out_f32[static_cast<size_t>(m) * a.N + n] = y[j];
+      mag = fabsf(y[j]);
     }
     if (a.out_absmax) {
       mag = warp_max(mag);
@@ -201,9 +212,10 @@ TL_DEV void tc_epilogue16(const TcArgs& a, int n, int m0c, const int* v) {
   }
 }
 
+
 // Epilogue of a single accumulator (split-K path). The SiLU pairing of rows
 // (2j, 2j+1) uses the neighbouring lane, which owns row n^1 for the same m.
-TL_DEV void tc_epilogue1(const TcArgs& a, int n, int m, int acc) {
+TL_DEV void tc_epilogue1(const TcArgs& a, int n, int m, int acc, double sxm, float resid) {
   const bool ok = n < a.N && m < a.M;
   if (a.epi == EPI_I32) {
     if (ok) a.out_i32[static_cast<size_t>(m) * a.N + n] = acc;
@@ -215,8 +227,7 @@ TL_DEV void tc_epilogue1(const TcArgs& a, int n, int m, int acc) {
     return;
   }
   const double sw = ok ? a.w_scale[n] : 0.0;
-  const double sx = ok ? quant_scale64(a.in_absmax ? a.in_absmax[m / a.rows_per_group] : 0.0f) : 1.0;
-  const float y = ok ? dequant(acc, sx, sw) : 0.0f;
+  const float y = ok ? dequant(acc, sxm, sw) : 0.0f;
   if (a.epi == EPI_SILU) {
     const float partner = __shfl_xor_sync(0xffffffffu, y, 1);
     if (ok && (n & 1) == 0) a.out_f32[static_cast<size_t>(m) * (a.N >> 1) + (n >> 1)] = silu_mul_tc(y, partner);
@@ -224,13 +235,14 @@ TL_DEV void tc_epilogue1(const TcArgs& a, int n, int m, int acc) {
   }
   if (!ok) return;
   const size_t o = static_cast<size_t>(m) * a.N + n;
-  a.out_f32[o] = (a.epi == EPI_RESID) ? __fadd_rn(a.resid[o], y) : y;
+  a.out_f32[o] = (a.epi == EPI_RESID) ? __fadd_rn(resid, y) : y;
 }
 
 template <int BN>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, TcArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
+  __shared__ double sx_sm[BN];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int kBBytes = BN * kTileK;
   constexpr int kStage = kABytes + kBBytes;
@@ -267,19 +279,31 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  pdl_wait();  // activations come from the previous kernel
-
   bool ok = true;
   if (warp == 0 && lane == 0) {
-    for (int kb = kb0, i = 0; kb < kb1 && ok; ++kb, ++i) {
+    // Weights do not depend on the previous kernel: the first `pre` weight
+    // tiles are requested before griddepcontrol.wait, so under programmatic
+    // dependent launch they stream while the producer of X is finishing.
+    const int pre = min(stages, kb1 - kb0);
+    for (int i = 0; i < pre; ++i) {
+      mbar_arrive_expect_tx(full + i, kStage);
+      tma_load_2d(smem + i * kStage, &tm_w, (kb0 + i) * kTileK, n0, full + i);
+    }
+    pdl_wait();
+    for (int i = 0; i < pre; ++i)
+      tma_load_2d(smem + i * kStage + kABytes, &tm_x, (kb0 + i) * kTileK, m0, full + i);
+    for (int kb = kb0 + pre, i = pre; kb < kb1 && ok; ++kb, ++i) {
       const int s = i % stages, round = i / stages;
-      if (round > 0) ok = mbar_wait(empty + s, (round - 1) & 1, 1u);
+      ok = mbar_wait(empty + s, (round - 1) & 1, 1u);
       if (!ok) break;
       mbar_arrive_expect_tx(full + s, kStage);
       tma_load_2d(smem + s * kStage, &tm_w, kb * kTileK, n0, full + s);
       tma_load_2d(smem + s * kStage + kABytes, &tm_x, kb * kTileK, m0, full + s);
     }
-  } else if (warp == 1 && lane == 0) {
+  } else {
+    pdl_wait();  // activations, scales and residuals come from earlier kernels
+  }
+  if (warp == 1 && lane == 0) {
     constexpr uint32_t idesc = idesc_i8(kTileN, BN);
     for (int kb = kb0, i = 0; kb < kb1 && ok; ++kb, ++i) {
       const int s = i % stages, round = i / stages;
@@ -300,6 +324,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const bool ready = __syncthreads_and(mbar_wait(done, 0, 3u) ? 1 : 0) != 0;
   tc_fence_after();
   pdl_launch_dependents();
+  // per-token activation scale (absmax / 127 in float64) once per CTA
+  for (int j = threadIdx.x; j < BN; j += kTcThreads) {
+    const int m = m0 + j;
+    sx_sm[j] = (m < a.M && a.in_absmax) ? quant_scale64(a.in_absmax[m / a.rows_per_group]) : 1.0;
+  }
+  __syncthreads();
 
   const int n = n0 + warp * 32 + lane;
   const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
@@ -308,7 +338,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int c = 0; c < BN / 16; ++c) {
         int v[16];
         tmem_ld16(lane_base + c * 16, v);
-        tc_epilogue16(a, n, m0 + c * 16, v);
+        tc_epilogue16(a, n, m0 + c * 16, v, sx_sm + c * 16);
       }
     }
   } else {
@@ -355,10 +385,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           acc.w += v[p].w;
         }
       if (ready) {
-        tc_epilogue1(a, n0 + nloc, m0 + q * 4 + 0, acc.x);
-        tc_epilogue1(a, n0 + nloc, m0 + q * 4 + 1, acc.y);
-        tc_epilogue1(a, n0 + nloc, m0 + q * 4 + 2, acc.z);
-        tc_epilogue1(a, n0 + nloc, m0 + q * 4 + 3, acc.w);
+        const int nn = n0 + nloc, mm = m0 + q * 4;
+        float r[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (a.epi == EPI_RESID && nn < a.N) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (mm + j < a.M) r[j] = a.resid[static_cast<size_t>(mm + j) * a.N + nn];
+        }
+        tc_epilogue1(a, nn, mm + 0, acc.x, sx_sm[q * 4 + 0], r[0]);
+        tc_epilogue1(a, nn, mm + 1, acc.y, sx_sm[q * 4 + 1], r[1]);
+        tc_epilogue1(a, nn, mm + 2, acc.z, sx_sm[q * 4 + 2], r[2]);
+        tc_epilogue1(a, nn, mm + 3, acc.w, sx_sm[q * 4 + 3], r[3]);
       }
     }
     cluster_sync();  // peers keep their smem until every CTA has read it
@@ -421,9 +458,12 @@ cudaError_t prepare_tc_t() {
 
 }  // namespace
 
+// Ring depth: at most 4 stages (<= 96 KB for 64-token tiles), so two CTAs
+// fit on an SM and the next kernel's CTAs can start under programmatic
+// dependent launch.
 int tc_max_stages(int bn) {
   const int stage = kABytes + bn * kTileK;
-  return std::max(2, std::min(8, (200 * 1024) / stage));
+  return std::max(2, std::min(4, (200 * 1024) / stage));
 }
 
 int tc_pick_bn(int M) {

@@ -359,8 +359,11 @@ static int gemv_grid_x(int N, int MR) {
   const int sms = (dev >= 0 && dev < 64 && g_num_sms[dev] > 0) ? g_num_sms[dev] : 148;
   const int groups = (N + kGemvRW - 1) / kGemvRW;
   const int need = (groups + kGemvWarps - 1) / kGemvWarps;
-  const int per_sm = MR <= 2 ? 2 : 1;  // register-limited residency (ptxas: <=104 vs >=128 regs)
-  return std::max(1, std::min(std::min(need, per_sm * sms), kGemvMaxGrid));
+  // One CTA per SM (8 warps, two work items in flight each) saturates HBM and
+  // leaves room on every SM for the next kernel's CTA to start streaming its
+  // weights early under programmatic dependent launch.
+  (void)MR;
+  return std::max(1, std::min(std::min(need, sms), kGemvMaxGrid));
 }
 
 size_t gemv_argmax_partials(int M, int N) {
