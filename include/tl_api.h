@@ -275,6 +275,25 @@ TL_API tl_status tl_attn_decode(const float* qkv, const int32_t* pos, const int3
                                 int32_t kv_heads, int32_t max_positions, int32_t rows, float* out,
                                 void* stream);
 
+/* tl_lmhead_argmax for callers that must not have a library allocate GPU
+ * memory -- a serving runtime that reserves the whole device at start-up and
+ * accounts for every byte, or a framework whose own caching allocator has to
+ * own all device memory. No counterpart in the reference (its argmax reduces
+ * in FPGA registers). Same arguments and results as tl_lmhead_argmax, but the
+ * cross-CTA reduction scratch is one fixed array inside the library (64 KiB +
+ * 256 B, held on every GPU that loads the library until the process exits)
+ * and the call makes no cudaMalloc/cudaFree. Limit: rows <=
+ * TL_LMHEAD_NOALLOC_MAX_ROWS, larger batches get TL_ERR_OUT_OF_RANGE. The
+ * first call on a device looks up the array's device address (make that
+ * first call before any stream capture). All calls share the one array: two
+ * calls that overlap on the GPU (other streams, other host threads) race, so
+ * the caller serializes them. */
+#define TL_LMHEAD_NOALLOC_MAX_ROWS 8
+TL_API tl_status tl_lmhead_argmax_noalloc(const float* x, const float* gamma, float eps, const int8_t* w_nk,
+                                          const double* w_scale, int32_t rows, int32_t vocab,
+                                          int32_t hidden, int32_t* token_out, float* logits_out,
+                                          void* stream);
+
 #ifdef __cplusplus
 }
 #endif
