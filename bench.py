@@ -45,6 +45,8 @@ TINYLLAMA = dict(hidden_size=2048, intermediate_size=5632, num_hidden_layers=22,
                  num_key_value_heads=4, head_dim=64, vocab_size=32000, max_position_embeddings=2048,
                  rms_norm_eps=1e-5, rope_theta=10000.0)
 FALLBACK_HBM_GBS = 6650.0
+# DRAM bytes (read + write) of one gate/up launch at 64 rows, measured by ncu
+GATE_UP_DRAM_BYTES = 23364864
 METRIC = "decode tok/s @bs64 (TinyLlama-1.1B INT8, 22 layers, 512-token prompts, 512 greedy tokens)"
 
 
@@ -222,25 +224,19 @@ def run_reference(a, rank, world):
 def run_ours(a, rank, world, local_rank):
     import torch
     torch.cuda.set_device(local_rank)
-    dist = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device(f"cuda:{local_rank}"))
     pkg = load_pkg()
+    from lpta_b200 import replicas
+    group = replicas.Group(world, "nccl", device=torch.device(f"cuda:{local_rank}"))
     B, S, T = a.batch, a.prompt, a.gen
     eng = pkg.Engine(TINYLLAMA, max_batch=B, device=local_rank, max_prefill_tokens=max(B * S, 8 * 2048))
     eng.init_random(1234 + rank)
-    rng = np.random.default_rng(42 + rank)
+    rng = np.random.default_rng(replicas.rank_seed(42, rank))
     prompts = rng.integers(0, 32000, (B, S)).astype(np.uint32)
     eng.prefill_batch_device(prompts)
     eng.synchronize()
     stream = torch.cuda.ExternalStream(eng.stream_handle())
 
-    def barrier():
-        if dist:
-            dist.barrier()
+    barrier = group.barrier
 
     def step():
         eng.decode_rewind(B, S)
@@ -260,13 +256,8 @@ def run_ours(a, rank, world, local_rank):
         e1.synchronize()
     torch.cuda.synchronize()
     barrier()
-    ms = e0.elapsed_time(e1)
-    if dist:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    tokens = world * B * T * a.steps
-    value = tokens / (ms / 1000.0)
+    ms = group.max(e0.elapsed_time(e1))
+    value = group.sum(B * T * a.steps) / (ms / 1000.0)
     per_step_kernels = eng.decode_step_kernel_count(B)
 
     # ---------------------------------------------- e2e through the C ABI
@@ -277,13 +268,9 @@ def run_ours(a, rank, world, local_rank):
     outs, sts = eng.generate_batch(prompts, T, out_cap=T)
     f1.record(stream)
     f1.synchronize()
-    e2e_ms = f0.elapsed_time(f1)
-    if dist:
-        t = torch.tensor([e2e_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    gen = sum(s["generated_count"] for s in sts)
-    e2e = {"value": world * gen / (e2e_ms / 1000.0), "unit": "tok/s",
+    e2e_ms = group.max(f0.elapsed_time(f1))
+    gen = group.sum(sum(s["generated_count"] for s in sts))
+    e2e = {"value": gen / (e2e_ms / 1000.0), "unit": "tok/s",
            "h2d_bytes_per_step": int(prompts.nbytes), "d2h_bytes_per_step": int(B * T * 4 + B * 3 * 4),
            "ms": e2e_ms, "includes": "prefill of the 64 prompts + 512 decode steps + host copies",
            "api": "tl_generate_batch"}
@@ -311,7 +298,10 @@ def run_ours(a, rank, world, local_rank):
         gu_ms = float(kern[3])
         achieved = bytes_gu / (gu_ms / 1e3) / 1e9
         line["roofline"] = {"bound": "hbm", "kernel": "tcgen05 gate/up GEMM + SiLU*up (M=64)", "achieved": achieved,
-                            "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "traffic": None,
+                            "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                            # dram__bytes_read.sum + dram__bytes_write.sum of this launch from
+                            # the ncu capture in profiles/gemm_tc_kernel_decode64.md
+                            "traffic": GATE_UP_DRAM_BYTES,
                             "peak_kind": peak_kind,
                             "algorithmic_bytes": bytes_gu}
         line["kernels_ms"] = {n: float(v) for n, v in zip(names, kern)}
@@ -347,12 +337,101 @@ def run_ours(a, rank, world, local_rank):
         pf_ms = h0.elapsed_time(h1)
         line["prefill"] = {"workload": "configs[4]: 8 x 2048-token prompts, 22 layers, 1 GPU",
                            "value": 8 * 2048 / (pf_ms / 1e3), "unit": "tok/s", "ms": pf_ms}
+        i8 = int8_gemm_rate(pkg, torch)
+        # prefill ops (config 4): linear 3.175e13 + causal attention 3.025e12 + LM head 1.05e9
+        pf_ops = 3.175e13 + 3.025e12 + 1.05e9
+        line["prefill"]["tensor_frac_of_cublaslt_int8"] = pf_ops / (pf_ms / 1e3) / 1e12 / i8["cublaslt_tops"]
+        line["int8_gemm"] = i8
         line["cpu_baseline"] = cpu_baseline_sample()
     eng.close()
-    if dist:
-        dist.destroy_process_group()
+    group.close()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def int8_gemm_rate(pkg, torch, n: int = 8192, iters: int = 10) -> dict:
+    """Dense INT8 tensor-core rate at n^3 (int32 out): cuBLASLt through
+    torch._int_mm, the library denominator for the prefill roofline, and this
+    build's tcgen05 kernel through tl_gemm_i8 on the same operands."""
+    lib = pkg.shim.load_library()
+    g = torch.Generator(device="cuda").manual_seed(5)
+    a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda", generator=g)
+    w = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda", generator=g)  # [N][K]
+    c = torch.empty((n, n), dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream()
+
+    def ours():
+        pkg.shim.check(lib.tl_gemm_i8(a.data_ptr(), w.data_ptr(), c.data_ptr(), n, n, n, s.cuda_stream),
+                       "tl_gemm_i8")
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(iters):
+            fn()
+        e1.record(s)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / iters
+
+    ref = torch._int_mm(a, w.t())
+    ms_lt = timed(lambda: torch._int_mm(a, w.t()))
+    ms_tl = timed(ours)
+    torch.cuda.synchronize()
+    ops = 2.0 * n ** 3
+    return {"shape": [n, n, n], "cublaslt_tops": ops / ms_lt / 1e9, "tl_gemm_i8_tops": ops / ms_tl / 1e9,
+            "tl_matches_cublaslt": bool(torch.equal(c, ref))}
+
+
+def run_profile_case(a):
+    """Bounded workload for ncu: only the kernels between cudaProfilerStart and
+    cudaProfilerStop are captured (``ncu --profile-from-start off``).
+
+    decode: full 22-layer model, ``--batch`` rows prefilled with
+    ``--profile-prompt`` tokens, rewound to position ``--profile-pos`` (the
+    mean context of the headline workload, 767), then ``--steps`` decode-step
+    graph replays inside the profiled range. KV rows between the prompt and
+    the rewind position hold whatever the cache memory holds (any int8 is a
+    valid cache byte); with the default prompt of 512 this is the headline
+    workload exactly.
+    prefill: one prefill of ``--batch`` x ``--prompt`` tokens inside the range.
+    """
+    import torch
+    torch.cuda.set_device(0)
+    torch.cuda.init()
+    pkg = load_pkg()
+    B = a.batch
+    rng = np.random.default_rng(42)
+    if a.profile_case == "decode":
+        S = a.profile_prompt
+        eng = pkg.Engine(TINYLLAMA, max_batch=B, device=0, max_prefill_tokens=B * S)
+        eng.init_random(1234)
+        eng.prefill_batch_device(rng.integers(0, 32000, (B, S)).astype(np.uint32))
+        eng.decode_rewind(B, a.profile_pos)
+        eng.decode_steps_device(B, 1)  # captures the step graph
+        eng.decode_rewind(B, a.profile_pos)
+        eng.synchronize()
+        torch.cuda.profiler.start()
+        eng.decode_steps_device(B, a.steps)
+        eng.synchronize()
+        torch.cuda.profiler.stop()
+        info = {"case": "decode", "rows": B, "prompt": S, "position": a.profile_pos, "steps": a.steps,
+                "launches_per_step": eng.decode_step_kernel_count(B)}
+    else:
+        S = a.prompt
+        eng = pkg.Engine(TINYLLAMA, max_batch=B, device=0, max_prefill_tokens=B * S)
+        eng.init_random(1234)
+        p = rng.integers(0, 32000, (B, S)).astype(np.uint32)
+        eng.prefill_batch_device(p)
+        eng.synchronize()
+        torch.cuda.profiler.start()
+        eng.prefill_batch_device(p)
+        eng.synchronize()
+        torch.cuda.profiler.stop()
+        info = {"case": "prefill", "rows": B, "prompt": S}
+    eng.close()
+    print(json.dumps({"profile_case": info}), flush=True)
 
 
 def main():
@@ -365,7 +444,14 @@ def main():
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--gen", type=int, default=512)
     ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--profile-case", choices=["decode", "prefill"], default=None,
+                    help="run a bounded workload for ncu instead of the benchmark")
+    ap.add_argument("--profile-prompt", type=int, default=512)
+    ap.add_argument("--profile-pos", type=int, default=767)
     a = ap.parse_args()
+    if a.profile_case:
+        run_profile_case(a)
+        return
     rank, world, local_rank = env_rank()
     if a.impl == "reference":
         run_reference(a, rank, world)

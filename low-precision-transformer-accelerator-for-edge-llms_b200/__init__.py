@@ -9,7 +9,7 @@ any module name. The compute lives in ``libtl_b200.so``; ``shim`` is its
 ctypes binding and mirrors the reference's Python operator API.
 """
 
-from . import shim  # noqa: F401
+from . import replicas, shim  # noqa: F401
 from .shim import (  # noqa: F401
     Engine, Linear, Layer, Model, TLError, forward_mixed, from_tinyllama_weights, load_library,
     quantize_int8, quantize_weight, quantized_linear, rms_norm, rope_tables,
