@@ -275,6 +275,21 @@ TL_API tl_status tl_attn_decode(const float* qkv, const int32_t* pos, const int3
                                 int32_t kv_heads, int32_t max_positions, int32_t rows, float* out,
                                 void* stream);
 
+/* Causal prefill attention of n_seqs sequences of seq_len tokens each over the
+ * INT8 KV cache. Replaces the attention core of mixed_precision_self_attention
+ * (model/tinyllama_gemm_int8.py:154-163: scores = Q.K^T / sqrt(64), causal
+ * mask of model/tinyllama.py:90-91, softmax of :100-103, weighted sum of V)
+ * with the cache rows of slot slot_base + i standing in for K and V.
+ * qkv: fp32 [n_seqs * seq_len][(heads + 2 * kv_heads) * 64], Q already rotated
+ * (RoPE); K/V are read from kc/vc ([slot][layer][kv_head][max_positions][64]
+ * int8, scales ks/vs [slot][layer][kv_head]). out: fp32 [rows][heads * 64].
+ * out_absmax (optional, one float per sequence, zero-initialised by the
+ * caller) receives max |out| over the sequence (atomic max). */
+TL_API tl_status tl_attn_prefill(const float* qkv, int32_t seq_len, int32_t n_seqs, const int8_t* kc,
+                                 const int8_t* vc, const float* ks, const float* vs, int32_t slot_base,
+                                 int32_t layer, int32_t num_layers, int32_t heads, int32_t kv_heads,
+                                 int32_t max_positions, float* out, float* out_absmax, void* stream);
+
 /* tl_lmhead_argmax for callers that must not have a library allocate GPU
  * memory -- a serving runtime that reserves the whole device at start-up and
  * accounts for every byte, or a framework whose own caching allocator has to

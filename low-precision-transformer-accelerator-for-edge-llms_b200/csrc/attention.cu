@@ -61,6 +61,7 @@ TL_DEV float pow2_scale(float amax) {
   frexpf(amax, &e);
   return ldexpf(1.0f, 14 - e);
 }
+TL_DEV uint32_t smem_u32_attn(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 constexpr float kPScale = 16384.0f;  // probabilities in [0, 1] -> [0, 2^14]
 TL_DEV uint32_t pack_i8(int8_t a, int8_t b) {
   return pack2(static_cast<float>(a), static_cast<float>(b));
@@ -303,7 +304,282 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_mma_kernel(AttnDecod
   if (tid == 0) a.counters[static_cast<size_t>(m) * a.Hkv + h] = 0u;
 }
 
+// ------------------------------------------------------------------ prefill
+// Causal prefill attention, flash-attention style on mma.sync m16n8k16 fp16
+// with the same hi/lo operand split as decode. CTA = (64-query tile, q head,
+// sequence), four warps of 16 query rows; key/value tiles of 64 positions
+// are read from the INT8 cache, converted once to fp16 in shared memory
+// (exact) and fed to the MMAs with ldmatrix (K as the col-major B of Q.K^T,
+// V transposed for P.V). The next tile's INT8 bytes are loaded into
+// registers while the current tile is computed.
+constexpr int kPfQTile = 64;
+constexpr int kPfKTile = 64;
+constexpr int kPfStride = 72;  // halves per smem row: 144 B, conflict-free ldmatrix
+
+// four int8 in a word -> two half2 (bytes 0,1 and bytes 2,3), exact:
+// 0x6400 | (b + 128) is the fp16 value 1024 + b + 128.
+TL_DEV void i8x4_to_h2x2(uint32_t w, uint32_t& h01, uint32_t& h23) {
+  const uint32_t u = w ^ 0x80808080u;
+  const uint32_t a = __byte_perm(u, 0x64646464u, 0x5140);
+  const uint32_t b = __byte_perm(u, 0x64646464u, 0x5342);
+  const __half2 bias = __float2half2_rn(1152.0f);
+  __half2 ha = __hsub2(*reinterpret_cast<const __half2*>(&a), bias);
+  __half2 hb = __hsub2(*reinterpret_cast<const __half2*>(&b), bias);
+  h01 = *reinterpret_cast<uint32_t*>(&ha);
+  h23 = *reinterpret_cast<uint32_t*>(&hb);
+}
+
+TL_DEV void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+TL_DEV void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+// D += A . B with all four A registers (rows 0..15 in use)
+TL_DEV void mma16816_full(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__global__ void __launch_bounds__(128) attn_prefill_mma_kernel(
+    const float* __restrict__ qkv, int ld, int seq_len, int H, int Hkv, const int8_t* __restrict__ kc,
+    const int8_t* __restrict__ vc, const float* __restrict__ ks, const float* __restrict__ vs, int slot_base,
+    int layer, int L, int P, float* __restrict__ out, float* __restrict__ out_absmax) {
+  __shared__ __align__(16) __half k_sm[kPfKTile * kPfStride];
+  __shared__ __align__(16) __half v_sm[kPfKTile * kPfStride];
+
+  const int n_qt = gridDim.x;
+  const int qt = n_qt - 1 - static_cast<int>(blockIdx.x);  // longest rows first
+  const int head = blockIdx.y, seq = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, q4 = lane & 3;
+  const int h = head / (H / Hkv);
+  const int Dq = H * 64;
+  const size_t sidx = (static_cast<size_t>(slot_base + seq) * L + layer) * Hkv + h;
+  const float sK = ks[sidx], sV = vs[sidx];
+  const int8_t* kbase = kc + sidx * static_cast<size_t>(P) * 64;
+  const int8_t* vbase = vc + sidx * static_cast<size_t>(P) * 64;
+
+  // ---- this warp's 16 query rows: fp32 -> power-of-two scaled hi/lo fragments
+  const int r0 = qt * kPfQTile + warp * 16 + g;  // rows r0 and r0 + 8
+  float qv[2][16];
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int t = r0 + hr * 8;
+    const float* q = qkv + static_cast<size_t>(seq * seq_len + (t < seq_len ? t : 0)) * ld + head * 64;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const float2 x0 = *reinterpret_cast<const float2*>(q + kk * 16 + q4 * 2);
+      const float2 x1 = *reinterpret_cast<const float2*>(q + kk * 16 + 8 + q4 * 2);
+      const bool ok = t < seq_len;
+      qv[hr][kk * 4 + 0] = ok ? x0.x : 0.0f;
+      qv[hr][kk * 4 + 1] = ok ? x0.y : 0.0f;
+      qv[hr][kk * 4 + 2] = ok ? x1.x : 0.0f;
+      qv[hr][kk * 4 + 3] = ok ? x1.y : 0.0f;
+    }
+  }
+  float qscale[2];
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    float mx = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) mx = fmaxf(mx, fabsf(qv[hr][i]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    qscale[hr] = pow2_scale(mx);
+  }
+  uint32_t qa_hi[4][4], qa_lo[4][4];
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    // a0: row g, k 0..1 | a1: row g+8, k 0..1 | a2: row g, k 8..9 | a3: row g+8, k 8..9
+    split2(qv[0][kk * 4 + 0] * qscale[0], qv[0][kk * 4 + 1] * qscale[0], qa_hi[kk][0], qa_lo[kk][0]);
+    split2(qv[1][kk * 4 + 0] * qscale[1], qv[1][kk * 4 + 1] * qscale[1], qa_hi[kk][1], qa_lo[kk][1]);
+    split2(qv[0][kk * 4 + 2] * qscale[0], qv[0][kk * 4 + 3] * qscale[0], qa_hi[kk][2], qa_lo[kk][2]);
+    split2(qv[1][kk * 4 + 2] * qscale[1], qv[1][kk * 4 + 3] * qscale[1], qa_hi[kk][3], qa_lo[kk][3]);
+  }
+  const float sc0 = sK * 0.125f / qscale[0], sc1 = sK * 0.125f / qscale[1];
+
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.0f, 0.0f};
+  float o[8][4];
+#pragma unroll
+  for (int dt = 0; dt < 8; ++dt) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.0f;
+
+  // ---- key/value tiles 0..qt (the causal frontier of this query tile)
+  const int n_kt = qt + 1;
+  // staging: thread tid moves 16 bytes of K rows and 16 bytes of V rows, twice
+  int4 kreg[2], vreg[2];
+  auto load_tile = [&](int kt) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int c = tid + i * 128;         // 16-byte chunk 0..255
+      const int row = c >> 2, col = c & 3;  // key row in tile, chunk in row
+      const int t = kt * kPfKTile + row;
+      if (t < seq_len) {
+        kreg[i] = __ldg(reinterpret_cast<const int4*>(kbase + static_cast<size_t>(t) * 64) + col);
+        vreg[i] = __ldg(reinterpret_cast<const int4*>(vbase + static_cast<size_t>(t) * 64) + col);
+      } else {
+        kreg[i] = make_int4(0, 0, 0, 0);
+        vreg[i] = make_int4(0, 0, 0, 0);
+      }
+    }
+  };
+  auto store_tile = [&]() {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int c = tid + i * 128;
+      const int row = c >> 2, col = c & 3;
+      uint4 a, b;
+      i8x4_to_h2x2(static_cast<uint32_t>(kreg[i].x), a.x, a.y);
+      i8x4_to_h2x2(static_cast<uint32_t>(kreg[i].y), a.z, a.w);
+      i8x4_to_h2x2(static_cast<uint32_t>(kreg[i].z), b.x, b.y);
+      i8x4_to_h2x2(static_cast<uint32_t>(kreg[i].w), b.z, b.w);
+      uint4* kd = reinterpret_cast<uint4*>(k_sm + row * kPfStride + col * 16);
+      kd[0] = a;
+      kd[1] = b;
+      i8x4_to_h2x2(static_cast<uint32_t>(vreg[i].x), a.x, a.y);
+      i8x4_to_h2x2(static_cast<uint32_t>(vreg[i].y), a.z, a.w);
+      i8x4_to_h2x2(static_cast<uint32_t>(vreg[i].z), b.x, b.y);
+      i8x4_to_h2x2(static_cast<uint32_t>(vreg[i].w), b.z, b.w);
+      uint4* vd = reinterpret_cast<uint4*>(v_sm + row * kPfStride + col * 16);
+      vd[0] = a;
+      vd[1] = b;
+    }
+  };
+
+  const uint32_t k_base = smem_u32_attn(k_sm), v_base = smem_u32_attn(v_sm);
+  // ldmatrix lane addresses (bytes): K, non-transposed: key = nt*8 + (lane&7),
+  // dim = kk*16 + (lane>>3)*8 (matrices: kk lo, kk hi, kk+1 lo, kk+1 hi).
+  const uint32_t k_lane = static_cast<uint32_t>(((lane & 7) * kPfStride + (lane >> 3) * 8) * 2);
+  // V, transposed: key = kk*16 + ((lane>>3)&1)*8 + (lane&7), dim = (dt + (lane>>4))*8.
+  const uint32_t v_lane = static_cast<uint32_t>(((((lane >> 3) & 1) * 8 + (lane & 7)) * kPfStride + (lane >> 4) * 8) * 2);
+
+  load_tile(0);
+  for (int kt = 0; kt < n_kt; ++kt) {
+    __syncthreads();  // previous tile fully consumed
+    store_tile();
+    __syncthreads();
+    if (kt + 1 < n_kt) load_tile(kt + 1);
+
+    // S = Q . K^T for 16 rows x 64 keys
+    float sacc[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
+#pragma unroll
+      for (int kk = 0; kk < 4; kk += 2) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(k_base + k_lane + static_cast<uint32_t>((nt * 8 * kPfStride + kk * 16) * 2), b0, b1, b2, b3);
+        mma16816_full(sacc[nt], qa_hi[kk], b0, b1);
+        mma16816_full(sacc[nt], qa_lo[kk], b0, b1);
+        mma16816_full(sacc[nt], qa_hi[kk + 1], b2, b3);
+        mma16816_full(sacc[nt], qa_lo[kk + 1], b2, b3);
+      }
+    }
+    // scale, causal mask (diagonal tile only), online softmax
+    const bool diag = kt == qt;
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int hr = j >> 1;
+        const int key = kt * kPfKTile + nt * 8 + q4 * 2 + (j & 1);
+        const int qrow = r0 + hr * 8;
+        float v = sacc[nt][j] * (hr ? sc1 : sc0);
+        if (diag && key > qrow) v = -INFINITY;
+        sacc[nt][j] = v;
+        mx[hr] = fmaxf(mx[hr], v);
+      }
+    float corr[2];
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 1));
+      mx[hr] = fmaxf(mx[hr], __shfl_xor_sync(0xffffffffu, mx[hr], 2));
+      const float m_new = fmaxf(m_run[hr], mx[hr]);  // finite: key 0 of a tile <= every row's position
+      corr[hr] = expf(m_run[hr] - m_new);
+      m_run[hr] = m_new;
+      l_run[hr] *= corr[hr];
+    }
+#pragma unroll
+    for (int dt = 0; dt < 8; ++dt) {
+      o[dt][0] *= corr[0];
+      o[dt][1] *= corr[0];
+      o[dt][2] *= corr[1];
+      o[dt][3] *= corr[1];
+    }
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int hr = j >> 1;
+        const float e = expf(sacc[nt][j] - m_run[hr]);
+        sacc[nt][j] = e;
+        l_run[hr] += e;
+      }
+    // O += P . V, P split into hi/lo fp16 (scaled by 2^14)
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t ph[4], pl[4];
+      split2(sacc[2 * kk][0] * kPScale, sacc[2 * kk][1] * kPScale, ph[0], pl[0]);
+      split2(sacc[2 * kk][2] * kPScale, sacc[2 * kk][3] * kPScale, ph[1], pl[1]);
+      split2(sacc[2 * kk + 1][0] * kPScale, sacc[2 * kk + 1][1] * kPScale, ph[2], pl[2]);
+      split2(sacc[2 * kk + 1][2] * kPScale, sacc[2 * kk + 1][3] * kPScale, ph[3], pl[3]);
+#pragma unroll
+      for (int dt = 0; dt < 8; dt += 2) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(v_base + v_lane + static_cast<uint32_t>((kk * 16 * kPfStride + dt * 8) * 2), b0, b1, b2, b3);
+        mma16816_full(o[dt], ph, b0, b1);
+        mma16816_full(o[dt], pl, b0, b1);
+        mma16816_full(o[dt + 1], ph, b2, b3);
+        mma16816_full(o[dt + 1], pl, b2, b3);
+      }
+    }
+  }
+
+  // ---- normalise and store; per-sequence |out| maximum for the next quantize
+  float local_max = 0.0f;
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    float l = l_run[hr];
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    const int t = r0 + hr * 8;
+    if (t >= seq_len) continue;
+    const float inv = sV / (l * kPScale);
+    float* orow = out + static_cast<size_t>(seq * seq_len + t) * Dq + head * 64;
+#pragma unroll
+    for (int dt = 0; dt < 8; ++dt) {
+      const float2 y = make_float2(o[dt][hr * 2] * inv, o[dt][hr * 2 + 1] * inv);
+      *reinterpret_cast<float2*>(orow + dt * 8 + q4 * 2) = y;
+      local_max = fmaxf(local_max, fmaxf(fabsf(y.x), fabsf(y.y)));
+    }
+  }
+  if (out_absmax) {
+    local_max = warp_max(local_max);
+    if (lane == 0) atomic_max_nonneg(out_absmax + seq, local_max);
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_attn_prefill(const float* qkv, int ld, int rows, int seq_len, int H, int Hkv,
+                                const int8_t* kc, const int8_t* vc, const float* ks,
+                                const float* vs, int slot_base, int layer, int L, int P,
+                                float* out, float* out_absmax, cudaStream_t s) {
+  if (seq_len <= 0 || rows % seq_len || H % Hkv || (ld & 1)) return cudaErrorInvalidValue;
+  const int nseq = rows / seq_len;
+  dim3 grid((seq_len + kPfQTile - 1) / kPfQTile, H, nseq);
+  attn_prefill_mma_kernel<<<grid, 128, 0, s>>>(qkv, ld, seq_len, H, Hkv, kc, vc, ks, vs, slot_base, layer,
+                                               L, P, out, out_absmax);
+  return cudaGetLastError();
+}
 
 // Chunk length and CTAs per (row, kv head): batched decode has many rows, so
 // few CTAs per row; a single sequence spreads its context over more CTAs.

@@ -733,131 +733,6 @@ cudaError_t launch_kv_write_prefill(const float* qkv, int ld, int rows, int seq_
   return cudaGetLastError();
 }
 
-// Causal prefill attention on CUDA cores: CTA = (head, 16-query tile, seq),
-// 4 warps x 4 query rows, keys streamed in 64-row chunks through shared memory.
-__global__ void __launch_bounds__(128) attn_prefill_kernel(
-    const float* qkv, int ld, int seq_len, int H, int Hkv, const int8_t* kc, const int8_t* vc,
-    const float* ks, const float* vs, int slot_base, int layer, int L, int P, float* out,
-    float* out_absmax) {
-  constexpr int QT = 16, RPW = 4, CH = 64, KSTRIDE = 68;
-  __shared__ __align__(16) int8_t k_sm[CH * KSTRIDE];
-  __shared__ __align__(16) int8_t v_sm[CH * 64];
-  __shared__ float q_sm[QT][64];
-  __shared__ float p_sm[4][RPW][CH];
-  const int g = blockIdx.x, qt0 = blockIdx.y * QT, seq = blockIdx.z;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int G = H / Hkv, h = g / G;
-  const int Dq = H * 64;
-  const size_t sidx = (static_cast<size_t>(slot_base + seq) * L + layer) * Hkv + h;
-  const float sK = ks[sidx], sV = vs[sidx];
-  const int8_t* kbase = kc + sidx * static_cast<size_t>(P) * 64;
-  const int8_t* vbase = vc + sidx * static_cast<size_t>(P) * 64;
-  for (int i = tid; i < QT * 64; i += 128) {
-    const int qi = i >> 6, d = i & 63;
-    const int t = qt0 + qi;
-    q_sm[qi][d] = t < seq_len ? qkv[static_cast<size_t>(seq * seq_len + t) * ld + g * 64 + d] : 0.0f;
-  }
-  float m_run[RPW], l_run[RPW], acc0[RPW], acc1[RPW];
-#pragma unroll
-  for (int i = 0; i < RPW; ++i) {
-    m_run[i] = -INFINITY;
-    l_run[i] = 0.0f;
-    acc0[i] = 0.0f;
-    acc1[i] = 0.0f;
-  }
-  const float score_scale = sK * 0.125f;
-  const int last_q = min(qt0 + QT, seq_len) - 1;
-  __syncthreads();
-  for (int t0 = 0; t0 <= last_q; t0 += CH) {
-    const int n = min(CH, last_q + 1 - t0);
-    for (int wi = tid; wi < n * 16; wi += 128) {
-      const int r = wi >> 4, c = wi & 15;
-      reinterpret_cast<int*>(k_sm + r * KSTRIDE)[c] =
-          reinterpret_cast<const int*>(kbase + static_cast<size_t>(t0 + r) * 64)[c];
-    }
-    for (int wi = tid; wi < n * 4; wi += 128) {
-      const int r = wi >> 2, c = wi & 3;
-      reinterpret_cast<int4*>(v_sm + r * 64)[c] =
-          reinterpret_cast<const int4*>(vbase + static_cast<size_t>(t0 + r) * 64)[c];
-    }
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < RPW; ++i) {
-      const int qi = warp * RPW + i;
-      const int tq = qt0 + qi;
-      float cmax = -INFINITY;
-      for (int tt = lane; tt < CH; tt += 32) {
-        float s = -INFINITY;
-        if (tt < n && t0 + tt <= tq) {
-          const int* kw = reinterpret_cast<const int*>(k_sm + tt * KSTRIDE);
-          float a = 0.0f;
-#pragma unroll
-          for (int w4 = 0; w4 < 16; ++w4) {
-            const int v = kw[w4];
-            a += static_cast<float>(static_cast<int8_t>(v & 0xff)) * q_sm[qi][4 * w4];
-            a += static_cast<float>(static_cast<int8_t>((v >> 8) & 0xff)) * q_sm[qi][4 * w4 + 1];
-            a += static_cast<float>(static_cast<int8_t>((v >> 16) & 0xff)) * q_sm[qi][4 * w4 + 2];
-            a += static_cast<float>(static_cast<int8_t>((v >> 24) & 0xff)) * q_sm[qi][4 * w4 + 3];
-          }
-          s = a * score_scale;
-        }
-        p_sm[warp][i][tt] = s;
-        cmax = fmaxf(cmax, s);
-      }
-      cmax = warp_max(cmax);
-      if (cmax == -INFINITY) continue;  // no visible key in this chunk (tq < t0)
-      const float m_new = fmaxf(m_run[i], cmax);
-      const float corr = expf(m_run[i] - m_new);
-      l_run[i] *= corr;
-      acc0[i] *= corr;
-      acc1[i] *= corr;
-      __syncwarp();
-      float lsum = 0.0f;
-      for (int tt = lane; tt < CH; tt += 32) {
-        const float e = expf(p_sm[warp][i][tt] - m_new);
-        p_sm[warp][i][tt] = e;
-        lsum += e;
-      }
-      l_run[i] += warp_sum(lsum);
-      m_run[i] = m_new;
-      __syncwarp();
-      for (int tt = 0; tt < n; ++tt) {
-        const float e = p_sm[warp][i][tt];
-        acc0[i] += e * static_cast<float>(v_sm[tt * 64 + lane]);
-        acc1[i] += e * static_cast<float>(v_sm[tt * 64 + lane + 32]);
-      }
-    }
-    __syncthreads();
-  }
-  float local_max = 0.0f;
-#pragma unroll
-  for (int i = 0; i < RPW; ++i) {
-    const int tq = qt0 + warp * RPW + i;
-    if (tq >= seq_len) continue;
-    const float inv = sV / l_run[i];
-    const float o0 = acc0[i] * inv, o1 = acc1[i] * inv;
-    float* o = out + static_cast<size_t>(seq * seq_len + tq) * Dq + g * 64;
-    o[lane] = o0;
-    o[lane + 32] = o1;
-    local_max = fmaxf(local_max, fmaxf(fabsf(o0), fabsf(o1)));
-  }
-  if (out_absmax) {
-    local_max = warp_max(local_max);
-    if (lane == 0) atomic_max_nonneg(out_absmax + seq, local_max);
-  }
-}
-
-cudaError_t launch_attn_prefill(const float* qkv, int ld, int rows, int seq_len, int H, int Hkv,
-                                const int8_t* kc, const int8_t* vc, const float* ks,
-                                const float* vs, int slot_base, int layer, int L, int P,
-                                float* out, float* out_absmax, cudaStream_t s) {
-  const int nseq = rows / seq_len;
-  dim3 grid(H, (seq_len + 15) / 16, nseq);
-  attn_prefill_kernel<<<grid, 128, 0, s>>>(qkv, ld, seq_len, H, Hkv, kc, vc, ks, vs, slot_base,
-                                           layer, L, P, out, out_absmax);
-  return cudaGetLastError();
-}
-
 // ==================================================================== misc
 // dst[n * dst_ld + k] = src[k * N + n]
 __global__ void transpose_i8_kernel(const int8_t* src, int8_t* dst, int K, int N, int dst_ld) {

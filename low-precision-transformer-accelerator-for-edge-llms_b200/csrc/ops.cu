@@ -206,4 +206,21 @@ tl_status tl_attn_decode(const float* qkv, const int32_t* pos, const int32_t* sl
   return st;
 }
 
+tl_status tl_attn_prefill(const float* qkv, int32_t seq_len, int32_t n_seqs, const int8_t* kc, const int8_t* vc,
+                          const float* ks, const float* vs, int32_t slot_base, int32_t layer, int32_t num_layers,
+                          int32_t heads, int32_t kv_heads, int32_t max_positions, float* out,
+                          float* out_absmax, void* stream) {
+  if (!qkv || !kc || !vc || !ks || !vs || !out) return TL_ERR_INVALID_ARGUMENT;
+  if (seq_len <= 0 || n_seqs <= 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads || slot_base < 0 ||
+      layer < 0 || layer >= num_layers || max_positions <= 0)
+    return TL_ERR_INVALID_ARGUMENT;
+  if (seq_len > max_positions) return TL_ERR_OUT_OF_RANGE;
+  if (reinterpret_cast<uintptr_t>(qkv) & 7u || reinterpret_cast<uintptr_t>(out) & 7u ||
+      reinterpret_cast<uintptr_t>(kc) & 15u || reinterpret_cast<uintptr_t>(vc) & 15u)
+    return TL_ERR_INVALID_ARGUMENT;
+  return cu(launch_attn_prefill(qkv, (heads + 2 * kv_heads) * 64, seq_len * n_seqs, seq_len, heads, kv_heads, kc,
+                                vc, ks, vs, slot_base, layer, num_layers, max_positions, out, out_absmax,
+                                static_cast<cudaStream_t>(stream)));
+}
+
 }  // extern "C"

@@ -50,7 +50,7 @@ EXPORTS = (
     "tl_decode_step_kernel_count", "tl_decode_step_kernel_count_rows", "tl_engine_stream", "tl_profile_decode_kernels", "tl_device_error",
     "tl_transpose_i8", "tl_quantize_int8",
     "tl_gemm_i8", "tl_gemm_i8_requant", "tl_quantized_linear", "tl_rmsnorm", "tl_lmhead_argmax",
-    "tl_attn_decode", "tl_lmhead_argmax_noalloc",
+    "tl_attn_decode", "tl_attn_prefill", "tl_lmhead_argmax_noalloc",
 )
 
 
@@ -138,6 +138,7 @@ def load_library(path: Path | str | None = None):
         "tl_rmsnorm": (i32, [vp, vp, C.c_float, vp, i32, i32, vp]),
         "tl_lmhead_argmax": (i32, [vp, vp, C.c_float, vp, vp, i32, i32, i32, vp, vp, vp]),
         "tl_attn_decode": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, vp]),
+        "tl_attn_prefill": (i32, [vp, i32, i32, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, vp, vp]),
         "tl_lmhead_argmax_noalloc": (i32, [vp, vp, C.c_float, vp, vp, i32, i32, i32, vp, vp, vp]),
     }
     for name, (res, args) in sig.items():

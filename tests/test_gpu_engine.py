@@ -127,6 +127,30 @@ def test_batched_tensor_core_path(pkg, gpu):
     eng.close()
 
 
+def test_long_prompts_multi_tile_prefill(pkg, gpu):
+    """Prompts longer than one 64-position attention tile (ragged 150 and 130
+    tokens): prefill logits and layer-0 KV bytes of one sequence, then a
+    two-sequence batch through generate_batch, each against its oracle."""
+    qm = small_model(13, 2)
+    eng = pkg.Engine(qm.cfg, max_batch=2, max_prefill_tokens=2 * 150)
+    eng.load(to_engine_model(pkg, qm))
+    rng = np.random.default_rng(14)
+    prompt = list(rng.integers(0, qm.cfg["vocab_size"], 150))
+    lg = eng.prefill_logits(prompt)
+    ora = KVGolden(qm, kv="int8")
+    ref = ora.prefill(prompt)
+    assert rel_err(lg, ref) <= FP_RTOL, rel_err(lg, ref)
+    k, v, _, _ = eng.read_kv(0, len(prompt))
+    np.testing.assert_array_equal(k, ora.k_cache[0, :, :len(prompt)])
+    np.testing.assert_array_equal(v, ora.v_cache[0, :, :len(prompt)])
+    prompts = rng.integers(0, qm.cfg["vocab_size"], (2, 130)).astype(np.uint32)
+    outs, sts = eng.generate_batch(prompts, 4)
+    for i in range(2):
+        ref_t, ref_logits, _ = oracle_generate(qm, list(prompts[i]), 4)
+        assert tokens_match_modulo_ties(outs[i], ref_t, ref_logits), (i, outs[i], ref_t)
+    eng.close()
+
+
 def test_stop_contract(small):
     qm, eng = small
     prompt = list(np.random.default_rng(6).integers(0, qm.cfg["vocab_size"], 5))

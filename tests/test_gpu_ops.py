@@ -269,3 +269,37 @@ def test_attn_decode_matches_reference(pkg, lib, rows, H, Hkv, positions):
     assert err < 2e-6, err
     np.testing.assert_array_equal(dkc.cpu().numpy(), kref)
     np.testing.assert_array_equal(dvc.cpu().numpy(), vref)
+
+
+@pytest.mark.parametrize("n_seqs,S,H,Hkv", [(1, 1, 32, 4), (2, 63, 4, 2), (1, 64, 32, 4), (2, 65, 32, 4),
+                                            (3, 200, 4, 2), (1, 2048, 32, 4)])
+def test_attn_prefill_matches_reference(pkg, lib, n_seqs, S, H, Hkv):
+    """Causal prefill attention over the INT8 cache vs the oracle's attention
+    core (float64 scores) on dequantized cache rows."""
+    rng = np.random.default_rng(S * 7 + n_seqs + H)
+    L, P, layer, slot_base = 2, 2048, 1, 1
+    slots = slot_base + n_seqs
+    kc = rng.integers(-127, 128, (slots, L, Hkv, P, 64), dtype=np.int8)
+    vc = rng.integers(-127, 128, (slots, L, Hkv, P, 64), dtype=np.int8)
+    ks = rng.uniform(0.005, 0.03, (slots, L, Hkv)).astype(np.float32)
+    vs = rng.uniform(0.005, 0.03, (slots, L, Hkv)).astype(np.float32)
+    qkv = (rng.standard_normal((n_seqs * S, (H + 2 * Hkv) * 64)) * 2.0).astype(np.float32)
+    ref = np.zeros((n_seqs * S, H * 64), np.float32)
+    for i in range(n_seqs):
+        sl = slot_base + i
+        q = G.split_heads(qkv[i * S:(i + 1) * S, :H * 64], H, 64)
+        kd = kc[sl, layer, :, :S].astype(np.float32) * ks[sl, layer][:, None, None]
+        vd = vc[sl, layer, :, :S].astype(np.float32) * vs[sl, layer][:, None, None]
+        ref[i * S:(i + 1) * S] = G.attention_core(q, kd, vd, H // Hkv, np.float64(0.125), True)
+    out = torch.empty((n_seqs * S, H * 64), dtype=torch.float32, device="cuda")
+    amax = torch.zeros(n_seqs, dtype=torch.float32, device="cuda")
+    pkg.shim.check(lib.tl_attn_prefill(dev(qkv).data_ptr(), S, n_seqs, dev(kc).data_ptr(), dev(vc).data_ptr(),
+                                       dev(ks).data_ptr(), dev(vs).data_ptr(), slot_base, layer, L, H, Hkv, P,
+                                       out.data_ptr(), amax.data_ptr(), stream()), "attn_prefill")
+    got = out.cpu().numpy()
+    err = np.max(np.abs(got - ref)) / np.max(np.abs(ref))
+    # fp32-level: one warp's fp32 accumulator carries the online softmax over
+    # up to 2048 keys (32 rescales); measured 5.9e-6 at S = 2048
+    assert err < 1e-5, err
+    per_seq = np.abs(got).reshape(n_seqs, -1).max(axis=1)
+    np.testing.assert_array_equal(amax.cpu().numpy(), per_seq)
