@@ -8,20 +8,19 @@
 // are quantized with the frozen per-(layer, kv head) scales and appended in
 // place (rtl/memory/kv_cache_manager.sv:43-47 layout).
 //
-// Mapping: a fixed number of CTAs per (kv head, sequence), each looping over
-// its share of TS-position context chunks, four warps. Each warp runs flash-attention tiles of 16 positions with
-// mma.sync m16n8k16 fp16: A = the group's query rows (8 heads, padded to 16)
-// for Q.K^T and the probabilities for P.V; B = INT8 K / V rows converted to
-// fp16, which is exact for |v| <= 127. To keep fp32-level accuracy the fp32
-// Q and P operands are split into fp16 hi + lo halves (two MMAs each, ~22
-// mantissa bits). Each query row is first scaled by a power of two that puts
-// its largest element in [2^13, 2^14) and the probabilities by 2^14, so the
-// lo halves stay in fp16's normal range; the scales are exact and undone on
-// the fp32 accumulators. (INT8 re-quantization of the attention output makes
-// float error visible as rounding flips, so attention has to be as accurate
-// as fp32 arithmetic.) Warps merge in shared memory; splits merge via a
-// per-(sequence, kv head) partial buffer, the last CTA to arrive (atomic
-// ticket) producing the output. CTAs with no chunk exit at once.
+// Decode maps one CTA to (kv head, row, context split) with eight warps that
+// stream 32-position chunks through bulk async copies; prefill maps one CTA
+// to (64-query tile, q head, sequence). Both run flash-attention tiles on
+// mma.sync m16n8k16 fp16 with fp32 accumulation: INT8 K / V values convert
+// to fp16 exactly (|v| <= 127), and to keep fp32-level accuracy the fp32 Q
+// and P operands are split into fp16 hi + lo halves (~22 mantissa bits).
+// Each query row is first scaled by a power of two that puts its largest
+// element in [2^13, 2^14) and the probabilities by 2^14, so the lo halves
+// stay in fp16's normal range; the scales are exact and undone on the fp32
+// accumulators. (INT8 re-quantization of the attention output makes float
+// error visible as rounding flips, so attention has to be as accurate as
+// fp32 arithmetic.) Decode splits merge via a per-(row, kv head) partial
+// buffer, the last CTA to arrive (atomic ticket) producing the output.
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -33,11 +32,6 @@
 namespace tl {
 
 namespace {
-
-constexpr int kAttnThreads = 128;
-constexpr int kAttnWarps = kAttnThreads / 32;
-constexpr int kKStride = 80;   // bytes per cached K row in smem (conflict-free B loads)
-constexpr int kVStride = 72;   // bytes per cached V row in smem
 
 // two floats -> packed fp16x2, first argument in the low half
 TL_DEV uint32_t pack2(float lo, float hi) {
@@ -63,259 +57,6 @@ TL_DEV float pow2_scale(float amax) {
 }
 TL_DEV uint32_t smem_u32_attn(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 constexpr float kPScale = 16384.0f;  // probabilities in [0, 1] -> [0, 2^14]
-TL_DEV uint32_t pack_i8(int8_t a, int8_t b) {
-  return pack2(static_cast<float>(a), static_cast<float>(b));
-}
-
-// D += A . B, m16n8k16, fp16 in, fp32 accumulate. a1/a3 (rows 8..15) are 0.
-TL_DEV void mma16816(float* d, uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
-}
-
-template <int TS>
-__global__ void __launch_bounds__(kAttnThreads) attn_decode_mma_kernel(AttnDecodeArgs a) {
-  __shared__ __align__(16) int8_t k_sm[TS * kKStride];
-  __shared__ __align__(16) int8_t v_sm[TS * kVStride];
-  __shared__ float q_sm[8][64];
-  __shared__ float q_scale[8];
-  __shared__ float comb[kAttnWarps][8][66];
-  __shared__ int last_cta;
-
-  const int h = blockIdx.x, m = blockIdx.y, sp = blockIdx.z;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int G = a.H / a.Hkv;
-  const int Dq = a.H * 64;
-  pdl_wait();
-  const int p = a.pos[m];
-  const bool valid_row = p >= 0 && p < a.P;
-  if (!valid_row) {
-    if (sp == 0)
-      for (int i = tid; i < G * 64; i += kAttnThreads) a.out[static_cast<size_t>(m) * Dq + h * G * 64 + i] = 0.0f;
-    return;
-  }
-  const int T = p + 1;
-  const int nz = gridDim.z;
-  const int n_chunks = (T + TS - 1) / TS;
-  if (sp >= n_chunks) return;  // no work for this CTA (not counted in the merge)
-  const int n_act = min(nz, n_chunks);
-  const int slot = a.slot[m];
-  const bool act = a.active ? (a.active[m] != 0) : true;
-  const size_t sidx = (static_cast<size_t>(slot) * a.L + a.layer) * a.Hkv + h;
-  const float sK = a.ks[sidx], sV = a.vs[sidx];
-  int8_t* kbase = a.kc + sidx * static_cast<size_t>(a.P) * 64;
-  int8_t* vbase = a.vc + sidx * static_cast<size_t>(a.P) * 64;
-  const float* row = a.qkv + static_cast<size_t>(m) * a.ld;
-  const float* cs = a.cos + static_cast<size_t>(p) * 64;
-  const float* sn = a.sin + static_cast<size_t>(p) * 64;
-
-  // ---- rotated queries of the group (rows >= G stay zero), power-of-two scaled
-  for (int g = warp; g < 8; g += kAttnWarps) {
-    float r0 = 0.0f, r1 = 0.0f;
-    if (g < G) {
-      const float* qr = row + (h * G + g) * 64;
-      const float q0 = qr[lane], q1 = qr[lane + 32];
-      r0 = __fadd_rn(__fmul_rn(q0, cs[lane]), __fmul_rn(-q1, sn[lane]));
-      r1 = __fadd_rn(__fmul_rn(q1, cs[lane + 32]), __fmul_rn(q0, sn[lane + 32]));
-    }
-    const float qs = pow2_scale(warp_max(fmaxf(fabsf(r0), fabsf(r1))));
-    q_sm[g][lane] = r0 * qs;
-    q_sm[g][lane + 32] = r1 * qs;
-    if (lane == 0) q_scale[g] = qs;
-  }
-  __syncthreads();
-
-  // ---- Q fragments (hi/lo) for the four 16-wide k steps over head_dim
-  const int g = lane >> 2, q4 = lane & 3;
-  uint32_t qa_hi[4][2], qa_lo[4][2];
-#pragma unroll
-  for (int ks = 0; ks < 4; ++ks) {
-    const int c = ks * 16 + q4 * 2;
-    split2(q_sm[g][c], q_sm[g][c + 1], qa_hi[ks][0], qa_lo[ks][0]);
-    split2(q_sm[g][c + 8], q_sm[g][c + 9], qa_hi[ks][1], qa_lo[ks][1]);
-  }
-  // undo the exact power-of-two query scale of this thread's row g
-  const float score_scale = sK * 0.125f / q_scale[g];
-  float m_run = -INFINITY, l_part = 0.0f;
-  float o[8][4];
-#pragma unroll
-  for (int dt = 0; dt < 8; ++dt) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.0f;
-
-  // This CTA owns chunks sp, sp + nz, ... of TS positions; the online
-  // softmax state of each warp carries across them.
-  for (int chunk = sp; chunk < n_chunks; chunk += nz) {
-    const int t_begin = chunk * TS;
-    const int n = min(TS, T - t_begin);
-    __syncthreads();  // previous chunk fully consumed
-    for (int i = tid; i < TS * 4; i += kAttnThreads) {
-      const int r = i >> 2, c = i & 3;
-      int4 v = make_int4(0, 0, 0, 0);
-      if (r < n) v = reinterpret_cast<const int4*>(kbase + static_cast<size_t>(t_begin + r) * 64)[c];
-      *reinterpret_cast<int4*>(k_sm + r * kKStride + c * 16) = v;
-    }
-    for (int i = tid; i < TS * 8; i += kAttnThreads) {
-      const int r = i >> 3, c = i & 7;
-      uint2 v = make_uint2(0u, 0u);
-      if (r < n) v = reinterpret_cast<const uint2*>(vbase + static_cast<size_t>(t_begin + r) * 64)[c];
-      *reinterpret_cast<uint2*>(v_sm + r * kVStride + c * 8) = v;
-    }
-    __syncthreads();
-    // the new position's K (RoPE) and V: quantize, append, and use
-    if (warp == 0 && p >= t_begin && p < t_begin + n) {
-      const float* kr = row + Dq + h * 64;
-      const float* vr = row + Dq + a.Hkv * 64 + h * 64;
-      const float k0 = kr[lane], k1 = kr[lane + 32];
-      const float r0 = __fadd_rn(__fmul_rn(k0, cs[lane]), __fmul_rn(-k1, sn[lane]));
-      const float r1 = __fadd_rn(__fmul_rn(k1, cs[lane + 32]), __fmul_rn(k0, sn[lane + 32]));
-      const int8_t qk0 = static_cast<int8_t>(quantize_one(r0, sK)), qk1 = static_cast<int8_t>(quantize_one(r1, sK));
-      const int8_t qv0 = static_cast<int8_t>(quantize_one(vr[lane], sV));
-      const int8_t qv1 = static_cast<int8_t>(quantize_one(vr[lane + 32], sV));
-      const int rl = p - t_begin;
-      k_sm[rl * kKStride + lane] = qk0;
-      k_sm[rl * kKStride + lane + 32] = qk1;
-      v_sm[rl * kVStride + lane] = qv0;
-      v_sm[rl * kVStride + lane + 32] = qv1;
-      if (act) {
-        kbase[static_cast<size_t>(p) * 64 + lane] = qk0;
-        kbase[static_cast<size_t>(p) * 64 + lane + 32] = qk1;
-        vbase[static_cast<size_t>(p) * 64 + lane] = qv0;
-        vbase[static_cast<size_t>(p) * 64 + lane + 32] = qv1;
-      }
-    }
-    __syncthreads();
-
-    for (int t0 = warp * 16; t0 < n; t0 += kAttnWarps * 16) {
-      float s[2][4];
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
-        const int8_t* kr = k_sm + (t0 + nt * 8 + g) * kKStride + q4 * 2;
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          const uint32_t b0 = pack_i8(kr[ks * 16], kr[ks * 16 + 1]);
-          const uint32_t b1 = pack_i8(kr[ks * 16 + 8], kr[ks * 16 + 9]);
-          mma16816(s[nt], qa_hi[ks][0], qa_hi[ks][1], b0, b1);
-          mma16816(s[nt], qa_lo[ks][0], qa_lo[ks][1], b0, b1);
-        }
-      }
-      float v4[4];
-      float mx = -INFINITY;
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int tl = t0 + nt * 8 + q4 * 2 + j;
-          const float val = tl < n ? s[nt][j] * score_scale : -INFINITY;
-          v4[nt * 2 + j] = val;
-          mx = fmaxf(mx, val);
-        }
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      const float m_new = fmaxf(m_run, mx);
-      const float corr = expf(m_run - m_new);
-      float pv[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) pv[j] = expf(v4[j] - m_new);
-      l_part = l_part * corr + (pv[0] + pv[1] + pv[2] + pv[3]);
-#pragma unroll
-      for (int dt = 0; dt < 8; ++dt) {
-        o[dt][0] *= corr;
-        o[dt][1] *= corr;
-      }
-      m_run = m_new;
-      uint32_t pa_hi0, pa_lo0, pa_hi2, pa_lo2;
-      split2(pv[0] * kPScale, pv[1] * kPScale, pa_hi0, pa_lo0);
-      split2(pv[2] * kPScale, pv[3] * kPScale, pa_hi2, pa_lo2);
-      const int8_t* vr = v_sm + (t0 + q4 * 2) * kVStride + g;
-#pragma unroll
-      for (int dt = 0; dt < 8; ++dt) {
-        const int8_t* vc = vr + dt * 8;
-        const uint32_t b0 = pack_i8(vc[0], vc[kVStride]);
-        const uint32_t b1 = pack_i8(vc[8 * kVStride], vc[9 * kVStride]);
-        mma16816(o[dt], pa_hi0, pa_hi2, b0, b1);
-        mma16816(o[dt], pa_lo0, pa_lo2, b0, b1);
-      }
-    }
-  }
-  pdl_launch_dependents();
-
-  // ---- merge the four warps of this CTA
-  float l_row = l_part;
-  l_row += __shfl_xor_sync(0xffffffffu, l_row, 1);
-  l_row += __shfl_xor_sync(0xffffffffu, l_row, 2);
-  if (q4 == 0) {
-    comb[warp][g][0] = m_run;
-    comb[warp][g][1] = l_row;
-  }
-#pragma unroll
-  for (int dt = 0; dt < 8; ++dt) {
-    comb[warp][g][2 + dt * 8 + q4 * 2] = o[dt][0] * (1.0f / kPScale);
-    comb[warp][g][2 + dt * 8 + q4 * 2 + 1] = o[dt][1] * (1.0f / kPScale);
-  }
-  __syncthreads();
-  float* part = a.part + (static_cast<size_t>(m) * a.Hkv + h) * a.splits * kAttnPartStride +
-                static_cast<size_t>(sp) * kAttnPartStride;
-  for (int i = tid; i < G * 64; i += kAttnThreads) {
-    const int gg = i >> 6, d = i & 63;
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, comb[w][gg][0]);
-    float L = 0.0f, O = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) {
-      const float f = comb[w][gg][0] == -INFINITY ? 0.0f : expf(comb[w][gg][0] - M);
-      L += comb[w][gg][1] * f;
-      O += comb[w][gg][2 + d] * f;
-    }
-    part[gg * 66 + 2 + d] = O;
-    if (d == 0) {
-      part[gg * 66] = M;
-      part[gg * 66 + 1] = L;
-    }
-  }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const unsigned prev = atomicAdd(a.counters + static_cast<size_t>(m) * a.Hkv + h, 1u);
-    last_cta = prev == static_cast<unsigned>(n_act - 1);
-  }
-  __syncthreads();
-  if (!last_cta) return;
-  __threadfence();
-  // ---- merge the splits (only the last CTA of this (sequence, kv head))
-  const float* pall = a.part + (static_cast<size_t>(m) * a.Hkv + h) * a.splits * kAttnPartStride;
-  for (int i = tid; i < G * 64; i += kAttnThreads) {
-    const int gg = i >> 6, d = i & 63;
-    float M = -INFINITY;
-    for (int s2 = 0; s2 < n_act; ++s2)
-      M = fmaxf(M, *reinterpret_cast<const volatile float*>(pall + s2 * kAttnPartStride + gg * 66));
-    float L = 0.0f, O = 0.0f;
-    for (int s2 = 0; s2 < n_act; ++s2) {
-      const volatile float* ps = pall + s2 * kAttnPartStride + gg * 66;
-      const float f = expf(ps[0] - M);
-      L += ps[1] * f;
-      O += ps[2 + d] * f;
-    }
-    a.out[static_cast<size_t>(m) * Dq + (h * G + gg) * 64 + d] = O / L * sV;
-  }
-  if (tid == 0) a.counters[static_cast<size_t>(m) * a.Hkv + h] = 0u;
-}
-
-// ------------------------------------------------------------------ prefill
-// Causal prefill attention, flash-attention style on mma.sync m16n8k16 fp16
-// with the same hi/lo operand split as decode. CTA = (64-query tile, q head,
-// sequence), four warps of 16 query rows; key/value tiles of 64 positions
-// are read from the INT8 cache, converted once to fp16 in shared memory
-// (exact) and fed to the MMAs with ldmatrix (K as the col-major B of Q.K^T,
-// V transposed for P.V). The next tile's INT8 bytes are loaded into
-// registers while the current tile is computed.
-constexpr int kPfQTile = 64;
-constexpr int kPfKTile = 64;
-constexpr int kPfStride = 72;  // halves per smem row: 144 B, conflict-free ldmatrix
-
 // four int8 in a word -> two half2 (bytes 0,1 and bytes 2,3), exact:
 // 0x6400 | (b + 128) is the fp16 value 1024 + b + 128.
 TL_DEV void i8x4_to_h2x2(uint32_t w, uint32_t& h01, uint32_t& h23) {
@@ -347,6 +88,425 @@ TL_DEV void mma16816_full(float* d, const uint32_t* a, uint32_t b0, uint32_t b1)
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+
+// D += A . B, m16n8k32, s8 in, s32 accumulate
+TL_DEV void mma16832_s8(int* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// 2^x on the special-function unit (flushes subnormal results to zero)
+TL_DEV float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// signed 8-bit digit of x in [-128, 127]: x = digit + 256 * rest
+TL_DEV int low_digit(int x) { return ((x + 128) & 255) - 128; }
+TL_DEV uint32_t pack_s8x4(int a, int b, int c, int d) {
+  return (static_cast<uint32_t>(a) & 0xffu) | ((static_cast<uint32_t>(b) & 0xffu) << 8) |
+         ((static_cast<uint32_t>(c) & 0xffu) << 16) | ((static_cast<uint32_t>(d) & 0xffu) << 24);
+}
+constexpr float kLog2e = 1.4426950408889634f;
+
+// ------------------------------------------------------------------- decode
+// One CTA per (kv head, row, split) with eight warps. The split's context is
+// cut into 32-position chunks; warp w takes chunks w, w+8, ... and streams
+// them through its own two ring slots (K 2 KB + V 2 KB each) with bulk async
+// copies (cp.async.bulk, completion on a per-slot mbarrier), so every warp
+// has its next chunk in flight while it computes the current one and no
+// CTA-wide barrier sits in the loop. The position being decoded is not in
+// the cache yet: its warp quantizes the rotated K and the V of this step,
+// writes them to its slot and (for running rows) to the cache.
+//
+// Q.K^T runs on the INT8 MMA (m16n8k32, s32 accumulate) straight from the
+// cache bytes: each rotated query row is scaled by a power of two into
+// [2^21, 2^22), rounded to an integer (error <= 2^-22 of the row maximum)
+// and split into three signed 8-bit digits, x = d0 + 256 d1 + 65536 d2.
+// Rows 0..7 of the first MMA carry d2 of the group's eight heads and rows
+// 8..15 carry d1; the second MMA carries d0 in rows 0..7. The exact INT32
+// digit dot products are combined in fp32. P.V uses fp16 (m16n8k16): P hi
+// halves in rows 0..7, lo halves in rows 8..15, INT8 V converted to fp16
+// exactly. The softmax runs in base 2 (scores pre-multiplied by log2 e,
+// ex2.approx). Head-dim and value-dim indices are permuted consistently on
+// both operands so that every B fragment comes from one 16-byte (K) or
+// 8-byte (V) shared load: thread (g, q4) reads K row g at bytes
+// [16 q4, 16 q4 + 16) and V rows at bytes [8 g, 8 g + 8); output column n of
+// value tile dt is dimension 8 n + dt.
+constexpr int kDecThreads = 256;
+constexpr int kDecWarps = kDecThreads / 32;
+constexpr int kDecChunk = 32;                     // positions per chunk
+constexpr int kDecHalf = kDecChunk * 64;          // bytes of K (or V) per chunk
+constexpr int kDecSlot = 2 * kDecHalf;            // K then V
+constexpr int kDecRing = kDecWarps * 2 * kDecSlot;  // two slots per warp
+constexpr size_t kDecSmem = kDecRing + 8 * 64 * 4 + 8 * 4 + 2 * kDecWarps * 8 + 16;
+constexpr long long kDecWaitCycles = 4000000000ll;  // ~2 s at 1.9 GHz
+
+__device__ unsigned int g_attn_error = 0;
+
+TL_DEV void dec_mbar_init(uint64_t* bar) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32_attn(bar)));
+}
+TL_DEV void dec_mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32_attn(bar)) : "memory");
+}
+TL_DEV void dec_mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32_attn(bar)), "r"(bytes)
+               : "memory");
+}
+// Bounded wait on a slot's phase: false (and g_attn_error set) on expiry.
+TL_DEV bool dec_mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = smem_u32_attn(bar);
+  const long long t0 = clock64();
+  while (true) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if (clock64() - t0 > kDecWaitCycles) {
+      atomicCAS(&g_attn_error, 0u, 4u);
+      return false;
+    }
+  }
+}
+TL_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32_attn(dst)), "l"(src), "r"(bytes), "r"(smem_u32_attn(bar))
+      : "memory");
+}
+
+// chunks [0, n_chunks) split into `nz` contiguous ranges of `per` chunks
+TL_DEV void dec_ranges(int n_chunks, int nz, int& per, int& n_act) {
+  per = (n_chunks + nz - 1) / nz;
+  n_act = (n_chunks + per - 1) / per;
+}
+
+__global__ void __launch_bounds__(kDecThreads, 2) attn_decode_kernel(AttnDecodeArgs a) {
+  extern __shared__ __align__(128) unsigned char dsm[];
+  unsigned char* ring = dsm;
+  float* q_sm = reinterpret_cast<float*>(dsm + kDecRing);   // [8][64]
+  float* q_scale = q_sm + 8 * 64;                           // [8]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(q_scale + 8);  // [warps][2]
+  int* last_cta = reinterpret_cast<int*>(bars + 2 * kDecWarps);
+  float* comb = reinterpret_cast<float*>(ring);  // [warps][8][66], after the chunk loop
+
+  const int h = blockIdx.x, m = blockIdx.y, sp = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, q4 = lane & 3;
+  const int G = a.H / a.Hkv;
+  const int Dq = a.H * 64;
+  pdl_wait();
+  const int p = a.pos[m];
+  if (p < 0 || p >= a.P) {
+    if (sp == 0)
+      for (int i = tid; i < G * 64; i += kDecThreads) a.out[static_cast<size_t>(m) * Dq + h * G * 64 + i] = 0.0f;
+    return;
+  }
+  const int T = p + 1;
+  const int n_chunks = (T + kDecChunk - 1) / kDecChunk;
+  int per, n_act;
+  dec_ranges(n_chunks, static_cast<int>(gridDim.z), per, n_act);
+  if (sp >= n_act) return;  // no chunk for this CTA (not counted in the merge)
+  const int c_begin = sp * per, c_end = min(c_begin + per, n_chunks);
+  const int slot = a.slot[m];
+  const bool act = a.active ? (a.active[m] != 0) : true;
+  const size_t sidx = (static_cast<size_t>(slot) * a.L + a.layer) * a.Hkv + h;
+  const float sK = a.ks[sidx], sV = a.vs[sidx];
+  int8_t* kbase = a.kc + sidx * static_cast<size_t>(a.P) * 64;
+  int8_t* vbase = a.vc + sidx * static_cast<size_t>(a.P) * 64;
+  const float* row = a.qkv + static_cast<size_t>(m) * a.ld;
+  const float* cs = a.cos + static_cast<size_t>(p) * 64;
+  const float* sn = a.sin + static_cast<size_t>(p) * 64;
+
+  if (tid == 0) {
+    for (int i = 0; i < 2 * kDecWarps; ++i) dec_mbar_init(bars + i);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  // ---- rotated queries of the group, one head per warp, power-of-two scaled
+  {
+    const int gg = warp;
+    float r0 = 0.0f, r1 = 0.0f;
+    if (gg < G) {
+      const float* qr = row + (h * G + gg) * 64;
+      const float q0 = qr[lane], q1 = qr[lane + 32];
+      r0 = __fadd_rn(__fmul_rn(q0, cs[lane]), __fmul_rn(-q1, sn[lane]));
+      r1 = __fadd_rn(__fmul_rn(q1, cs[lane + 32]), __fmul_rn(q0, sn[lane + 32]));
+    }
+    // power of two taking max |q| into [2^21, 2^22): 22-bit integer queries
+    const float qs = pow2_scale(warp_max(fmaxf(fabsf(r0), fabsf(r1)))) * 256.0f;
+    q_sm[gg * 64 + lane] = rintf(r0 * qs);
+    q_sm[gg * 64 + lane + 32] = rintf(r1 * qs);
+    if (lane == 0) q_scale[gg] = qs;
+  }
+  __syncthreads();
+
+  // ---- this warp's chunks and their bulk copies
+  uint64_t* wbar = bars + 2 * warp;
+  unsigned char* wslot = ring + warp * 2 * kDecSlot;
+  const int first = c_begin + warp;
+  const int nmine = first < c_end ? (c_end - first + kDecWarps - 1) / kDecWarps : 0;
+  // Copies positions [t0, t0 + rows) of K and V, rows excluding position p
+  // (written by the warp itself); a copy of nothing still completes the phase.
+  auto issue = [&](int c, int s) {
+    const int t0 = c * kDecChunk;
+    const int rows = min(kDecChunk, T - t0) - ((p >= t0 && p < t0 + kDecChunk) ? 1 : 0);
+    uint64_t* bar = wbar + s;
+    unsigned char* dst = wslot + s * kDecSlot;
+    if (rows > 0) {
+      const uint32_t bytes = static_cast<uint32_t>(rows) * 64u;
+      dec_mbar_expect_tx(bar, 2 * bytes);
+      bulk_g2s(dst, kbase + static_cast<size_t>(t0) * 64, bytes, bar);
+      bulk_g2s(dst + kDecHalf, vbase + static_cast<size_t>(t0) * 64, bytes, bar);
+    } else {
+      dec_mbar_arrive(bar);
+    }
+  };
+  if (lane == 0)
+    for (int i = 0; i < min(2, nmine); ++i) issue(first + i * kDecWarps, i);
+
+  // ---- Q digit fragments. k-step ks (32 of the 64 head dims) of thread q4:
+  // k 4 q4 + {0..3} <-> dims 16 q4 + 8 ks + {0..3}, k 16 + 4 q4 + {0..3} <->
+  // dims 16 q4 + 8 ks + {4..7}. qa2: rows 0..7 d2, rows 8..15 d1; qa0: d0.
+  uint32_t qa2[2][4], qa0[2][4];
+#pragma unroll
+  for (int ks = 0; ks < 2; ++ks)
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const float* qr = q_sm + g * 64 + q4 * 16 + ks * 8 + half * 4;
+      int d0[4], d1[4], d2[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int x = static_cast<int>(qr[j]);
+        d0[j] = low_digit(x);
+        const int x1 = (x - d0[j]) >> 8;
+        d1[j] = low_digit(x1);
+        d2[j] = (x1 - d1[j]) >> 8;
+      }
+      qa2[ks][half * 2] = pack_s8x4(d2[0], d2[1], d2[2], d2[3]);
+      qa2[ks][half * 2 + 1] = pack_s8x4(d1[0], d1[1], d1[2], d1[3]);
+      qa0[ks][half * 2] = pack_s8x4(d0[0], d0[1], d0[2], d0[3]);
+      qa0[ks][half * 2 + 1] = 0u;
+    }
+  // scores in base 2: dot * sK / 8 * log2(e), the query scale undone exactly
+  const float score_scale = sK * 0.125f * kLog2e / q_scale[g];
+  float m_run = -INFINITY, l_part = 0.0f;
+  float o[8][4];
+#pragma unroll
+  for (int dt = 0; dt < 8; ++dt) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.0f;
+
+  bool ok = true;
+  for (int i = 0; i < nmine && ok; ++i) {
+    const int c = first + i * kDecWarps, s = i & 1;
+    const int t0 = c * kDecChunk;
+    const int n = min(kDecChunk, T - t0);
+    ok = dec_mbar_wait(wbar + s, (i >> 1) & 1);
+    if (!ok) break;
+    unsigned char* ksm = wslot + s * kDecSlot;
+    unsigned char* vsm = ksm + kDecHalf;
+    if (p >= t0 && p < t0 + kDecChunk) {
+      // the new position: RoPE(K), quantize K and V with the frozen scales
+      const float* kr = row + Dq + h * 64;
+      const float* vr = row + Dq + a.Hkv * 64 + h * 64;
+      const float k0 = kr[lane], k1 = kr[lane + 32];
+      const float r0 = __fadd_rn(__fmul_rn(k0, cs[lane]), __fmul_rn(-k1, sn[lane]));
+      const float r1 = __fadd_rn(__fmul_rn(k1, cs[lane + 32]), __fmul_rn(k0, sn[lane + 32]));
+      const int8_t qk0 = static_cast<int8_t>(quantize_one(r0, sK)), qk1 = static_cast<int8_t>(quantize_one(r1, sK));
+      const int8_t qv0 = static_cast<int8_t>(quantize_one(vr[lane], sV));
+      const int8_t qv1 = static_cast<int8_t>(quantize_one(vr[lane + 32], sV));
+      const int rl = p - t0;
+      ksm[rl * 64 + lane] = static_cast<unsigned char>(qk0);
+      ksm[rl * 64 + lane + 32] = static_cast<unsigned char>(qk1);
+      vsm[rl * 64 + lane] = static_cast<unsigned char>(qv0);
+      vsm[rl * 64 + lane + 32] = static_cast<unsigned char>(qv1);
+      if (act) {
+        kbase[static_cast<size_t>(p) * 64 + lane] = qk0;
+        kbase[static_cast<size_t>(p) * 64 + lane + 32] = qk1;
+        vbase[static_cast<size_t>(p) * 64 + lane] = qv0;
+        vbase[static_cast<size_t>(p) * 64 + lane + 32] = qv1;
+      }
+      __syncwarp();
+    }
+    // S = Q.K^T: 4 key tiles of 8
+    float sc[4][2];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      int a21[4] = {0, 0, 0, 0}, a0[4] = {0, 0, 0, 0};
+      const uint4 kw = *reinterpret_cast<const uint4*>(ksm + (nt * 8 + g) * 64 + q4 * 16);
+      mma16832_s8(a21, qa2[0], kw.x, kw.y);
+      mma16832_s8(a0, qa0[0], kw.x, kw.y);
+      mma16832_s8(a21, qa2[1], kw.z, kw.w);
+      mma16832_s8(a0, qa0[1], kw.z, kw.w);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int kl = nt * 8 + q4 * 2 + j;
+        const float dot = fmaf(static_cast<float>(a21[j]), 65536.0f,
+                               fmaf(static_cast<float>(a21[j + 2]), 256.0f, static_cast<float>(a0[j])));
+        const float v = kl < n ? dot * score_scale : -INFINITY;
+        sc[nt][j] = v;
+        mx = fmaxf(mx, v);
+      }
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float m_new = fmaxf(m_run, mx);  // finite: position t0 < T is always valid
+    const float corr = ex2f(m_run - m_new);
+    m_run = m_new;
+    float psum = 0.0f;
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        sc[nt][j] = ex2f(sc[nt][j] - m_new);
+        psum += sc[nt][j];
+      }
+    l_part = l_part * corr + psum;
+    if (__any_sync(0xffffffffu, corr != 1.0f)) {
+#pragma unroll
+      for (int dt = 0; dt < 8; ++dt) {
+        o[dt][0] *= corr;
+        o[dt][1] *= corr;
+        o[dt][2] *= corr;
+        o[dt][3] *= corr;
+      }
+    }
+    // O += P.V over two 16-key steps
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      uint32_t pa[4];
+      split2(sc[2 * kk][0] * kPScale, sc[2 * kk][1] * kPScale, pa[0], pa[1]);
+      split2(sc[2 * kk + 1][0] * kPScale, sc[2 * kk + 1][1] * kPScale, pa[2], pa[3]);
+      const int ra = kk * 16 + q4 * 2;  // keys ra, ra+1 (b0) and ra+8, ra+9 (b1)
+      const uint2 A0 = *reinterpret_cast<const uint2*>(vsm + ra * 64 + g * 8);
+      const uint2 A1 = *reinterpret_cast<const uint2*>(vsm + (ra + 1) * 64 + g * 8);
+      const uint2 B0 = *reinterpret_cast<const uint2*>(vsm + (ra + 8) * 64 + g * 8);
+      const uint2 B1 = *reinterpret_cast<const uint2*>(vsm + (ra + 9) * 64 + g * 8);
+      uint32_t bl[8], bh[8];
+      i8x4_to_h2x2(__byte_perm(A0.x, A1.x, 0x5140), bl[0], bl[1]);
+      i8x4_to_h2x2(__byte_perm(A0.x, A1.x, 0x7362), bl[2], bl[3]);
+      i8x4_to_h2x2(__byte_perm(A0.y, A1.y, 0x5140), bl[4], bl[5]);
+      i8x4_to_h2x2(__byte_perm(A0.y, A1.y, 0x7362), bl[6], bl[7]);
+      i8x4_to_h2x2(__byte_perm(B0.x, B1.x, 0x5140), bh[0], bh[1]);
+      i8x4_to_h2x2(__byte_perm(B0.x, B1.x, 0x7362), bh[2], bh[3]);
+      i8x4_to_h2x2(__byte_perm(B0.y, B1.y, 0x5140), bh[4], bh[5]);
+      i8x4_to_h2x2(__byte_perm(B0.y, B1.y, 0x7362), bh[6], bh[7]);
+#pragma unroll
+      for (int dt = 0; dt < 8; ++dt) mma16816_full(o[dt], pa, bl[dt], bh[dt]);
+    }
+    __syncwarp();  // every lane is done with this slot
+    if (lane == 0 && i + 2 < nmine) issue(c + 2 * kDecWarps, s);
+  }
+  if (!ok && lane == 0) {
+    // give copies still in flight a bounded chance to land before the slot
+    // memory is reused for the merge
+    for (int s = 0; s < 2; ++s) (void)dec_mbar_wait(wbar + s, 0u), (void)dec_mbar_wait(wbar + s, 1u);
+  }
+  pdl_launch_dependents();
+  __syncthreads();  // all chunks consumed: the ring becomes the merge buffer
+
+  // ---- merge the warps of this CTA: comb[w][head][0] = max, [1] = sum, [2 + dim] = O
+  {
+    float l_row = l_part;
+    l_row += __shfl_xor_sync(0xffffffffu, l_row, 1);
+    l_row += __shfl_xor_sync(0xffffffffu, l_row, 2);
+    float* cw = comb + (warp * 8 + g) * 66;
+    if (q4 == 0) {
+      cw[0] = m_run;
+      cw[1] = l_row;
+    }
+#pragma unroll
+    for (int dt = 0; dt < 8; ++dt) {
+      cw[2 + (q4 * 2) * 8 + dt] = (o[dt][0] + o[dt][2]) * (1.0f / kPScale);
+      cw[2 + (q4 * 2 + 1) * 8 + dt] = (o[dt][1] + o[dt][3]) * (1.0f / kPScale);
+    }
+  }
+  __syncthreads();
+  if (n_act == 1) {
+    for (int i = tid; i < G * 64; i += kDecThreads) {
+      const int gg = i >> 6, d = i & 63;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, comb[(w * 8 + gg) * 66]);
+      float L = 0.0f, O = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kDecWarps; ++w) {
+        const float* cw = comb + (w * 8 + gg) * 66;
+        const float f = cw[0] == -INFINITY ? 0.0f : ex2f(cw[0] - M);
+        L += cw[1] * f;
+        O += cw[2 + d] * f;
+      }
+      a.out[static_cast<size_t>(m) * Dq + (h * G + gg) * 64 + d] = O / L * sV;
+    }
+    return;
+  }
+  float* part = a.part + (static_cast<size_t>(m) * a.Hkv + h) * a.splits * kAttnPartStride +
+                static_cast<size_t>(sp) * kAttnPartStride;
+  for (int i = tid; i < G * 64; i += kDecThreads) {
+    const int gg = i >> 6, d = i & 63;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, comb[(w * 8 + gg) * 66]);
+    float L = 0.0f, O = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kDecWarps; ++w) {
+      const float* cw = comb + (w * 8 + gg) * 66;
+      const float f = cw[0] == -INFINITY ? 0.0f : ex2f(cw[0] - M);
+      L += cw[1] * f;
+      O += cw[2 + d] * f;
+    }
+    part[gg * 66 + 2 + d] = O;
+    if (d == 0) {
+      part[gg * 66] = M;
+      part[gg * 66 + 1] = L;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned prev = atomicAdd(a.counters + static_cast<size_t>(m) * a.Hkv + h, 1u);
+    *last_cta = prev == static_cast<unsigned>(n_act - 1);
+  }
+  __syncthreads();
+  if (!*last_cta) return;
+  __threadfence();
+  // ---- merge the splits (only the last CTA of this (row, kv head))
+  const float* pall = a.part + (static_cast<size_t>(m) * a.Hkv + h) * a.splits * kAttnPartStride;
+  for (int i = tid; i < G * 64; i += kDecThreads) {
+    const int gg = i >> 6, d = i & 63;
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < n_act; ++s2)
+      M = fmaxf(M, *reinterpret_cast<const volatile float*>(pall + s2 * kAttnPartStride + gg * 66));
+    float L = 0.0f, O = 0.0f;
+    for (int s2 = 0; s2 < n_act; ++s2) {
+      const volatile float* ps = pall + s2 * kAttnPartStride + gg * 66;
+      const float f = ex2f(ps[0] - M);
+      L += ps[1] * f;
+      O += ps[2 + d] * f;
+    }
+    a.out[static_cast<size_t>(m) * Dq + (h * G + gg) * 64 + d] = O / L * sV;
+  }
+  if (tid == 0) a.counters[static_cast<size_t>(m) * a.Hkv + h] = 0u;
+}
+
+// ------------------------------------------------------------------ prefill
+// Causal prefill attention, flash-attention style on mma.sync m16n8k16 fp16
+// with the same hi/lo operand split as decode. CTA = (64-query tile, q head,
+// sequence), four warps of 16 query rows; key/value tiles of 64 positions
+// are read from the INT8 cache, converted once to fp16 in shared memory
+// (exact) and fed to the MMAs with ldmatrix (K as the col-major B of Q.K^T,
+// V transposed for P.V). The next tile's INT8 bytes are loaded into
+// registers while the current tile is computed.
+constexpr int kPfQTile = 64;
+constexpr int kPfKTile = 64;
+constexpr int kPfStride = 72;  // halves per smem row: 144 B, conflict-free ldmatrix
 
 __global__ void __launch_bounds__(128) attn_prefill_mma_kernel(
     const float* __restrict__ qkv, int ld, int seq_len, int H, int Hkv, const int8_t* __restrict__ kc,
@@ -581,36 +741,56 @@ cudaError_t launch_attn_prefill(const float* qkv, int ld, int rows, int seq_len,
   return cudaGetLastError();
 }
 
-// Chunk length and CTAs per (row, kv head): batched decode has many rows, so
-// few CTAs per row; a single sequence spreads its context over more CTAs.
-int attn_split_len(int M) { return M >= 16 ? 128 : 64; }
-int attn_splits(int M, int P) {
-  const int ts = attn_split_len(M);
-  const int most = (P + ts - 1) / ts;
-  return std::min(most, M >= 16 ? 4 : 16);
+// CTAs per (row, kv head): at most two resident CTAs per SM in one wave
+// (no split once the (row, kv head) pairs alone fill the GPU), each split
+// keeping at least two 32-position chunks of the longest context. The
+// engine's partial buffer is sized for the largest count over 1..M rows
+// (attn_part_floats).
+int attn_splits(int M, int Hkv, int P) {
+  const int pairs = std::max(1, M * Hkv);
+  const int want = (2 * device_sm_count()) / pairs;
+  const int cap = std::max(1, (P + 2 * kDecChunk - 1) / (2 * kDecChunk));
+  return std::max(1, std::min(want, cap));
+}
+
+cudaError_t attn_prepare() {
+  return cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(kDecSmem));
+}
+
+cudaError_t attn_read_error(unsigned int* code) {
+  cudaError_t e = cudaMemcpyFromSymbol(code, g_attn_error, sizeof(unsigned int));
+  if (e != cudaSuccess) return e;
+  if (*code) {
+    unsigned int zero = 0;
+    return cudaMemcpyToSymbol(g_attn_error, &zero, sizeof(unsigned int));
+  }
+  return cudaSuccess;
 }
 
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a0, cudaStream_t s, bool pdl) {
   AttnDecodeArgs a = a0;
   const int G = a.H / a.Hkv;
   if (G < 1 || G > 8 || a.H % a.Hkv || !a.part || !a.counters) return cudaErrorInvalidValue;
-  const int ts = attn_split_len(a.M);
-  a.splits = attn_splits(a.M, a.P);
+  a.splits = attn_splits(a.M, a.Hkv, a.P);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.Hkv, a.M, a.splits);
-  cfg.blockDim = dim3(kAttnThreads);
+  cfg.blockDim = dim3(kDecThreads);
+  cfg.dynamicSmemBytes = kDecSmem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  if (ts == 128) return cudaLaunchKernelEx(&cfg, attn_decode_mma_kernel<128>, a);
-  return cudaLaunchKernelEx(&cfg, attn_decode_mma_kernel<64>, a);
+  return cudaLaunchKernelEx(&cfg, attn_decode_kernel, a);
 }
 
 size_t attn_part_floats(int M, int Hkv, int P) {
-  return static_cast<size_t>(M) * Hkv * attn_splits(M, P) * kAttnPartStride;
+  size_t most = 0;
+  for (int m = 1; m <= M; ++m)
+    most = std::max(most, static_cast<size_t>(m) * Hkv * attn_splits(m, Hkv, P) * kAttnPartStride);
+  return most;
 }
 
 }  // namespace tl

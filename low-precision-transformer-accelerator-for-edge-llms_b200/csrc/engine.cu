@@ -181,9 +181,7 @@ tl_status alloc_decode(tl_engine* e) {
   TL_TRY(dmalloc(&d.logits, static_cast<size_t>(B) * e->V));
   TL_TRY(dmalloc(&d.xq, static_cast<size_t>(B) * std::max(e->D, e->F)));
   TL_TRY(dmalloc(&d.amax, B));
-  // upper bound over both split lengths (64 positions below 16 rows, 128 above)
-  TL_TRY(dmalloc(&d.attn_part, std::max(attn_part_floats(B, e->Hkv, e->P),
-                                        attn_part_floats(std::min(B, 15), e->Hkv, e->P))));
+  TL_TRY(dmalloc(&d.attn_part, attn_part_floats(B, e->Hkv, e->P)));
   TL_TRY(dmalloc(&d.attn_cnt, static_cast<size_t>(B) * e->Hkv));
   TL_CU(cudaMemset(d.attn_cnt, 0, static_cast<size_t>(B) * e->Hkv * sizeof(unsigned int)));
   TL_CU(cudaMemset(d.am_counter, 0, (gemv_argmax_row_blocks(B) + 1) * sizeof(unsigned int)));

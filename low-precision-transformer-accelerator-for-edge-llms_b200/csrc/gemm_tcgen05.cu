@@ -537,6 +537,8 @@ cudaError_t prepare_tc() {
   return prepare_tc_t<256>();
 }
 
+// Reads and clears the bounded-wait error words of the tcgen05 GEMM and of
+// the decode attention (0 = none expired).
 cudaError_t tc_read_error(unsigned int* code) {
   cudaError_t e = cudaMemcpyFromSymbol(code, g_tc_error, sizeof(unsigned int));
   if (e != cudaSuccess) return e;
@@ -544,7 +546,7 @@ cudaError_t tc_read_error(unsigned int* code) {
     unsigned int zero = 0;
     return cudaMemcpyToSymbol(g_tc_error, &zero, sizeof(unsigned int));
   }
-  return cudaSuccess;
+  return attn_read_error(code);
 }
 
 }  // namespace tl

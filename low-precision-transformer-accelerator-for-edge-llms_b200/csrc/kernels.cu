@@ -444,8 +444,13 @@ cudaError_t launch_gemv(int pro, int epi, const GemvArgs& a, cudaStream_t s, boo
 
 int device_sm_count() {
   int dev = 0;
-  cudaGetDevice(&dev);
-  return (dev >= 0 && dev < 64 && g_num_sms[dev] > 0) ? g_num_sms[dev] : 148;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (g_num_sms[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+    g_num_sms[dev] = n;
+  }
+  return g_num_sms[dev];
 }
 
 static size_t rmsnorm_rows_smem(int D);
@@ -470,6 +475,7 @@ cudaError_t prepare_kernels(int max_k) {
                            static_cast<int>(rmsnorm_rows_smem(max_k)));
   if (e != cudaSuccess) return e;
   if ((e = prepare_tc()) != cudaSuccess) return e;
+  if ((e = attn_prepare()) != cudaSuccess) return e;
   prepared_k[dev] = max_k;
   return cudaSuccess;
 }
@@ -567,11 +573,110 @@ __global__ void __launch_bounds__(256) norm_quant_rows_kernel(const float* x, co
   if (threadIdx.x == 0) out_absmax[r] = amax;
 }
 
+// RMSNorm + INT8 quantization, one 128-thread CTA per row, for rows whose
+// NumPy reduction tree has 16 leaves of 128 elements (D = 2048). Thread t
+// owns accumulator j = t & 7 of leaf l = t >> 3 and sums its 16 squares
+// x[128 l + j + 8 k], k = 0..15, in order (block_sumsq_numpy's inner loop);
+// the leaf's accumulators fold ((r0 + r1) + (r2 + r3)) + ((r4 + r5) +
+// (r6 + r7)) by XOR shuffles 1, 2, 4 among its eight lanes, the four leaves
+// of a warp pair up by shuffles 8 and 16, and the four warp sums combine as
+// (w0 + w1) + (w2 + w3) -- the same additions as the tree (float addition is
+// commutative, so which partner adds is immaterial). All row elements stay
+// in registers: one memory round trip, two CTA barriers.
+__global__ void __launch_bounds__(128) norm_quant_rows_d2048_kernel(const float* x, const float* gamma,
+                                                                     float eps, int8_t* out_q,
+                                                                     float* out_absmax) {
+  constexpr int D = 2048;
+  __shared__ float red[2][4];
+  const int r = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int base = (t >> 3) * 128 + (t & 7);
+  float gm[16], v[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) gm[k] = gamma[base + 8 * k];
+  pdl_wait();
+  const float* xr = x + static_cast<size_t>(r) * D + base;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) v[k] = xr[8 * k];
+  float acc = __fmul_rn(v[0], v[0]);
+#pragma unroll
+  for (int k = 1; k < 16; ++k) acc = __fadd_rn(acc, __fmul_rn(v[k], v[k]));
+#pragma unroll
+  for (int st = 1; st < 32; st *= 2) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, st));
+  if (lane == 0) red[0][warp] = acc;
+  __syncthreads();
+  const float tot = __fadd_rn(__fadd_rn(red[0][0], red[0][1]), __fadd_rn(red[0][2], red[0][3]));
+  const float mean = __fdiv_rn(tot, static_cast<float>(D));
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+  float m = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    v[k] = __fmul_rn(__fmul_rn(v[k], inv), gm[k]);
+    m = fmaxf(m, fabsf(v[k]));
+  }
+  m = warp_max(m);
+  if (lane == 0) red[1][warp] = m;
+  __syncthreads();
+  m = fmaxf(fmaxf(red[1][0], red[1][1]), fmaxf(red[1][2], red[1][3]));
+  pdl_launch_dependents();
+  const float sf = static_cast<float>(quant_scale64(m));
+  int8_t* dst = out_q + static_cast<size_t>(r) * D + base;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) dst[8 * k] = static_cast<int8_t>(quantize_one(v[k], sf));
+  if (t == 0) out_absmax[r] = m;
+}
+
+// Per-row INT8 quantization (quantize_int8 of model/tinyllama_gemm_int8.py:36-42
+// applied to one row): one 256-thread CTA per row, the row held in registers
+// (up to 8 float4 per thread, K <= 8192), one CTA barrier for max |x|.
+constexpr int kQuantThreads = 256;
+constexpr int kQuantVec = 8;
+__global__ void __launch_bounds__(kQuantThreads) quant_rows_reg_kernel(const float* x, int K, int8_t* out_q,
+                                                                       float* out_absmax) {
+  __shared__ float red[kQuantThreads / 32];
+  const int r = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int n4 = K >> 2;
+  pdl_wait();
+  const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(r) * K);
+  float4 v[kQuantVec];
+  float m = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kQuantVec; ++i) {
+    const int c = t + i * kQuantThreads;
+    v[i] = c < n4 ? src[c] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  }
+#pragma unroll
+  for (int i = 0; i < kQuantVec; ++i)
+    m = fmaxf(m, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+  m = warp_max(m);
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  m = red[0];
+#pragma unroll
+  for (int w = 1; w < kQuantThreads / 32; ++w) m = fmaxf(m, red[w]);
+  pdl_launch_dependents();
+  const float sf = static_cast<float>(quant_scale64(m));
+  uint32_t* dst = reinterpret_cast<uint32_t*>(out_q + static_cast<size_t>(r) * K);
+#pragma unroll
+  for (int i = 0; i < kQuantVec; ++i) {
+    const int c = t + i * kQuantThreads;
+    if (c < n4)
+      dst[c] = (static_cast<uint32_t>(quantize_one(v[i].x, sf)) & 0xffu) |
+               ((static_cast<uint32_t>(quantize_one(v[i].y, sf)) & 0xffu) << 8) |
+               ((static_cast<uint32_t>(quantize_one(v[i].z, sf)) & 0xffu) << 16) |
+               ((static_cast<uint32_t>(quantize_one(v[i].w, sf)) & 0xffu) << 24);
+  }
+  if (t == 0) out_absmax[r] = m;
+}
+
 cudaError_t launch_norm_quant_rows(const float* x, const float* gamma, float eps, int rows, int D,
                                    int8_t* out_q, float* out_absmax, cudaStream_t s, bool pdl) {
   NormPlan plan;
   if (!norm_plan(D, &plan) || D % 4) return cudaErrorInvalidValue;
   cudaLaunchAttribute attr[1];
+  if (D == 2048 && plan.n_leaves == 16 && plan.leaf_len == 128) {
+    cudaLaunchConfig_t cfg = row_cfg(rows, 128, 0, s, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, norm_quant_rows_d2048_kernel, x, gamma, eps, out_q, out_absmax);
+  }
   cudaLaunchConfig_t cfg = row_cfg(rows, 256, rmsnorm_rows_smem(D), s, pdl, attr);
   return cudaLaunchKernelEx(&cfg, norm_quant_rows_kernel, x, gamma, eps, D, plan, out_q, out_absmax);
 }
@@ -598,6 +703,10 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const float* x, int K, 
 cudaError_t launch_quant_rows(const float* x, int rows, int K, int8_t* out_q, float* out_absmax,
                               cudaStream_t s, bool pdl) {
   cudaLaunchAttribute attr[1];
+  if (K % 4 == 0 && K <= 4 * kQuantVec * kQuantThreads) {
+    cudaLaunchConfig_t cfg = row_cfg(rows, kQuantThreads, 0, s, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, quant_rows_reg_kernel, x, K, out_q, out_absmax);
+  }
   cudaLaunchConfig_t cfg = row_cfg(rows, 256, 0, s, pdl, attr);
   return cudaLaunchKernelEx(&cfg, quant_rows_kernel, x, K, out_q, out_absmax);
 }

@@ -118,9 +118,10 @@ struct AttnDecodeArgs {
 };
 constexpr int kAttnPartStride = 8 * 66;  // per split: 8 heads x (max, sum, 64 values)
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);
-int attn_split_len(int M);
-int attn_splits(int M, int P);
+int attn_splits(int M, int Hkv, int P);
 size_t attn_part_floats(int M, int Hkv, int P);
+cudaError_t attn_prepare();
+cudaError_t attn_read_error(unsigned int* code);
 
 // ---- prefill helpers (rows of n_seq sequences of seq_len tokens each)
 cudaError_t launch_embed(const float* table, const int* ids, float* x, int rows, int D,

@@ -186,6 +186,7 @@ tl_status tl_attn_decode(const float* qkv, const int32_t* pos, const int32_t* sl
   if (rows <= 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads || heads / kv_heads > 8 ||
       layer < 0 || layer >= num_layers || max_positions <= 0)
     return TL_ERR_INVALID_ARGUMENT;
+  TL_OPS_TRY(cu(attn_prepare()));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   float* part = nullptr;
   unsigned int* cnt = nullptr;

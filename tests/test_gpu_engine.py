@@ -127,6 +127,31 @@ def test_batched_tensor_core_path(pkg, gpu):
     eng.close()
 
 
+def test_batched_decode_full_width(pkg, gpu):
+    """TinyLlama widths (hidden 2048, FFN 5632, 32/4 heads; 1 layer, vocab
+    2048) at 16 sequences: the batched decode step runs its tcgen05 GEMMs and
+    the warp-per-row RMSNorm/quantize kernels at their production shapes;
+    every sequence must follow its own oracle, layer-0 KV bytes exact."""
+    dims = W.small_dims(vocab=2048, hidden=2048, ffn=5632, heads=32, kv_heads=4)
+    qm = W.quantize_archive(W.random_archive(21, 1, dims, gamma_one=False), "channel")
+    eng = pkg.Engine(qm.cfg, max_batch=16, max_prefill_tokens=16 * 6)
+    eng.load(to_engine_model(pkg, qm))
+    rng = np.random.default_rng(22)
+    prompts = rng.integers(0, dims["vocab_size"], (16, 6)).astype(np.uint32)
+    outs, sts = eng.generate_batch(prompts, 4)
+    assert pkg.shim.load_library().tl_device_error() == 0
+    for i in range(16):
+        ref, ref_logits, ora = oracle_generate(qm, list(prompts[i]), 4)
+        assert sts[i]["generated_count"] == 4
+        assert tokens_match_modulo_ties(outs[i], ref, ref_logits), (i, outs[i], ref)
+        if outs[i] == ref:
+            n = 6 + len(ref) - 1
+            k, v, _, _ = eng.read_kv(0, n, slot=i)
+            np.testing.assert_array_equal(k, ora.k_cache[0, :, :n])
+            np.testing.assert_array_equal(v, ora.v_cache[0, :, :n])
+    eng.close()
+
+
 def test_long_prompts_multi_tile_prefill(pkg, gpu):
     """Prompts longer than one 64-position attention tile (ragged 150 and 130
     tokens): prefill logits and layer-0 KV bytes of one sequence, then a
