@@ -226,7 +226,7 @@ void invalidate_graphs(tl_engine* e) {
 tl_status tc_gemm(tl_engine* e, const int8_t* w, int N, const int8_t* x, int M, int K, const TcArgs& args,
                   bool pdl) {
   TcPlan p;
-  TL_CU(tc_make_plan(&p, w, N, x, M, K, device_sm_count()));
+  TL_CU(tc_make_plan(&p, w, N, x, M, K, device_sm_count(), args.epi));
   TL_CU(launch_gemm_tc(p, args, e->stream, pdl));
   return TL_OK;
 }
@@ -371,7 +371,7 @@ tl_status prefill_gemm(tl_engine* e, const int8_t* w, const double* ws, int N, i
   PrefillBufs& p = e->pf;
   if (R >= kTcMinRows) {
     TcPlan plan;
-    TL_CU(tc_make_plan(&plan, w, N, p.xq, R, K, device_sm_count()));
+    TL_CU(tc_make_plan(&plan, w, N, p.xq, R, K, device_sm_count(), epi));
     TcArgs a;
     a.epi = epi; a.w_scale = ws; a.in_absmax = in_absmax; a.rows_per_group = S; a.out_f32 = out;
     a.resid = resid;

@@ -149,104 +149,79 @@ TL_DEV float silu_mul_tc(float g, float u) {
   return __fmul_rn(__fdiv_rn(g, den), u);
 }
 
-// Epilogue of one group of 16 accumulators (tokens m0c..m0c+15) of TMEM lane
-// (output channel) n; sx[j] is the float64 activation scale of token m0c+j.
-// Every lane of the warp calls it (the SiLU pairing shuffles). Residual reads
-// are all issued before the first store (out may alias resid).
-TL_DEV void tc_epilogue16(const TcArgs& a, int n, int m0c, const int* v, const double* sx) {
-  const bool n_ok = n < a.N;
-  if (a.epi == EPI_I32) {
-    if (!n_ok) return;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int m = m0c + j;
-      if (m < a.M) a.out_i32[static_cast<size_t>(m) * a.N + n] = v[j];
-    }
-    return;
-  }
-  if (a.epi == EPI_REQ) {
-    if (!n_ok) return;
-    const uint32_t sc = a.req_scale[a.req_per_col ? n : 0];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int m = m0c + j;
-      if (m < a.M) a.out_i8[static_cast<size_t>(m) * a.N + n] = static_cast<int8_t>(requant_q16(v[j], sc, a.req_nonneg != 0));
-    }
-    return;
-  }
-  const double sw = n_ok ? a.w_scale[n] : 0.0;
-  const int lane = threadIdx.x & 31;
-  float y[16];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) y[j] = dequant(v[j], sx[j], sw);
-  if (a.epi == EPI_RESID) {
-    float r[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int m = m0c + j;
-      r[j] = (n_ok && m < a.M) ? a.resid[static_cast<size_t>(m) * a.N + n] : 0.0f;
-    }
-#pragma unroll
-    for (int j = 0; j < 16; ++j) y[j] = __fadd_rn(r[j], y[j]);
-  }
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const int m = m0c + j;
-    const bool ok = n_ok && m < a.M;
-    float mag = 0.0f;
-    if (a.epi == EPI_SILU) {
-      const float partner = __shfl_xor_sync(0xffffffffu, y[j], 1);
-      if (ok && (lane & 1) == 0) {
-        const float h = silu_mul_tc(y[j], partner);
-        a.out_f32[static_cast<size_t>(m) * (a.N >> 1) + (n >> 1)] = h;
-        mag = fabsf(h);
-      }
-    } else if (ok) {
-      a.out_f32[static_cast<size_t>(m) * a.N + n] = y[j];
-      mag = fabsf(y[j]);
-    }
-    if (a.out_absmax) {
-      mag = warp_max(mag);
-      if (lane == 0 && m < a.M) atomic_max_nonneg(a.out_absmax + m / a.rows_per_group, mag);
-    }
-  }
+// Per-channel constants of output channel n that the epilogue needs,
+// loaded before the accumulator is ready.
+struct ChanConst {
+  double sw = 0.0;    // weight scale (float epilogues)
+  uint32_t rq = 0u;   // Q16.16 requantize multiplier (EPI_REQ)
+};
+template <int EPI>
+TL_DEV ChanConst chan_const(const TcArgs& a, int n) {
+  ChanConst c;
+  if (n >= a.N) return c;
+  if (EPI == EPI_REQ) c.rq = a.req_scale[a.req_per_col ? n : 0];
+  else if (EPI != EPI_I32) c.sw = a.w_scale[n];
+  return c;
 }
 
-
-// Epilogue of a single accumulator (split-K path). The SiLU pairing of rows
-// (2j, 2j+1) uses the neighbouring lane, which owns row n^1 for the same m.
-TL_DEV void tc_epilogue1(const TcArgs& a, int n, int m, int acc, double sxm, float resid) {
-  const bool ok = n < a.N && m < a.M;
-  if (a.epi == EPI_I32) {
-    if (ok) a.out_i32[static_cast<size_t>(m) * a.N + n] = acc;
-    return;
-  }
-  if (a.epi == EPI_REQ) {
-    if (ok) a.out_i8[static_cast<size_t>(m) * a.N + n] =
-        static_cast<int8_t>(requant_q16(acc, a.req_scale[a.req_per_col ? n : 0], a.req_nonneg != 0));
-    return;
-  }
-  const double sw = ok ? a.w_scale[n] : 0.0;
-  const float y = ok ? dequant(acc, sxm, sw) : 0.0f;
-  if (a.epi == EPI_SILU) {
-    const float partner = __shfl_xor_sync(0xffffffffu, y, 1);
-    if (ok && (n & 1) == 0) a.out_f32[static_cast<size_t>(m) * (a.N >> 1) + (n >> 1)] = silu_mul_tc(y, partner);
-    return;
-  }
-  if (!ok) return;
+// Writes the output element(s) of accumulator `acc` at (token m, channel n);
+// `y` is the dequantized value (float epilogues), `partner` the value of
+// channel n ^ 1 (SiLU pairs rows 2j, 2j+1 into output column j). Returns
+// |value written| for the optional per-token absmax (0 when nothing written).
+template <int EPI>
+TL_DEV float tc_store(const TcArgs& a, int n, int m, int acc, float y, float partner, float resid,
+                      const ChanConst& c) {
   const size_t o = static_cast<size_t>(m) * a.N + n;
-  a.out_f32[o] = (a.epi == EPI_RESID) ? __fadd_rn(resid, y) : y;
+  if (EPI == EPI_I32) {
+    a.out_i32[o] = acc;
+    return 0.0f;
+  } else if (EPI == EPI_REQ) {
+    a.out_i8[o] = static_cast<int8_t>(requant_q16(acc, c.rq, a.req_nonneg != 0));
+    return 0.0f;
+  } else if (EPI == EPI_SILU) {
+    if (n & 1) return 0.0f;
+    const float h = silu_mul_tc(y, partner);
+    a.out_f32[static_cast<size_t>(m) * (a.N >> 1) + (n >> 1)] = h;
+    return fabsf(h);
+  } else if (EPI == EPI_RESID) {
+    const float r = __fadd_rn(resid, y);
+    a.out_f32[o] = r;
+    return fabsf(r);
+  } else {
+    a.out_f32[o] = y;
+    return fabsf(y);
+  }
 }
 
-template <int BN>
+// Split-K reduction slice of one thread: KS CTAs of a cluster each reduce
+// R = 128 / KS accumulator rows (output channels) over all peers. Thread t
+// takes row t % R and a run of BN / KS consecutive tokens; for SiLU it takes
+// the row pair (2p, 2p+1), p = t % (R / 2), and a run of BN / (2 KS) tokens,
+// so both halves of each output live in the same thread. Either way a thread
+// issues exactly BN / 4 sixteen-byte DSMEM loads, all before the first add.
+template <int BN, int KS, int EPI>
+struct SplitSlice {
+  static constexpr int R = 128 / KS;
+  static constexpr bool kPair = EPI == EPI_SILU;
+  static constexpr int kRowsPer = kPair ? 2 : 1;
+  static constexpr int kLanesPerRun = kPair ? R / 2 : R;   // threads sharing a token run
+  static constexpr int kTok = BN * kLanesPerRun / 128;     // tokens per thread
+  static constexpr int kQuads = kTok / 4;                  // int4 per (row, peer)
+  static_assert(kTok % 4 == 0 && kQuads >= 1, "split slice must be whole int4s");
+};
+
+template <int BN, int EPI, int KS>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, TcArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   __shared__ double sx_sm[BN];
+  __shared__ double sw_sm[kTileN];
+  __shared__ unsigned int amax_sm[BN];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int kBBytes = BN * kTileK;
   constexpr int kStage = kABytes + kBBytes;
   constexpr int kTmemCols = BN < 32 ? 32 : BN;
+  constexpr bool kFloatEpi = EPI != EPI_I32 && EPI != EPI_REQ;
   const int stages = a.stages;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * kStage);
   uint64_t* empty = full + stages;
@@ -256,8 +231,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * kTileN, m0 = blockIdx.y * BN;
   const int nkb = (a.K + kTileK - 1) / kTileK;
-  const int kb0 = static_cast<int>(static_cast<long long>(blockIdx.z) * nkb / a.k_splits);
-  const int kb1 = static_cast<int>(static_cast<long long>(blockIdx.z + 1) * nkb / a.k_splits);
+  const int kb0 = static_cast<int>(static_cast<long long>(blockIdx.z) * nkb / KS);
+  const int kb1 = static_cast<int>(static_cast<long long>(blockIdx.z + 1) * nkb / KS);
+  const bool has_amax = kFloatEpi && a.out_absmax != nullptr;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -269,6 +245,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_w)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_x)) : "memory");
   }
+  for (int j = threadIdx.x; j < BN; j += kTcThreads) amax_sm[j] = 0u;
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(kTmemCols));
@@ -300,10 +277,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tma_load_2d(smem + s * kStage, &tm_w, kb * kTileK, n0, full + s);
       tma_load_2d(smem + s * kStage + kABytes, &tm_x, kb * kTileK, m0, full + s);
     }
-  } else {
-    pdl_wait();  // activations, scales and residuals come from earlier kernels
-  }
-  if (warp == 1 && lane == 0) {
+  } else if (warp == 1 && lane == 0) {
+    pdl_wait();
     constexpr uint32_t idesc = idesc_i8(kTileN, BN);
     for (int kb = kb0, i = 0; kb < kb1 && ok; ++kb, ++i) {
       const int s = i % stages, round = i / stages;
@@ -318,90 +293,181 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mma_commit(empty + s);
     }
     mma_commit(done);  // arrives once every MMA issued above has completed
+  } else if (warp >= 2) {
+    // Warps 2 and 3 fetch the epilogue's constants while the MMAs run: the
+    // weight scales of this CTA's 128 channels, then (once the producer of X
+    // has finished) the per-token activation scales absmax / 127 in float64.
+    const int t = threadIdx.x - 64;
+    if (kFloatEpi)
+      for (int j = t; j < kTileN; j += 64) sw_sm[j] = n0 + j < a.N ? a.w_scale[n0 + j] : 0.0;
+    pdl_wait();
+    if (kFloatEpi)
+      for (int j = t; j < BN; j += 64) {
+        const int m = m0 + j;
+        sx_sm[j] = (m < a.M && a.in_absmax) ? quant_scale64(a.in_absmax[m / a.rows_per_group]) : 1.0;
+      }
   }
+  // every thread reads the previous kernel's outputs (residuals) below
+  pdl_wait();
   __syncwarp();
-  // all threads: accumulator ready (uniform across the CTA)
+  // all threads: accumulator ready (uniform across the CTA); also publishes
+  // sw_sm / sx_sm / amax_sm
   const bool ready = __syncthreads_and(mbar_wait(done, 0, 3u) ? 1 : 0) != 0;
   tc_fence_after();
   pdl_launch_dependents();
-  // per-token activation scale (absmax / 127 in float64) once per CTA
-  for (int j = threadIdx.x; j < BN; j += kTcThreads) {
-    const int m = m0 + j;
-    sx_sm[j] = (m < a.M && a.in_absmax) ? quant_scale64(a.in_absmax[m / a.rows_per_group]) : 1.0;
-  }
-  __syncthreads();
 
-  const int n = n0 + warp * 32 + lane;
   const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-  if (a.k_splits == 1) {
+  if constexpr (KS == 1) {
+    const int nl = warp * 32 + lane;
+    const int n = n0 + nl;
+    const bool n_ok = n < a.N;
+    ChanConst cc;
+    if (EPI == EPI_REQ) cc = chan_const<EPI>(a, n);
+    else cc.sw = sw_sm[nl];
+    // residuals of the first 16 tokens; each chunk prefetches the next
+    float rcur[16], rnext[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      rcur[j] = 0.0f;
+      rnext[j] = 0.0f;
+    }
+    if (EPI == EPI_RESID && n_ok) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (m0 + j < a.M) rcur[j] = a.resid[static_cast<size_t>(m0 + j) * a.N + n];
+    }
     if (ready && kb1 > kb0) {
+#pragma unroll 1
       for (int c = 0; c < BN / 16; ++c) {
+        const int mc = m0 + c * 16;
+        if (EPI == EPI_RESID && n_ok && c + 1 < BN / 16) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            rnext[j] = (mc + 16 + j < a.M) ? a.resid[static_cast<size_t>(mc + 16 + j) * a.N + n] : 0.0f;
+        }
         int v[16];
         tmem_ld16(lane_base + c * 16, v);
-        tc_epilogue16(a, n, m0 + c * 16, v, sx_sm + c * 16);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int m = mc + j;
+          const float y = kFloatEpi ? dequant(v[j], sx_sm[c * 16 + j], cc.sw) : 0.0f;
+          const float partner = EPI == EPI_SILU ? __shfl_xor_sync(0xffffffffu, y, 1) : 0.0f;
+          if (n_ok && m < a.M) {
+            const float mag = tc_store<EPI>(a, n, m, v[j], y, partner, rcur[j], cc);
+            if (has_amax) atomicMax(amax_sm + c * 16 + j, __float_as_uint(mag));
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) rcur[j] = rnext[j];
       }
     }
   } else {
-    // Split-K across the CTAs of one cluster (cluster dims 1 x 1 x k_splits):
-    // each CTA parks its INT32 partial tile [128 n][BN m] in its own shared
-    // memory (the operand ring is idle now), then CTA `rank` sums rows
+    // Split-K across the CTAs of one cluster (cluster dims 1 x 1 x KS): each
+    // CTA parks its INT32 partial tile [128 n][BN m] (row stride BN + 4 ints,
+    // so 16-byte accesses spread over the banks) in its own shared memory
+    // (the operand ring is idle now); then CTA `rank` sums rows
     // [rank*R, (rank+1)*R) over all peers through distributed shared memory
-    // and runs the epilogue for those rows. Both cluster barriers are reached
-    // by every CTA whatever happened before, so none can wait forever.
+    // and runs the epilogue for them. Both cluster barriers are reached by
+    // every CTA whatever happened before, so none can wait forever.
+    using SL = SplitSlice<BN, KS, EPI>;
+    constexpr int PS = BN + 4;
     int* part = reinterpret_cast<int*>(smem);
     const int nl = warp * 32 + lane;
+    const int rank = static_cast<int>(cluster_rank());
+    // this thread's slice and the residuals / constants it needs (issued now,
+    // consumed after the reduction)
+    const int sub = threadIdx.x % SL::kLanesPerRun;
+    const int run = threadIdx.x / SL::kLanesPerRun;
+    const int r0 = rank * SL::R + sub * SL::kRowsPer;  // first local row of the slice
+    const int t0 = run * SL::kTok;                     // first token (in the tile)
+    float rres[SL::kRowsPer][SL::kTok];
+    ChanConst cc[SL::kRowsPer];
+#pragma unroll
+    for (int h = 0; h < SL::kRowsPer; ++h) {
+      const int n = n0 + r0 + h;
+      if (EPI == EPI_REQ) cc[h] = chan_const<EPI>(a, n);
+      else cc[h].sw = sw_sm[r0 + h];
+#pragma unroll
+      for (int j = 0; j < SL::kTok; ++j) {
+        const int m = m0 + t0 + j;
+        rres[h][j] = (EPI == EPI_RESID && n < a.N && m < a.M) ? a.resid[static_cast<size_t>(m) * a.N + n] : 0.0f;
+      }
+    }
     if (ready) {
+#pragma unroll
       for (int c = 0; c < BN / 16; ++c) {
         int v[16];
         tmem_ld16(lane_base + c * 16, v);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) part[nl * BN + c * 16 + j] = v[j];
+        int4* dst = reinterpret_cast<int4*>(part + nl * PS + c * 16);
+        dst[0] = make_int4(v[0], v[1], v[2], v[3]);
+        dst[1] = make_int4(v[4], v[5], v[6], v[7]);
+        dst[2] = make_int4(v[8], v[9], v[10], v[11]);
+        dst[3] = make_int4(v[12], v[13], v[14], v[15]);
       }
     }
     cluster_sync();
-    const int ks = a.k_splits;
-    const int rank = static_cast<int>(cluster_rank());
-    const int R = kTileN / ks;                 // rows reduced by this CTA
     const uint32_t base = smem_u32(part);
-    // Work item = (row r, 4 consecutive tokens): one 16-byte DSMEM load per
-    // peer, all peers' loads issued before any add. Consecutive threads take
-    // consecutive rows n, so each output row m is written as a contiguous run.
-    const int quads = BN / 4;
-    for (int e = threadIdx.x; e < R * quads; e += kTcThreads) {
-      const int r = e % R, q = e / R;
-      const int nloc = rank * R + r;
-      const uint32_t off = base + static_cast<uint32_t>((nloc * BN + q * 4) * 4);
-      int4 v[8];
+    int4 buf[KS][SL::kRowsPer][SL::kQuads];
 #pragma unroll
-      for (int p = 0; p < 8; ++p)
-        if (p < ks) v[p] = ld_dsmem_v4(off, static_cast<uint32_t>(p));
-      int4 acc = v[0];
+    for (int p = 0; p < KS; ++p)
 #pragma unroll
-      for (int p = 1; p < 8; ++p)
-        if (p < ks) {
-          acc.x += v[p].x;
-          acc.y += v[p].y;
-          acc.z += v[p].z;
-          acc.w += v[p].w;
+      for (int h = 0; h < SL::kRowsPer; ++h)
+#pragma unroll
+        for (int q = 0; q < SL::kQuads; ++q)
+          buf[p][h][q] = ld_dsmem_v4(base + static_cast<uint32_t>(((r0 + h) * PS + t0 + 4 * q) * 4),
+                                     static_cast<uint32_t>(p));
+    if (ready) {
+#pragma unroll
+      for (int q = 0; q < SL::kQuads; ++q) {
+        int acc[SL::kRowsPer][4];
+#pragma unroll
+        for (int h = 0; h < SL::kRowsPer; ++h) {
+          acc[h][0] = buf[0][h][q].x;
+          acc[h][1] = buf[0][h][q].y;
+          acc[h][2] = buf[0][h][q].z;
+          acc[h][3] = buf[0][h][q].w;
+#pragma unroll
+          for (int p = 1; p < KS; ++p) {
+            acc[h][0] += buf[p][h][q].x;
+            acc[h][1] += buf[p][h][q].y;
+            acc[h][2] += buf[p][h][q].z;
+            acc[h][3] += buf[p][h][q].w;
+          }
         }
-      if (ready) {
-        const int nn = n0 + nloc, mm = m0 + q * 4;
-        float r[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        if (a.epi == EPI_RESID && nn < a.N) {
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            if (mm + j < a.M) r[j] = a.resid[static_cast<size_t>(mm + j) * a.N + nn];
+        for (int j = 0; j < 4; ++j) {
+          const int tt = t0 + 4 * q + j;
+          const int m = m0 + tt;
+          if (m >= a.M) continue;
+          if (SL::kPair) {
+            const int n = n0 + r0;  // even channel of the pair
+            if (n + 1 < a.N) {
+              const float g = dequant(acc[0][j], sx_sm[tt], cc[0].sw);
+              const float u = dequant(acc[SL::kRowsPer - 1][j], sx_sm[tt], cc[SL::kRowsPer - 1].sw);
+              const float mag = tc_store<EPI>(a, n, m, acc[0][j], g, u, 0.0f, cc[0]);
+              if (has_amax) atomicMax(amax_sm + tt, __float_as_uint(mag));
+            }
+          } else {
+            const int n = n0 + r0;
+            if (n < a.N) {
+              const float y = kFloatEpi ? dequant(acc[0][j], sx_sm[tt], cc[0].sw) : 0.0f;
+              const float mag = tc_store<EPI>(a, n, m, acc[0][j], y, 0.0f, rres[0][4 * q + j], cc[0]);
+              if (has_amax) atomicMax(amax_sm + tt, __float_as_uint(mag));
+            }
+          }
         }
-        tc_epilogue1(a, nn, mm + 0, acc.x, sx_sm[q * 4 + 0], r[0]);
-        tc_epilogue1(a, nn, mm + 1, acc.y, sx_sm[q * 4 + 1], r[1]);
-        tc_epilogue1(a, nn, mm + 2, acc.z, sx_sm[q * 4 + 2], r[2]);
-        tc_epilogue1(a, nn, mm + 3, acc.w, sx_sm[q * 4 + 3], r[3]);
       }
     }
     cluster_sync();  // peers keep their smem until every CTA has read it
   }
   tc_fence_before();
   __syncthreads();
+  if (has_amax && ready) {
+    for (int j = threadIdx.x; j < BN; j += kTcThreads) {
+      const int m = m0 + j;
+      if (m < a.M && amax_sm[j]) atomic_max_nonneg(a.out_absmax + m / a.rows_per_group, __uint_as_float(amax_sm[j]));
+    }
+  }
   if (warp == 0) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
   }
@@ -425,11 +491,11 @@ size_t tc_smem(int stages) {
   return static_cast<size_t>(stages) * (kABytes + BN * kTileK) + 1024 + 16 * (2 * stages + 2);
 }
 
-template <int BN>
-cudaError_t launch_tc_t(const TcPlan& p, const TcArgs& a, cudaStream_t s, bool pdl) {
+template <int BN, int EPI, int KS>
+cudaError_t launch_tc_k(const TcPlan& p, const TcArgs& a, cudaStream_t s, bool pdl) {
   const size_t smem = tc_smem<BN>(a.stages);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.N + kTileN - 1) / kTileN, (a.M + BN - 1) / BN, a.k_splits);
+  cfg.gridDim = dim3((a.N + kTileN - 1) / kTileN, (a.M + BN - 1) / BN, KS);
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -438,7 +504,7 @@ cudaError_t launch_tc_t(const TcPlan& p, const TcArgs& a, cudaStream_t s, bool p
   attr[na].id = cudaLaunchAttributeClusterDimension;
   attr[na].val.clusterDim.x = 1;
   attr[na].val.clusterDim.y = 1;
-  attr[na].val.clusterDim.z = a.k_splits;
+  attr[na].val.clusterDim.z = KS;
   ++na;
   if (pdl) {
     attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -447,13 +513,66 @@ cudaError_t launch_tc_t(const TcPlan& p, const TcArgs& a, cudaStream_t s, bool p
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN>, p.tm_w, p.tm_x, a);
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, EPI, KS>, p.tm_w, p.tm_x, a);
+}
+
+// Split counts a tile width supports: every thread's split-K slice must be
+// whole 16-byte runs (BN / KS tokens, BN / (2 KS) for the SiLU row pairs).
+constexpr bool tc_split_ok(int bn, int epi, int ks) {
+  return ks == 1 || (bn <= 64 && (epi == EPI_SILU ? bn / (2 * ks) >= 4 : bn / ks >= 4));
+}
+
+template <int BN, int EPI>
+cudaError_t launch_tc_e(const TcPlan& p, const TcArgs& a, cudaStream_t s, bool pdl) {
+  switch (a.k_splits) {
+    case 1: return launch_tc_k<BN, EPI, 1>(p, a, s, pdl);
+    case 2: if constexpr (tc_split_ok(BN, EPI, 2)) return launch_tc_k<BN, EPI, 2>(p, a, s, pdl); break;
+    case 4: if constexpr (tc_split_ok(BN, EPI, 4)) return launch_tc_k<BN, EPI, 4>(p, a, s, pdl); break;
+    case 8: if constexpr (tc_split_ok(BN, EPI, 8)) return launch_tc_k<BN, EPI, 8>(p, a, s, pdl); break;
+    default: break;
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <int BN>
+cudaError_t launch_tc_t(const TcPlan& p, const TcArgs& a, cudaStream_t s, bool pdl) {
+  switch (a.epi) {
+    case EPI_I32: return launch_tc_e<BN, EPI_I32>(p, a, s, pdl);
+    case EPI_F32: return launch_tc_e<BN, EPI_F32>(p, a, s, pdl);
+    case EPI_RESID: return launch_tc_e<BN, EPI_RESID>(p, a, s, pdl);
+    case EPI_SILU: return launch_tc_e<BN, EPI_SILU>(p, a, s, pdl);
+    case EPI_REQ: return launch_tc_e<BN, EPI_REQ>(p, a, s, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <int BN, int EPI, int KS>
+cudaError_t prepare_tc_k() {
+  if constexpr (!tc_split_ok(BN, EPI, KS)) {
+    return cudaSuccess;
+  } else {
+    return cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(tc_smem<BN>(tc_max_stages(BN))));
+  }
+}
+
+template <int BN, int EPI>
+cudaError_t prepare_tc_e() {
+  cudaError_t e;
+  if ((e = prepare_tc_k<BN, EPI, 1>()) != cudaSuccess) return e;
+  if ((e = prepare_tc_k<BN, EPI, 2>()) != cudaSuccess) return e;
+  if ((e = prepare_tc_k<BN, EPI, 4>()) != cudaSuccess) return e;
+  return prepare_tc_k<BN, EPI, 8>();
 }
 
 template <int BN>
 cudaError_t prepare_tc_t() {
-  return cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(tc_smem<BN>(tc_max_stages(BN))));
+  cudaError_t e;
+  if ((e = prepare_tc_e<BN, EPI_I32>()) != cudaSuccess) return e;
+  if ((e = prepare_tc_e<BN, EPI_F32>()) != cudaSuccess) return e;
+  if ((e = prepare_tc_e<BN, EPI_RESID>()) != cudaSuccess) return e;
+  if ((e = prepare_tc_e<BN, EPI_SILU>()) != cudaSuccess) return e;
+  return prepare_tc_e<BN, EPI_REQ>();
 }
 
 }  // namespace
@@ -487,7 +606,7 @@ cudaError_t tc_encode_operand(CUtensorMap* tm, const int8_t* base, int rows, int
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-cudaError_t tc_make_plan(TcPlan* p, const int8_t* w_nk, int N, const int8_t* x, int M, int K, int num_sms) {
+cudaError_t tc_make_plan(TcPlan* p, const int8_t* w_nk, int N, const int8_t* x, int M, int K, int num_sms, int epi) {
   p->bn = tc_pick_bn(M);
   cudaError_t e = tc_encode_operand(&p->tm_w, w_nk, N, K, kTileN);
   if (e != cudaSuccess) return e;
@@ -499,12 +618,13 @@ cudaError_t tc_make_plan(TcPlan* p, const int8_t* w_nk, int N, const int8_t* x, 
   int ks = 1;
   // split K over a cluster of 2/4/8 CTAs until the grid covers the SMs;
   // only for tiles of <= 64 tokens (the partial tile must fit the ring)
-  while (p->bn <= 64 && ks < 8 && tiles * ks < want && 2 * ks <= nkb) ks *= 2;
+  while (p->bn <= 64 && ks < 8 && tiles * ks < want && 2 * ks <= nkb && tc_split_ok(p->bn, epi, 2 * ks)) ks *= 2;
   p->k_splits = ks;
   const int per = (nkb + ks - 1) / ks;
   p->stages = std::max(2, std::min(tc_max_stages(p->bn), per));
-  // the split-K partial tile [128][bn] int32 is staged in the ring
-  while (ks > 1 && static_cast<size_t>(p->stages) * (kABytes + p->bn * kTileK) < static_cast<size_t>(kTileN) * p->bn * 4)
+  // the split-K partial tile [128][bn + 4] int32 is staged in the ring
+  while (ks > 1 &&
+         static_cast<size_t>(p->stages) * (kABytes + p->bn * kTileK) < static_cast<size_t>(kTileN) * (p->bn + 4) * 4)
     ++p->stages;
   p->M = M;
   p->N = N;

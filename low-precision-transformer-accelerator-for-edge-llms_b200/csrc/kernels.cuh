@@ -88,7 +88,7 @@ struct TcPlan {
   int bn = 64, k_splits = 1, stages = 2, M = 0, N = 0, K = 0;
 };
 // Encodes the two operand tensor maps and picks tile/split/stage counts.
-cudaError_t tc_make_plan(TcPlan* p, const int8_t* w_nk, int N, const int8_t* x, int M, int K, int num_sms);
+cudaError_t tc_make_plan(TcPlan* p, const int8_t* w_nk, int N, const int8_t* x, int M, int K, int num_sms, int epi);
 cudaError_t launch_gemm_tc(const TcPlan& p, const TcArgs& a, cudaStream_t s, bool pdl);
 cudaError_t prepare_tc();
 int tc_max_stages(int bn);

@@ -62,7 +62,7 @@ static constexpr int kOpsTcMinRows = 16;
 
 static tl_status tc_op(const int8_t* a, const int8_t* w_nk, int M, int N, int K, const TcArgs& args, cudaStream_t s) {
   TcPlan p;
-  TL_OPS_TRY(cu(tc_make_plan(&p, w_nk, N, a, M, K, device_sm_count())));
+  TL_OPS_TRY(cu(tc_make_plan(&p, w_nk, N, a, M, K, device_sm_count(), args.epi)));
   return cu(launch_gemm_tc(p, args, s, false));
 }
 
