@@ -17,10 +17,14 @@
 // Pipeline per CTA (128 threads): warp 0 lane 0 issues TMA loads into a ring
 // of `stages` (A 16 KB + B BN*128 B, 128-byte swizzle); warp 1 lane 0 issues
 // four 128xBNx32 MMAs per stage and commits each stage back to its producer
-// barrier; all four warps then drain TMEM with tcgen05.ld. With k_splits > 1
-// the CTAs of one tile each reduce a K range and add their INT32 partials
-// into an L2-resident workspace (integer addition: exact, order-free); the
-// last CTA of the tile runs the epilogue and re-zeroes the workspace.
+// barrier; warps 2 and 3 meanwhile fetch the weight and activation scales
+// into shared memory; all four warps then drain TMEM with tcgen05.ld. The
+// kernel is instantiated per tile width, epilogue and split count, so the
+// epilogue is straight-line code. With k_splits > 1 the CTAs of one tile
+// (a cluster of 1 x 1 x k_splits) each reduce a K range; the INT32 partials
+// are exchanged with bulk async copies between the CTAs' shared memories
+// and summed locally (integer addition: exact, order-free), each CTA running
+// the epilogue for 128 / k_splits of the tile's channels.
 //
 // No TMA multicast is used anywhere. Every mbarrier wait is bounded (about a
 // second of clock cycles); on expiry the kernel records an error code in
@@ -133,15 +137,6 @@ TL_DEV uint32_t cluster_rank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
-TL_DEV int4 ld_dsmem_v4(uint32_t local_addr, uint32_t peer) {
-  uint32_t remote;
-  int4 v;
-  asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(peer));
-  asm volatile("ld.shared::cluster.v4.s32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(remote));
-  return v;
-}
 
 TL_DEV float silu_mul_tc(float g, float u) {
   float c = fminf(fmaxf(g, -60.0f), 60.0f);
@@ -226,7 +221,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * kStage);
   uint64_t* empty = full + stages;
   uint64_t* done = empty + stages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* recv_bar = done + 1;  // split-K: peers' partial slices have landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * kTileN, m0 = blockIdx.y * BN;
@@ -241,6 +237,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(empty + s, 1);
     }
     mbar_init(done, 1);
+    mbar_init(recv_bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_w)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_x)) : "memory");
@@ -363,22 +360,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else {
     // Split-K across the CTAs of one cluster (cluster dims 1 x 1 x KS): each
-    // CTA parks its INT32 partial tile [128 n][BN m] (row stride BN + 4 ints,
-    // so 16-byte accesses spread over the banks) in its own shared memory
-    // (the operand ring is idle now); then CTA `rank` sums rows
-    // [rank*R, (rank+1)*R) over all peers through distributed shared memory
-    // and runs the epilogue for them. Both cluster barriers are reached by
-    // every CTA whatever happened before, so none can wait forever.
+    // CTA parks its INT32 partial tile [128 n][BN m] (row stride BN + 4 ints)
+    // in its own shared memory (the operand ring is idle now). After one
+    // cluster barrier, CTA `rank` owns rows [rank*R, (rank+1)*R): every CTA
+    // pushes the rows each peer owns into that peer's receive area with bulk
+    // async copies (shared::cta -> shared::cluster), whose completion lands
+    // on the receiver's mbarrier; each CTA then sums its rows over the KS
+    // slices from its own shared memory and runs the epilogue for them.
+    // Integer addition: exact and order-free.
     using SL = SplitSlice<BN, KS, EPI>;
     constexpr int PS = BN + 4;
+    constexpr uint32_t kSliceBytes = SL::R * PS * 4;
     int* part = reinterpret_cast<int*>(smem);
+    int* recv = part + kTileN * PS;  // [KS][R][PS], slot p from CTA p
     const int nl = warp * 32 + lane;
     const int rank = static_cast<int>(cluster_rank());
     // this thread's slice and the residuals / constants it needs (issued now,
     // consumed after the reduction)
     const int sub = threadIdx.x % SL::kLanesPerRun;
     const int run = threadIdx.x / SL::kLanesPerRun;
-    const int r0 = rank * SL::R + sub * SL::kRowsPer;  // first local row of the slice
+    const int rl = sub * SL::kRowsPer;                 // first row of the slice within the owned rows
+    const int r0 = rank * SL::R + rl;                  // ... within the tile
     const int t0 = run * SL::kTok;                     // first token (in the tile)
     float rres[SL::kRowsPer][SL::kTok];
     ChanConst cc[SL::kRowsPer];
@@ -405,33 +407,46 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         dst[3] = make_int4(v[12], v[13], v[14], v[15]);
       }
     }
-    cluster_sync();
-    const uint32_t base = smem_u32(part);
-    int4 buf[KS][SL::kRowsPer][SL::kQuads];
+    // the bulk copies read `part` through the async proxy
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    cluster_sync();  // every partial is parked; every receive barrier is armed
+    if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(recv_bar, (KS - 1) * kSliceBytes);
+      const uint32_t bar_local = smem_u32(recv_bar);
+      const uint32_t dst_local = smem_u32(recv + rank * SL::R * PS);
 #pragma unroll
-    for (int p = 0; p < KS; ++p)
-#pragma unroll
-      for (int h = 0; h < SL::kRowsPer; ++h)
-#pragma unroll
-        for (int q = 0; q < SL::kQuads; ++q)
-          buf[p][h][q] = ld_dsmem_v4(base + static_cast<uint32_t>(((r0 + h) * PS + t0 + 4 * q) * 4),
-                                     static_cast<uint32_t>(p));
-    if (ready) {
+      for (int p = 0; p < KS; ++p) {
+        if (p == rank) continue;
+        uint32_t dst, bar;
+        asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(dst) : "r"(dst_local), "r"(static_cast<uint32_t>(p)));
+        asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(bar) : "r"(bar_local), "r"(static_cast<uint32_t>(p)));
+        asm volatile(
+            "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+            ::"r"(dst), "r"(smem_u32(part + p * SL::R * PS)), "r"(kSliceBytes), "r"(bar)
+            : "memory");
+      }
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+    const bool got = mbar_wait(recv_bar, 0, 4u);
+    if (ready && got) {
 #pragma unroll
       for (int q = 0; q < SL::kQuads; ++q) {
         int acc[SL::kRowsPer][4];
 #pragma unroll
         for (int h = 0; h < SL::kRowsPer; ++h) {
-          acc[h][0] = buf[0][h][q].x;
-          acc[h][1] = buf[0][h][q].y;
-          acc[h][2] = buf[0][h][q].z;
-          acc[h][3] = buf[0][h][q].w;
+          const int4 own = *reinterpret_cast<const int4*>(part + (r0 + h) * PS + t0 + 4 * q);
+          acc[h][0] = own.x;
+          acc[h][1] = own.y;
+          acc[h][2] = own.z;
+          acc[h][3] = own.w;
 #pragma unroll
-          for (int p = 1; p < KS; ++p) {
-            acc[h][0] += buf[p][h][q].x;
-            acc[h][1] += buf[p][h][q].y;
-            acc[h][2] += buf[p][h][q].z;
-            acc[h][3] += buf[p][h][q].w;
+          for (int p = 0; p < KS; ++p) {
+            if (p == rank) continue;
+            const int4 v = *reinterpret_cast<const int4*>(recv + (p * SL::R + rl + h) * PS + t0 + 4 * q);
+            acc[h][0] += v.x;
+            acc[h][1] += v.y;
+            acc[h][2] += v.z;
+            acc[h][3] += v.w;
           }
         }
 #pragma unroll
@@ -458,7 +473,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
     }
-    cluster_sync();  // peers keep their smem until every CTA has read it
+    // this CTA's outgoing copies must have read `part` before it exits
+    if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
   }
   tc_fence_before();
   __syncthreads();
@@ -488,7 +504,7 @@ cudaError_t get_encode() {
 
 template <int BN>
 size_t tc_smem(int stages) {
-  return static_cast<size_t>(stages) * (kABytes + BN * kTileK) + 1024 + 16 * (2 * stages + 2);
+  return static_cast<size_t>(stages) * (kABytes + BN * kTileK) + 1024 + 16 * (2 * stages + 3);
 }
 
 template <int BN, int EPI, int KS>
@@ -622,9 +638,10 @@ cudaError_t tc_make_plan(TcPlan* p, const int8_t* w_nk, int N, const int8_t* x, 
   p->k_splits = ks;
   const int per = (nkb + ks - 1) / ks;
   p->stages = std::max(2, std::min(tc_max_stages(p->bn), per));
-  // the split-K partial tile [128][bn + 4] int32 is staged in the ring
-  while (ks > 1 &&
-         static_cast<size_t>(p->stages) * (kABytes + p->bn * kTileK) < static_cast<size_t>(kTileN) * (p->bn + 4) * 4)
+  // the split-K partial tile [128][bn + 4] int32 and the receive area of
+  // the same size are staged in the ring
+  while (ks > 1 && static_cast<size_t>(p->stages) * (kABytes + p->bn * kTileK) <
+                       2 * static_cast<size_t>(kTileN) * (p->bn + 4) * 4)
     ++p->stages;
   p->M = M;
   p->N = N;
