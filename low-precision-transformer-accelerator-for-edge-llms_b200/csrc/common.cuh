@@ -53,6 +53,19 @@ TL_DEV void atomic_max_nonneg(float* addr, float v) {
   atomicMax(reinterpret_cast<unsigned int*>(addr), __float_as_uint(v));
 }
 
+// Packed argmax key: order-preserving bits of the float value above the
+// complement of the index, so the 64-bit maximum is the largest value and,
+// among equal values, the lowest index (np.argmax, argmax_reduction.sv:47-58).
+TL_DEV unsigned long long argmax_key(float v, int idx) {
+  unsigned int b = __float_as_uint(v);
+  unsigned int ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return (static_cast<unsigned long long>(ord) << 32) |
+         static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<unsigned int>(idx));
+}
+TL_DEV int argmax_key_index(unsigned long long k) {
+  return static_cast<int>(0xFFFFFFFFu - static_cast<unsigned int>(k & 0xFFFFFFFFull));
+}
+
 // ------------------------------------------------------------ quantization
 // quantize_int8 (model/tinyllama_gemm_int8.py:36-42): scale = absmax/127 in
 // float64 (1.0 when absmax == 0); q = clip(rint(x / float32(scale))).

@@ -82,6 +82,7 @@ struct DecodeBufs {
   int *count = nullptr, *stop = nullptr, *out_ids = nullptr, *run = nullptr;
   int32_t* argmax = nullptr;
   unsigned long long* am_partial = nullptr;
+  unsigned long long* am_key = nullptr;  // [B] fused LM-head argmax keys (zero between steps)
   unsigned int* am_counter = nullptr;
   float* logits = nullptr;  // [rows][V]
   int8_t* xq = nullptr;     // [rows][max(D, F)] int8 activations (tensor-core path)
@@ -176,6 +177,8 @@ tl_status alloc_decode(tl_engine* e) {
   TL_TRY(dmalloc(&d.out_ids, static_cast<size_t>(B) * e->P));
   TL_TRY(dmalloc(&d.run, 4));
   TL_TRY(dmalloc(&d.argmax, B));
+  TL_TRY(dmalloc(&d.am_key, B));
+  TL_CU(cudaMemset(d.am_key, 0, B * sizeof(unsigned long long)));
   TL_TRY(dmalloc(&d.am_partial, gemv_argmax_partials(B, e->V)));
   TL_TRY(dmalloc(&d.am_counter, gemv_argmax_row_blocks(B) + 1));
   TL_TRY(dmalloc(&d.logits, static_cast<size_t>(B) * e->V));
@@ -269,13 +272,17 @@ tl_status enqueue_decode_step_tc(tl_engine* e, int M, bool finalize) {
     TL_TRY(tc_gemm(e, ly.wd, e->D, d.xq, M, e->F, dn, pdl));
   }
   TL_CU(launch_norm_quant_rows(d.x, e->gfinal, eps, M, e->D, d.xq, d.amax, s, pdl));
+  // LM head with the greedy argmax fused into the epilogue (packed keys in
+  // d.am_key, consumed and re-armed by step_finalize / keys_to_tokens); the
+  // logits themselves are not written
   TcArgs lm;
-  lm.epi = EPI_F32; lm.w_scale = e->slm; lm.in_absmax = d.amax; lm.rows_per_group = 1; lm.out_f32 = d.logits;
+  lm.epi = EPI_F32; lm.w_scale = e->slm; lm.in_absmax = d.amax; lm.rows_per_group = 1; lm.out_f32 = nullptr;
+  lm.am_key = d.am_key;
   TL_TRY(tc_gemm(e, e->wlm, e->V, d.xq, M, e->D, lm, pdl));
-  TL_CU(launch_row_argmax(d.logits, M, e->V, d.argmax, s, pdl));
+  if (!finalize) TL_CU(launch_keys_to_tokens(d.am_key, d.argmax, M, s));
   if (finalize) {
     StepArgs st;
-    st.M = M; st.argmax = d.argmax; st.tokens = d.tokens; st.pos = d.pos; st.active = d.active;
+    st.M = M; st.am_key = d.am_key; st.tokens = d.tokens; st.pos = d.pos; st.active = d.active;
     st.count = d.count; st.stop = d.stop; st.out_ids = d.out_ids; st.out_stride = e->P;
     st.run = d.run; st.P = e->P;
     TL_CU(launch_step_finalize(st, s, pdl));
@@ -621,7 +628,7 @@ tl_status tl_destroy(tl_engine* e) {
   DecodeBufs& d = e->dec;
   cudaFree(d.x); cudaFree(d.qkv); cudaFree(d.att); cudaFree(d.hid); cudaFree(d.tokens); cudaFree(d.pos);
   cudaFree(d.slots); cudaFree(d.active); cudaFree(d.count); cudaFree(d.stop); cudaFree(d.out_ids);
-  cudaFree(d.run); cudaFree(d.argmax); cudaFree(d.am_partial); cudaFree(d.am_counter); cudaFree(d.logits);
+  cudaFree(d.run); cudaFree(d.argmax); cudaFree(d.am_key); cudaFree(d.am_partial); cudaFree(d.am_counter); cudaFree(d.logits);
   cudaFree(d.xq); cudaFree(d.amax); cudaFree(d.attn_part); cudaFree(d.attn_cnt);
   PrefillBufs& p = e->pf;
   cudaFree(p.ids); cudaFree(p.x); cudaFree(p.h); cudaFree(p.qkv); cudaFree(p.att); cudaFree(p.hid);
@@ -1067,9 +1074,8 @@ tl_status tl_profile_decode_kernels(tl_engine* e, uint32_t n_seqs, uint32_t iter
           break;
         case 5:
           if (tc) {
-            t.epi = EPI_F32; t.w_scale = e->slm; t.out_f32 = d.logits;
+            t.epi = EPI_F32; t.w_scale = e->slm; t.out_f32 = nullptr; t.am_key = d.am_key;
             ts = tc_gemm(e, e->wlm, e->V, d.xq, M, e->D, t, false);
-            if (ts == TL_OK) ce = launch_row_argmax(d.logits, M, e->V, d.argmax, s, false);
           } else {
             g.x_f32 = d.x; g.gamma = e->gfinal; g.w = e->wlm; g.w_scale = e->slm; g.N = e->V; g.K = e->D;
             g.am_partial = d.am_partial; g.am_counter = d.am_counter; g.am_token = d.argmax;
@@ -1106,6 +1112,8 @@ tl_status tl_profile_decode_kernels(tl_engine* e, uint32_t n_seqs, uint32_t iter
   }
   for (auto& x : ev) cudaEventDestroy(x);
   cudaFreeAsync(flush, s);
+  // the LM-head timing accumulated argmax keys: re-arm them for the next step
+  if (tc) cudaMemsetAsync(d.am_key, 0, static_cast<size_t>(e->B) * sizeof(unsigned long long), s);
   cudaStreamSynchronize(s);
   return result;
 }

@@ -183,9 +183,45 @@ TL_DEV float tc_store(const TcArgs& a, int n, int m, int acc, float y, float par
     a.out_f32[o] = r;
     return fabsf(r);
   } else {
-    a.out_f32[o] = y;
+    if (a.out_f32) a.out_f32[o] = y;
     return fabsf(y);
   }
+}
+
+// Per-token maximum over the 32 lanes of a warp of 16 packed argmax keys
+// (one per token of a 16-token group, lane = output channel): four
+// exchange-and-keep-half steps (16 -> 8 -> 4 -> 2 -> 1 keys per lane) and a
+// final pair exchange. Returns the warp maximum of token
+// 8 b4 + 4 b3 + 2 b2 + b1 (bits of the lane index), held by both lanes of
+// each even/odd pair: 16 64-bit shuffles instead of 16 full reductions.
+TL_DEV unsigned long long warp_key_max16(const unsigned long long* k, int lane, int& token) {
+  unsigned long long a8[8], a4[4], a2[2];
+  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const unsigned long long keep = b4 ? k[i + 8] : k[i], send = b4 ? k[i] : k[i + 8];
+    const unsigned long long r = __shfl_xor_sync(0xffffffffu, send, 16);
+    a8[i] = keep > r ? keep : r;
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const unsigned long long keep = b3 ? a8[i + 4] : a8[i], send = b3 ? a8[i] : a8[i + 4];
+    const unsigned long long r = __shfl_xor_sync(0xffffffffu, send, 8);
+    a4[i] = keep > r ? keep : r;
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const unsigned long long keep = b2 ? a4[i + 2] : a4[i], send = b2 ? a4[i] : a4[i + 2];
+    const unsigned long long r = __shfl_xor_sync(0xffffffffu, send, 4);
+    a2[i] = keep > r ? keep : r;
+  }
+  const unsigned long long keep = b1 ? a2[1] : a2[0], send = b1 ? a2[0] : a2[1];
+  const unsigned long long r = __shfl_xor_sync(0xffffffffu, send, 2);
+  unsigned long long m = keep > r ? keep : r;
+  const unsigned long long o = __shfl_xor_sync(0xffffffffu, m, 1);
+  m = m > o ? m : o;
+  token = (b4 ? 8 : 0) + (b3 ? 4 : 0) + (b2 ? 2 : 0) + (b1 ? 1 : 0);
+  return m;
 }
 
 // Split-K reduction slice of one thread: KS CTAs of a cluster each reduce
@@ -212,6 +248,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __shared__ double sx_sm[BN];
   __shared__ double sw_sm[kTileN];
   __shared__ unsigned int amax_sm[BN];
+  __shared__ unsigned long long key_sm[EPI == EPI_F32 ? BN : 1];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int kBBytes = BN * kTileK;
   constexpr int kStage = kABytes + kBBytes;
@@ -243,6 +280,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_x)) : "memory");
   }
   for (int j = threadIdx.x; j < BN; j += kTcThreads) amax_sm[j] = 0u;
+  if constexpr (EPI == EPI_F32)
+    for (int j = threadIdx.x; j < BN; j += kTcThreads) key_sm[j] = 0ull;
+  const bool has_key = EPI == EPI_F32 && a.am_key != nullptr;
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(kTmemCols));
@@ -344,15 +384,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         int v[16];
         tmem_ld16(lane_base + c * 16, v);
+        unsigned long long key[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int m = mc + j;
           const float y = kFloatEpi ? dequant(v[j], sx_sm[c * 16 + j], cc.sw) : 0.0f;
           const float partner = EPI == EPI_SILU ? __shfl_xor_sync(0xffffffffu, y, 1) : 0.0f;
+          key[j] = 0ull;
           if (n_ok && m < a.M) {
             const float mag = tc_store<EPI>(a, n, m, v[j], y, partner, rcur[j], cc);
             if (has_amax) atomicMax(amax_sm + c * 16 + j, __float_as_uint(mag));
+            if (EPI == EPI_F32) key[j] = argmax_key(y, n);
           }
+        }
+        if (EPI == EPI_F32 && has_key) {
+          int tok;
+          const unsigned long long km = warp_key_max16(key, lane, tok);
+          if ((lane & 1) == 0 && km) atomicMax(key_sm + c * 16 + tok, km);
         }
 #pragma unroll
         for (int j = 0; j < 16; ++j) rcur[j] = rnext[j];
@@ -468,6 +516,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               const float y = kFloatEpi ? dequant(acc[0][j], sx_sm[tt], cc[0].sw) : 0.0f;
               const float mag = tc_store<EPI>(a, n, m, acc[0][j], y, 0.0f, rres[0][4 * q + j], cc[0]);
               if (has_amax) atomicMax(amax_sm + tt, __float_as_uint(mag));
+              if (EPI == EPI_F32 && has_key) atomicMax(key_sm + tt, argmax_key(y, n));
             }
           }
         }
@@ -483,6 +532,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int m = m0 + j;
       if (m < a.M && amax_sm[j]) atomic_max_nonneg(a.out_absmax + m / a.rows_per_group, __uint_as_float(amax_sm[j]));
     }
+  }
+  if constexpr (EPI == EPI_F32) {
+    if (has_key && ready)
+      for (int j = threadIdx.x; j < BN; j += kTcThreads)
+        if (m0 + j < a.M && key_sm[j]) atomicMax(a.am_key + m0 + j, key_sm[j]);
   }
   if (warp == 0) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));

@@ -79,15 +79,6 @@ constexpr int kGemvU = 4;    // 16-byte chunks per lane per row per item
 constexpr int kGemvMaxGrid = 1024;
 static int g_num_sms[64] = {0};
 
-TL_DEV unsigned long long argmax_key(float v, int idx) {
-  unsigned int b = __float_as_uint(v);
-  unsigned int ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-  return (static_cast<unsigned long long>(ord) << 32) |
-         static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<unsigned int>(idx));
-}
-TL_DEV int argmax_key_index(unsigned long long k) {
-  return static_cast<int>(0xFFFFFFFFu - static_cast<unsigned int>(k & 0xFFFFFFFFull));
-}
 
 TL_DEV float silu_mul(float g, float u) {
   // model/tinyllama.py:159-161: x / (1 + exp(-clip(x, -60, 60))), then * up
@@ -933,9 +924,15 @@ __global__ void step_finalize_kernel(StepArgs a) {
   pdl_wait();
   const int m = blockIdx.x * blockDim.x + threadIdx.x;
   if (m >= a.M) return;
+  int tok = 0;
+  if (a.am_key) {  // packed (logit, id) key of the LM-head GEMM; re-armed for the next step
+    tok = argmax_key_index(a.am_key[m]);
+    a.am_key[m] = 0ull;
+  } else {
+    tok = a.argmax[m];
+  }
   if (a.stop[m] != 0 || !a.active[m]) return;
   const int max_new = a.run[0], eos = a.run[1], out_cap = a.run[2];
-  const int tok = a.argmax[m];
   const int c = a.count[m];
   if (c < out_cap) a.out_ids[static_cast<size_t>(m) * a.out_stride + c] = tok;
   a.count[m] = c + 1;
@@ -962,6 +959,20 @@ cudaError_t launch_step_finalize(const StepArgs& a, cudaStream_t s, bool pdl) {
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, step_finalize_kernel, a);
+}
+
+// token id of each row's packed argmax key; the key is re-armed (zeroed)
+__global__ void keys_to_tokens_kernel(unsigned long long* key, int32_t* token, int M) {
+  pdl_wait();
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= M) return;
+  token[m] = argmax_key_index(key[m]);
+  key[m] = 0ull;
+}
+
+cudaError_t launch_keys_to_tokens(unsigned long long* key, int32_t* token, int M, cudaStream_t s) {
+  keys_to_tokens_kernel<<<(M + 127) / 128, 128, 0, s>>>(key, token, M);
+  return cudaGetLastError();
 }
 
 __global__ void rows_rewind_kernel(int* pos, int* active, int* count, int* stop, int M, int position) {

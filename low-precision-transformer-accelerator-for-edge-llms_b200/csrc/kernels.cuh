@@ -80,7 +80,8 @@ struct TcArgs {
   int8_t* out_i8 = nullptr;
   const uint32_t* req_scale = nullptr;
   int req_per_col = 0, req_nonneg = 0;
-  float* out_absmax = nullptr;         // only without split-K
+  float* out_absmax = nullptr;         // per-token max |output| (float epilogues)
+  unsigned long long* am_key = nullptr;  // EPI_F32: per-token argmax key (atomic max), zero on entry
 };
 struct TcPlan {
   CUtensorMap tm_w;                    // W^T [N][K], 128-row boxes
@@ -175,7 +176,8 @@ cudaError_t launch_fill_f64(double* dst, size_t n, double v, cudaStream_t s);
 // Decode-step bookkeeping on the device (after the LM-head argmax).
 struct StepArgs {
   int M = 0;
-  const int32_t* argmax = nullptr;  // [M]
+  const int32_t* argmax = nullptr;  // [M] token ids, or
+  unsigned long long* am_key = nullptr;  // [M] packed argmax keys (read, then zeroed)
   int* tokens = nullptr;            // [M] next input token
   int* pos = nullptr;               // [M]
   int* active = nullptr;            // [M]
@@ -187,6 +189,7 @@ struct StepArgs {
   int P = 0;
 };
 cudaError_t launch_step_finalize(const StepArgs& a, cudaStream_t s, bool pdl);
+cudaError_t launch_keys_to_tokens(unsigned long long* key, int32_t* token, int M, cudaStream_t s);
 // rows 0..M-1: pos = position, active = 1, count = 0, stop = 0
 cudaError_t launch_rows_rewind(int* pos, int* active, int* count, int* stop, int M, int position,
                                cudaStream_t s);

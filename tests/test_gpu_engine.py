@@ -152,6 +152,41 @@ def test_batched_decode_full_width(pkg, gpu):
     eng.close()
 
 
+def test_batched_decode_full_vocab_argmax(pkg, gpu):
+    """Vocabulary 32000 at 16 sequences: the LM head of each decode step runs
+    as 250 unsplit tcgen05 tiles with the greedy argmax fused into the
+    epilogue (per-warp key exchange, per-CTA and global 64-bit maxima). The
+    LM-head row of t2, the oracle's token from sequence 0's first decode
+    step, is copied to another id d in a different tile, so at that step the
+    two logits tie exactly and the lower id must be emitted."""
+    import dataclasses
+    dims = W.small_dims(vocab=32000)
+    qm = W.quantize_archive(W.random_archive(31, 1, dims, gamma_one=False), "channel")
+    rng = np.random.default_rng(32)
+    prompts = rng.integers(0, dims["vocab_size"], (16, 5)).astype(np.uint32)
+    ref0, _, _ = oracle_generate(qm, list(prompts[0]), 2)
+    t1, t2 = ref0
+    d = next(c for c in ((t2 + 16000) % 32000, (t2 + 9000) % 32000) if c != t1)
+    w = qm.lm_head.w_q.copy()
+    sc = qm.lm_head.scale.copy()
+    w[:, d] = w[:, t2]
+    sc[d] = sc[t2]
+    qm = dataclasses.replace(qm, lm_head=W.QLinear(w, sc))
+    eng = pkg.Engine(qm.cfg, max_batch=16, max_prefill_tokens=16 * 5)
+    eng.load(to_engine_model(pkg, qm))
+    outs, sts = eng.generate_batch(prompts, 4)
+    assert pkg.shim.load_library().tl_device_error() == 0
+    for i in range(16):
+        ref, ref_logits, _ = oracle_generate(qm, list(prompts[i]), 4)
+        assert sts[i]["generated_count"] == 4
+        assert tokens_match_modulo_ties(outs[i], ref, ref_logits), (i, outs[i], ref)
+    ref, ref_logits, _ = oracle_generate(qm, list(prompts[0]), 2)
+    lg = np.asarray(ref_logits[1])
+    assert lg[d] == lg[t2] and lg.argmax() == min(d, t2)  # the tie is real and on top
+    assert outs[0][:2] == [t1, min(d, t2)], (outs[0], t1, t2, d)
+    eng.close()
+
+
 def test_long_prompts_multi_tile_prefill(pkg, gpu):
     """Prompts longer than one 64-position attention tile (ragged 150 and 130
     tokens): prefill logits and layer-0 KV bytes of one sequence, then a
