@@ -221,6 +221,38 @@ def run_reference(a, rank, world):
 
 
 # ------------------------------------------------------------------ ours
+def tp_prefill_bench(pkg, group, rank, world, local_rank):
+    """configs[4] on `world` GPUs: one 8 x 2048-token prefill split by KV head
+    (tl_tp_create, NCCL INT32 all-reduces after O and down), CUDA events on
+    every rank, max over ranks. Random weights of the same seed on every rank
+    (each draws its slice of one model)."""
+    import torch
+    import torch.distributed as dist
+    box = [pkg.tp_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    eng = pkg.Engine(TINYLLAMA, max_batch=8, device=local_rank, max_prefill_tokens=8 * 2048,
+                     tp_rank=rank, tp_world=world, tp_id=box[0])
+    eng.init_random(1234)
+    p8 = np.random.default_rng(7).integers(0, 32000, (8, 2048)).astype(np.uint32)
+    stream = torch.cuda.ExternalStream(eng.stream_handle())
+    eng.prefill_batch_device(p8)  # warm-up (same collective sequence on every rank)
+    eng.synchronize()
+    times = []
+    for _ in range(3):
+        group.barrier()
+        h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        h0.record(stream)
+        eng.prefill_batch_device(p8)
+        h1.record(stream)
+        h1.synchronize()
+        times.append(group.max(h0.elapsed_time(h1)))
+    eng.close()
+    ms = float(np.median(times))
+    return {"workload": "configs[4]: 8 x 2048-token prompts, 22 layers, tensor parallel by KV head",
+            "world": world, "value": 8 * 2048 / (ms / 1e3), "unit": "tok/s", "ms": ms,
+            "collectives": "per layer: 2 x all-reduce max (8 floats) + 2 x all-reduce sum INT32 [16384][2048]"}
+
+
 def run_ours(a, rank, world, local_rank):
     import torch
     torch.cuda.set_device(local_rank)
@@ -344,6 +376,8 @@ def run_ours(a, rank, world, local_rank):
         line["int8_gemm"] = i8
         line["cpu_baseline"] = cpu_baseline_sample()
     eng.close()
+    if world in (2, 4) and not a.no_extras:
+        line["tp_prefill"] = tp_prefill_bench(pkg, group, rank, world, local_rank)
     group.close()
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -143,6 +143,31 @@ TL_API int32_t tl_version(void);
 
 TL_API tl_status tl_create(const tl_config* cfg, int32_t device, tl_engine** out);
 TL_API tl_status tl_destroy(tl_engine* eng);
+
+/* Tensor-parallel prefill over `world` GPUs, one process (or thread) and one
+ * engine per GPU. The reference's prefill is the recompute forward_mixed
+ * (model/tinyllama_gemm_int8.py:432-467); its TP-2/4 split is by KV head:
+ * rank r holds kv heads [r Hkv/world, (r+1) Hkv/world) and their query
+ * heads, the matching columns of Q/K/V and gate/up and rows of O and down,
+ * with RMSNorm, embedding and LM head replicated. INT32 partial sums after O
+ * and after down are added with an NCCL all-reduce, so the logits are
+ * bit-identical to one GPU's. world must divide num_kv_heads and
+ * intermediate_size / 16.
+ * tl_tp_unique_id: rank 0 draws the group id; the host hands the same
+ * TL_TP_ID_BYTES bytes to every rank's tl_tp_create (all ranks must call it
+ * concurrently: it blocks until the group is complete). tl_load_weights on
+ * a TP engine takes the FULL model view and keeps this rank's slice;
+ * tl_init_random_weights draws exactly the slice of the single-GPU model of
+ * the same seed. Prefill calls (tl_prefill_logits, tl_prefill_batch_device,
+ * tl_generate / tl_generate_batch with max_new_tokens == 0) are collective:
+ * every rank makes the same calls in the same order. Decode entry points
+ * return TL_ERR_UNIMPLEMENTED on a TP engine (decode scales by sequence).
+ * tl_read_kv returns this rank's kv heads. NCCL (libnccl.so.2) is loaded at
+ * run time; TL_ERR_NCCL when it is missing or a collective fails. */
+#define TL_TP_ID_BYTES 128
+TL_API tl_status tl_tp_unique_id(uint8_t* id_out);
+TL_API tl_status tl_tp_create(const tl_config* cfg, int32_t device, int32_t rank, int32_t world, const uint8_t* id,
+                              tl_engine** out);
 /* Copies (and lays out) the host weights into the engine's device arena. */
 TL_API tl_status tl_load_weights(tl_engine* eng, const tl_weights_view* w);
 /* Random INT8 weights drawn on the device (benchmarks of the full model

@@ -12,5 +12,5 @@ ctypes binding and mirrors the reference's Python operator API.
 from . import replicas, shim  # noqa: F401
 from .shim import (  # noqa: F401
     Engine, Linear, Layer, Model, TLError, forward_mixed, from_tinyllama_weights, load_library,
-    quantize_int8, quantize_weight, quantized_linear, rms_norm, rope_tables,
+    quantize_int8, quantize_weight, quantized_linear, rms_norm, rope_tables, tp_unique_id,
 )

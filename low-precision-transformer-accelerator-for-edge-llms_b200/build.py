@@ -69,7 +69,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(compile_one, sources()))
     tmp = OUT.with_suffix(".so.tmp")
-    cmd = [cc, *ARCH, "-shared", "-o", str(tmp), *map(str, objs)]
+    cmd = [cc, *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-ldl"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -19,6 +19,17 @@
 //  * KV cache: int8 [slot][layer][kv_head][max_pos][64] for K and for V
 //    (kv_cache_manager.sv:43-47 layout per slot), float32 scales
 //    [slot][layer][kv_head].
+// Tensor-parallel prefill (tl_tp_create): rank r of `world` holds kv heads
+// [r Hkv/world, (r+1) Hkv/world) with their query heads, the matching
+// columns of Q/K/V, rows of O (its input features), columns of gate/up and
+// rows of down; RMSNorm, embedding and LM head are replicated. After O and
+// after down the INT32 partial products are summed with an NCCL all-reduce
+// (exact), and the per-sequence activation maxima that set the O and down
+// input scales are combined with an all-reduce max first, so every rank
+// quantizes with the same scale as one GPU: the result is bit-identical.
+#include <dlfcn.h>
+#include <nccl.h>
+
 #include <algorithm>
 #include <atomic>
 #include <cmath>
@@ -103,7 +114,45 @@ struct PrefillBufs {
   int8_t* xq = nullptr;
   float* amax = nullptr;     // [L][4][n_seq] + [n_seq] (final norm)
   float* kvamax = nullptr;   // [L][n_seq][2][Hkv]
+  int32_t* acc32 = nullptr;  // tensor parallel: INT32 partial sums [rows][D]
 };
+
+// NCCL entry points, resolved at run time from libnccl.so.2 (the copy a host
+// framework already loaded, if any), so the library has no link-time NCCL
+// dependency and single-GPU use never touches it.
+struct NcclApi {
+  bool ok = false;
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+};
+const NcclApi& nccl_api() {
+  static const NcclApi api = [] {
+    NcclApi a;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+    if (!h) return a;
+    a.get_unique_id = reinterpret_cast<decltype(a.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    a.comm_init_rank = reinterpret_cast<decltype(a.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    a.comm_destroy = reinterpret_cast<decltype(a.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
+    a.ok = a.get_unique_id && a.comm_init_rank && a.all_reduce && a.comm_destroy && a.error_string;
+    return a;
+  }();
+  return api;
+}
+
+#define TL_NCCL(call)                                                                    \
+  do {                                                                                   \
+    const ncclResult_t _r = (call);                                                      \
+    if (_r != ncclSuccess) {                                                             \
+      g_last_error = std::string(#call) + ": " + nccl_api().error_string(_r);            \
+      return TL_ERR_NCCL;                                                                \
+    }                                                                                    \
+  } while (0)
 
 }  // namespace
 
@@ -128,6 +177,10 @@ struct tl_engine {
   int* h_pinned = nullptr;         // pinned staging
   size_t h_pinned_ints = 0;
   bool use_pdl = true;
+  // tensor parallelism (prefill only): H, Hkv, Dq, Dkv, Nqkv and F above are
+  // this rank's shares; cfg keeps the model's global sizes
+  int tp_rank = 0, tp_world = 1;
+  ncclComm_t comm = nullptr;
 };
 
 namespace {
@@ -203,7 +256,7 @@ tl_status ensure_prefill(tl_engine* e, size_t rows, int n_seq) {
   rows = std::max(rows, p.rows);
   n_seq = std::max(n_seq, p.n_seq_cap);
   cudaFree(p.ids); cudaFree(p.x); cudaFree(p.h); cudaFree(p.qkv); cudaFree(p.att);
-  cudaFree(p.hid); cudaFree(p.xq); cudaFree(p.amax); cudaFree(p.kvamax);
+  cudaFree(p.hid); cudaFree(p.xq); cudaFree(p.amax); cudaFree(p.kvamax); cudaFree(p.acc32);
   p = PrefillBufs{};
   TL_TRY(dmalloc(&p.ids, rows));
   TL_TRY(dmalloc(&p.x, rows * e->D));
@@ -214,6 +267,7 @@ tl_status ensure_prefill(tl_engine* e, size_t rows, int n_seq) {
   TL_TRY(dmalloc(&p.xq, rows * std::max(e->F, e->D)));
   TL_TRY(dmalloc(&p.amax, static_cast<size_t>(e->L) * 4 * n_seq + n_seq));
   TL_TRY(dmalloc(&p.kvamax, static_cast<size_t>(e->L) * n_seq * 2 * e->Hkv));
+  if (e->tp_world > 1) TL_TRY(dmalloc(&p.acc32, rows * e->D));
   p.rows = rows;
   p.n_seq_cap = n_seq;
   return TL_OK;
@@ -381,17 +435,36 @@ tl_status prefill_gemm(tl_engine* e, const int8_t* w, const double* ws, int N, i
     TL_CU(tc_make_plan(&plan, w, N, p.xq, R, K, device_sm_count(), epi));
     TcArgs a;
     a.epi = epi; a.w_scale = ws; a.in_absmax = in_absmax; a.rows_per_group = S; a.out_f32 = out;
-    a.resid = resid;
-    a.out_absmax = plan.k_splits == 1 ? out_absmax : nullptr;
+    a.resid = resid; a.out_absmax = out_absmax;
+    a.out_i32 = epi == EPI_I32 ? p.acc32 : nullptr;
     TL_CU(launch_gemm_tc(plan, a, e->stream, false));
-    if (out_absmax && plan.k_splits > 1)
-      TL_CU(launch_absmax_rows(out, R, epi == EPI_SILU ? N / 2 : N, S, out_absmax, e->stream));
     return TL_OK;
   }
   GemvArgs g;
   g.x_q = p.xq; g.in_absmax = in_absmax; g.rows_per_group = S;
   g.w = w; g.w_scale = ws; g.M = R; g.N = N; g.K = K; g.out_f32 = out; g.resid = resid; g.out_absmax = out_absmax;
+  g.out_i32 = epi == EPI_I32 ? p.acc32 : nullptr;
   TL_CU(launch_gemv(PRO_Q8, epi, g, e->stream, false));
+  return TL_OK;
+}
+
+// Tensor parallel: max over ranks of per-sequence activation maxima (in place)
+tl_status tp_allreduce_max(tl_engine* e, float* v, int n) {
+  TL_NCCL(nccl_api().all_reduce(v, v, static_cast<size_t>(n), ncclFloat32, ncclMax, e->comm, e->stream));
+  return TL_OK;
+}
+
+// Tensor parallel row-split projection (O, down): this rank's INT32 partial
+// products of its input features, summed over ranks with an INT32 all-reduce
+// (exact), then dequantized and added to the residual stream x exactly as the
+// single-GPU EPI_RESID epilogue does.
+tl_status tp_rowsplit_resid(tl_engine* e, const int8_t* w, const double* ws, int N, int K, int R, int S,
+                            const float* in_absmax) {
+  PrefillBufs& p = e->pf;
+  TL_TRY(prefill_gemm(e, w, ws, N, K, R, S, in_absmax, EPI_I32, nullptr, nullptr, nullptr));
+  TL_NCCL(nccl_api().all_reduce(p.acc32, p.acc32, static_cast<size_t>(R) * N, ncclInt32, ncclSum, e->comm,
+                                e->stream));
+  TL_CU(launch_dequant_resid_rows(p.acc32, in_absmax, S, ws, p.x, R, N, e->stream));
   return TL_OK;
 }
 
@@ -401,6 +474,7 @@ tl_status prefill_gemm(tl_engine* e, const int8_t* w, const double* ws, int N, i
 tl_status enqueue_prefill(tl_engine* e, int n_seq, int S, int slot_base, bool head, float* logits) {
   PrefillBufs& p = e->pf;
   cudaStream_t s = e->stream;
+  const bool tp = e->tp_world > 1;
   const int R = n_seq * S;
   const float eps = e->cfg.rms_norm_eps;
   TL_CU(cudaMemsetAsync(p.amax, 0, (static_cast<size_t>(e->L) * 4 * n_seq + n_seq) * sizeof(float), s));
@@ -419,15 +493,19 @@ tl_status enqueue_prefill(tl_engine* e, int n_seq, int S, int slot_base, bool he
                                   slot_base, l, e->L, e->P, s));
     TL_CU(launch_attn_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->kc, e->vc, e->ks, e->vs, slot_base,
                               l, e->L, e->P, p.att, am + n_seq, s));
+    if (tp) TL_TRY(tp_allreduce_max(e, am + n_seq, n_seq));
     TL_CU(launch_quantize_rows(p.att, am + n_seq, R, e->Dq, S, p.xq, s));
-    TL_TRY(prefill_gemm(e, ly.wo, ly.so, e->D, e->Dq, R, S, am + n_seq, EPI_RESID, p.x, p.x, nullptr));
+    if (tp) TL_TRY(tp_rowsplit_resid(e, ly.wo, ly.so, e->D, e->Dq, R, S, am + n_seq));
+    else TL_TRY(prefill_gemm(e, ly.wo, ly.so, e->D, e->Dq, R, S, am + n_seq, EPI_RESID, p.x, p.x, nullptr));
     // feed-forward block
     TL_CU(launch_rmsnorm_rows(p.x, ly.g2, eps, p.h, am + 2 * n_seq, R, e->D, S, s));
     TL_CU(launch_quantize_rows(p.h, am + 2 * n_seq, R, e->D, S, p.xq, s));
     TL_TRY(prefill_gemm(e, ly.wgu, ly.sgu, 2 * e->F, e->D, R, S, am + 2 * n_seq, EPI_SILU, p.hid, nullptr,
                         am + 3 * n_seq));
+    if (tp) TL_TRY(tp_allreduce_max(e, am + 3 * n_seq, n_seq));
     TL_CU(launch_quantize_rows(p.hid, am + 3 * n_seq, R, e->F, S, p.xq, s));
-    TL_TRY(prefill_gemm(e, ly.wd, ly.sd, e->D, e->F, R, S, am + 3 * n_seq, EPI_RESID, p.x, p.x, nullptr));
+    if (tp) TL_TRY(tp_rowsplit_resid(e, ly.wd, ly.sd, e->D, e->F, R, S, am + 3 * n_seq));
+    else TL_TRY(prefill_gemm(e, ly.wd, ly.sd, e->D, e->F, R, S, am + 3 * n_seq, EPI_RESID, p.x, p.x, nullptr));
   }
   if (!head) return TL_OK;
   float* amf = p.amax + static_cast<size_t>(e->L) * 4 * n_seq;
@@ -561,18 +639,40 @@ const char* tl_status_string(int32_t s) {
 
 int32_t tl_version(void) { return 0x00010000; }
 
-tl_status tl_create(const tl_config* cfg, int32_t device, tl_engine** out) {
+namespace {
+// Engine for rank `rank` of a tensor-parallel group of `world` GPUs (world 1:
+// the whole model on one GPU). `id` is the NCCL group id (world > 1 only).
+tl_status create_engine(const tl_config* cfg, int32_t device, int rank, int world, const ncclUniqueId* id,
+                        tl_engine** out) {
   if (!out) return TL_ERR_INVALID_ARGUMENT;
   *out = nullptr;
   TL_TRY(check_cfg(cfg));
+  if (world < 1 || rank < 0 || rank >= world || cfg->num_kv_heads % world ||
+      cfg->intermediate_size % (16 * world))
+    return TL_ERR_INVALID_ARGUMENT;
   TL_CU(cudaSetDevice(device));
   tl_engine* e = new tl_engine();
   e->cfg = *cfg;
   e->device = device;
-  e->D = cfg->hidden_size; e->F = cfg->intermediate_size; e->H = cfg->num_heads; e->Hkv = cfg->num_kv_heads;
+  e->tp_rank = rank;
+  e->tp_world = world;
+  e->D = cfg->hidden_size; e->F = cfg->intermediate_size / world; e->H = cfg->num_heads / world;
+  e->Hkv = cfg->num_kv_heads / world;
   e->Dq = e->H * 64; e->Dkv = e->Hkv * 64; e->Nqkv = e->Dq + 2 * e->Dkv; e->V = cfg->vocab_size;
   e->L = cfg->num_layers; e->P = cfg->max_positions; e->B = cfg->max_batch;
   auto fail = [&](tl_status s) { tl_destroy(e); return s; };
+  if (world > 1) {
+    if (!id || !nccl_api().ok) {
+      g_last_error = "libnccl.so.2 not loadable";
+      return fail(TL_ERR_NCCL);
+    }
+    const ncclResult_t r = nccl_api().comm_init_rank(&e->comm, world, *id, rank);
+    if (r != ncclSuccess) {
+      g_last_error = std::string("ncclCommInitRank: ") + nccl_api().error_string(r);
+      e->comm = nullptr;
+      return fail(TL_ERR_NCCL);
+    }
+  }
   cudaError_t ce = prepare_kernels(std::max(e->F, e->D));
   if (ce == cudaSuccess) ce = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
   if (ce != cudaSuccess) { g_last_error = cudaGetErrorString(ce); return fail(TL_ERR_CUDA); }
@@ -613,12 +713,40 @@ tl_status tl_create(const tl_config* cfg, int32_t device, tl_engine** out) {
   *out = e;
   return TL_OK;
 }
+}  // namespace
+
+tl_status tl_create(const tl_config* cfg, int32_t device, tl_engine** out) {
+  return create_engine(cfg, device, 0, 1, nullptr, out);
+}
+
+tl_status tl_tp_unique_id(uint8_t* id_out) {
+  if (!id_out) return TL_ERR_INVALID_ARGUMENT;
+  if (!nccl_api().ok) {
+    g_last_error = "libnccl.so.2 not loadable";
+    return TL_ERR_NCCL;
+  }
+  ncclUniqueId id;
+  TL_NCCL(nccl_api().get_unique_id(&id));
+  static_assert(sizeof(ncclUniqueId) == TL_TP_ID_BYTES, "NCCL unique id size");
+  std::memcpy(id_out, &id, sizeof(id));
+  return TL_OK;
+}
+
+tl_status tl_tp_create(const tl_config* cfg, int32_t device, int32_t rank, int32_t world, const uint8_t* id,
+                       tl_engine** out) {
+  if (!id || world < 2) return TL_ERR_INVALID_ARGUMENT;
+  ncclUniqueId uid;
+  std::memcpy(&uid, id, sizeof(uid));
+  return create_engine(cfg, device, rank, world, &uid, out);
+}
 
 tl_status tl_destroy(tl_engine* e) {
   if (!e) return TL_OK;
   cudaSetDevice(e->device);
   if (e->stream) cudaStreamSynchronize(e->stream);
   invalidate_graphs(e);
+  if (e->comm) nccl_api().comm_destroy(e->comm);
+  e->comm = nullptr;
   for (auto& ly : e->layers) {
     cudaFree(ly.wqkv); cudaFree(ly.sqkv); cudaFree(ly.wo); cudaFree(ly.so); cudaFree(ly.wgu);
     cudaFree(ly.sgu); cudaFree(ly.wd); cudaFree(ly.sd); cudaFree(ly.g1); cudaFree(ly.g2);
@@ -632,7 +760,7 @@ tl_status tl_destroy(tl_engine* e) {
   cudaFree(d.xq); cudaFree(d.amax); cudaFree(d.attn_part); cudaFree(d.attn_cnt);
   PrefillBufs& p = e->pf;
   cudaFree(p.ids); cudaFree(p.x); cudaFree(p.h); cudaFree(p.qkv); cudaFree(p.att); cudaFree(p.hid);
-  cudaFree(p.xq); cudaFree(p.amax); cudaFree(p.kvamax);
+  cudaFree(p.xq); cudaFree(p.amax); cudaFree(p.kvamax); cudaFree(p.acc32);
   if (e->h_pinned) cudaFreeHost(e->h_pinned);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
@@ -646,6 +774,44 @@ static tl_status upload_transposed(tl_engine* e, int8_t* tmp, const int8_t* host
   return TL_OK;
 }
 
+namespace {
+// Host-side slice of one layer for tensor-parallel rank r: the columns of
+// Q/K/V and gate/up it produces and the rows of O and down it consumes
+// (pointer offsets into the caller's arrays where rows are contiguous).
+struct LayerSlice {
+  std::vector<int8_t> q, k, v, gate, up;
+  std::vector<double> sq, sk, sv, sg, su;
+  tl_layer_view view{};
+};
+void slice_cols(const int8_t* src, int rows, int src_cols, int col0, int cols, std::vector<int8_t>& dst) {
+  dst.resize(static_cast<size_t>(rows) * cols);
+  for (int i = 0; i < rows; ++i)
+    std::memcpy(dst.data() + static_cast<size_t>(i) * cols, src + static_cast<size_t>(i) * src_cols + col0, cols);
+}
+void slice_layer(const tl_engine* e, const tl_layer_view& lv, LayerSlice& out) {
+  const int r = e->tp_rank, D = e->D;
+  const int Dqg = e->cfg.num_heads * 64, Dkvg = e->cfg.num_kv_heads * 64, Fg = e->cfg.intermediate_size;
+  slice_cols(lv.q.w, D, Dqg, r * e->Dq, e->Dq, out.q);
+  slice_cols(lv.k.w, D, Dkvg, r * e->Dkv, e->Dkv, out.k);
+  slice_cols(lv.v.w, D, Dkvg, r * e->Dkv, e->Dkv, out.v);
+  slice_cols(lv.gate.w, D, Fg, r * e->F, e->F, out.gate);
+  slice_cols(lv.up.w, D, Fg, r * e->F, e->F, out.up);
+  out.sq.assign(lv.q.scale + r * e->Dq, lv.q.scale + (r + 1) * e->Dq);
+  out.sk.assign(lv.k.scale + r * e->Dkv, lv.k.scale + (r + 1) * e->Dkv);
+  out.sv.assign(lv.v.scale + r * e->Dkv, lv.v.scale + (r + 1) * e->Dkv);
+  out.sg.assign(lv.gate.scale + r * e->F, lv.gate.scale + (r + 1) * e->F);
+  out.su.assign(lv.up.scale + r * e->F, lv.up.scale + (r + 1) * e->F);
+  out.view = lv;
+  out.view.q = {out.q.data(), out.sq.data()};
+  out.view.k = {out.k.data(), out.sk.data()};
+  out.view.v = {out.v.data(), out.sv.data()};
+  out.view.gate = {out.gate.data(), out.sg.data()};
+  out.view.up = {out.up.data(), out.su.data()};
+  out.view.o = {lv.o.w + static_cast<size_t>(r) * e->Dq * D, lv.o.scale};
+  out.view.down = {lv.down.w + static_cast<size_t>(r) * e->F * D, lv.down.scale};
+}
+}  // namespace
+
 tl_status tl_load_weights(tl_engine* e, const tl_weights_view* w) {
   if (!e || !w || !w->embed || !w->final_norm || !w->lm_head.w || !w->lm_head.scale || !w->layers)
     return TL_ERR_INVALID_ARGUMENT;
@@ -655,12 +821,18 @@ tl_status tl_load_weights(tl_engine* e, const tl_weights_view* w) {
   int8_t* tmp = nullptr;
   TL_TRY(dmalloc(&tmp, tmp_bytes));
   auto body = [&]() -> tl_status {
+    LayerSlice slice;
     for (int l = 0; l < e->L; ++l) {
-      const tl_layer_view& lv = w->layers[l];
-      const tl_linear_view* all[7] = {&lv.q, &lv.k, &lv.v, &lv.o, &lv.gate, &lv.up, &lv.down};
+      const tl_layer_view& full = w->layers[l];
+      const tl_linear_view* all[7] = {&full.q, &full.k, &full.v, &full.o, &full.gate, &full.up, &full.down};
       for (auto* p : all)
         if (!p->w || !p->scale) return TL_ERR_INVALID_ARGUMENT;
-      if (!lv.input_norm || !lv.post_norm) return TL_ERR_INVALID_ARGUMENT;
+      if (!full.input_norm || !full.post_norm) return TL_ERR_INVALID_ARGUMENT;
+      if (e->tp_world > 1) {
+        TL_CU(cudaStreamSynchronize(e->stream));  // the previous layer's slices are still being read
+        slice_layer(e, full, slice);
+      }
+      const tl_layer_view& lv = e->tp_world > 1 ? slice.view : full;
       Layer& ly = e->layers[l];
       TL_TRY(upload_transposed(e, tmp, lv.q.w, D, Dq, ly.wqkv));
       TL_TRY(upload_transposed(e, tmp, lv.k.w, D, Dkv, ly.wqkv + static_cast<size_t>(Dq) * D));
@@ -721,11 +893,23 @@ tl_status tl_init_random_weights(tl_engine* e, uint64_t seed) {
   cudaStream_t s = e->stream;
   const double wscale = 0.02 / 73.3;  // int8 uniform[-127,127] has std ~73.3
   uint64_t k = seed * 1000003ull;
+  // Each matrix is drawn as the global model's [out][in] matrix with the
+  // element hash of its flat index; a tensor-parallel rank draws exactly its
+  // slice, so every rank holds a piece of the same model as one GPU would.
+  const long long D = e->D, r = e->tp_rank;
+  const long long Dqg = static_cast<long long>(e->cfg.num_heads) * 64;
+  const long long Dkvg = static_cast<long long>(e->cfg.num_kv_heads) * 64;
+  const long long Fg = e->cfg.intermediate_size;
   for (auto& ly : e->layers) {
-    TL_CU(launch_random_i8(ly.wqkv, static_cast<size_t>(e->Nqkv) * e->D, ++k, s));
-    TL_CU(launch_random_i8(ly.wo, static_cast<size_t>(e->D) * e->Dq, ++k, s));
-    TL_CU(launch_random_i8(ly.wgu, static_cast<size_t>(2) * e->F * e->D, ++k, s));
-    TL_CU(launch_random_i8(ly.wd, static_cast<size_t>(e->D) * e->F, ++k, s));
+    const uint64_t kqkv = ++k;
+    TL_CU(launch_random_i8_block(ly.wqkv, e->Dq, e->D, r * e->Dq, 0, D, kqkv, s));
+    TL_CU(launch_random_i8_block(ly.wqkv + static_cast<size_t>(e->Dq) * e->D, e->Dkv, e->D, Dqg + r * e->Dkv, 0, D,
+                                 kqkv, s));
+    TL_CU(launch_random_i8_block(ly.wqkv + static_cast<size_t>(e->Dq + e->Dkv) * e->D, e->Dkv, e->D,
+                                 Dqg + Dkvg + r * e->Dkv, 0, D, kqkv, s));
+    TL_CU(launch_random_i8_block(ly.wo, e->D, e->Dq, 0, r * e->Dq, Dqg, ++k, s));
+    TL_CU(launch_random_i8_block(ly.wgu, 2 * e->F, e->D, 2 * r * e->F, 0, D, ++k, s));
+    TL_CU(launch_random_i8_block(ly.wd, e->D, e->F, 0, r * e->F, Fg, ++k, s));
     TL_CU(launch_fill_f64(ly.sqkv, e->Nqkv, wscale, s));
     TL_CU(launch_fill_f64(ly.so, e->D, wscale, s));
     TL_CU(launch_fill_f64(ly.sgu, 2 * e->F, wscale, s));
@@ -768,6 +952,7 @@ static tl_status prefill_common(tl_engine* e, uint32_t n_seq, const uint32_t* pr
 tl_status tl_generate_batch(tl_engine* e, uint32_t n_seqs, const uint32_t* prompts, uint32_t n_prompt,
                             uint32_t max_new, uint32_t eos, uint32_t* out_ids, uint32_t out_cap,
                             tl_run_status* st) {
+  if (e && e->tp_world > 1 && max_new != 0) return TL_ERR_UNIMPLEMENTED;  // prefill-only under TP
   if (!e || !prompts || (!out_ids && out_cap)) return TL_ERR_INVALID_ARGUMENT;
   if (!e->loaded) return TL_ERR_NOT_LOADED;
   TL_CU(cudaSetDevice(e->device));
@@ -797,6 +982,7 @@ tl_status tl_generate_batch(tl_engine* e, uint32_t n_seqs, const uint32_t* promp
 
 tl_status tl_generate(tl_engine* e, const uint32_t* prompt, uint32_t n, uint32_t max_new, uint32_t eos,
                       uint32_t mode, uint32_t* out_ids, uint32_t out_cap, tl_run_status* st) {
+  if (e && e->tp_world > 1 && (max_new != 0 || mode != TL_MODE_PREFILL)) return TL_ERR_UNIMPLEMENTED;
   if (!e) return TL_ERR_INVALID_ARGUMENT;
   if (!e->loaded) return TL_ERR_NOT_LOADED;
   if (mode == TL_MODE_PREFILL) {
@@ -887,6 +1073,7 @@ tl_status tl_prefill_logits(tl_engine* e, uint32_t slot, const uint32_t* ids, ui
 }
 
 tl_status tl_decode_logits(tl_engine* e, uint32_t slot, uint32_t token, float* logits_out) {
+  if (e && e->tp_world > 1) return TL_ERR_UNIMPLEMENTED;  // decode shards by sequence, not by head
   if (!e || !logits_out) return TL_ERR_INVALID_ARGUMENT;
   if (!e->loaded) return TL_ERR_NOT_LOADED;
   if (slot >= static_cast<uint32_t>(e->B)) return TL_ERR_OUT_OF_RANGE;
@@ -951,6 +1138,7 @@ tl_status tl_prefill_batch_device(tl_engine* e, uint32_t n_seqs, const uint32_t*
 }
 
 tl_status tl_decode_steps_device(tl_engine* e, uint32_t n_seqs, uint32_t steps) {
+  if (e && e->tp_world > 1) return TL_ERR_UNIMPLEMENTED;  // decode shards by sequence, not by head
   if (!e) return TL_ERR_INVALID_ARGUMENT;
   if (!e->loaded) return TL_ERR_NOT_LOADED;
   if (n_seqs == 0 || n_seqs > static_cast<uint32_t>(e->B)) return TL_ERR_OUT_OF_RANGE;
@@ -962,6 +1150,7 @@ tl_status tl_decode_steps_device(tl_engine* e, uint32_t n_seqs, uint32_t steps) 
 }
 
 tl_status tl_decode_rewind(tl_engine* e, uint32_t n_seqs, uint32_t position) {
+  if (e && e->tp_world > 1) return TL_ERR_UNIMPLEMENTED;  // decode shards by sequence, not by head
   if (!e) return TL_ERR_INVALID_ARGUMENT;
   if (n_seqs == 0 || n_seqs > static_cast<uint32_t>(e->B) || position >= static_cast<uint32_t>(e->P))
     return TL_ERR_OUT_OF_RANGE;
@@ -987,6 +1176,7 @@ tl_status tl_synchronize(tl_engine* e) {
 }
 
 tl_status tl_profile_decode_kernels(tl_engine* e, uint32_t n_seqs, uint32_t iters, float* avg_ms_out) {
+  if (e && e->tp_world > 1) return TL_ERR_UNIMPLEMENTED;  // decode shards by sequence, not by head
   if (!e || !avg_ms_out || iters == 0) return TL_ERR_INVALID_ARGUMENT;
   if (!e->loaded) return TL_ERR_NOT_LOADED;
   if (n_seqs == 0 || n_seqs > static_cast<uint32_t>(e->B)) return TL_ERR_OUT_OF_RANGE;

@@ -904,6 +904,22 @@ cudaError_t launch_random_i8(int8_t* dst, size_t n, uint64_t seed, cudaStream_t 
   random_i8_kernel<<<148 * 8, 256, 0, s>>>(dst, n, seed);
   return cudaGetLastError();
 }
+__global__ void random_i8_block_kernel(int8_t* dst, int rows, int cols, long long r0, long long c0,
+                                       long long src_cols, uint64_t seed) {
+  const size_t n = static_cast<size_t>(rows) * cols;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const long long r = static_cast<long long>(i / cols), c = static_cast<long long>(i % cols);
+    const uint64_t g = static_cast<uint64_t>((r0 + r) * src_cols + c0 + c);
+    const uint64_t h = splitmix64(seed ^ (g * 0xD1B54A32D192ED03ull));
+    dst[i] = static_cast<int8_t>(static_cast<int>(h % 255ull) - 127);
+  }
+}
+cudaError_t launch_random_i8_block(int8_t* dst, int rows, int cols, long long src_row0, long long src_col0,
+                                   long long src_cols, uint64_t seed, cudaStream_t s) {
+  random_i8_block_kernel<<<148 * 8, 256, 0, s>>>(dst, rows, cols, src_row0, src_col0, src_cols, seed);
+  return cudaGetLastError();
+}
 cudaError_t launch_random_normal_f32(float* dst, size_t n, float std, uint64_t seed, cudaStream_t s) {
   random_normal_kernel<<<148 * 8, 256, 0, s>>>(dst, n, std, seed);
   return cudaGetLastError();
@@ -959,6 +975,33 @@ cudaError_t launch_step_finalize(const StepArgs& a, cudaStream_t s, bool pdl) {
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, step_finalize_kernel, a);
+}
+
+// x[m][n] += dequant(acc[m][n]) with the token scale absmax[m / rpg] / 127
+// and the channel scale w_scale[n] -- the EPI_RESID epilogue applied to
+// INT32 sums gathered from several GPUs. One CTA per (row, 1024 columns).
+__global__ void __launch_bounds__(256) dequant_resid_rows_kernel(const int32_t* acc, const float* absmax, int rpg,
+                                                                  const double* w_scale, float* x, int N) {
+  const int m = blockIdx.y;
+  const double sx = quant_scale64(absmax[m / rpg]);
+  const int n = (blockIdx.x * 256 + threadIdx.x) * 4;
+  if (n >= N) return;
+  const size_t o = static_cast<size_t>(m) * N + n;
+  const int4 a = *reinterpret_cast<const int4*>(acc + o);
+  float4 r = *reinterpret_cast<const float4*>(x + o);
+  r.x = __fadd_rn(r.x, dequant(a.x, sx, w_scale[n]));
+  r.y = __fadd_rn(r.y, dequant(a.y, sx, w_scale[n + 1]));
+  r.z = __fadd_rn(r.z, dequant(a.z, sx, w_scale[n + 2]));
+  r.w = __fadd_rn(r.w, dequant(a.w, sx, w_scale[n + 3]));
+  *reinterpret_cast<float4*>(x + o) = r;
+}
+
+cudaError_t launch_dequant_resid_rows(const int32_t* acc, const float* absmax, int rows_per_group,
+                                      const double* w_scale, float* x, int rows, int N, cudaStream_t s) {
+  if (N % 4 || rows <= 0) return cudaErrorInvalidValue;
+  dim3 grid((N + 1023) / 1024, rows);
+  dequant_resid_rows_kernel<<<grid, 256, 0, s>>>(acc, absmax, rows_per_group, w_scale, x, N);
+  return cudaGetLastError();
 }
 
 // token id of each row's packed argmax key; the key is re-armed (zeroed)

@@ -190,6 +190,12 @@ struct StepArgs {
 };
 cudaError_t launch_step_finalize(const StepArgs& a, cudaStream_t s, bool pdl);
 cudaError_t launch_keys_to_tokens(unsigned long long* key, int32_t* token, int M, cudaStream_t s);
+cudaError_t launch_dequant_resid_rows(const int32_t* acc, const float* absmax, int rows_per_group,
+                                      const double* w_scale, float* x, int rows, int N, cudaStream_t s);
+// random int8 sub-block [rows][cols] of a global [*][src_cols] matrix whose
+// element (i, j) is hash(seed, i * src_cols + j), at (src_row0, src_col0)
+cudaError_t launch_random_i8_block(int8_t* dst, int rows, int cols, long long src_row0, long long src_col0,
+                                   long long src_cols, uint64_t seed, cudaStream_t s);
 // rows 0..M-1: pos = position, active = 1, count = 0, stop = 0
 cudaError_t launch_rows_rewind(int* pos, int* active, int* count, int* stop, int M, int position,
                                cudaStream_t s);

@@ -43,7 +43,7 @@ MODE_PREFILL, MODE_DECODE = 0, 1
 
 # Every symbol the header declares (checked by the CPU tests).
 EXPORTS = (
-    "tl_status_string", "tl_version", "tl_create", "tl_destroy", "tl_load_weights",
+    "tl_status_string", "tl_version", "tl_create", "tl_destroy", "tl_tp_unique_id", "tl_tp_create", "tl_load_weights",
     "tl_init_random_weights", "tl_generate", "tl_generate_batch", "tl_abort",
     "tl_prefill_logits", "tl_decode_logits", "tl_read_kv", "tl_get_position",
     "tl_decode_steps_device", "tl_prefill_batch_device", "tl_decode_rewind", "tl_synchronize",
@@ -112,6 +112,8 @@ def load_library(path: Path | str | None = None):
         "tl_version": (i32, []),
         "tl_create": (i32, [C.POINTER(Config), i32, C.POINTER(vp)]),
         "tl_destroy": (i32, [vp]),
+        "tl_tp_unique_id": (i32, [vp]),
+        "tl_tp_create": (i32, [C.POINTER(Config), i32, i32, i32, vp, C.POINTER(vp)]),
         "tl_load_weights": (i32, [vp, C.POINTER(WeightsView)]),
         "tl_init_random_weights": (i32, [vp, u64]),
         "tl_generate": (i32, [vp, vp, u32, u32, u32, u32, vp, u32, C.POINTER(RunStatus)]),
@@ -242,12 +244,28 @@ def rope_tables(n_pos: int, head_dim: int, theta: float) -> tuple[np.ndarray, np
 # --------------------------------------------------------------------------
 # Engine (runtime contract)
 # --------------------------------------------------------------------------
+TP_ID_BYTES = 128
+
+
+def tp_unique_id() -> bytes:
+    """NCCL group id for a tensor-parallel prefill group (drawn on rank 0 and
+    handed to every rank's Engine(..., tp_id=...))."""
+    lib = load_library()
+    buf = (C.c_uint8 * TP_ID_BYTES)()
+    check(lib.tl_tp_unique_id(C.addressof(buf)), "tl_tp_unique_id")
+    return bytes(buf)
+
+
 class Engine:
     """One engine per GPU: weights arena, INT8 KV cache for ``max_batch``
     sequences, captured decode graphs."""
 
     def __init__(self, cfg: dict, max_batch: int = 1, device: int = 0,
-                 max_prefill_tokens: int | None = None):
+                 max_prefill_tokens: int | None = None, tp_rank: int = 0, tp_world: int = 1,
+                 tp_id: bytes | None = None):
+        """``tp_world > 1`` makes rank ``tp_rank`` of a tensor-parallel
+        prefill group (tl_tp_create); every rank passes the same ``tp_id``
+        from :func:`tp_unique_id` and all ranks construct concurrently."""
         self.lib = load_library()
         self.cfg = dict(cfg)
         c = Config(hidden_size=cfg["hidden_size"], intermediate_size=cfg["intermediate_size"],
@@ -258,8 +276,16 @@ class Engine:
                    max_batch=max_batch,
                    max_prefill_tokens=max_prefill_tokens or cfg["max_position_embeddings"])
         h = C.c_void_p()
-        check(self.lib.tl_create(C.byref(c), device, C.byref(h)), "tl_create")
+        if tp_world > 1:
+            if tp_id is None or len(tp_id) != TP_ID_BYTES:
+                raise ValueError("tensor-parallel engines need the group's tp_unique_id() bytes")
+            idbuf = (C.c_uint8 * TP_ID_BYTES).from_buffer_copy(tp_id)
+            check(self.lib.tl_tp_create(C.byref(c), device, tp_rank, tp_world, C.addressof(idbuf), C.byref(h)),
+                  "tl_tp_create")
+        else:
+            check(self.lib.tl_create(C.byref(c), device, C.byref(h)), "tl_create")
         self.h = h
+        self.tp_rank, self.tp_world = tp_rank, tp_world
         self.max_batch = max_batch
         self._keep = []
 
@@ -344,7 +370,9 @@ class Engine:
         return out
 
     def read_kv(self, layer: int, n_pos: int, slot: int = 0):
-        hkv = self.cfg["num_key_value_heads"]
+        """INT8 K/V rows [kv_head][pos][64] and scales of one layer (this
+        rank's kv heads on a tensor-parallel engine)."""
+        hkv = self.cfg["num_key_value_heads"] // self.tp_world
         k = np.zeros((hkv, n_pos, 64), np.int8)
         v = np.zeros((hkv, n_pos, 64), np.int8)
         ks = np.zeros(hkv, np.float32)
