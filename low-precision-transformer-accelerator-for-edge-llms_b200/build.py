@@ -22,7 +22,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 OUT = PKG / "libtl_b200.so"
 BUILD = ROOT / "_build"
-SOURCES = ["kernels.cu", "gemm_tcgen05.cu", "attention.cu", "engine.cu", "ops.cu", "noalloc.cu"]
+SOURCES = ["kernels.cu", "gemm_tcgen05.cu", "attention.cu", "engine.cu", "ops.cu", "noalloc.cu", "decode1.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          "-diag-suppress", "128", "-I", str(ROOT / "include")]

@@ -100,6 +100,10 @@ struct DecodeBufs {
   float* amax = nullptr;    // [rows] per-row absmax of the activation in xq
   float* attn_part = nullptr;         // decode attention split partials
   unsigned int* attn_cnt = nullptr;   // [rows][Hkv] merge tickets
+  // persistent single-sequence step (decode1.cu)
+  D1Layer* d1_layers = nullptr;       // device copy of the layer pointers
+  float* d1_part = nullptr;
+  unsigned int* d1_sync = nullptr;
 };
 
 // Batches of at least this many rows use the tcgen05 GEMM; smaller ones the
@@ -181,6 +185,7 @@ struct tl_engine {
   // this rank's shares; cfg keeps the model's global sizes
   int tp_rank = 0, tp_world = 1;
   ncclComm_t comm = nullptr;
+  bool use_decode1 = false;         // batch-1 steps run as one persistent kernel
 };
 
 namespace {
@@ -240,6 +245,17 @@ tl_status alloc_decode(tl_engine* e) {
   TL_TRY(dmalloc(&d.attn_part, attn_part_floats(B, e->Hkv, e->P)));
   TL_TRY(dmalloc(&d.attn_cnt, static_cast<size_t>(B) * e->Hkv));
   TL_CU(cudaMemset(d.attn_cnt, 0, static_cast<size_t>(B) * e->Hkv * sizeof(unsigned int)));
+  if (e->use_decode1) {
+    TL_TRY(dmalloc(&d.d1_layers, e->L));
+    TL_TRY(dmalloc(&d.d1_part, decode1_part_floats(e->Hkv, e->P)));
+    TL_TRY(dmalloc(&d.d1_sync, 64));  // grid barrier: count and generation in separate lines
+    std::vector<D1Layer> h(e->L);
+    for (int l = 0; l < e->L; ++l) {
+      const Layer& ly = e->layers[l];
+      h[l] = {ly.wqkv, ly.sqkv, ly.wo, ly.so, ly.wgu, ly.sgu, ly.wd, ly.sd, ly.g1, ly.g2};
+    }
+    TL_CU(cudaMemcpy(d.d1_layers, h.data(), h.size() * sizeof(D1Layer), cudaMemcpyHostToDevice));
+  }
   TL_CU(cudaMemset(d.am_counter, 0, (gemv_argmax_row_blocks(B) + 1) * sizeof(unsigned int)));
   TL_CU(cudaMemset(d.active, 0, B * sizeof(int)));
   TL_CU(cudaMemset(d.stop, 0, B * sizeof(int)));
@@ -348,8 +364,36 @@ tl_status enqueue_decode_step_tc(tl_engine* e, int M, bool finalize) {
 // One decode step for rows 0..M-1 (row m uses KV slot dec.slots[m]). All
 // inputs (token, position, active) come from device memory, so the sequence
 // is graph-capturable.
+// The batch-1 step as one persistent kernel (decode1.cu) plus finalize.
+tl_status enqueue_decode_step_d1(tl_engine* e, bool finalize) {
+  DecodeBufs& d = e->dec;
+  cudaStream_t s = e->stream;
+  D1Args a;
+  a.layers = d.d1_layers; a.L = e->L; a.D = e->D; a.F = e->F; a.H = e->H; a.Hkv = e->Hkv; a.V = e->V;
+  a.P = e->P; a.Nqkv = e->Nqkv; a.Dq = e->Dq; a.eps = e->cfg.rms_norm_eps;
+  if (!norm_plan(e->D, &a.plan)) return TL_ERR_INVALID_ARGUMENT;
+  a.embed = e->embed; a.gfinal = e->gfinal; a.wlm = e->wlm; a.slm = e->slm;
+  a.kc = e->kc; a.vc = e->vc; a.ks = e->ks; a.vs = e->vs; a.cos = e->cosT; a.sin = e->sinT;
+  a.x = d.x; a.qkv = d.qkv; a.att = d.att; a.hid = d.hid;
+  a.token = d.tokens; a.pos = d.pos; a.slot = d.slots; a.active = d.active;
+  a.part = d.d1_part; a.sync = d.d1_sync; a.am_key = d.am_key;
+  TL_CU(cudaMemsetAsync(d.d1_sync, 0, 64 * sizeof(unsigned int), s));
+  TL_CU(launch_decode1(a, device_sm_count(), s));
+  if (finalize) {
+    StepArgs st;
+    st.M = 1; st.am_key = d.am_key; st.tokens = d.tokens; st.pos = d.pos; st.active = d.active;
+    st.count = d.count; st.stop = d.stop; st.out_ids = d.out_ids; st.out_stride = e->P;
+    st.run = d.run; st.P = e->P;
+    TL_CU(launch_step_finalize(st, s, false));
+  } else {
+    TL_CU(launch_keys_to_tokens(d.am_key, d.argmax, 1, s));
+  }
+  return TL_OK;
+}
+
 tl_status enqueue_decode_step(tl_engine* e, int M, float* logits, bool finalize) {
   if (M >= kTcMinRows && !logits) return enqueue_decode_step_tc(e, M, finalize);
+  if (M == 1 && !logits && e->use_decode1) return enqueue_decode_step_d1(e, finalize);
   DecodeBufs& d = e->dec;
   cudaStream_t s = e->stream;
   const bool pdl = e->use_pdl;
@@ -560,7 +604,11 @@ tl_status run_decode_loop(tl_engine* e, int M, int budget, bool* aborted) {
   }
   unsigned int code = 0;
   TL_CU(tc_read_error(&code));
-  if (code) return TL_ERR_TIMEOUT;
+  if (code) {
+    g_last_error = "device wait expired (code " + std::to_string(code) + ", detail " +
+                   std::to_string(decode1_last_detail()) + ")";
+    return TL_ERR_TIMEOUT;
+  }
   return TL_OK;
 }
 
@@ -629,8 +677,8 @@ const char* tl_status_string(int32_t s) {
     case TL_ERR_INVALID_ARGUMENT: return "invalid argument";
     case TL_ERR_OUT_OF_RANGE: return "out of range";
     case TL_ERR_CUDA: return g_last_error.empty() ? "cuda error" : g_last_error.c_str();
-    case TL_ERR_NCCL: return "nccl error";
-    case TL_ERR_TIMEOUT: return "timeout";
+    case TL_ERR_NCCL: return g_last_error.empty() ? "nccl error" : g_last_error.c_str();
+    case TL_ERR_TIMEOUT: return g_last_error.empty() ? "timeout" : g_last_error.c_str();
     case TL_ERR_NOT_LOADED: return "weights not loaded";
     case TL_ERR_UNIMPLEMENTED: return "unimplemented";
     default: return "error";
@@ -702,6 +750,12 @@ tl_status create_engine(const tl_config* cfg, int32_t device, int rank, int worl
   if ((s = dmalloc(&e->vc, kv)) != TL_OK) return fail(s);
   if ((s = dmalloc(&e->ks, static_cast<size_t>(e->B) * e->L * e->Hkv)) != TL_OK) return fail(s);
   if ((s = dmalloc(&e->vs, static_cast<size_t>(e->B) * e->L * e->Hkv)) != TL_OK) return fail(s);
+  // TL_DISABLE_DECODE1=1 keeps batch-1 steps on the multi-kernel GEMV path
+  // (a comparison aid, off by default).
+  const char* no_d1 = std::getenv("TL_DISABLE_DECODE1");
+  e->use_decode1 = world == 1 && !(no_d1 && no_d1[0] == '1') &&
+                   decode1_supported(e->D, e->F, e->Dq, e->H, e->Hkv, e->P) &&
+                   decode1_prepare(e->D, e->F, e->Dq) == cudaSuccess;
   if ((s = alloc_decode(e)) != TL_OK) return fail(s);
   const size_t pf_rows = cfg->max_prefill_tokens > 0 ? cfg->max_prefill_tokens : e->P;
   if ((s = ensure_prefill(e, pf_rows, e->B)) != TL_OK) return fail(s);
@@ -758,6 +812,7 @@ tl_status tl_destroy(tl_engine* e) {
   cudaFree(d.slots); cudaFree(d.active); cudaFree(d.count); cudaFree(d.stop); cudaFree(d.out_ids);
   cudaFree(d.run); cudaFree(d.argmax); cudaFree(d.am_key); cudaFree(d.am_partial); cudaFree(d.am_counter); cudaFree(d.logits);
   cudaFree(d.xq); cudaFree(d.amax); cudaFree(d.attn_part); cudaFree(d.attn_cnt);
+  cudaFree(d.d1_layers); cudaFree(d.d1_part); cudaFree(d.d1_sync);
   PrefillBufs& p = e->pf;
   cudaFree(p.ids); cudaFree(p.x); cudaFree(p.h); cudaFree(p.qkv); cudaFree(p.att); cudaFree(p.hid);
   cudaFree(p.xq); cudaFree(p.amax); cudaFree(p.kvamax); cudaFree(p.acc32);
@@ -1169,7 +1224,8 @@ tl_status tl_synchronize(tl_engine* e) {
   unsigned int code = 0;
   TL_CU(tc_read_error(&code));
   if (code) {
-    g_last_error = "tensor-core pipeline wait expired (code " + std::to_string(code) + ")";
+    g_last_error = "device wait expired (code " + std::to_string(code) + ", detail " +
+                   std::to_string(decode1_last_detail()) + ")";
     return TL_ERR_TIMEOUT;
   }
   return TL_OK;
@@ -1308,11 +1364,13 @@ tl_status tl_profile_decode_kernels(tl_engine* e, uint32_t n_seqs, uint32_t iter
   return result;
 }
 
-int32_t tl_decode_step_kernel_count(tl_engine* e) { return e ? 1 + 5 * e->L + 2 : 0; }
+int32_t tl_decode_step_kernel_count(tl_engine* e) { return tl_decode_step_kernel_count_rows(e, 1); }
 
 int32_t tl_decode_step_kernel_count_rows(tl_engine* e, uint32_t n_seqs) {
   if (!e) return 0;
-  if (static_cast<int>(n_seqs) >= kTcMinRows) return 1 + 8 * e->L + 3 + 1;
+  // embed, 9 per layer, final norm, LM head with fused argmax, finalize
+  if (static_cast<int>(n_seqs) >= kTcMinRows) return 1 + 9 * e->L + 3;
+  if (n_seqs == 1 && e->use_decode1) return 2;  // persistent step + finalize
   return 1 + 5 * e->L + 2;
 }
 

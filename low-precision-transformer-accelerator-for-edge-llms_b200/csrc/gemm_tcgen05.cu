@@ -737,7 +737,9 @@ cudaError_t tc_read_error(unsigned int* code) {
     unsigned int zero = 0;
     return cudaMemcpyToSymbol(g_tc_error, &zero, sizeof(unsigned int));
   }
-  return attn_read_error(code);
+  e = attn_read_error(code);
+  if (e != cudaSuccess || *code) return e;
+  return decode1_read_error(code);
 }
 
 }  // namespace tl

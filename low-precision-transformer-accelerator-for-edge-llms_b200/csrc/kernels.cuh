@@ -99,6 +99,57 @@ int tc_pick_bn(int M);
 cudaError_t tc_read_error(unsigned int* code);
 int device_sm_count();
 
+// ---- persistent single-sequence decode step (decode1.cu)
+struct D1Layer {
+  const int8_t* wqkv;
+  const double* sqkv;
+  const int8_t* wo;
+  const double* so;
+  const int8_t* wgu;
+  const double* sgu;
+  const int8_t* wd;
+  const double* sd;
+  const float* g1;
+  const float* g2;
+};
+struct D1Args {
+  const D1Layer* layers = nullptr;     // device array [L]
+  int L = 0, D = 0, F = 0, H = 0, Hkv = 0, V = 0, P = 0, Nqkv = 0, Dq = 0;
+  float eps = 1e-5f;
+  NormPlan plan{8, 1};
+  const float* embed = nullptr;
+  const float* gfinal = nullptr;
+  const int8_t* wlm = nullptr;
+  const double* slm = nullptr;
+  int8_t* kc = nullptr;
+  int8_t* vc = nullptr;
+  const float* ks = nullptr;
+  const float* vs = nullptr;
+  const float* cos = nullptr;
+  const float* sin = nullptr;
+  float* x = nullptr;                  // [D] residual stream (row 0)
+  float* qkv = nullptr;
+  float* att = nullptr;
+  float* hid = nullptr;
+  const int* token = nullptr;
+  const int* pos = nullptr;
+  const int* slot = nullptr;
+  const int* active = nullptr;
+  float* part = nullptr;               // decode1_part_floats(Hkv, P)
+  unsigned int* sync = nullptr;        // [64] grid barrier (count [0], generation [32]), zeroed before every launch
+  unsigned long long* am_key = nullptr;  // [1], zero
+};
+bool decode1_supported(int D, int F, int Dq, int H, int Hkv, int P);
+size_t decode1_smem(int D, int F, int Dq);
+size_t decode1_part_floats(int Hkv, int P);
+cudaError_t decode1_prepare(int D, int F, int Dq);
+cudaError_t launch_decode1(const D1Args& a, int grid, cudaStream_t s);
+// Reads and clears the persistent step's error word; a nonzero code encodes
+// (wait kind) * 1e6 + CTA * 1e3 + warp; decode1_last_detail() gives the ring
+// chunk or barrier target of that wait.
+cudaError_t decode1_read_error(unsigned int* code);
+unsigned int decode1_last_detail();
+
 struct AttnDecodeArgs {
   const float* qkv = nullptr;   // [M][ld]; q at 0, k at H*64, v at H*64 + Hkv*64
   int ld = 0;
