@@ -59,7 +59,7 @@ constexpr int kD1Slot = 8192;                    // bytes per ring slot
 // would alias.
 constexpr int kD1Slots = 2 * kD1Consumers;       // 192 KB ring, two slots per warp
 static_assert(kD1Slots % kD1Consumers == 0, "slot reuse must stay within one warp");
-constexpr int kD1AttnChunk = 64;                 // positions per attention work item
+constexpr int kD1AttnChunk = 32;                 // positions per attention work item (<= 32: one per lane)
 // partial record per (kv head, query head, chunk): max, sum, 2 pad, 64 values
 // (272 bytes: the values start 16-byte aligned for vector loads)
 constexpr int kD1Rec = 68;
@@ -112,39 +112,44 @@ TL_DEV void d1_bulk(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
                ::"r"(d1_smem(dst)), "l"(src), "r"(bytes), "r"(d1_smem(bar))
                : "memory");
 }
+TL_DEV unsigned int ld_relaxed_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 TL_DEV unsigned int ld_acquire_u32(const unsigned int* p) {
   unsigned int v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 
-// Grid-wide barrier of the consumer warps of every CTA (sense reversal):
-// bar[0] counts arrivals, bar[32] (its own 128-byte line, so polling does not
-// contend with the arrivals) is the generation. Each CTA adds one arrival
-// with an acquire-release atomic; the last one resets the count and then
-// publishes the next generation with a release store, which the others poll
-// with acquire loads. The release/acquire chain orders every CTA's writes
-// before the barrier ahead of every read after it. Both words are zeroed
-// before the launch.
-TL_DEV void d1_grid_sync(unsigned int* bar, unsigned int& gen) {
+// Grid-wide barrier of the consumer warps of every CTA: a monotonic arrival
+// counter (zeroed before the launch). Each CTA adds its arrival with a
+// fire-and-forget release reduction, then polls the counter with relaxed
+// loads until it reaches (barriers so far) x (CTAs), and issues one acquire
+// fence. Release is cumulative over the writes the CTA's threads ordered
+// before it with the CTA barrier; the fence orders the other CTAs' writes
+// before every read after the closing CTA barrier. (Measured on B200 with
+// 148 CTAs: ~1.25 us per barrier, below an arrival counter plus a published
+// generation word, a hierarchical counter tree, or polled per-CTA flags.)
+TL_DEV void d1_grid_sync(unsigned int* counter, unsigned int& gen) {
   bar_cons();
+  const unsigned int next = gen + 1;
   if (threadIdx.x == 0) {
-    unsigned int prev;
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(bar) : "memory");
-    if (prev == gridDim.x - 1) {
-      asm volatile("st.relaxed.gpu.global.u32 [%0], 0;" ::"l"(bar) : "memory");
-      asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(bar + 32), "r"(gen + 1) : "memory");
-    } else if (!d1_failed()) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
+    if (!d1_failed()) {
+      const unsigned int target = next * gridDim.x;
       const long long t0 = clock64();
-      while (ld_acquire_u32(bar + 32) == gen) {
+      while (ld_relaxed_u32(counter) < target) {
         if (clock64() - t0 > kD1Wait) {
           d1_fail(5u, gen);
           break;
         }
       }
+      asm volatile("fence.acq_rel.gpu;" ::: "memory");
     }
   }
-  ++gen;
+  gen = next;
   bar_cons();
 }
 
@@ -218,6 +223,55 @@ TL_DEV float cons_sumsq(const float* v, NormPlan plan, float* part, float* leaf)
 // xf[0..K) <- src (written by other CTAs: L2 reads), optionally RMSNorm'd
 // with gamma; then xq <- quantize_int8 of it and sm.sx <- its scale.
 constexpr int kD1RowVec = 4;  // float4 per consumer thread: rows of up to 4 * 4 * 384 = 6144
+
+// named barrier of consumer warps 0..3 (the RMSNorm fast path)
+TL_DEV void bar_norm4() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
+
+// RMSNorm + INT8 quantization of a 2048-wide row (NumPy tree: 16 leaves of
+// 128) by consumer warps 0..3 alone: thread t owns accumulator t & 7 of leaf
+// t >> 3 and its 16 elements x[128 (t >> 3) + (t & 7) + 8 k] in registers;
+// the leaf folds ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) by XOR shuffles 1, 2,
+// 4, leaves pair up by shuffles 8 and 16, the four warp sums combine as
+// (w0+w1)+(w2+w3) -- block_sumsq_numpy's additions. Then normalize, max,
+// quantize into xq; the other warps only meet the closing barrier.
+TL_DEV void cons_norm_quant_d2048(const D1Smem& sm, const float* src, const float* gamma, float eps) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (warp < 4) {
+    const int base = (tid >> 3) * 128 + (tid & 7);
+    float v[16], gm[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      v[k] = __ldcg(src + base + 8 * k);
+      gm[k] = __ldg(gamma + base + 8 * k);
+    }
+    float acc = __fmul_rn(v[0], v[0]);
+#pragma unroll
+    for (int k = 1; k < 16; ++k) acc = __fadd_rn(acc, __fmul_rn(v[k], v[k]));
+#pragma unroll
+    for (int st = 1; st < 32; st *= 2) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, st));
+    if (lane == 0) sm.red[32 + warp] = acc;
+    bar_norm4();
+    const float tot = __fadd_rn(__fadd_rn(sm.red[32], sm.red[33]), __fadd_rn(sm.red[34], sm.red[35]));
+    const float mean = __fdiv_rn(tot, 2048.0f);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    float m = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      v[k] = __fmul_rn(__fmul_rn(v[k], inv), gm[k]);
+      m = fmaxf(m, fabsf(v[k]));
+    }
+    m = warp_max(m);
+    if (lane == 0) sm.red[36 + warp] = m;
+    bar_norm4();
+    m = fmaxf(fmaxf(sm.red[36], sm.red[37]), fmaxf(sm.red[38], sm.red[39]));
+    const double s64 = quant_scale64(m);
+    const float sf = static_cast<float>(s64);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) sm.xq[base + 8 * k] = static_cast<int8_t>(quantize_one(v[k], sf));
+    if (tid == 0) *sm.sx = s64;
+  }
+  bar_cons();
+}
 TL_DEV void cons_quant_regs(const D1Smem& sm, float4* v, int K);
 
 // xf[0..K) <- src (written by other CTAs: L2 reads), optionally RMSNorm'd
@@ -461,12 +515,11 @@ TL_DEV void d1_attention_item(const D1Args& a, int layer, int h, int c, const D1
   float* pm = sm.red;  // [8] max, [8..16) sum
   if (warp < G) {
     const int g = warp;
-    const float s0 = sc[g * 64 + lane], s1 = sc[g * 64 + lane + 32];
-    const float m = warp_max(fmaxf(s0, s1));
-    const float e0 = expf(s0 - m), e1 = expf(s1 - m);
-    sc[g * 64 + lane] = e0;
-    sc[g * 64 + lane + 32] = e1;
-    const float l = warp_sum(e0 + e1);
+    const float s0 = lane < kD1AttnChunk ? sc[g * 64 + lane] : -INFINITY;
+    const float m = warp_max(s0);
+    const float e0 = expf(s0 - m);
+    if (lane < kD1AttnChunk) sc[g * 64 + lane] = e0;
+    const float l = warp_sum(e0);
     if (lane == 0) {
       pm[g] = m;
       pm[8 + g] = l;
@@ -490,31 +543,14 @@ TL_DEV void d1_attention_item(const D1Args& a, int layer, int h, int c, const D1
 }
 
 // The O projection's input, merged from the attention partials by every CTA
-// (identical arithmetic everywhere): att[(h G + g) 64 + d] = (sum_c o_c e_c)
-// / (sum_c l_c e_c) * sV, e_c = exp(m_c - max_c m_c); then quantized into xq.
+// (identical arithmetic everywhere): for each query head and dimension the
+// chunks' (max, sum, P.V) are combined in chunk order, eight chunks per load
+// round, as att = (sum_c o_c e_c) / (sum_c l_c e_c) * sV with
+// e_c = exp(m_c - running max); then quantized into xq.
 TL_DEV void cons_merge_attn_quant(const D1Args& a, int layer, int nch, const D1Smem& sm) {
   const int tid = threadIdx.x;
   const int G = a.H / a.Hkv;
   const int maxch = (a.P + kD1AttnChunk - 1) / kD1AttnChunk;
-  float* ml = sm.xf;  // [H][nch][2]: chunk max, chunk sum; then [H][2]: max, total
-  for (int i = tid; i < a.H * nch; i += kD1ConsThreads) {
-    const int gq = i / nch, cc = i % nch;
-    const int h = gq / G, g = gq % G;
-    const float* pr = a.part + ((static_cast<size_t>(h) * 8 + g) * maxch + cc) * kD1Rec;
-    ml[2 * i] = __ldcg(pr);
-    ml[2 * i + 1] = __ldcg(pr + 1);
-  }
-  bar_cons();
-  float* mt = ml + 2 * a.H * nch;  // [H][2]
-  for (int gq = tid; gq < a.H; gq += kD1ConsThreads) {
-    float M = -INFINITY;
-    for (int cc = 0; cc < nch; ++cc) M = fmaxf(M, ml[2 * (gq * nch + cc)]);
-    float L = 0.0f;
-    for (int cc = 0; cc < nch; ++cc) L += ml[2 * (gq * nch + cc) + 1] * expf(ml[2 * (gq * nch + cc)] - M);
-    mt[2 * gq] = M;
-    mt[2 * gq + 1] = L;
-  }
-  bar_cons();
   float4 v[kD1RowVec];
   const int n4 = a.Dq >> 2;
 #pragma unroll
@@ -524,27 +560,42 @@ TL_DEV void cons_merge_attn_quant(const D1Args& a, int layer, int nch, const D1S
     if (qd >= n4) continue;
     const int gq = (qd * 4) >> 6, d = (qd * 4) & 63;
     const int h = gq / G, g = gq % G;
-    const float M = mt[2 * gq];
-    const float* pbase = a.part + (static_cast<size_t>(h) * 8 + g) * maxch * kD1Rec + kD1RecO + d;
+    const float* rec = a.part + (static_cast<size_t>(h) * 8 + g) * maxch * kD1Rec;
+    float M = -INFINITY, L = 0.0f;
     float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     for (int c0 = 0; c0 < nch; c0 += 8) {
+      float mv[8], lv[8];
       float4 ov[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        ov[j] = c0 + j < nch ? __ldcg(reinterpret_cast<const float4*>(pbase + (c0 + j) * kD1Rec))
-                             : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      for (int j = 0; j < 8; ++j) {
+        const float* r = rec + static_cast<size_t>(c0 + j) * kD1Rec;
+        const bool ok = c0 + j < nch;
+        mv[j] = ok ? __ldcg(r) : -INFINITY;
+        lv[j] = ok ? __ldcg(r + 1) : 0.0f;
+        ov[j] = ok ? __ldcg(reinterpret_cast<const float4*>(r + kD1RecO + d)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      }
+      float bm = M;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) bm = fmaxf(bm, mv[j]);
+      const float keep = expf(M - bm);  // 0 on the first batch (M = -inf)
+      L *= keep;
+      o.x *= keep;
+      o.y *= keep;
+      o.z *= keep;
+      o.w *= keep;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         if (c0 + j >= nch) continue;
-        const float f = expf(ml[2 * (gq * nch + c0 + j)] - M);
+        const float f = expf(mv[j] - bm);
+        L += lv[j] * f;
         o.x += ov[j].x * f;
         o.y += ov[j].y * f;
         o.z += ov[j].z * f;
         o.w += ov[j].w * f;
       }
+      M = bm;
     }
     const float sV = a.vs[(static_cast<size_t>(a.slot[0]) * a.L + layer) * a.Hkv + h];
-    const float L = mt[2 * gq + 1];
     v[u] = make_float4(o.x / L * sV, o.y / L * sV, o.z / L * sV, o.w / L * sV);
   }
   cons_quant_regs(sm, v, a.Dq);
@@ -643,12 +694,14 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode1_kernel(D1Args a) {
   }
   d1_grid_sync(a.sync, target);
 
+  const bool fast_norm = a.D == 2048 && a.plan.n_leaves == 16 && a.plan.leaf_len == 128;
   const int T = a.pos[0] + 1;
   const int nch = (T + kD1AttnChunk - 1) / kD1AttnChunk;
   const int items = a.Hkv * nch;
   for (int l = 0; l < a.L; ++l) {
     const D1Layer& ly = a.layers[l];
-    cons_load_quant(sm, a.x, a.D, ly.g1, a.eps, a.plan);
+    if (fast_norm) cons_norm_quant_d2048(sm, a.x, ly.g1, a.eps);
+    else cons_load_quant(sm, a.x, a.D, ly.g1, a.eps, a.plan);
     consume_matrix(ly.sqkv, D1_QKV, a.Nqkv, a.D, false);
     d1_grid_sync(a.sync, target);
     for (int w = blockIdx.x; w < items; w += gridDim.x) d1_attention_item(a, l, w / nch, w % nch, sm);
@@ -656,14 +709,16 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode1_kernel(D1Args a) {
     cons_merge_attn_quant(a, l, nch, sm);
     consume_matrix(ly.so, D1_O, a.D, a.Dq, false);
     d1_grid_sync(a.sync, target);
-    cons_load_quant(sm, a.x, a.D, ly.g2, a.eps, a.plan);
+    if (fast_norm) cons_norm_quant_d2048(sm, a.x, ly.g2, a.eps);
+    else cons_load_quant(sm, a.x, a.D, ly.g2, a.eps, a.plan);
     consume_matrix(ly.sgu, D1_GU, 2 * a.F, a.D, true);
     d1_grid_sync(a.sync, target);
     cons_load_quant(sm, a.hid, a.F, nullptr, a.eps, a.plan);
     consume_matrix(ly.sd, D1_DOWN, a.D, a.F, false);
     d1_grid_sync(a.sync, target);
   }
-  cons_load_quant(sm, a.x, a.D, a.gfinal, a.eps, a.plan);
+  if (fast_norm) cons_norm_quant_d2048(sm, a.x, a.gfinal, a.eps);
+  else cons_load_quant(sm, a.x, a.D, a.gfinal, a.eps, a.plan);
   consume_matrix(a.slm, D1_LM, a.V, a.D, false);
   bar_cons();
   if (tid == 0 && *sm.key) atomicMax(a.am_key, *sm.key);
@@ -684,13 +739,12 @@ size_t decode1_smem(int D, int F, int Dq) {
 }
 
 bool decode1_supported(int D, int F, int Dq, int H, int Hkv, int P) {
+  (void)P;
   const int row_max = kD1RowVec * 4 * kD1ConsThreads;  // row phases hold the row in registers
   const int K_max = std::max(std::max(D, F), Dq);
-  const int xf = std::max(K_max, 2 * 8 * 64 + 2 * kD1AttnChunk * 16);
-  const int maxch = (P + kD1AttnChunk - 1) / kD1AttnChunk;
-  return K_max <= kD1Slot && K_max <= row_max && H / Hkv <= 8 && D % 16 == 0 && F % 16 == 0 &&
-         (D + device_sm_count() - 1) / device_sm_count() <= kD1XOwn &&
-         Dq % 16 == 0 && 2 * H * maxch + 2 * H <= xf && decode1_smem(D, F, Dq) <= 227 * 1024;
+  return device_sm_count() <= 256 && K_max <= kD1Slot && K_max <= row_max && H / Hkv <= 8 && D % 16 == 0 &&
+         F % 16 == 0 && (D + device_sm_count() - 1) / device_sm_count() <= kD1XOwn && Dq % 16 == 0 &&
+         decode1_smem(D, F, Dq) <= 227 * 1024;
 }
 
 size_t decode1_part_floats(int Hkv, int P) {

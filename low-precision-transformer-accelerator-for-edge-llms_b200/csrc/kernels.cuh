@@ -136,7 +136,7 @@ struct D1Args {
   const int* slot = nullptr;
   const int* active = nullptr;
   float* part = nullptr;               // decode1_part_floats(Hkv, P)
-  unsigned int* sync = nullptr;        // [64] grid barrier (count [0], generation [32]), zeroed before every launch
+  unsigned int* sync = nullptr;        // [256] grid barrier flags (one per CTA), zeroed before every launch
   unsigned long long* am_key = nullptr;  // [1], zero
 };
 bool decode1_supported(int D, int F, int Dq, int H, int Hkv, int P);
