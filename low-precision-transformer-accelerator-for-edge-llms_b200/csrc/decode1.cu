@@ -153,6 +153,29 @@ TL_DEV void d1_grid_sync(unsigned int* counter, unsigned int& gen) {
   bar_cons();
 }
 
+// The same barrier in two halves, so that loads that do not depend on the
+// other CTAs' writes can be in flight while it completes.
+TL_DEV void d1_grid_arrive(unsigned int* counter) {
+  bar_cons();
+  if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
+}
+TL_DEV void d1_grid_wait(unsigned int* counter, unsigned int& gen) {
+  const unsigned int next = gen + 1;
+  if (threadIdx.x == 0 && !d1_failed()) {
+    const unsigned int target = next * gridDim.x;
+    const long long t0 = clock64();
+    while (ld_relaxed_u32(counter) < target) {
+      if (clock64() - t0 > kD1Wait) {
+        d1_fail(5u, gen);
+        break;
+      }
+    }
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+  }
+  gen = next;
+  bar_cons();
+}
+
 TL_DEV float silu_mul_d1(float g, float u) {
   const float c = fminf(fmaxf(g, -60.0f), 60.0f);
   const float den = __fadd_rn(1.0f, expf(-c));
@@ -432,7 +455,29 @@ TL_DEV void d1_rows(const D1Args& a, int mat, const int8_t* w, int r, int nr, do
 // issued up front: warps take the rotated queries and the cached K/V rows
 // while the last consumer warp RoPEs, quantizes and appends the new
 // position's K/V (written to the cache for running rows).
-TL_DEV void d1_attention_item(const D1Args& a, int layer, int h, int c, const D1Smem& sm) {
+// This thread's 16-byte piece of the item's cached K and V rows (row
+// tid / 4, piece tid % 4; positions other than the new one), loaded from HBM.
+struct D1KvPiece {
+  int4 k, v;
+};
+TL_DEV D1KvPiece d1_load_kv_piece(const D1Args& a, int layer, int h, int c) {
+  D1KvPiece r{make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0)};
+  const int tid = threadIdx.x;
+  if (tid >= kD1AttnChunk * 4) return r;
+  const int p = a.pos[0];
+  const int t0 = c * kD1AttnChunk;
+  const int n = min(kD1AttnChunk, p + 1 - t0);
+  const int row = tid >> 2, cc = tid & 3;
+  if (row < n && t0 + row != p) {
+    const size_t sidx = (static_cast<size_t>(a.slot[0]) * a.L + layer) * a.Hkv + h;
+    const size_t off = (sidx * a.P + t0 + row) * 64;
+    r.k = __ldcg(reinterpret_cast<const int4*>(a.kc + off) + cc);
+    r.v = __ldcg(reinterpret_cast<const int4*>(a.vc + off) + cc);
+  }
+  return r;
+}
+
+TL_DEV void d1_attention_item(const D1Args& a, int layer, int h, int c, const D1Smem& sm, const D1KvPiece& pre) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = a.H / a.Hkv;
   const int p = a.pos[0];
@@ -462,13 +507,8 @@ TL_DEV void d1_attention_item(const D1Args& a, int layer, int h, int c, const D1
   if (tid < kD1AttnChunk * 4) {
     const int r = tid >> 2, cc = tid & 3;
     if (t0 + r != p) {  // the new row is written by the append warp below
-      int4 kv = make_int4(0, 0, 0, 0), vv = make_int4(0, 0, 0, 0);
-      if (r < n) {
-        kv = __ldcg(reinterpret_cast<const int4*>(kbase + static_cast<size_t>(t0 + r) * 64) + cc);
-        vv = __ldcg(reinterpret_cast<const int4*>(vbase + static_cast<size_t>(t0 + r) * 64) + cc);
-      }
-      reinterpret_cast<int4*>(kb + r * 64)[cc] = kv;
-      reinterpret_cast<int4*>(vb + r * 64)[cc] = vv;
+      reinterpret_cast<int4*>(kb + r * 64)[cc] = pre.k;
+      reinterpret_cast<int4*>(vb + r * 64)[cc] = pre.v;
     }
   }
   if (warp == kD1Consumers - 1 && p >= t0 && p < t0 + n) {
@@ -703,8 +743,15 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode1_kernel(D1Args a) {
     if (fast_norm) cons_norm_quant_d2048(sm, a.x, ly.g1, a.eps);
     else cons_load_quant(sm, a.x, a.D, ly.g1, a.eps, a.plan);
     consume_matrix(ly.sqkv, D1_QKV, a.Nqkv, a.D, false);
-    d1_grid_sync(a.sync, target);
-    for (int w = blockIdx.x; w < items; w += gridDim.x) d1_attention_item(a, l, w / nch, w % nch, sm);
+    d1_grid_arrive(a.sync);
+    // the cached K/V rows of this CTA's first item stream in during the barrier
+    D1KvPiece pre{make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0)};
+    if (static_cast<int>(blockIdx.x) < items) pre = d1_load_kv_piece(a, l, blockIdx.x / nch, blockIdx.x % nch);
+    d1_grid_wait(a.sync, target);
+    for (int w = blockIdx.x; w < items; w += gridDim.x) {
+      if (w != static_cast<int>(blockIdx.x)) pre = d1_load_kv_piece(a, l, w / nch, w % nch);
+      d1_attention_item(a, l, w / nch, w % nch, sm, pre);
+    }
     d1_grid_sync(a.sync, target);
     cons_merge_attn_quant(a, l, nch, sm);
     consume_matrix(ly.so, D1_O, a.D, a.Dq, false);

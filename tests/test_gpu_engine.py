@@ -211,6 +211,27 @@ def test_long_prompts_multi_tile_prefill(pkg, gpu):
     eng.close()
 
 
+def test_single_sequence_long_context(pkg, gpu):
+    """Batch-1 decode (the persistent single-sequence step) past 256 cached
+    positions, where the attention partials of more than eight 32-position
+    chunks are merged in several load rounds: tokens and logits follow the
+    oracle; layer-0 KV bytes exact."""
+    qm = small_model(17, 2)
+    eng = pkg.Engine(qm.cfg, max_batch=1, max_prefill_tokens=320)
+    eng.load(to_engine_model(pkg, qm))
+    prompt = list(np.random.default_rng(18).integers(0, qm.cfg["vocab_size"], 300))
+    toks, st = eng.generate(prompt, 6)
+    ref, ref_logits, ora = oracle_generate(qm, prompt, 6)
+    assert st["generated_count"] == 6
+    assert tokens_match_modulo_ties(toks, ref, ref_logits), (toks, ref)
+    if toks == ref:
+        n = len(prompt) + len(ref) - 1
+        k, v, _, _ = eng.read_kv(0, n)
+        np.testing.assert_array_equal(k, ora.k_cache[0, :, :n])
+        np.testing.assert_array_equal(v, ora.v_cache[0, :, :n])
+    eng.close()
+
+
 def test_stop_contract(small):
     qm, eng = small
     prompt = list(np.random.default_rng(6).integers(0, qm.cfg["vocab_size"], 5))
