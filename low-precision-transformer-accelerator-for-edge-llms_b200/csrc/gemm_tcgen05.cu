@@ -385,6 +385,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         int v[16];
         tmem_ld16(lane_base + c * 16, v);
         unsigned long long key[16];
+        // when the 16 tokens share one absmax group (prefill: one sequence),
+        // the chunk's maximum is reduced in registers and across the warp
+        // and lands with one shared atomic per warp instead of one per element
+        const bool one_group = has_amax && mc / a.rows_per_group == (mc + 15) / a.rows_per_group;
+        float chunk_max = 0.0f;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int m = mc + j;
@@ -393,9 +398,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           key[j] = 0ull;
           if (n_ok && m < a.M) {
             const float mag = tc_store<EPI>(a, n, m, v[j], y, partner, rcur[j], cc);
-            if (has_amax) atomicMax(amax_sm + c * 16 + j, __float_as_uint(mag));
+            if (one_group) chunk_max = fmaxf(chunk_max, mag);
+            else if (has_amax) atomicMax(amax_sm + c * 16 + j, __float_as_uint(mag));
             if (EPI == EPI_F32) key[j] = argmax_key(y, n);
           }
+        }
+        if (one_group) {
+          chunk_max = warp_max(chunk_max);
+          if (lane == 0) atomicMax(amax_sm + c * 16, __float_as_uint(chunk_max));
         }
         if (EPI == EPI_F32 && has_key) {
           int tok;
@@ -649,10 +659,11 @@ cudaError_t prepare_tc_t() {
 
 // Ring depth: at most 4 stages (<= 96 KB for 64-token tiles), so two CTAs
 // fit on an SM and the next kernel's CTAs can start under programmatic
-// dependent launch.
+// dependent launch. Wide prefill tiles keep the ring at <= 100 KB as well:
+// with two CTAs per SM one CTA's epilogue runs under the other's main loop.
 int tc_max_stages(int bn) {
   const int stage = kABytes + bn * kTileK;
-  return std::max(2, std::min(4, (200 * 1024) / stage));
+  return std::max(2, std::min(4, (100 * 1024) / stage));
 }
 
 int tc_pick_bn(int M) {
