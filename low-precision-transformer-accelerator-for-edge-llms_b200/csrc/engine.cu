@@ -115,6 +115,7 @@ struct PrefillBufs {
   int n_seq_cap = 0;
   int* ids = nullptr;
   float *x = nullptr, *h = nullptr, *qkv = nullptr, *att = nullptr, *hid = nullptr;
+  float* inv = nullptr;       // [rows] per-row 1/rms of the two-pass prefill norm
   int8_t* xq = nullptr;
   float* amax = nullptr;     // [L][4][n_seq] + [n_seq] (final norm)
   float* kvamax = nullptr;   // [L][n_seq][2][Hkv]
@@ -273,10 +274,12 @@ tl_status ensure_prefill(tl_engine* e, size_t rows, int n_seq) {
   n_seq = std::max(n_seq, p.n_seq_cap);
   cudaFree(p.ids); cudaFree(p.x); cudaFree(p.h); cudaFree(p.qkv); cudaFree(p.att);
   cudaFree(p.hid); cudaFree(p.xq); cudaFree(p.amax); cudaFree(p.kvamax); cudaFree(p.acc32);
+  cudaFree(p.inv);
   p = PrefillBufs{};
   TL_TRY(dmalloc(&p.ids, rows));
   TL_TRY(dmalloc(&p.x, rows * e->D));
   TL_TRY(dmalloc(&p.h, rows * e->D));
+  TL_TRY(dmalloc(&p.inv, rows));
   TL_TRY(dmalloc(&p.qkv, rows * e->Nqkv));
   TL_TRY(dmalloc(&p.att, rows * e->Dq));
   TL_TRY(dmalloc(&p.hid, rows * e->F));
@@ -529,8 +532,7 @@ tl_status enqueue_prefill(tl_engine* e, int n_seq, int S, int slot_base, bool he
     float* am = p.amax + static_cast<size_t>(l) * 4 * n_seq;
     float* kva = p.kvamax + static_cast<size_t>(l) * n_seq * 2 * e->Hkv;
     // attention block
-    TL_CU(launch_rmsnorm_rows(p.x, ly.g1, eps, p.h, am, R, e->D, S, s));
-    TL_CU(launch_quantize_rows(p.h, am, R, e->D, S, p.xq, s));
+    TL_CU(launch_norm_quant_prefill(p.x, ly.g1, eps, R, e->D, S, p.inv, am, p.h, p.xq, s));
     TL_TRY(prefill_gemm(e, ly.wqkv, ly.sqkv, e->Nqkv, e->D, R, S, am, EPI_F32, p.qkv, nullptr, nullptr));
     TL_CU(launch_rope_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->cosT, e->sinT, kva, s));
     TL_CU(launch_kv_write_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, kva, e->kc, e->vc, e->ks, e->vs,
@@ -542,8 +544,7 @@ tl_status enqueue_prefill(tl_engine* e, int n_seq, int S, int slot_base, bool he
     if (tp) TL_TRY(tp_rowsplit_resid(e, ly.wo, ly.so, e->D, e->Dq, R, S, am + n_seq));
     else TL_TRY(prefill_gemm(e, ly.wo, ly.so, e->D, e->Dq, R, S, am + n_seq, EPI_RESID, p.x, p.x, nullptr));
     // feed-forward block
-    TL_CU(launch_rmsnorm_rows(p.x, ly.g2, eps, p.h, am + 2 * n_seq, R, e->D, S, s));
-    TL_CU(launch_quantize_rows(p.h, am + 2 * n_seq, R, e->D, S, p.xq, s));
+    TL_CU(launch_norm_quant_prefill(p.x, ly.g2, eps, R, e->D, S, p.inv, am + 2 * n_seq, p.h, p.xq, s));
     TL_TRY(prefill_gemm(e, ly.wgu, ly.sgu, 2 * e->F, e->D, R, S, am + 2 * n_seq, EPI_SILU, p.hid, nullptr,
                         am + 3 * n_seq));
     if (tp) TL_TRY(tp_allreduce_max(e, am + 3 * n_seq, n_seq));
@@ -815,7 +816,7 @@ tl_status tl_destroy(tl_engine* e) {
   cudaFree(d.d1_layers); cudaFree(d.d1_part); cudaFree(d.d1_sync);
   PrefillBufs& p = e->pf;
   cudaFree(p.ids); cudaFree(p.x); cudaFree(p.h); cudaFree(p.qkv); cudaFree(p.att); cudaFree(p.hid);
-  cudaFree(p.xq); cudaFree(p.amax); cudaFree(p.kvamax); cudaFree(p.acc32);
+  cudaFree(p.xq); cudaFree(p.amax); cudaFree(p.kvamax); cudaFree(p.acc32); cudaFree(p.inv);
   if (e->h_pinned) cudaFreeHost(e->h_pinned);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;

@@ -34,6 +34,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -553,6 +554,355 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
+// ------------------------------------------------ persistent wide-tile GEMM
+// Prefill-sized problems (M > 128 tokens, no split-K) run on a persistent
+// kernel: one CTA per SM walks the 128-channel x 256-token tiles
+// t = blockIdx.x, blockIdx.x + gridDim.x, ... (channel tile fastest, so the
+// CTAs in flight share token tiles in L2). Roles: warp 0 lane 0 streams A/B
+// k-blocks through a 4-stage ring (48 KB a stage) across tile boundaries;
+// warp 1 lane 0 issues the MMAs of tile i into TMEM accumulator i % 2 (two
+// 256-column buffers, all 512 columns); warps 2..9 drain accumulator i % 2
+// while tile i + 1 accumulates in the other, so the epilogue runs under the
+// main loop instead of after it. Epilogue warp w reads TMEM lanes
+// 32 (w % 4) .. + 31 (the lanes its warp rank may access) and tokens
+// 128 ((w - 2) / 4) .. + 127 of the tile. Handshakes: acc_full[b] (MMA
+// commit -> epilogue), acc_empty[b] (8 epilogue-warp arrivals -> MMA).
+constexpr int kPThreads = 320;
+constexpr int kPBN = 256;
+constexpr int kPStages = 4;
+constexpr int kPStage = kABytes + kPBN * kTileK;
+
+TL_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kPThreads, 1)
+    gemm_tcp_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, TcArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr bool kFloatEpi = EPI != EPI_I32 && EPI != EPI_REQ;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kPStages * kPStage);
+  uint64_t* empty = full + kPStages;
+  uint64_t* acc_full = empty + kPStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tiles = (a.N + kTileN - 1) / kTileN;
+  const int tiles = n_tiles * ((a.M + kPBN - 1) / kPBN);
+  const int nkb = (a.K + kTileK - 1) / kTileK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPStages; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full + b, 1);
+      mbar_init(acc_empty + b, 8);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_w)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_x)) : "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(2 * kPBN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      bool ok = true;
+      int it = 0;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int n0 = (t % n_tiles) * kTileN, m0 = (t / n_tiles) * kPBN;
+        int kb = 0;
+        if (t == static_cast<int>(blockIdx.x)) {
+          // weights do not depend on the previous kernel: the first ring's
+          // worth is requested before the grid-dependency wait
+          const int pre = min(kPStages, nkb);
+          for (int i = 0; i < pre; ++i) {
+            mbar_arrive_expect_tx(full + i, kPStage);
+            tma_load_2d(smem + i * kPStage, &tm_w, i * kTileK, n0, full + i);
+          }
+          pdl_wait();
+          for (int i = 0; i < pre; ++i)
+            tma_load_2d(smem + i * kPStage + kABytes, &tm_x, i * kTileK, m0, full + i);
+          kb = it = pre;
+        }
+        for (; kb < nkb; ++kb, ++it) {
+          const int s = it % kPStages, round = it / kPStages;
+          if (round > 0 && !(ok = mbar_wait(empty + s, (round - 1) & 1, 11u))) break;
+          mbar_arrive_expect_tx(full + s, kPStage);
+          tma_load_2d(smem + s * kPStage, &tm_w, kb * kTileK, n0, full + s);
+          tma_load_2d(smem + s * kPStage + kABytes, &tm_x, kb * kTileK, m0, full + s);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_i8(kTileN, kPBN);
+      bool ok = true;
+      int it = 0, i = 0;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++i) {
+        const int b = i & 1, u = i >> 1;
+        if (u > 0 && !(ok = mbar_wait(acc_empty + b, (u - 1) & 1, 12u))) break;
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(b * kPBN);
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % kPStages, round = it / kPStages;
+          if (!(ok = mbar_wait(full + s, round & 1, 13u))) break;
+          tc_fence_after();
+          const uint64_t ad = smem_desc_sw128(smem_u32(smem + s * kPStage));
+          const uint64_t bd = smem_desc_sw128(smem_u32(smem + s * kPStage + kABytes));
+#pragma unroll
+          for (int kk = 0; kk < kTileK / 32; ++kk)
+            mma_i8(d, ad + 2 * kk, bd + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(empty + s);
+        }
+        mma_commit(acc_full + b);  // arrives once this tile's MMAs have completed
+      }
+    }
+  } else {
+    // epilogue warps
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(half * 128);
+    const bool has_amax = kFloatEpi && a.out_absmax != nullptr;
+    pdl_wait();  // token scales and residuals come from the previous kernel
+    int i = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+      const int b = i & 1, u = i >> 1;
+      const int n0 = (t % n_tiles) * kTileN, m0 = (t / n_tiles) * kPBN + half * 128;
+      const int n = n0 + q * 32 + lane;
+      const bool n_ok = n < a.N;
+      double sw = 0.0;
+      uint32_t rq = 0u;
+      if (EPI == EPI_REQ) {
+        if (n_ok) rq = a.req_scale[a.req_per_col ? n : 0];
+      } else if (kFloatEpi) {
+        if (n_ok) sw = a.w_scale[n];
+      }
+      if (t + static_cast<int>(gridDim.x) >= tiles) pdl_launch_dependents();
+      float rcur[16], rnext[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) rcur[j] = rnext[j] = 0.0f;
+      if (EPI == EPI_RESID && n_ok) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (m0 + j < a.M) rcur[j] = a.resid[static_cast<size_t>(m0 + j) * a.N + n];
+      }
+      const bool ready = mbar_wait(acc_full + b, u & 1, 14u);
+      tc_fence_after();
+      if (!ready) break;
+      // chunks of 16 tokens this warp holds; a warp with none still releases
+      // the buffer (after the acc_full wait, so no arrival runs a phase ahead)
+      const int nch = a.M > m0 ? min(8, (a.M - m0 + 15) / 16) : 0;
+      if (nch == 0) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty + b);
+        continue;
+      }
+      // dequantization scale float32(sx * sw) of the current absmax group
+      int cur_g = -1;
+      float cur_s = 0.0f;
+      // running |output| maximum of group run_g (flushed when it changes)
+      int run_g = -1;
+      float run_max = 0.0f;
+#pragma unroll 1
+      for (int c = 0; c < nch; ++c) {
+        const int mc = m0 + c * 16;
+        if (EPI == EPI_RESID && n_ok && c + 1 < nch) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            rnext[j] = (mc + 16 + j < a.M) ? a.resid[static_cast<size_t>(mc + 16 + j) * a.N + n] : 0.0f;
+        }
+        int v[16];
+        tmem_ld16(lane_base + static_cast<uint32_t>(b * kPBN + c * 16), v);
+        if (c == nch - 1) {
+          // this warp's last read of accumulator b for this tile
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(acc_empty + b);
+        }
+        const int mlast = min(mc + 15, a.M - 1);
+        const int g0 = mc / a.rows_per_group, g1 = mlast / a.rows_per_group;
+        const bool one_group = g0 == g1;
+        float s[16];
+        if (kFloatEpi) {
+          if (one_group) {
+            if (g0 != cur_g) {
+              cur_g = g0;
+              const double sx = a.in_absmax ? quant_scale64(a.in_absmax[g0]) : 1.0;
+              cur_s = static_cast<float>(sx * sw);
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) s[j] = cur_s;
+          } else {
+            const int mj = mc + (lane & 15);
+            const double mine = (a.in_absmax && mj < a.M) ? quant_scale64(a.in_absmax[mj / a.rows_per_group]) : 1.0;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) s[j] = static_cast<float>(__shfl_sync(0xffffffffu, mine, j) * sw);
+          }
+        }
+        float mag[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) mag[j] = 0.0f;
+        if (EPI == EPI_SILU) {
+          // channel pairs (2p gate, 2p + 1 up) sit in adjacent lanes: the
+          // even lane finishes tokens 0..7 of the chunk, the odd lane 8..15
+          const bool odd = lane & 1;
+          float y[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) y[j] = __fmul_rn(__int2float_rn(v[j]), s[j]);
+          const int tok0 = odd ? 8 : 0;
+          const size_t ldo = static_cast<size_t>(a.N >> 1);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float r = __shfl_xor_sync(0xffffffffu, odd ? y[j] : y[8 + j], 1);
+            const float g = odd ? r : y[j];
+            const float up = odd ? y[8 + j] : r;
+            const int m = mc + tok0 + j;
+            if (n_ok && m < a.M) {
+              const float hv = silu_mul_tc(g, up);
+              a.out_f32[static_cast<size_t>(m) * ldo + (n >> 1)] = hv;
+              mag[j] = fabsf(hv);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int m = mc + j;
+            if (!n_ok || m >= a.M) continue;
+            const size_t o = static_cast<size_t>(m) * a.N + n;
+            if (EPI == EPI_I32) {
+              a.out_i32[o] = v[j];
+            } else if (EPI == EPI_REQ) {
+              a.out_i8[o] = static_cast<int8_t>(requant_q16(v[j], rq, a.req_nonneg != 0));
+            } else {
+              const float y = __fmul_rn(__int2float_rn(v[j]), s[j]);
+              if (EPI == EPI_RESID) {
+                const float r = __fadd_rn(rcur[j], y);
+                a.out_f32[o] = r;
+                mag[j] = fabsf(r);
+              } else {
+                if (a.out_f32) a.out_f32[o] = y;
+                mag[j] = fabsf(y);
+              }
+            }
+          }
+        }
+        if (has_amax) {
+          if (one_group) {
+            float cm = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) cm = fmaxf(cm, mag[j]);
+            if (g0 != run_g) {
+              if (run_g >= 0) {
+                const float wm = warp_max(run_max);
+                if (lane == 0 && wm > 0.0f) atomic_max_nonneg(a.out_absmax + run_g, wm);
+              }
+              run_g = g0;
+              run_max = 0.0f;
+            }
+            run_max = fmaxf(run_max, cm);
+          } else {
+            // rows of this chunk span several groups: one warp maximum per
+            // token (SiLU: mag[j] of an even lane is token j, of an odd lane
+            // token 8 + j)
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              float wm;
+              int m;
+              if (EPI == EPI_SILU) {
+                const bool mine = (j < 8) == ((lane & 1) == 0);
+                wm = warp_max(mine ? mag[j & 7] : 0.0f);
+                m = mc + j;
+              } else {
+                wm = warp_max(mag[j]);
+                m = mc + j;
+              }
+              if (lane == 0 && m < a.M && wm > 0.0f) atomic_max_nonneg(a.out_absmax + m / a.rows_per_group, wm);
+            }
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) rcur[j] = rnext[j];
+      }
+      if (has_amax && run_g >= 0) {
+        const float wm = warp_max(run_max);
+        if (lane == 0 && wm > 0.0f) atomic_max_nonneg(a.out_absmax + run_g, wm);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kPBN));
+  }
+}
+
+size_t tcp_smem() { return static_cast<size_t>(kPStages) * kPStage + 1024 + 8 * (2 * kPStages + 4) + 16; }
+
+template <int EPI>
+cudaError_t launch_tcp_e(const TcPlan& p, const TcArgs& a, cudaStream_t s, bool pdl) {
+  const int tiles = ((a.N + kTileN - 1) / kTileN) * ((a.M + kPBN - 1) / kPBN);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(std::min(tiles, device_sm_count()));
+  cfg.blockDim = dim3(kPThreads);
+  cfg.dynamicSmemBytes = tcp_smem();
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, gemm_tcp_kernel<EPI>, p.tm_w, p.tm_x, a);
+}
+
+cudaError_t launch_tcp(const TcPlan& p, const TcArgs& a, cudaStream_t s, bool pdl) {
+  switch (a.epi) {
+    case EPI_I32: return launch_tcp_e<EPI_I32>(p, a, s, pdl);
+    case EPI_F32: return launch_tcp_e<EPI_F32>(p, a, s, pdl);
+    case EPI_RESID: return launch_tcp_e<EPI_RESID>(p, a, s, pdl);
+    case EPI_SILU: return launch_tcp_e<EPI_SILU>(p, a, s, pdl);
+    case EPI_REQ: return launch_tcp_e<EPI_REQ>(p, a, s, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t prepare_tcp() {
+  const int smem = static_cast<int>(tcp_smem());
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(gemm_tcp_kernel<EPI_I32>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem))) return e;
+  if ((e = cudaFuncSetAttribute(gemm_tcp_kernel<EPI_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem))) return e;
+  if ((e = cudaFuncSetAttribute(gemm_tcp_kernel<EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem))) return e;
+  if ((e = cudaFuncSetAttribute(gemm_tcp_kernel<EPI_SILU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem))) return e;
+  return cudaFuncSetAttribute(gemm_tcp_kernel<EPI_REQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+}
+
+// The persistent kernel takes wide-tile problems without split-K and
+// without the fused argmax; TL_DISABLE_PERSISTENT_GEMM=1 keeps them on the
+// one-tile-per-CTA kernel (A/B comparisons).
+bool use_tcp(const TcPlan& p, const TcArgs& a) {
+  static const bool disabled = [] {
+    const char* v = std::getenv("TL_DISABLE_PERSISTENT_GEMM");
+    return v && v[0] == '1';
+  }();
+  return !disabled && p.bn == kPBN && p.k_splits == 1 && a.am_key == nullptr;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 cudaError_t get_encode() {
@@ -722,6 +1072,7 @@ cudaError_t launch_gemm_tc(const TcPlan& p, const TcArgs& a0, cudaStream_t s, bo
   a.k_splits = p.k_splits;
   a.stages = p.stages;
   if (a.epi == EPI_SILU && (a.N % 2)) return cudaErrorInvalidValue;
+  if (use_tcp(p, a)) return launch_tcp(p, a, s, pdl);
   switch (p.bn) {
     case 32: return launch_tc_t<32>(p, a, s, pdl);
     case 64: return launch_tc_t<64>(p, a, s, pdl);
@@ -736,7 +1087,8 @@ cudaError_t prepare_tc() {
   if ((e = prepare_tc_t<32>()) != cudaSuccess) return e;
   if ((e = prepare_tc_t<64>()) != cudaSuccess) return e;
   if ((e = prepare_tc_t<128>()) != cudaSuccess) return e;
-  return prepare_tc_t<256>();
+  if ((e = prepare_tc_t<256>()) != cudaSuccess) return e;
+  return prepare_tcp();
 }
 
 // Reads and clears the bounded-wait error words of the tcgen05 GEMM and of

@@ -574,18 +574,14 @@ __global__ void __launch_bounds__(256) norm_quant_rows_kernel(const float* x, co
 // (w0 + w1) + (w2 + w3) -- the same additions as the tree (float addition is
 // commutative, so which partner adds is immaterial). All row elements stay
 // in registers: one memory round trip, two CTA barriers.
-__global__ void __launch_bounds__(128) norm_quant_rows_d2048_kernel(const float* x, const float* gamma,
-                                                                     float eps, int8_t* out_q,
-                                                                     float* out_absmax) {
+// Loads thread t's 16 elements of a D = 2048 row (layout above), returns
+// the row's 1 / rms in every thread and leaves v[k] = x * inv * gamma with
+// gamma's elements `gm` (loaded by the caller, ahead of any dependency wait).
+// `red` is four floats of shared scratch; one CTA barrier.
+TL_DEV float d2048_norm_regs(const float* xrow, const float (&gm)[16], float eps, float (&v)[16], float* red) {
   constexpr int D = 2048;
-  __shared__ float red[2][4];
-  const int r = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  const int base = (t >> 3) * 128 + (t & 7);
-  float gm[16], v[16];
-#pragma unroll
-  for (int k = 0; k < 16; ++k) gm[k] = gamma[base + 8 * k];
-  pdl_wait();
-  const float* xr = x + static_cast<size_t>(r) * D + base;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const float* xr = xrow + (t >> 3) * 128 + (t & 7);
 #pragma unroll
   for (int k = 0; k < 16; ++k) v[k] = xr[8 * k];
   float acc = __fmul_rn(v[0], v[0]);
@@ -593,27 +589,118 @@ __global__ void __launch_bounds__(128) norm_quant_rows_d2048_kernel(const float*
   for (int k = 1; k < 16; ++k) acc = __fadd_rn(acc, __fmul_rn(v[k], v[k]));
 #pragma unroll
   for (int st = 1; st < 32; st *= 2) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, st));
-  if (lane == 0) red[0][warp] = acc;
+  if (lane == 0) red[warp] = acc;
   __syncthreads();
-  const float tot = __fadd_rn(__fadd_rn(red[0][0], red[0][1]), __fadd_rn(red[0][2], red[0][3]));
+  const float tot = __fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3]));
   const float mean = __fdiv_rn(tot, static_cast<float>(D));
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+#pragma unroll
+  for (int k = 0; k < 16; ++k) v[k] = __fmul_rn(__fmul_rn(v[k], inv), gm[k]);
+  return inv;
+}
+
+// Maximum of |v[k]| over the CTA's 128 threads (one CTA barrier).
+TL_DEV float d2048_absmax(const float (&v)[16], float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float m = 0.0f;
 #pragma unroll
-  for (int k = 0; k < 16; ++k) {
-    v[k] = __fmul_rn(__fmul_rn(v[k], inv), gm[k]);
-    m = fmaxf(m, fabsf(v[k]));
-  }
+  for (int k = 0; k < 16; ++k) m = fmaxf(m, fabsf(v[k]));
   m = warp_max(m);
-  if (lane == 0) red[1][warp] = m;
+  if (lane == 0) red[warp] = m;
   __syncthreads();
-  m = fmaxf(fmaxf(red[1][0], red[1][1]), fmaxf(red[1][2], red[1][3]));
+  return fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+}
+
+TL_DEV uint32_t quant_pack4(float4 v, float sf) {
+  return (static_cast<uint32_t>(quantize_one(v.x, sf)) & 0xffu) |
+         ((static_cast<uint32_t>(quantize_one(v.y, sf)) & 0xffu) << 8) |
+         ((static_cast<uint32_t>(quantize_one(v.z, sf)) & 0xffu) << 16) |
+         ((static_cast<uint32_t>(quantize_one(v.w, sf)) & 0xffu) << 24);
+}
+
+__global__ void __launch_bounds__(128) norm_quant_rows_d2048_kernel(const float* x, const float* gamma,
+                                                                     float eps, int8_t* out_q,
+                                                                     float* out_absmax) {
+  constexpr int D = 2048;
+  __shared__ float red[2][4];
+  const int r = blockIdx.x, t = threadIdx.x;
+  const int base = (t >> 3) * 128 + (t & 7);
+  float gm[16], v[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) gm[k] = gamma[base + 8 * k];
+  pdl_wait();
+  d2048_norm_regs(x + static_cast<size_t>(r) * D, gm, eps, v, red[0]);
+  const float m = d2048_absmax(v, red[1]);
   pdl_launch_dependents();
   const float sf = static_cast<float>(quant_scale64(m));
   int8_t* dst = out_q + static_cast<size_t>(r) * D + base;
 #pragma unroll
   for (int k = 0; k < 16; ++k) dst[8 * k] = static_cast<int8_t>(quantize_one(v[k], sf));
   if (t == 0) out_absmax[r] = m;
+}
+
+// Prefill RMSNorm + per-sequence INT8 quantization of D = 2048 rows in two
+// passes that never store the float normalized rows. Pass 1 evaluates each
+// row's 1 / rms (the tree above) and folds max |x * inv * gamma| into its
+// sequence's absmax; pass 2 recomputes the same two roundings from the same
+// x, inv and gamma (so the values are bit-identical) and quantizes them with
+// the sequence scale. Bytes: 8 KB read per row, then 8 KB read + 2 KB written.
+__global__ void __launch_bounds__(128) norm_stats_rows_d2048_kernel(const float* x, const float* gamma,
+                                                                     float eps, float* inv_out, float* absmax,
+                                                                     int rows_per_group) {
+  constexpr int D = 2048;
+  __shared__ float red[2][4];
+  const int r = blockIdx.x, t = threadIdx.x;
+  const int base = (t >> 3) * 128 + (t & 7);
+  float gm[16], v[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) gm[k] = gamma[base + 8 * k];
+  const float inv = d2048_norm_regs(x + static_cast<size_t>(r) * D, gm, eps, v, red[0]);
+  const float m = d2048_absmax(v, red[1]);
+  if (t == 0) {
+    inv_out[r] = inv;
+    atomic_max_nonneg(absmax + r / rows_per_group, m);
+  }
+}
+
+__global__ void __launch_bounds__(128) norm_quant_apply_d2048_kernel(const float* x, const float* gamma,
+                                                                      const float* inv, const float* absmax,
+                                                                      int rows_per_group, int8_t* out_q) {
+  constexpr int D = 2048;
+  const int r = blockIdx.x, t = threadIdx.x;
+  const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(r) * D);
+  float4 v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = src[t + 128 * i];
+  const float iv = inv[r];
+  const float sf = static_cast<float>(quant_scale64(absmax[r / rows_per_group]));
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  uint32_t* dst = reinterpret_cast<uint32_t*>(out_q + static_cast<size_t>(r) * D);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float4 g = g4[t + 128 * i];
+    float4 y;
+    y.x = __fmul_rn(__fmul_rn(v[i].x, iv), g.x);
+    y.y = __fmul_rn(__fmul_rn(v[i].y, iv), g.y);
+    y.z = __fmul_rn(__fmul_rn(v[i].z, iv), g.z);
+    y.w = __fmul_rn(__fmul_rn(v[i].w, iv), g.w);
+    dst[t + 128 * i] = quant_pack4(y, sf);
+  }
+}
+
+cudaError_t launch_norm_quant_prefill(const float* x, const float* gamma, float eps, int rows, int D,
+                                      int rows_per_group, float* inv_buf, float* absmax_groups, float* h_buf,
+                                      int8_t* out_q, cudaStream_t s) {
+  NormPlan plan;
+  if (!norm_plan(D, &plan) || D % 4) return cudaErrorInvalidValue;
+  if (D == 2048 && plan.n_leaves == 16 && plan.leaf_len == 128) {
+    norm_stats_rows_d2048_kernel<<<rows, 128, 0, s>>>(x, gamma, eps, inv_buf, absmax_groups, rows_per_group);
+    norm_quant_apply_d2048_kernel<<<rows, 128, 0, s>>>(x, gamma, inv_buf, absmax_groups, rows_per_group, out_q);
+    return cudaGetLastError();
+  }
+  cudaError_t e = launch_rmsnorm_rows(x, gamma, eps, h_buf, absmax_groups, rows, D, rows_per_group, s);
+  if (e != cudaSuccess) return e;
+  return launch_quantize_rows(h_buf, absmax_groups, rows, D, rows_per_group, out_q, s);
 }
 
 // Per-row INT8 quantization (quantize_int8 of model/tinyllama_gemm_int8.py:36-42
@@ -650,11 +737,7 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rows_reg_kernel(const flo
 #pragma unroll
   for (int i = 0; i < kQuantVec; ++i) {
     const int c = t + i * kQuantThreads;
-    if (c < n4)
-      dst[c] = (static_cast<uint32_t>(quantize_one(v[i].x, sf)) & 0xffu) |
-               ((static_cast<uint32_t>(quantize_one(v[i].y, sf)) & 0xffu) << 8) |
-               ((static_cast<uint32_t>(quantize_one(v[i].z, sf)) & 0xffu) << 16) |
-               ((static_cast<uint32_t>(quantize_one(v[i].w, sf)) & 0xffu) << 24);
+    if (c < n4) dst[c] = quant_pack4(v[i], sf);
   }
   if (t == 0) out_absmax[r] = m;
 }
@@ -760,9 +843,34 @@ __global__ void quantize_rows_kernel(const float* x, const float* absmax, int K,
   for (int i = threadIdx.x; i < K; i += blockDim.x) dst[i] = static_cast<int8_t>(quantize_one(src[i], sf));
 }
 
+// Same, for rows of K % 4 == 0 and K <= 8192: every load of the row is
+// issued before the first store (16-byte loads, 4-byte stores).
+__global__ void __launch_bounds__(kQuantThreads) quantize_rows_vec_kernel(const float* x, const float* absmax,
+                                                                          int K, int rows_per_group,
+                                                                          int8_t* out) {
+  const int r = blockIdx.x, t = threadIdx.x, n4 = K >> 2;
+  const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(r) * K);
+  float4 v[kQuantVec];
+#pragma unroll
+  for (int i = 0; i < kQuantVec; ++i) {
+    const int c = t + i * kQuantThreads;
+    v[i] = c < n4 ? src[c] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  }
+  const float sf = static_cast<float>(quant_scale64(absmax[r / rows_per_group]));
+  uint32_t* dst = reinterpret_cast<uint32_t*>(out + static_cast<size_t>(r) * K);
+#pragma unroll
+  for (int i = 0; i < kQuantVec; ++i) {
+    const int c = t + i * kQuantThreads;
+    if (c < n4) dst[c] = quant_pack4(v[i], sf);
+  }
+}
+
 cudaError_t launch_quantize_rows(const float* x, const float* absmax_groups, int rows, int K,
                                  int rows_per_group, int8_t* out, cudaStream_t s) {
-  quantize_rows_kernel<<<rows, 256, 0, s>>>(x, absmax_groups, K, rows_per_group, out);
+  if (K % 4 == 0 && K <= 4 * kQuantVec * kQuantThreads)
+    quantize_rows_vec_kernel<<<rows, kQuantThreads, 0, s>>>(x, absmax_groups, K, rows_per_group, out);
+  else
+    quantize_rows_kernel<<<rows, 256, 0, s>>>(x, absmax_groups, K, rows_per_group, out);
   return cudaGetLastError();
 }
 

@@ -183,6 +183,13 @@ cudaError_t launch_rmsnorm_rows(const float* x, const float* gamma, float eps, f
                                 cudaStream_t s);
 cudaError_t launch_quantize_rows(const float* x, const float* absmax_groups, int rows, int K,
                                  int rows_per_group, int8_t* out, cudaStream_t s);
+// Prefill RMSNorm + per-sequence INT8 quantization of x into out_q: for
+// D = 2048 two passes (row 1/rms into inv_buf [rows] and the sequence absmax,
+// then recompute + quantize; h_buf unused), else rmsnorm into h_buf then
+// quantize. absmax_groups must be zero on entry.
+cudaError_t launch_norm_quant_prefill(const float* x, const float* gamma, float eps, int rows, int D,
+                                      int rows_per_group, float* inv_buf, float* absmax_groups, float* h_buf,
+                                      int8_t* out_q, cudaStream_t s);
 cudaError_t launch_absmax_rows(const float* x, int rows, int K, int rows_per_group, float* absmax,
                                cudaStream_t s);
 // RoPE on q and k of qkv [rows][ld] in place (positions t = row % seq_len) and
