@@ -25,9 +25,11 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "tc_common.cuh"
 
 namespace tl {
 
@@ -727,6 +729,429 @@ __global__ void __launch_bounds__(128) attn_prefill_mma_kernel(
   }
 }
 
+// ------------------------------------------------- prefill on tcgen05
+// The same causal attention with the products on the 5th-generation tensor
+// cores. CTA = (128-query tile, q head, sequence); with S = kApfSplit key
+// slices per row, 32 (4 S + 4) threads:
+//   warps 0 .. 4S-1  softmax: warps w, w + 4, .. share query rows 32 (w % 4)
+//              .. + 31 (the TMEM lanes their warp rank may read); warp w
+//              takes key slice w / 4 of each 128-key tile (128 / S keys) and
+//              output dims (64 / S) (w / 4) ..; warps 0-3 also prepare Q;
+//   warp 4S    issues the MMAs (one thread);
+//   warps 4S+1 .. 4S+3  convert each tile's INT8 K rows (contiguous in the
+//              cache; every 16-byte load of a lane is issued before the
+//              first conversion) to fp16, the K-major B operand of
+//              S = Q.K^T, in two buffers (two tiles ahead of the MMAs);
+//   warps 4S+4 .. 4S+7  the same for V into its natural [key][dim] layout,
+//              the MN-major B operand of O = P.V (one buffer: V_j waits for
+//              PV_{j-1}, its loads do not).
+// Per key tile j: S_j = Q_hi.K^T + Q_lo.K^T (kind::f16, fp32 accumulate)
+// into TMEM columns 128 (j % 2) ..; each softmax thread reads its slice of
+// S_j once, the slices of a row exchange their maxima through shared
+// memory, and write P_j * 2^14 as fp16 hi + lo halves into shared-memory
+// buffer j % 2 (the A operand of P.V); P_j.V_j lands in TMEM columns
+// 256 + 64 (j % 2) and is folded into the fp32 registers of O two tiles
+// later, so no softmax step waits for the P.V it has just fed; the MMA
+// thread issues QK_{j+2} before PV_j (the softmax is the critical path).
+// The K / V loads and conversions start before Q is prepared (only QK_0
+// waits for it). Numerics are those of the mma.sync kernel above (exact fp16 K / V,
+// hi/lo Q and P, fp32 accumulation, base-2 online softmax).
+constexpr int kApfRows = 128;
+constexpr int kApfKeys = 128;
+constexpr int kApfSplit = 2;                       // key slices per row
+constexpr int kApfSoftWarps = 4 * kApfSplit;
+constexpr int kApfSliceKeys = kApfKeys / kApfSplit;  // 64
+constexpr int kApfSliceDims = 64 / kApfSplit;        // 32
+constexpr int kApfConvK = 3, kApfConvV = 4;        // converter warps per operand
+constexpr int kApfThreads = 32 * (kApfSoftWarps + 1 + kApfConvK + kApfConvV);
+constexpr int kApfWarpMma = kApfSoftWarps, kApfWarpConvK = kApfSoftWarps + 1;
+constexpr int kApfOffQHi = 0;          // [128 rows][64 dims] fp16, SW128 K-major (16 KB)
+constexpr int kApfOffQLo = 16384;
+constexpr int kApfOffK = 32768;        // [2 bufs][128 keys][64 dims] fp16, SW128 K-major
+constexpr int kApfOffV = 65536;        // [128 keys][64 dims] fp16, SW128 MN-major
+constexpr int kApfOffP = 81920;        // [2 bufs][hi | lo][2 key blocks][128 rows][64 keys] fp16, SW128
+constexpr int kApfPBuf = 65536;
+constexpr int kApfOffXch = 212992;     // floats: [2 tiles][S][128] row maxima, [S][128] l, [128] scale
+constexpr int kApfOffBar = kApfOffXch + (3 * kApfSplit * 128 + 128) * 4;
+constexpr size_t kApfSmem = kApfOffBar + 256 + 1024;
+constexpr uint32_t kApfTmemCols = 512;  // S x 2 (256) + O tile x 2 (128), rounded up
+
+__device__ unsigned int g_apf_error = 0;
+
+// TL_DISABLE_TC_ATTN_PREFILL=1 keeps prefill attention on the mma.sync
+// kernel (A/B comparisons).
+bool use_apf_tc() {
+  static const bool disabled = [] {
+    const char* v = std::getenv("TL_DISABLE_TC_ATTN_PREFILL");
+    return v && v[0] == '1';
+  }();
+  return !disabled;
+}
+TL_DEV bool apf_wait(uint64_t* bar, uint32_t parity, unsigned code) {
+  return mbar_wait_err(bar, parity, code, &g_apf_error);
+}
+// MN-major SW128 operand whose MN extent is one 128-byte swizzle row: both
+// offsets = 1024 B (the 8-row group stride along K; the MN-direction
+// stride is never used).
+TL_DEV uint64_t smem_desc_sw128_mn(uint32_t addr) {
+  return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (64ull << 16) | (64ull << 32) | (1ull << 46) |
+         (2ull << 61);
+}
+// fp32 pair -> fp16 hi (x rounded to 11 significant bits in the integer
+// domain: half an ulp added to the magnitude bits, the 13 low mantissa bits
+// cleared; exactly representable in fp16) and fp16 lo (the exact fp32
+// remainder, |lo| <= ulp / 2, rounded): two packed conversions per pair,
+// ~22 bits kept, like split2.
+TL_DEV float round11(float x) { return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u); }
+TL_DEV void split2_fast(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const float h0 = round11(x0), h1 = round11(x1);
+  hi = pack2(h0, h1);
+  lo = pack2(x0 - h0, x1 - h1);
+}
+// A converter thread's share of one 128-row INT8 tile (64-byte rows): the
+// 16-byte chunks t, t + T, .. (T = threads converting this operand, at most
+// six each); rows >= `rows` read as zero (the cache's last position).
+constexpr int kApfConvMax = 6;
+struct ApfChunks {
+  uint4 w[kApfConvMax];
+};
+TL_DEV void apf_load_rows(const unsigned char* src, int t, int T, int rows, ApfChunks& c) {
+#pragma unroll
+  for (int i = 0; i < kApfConvMax; ++i) {
+    const int unit = t + T * i, r = unit >> 2;
+    c.w[i] = (unit < 512 && r < rows) ? __ldg(reinterpret_cast<const uint4*>(src + unit * 16)) : make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+// ... converted to fp16 rows SW128: each 16-byte chunk (16 values) becomes
+// two swizzled 16-byte chunks.
+TL_DEV void apf_store_rows(unsigned char* dst, int t, int T, const ApfChunks& c) {
+#pragma unroll
+  for (int i = 0; i < kApfConvMax; ++i) {
+    const int unit = t + T * i, r = unit >> 2, k = unit & 3;
+    if (unit >= 512) break;
+    uint4 a, e;
+    i8x4_to_h2x2(c.w[i].x, a.x, a.y);
+    i8x4_to_h2x2(c.w[i].y, a.z, a.w);
+    i8x4_to_h2x2(c.w[i].z, e.x, e.y);
+    i8x4_to_h2x2(c.w[i].w, e.z, e.w);
+    *reinterpret_cast<uint4*>(dst + sw128_offset(r, 2 * k)) = a;
+    *reinterpret_cast<uint4*>(dst + sw128_offset(r, 2 * k + 1)) = e;
+  }
+}
+
+__global__ void __launch_bounds__(kApfThreads, 1) attn_prefill_tc_kernel(
+    const float* __restrict__ qkv, int ld, int seq_len, int H, int Hkv, const int8_t* __restrict__ kc,
+    const int8_t* __restrict__ vc, const float* __restrict__ ks, const float* __restrict__ vs, int slot_base,
+    int layer, int L, int P, float* __restrict__ out, float* __restrict__ out_absmax) {
+  extern __shared__ __align__(1024) unsigned char apf_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(apf_raw) + 1023) & ~uintptr_t(1023));
+  float* xmax = reinterpret_cast<float*>(sm + kApfOffXch);   // [2 tiles][S][128]
+  float* xl = xmax + 2 * kApfSplit * 128;                      // [S][128] final l
+  float* xsc = xl + kApfSplit * 128;                           // [128] row score scales
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kApfOffBar);
+  uint64_t* k_full = bar + 0;       // [2] fp16 K operand of tile j written to buffer j % 2
+  uint64_t* k_free = bar + 2;       // [2] S MMAs reading buffer j % 2 completed
+  uint64_t* v_full = bar + 6;       // fp16 V operand written
+  uint64_t* v_free = bar + 7;       // P.V MMAs reading it completed
+  uint64_t* s_full = bar + 8;       // [2] S_j in TMEM
+  uint64_t* s_free = bar + 10;      // [2] the softmax warps have read S_j
+  uint64_t* p_full = bar + 12;      // [2] P_j written to buffer j % 2
+  uint64_t* o_full = bar + 14;      // [2] P_j.V_j in TMEM; P buffer j % 2 no longer read
+  uint64_t* xbar = bar + 16;        // [4] the softmax warps of rows 32 q .. exchanged values
+  uint64_t* q_full = bar + 20;      // Q operands and row scales written (warps 0-3)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 21);
+
+  const int qt = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);  // longest rows first
+  const int head = blockIdx.y, seq = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int h = head / (H / Hkv);
+  const int Dq = H * 64;
+  const int q0 = qt * kApfRows;
+  const int n_kt = qt + 1;  // key tiles 0..qt cover positions 0..q0 + 127
+  const size_t sidx = (static_cast<size_t>(slot_base + seq) * L + layer) * Hkv + h;
+
+  if (tid == 0) {
+    for (int i = 0; i < 8; ++i) mbar_init(bar + i, 1);
+    for (int i = 0; i < 2; ++i) mbar_init(k_full + i, kApfConvK);
+    mbar_init(v_full, kApfConvV);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(s_full + i, 1);
+      mbar_init(s_free + i, kApfSoftWarps);
+      mbar_init(p_full + i, kApfSoftWarps);
+      mbar_init(o_full + i, 1);
+    }
+    for (int i = 0; i < 4; ++i) mbar_init(xbar + i, 32 * kApfSplit);
+    mbar_init(q_full, 4);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kApfWarpMma) tmem_alloc(tmem_slot, kApfTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == kApfWarpMma) {
+    if (lane == 0) {
+      constexpr uint32_t id_s = idesc_f16(kApfRows, kApfKeys);
+      constexpr uint32_t id_o = idesc_f16(kApfRows, 64) | (1u << 16);  // B (V) MN-major
+      // descriptor start fields advance in 16-byte units: +2 per 32-byte K
+      // step, +1024 per 16 KB key block, +128 per 2 KB (16 MN-major V rows)
+      const uint64_t dqh = smem_desc_sw128(smem_u32(sm + kApfOffQHi));
+      const uint64_t dql = smem_desc_sw128(smem_u32(sm + kApfOffQLo));
+      const uint64_t dk0 = smem_desc_sw128(smem_u32(sm + kApfOffK));
+      const uint64_t dv = smem_desc_sw128_mn(smem_u32(sm + kApfOffV));
+      const uint64_t dp = smem_desc_sw128(smem_u32(sm + kApfOffP));
+      bool ok = apf_wait(q_full, 0, 20u);
+      auto issue_qk = [&](int j) -> bool {
+        const int b = j & 1, u = j >> 1;
+        if (!apf_wait(k_full + b, u & 1, 22u)) return false;
+        if (u > 0 && !apf_wait(s_free + b, (u - 1) & 1, 23u)) return false;
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(b * kApfKeys);
+        const uint64_t dk = dk0 + static_cast<uint64_t>(b * 1024);  // + 16 KB
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          mma_f16(d, dqh + 2 * kk, dk + 2 * kk, id_s, kk > 0 ? 1u : 0u);
+          mma_f16(d, dql + 2 * kk, dk + 2 * kk, id_s, 1u);
+        }
+        mma_commit(s_full + b);
+        mma_commit(k_free + b);
+        return true;
+      };
+      auto issue_pv = [&](int j) -> bool {
+        const int b = j & 1, u = j >> 1;
+        if (!apf_wait(p_full + b, u & 1, 24u)) return false;
+        if (!apf_wait(v_full, j & 1, 25u)) return false;
+        tc_fence_after();
+        const uint32_t d = tmem + 256u + static_cast<uint32_t>(64 * b);
+        const uint64_t pbuf = dp + static_cast<uint64_t>(b * (kApfPBuf >> 4));
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t dph = pbuf + (kk >> 2) * 1024 + (kk & 3) * 2;
+          mma_f16(d, dph, dv + kk * 128, id_o, kk > 0 ? 1u : 0u);
+          mma_f16(d, dph + 2048, dv + kk * 128, id_o, 1u);  // lo halves: +32 KB
+        }
+        mma_commit(o_full + b);
+        mma_commit(v_free);
+        return true;
+      };
+      if (ok) ok = issue_qk(0);
+      if (ok && n_kt > 1) ok = issue_qk(1);
+      for (int j = 0; j < n_kt && ok; ++j) {
+        if (j + 2 < n_kt) ok = issue_qk(j + 2);
+        if (ok) ok = issue_pv(j);
+      }
+    }
+  } else if (warp >= kApfWarpConvK) {
+    // K: tile j into buffer j % 2 once QK_{j-2} (its last reader) completed;
+    // V: tile j once PV_{j-1} completed. The tile's loads go first.
+    const bool is_v = warp >= kApfWarpConvK + kApfConvK;
+    const int T = 32 * (is_v ? kApfConvV : kApfConvK);
+    const int ct = tid - 32 * (is_v ? kApfWarpConvK + kApfConvK : kApfWarpConvK);
+    const unsigned char* rows =
+        reinterpret_cast<const unsigned char*>(is_v ? vc : kc) + sidx * static_cast<size_t>(P) * 64;
+    for (int j = 0; j < n_kt; ++j) {
+      const int b = j & 1, u = j >> 1;
+      const int kv0 = j * kApfKeys;
+      ApfChunks c;
+      apf_load_rows(rows + static_cast<size_t>(kv0) * 64, ct, T, min(kApfKeys, P - kv0), c);
+      if (is_v) {
+        if (j > 0 && !apf_wait(v_free, (j - 1) & 1, 27u)) break;
+        apf_store_rows(sm + kApfOffV, ct, T, c);
+      } else {
+        if (u > 0 && !apf_wait(k_free + b, (u - 1) & 1, 26u)) break;
+        apf_store_rows(sm + kApfOffK + b * 16384, ct, T, c);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(is_v ? v_full : k_full + b);
+    }
+  } else {
+    if (warp < 4) {
+      // row tid's query -> power-of-two scaled fp16 hi/lo operands
+      const int t = q0 + tid;
+      const bool ok = t < seq_len;
+      // (two passes over the row, the second from L1: max |q|, then the
+      // scaled halves eight dims at a time)
+      const float* q = qkv + static_cast<size_t>(seq * seq_len + (ok ? t : 0)) * ld + head * 64;
+      float mx = 0.0f;
+#pragma unroll
+      for (int d = 0; d < 64; d += 2) {
+        const float2 x = *reinterpret_cast<const float2*>(q + d);
+        mx = fmaxf(mx, fmaxf(fabsf(x.x), fabsf(x.y)));
+      }
+      if (!ok) mx = 0.0f;
+      const float qs = pow2_scale(mx);
+      xsc[tid] = ks[sidx] * 0.125f / qs * kLog2e;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        float qv[8];
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+          const float2 x = *reinterpret_cast<const float2*>(q + 8 * c + i);
+          qv[i] = ok ? x.x : 0.0f;
+          qv[i + 1] = ok ? x.y : 0.0f;
+        }
+        uint4 hi, lo;
+        split2_fast(qv[0] * qs, qv[1] * qs, hi.x, lo.x);
+        split2_fast(qv[2] * qs, qv[3] * qs, hi.y, lo.y);
+        split2_fast(qv[4] * qs, qv[5] * qs, hi.z, lo.z);
+        split2_fast(qv[6] * qs, qv[7] * qs, hi.w, lo.w);
+        const uint32_t off = sw128_offset(tid, c);
+        *reinterpret_cast<uint4*>(sm + kApfOffQHi + off) = hi;
+        *reinterpret_cast<uint4*>(sm + kApfOffQLo + off) = lo;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_full);
+    }
+    // softmax warps: row r, key slice ks_ (keys kApfSliceKeys ks_ ..), dims kApfSliceDims ks_ ..
+    const int qq = warp & 3, ks_ = warp >> 2;
+    const int r = qq * 32 + lane, t = q0 + r;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(qq * 32) << 16);
+    float m2 = -INFINITY, l = 0.0f;  // running max (log2 units), running sum of p * 2^14 (this slice)
+    float c_prev = 1.0f;             // correction of the previous tile (m_{j-2} -> m_{j-1})
+    uint32_t xph = 0;                // phases of xbar[qq] completed so far
+    float o[kApfSliceDims];
+#pragma unroll
+    for (int i = 0; i < kApfSliceDims; ++i) o[i] = 0.0f;
+    auto fold = [&](int jj, float scale) -> bool {
+      // o += scale * (P_jj . V_jj) for this slice's dims
+      if (!apf_wait(o_full + (jj & 1), (jj >> 1) & 1, 30u)) return false;
+      tc_fence_after();
+#pragma unroll
+      for (int hh = 0; hh < kApfSliceDims / 16; ++hh) {
+        int w[16];
+        tmem_ld16(lane_base + 256u + static_cast<uint32_t>(64 * (jj & 1) + kApfSliceDims * ks_ + 16 * hh), w);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[16 * hh + i] = fmaf(__int_as_float(w[i]), scale, o[16 * hh + i]);
+      }
+      return true;
+    };
+    bool ok = apf_wait(q_full, 0, 28u);  // the row scales in xsc
+    const float sc2 = xsc[r];
+    for (int j = 0; j < n_kt && ok; ++j) {
+      const int b = j & 1, u = j >> 1;
+      if (!(ok = apf_wait(s_full + b, u & 1, 29u))) break;
+      tc_fence_after();
+      const bool diag = j == qt;
+      const int lim = t - j * kApfKeys - kApfSliceKeys * ks_;  // keys k > lim of this slice are masked
+      const uint32_t sb = lane_base + static_cast<uint32_t>(b * kApfKeys + kApfSliceKeys * ks_);
+      // row maximum of the raw scores (the scale is positive), 32 columns at
+      // a time in 8-way trees, then across the row's slices through shared
+      // memory (double-buffered by tile parity: a warp writes buffer b again
+      // only after every partner's arrival for tile j + 1, which follows its
+      // read of tile j)
+      float mraw = -INFINITY;
+#pragma unroll
+      for (int cc = 0; cc < kApfSliceKeys / 32; ++cc) {
+        uint32_t v[32];
+        tmem_ld32(sb + 32 * cc, v);
+        if (diag) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (32 * cc + i > lim) v[i] = __float_as_uint(-INFINITY);
+        }
+        float mq[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          mq[i] = fmaxf(fmaxf(__uint_as_float(v[i]), __uint_as_float(v[i + 8])),
+                        fmaxf(__uint_as_float(v[i + 16]), __uint_as_float(v[i + 24])));
+        mraw = fmaxf(mraw, fmaxf(fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])),
+                                 fmaxf(fmaxf(mq[4], mq[5]), fmaxf(mq[6], mq[7]))));
+      }
+      xmax[(b * kApfSplit + ks_) * 128 + r] = mraw;
+      mbar_arrive(xbar + qq);
+      if (!(ok = apf_wait(xbar + qq, xph & 1, 32u))) break;
+      ++xph;
+      mraw = xmax[(b * kApfSplit) * 128 + r];
+#pragma unroll
+      for (int k = 1; k < kApfSplit; ++k) mraw = fmaxf(mraw, xmax[(b * kApfSplit + k) * 128 + r]);
+      const float m_new = fmaxf(m2, mraw * sc2);
+      const float corr = ex2f(m2 - m_new);
+      m2 = m_new;
+      // o holds tiles <= j - 3 at max m_{j-1}; P_{j-2}.V_{j-2} is at m_{j-2}.
+      // Its completion also frees P buffer b for P_j.
+#pragma unroll
+      for (int i = 0; i < kApfSliceDims; ++i) o[i] *= corr;
+      if (j >= 2 && !(ok = fold(j - 2, c_prev * corr))) break;
+      c_prev = corr;
+      // p * 2^14 = 2^(s * sc2 - m + 14) (masked scores are -inf: p = 0) as
+      // fp16 hi + lo into this slice's chunks of P buffer b; l sums the p in
+      // an 8-way tree
+      const float off14 = 14.0f - m_new;
+      float lq[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) lq[i] = 0.0f;
+      unsigned char* pb = sm + kApfOffP + b * kApfPBuf;
+#pragma unroll
+      for (int cc = 0; cc < kApfSliceKeys / 32; ++cc) {
+        uint32_t v[32];
+        tmem_ld32(sb + 32 * cc, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const bool live = !diag || 32 * cc + i <= lim;
+          const float p = live ? ex2f(fmaf(__uint_as_float(v[i]), sc2, off14)) : 0.0f;
+          v[i] = __float_as_uint(p);
+          lq[i & 7] += p;
+        }
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          uint4 hi, lo;
+          split2_fast(__uint_as_float(v[8 * g + 0]), __uint_as_float(v[8 * g + 1]), hi.x, lo.x);
+          split2_fast(__uint_as_float(v[8 * g + 2]), __uint_as_float(v[8 * g + 3]), hi.y, lo.y);
+          split2_fast(__uint_as_float(v[8 * g + 4]), __uint_as_float(v[8 * g + 5]), hi.z, lo.z);
+          split2_fast(__uint_as_float(v[8 * g + 6]), __uint_as_float(v[8 * g + 7]), hi.w, lo.w);
+          const int key = kApfSliceKeys * ks_ + 32 * cc + 8 * g;
+          const uint32_t off = static_cast<uint32_t>((key >> 6) * 16384) + sw128_offset(r, (key & 63) >> 3);
+          *reinterpret_cast<uint4*>(pb + off) = hi;
+          *reinterpret_cast<uint4*>(pb + 32768 + off) = lo;
+        }
+      }
+      l = fmaf(l, corr, ((lq[0] + lq[1]) + (lq[2] + lq[3])) + ((lq[4] + lq[5]) + (lq[6] + lq[7])));
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(s_free + b);
+        mbar_arrive(p_full + b);
+      }
+    }
+    // the last two tiles' P.V: P_{J-1}.V_{J-1} at m_{J-1} (scaled by the last
+    // correction), P_J.V_J at the final maximum
+    const int J = n_kt - 1;
+    if (ok && J >= 1) ok = fold(J - 1, c_prev);
+    if (ok) ok = fold(J, 1.0f);
+    if (ok) {
+      // the row's l is the sum of its slices' (same running maximum)
+      xl[ks_ * 128 + r] = l;
+      mbar_arrive(xbar + qq);
+      const bool got = apf_wait(xbar + qq, xph & 1, 33u);
+      float lt = xl[r];
+#pragma unroll
+      for (int k = 1; k < kApfSplit; ++k) lt += xl[k * 128 + r];
+      float local_max = 0.0f;
+      if (got && t < seq_len) {
+        const float inv = vs[sidx] / lt;
+        float* orow = out + static_cast<size_t>(seq * seq_len + t) * Dq + head * 64 + kApfSliceDims * ks_;
+#pragma unroll
+        for (int d = 0; d < kApfSliceDims; d += 4) {
+          const float4 y = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
+          *reinterpret_cast<float4*>(orow + d) = y;
+          local_max = fmaxf(local_max, fmaxf(fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w))));
+        }
+      }
+      if (out_absmax) {
+        local_max = warp_max(local_max);
+        if (lane == 0) atomic_max_nonneg(out_absmax + seq, local_max);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kApfWarpMma) tmem_free(tmem, kApfTmemCols);
+}
+
 }  // namespace
 
 cudaError_t launch_attn_prefill(const float* qkv, int ld, int rows, int seq_len, int H, int Hkv,
@@ -735,6 +1160,13 @@ cudaError_t launch_attn_prefill(const float* qkv, int ld, int rows, int seq_len,
                                 float* out, float* out_absmax, cudaStream_t s) {
   if (seq_len <= 0 || rows % seq_len || H % Hkv || (ld & 1)) return cudaErrorInvalidValue;
   const int nseq = rows / seq_len;
+  if (use_apf_tc() && (reinterpret_cast<uintptr_t>(out) & 15u) == 0) {
+    // (its float4 output stores need 16-byte aligned rows; Dq is a multiple of 64)
+    dim3 grid((seq_len + kApfRows - 1) / kApfRows, H, nseq);
+    attn_prefill_tc_kernel<<<grid, kApfThreads, kApfSmem, s>>>(qkv, ld, seq_len, H, Hkv, kc, vc, ks, vs,
+                                                                slot_base, layer, L, P, out, out_absmax);
+    return cudaGetLastError();
+  }
   dim3 grid((seq_len + kPfQTile - 1) / kPfQTile, H, nseq);
   attn_prefill_mma_kernel<<<grid, 128, 0, s>>>(qkv, ld, seq_len, H, Hkv, kc, vc, ks, vs, slot_base, layer,
                                                L, P, out, out_absmax);
@@ -754,16 +1186,21 @@ int attn_splits(int M, int Hkv, int P) {
 }
 
 cudaError_t attn_prepare() {
-  return cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(kDecSmem));
+  cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(kDecSmem));
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(attn_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(kApfSmem));
 }
 
 cudaError_t attn_read_error(unsigned int* code) {
-  cudaError_t e = cudaMemcpyFromSymbol(code, g_attn_error, sizeof(unsigned int));
-  if (e != cudaSuccess) return e;
-  if (*code) {
-    unsigned int zero = 0;
-    return cudaMemcpyToSymbol(g_attn_error, &zero, sizeof(unsigned int));
+  for (const void* sym : {static_cast<const void*>(&g_attn_error), static_cast<const void*>(&g_apf_error)}) {
+    cudaError_t e = cudaMemcpyFromSymbol(code, sym, sizeof(unsigned int));
+    if (e != cudaSuccess) return e;
+    if (*code) {
+      unsigned int zero = 0;
+      return cudaMemcpyToSymbol(sym, &zero, sizeof(unsigned int));
+    }
   }
   return cudaSuccess;
 }

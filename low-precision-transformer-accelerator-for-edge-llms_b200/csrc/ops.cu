@@ -219,6 +219,7 @@ tl_status tl_attn_prefill(const float* qkv, int32_t seq_len, int32_t n_seqs, con
   if (reinterpret_cast<uintptr_t>(qkv) & 7u || reinterpret_cast<uintptr_t>(out) & 7u ||
       reinterpret_cast<uintptr_t>(kc) & 15u || reinterpret_cast<uintptr_t>(vc) & 15u)
     return TL_ERR_INVALID_ARGUMENT;
+  TL_OPS_TRY(cu(attn_prepare()));
   return cu(launch_attn_prefill(qkv, (heads + 2 * kv_heads) * 64, seq_len * n_seqs, seq_len, heads, kv_heads, kc,
                                 vc, ks, vs, slot_base, layer, num_layers, max_positions, out, out_absmax,
                                 static_cast<cudaStream_t>(stream)));

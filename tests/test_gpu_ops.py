@@ -271,13 +271,15 @@ def test_attn_decode_matches_reference(pkg, lib, rows, H, Hkv, positions):
     np.testing.assert_array_equal(dvc.cpu().numpy(), vref)
 
 
-@pytest.mark.parametrize("n_seqs,S,H,Hkv", [(1, 1, 32, 4), (2, 63, 4, 2), (1, 64, 32, 4), (2, 65, 32, 4),
-                                            (3, 200, 4, 2), (1, 2048, 32, 4)])
-def test_attn_prefill_matches_reference(pkg, lib, n_seqs, S, H, Hkv):
+@pytest.mark.parametrize("n_seqs,S,H,Hkv,P", [(1, 1, 32, 4, 2048), (2, 63, 4, 2, 2048), (1, 64, 32, 4, 2048),
+                                              (2, 65, 32, 4, 2048), (3, 200, 4, 2, 2048), (1, 2048, 32, 4, 2048),
+                                              # cache capacity not a multiple of the 128-key tile
+                                              (2, 250, 8, 2, 250)])
+def test_attn_prefill_matches_reference(pkg, lib, n_seqs, S, H, Hkv, P):
     """Causal prefill attention over the INT8 cache vs the oracle's attention
     core (float64 scores) on dequantized cache rows."""
     rng = np.random.default_rng(S * 7 + n_seqs + H)
-    L, P, layer, slot_base = 2, 2048, 1, 1
+    L, layer, slot_base = 2, 1, 1
     slots = slot_base + n_seqs
     kc = rng.integers(-127, 128, (slots, L, Hkv, P, 64), dtype=np.int8)
     vc = rng.integers(-127, 128, (slots, L, Hkv, P, 64), dtype=np.int8)
