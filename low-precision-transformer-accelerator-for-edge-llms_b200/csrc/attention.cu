@@ -968,39 +968,33 @@ __global__ void __launch_bounds__(kApfThreads, 1) attn_prefill_tc_kernel(
     }
   } else {
     if (warp < 4) {
-      // row tid's query -> power-of-two scaled fp16 hi/lo operands
+      // row tid's query -> power-of-two scaled fp16 hi/lo operands; the
+      // row's sixteen 16-byte loads are all in flight before the first use
       const int t = q0 + tid;
-      const bool ok = t < seq_len;
-      // (two passes over the row, the second from L1: max |q|, then the
-      // scaled halves eight dims at a time)
-      const float* q = qkv + static_cast<size_t>(seq * seq_len + (ok ? t : 0)) * ld + head * 64;
+      const float4* q4 = reinterpret_cast<const float4*>(
+          qkv + static_cast<size_t>(seq * seq_len + (t < seq_len ? t : 0)) * ld + head * 64);
+      float4 x[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) x[i] = t < seq_len ? __ldg(q4 + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       float mx = 0.0f;
 #pragma unroll
-      for (int d = 0; d < 64; d += 2) {
-        const float2 x = *reinterpret_cast<const float2*>(q + d);
-        mx = fmaxf(mx, fmaxf(fabsf(x.x), fabsf(x.y)));
-      }
-      if (!ok) mx = 0.0f;
+      for (int i = 0; i < 16; ++i)
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(x[i].x), fabsf(x[i].y)), fmaxf(fabsf(x[i].z), fabsf(x[i].w))));
       const float qs = pow2_scale(mx);
-      xsc[tid] = ks[sidx] * 0.125f / qs * kLog2e;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
-        float qv[8];
-#pragma unroll
-        for (int i = 0; i < 8; i += 2) {
-          const float2 x = *reinterpret_cast<const float2*>(q + 8 * c + i);
-          qv[i] = ok ? x.x : 0.0f;
-          qv[i + 1] = ok ? x.y : 0.0f;
-        }
         uint4 hi, lo;
-        split2_fast(qv[0] * qs, qv[1] * qs, hi.x, lo.x);
-        split2_fast(qv[2] * qs, qv[3] * qs, hi.y, lo.y);
-        split2_fast(qv[4] * qs, qv[5] * qs, hi.z, lo.z);
-        split2_fast(qv[6] * qs, qv[7] * qs, hi.w, lo.w);
+        split2_fast(x[2 * c].x * qs, x[2 * c].y * qs, hi.x, lo.x);
+        split2_fast(x[2 * c].z * qs, x[2 * c].w * qs, hi.y, lo.y);
+        split2_fast(x[2 * c + 1].x * qs, x[2 * c + 1].y * qs, hi.z, lo.z);
+        split2_fast(x[2 * c + 1].z * qs, x[2 * c + 1].w * qs, hi.w, lo.w);
         const uint32_t off = sw128_offset(tid, c);
         *reinterpret_cast<uint4*>(sm + kApfOffQHi + off) = hi;
         *reinterpret_cast<uint4*>(sm + kApfOffQLo + off) = lo;
       }
+      // (the K scale is applied by the softmax threads: sc2 = xsc * sK,
+      // the same single rounding of sK * log2 e as sK * 0.125 * log2 e / qs)
+      xsc[tid] = 0.125f * kLog2e / qs;
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(q_full);
@@ -1028,8 +1022,9 @@ __global__ void __launch_bounds__(kApfThreads, 1) attn_prefill_tc_kernel(
       }
       return true;
     };
+    const float sk = __ldg(ks + sidx);
     bool ok = apf_wait(q_full, 0, 28u);  // the row scales in xsc
-    const float sc2 = xsc[r];
+    const float sc2 = xsc[r] * sk;
     for (int j = 0; j < n_kt && ok; ++j) {
       const int b = j & 1, u = j >> 1;
       if (!(ok = apf_wait(s_full + b, u & 1, 29u))) break;
