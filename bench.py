@@ -250,7 +250,7 @@ def tp_prefill_bench(pkg, group, rank, world, local_rank):
     ms = float(np.median(times))
     return {"workload": "configs[4]: 8 x 2048-token prompts, 22 layers, tensor parallel by KV head",
             "world": world, "value": 8 * 2048 / (ms / 1e3), "unit": "tok/s", "ms": ms,
-            "collectives": "per layer: 2 x all-reduce max (8 floats) + 2 x all-reduce sum INT32 [16384][2048]"}
+            "collectives": "per layer: 2 x all-reduce max (one float per sequence), then the INT8 O and down inputs all-gathered by peer stores over NVLink (quantize_scatter_kernel)"}
 
 
 def run_ours(a, rank, world, local_rank):

@@ -21,12 +21,16 @@
 //    [slot][layer][kv_head].
 // Tensor-parallel prefill (tl_tp_create): rank r of `world` holds kv heads
 // [r Hkv/world, (r+1) Hkv/world) with their query heads, the matching
-// columns of Q/K/V, rows of O (its input features), columns of gate/up and
-// rows of down; RMSNorm, embedding and LM head are replicated. After O and
-// after down the INT32 partial products are summed with an NCCL all-reduce
-// (exact), and the per-sequence activation maxima that set the O and down
-// input scales are combined with an all-reduce max first, so every rank
-// quantizes with the same scale as one GPU: the result is bit-identical.
+// columns of Q/K/V and the matching columns of gate/up; O, down, RMSNorm,
+// embedding and LM head are replicated. The per-sequence activation maxima
+// that set the O and down input scales are combined with an NCCL all-reduce
+// max; each rank then quantizes its column block of the attention output
+// (SiLU*up) with that scale and writes the INT8 bytes into the full-width
+// input matrix of every rank -- its own and its peers', through CUDA-IPC
+// mapped memory over NVLink -- and the O (down) GEMM runs on the whole
+// input everywhere. Every rank thus computes exactly the one-GPU O / down
+// products: the result is bit-identical, and the exchange moves INT8
+// activations (1 byte per element, once) instead of INT32 partial sums.
 #include <dlfcn.h>
 #include <nccl.h>
 
@@ -119,7 +123,6 @@ struct PrefillBufs {
   int8_t* xq = nullptr;
   float* amax = nullptr;     // [L][4][n_seq] + [n_seq] (final norm)
   float* kvamax = nullptr;   // [L][n_seq][2][Hkv]
-  int32_t* acc32 = nullptr;  // tensor parallel: INT32 partial sums [rows][D]
 };
 
 // NCCL entry points, resolved at run time from libnccl.so.2 (the copy a host
@@ -131,6 +134,7 @@ struct NcclApi {
   ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
   ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                              cudaStream_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
 };
@@ -142,9 +146,10 @@ const NcclApi& nccl_api() {
     a.get_unique_id = reinterpret_cast<decltype(a.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
     a.comm_init_rank = reinterpret_cast<decltype(a.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
     a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    a.all_gather = reinterpret_cast<decltype(a.all_gather)>(dlsym(h, "ncclAllGather"));
     a.comm_destroy = reinterpret_cast<decltype(a.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
     a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
-    a.ok = a.get_unique_id && a.comm_init_rank && a.all_reduce && a.comm_destroy && a.error_string;
+    a.ok = a.get_unique_id && a.comm_init_rank && a.all_reduce && a.all_gather && a.comm_destroy && a.error_string;
     return a;
   }();
   return api;
@@ -185,7 +190,16 @@ struct tl_engine {
   // tensor parallelism (prefill only): H, Hkv, Dq, Dkv, Nqkv and F above are
   // this rank's shares; cfg keeps the model's global sizes
   int tp_rank = 0, tp_world = 1;
+  int Dq_full = 0, F_full = 0;      // the model's O / down input widths (O and down are replicated)
   ncclComm_t comm = nullptr;
+  // INT8 exchange buffers of the tensor-parallel prefill: two [tp_rows][max(Dq_full, F_full)]
+  // matrices (exchange k uses k % 2) and `world` flag words per rank, in one
+  // allocation mapped by every peer (tp_peer[q]: rank q's base; tp_peer[rank] = tp_base)
+  unsigned char* tp_base = nullptr;
+  unsigned char* tp_peer[4] = {nullptr, nullptr, nullptr, nullptr};
+  unsigned int* tp_done = nullptr;  // CTA ticket of the scatter kernel
+  size_t tp_rows = 0, tp_buf_bytes = 0;
+  unsigned int tp_epoch = 0;
   bool use_decode1 = false;         // batch-1 steps run as one persistent kernel
 };
 
@@ -273,8 +287,7 @@ tl_status ensure_prefill(tl_engine* e, size_t rows, int n_seq) {
   rows = std::max(rows, p.rows);
   n_seq = std::max(n_seq, p.n_seq_cap);
   cudaFree(p.ids); cudaFree(p.x); cudaFree(p.h); cudaFree(p.qkv); cudaFree(p.att);
-  cudaFree(p.hid); cudaFree(p.xq); cudaFree(p.amax); cudaFree(p.kvamax); cudaFree(p.acc32);
-  cudaFree(p.inv);
+  cudaFree(p.hid); cudaFree(p.xq); cudaFree(p.amax); cudaFree(p.kvamax); cudaFree(p.inv);
   p = PrefillBufs{};
   TL_TRY(dmalloc(&p.ids, rows));
   TL_TRY(dmalloc(&p.x, rows * e->D));
@@ -286,7 +299,6 @@ tl_status ensure_prefill(tl_engine* e, size_t rows, int n_seq) {
   TL_TRY(dmalloc(&p.xq, rows * std::max(e->F, e->D)));
   TL_TRY(dmalloc(&p.amax, static_cast<size_t>(e->L) * 4 * n_seq + n_seq));
   TL_TRY(dmalloc(&p.kvamax, static_cast<size_t>(e->L) * n_seq * 2 * e->Hkv));
-  if (e->tp_world > 1) TL_TRY(dmalloc(&p.acc32, rows * e->D));
   p.rows = rows;
   p.n_seq_cap = n_seq;
   return TL_OK;
@@ -471,26 +483,23 @@ tl_status get_graph(tl_engine* e, int M, cudaGraphExec_t* out) {
 }
 
 // ------------------------------------------------------------------ prefill
-// One prefill projection from pf.xq (rows grouped by sequence of S tokens):
-// tcgen05 for R >= kTcMinRows rows, else the dp4a GEMV. out_absmax (per
-// sequence) only where no split-K is used; otherwise a separate pass.
-tl_status prefill_gemm(tl_engine* e, const int8_t* w, const double* ws, int N, int K, int R, int S,
+// One prefill projection from the INT8 matrix xq [R][K] (rows grouped by
+// sequence of S tokens): tcgen05 for R >= kTcMinRows rows, else the dp4a
+// GEMV.
+tl_status prefill_gemm(tl_engine* e, const int8_t* xq, const int8_t* w, const double* ws, int N, int K, int R, int S,
                        const float* in_absmax, int epi, float* out, const float* resid, float* out_absmax) {
-  PrefillBufs& p = e->pf;
   if (R >= kTcMinRows) {
     TcPlan plan;
-    TL_CU(tc_make_plan(&plan, w, N, p.xq, R, K, device_sm_count(), epi));
+    TL_CU(tc_make_plan(&plan, w, N, xq, R, K, device_sm_count(), epi));
     TcArgs a;
     a.epi = epi; a.w_scale = ws; a.in_absmax = in_absmax; a.rows_per_group = S; a.out_f32 = out;
     a.resid = resid; a.out_absmax = out_absmax;
-    a.out_i32 = epi == EPI_I32 ? p.acc32 : nullptr;
     TL_CU(launch_gemm_tc(plan, a, e->stream, false));
     return TL_OK;
   }
   GemvArgs g;
-  g.x_q = p.xq; g.in_absmax = in_absmax; g.rows_per_group = S;
+  g.x_q = xq; g.in_absmax = in_absmax; g.rows_per_group = S;
   g.w = w; g.w_scale = ws; g.M = R; g.N = N; g.K = K; g.out_f32 = out; g.resid = resid; g.out_absmax = out_absmax;
-  g.out_i32 = epi == EPI_I32 ? p.acc32 : nullptr;
   TL_CU(launch_gemv(PRO_Q8, epi, g, e->stream, false));
   return TL_OK;
 }
@@ -501,17 +510,29 @@ tl_status tp_allreduce_max(tl_engine* e, float* v, int n) {
   return TL_OK;
 }
 
-// Tensor parallel row-split projection (O, down): this rank's INT32 partial
-// products of its input features, summed over ranks with an INT32 all-reduce
-// (exact), then dequantized and added to the residual stream x exactly as the
-// single-GPU EPI_RESID epilogue does.
-tl_status tp_rowsplit_resid(tl_engine* e, const int8_t* w, const double* ws, int N, int K, int R, int S,
-                            const float* in_absmax) {
-  PrefillBufs& p = e->pf;
-  TL_TRY(prefill_gemm(e, w, ws, N, K, R, S, in_absmax, EPI_I32, nullptr, nullptr, nullptr));
-  TL_NCCL(nccl_api().all_reduce(p.acc32, p.acc32, static_cast<size_t>(R) * N, ncclInt32, ncclSum, e->comm,
-                                e->stream));
-  TL_CU(launch_dequant_resid_rows(p.acc32, in_absmax, S, ws, p.x, R, N, e->stream));
+// Tensor parallel: this rank's column block x [R][Kl] (columns rank * Kl ..)
+// quantized with the group-wide per-sequence scale and written into the
+// full-width INT8 input [R][Kf] of every rank, then a bounded wait until
+// every peer's block has arrived here. Returns the local full-width input.
+tl_status tp_exchange(tl_engine* e, const float* x, int Kl, int Kf, int R, int S, const float* absmax,
+                      const int8_t** full) {
+  if (static_cast<size_t>(R) > e->tp_rows) return TL_ERR_OUT_OF_RANGE;
+  const unsigned int epoch = ++e->tp_epoch;
+  const size_t buf = (epoch & 1u) * e->tp_buf_bytes;   // exchange k uses buffer k % 2
+  const size_t flag_off = 2 * e->tp_buf_bytes;
+  TpScatter t;
+  t.ndst = 0;
+  t.dst[t.ndst] = reinterpret_cast<int8_t*>(e->tp_base + buf);
+  t.flag[t.ndst++] = nullptr;
+  for (int q = 0; q < e->tp_world; ++q) {
+    if (q == e->tp_rank) continue;
+    t.dst[t.ndst] = reinterpret_cast<int8_t*>(e->tp_peer[q] + buf);
+    t.flag[t.ndst++] = reinterpret_cast<unsigned int*>(e->tp_peer[q] + flag_off) + e->tp_rank;
+  }
+  TL_CU(launch_quantize_scatter(x, absmax, S, R, Kl, Kf, e->tp_rank * Kl, t, e->tp_done, epoch, e->stream));
+  TL_CU(launch_tp_wait(reinterpret_cast<const unsigned int*>(e->tp_base + flag_off), e->tp_world, e->tp_rank, epoch,
+                       e->stream));
+  *full = reinterpret_cast<const int8_t*>(e->tp_base + buf);
   return TL_OK;
 }
 
@@ -533,24 +554,32 @@ tl_status enqueue_prefill(tl_engine* e, int n_seq, int S, int slot_base, bool he
     float* kva = p.kvamax + static_cast<size_t>(l) * n_seq * 2 * e->Hkv;
     // attention block
     TL_CU(launch_norm_quant_prefill(p.x, ly.g1, eps, R, e->D, S, p.inv, am, p.h, p.xq, s));
-    TL_TRY(prefill_gemm(e, ly.wqkv, ly.sqkv, e->Nqkv, e->D, R, S, am, EPI_F32, p.qkv, nullptr, nullptr));
+    TL_TRY(prefill_gemm(e, p.xq, ly.wqkv, ly.sqkv, e->Nqkv, e->D, R, S, am, EPI_F32, p.qkv, nullptr, nullptr));
     TL_CU(launch_rope_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->cosT, e->sinT, kva, s));
     TL_CU(launch_kv_write_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, kva, e->kc, e->vc, e->ks, e->vs,
                                   slot_base, l, e->L, e->P, s));
     TL_CU(launch_attn_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->kc, e->vc, e->ks, e->vs, slot_base,
                               l, e->L, e->P, p.att, am + n_seq, s));
-    if (tp) TL_TRY(tp_allreduce_max(e, am + n_seq, n_seq));
-    TL_CU(launch_quantize_rows(p.att, am + n_seq, R, e->Dq, S, p.xq, s));
-    if (tp) TL_TRY(tp_rowsplit_resid(e, ly.wo, ly.so, e->D, e->Dq, R, S, am + n_seq));
-    else TL_TRY(prefill_gemm(e, ly.wo, ly.so, e->D, e->Dq, R, S, am + n_seq, EPI_RESID, p.x, p.x, nullptr));
+    const int8_t* xin = p.xq;
+    if (tp) {
+      TL_TRY(tp_allreduce_max(e, am + n_seq, n_seq));
+      TL_TRY(tp_exchange(e, p.att, e->Dq, e->Dq_full, R, S, am + n_seq, &xin));
+    } else {
+      TL_CU(launch_quantize_rows(p.att, am + n_seq, R, e->Dq, S, p.xq, s));
+    }
+    TL_TRY(prefill_gemm(e, xin, ly.wo, ly.so, e->D, e->Dq_full, R, S, am + n_seq, EPI_RESID, p.x, p.x, nullptr));
     // feed-forward block
     TL_CU(launch_norm_quant_prefill(p.x, ly.g2, eps, R, e->D, S, p.inv, am + 2 * n_seq, p.h, p.xq, s));
-    TL_TRY(prefill_gemm(e, ly.wgu, ly.sgu, 2 * e->F, e->D, R, S, am + 2 * n_seq, EPI_SILU, p.hid, nullptr,
+    TL_TRY(prefill_gemm(e, p.xq, ly.wgu, ly.sgu, 2 * e->F, e->D, R, S, am + 2 * n_seq, EPI_SILU, p.hid, nullptr,
                         am + 3 * n_seq));
-    if (tp) TL_TRY(tp_allreduce_max(e, am + 3 * n_seq, n_seq));
-    TL_CU(launch_quantize_rows(p.hid, am + 3 * n_seq, R, e->F, S, p.xq, s));
-    if (tp) TL_TRY(tp_rowsplit_resid(e, ly.wd, ly.sd, e->D, e->F, R, S, am + 3 * n_seq));
-    else TL_TRY(prefill_gemm(e, ly.wd, ly.sd, e->D, e->F, R, S, am + 3 * n_seq, EPI_RESID, p.x, p.x, nullptr));
+    xin = p.xq;
+    if (tp) {
+      TL_TRY(tp_allreduce_max(e, am + 3 * n_seq, n_seq));
+      TL_TRY(tp_exchange(e, p.hid, e->F, e->F_full, R, S, am + 3 * n_seq, &xin));
+    } else {
+      TL_CU(launch_quantize_rows(p.hid, am + 3 * n_seq, R, e->F, S, p.xq, s));
+    }
+    TL_TRY(prefill_gemm(e, xin, ly.wd, ly.sd, e->D, e->F_full, R, S, am + 3 * n_seq, EPI_RESID, p.x, p.x, nullptr));
   }
   if (!head) return TL_OK;
   float* amf = p.amax + static_cast<size_t>(e->L) * 4 * n_seq;
@@ -689,6 +718,55 @@ const char* tl_status_string(int32_t s) {
 int32_t tl_version(void) { return 0x00010000; }
 
 namespace {
+// Tensor-parallel exchange memory: one allocation per rank holding the two
+// INT8 exchange matrices and the flag words, exported with a CUDA-IPC handle;
+// the handles are all-gathered over the group's NCCL communicator and every
+// peer's allocation is mapped here (peer access over NVLink).
+tl_status tp_setup_exchange(tl_engine* e, size_t rows) {
+  if (e->tp_world > 4) return TL_ERR_INVALID_ARGUMENT;
+  e->tp_rows = rows;
+  const size_t width = static_cast<size_t>(std::max(e->Dq_full, e->F_full));
+  e->tp_buf_bytes = (rows * width + 255) / 256 * 256;
+  const size_t bytes = 2 * e->tp_buf_bytes + 64 * sizeof(unsigned int);
+  TL_CU(cudaMalloc(&e->tp_base, bytes));
+  TL_CU(cudaMemset(e->tp_base + 2 * e->tp_buf_bytes, 0, 64 * sizeof(unsigned int)));
+  TL_TRY(dmalloc(&e->tp_done, 1));
+  TL_CU(cudaMemset(e->tp_done, 0, sizeof(unsigned int)));
+  cudaIpcMemHandle_t mine;
+  TL_CU(cudaIpcGetMemHandle(&mine, e->tp_base));
+  constexpr size_t kH = sizeof(cudaIpcMemHandle_t);
+  unsigned char* dev = nullptr;
+  TL_CU(cudaMalloc(&dev, kH * (e->tp_world + 1)));
+  std::vector<unsigned char> all(kH * e->tp_world);
+  tl_status st = TL_OK;
+  cudaError_t ce = cudaMemcpy(dev + kH * e->tp_world, &mine, kH, cudaMemcpyHostToDevice);
+  if (ce == cudaSuccess) {
+    const ncclResult_t r =
+        nccl_api().all_gather(dev + kH * e->tp_world, dev, kH, ncclUint8, e->comm, e->stream);
+    if (r != ncclSuccess) {
+      g_last_error = std::string("ncclAllGather: ") + nccl_api().error_string(r);
+      st = TL_ERR_NCCL;
+    }
+  }
+  if (st == TL_OK && ce == cudaSuccess) ce = cudaStreamSynchronize(e->stream);
+  if (st == TL_OK && ce == cudaSuccess) ce = cudaMemcpy(all.data(), dev, all.size(), cudaMemcpyDeviceToHost);
+  cudaFree(dev);
+  if (st != TL_OK) return st;
+  TL_CU(ce);
+  for (int q = 0; q < e->tp_world; ++q) {
+    if (q == e->tp_rank) {
+      e->tp_peer[q] = e->tp_base;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, all.data() + kH * q, kH);
+    void* ptr = nullptr;
+    TL_CU(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+    e->tp_peer[q] = static_cast<unsigned char*>(ptr);
+  }
+  return TL_OK;
+}
+
 // Engine for rank `rank` of a tensor-parallel group of `world` GPUs (world 1:
 // the whole model on one GPU). `id` is the NCCL group id (world > 1 only).
 tl_status create_engine(const tl_config* cfg, int32_t device, int rank, int world, const ncclUniqueId* id,
@@ -708,6 +786,7 @@ tl_status create_engine(const tl_config* cfg, int32_t device, int rank, int worl
   e->D = cfg->hidden_size; e->F = cfg->intermediate_size / world; e->H = cfg->num_heads / world;
   e->Hkv = cfg->num_kv_heads / world;
   e->Dq = e->H * 64; e->Dkv = e->Hkv * 64; e->Nqkv = e->Dq + 2 * e->Dkv; e->V = cfg->vocab_size;
+  e->Dq_full = cfg->num_heads * 64; e->F_full = cfg->intermediate_size;
   e->L = cfg->num_layers; e->P = cfg->max_positions; e->B = cfg->max_batch;
   auto fail = [&](tl_status s) { tl_destroy(e); return s; };
   if (world > 1) {
@@ -730,11 +809,11 @@ tl_status create_engine(const tl_config* cfg, int32_t device, int rank, int worl
     tl_status s;
     if ((s = dmalloc(&ly.wqkv, static_cast<size_t>(e->Nqkv) * e->D)) != TL_OK) return fail(s);
     if ((s = dmalloc(&ly.sqkv, e->Nqkv)) != TL_OK) return fail(s);
-    if ((s = dmalloc(&ly.wo, static_cast<size_t>(e->D) * e->Dq)) != TL_OK) return fail(s);
+    if ((s = dmalloc(&ly.wo, static_cast<size_t>(e->D) * e->Dq_full)) != TL_OK) return fail(s);
     if ((s = dmalloc(&ly.so, e->D)) != TL_OK) return fail(s);
     if ((s = dmalloc(&ly.wgu, static_cast<size_t>(2) * e->F * e->D)) != TL_OK) return fail(s);
     if ((s = dmalloc(&ly.sgu, 2 * e->F)) != TL_OK) return fail(s);
-    if ((s = dmalloc(&ly.wd, static_cast<size_t>(e->D) * e->F)) != TL_OK) return fail(s);
+    if ((s = dmalloc(&ly.wd, static_cast<size_t>(e->D) * e->F_full)) != TL_OK) return fail(s);
     if ((s = dmalloc(&ly.sd, e->D)) != TL_OK) return fail(s);
     if ((s = dmalloc(&ly.g1, e->D)) != TL_OK) return fail(s);
     if ((s = dmalloc(&ly.g2, e->D)) != TL_OK) return fail(s);
@@ -765,6 +844,7 @@ tl_status create_engine(const tl_config* cfg, int32_t device, int rank, int worl
   // TL_DISABLE_PDL=1 launches every kernel without programmatic dependent
   // launch (plain stream order); a debugging aid, off by default.
   if (const char* v = std::getenv("TL_DISABLE_PDL")) e->use_pdl = !(v[0] == '1');
+  if (world > 1 && (s = tp_setup_exchange(e, pf_rows)) != TL_OK) return fail(s);
   *out = e;
   return TL_OK;
 }
@@ -800,6 +880,10 @@ tl_status tl_destroy(tl_engine* e) {
   cudaSetDevice(e->device);
   if (e->stream) cudaStreamSynchronize(e->stream);
   invalidate_graphs(e);
+  for (int q = 0; q < 4; ++q)
+    if (e->tp_peer[q] && e->tp_peer[q] != e->tp_base) cudaIpcCloseMemHandle(e->tp_peer[q]);
+  cudaFree(e->tp_base);
+  cudaFree(e->tp_done);
   if (e->comm) nccl_api().comm_destroy(e->comm);
   e->comm = nullptr;
   for (auto& ly : e->layers) {
@@ -816,7 +900,7 @@ tl_status tl_destroy(tl_engine* e) {
   cudaFree(d.d1_layers); cudaFree(d.d1_part); cudaFree(d.d1_sync);
   PrefillBufs& p = e->pf;
   cudaFree(p.ids); cudaFree(p.x); cudaFree(p.h); cudaFree(p.qkv); cudaFree(p.att); cudaFree(p.hid);
-  cudaFree(p.xq); cudaFree(p.amax); cudaFree(p.kvamax); cudaFree(p.acc32); cudaFree(p.inv);
+  cudaFree(p.xq); cudaFree(p.amax); cudaFree(p.kvamax); cudaFree(p.inv);
   if (e->h_pinned) cudaFreeHost(e->h_pinned);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
@@ -832,8 +916,7 @@ static tl_status upload_transposed(tl_engine* e, int8_t* tmp, const int8_t* host
 
 namespace {
 // Host-side slice of one layer for tensor-parallel rank r: the columns of
-// Q/K/V and gate/up it produces and the rows of O and down it consumes
-// (pointer offsets into the caller's arrays where rows are contiguous).
+// Q/K/V and gate/up it produces; O and down stay whole (replicated).
 struct LayerSlice {
   std::vector<int8_t> q, k, v, gate, up;
   std::vector<double> sq, sk, sv, sg, su;
@@ -863,8 +946,6 @@ void slice_layer(const tl_engine* e, const tl_layer_view& lv, LayerSlice& out) {
   out.view.v = {out.v.data(), out.sv.data()};
   out.view.gate = {out.gate.data(), out.sg.data()};
   out.view.up = {out.up.data(), out.su.data()};
-  out.view.o = {lv.o.w + static_cast<size_t>(r) * e->Dq * D, lv.o.scale};
-  out.view.down = {lv.down.w + static_cast<size_t>(r) * e->F * D, lv.down.scale};
 }
 }  // namespace
 
@@ -873,7 +954,8 @@ tl_status tl_load_weights(tl_engine* e, const tl_weights_view* w) {
     return TL_ERR_INVALID_ARGUMENT;
   TL_CU(cudaSetDevice(e->device));
   const int D = e->D, F = e->F, Dq = e->Dq, Dkv = e->Dkv, V = e->V;
-  const size_t tmp_bytes = std::max<size_t>(static_cast<size_t>(V) * D, 2 * static_cast<size_t>(F) * D);
+  const size_t tmp_bytes = std::max<size_t>(std::max<size_t>(static_cast<size_t>(V) * D, 2 * static_cast<size_t>(F) * D),
+                                             static_cast<size_t>(std::max(e->Dq_full, e->F_full)) * D);
   int8_t* tmp = nullptr;
   TL_TRY(dmalloc(&tmp, tmp_bytes));
   auto body = [&]() -> tl_status {
@@ -896,7 +978,7 @@ tl_status tl_load_weights(tl_engine* e, const tl_weights_view* w) {
       TL_CU(cudaMemcpyAsync(ly.sqkv, lv.q.scale, Dq * sizeof(double), cudaMemcpyHostToDevice, e->stream));
       TL_CU(cudaMemcpyAsync(ly.sqkv + Dq, lv.k.scale, Dkv * sizeof(double), cudaMemcpyHostToDevice, e->stream));
       TL_CU(cudaMemcpyAsync(ly.sqkv + Dq + Dkv, lv.v.scale, Dkv * sizeof(double), cudaMemcpyHostToDevice, e->stream));
-      TL_TRY(upload_transposed(e, tmp, lv.o.w, Dq, D, ly.wo));
+      TL_TRY(upload_transposed(e, tmp, lv.o.w, e->Dq_full, D, ly.wo));
       TL_CU(cudaMemcpyAsync(ly.so, lv.o.scale, D * sizeof(double), cudaMemcpyHostToDevice, e->stream));
       TL_CU(cudaMemcpyAsync(tmp, lv.gate.w, static_cast<size_t>(D) * F, cudaMemcpyHostToDevice, e->stream));
       TL_CU(cudaMemcpyAsync(tmp + static_cast<size_t>(D) * F, lv.up.w, static_cast<size_t>(D) * F,
@@ -909,7 +991,7 @@ tl_status tl_load_weights(tl_engine* e, const tl_weights_view* w) {
       }
       TL_CU(cudaMemcpyAsync(ly.sgu, sgu.data(), sgu.size() * sizeof(double), cudaMemcpyHostToDevice, e->stream));
       TL_CU(cudaStreamSynchronize(e->stream));  // sgu is a host temporary
-      TL_TRY(upload_transposed(e, tmp, lv.down.w, F, D, ly.wd));
+      TL_TRY(upload_transposed(e, tmp, lv.down.w, e->F_full, D, ly.wd));
       TL_CU(cudaMemcpyAsync(ly.sd, lv.down.scale, D * sizeof(double), cudaMemcpyHostToDevice, e->stream));
       TL_CU(cudaMemcpyAsync(ly.g1, lv.input_norm, D * sizeof(float), cudaMemcpyHostToDevice, e->stream));
       TL_CU(cudaMemcpyAsync(ly.g2, lv.post_norm, D * sizeof(float), cudaMemcpyHostToDevice, e->stream));
@@ -963,9 +1045,9 @@ tl_status tl_init_random_weights(tl_engine* e, uint64_t seed) {
                                  kqkv, s));
     TL_CU(launch_random_i8_block(ly.wqkv + static_cast<size_t>(e->Dq + e->Dkv) * e->D, e->Dkv, e->D,
                                  Dqg + Dkvg + r * e->Dkv, 0, D, kqkv, s));
-    TL_CU(launch_random_i8_block(ly.wo, e->D, e->Dq, 0, r * e->Dq, Dqg, ++k, s));
+    TL_CU(launch_random_i8_block(ly.wo, e->D, e->Dq_full, 0, 0, Dqg, ++k, s));
     TL_CU(launch_random_i8_block(ly.wgu, 2 * e->F, e->D, 2 * r * e->F, 0, D, ++k, s));
-    TL_CU(launch_random_i8_block(ly.wd, e->D, e->F, 0, r * e->F, Fg, ++k, s));
+    TL_CU(launch_random_i8_block(ly.wd, e->D, e->F_full, 0, 0, Fg, ++k, s));
     TL_CU(launch_fill_f64(ly.sqkv, e->Nqkv, wscale, s));
     TL_CU(launch_fill_f64(ly.so, e->D, wscale, s));
     TL_CU(launch_fill_f64(ly.sgu, 2 * e->F, wscale, s));

@@ -1004,8 +1004,9 @@ cudaError_t prepare_tc() {
   return prepare_tcp();
 }
 
-// Reads and clears the bounded-wait error words of the tcgen05 GEMM and of
-// the decode attention (0 = none expired).
+// Reads and clears the bounded-wait error words of the tcgen05 GEMM, the
+// attention kernels, the persistent decode step and the tensor-parallel
+// exchange (0 = none expired).
 cudaError_t tc_read_error(unsigned int* code) {
   cudaError_t e = cudaMemcpyFromSymbol(code, g_tc_error, sizeof(unsigned int));
   if (e != cudaSuccess) return e;
@@ -1015,7 +1016,9 @@ cudaError_t tc_read_error(unsigned int* code) {
   }
   e = attn_read_error(code);
   if (e != cudaSuccess || *code) return e;
-  return decode1_read_error(code);
+  e = decode1_read_error(code);
+  if (e != cudaSuccess || *code) return e;
+  return tp_read_error(code);
 }
 
 }  // namespace tl

@@ -1085,31 +1085,83 @@ cudaError_t launch_step_finalize(const StepArgs& a, cudaStream_t s, bool pdl) {
   return cudaLaunchKernelEx(&cfg, step_finalize_kernel, a);
 }
 
-// x[m][n] += dequant(acc[m][n]) with the token scale absmax[m / rpg] / 127
-// and the channel scale w_scale[n] -- the EPI_RESID epilogue applied to
-// INT32 sums gathered from several GPUs. One CTA per (row, 1024 columns).
-__global__ void __launch_bounds__(256) dequant_resid_rows_kernel(const int32_t* acc, const float* absmax, int rpg,
-                                                                  const double* w_scale, float* x, int N) {
-  const int m = blockIdx.y;
-  const double sx = quant_scale64(absmax[m / rpg]);
-  const int n = (blockIdx.x * 256 + threadIdx.x) * 4;
-  if (n >= N) return;
-  const size_t o = static_cast<size_t>(m) * N + n;
-  const int4 a = *reinterpret_cast<const int4*>(acc + o);
-  float4 r = *reinterpret_cast<const float4*>(x + o);
-  r.x = __fadd_rn(r.x, dequant(a.x, sx, w_scale[n]));
-  r.y = __fadd_rn(r.y, dequant(a.y, sx, w_scale[n + 1]));
-  r.z = __fadd_rn(r.z, dequant(a.z, sx, w_scale[n + 2]));
-  r.w = __fadd_rn(r.w, dequant(a.w, sx, w_scale[n + 3]));
-  *reinterpret_cast<float4*>(x + o) = r;
+// ============================================== tensor-parallel exchange
+// Per-sequence INT8 quantization of this rank's column block [col0, col0 +
+// Kl) of a float matrix [rows][Kl], written into the full-width INT8 matrix
+// [rows][Kf] of every rank of the group -- its own and, through CUDA-IPC
+// mapped pointers over NVLink, its peers': the all-gather of the quantized
+// activations fused into the quantization. Every CTA fences at system
+// scope before taking a ticket; the last one publishes `epoch` into each
+// peer's flag slot for this rank with a system-scope release, so a peer
+// that acquires the epoch also sees every byte.
+__device__ unsigned int g_tp_error = 0;
+
+TL_DEV void st_release_sys(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+TL_DEV unsigned int ld_acquire_sys(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
-cudaError_t launch_dequant_resid_rows(const int32_t* acc, const float* absmax, int rows_per_group,
-                                      const double* w_scale, float* x, int rows, int N, cudaStream_t s) {
-  if (N % 4 || rows <= 0) return cudaErrorInvalidValue;
-  dim3 grid((N + 1023) / 1024, rows);
-  dequant_resid_rows_kernel<<<grid, 256, 0, s>>>(acc, absmax, rows_per_group, w_scale, x, N);
+__global__ void __launch_bounds__(256) quantize_scatter_kernel(const float* x, const float* absmax, int rpg, int Kl,
+                                                               int Kf, int col0, TpScatter t, unsigned int* done,
+                                                               unsigned int epoch) {
+  const int r = blockIdx.x;
+  const float sf = static_cast<float>(quant_scale64(absmax[r / rpg]));
+  const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(r) * Kl);
+  const size_t off = static_cast<size_t>(r) * Kf + col0;
+  for (int c = threadIdx.x; c < Kl / 4; c += blockDim.x) {
+    const uint32_t q = quant_pack4(src[c], sf);
+    for (int d = 0; d < t.ndst; ++d) reinterpret_cast<uint32_t*>(t.dst[d] + off)[c] = q;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    if (atomicAdd(done, 1u) == gridDim.x - 1) {
+      __threadfence_system();
+      *done = 0u;
+      for (int d = 1; d < t.ndst; ++d) st_release_sys(t.flag[d], epoch);
+    }
+  }
+}
+
+cudaError_t launch_quantize_scatter(const float* x, const float* absmax, int rows_per_group, int rows, int Kl, int Kf,
+                                    int col0, const TpScatter& t, unsigned int* done, unsigned int epoch,
+                                    cudaStream_t s) {
+  if (Kl % 4 || Kf % 4 || col0 % 4 || t.ndst < 1 || t.ndst > 4) return cudaErrorInvalidValue;
+  quantize_scatter_kernel<<<rows, 256, 0, s>>>(x, absmax, rows_per_group, Kl, Kf, col0, t, done, epoch);
   return cudaGetLastError();
+}
+
+// Waits (one thread, ~2 s bound) until every peer q != rank has published
+// `epoch` into flags[q]; on expiry records 1 + q in the tensor-parallel
+// error word and returns, so the host reports TL_ERR_TIMEOUT.
+__global__ void tp_wait_kernel(const unsigned int* flags, int world, int rank, unsigned int epoch) {
+  if (threadIdx.x != 0) return;
+  const long long t0 = clock64();
+  for (int q = 0; q < world; ++q) {
+    if (q == rank) continue;
+    while (static_cast<int>(ld_acquire_sys(flags + q) - epoch) < 0) {
+      if (clock64() - t0 > 4000000000ll) {
+        atomicCAS(&g_tp_error, 0u, 1u + static_cast<unsigned int>(q));
+        return;
+      }
+    }
+  }
+}
+
+cudaError_t launch_tp_wait(const unsigned int* flags, int world, int rank, unsigned int epoch, cudaStream_t s) {
+  tp_wait_kernel<<<1, 32, 0, s>>>(flags, world, rank, epoch);
+  return cudaGetLastError();
+}
+
+cudaError_t tp_read_error(unsigned int* code) {
+  cudaError_t e = cudaMemcpyFromSymbol(code, g_tp_error, sizeof(unsigned int));
+  if (e != cudaSuccess || !*code) return e;
+  unsigned int zero = 0;
+  return cudaMemcpyToSymbol(g_tp_error, &zero, sizeof(unsigned int));
 }
 
 // token id of each row's packed argmax key; the key is re-armed (zeroed)

@@ -248,8 +248,21 @@ struct StepArgs {
 };
 cudaError_t launch_step_finalize(const StepArgs& a, cudaStream_t s, bool pdl);
 cudaError_t launch_keys_to_tokens(unsigned long long* key, int32_t* token, int M, cudaStream_t s);
-cudaError_t launch_dequant_resid_rows(const int32_t* acc, const float* absmax, int rows_per_group,
-                                      const double* w_scale, float* x, int rows, int N, cudaStream_t s);
+// Tensor-parallel exchange (kernels.cu): quantize this rank's column block
+// and write it into every rank's full-width INT8 matrix (dst[0] local, the
+// rest CUDA-IPC mapped peers); the last CTA publishes `epoch` into each
+// peer's flag slot for this rank. tp_wait blocks the stream (bounded) until
+// every peer's epoch has arrived in this rank's flags.
+struct TpScatter {
+  int8_t* dst[4];
+  unsigned int* flag[4];
+  int ndst;
+};
+cudaError_t launch_quantize_scatter(const float* x, const float* absmax, int rows_per_group, int rows, int Kl, int Kf,
+                                    int col0, const TpScatter& t, unsigned int* done, unsigned int epoch,
+                                    cudaStream_t s);
+cudaError_t launch_tp_wait(const unsigned int* flags, int world, int rank, unsigned int epoch, cudaStream_t s);
+cudaError_t tp_read_error(unsigned int* code);
 // random int8 sub-block [rows][cols] of a global [*][src_cols] matrix whose
 // element (i, j) is hash(seed, i * src_cols + j), at (src_row0, src_col0)
 cudaError_t launch_random_i8_block(int8_t* dst, int rows, int cols, long long src_row0, long long src_col0,

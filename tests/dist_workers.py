@@ -47,9 +47,9 @@ def tp_prefill_rank(rank: int, world: int, port: int, seed: int, prompt: list, o
     """One rank of the tensor-parallel prefill decomposition the engine runs
     (tl_tp_create), restated over the oracle's NumPy blocks with gloo
     collectives: kv heads [r*hr, (r+1)*hr) and their query heads, Q/K/V and
-    gate/up column slices, O and down row slices; per-sequence activation
-    maxima combined with all-reduce MAX before the O and down inputs are
-    quantized, INT32 partial products combined with all-reduce SUM."""
+    gate/up column slices; per-sequence activation maxima combined with
+    all-reduce MAX, each rank's column block of the O (down) input quantized
+    with that scale and all-gathered as INT8, O and down applied whole."""
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
     import torch
@@ -78,6 +78,12 @@ def tp_prefill_rank(rank: int, world: int, port: int, seed: int, prompt: list, o
             dist.all_reduce(t, op=op)
             return t.numpy()
 
+        def allgather_cols(a: np.ndarray) -> np.ndarray:
+            t = torch.from_numpy(np.ascontiguousarray(a))
+            parts = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(parts, t)
+            return np.concatenate([p.numpy() for p in parts], axis=1)
+
         x = qm.embed[np.asarray(prompt)].astype(np.float32)
         k_local = []
         for lay in qm.layers:
@@ -101,18 +107,16 @@ def tp_prefill_rank(rank: int, world: int, port: int, seed: int, prompt: list, o
             att = G.attention_core(qh, kd, vd, grp, c["attn_scale"], True)
             peak = allreduce(np.array([np.max(np.abs(att))], np.float32), dist.ReduceOp.MAX)[0]
             sx = 1.0 if peak == 0.0 else float(peak) / 127.0
-            acc = G.int8_matmul(G.quantize_with_scale(att, sx), lay.o.w_q[qcols, :]).astype(np.int64)
-            acc = allreduce(acc, dist.ReduceOp.SUM).astype(np.int32)
-            x1 = x + G.dequantize_int32(acc, sx, lay.o.scale)
+            att_q = allgather_cols(G.quantize_with_scale(att, sx))
+            x1 = x + G.dequantize_int32(G.int8_matmul(att_q, lay.o.w_q), sx, lay.o.scale)
             h2 = G.rms_norm(x1, lay.post_norm, eps)
             g, _, _, _ = G.linear_q(h2, lay.gate.w_q[:, fcols], lay.gate.scale[fcols])
             u, _, _, _ = G.linear_q(h2, lay.up.w_q[:, fcols], lay.up.scale[fcols])
             hid = G.silu(g) * u
             peak = allreduce(np.array([np.max(np.abs(hid))], np.float32), dist.ReduceOp.MAX)[0]
             sh = 1.0 if peak == 0.0 else float(peak) / 127.0
-            acc = G.int8_matmul(G.quantize_with_scale(hid, sh), lay.down.w_q[fcols, :]).astype(np.int64)
-            acc = allreduce(acc, dist.ReduceOp.SUM).astype(np.int32)
-            x = (x1 + G.dequantize_int32(acc, sh, lay.down.scale)).astype(np.float32)
+            hid_q = allgather_cols(G.quantize_with_scale(hid, sh))
+            x = (x1 + G.dequantize_int32(G.int8_matmul(hid_q, lay.down.w_q), sh, lay.down.scale)).astype(np.float32)
         hn = G.rms_norm(x, qm.final_norm, eps)
         xq, sxh = G.quantize_int8(hn)
         logits = G.dequantize_int32(G.int8_matmul(xq[-1:], qm.lm_head.w_q), sxh, qm.lm_head.scale)[0]
