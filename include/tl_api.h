@@ -148,11 +148,13 @@ TL_API tl_status tl_destroy(tl_engine* eng);
  * engine per GPU. The reference's prefill is the recompute forward_mixed
  * (model/tinyllama_gemm_int8.py:432-467); its TP-2/4 split is by KV head:
  * rank r holds kv heads [r Hkv/world, (r+1) Hkv/world) and their query
- * heads, the matching columns of Q/K/V and gate/up and rows of O and down,
- * with RMSNorm, embedding and LM head replicated. INT32 partial sums after O
- * and after down are added with an NCCL all-reduce, so the logits are
- * bit-identical to one GPU's. world must divide num_kv_heads and
- * intermediate_size / 16.
+ * heads and the matching columns of Q/K/V and gate/up, with O, down,
+ * RMSNorm, embedding and LM head replicated. The O and down inputs are
+ * quantized with group-wide scales (NCCL all-reduce max) and all-gathered as
+ * INT8 by peer stores over NVLink (CUDA-IPC mappings set up here; one
+ * process per GPU), so the logits are bit-identical to one GPU's. world
+ * (<= 4) must divide num_kv_heads and intermediate_size / 16; a prefill call
+ * may hold at most max_prefill_tokens rows.
  * tl_tp_unique_id: rank 0 draws the group id; the host hands the same
  * TL_TP_ID_BYTES bytes to every rank's tl_tp_create (all ranks must call it
  * concurrently: it blocks until the group is complete). tl_load_weights on
@@ -163,7 +165,8 @@ TL_API tl_status tl_destroy(tl_engine* eng);
  * every rank makes the same calls in the same order. Decode entry points
  * return TL_ERR_UNIMPLEMENTED on a TP engine (decode scales by sequence).
  * tl_read_kv returns this rank's kv heads. NCCL (libnccl.so.2) is loaded at
- * run time; TL_ERR_NCCL when it is missing or a collective fails. */
+ * run time; TL_ERR_NCCL when it is missing or a collective fails;
+ * TL_ERR_TIMEOUT (tl_synchronize) when a peer's activations do not arrive. */
 #define TL_TP_ID_BYTES 128
 TL_API tl_status tl_tp_unique_id(uint8_t* id_out);
 TL_API tl_status tl_tp_create(const tl_config* cfg, int32_t device, int32_t rank, int32_t world, const uint8_t* id,
