@@ -555,9 +555,10 @@ tl_status enqueue_prefill(tl_engine* e, int n_seq, int S, int slot_base, bool he
     // attention block
     TL_CU(launch_norm_quant_prefill(p.x, ly.g1, eps, R, e->D, S, p.inv, am, p.h, p.xq, s));
     TL_TRY(prefill_gemm(e, p.xq, ly.wqkv, ly.sqkv, e->Nqkv, e->D, R, S, am, EPI_F32, p.qkv, nullptr, nullptr));
-    TL_CU(launch_rope_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->cosT, e->sinT, kva, s));
-    TL_CU(launch_kv_write_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, kva, e->kc, e->vc, e->ks, e->vs,
-                                  slot_base, l, e->L, e->P, s));
+    // RoPE of q in place, RoPE(k) and v maxima per (sequence, kv head), then the INT8 cache
+    TL_CU(launch_rope_stats_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->cosT, e->sinT, kva, s));
+    TL_CU(launch_kv_write_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->cosT, e->sinT, kva, e->kc, e->vc, e->ks,
+                                  e->vs, slot_base, l, e->L, e->P, s));
     TL_CU(launch_attn_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->kc, e->vc, e->ks, e->vs, slot_base,
                               l, e->L, e->P, p.att, am + n_seq, s));
     const int8_t* xin = p.xq;

@@ -874,70 +874,109 @@ cudaError_t launch_quantize_rows(const float* x, const float* absmax_groups, int
   return cudaGetLastError();
 }
 
-// RoPE in place on all q and k heads of one row; absmax of rotated K and of V
-// per (sequence, kv head). One warp per head, lane = pair index.
-__global__ void rope_prefill_kernel(float* qkv, int ld, int seq_len, int H, int Hkv,
-                                    const float* cos, const float* sin, float* kv_absmax) {
-  const int r = blockIdx.x;
-  const int t = r % seq_len, seq = r / seq_len;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  float* row = qkv + static_cast<size_t>(r) * ld;
-  const float* cs = cos + static_cast<size_t>(t) * 64;
-  const float* sn = sin + static_cast<size_t>(t) * 64;
-  for (int hh = warp; hh < H + 2 * Hkv; hh += nw) {
-    if (hh < H + Hkv) {
-      float* x = row + hh * 64;  // q heads then k heads are contiguous
-      const float a0 = x[lane], a1 = x[lane + 32];
-      const float r0 = __fadd_rn(__fmul_rn(a0, cs[lane]), __fmul_rn(-a1, sn[lane]));
-      const float r1 = __fadd_rn(__fmul_rn(a1, cs[lane + 32]), __fmul_rn(a0, sn[lane + 32]));
-      x[lane] = r0;
-      x[lane + 32] = r1;
-      if (hh >= H) {
-        const float m = warp_max(fmaxf(fabsf(r0), fabsf(r1)));
-        if (lane == 0) atomic_max_nonneg(kv_absmax + (seq * 2 + 0) * Hkv + (hh - H), m);
+// Prefill RoPE and K / V cache fill. rope_stats_prefill_kernel rotates each
+// row's q heads in place and folds max |RoPE(k)| and max |v| per (sequence,
+// kv head) into kv_absmax without writing k; kv_write_prefill_kernel
+// recomputes the same rotated k and writes K and V quantized with those
+// scales. Rotations use the float32 roundings of the decode path. One warp
+// per row: for q, lanes 0-15 / 16-31 take two heads at a time with float2
+// accesses to dims (2j, 2j + 1) and (2j + 32, 2j + 33); for k and v, lane l
+// owns dims (l, l + 32) of every head.
+TL_DEV void rope_pair(float a0, float a1, const float* cs, const float* sn, int d, float& r0, float& r1) {
+  r0 = __fadd_rn(__fmul_rn(a0, cs[d]), __fmul_rn(-a1, sn[d]));
+  r1 = __fadd_rn(__fmul_rn(a1, cs[d + 32]), __fmul_rn(a0, sn[d + 32]));
+}
+constexpr int kKvRowsPerWarp = 8;
+__global__ void __launch_bounds__(256) rope_stats_prefill_kernel(float* qkv, int ld, int rows, int seq_len, int H,
+                                                                 int Hkv, const float* cos, const float* sin,
+                                                                 float* kv_absmax) {
+  const int lane = threadIdx.x & 31;
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int r0 = w * kKvRowsPerWarp;
+  float mk[8], mv[8];  // running maxima over this warp's rows of one sequence
+  int cur = -1;
+  auto flush = [&]() {
+    if (cur < 0) return;
+    for (int h = 0; h < Hkv; ++h) {
+      const float a = warp_max(mk[h]), b = warp_max(mv[h]);
+      if (lane == 0) {
+        atomic_max_nonneg(kv_absmax + (cur * 2 + 0) * Hkv + h, a);
+        atomic_max_nonneg(kv_absmax + (cur * 2 + 1) * Hkv + h, b);
       }
-    } else {
-      const int vh = hh - H - Hkv;
-      const float* x = row + (H + Hkv) * 64 + vh * 64;
-      const float m = warp_max(fmaxf(fabsf(x[lane]), fabsf(x[lane + 32])));
-      if (lane == 0) atomic_max_nonneg(kv_absmax + (seq * 2 + 1) * Hkv + vh, m);
+    }
+  };
+  const int j = lane & 15, hsub = lane >> 4;
+  for (int r = r0; r < min(r0 + kKvRowsPerWarp, rows); ++r) {
+    const int seq = r / seq_len, t = r % seq_len;
+    if (seq != cur) {
+      flush();
+      cur = seq;
+      for (int h = 0; h < 8; ++h) mk[h] = mv[h] = 0.0f;
+    }
+    float* row = qkv + static_cast<size_t>(r) * ld;
+    const float* cs = cos + static_cast<size_t>(t) * 64;
+    const float* sn = sin + static_cast<size_t>(t) * 64;
+    const float2 c0 = *reinterpret_cast<const float2*>(cs + 2 * j), c1 = *reinterpret_cast<const float2*>(cs + 2 * j + 32);
+    const float2 s0 = *reinterpret_cast<const float2*>(sn + 2 * j), s1 = *reinterpret_cast<const float2*>(sn + 2 * j + 32);
+    for (int h = hsub; h < H; h += 2) {
+      float2* a = reinterpret_cast<float2*>(row + h * 64 + 2 * j);
+      float2* b = reinterpret_cast<float2*>(row + h * 64 + 2 * j + 32);
+      const float2 x = *a, y = *b;
+      *a = make_float2(__fadd_rn(__fmul_rn(x.x, c0.x), __fmul_rn(-y.x, s0.x)),
+                       __fadd_rn(__fmul_rn(x.y, c0.y), __fmul_rn(-y.y, s0.y)));
+      *b = make_float2(__fadd_rn(__fmul_rn(y.x, c1.x), __fmul_rn(x.x, s1.x)),
+                       __fadd_rn(__fmul_rn(y.y, c1.y), __fmul_rn(x.y, s1.y)));
+    }
+    const float* kv = row + H * 64;
+    for (int h = 0; h < Hkv; ++h) {
+      float k0, k1;
+      rope_pair(kv[h * 64 + lane], kv[h * 64 + lane + 32], cs, sn, lane, k0, k1);
+      const float* v = kv + (Hkv + h) * 64;
+      mk[h] = fmaxf(mk[h], fmaxf(fabsf(k0), fabsf(k1)));
+      mv[h] = fmaxf(mv[h], fmaxf(fabsf(v[lane]), fabsf(v[lane + 32])));
     }
   }
+  flush();
 }
 
-cudaError_t launch_rope_prefill(float* qkv, int ld, int rows, int seq_len, int H, int Hkv,
-                                const float* cos, const float* sin, float* kv_absmax,
-                                cudaStream_t s) {
-  rope_prefill_kernel<<<rows, 256, 0, s>>>(qkv, ld, seq_len, H, Hkv, cos, sin, kv_absmax);
+cudaError_t launch_rope_stats_prefill(float* qkv, int ld, int rows, int seq_len, int H, int Hkv, const float* cos,
+                                      const float* sin, float* kv_absmax, cudaStream_t s) {
+  if (Hkv > 8 || (ld & 1)) return cudaErrorInvalidValue;
+  const int warps = (rows + kKvRowsPerWarp - 1) / kKvRowsPerWarp;
+  rope_stats_prefill_kernel<<<(warps + 7) / 8, 256, 0, s>>>(qkv, ld, rows, seq_len, H, Hkv, cos, sin, kv_absmax);
   return cudaGetLastError();
 }
 
-__global__ void kv_write_prefill_kernel(const float* qkv, int ld, int seq_len, int H, int Hkv,
-                                        const float* kv_absmax, int8_t* kc, int8_t* vc, float* ks,
-                                        float* vs, int slot_base, int layer, int L, int P) {
-  const int r = blockIdx.x;
-  const int t = r % seq_len, seq = r / seq_len;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  const float* row = qkv + static_cast<size_t>(r) * ld;
-  for (int hh = warp; hh < 2 * Hkv; hh += nw) {
+__global__ void __launch_bounds__(256) kv_write_prefill_kernel(const float* qkv, int ld, int rows, int seq_len, int H,
+                                                               int Hkv, const float* cos, const float* sin,
+                                                               const float* kv_absmax, int8_t* kc, int8_t* vc,
+                                                               float* ks, float* vs, int slot_base, int layer, int L,
+                                                               int P) {
+  const int lane = threadIdx.x & 31;
+  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (r >= rows) return;
+  const int seq = r / seq_len, t = r % seq_len;
+  const float* row = qkv + static_cast<size_t>(r) * ld + H * 64;
+  const float* cs = cos + static_cast<size_t>(t) * 64;
+  const float* sn = sin + static_cast<size_t>(t) * 64;
+  for (int hh = 0; hh < 2 * Hkv; ++hh) {
     const int kind = hh / Hkv, h = hh % Hkv;  // 0 = K, 1 = V
-    const double s64 = quant_scale64(kv_absmax[(seq * 2 + kind) * Hkv + h]);
-    const float sf = static_cast<float>(s64);
-    const float* x = row + (H + kind * Hkv + h) * 64;
+    const float sf = static_cast<float>(quant_scale64(kv_absmax[(seq * 2 + kind) * Hkv + h]));
+    float a0 = row[hh * 64 + lane], a1 = row[hh * 64 + lane + 32];
+    if (kind == 0) rope_pair(a0, a1, cs, sn, lane, a0, a1);
     const size_t sidx = (static_cast<size_t>(slot_base + seq) * L + layer) * Hkv + h;
     int8_t* dst = (kind == 0 ? kc : vc) + (sidx * P + t) * 64;
-    dst[lane] = static_cast<int8_t>(quantize_one(x[lane], sf));
-    dst[lane + 32] = static_cast<int8_t>(quantize_one(x[lane + 32], sf));
+    dst[lane] = static_cast<int8_t>(quantize_one(a0, sf));
+    dst[lane + 32] = static_cast<int8_t>(quantize_one(a1, sf));
     if (t == 0 && lane == 0) (kind == 0 ? ks : vs)[sidx] = sf;
   }
 }
 
-cudaError_t launch_kv_write_prefill(const float* qkv, int ld, int rows, int seq_len, int H,
-                                    int Hkv, const float* kv_absmax, int8_t* kc, int8_t* vc,
-                                    float* ks, float* vs, int slot_base, int layer, int L, int P,
-                                    cudaStream_t s) {
-  kv_write_prefill_kernel<<<rows, 256, 0, s>>>(qkv, ld, seq_len, H, Hkv, kv_absmax, kc, vc, ks, vs,
-                                               slot_base, layer, L, P);
+cudaError_t launch_kv_write_prefill(const float* qkv, int ld, int rows, int seq_len, int H, int Hkv, const float* cos,
+                                    const float* sin, const float* kv_absmax, int8_t* kc, int8_t* vc, float* ks,
+                                    float* vs, int slot_base, int layer, int L, int P, cudaStream_t s) {
+  kv_write_prefill_kernel<<<(rows + 7) / 8, 256, 0, s>>>(qkv, ld, rows, seq_len, H, Hkv, cos, sin, kv_absmax, kc, vc,
+                                                          ks, vs, slot_base, layer, L, P);
   return cudaGetLastError();
 }
 

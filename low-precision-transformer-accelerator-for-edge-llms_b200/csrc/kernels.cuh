@@ -192,17 +192,16 @@ cudaError_t launch_norm_quant_prefill(const float* x, const float* gamma, float 
                                       int8_t* out_q, cudaStream_t s);
 cudaError_t launch_absmax_rows(const float* x, int rows, int K, int rows_per_group, float* absmax,
                                cudaStream_t s);
-// RoPE on q and k of qkv [rows][ld] in place (positions t = row % seq_len) and
-// per (seq, kv head) absmax of rotated K and of V -> kv_absmax[seq][2][Hkv].
-cudaError_t launch_rope_prefill(float* qkv, int ld, int rows, int seq_len, int H, int Hkv,
-                                const float* cos, const float* sin, float* kv_absmax,
-                                cudaStream_t s);
-// Quantize K/V of qkv with the calibrated per-head scales into the cache and
-// store the float32 scales.
-cudaError_t launch_kv_write_prefill(const float* qkv, int ld, int rows, int seq_len, int H,
-                                    int Hkv, const float* kv_absmax, int8_t* kc, int8_t* vc,
-                                    float* ks, float* vs, int slot_base, int layer, int L, int P,
-                                    cudaStream_t s);
+// Prefill RoPE and K / V cache fill (rows grouped by sequence of seq_len,
+// positions 0..seq_len-1): rope_stats rotates q in place and folds max
+// |RoPE(k)| and max |v| per (sequence, kv head) into kv_absmax (zero on
+// entry, [seq][2][Hkv]); kv_write recomputes RoPE(k) and stores K and V
+// quantized with those scales (and the scales).
+cudaError_t launch_rope_stats_prefill(float* qkv, int ld, int rows, int seq_len, int H, int Hkv, const float* cos,
+                                      const float* sin, float* kv_absmax, cudaStream_t s);
+cudaError_t launch_kv_write_prefill(const float* qkv, int ld, int rows, int seq_len, int H, int Hkv, const float* cos,
+                                    const float* sin, const float* kv_absmax, int8_t* kc, int8_t* vc, float* ks,
+                                    float* vs, int slot_base, int layer, int L, int P, cudaStream_t s);
 // Causal attention of a prefilled batch: q from qkv (rotated), K/V from cache.
 cudaError_t launch_attn_prefill(const float* qkv, int ld, int rows, int seq_len, int H, int Hkv,
                                 const int8_t* kc, const int8_t* vc, const float* ks,
