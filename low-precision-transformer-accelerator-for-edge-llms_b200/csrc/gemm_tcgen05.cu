@@ -478,13 +478,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // CTAs in flight share token tiles in L2). Roles: warp 0 lane 0 streams A/B
 // k-blocks through a 4-stage ring (48 KB a stage) across tile boundaries;
 // warp 1 lane 0 issues the MMAs of tile i into TMEM accumulator i % 2 (two
-// 256-column buffers, all 512 columns); warps 2..9 drain accumulator i % 2
+// 256-column buffers, all 512 columns); warps 2..13 drain accumulator i % 2
 // while tile i + 1 accumulates in the other, so the epilogue runs under the
 // main loop instead of after it. Epilogue warp w reads TMEM lanes
-// 32 (w % 4) .. + 31 (the lanes its warp rank may access) and tokens
-// 128 ((w - 2) / 4) .. + 127 of the tile. Handshakes: acc_full[b] (MMA
-// commit -> epilogue), acc_empty[b] (8 epilogue-warp arrivals -> MMA).
-constexpr int kPThreads = 320;
+// 32 (w % 4) .. + 31 (the lanes its warp rank may access) and token chunks
+// [16 p / 3, 16 (p + 1) / 3) of 16 tokens, p = (w - 2) / 4 (three warps per
+// lane quarter). Handshakes: acc_full[b] (MMA commit -> epilogue),
+// acc_empty[b] (12 epilogue-warp arrivals -> MMA).
+constexpr int kPEpiWarps = 12;
+constexpr int kPParts = kPEpiWarps / 4;  // epilogue warps per TMEM lane quarter
+constexpr int kPThreads = 32 * (2 + kPEpiWarps);
 constexpr int kPBN = 256;
 constexpr int kPStages = 4;
 constexpr int kPStage = kABytes + kPBN * kTileK;
@@ -513,7 +516,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(acc_full + b, 1);
-      mbar_init(acc_empty + b, 8);
+      mbar_init(acc_empty + b, kPEpiWarps);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_w)) : "memory");
@@ -585,14 +588,15 @@ __global__ void __launch_bounds__(kPThreads, 1)
   } else {
     // epilogue warps
     const int q = warp & 3;
-    const int half = (warp - 2) >> 2;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(half * 128);
+    const int part = (warp - 2) >> 2;
+    const int c0 = part * 16 / kPParts, c1 = (part + 1) * 16 / kPParts;  // this warp's 16-token chunks
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(c0 * 16);
     const bool has_amax = kFloatEpi && a.out_absmax != nullptr;
     pdl_wait();  // token scales and residuals come from the previous kernel
     int i = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
       const int b = i & 1, u = i >> 1;
-      const int n0 = (t % n_tiles) * kTileN, m0 = (t / n_tiles) * kPBN + half * 128;
+      const int n0 = (t % n_tiles) * kTileN, m0 = (t / n_tiles) * kPBN + c0 * 16;
       const int n = n0 + q * 32 + lane;
       const bool n_ok = n < a.N;
       double sw = 0.0;
@@ -616,7 +620,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
       if (!ready) break;
       // chunks of 16 tokens this warp holds; a warp with none still releases
       // the buffer (after the acc_full wait, so no arrival runs a phase ahead)
-      const int nch = a.M > m0 ? min(8, (a.M - m0 + 15) / 16) : 0;
+      const int nch = a.M > m0 ? min(c1 - c0, (a.M - m0 + 15) / 16) : 0;
       if (nch == 0) {
         tc_fence_before();
         __syncwarp();
