@@ -731,12 +731,13 @@ __global__ void __launch_bounds__(128) attn_prefill_mma_kernel(
 
 // ------------------------------------------------- prefill on tcgen05
 // The same causal attention with the products on the 5th-generation tensor
-// cores. CTA = (128-query tile, q head, sequence); with S = kApfSplit key
-// slices per row, 32 (4 S + 4) threads:
+// cores, as a persistent grid: one CTA per SM walks work items = (128-query
+// tile, q head, sequence), longest rows first. With S = kApfSplit key slices
+// per row, 32 (4 S + 1 + 3 + 4) threads:
 //   warps 0 .. 4S-1  softmax: warps w, w + 4, .. share query rows 32 (w % 4)
 //              .. + 31 (the TMEM lanes their warp rank may read); warp w
 //              takes key slice w / 4 of each 128-key tile (128 / S keys) and
-//              output dims (64 / S) (w / 4) ..; warps 0-3 also prepare Q;
+//              output dims (64 / S) (w / 4) ..;
 //   warp 4S    issues the MMAs (one thread);
 //   warps 4S+1 .. 4S+3  convert each tile's INT8 K rows (contiguous in the
 //              cache; every 16-byte load of a lane is issued before the
@@ -744,7 +745,9 @@ __global__ void __launch_bounds__(128) attn_prefill_mma_kernel(
 //              S = Q.K^T, in two buffers (two tiles ahead of the MMAs);
 //   warps 4S+4 .. 4S+7  the same for V into its natural [key][dim] layout,
 //              the MN-major B operand of O = P.V (one buffer: V_j waits for
-//              PV_{j-1}, its loads do not).
+//              PV_{j-1}, its loads do not); they also prepare each item's
+//              query rows (fp16 hi/lo operands), the next item's while the
+//              current one finishes.
 // Per key tile j: S_j = Q_hi.K^T + Q_lo.K^T (kind::f16, fp32 accumulate)
 // into TMEM columns 128 (j % 2) ..; each softmax thread reads its slice of
 // S_j once, the slices of a row exchange their maxima through shared
@@ -753,9 +756,8 @@ __global__ void __launch_bounds__(128) attn_prefill_mma_kernel(
 // 256 + 64 (j % 2) and is folded into the fp32 registers of O two tiles
 // later, so no softmax step waits for the P.V it has just fed; the MMA
 // thread issues QK_{j+2} before PV_j (the softmax is the critical path).
-// The K / V loads and conversions start before Q is prepared (only QK_0
-// waits for it). Numerics are those of the mma.sync kernel above (exact fp16 K / V,
-// hi/lo Q and P, fp32 accumulation, base-2 online softmax).
+// Numerics are those of the mma.sync kernel above (exact fp16 K / V, hi/lo
+// Q and P, fp32 accumulation, base-2 online softmax).
 constexpr int kApfRows = 128;
 constexpr int kApfKeys = 128;
 constexpr int kApfSplit = 2;                       // key slices per row
@@ -839,8 +841,57 @@ TL_DEV void apf_store_rows(unsigned char* dst, int t, int T, const ApfChunks& c)
   }
 }
 
+// Work item `it` of the persistent grid, longest query rows first: query
+// tile qt (rows 128 qt ..), q head, sequence, its kv head and cache index.
+struct ApfItem {
+  int qt, head, seq;
+  size_t sidx;
+};
+TL_DEV ApfItem apf_item(int it, int n_qt, int H, int Hkv, int nseq, int slot_base, int L, int layer) {
+  const int per = H * nseq;
+  ApfItem w;
+  w.qt = n_qt - 1 - it / per;
+  const int rem = it % per;
+  w.head = rem % H;
+  w.seq = rem / H;
+  w.sidx = (static_cast<size_t>(slot_base + w.seq) * L + layer) * Hkv + w.head / (H / Hkv);
+  return w;
+}
+
+// Query row `row` of item w -> power-of-two scaled fp16 hi/lo operand rows
+// and the row's score scale (without the K scale) in xsc; the sixteen
+// 16-byte loads are in flight before the first use.
+TL_DEV void apf_prep_q_row(unsigned char* sm, float* xsc, const float* qkv, int ld, int seq_len, const ApfItem& w,
+                           int row) {
+  const int t = w.qt * kApfRows + row;
+  const float4* q4 = reinterpret_cast<const float4*>(
+      qkv + static_cast<size_t>(w.seq * seq_len + (t < seq_len ? t : 0)) * ld + w.head * 64);
+  float4 x[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) x[i] = t < seq_len ? __ldg(q4 + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  float mx = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(x[i].x), fabsf(x[i].y)), fmaxf(fabsf(x[i].z), fabsf(x[i].w))));
+  const float qs = pow2_scale(mx);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint4 hi, lo;
+    split2_fast(x[2 * c].x * qs, x[2 * c].y * qs, hi.x, lo.x);
+    split2_fast(x[2 * c].z * qs, x[2 * c].w * qs, hi.y, lo.y);
+    split2_fast(x[2 * c + 1].x * qs, x[2 * c + 1].y * qs, hi.z, lo.z);
+    split2_fast(x[2 * c + 1].z * qs, x[2 * c + 1].w * qs, hi.w, lo.w);
+    const uint32_t off = sw128_offset(row, c);
+    *reinterpret_cast<uint4*>(sm + kApfOffQHi + off) = hi;
+    *reinterpret_cast<uint4*>(sm + kApfOffQLo + off) = lo;
+  }
+  // (the K scale is applied by the softmax threads: sc2 = xsc * sK, the same
+  // single rounding of sK * log2 e as sK * 0.125 * log2 e / qs)
+  xsc[row] = 0.125f * kLog2e / qs;
+}
+
 __global__ void __launch_bounds__(kApfThreads, 1) attn_prefill_tc_kernel(
-    const float* __restrict__ qkv, int ld, int seq_len, int H, int Hkv, const int8_t* __restrict__ kc,
+    const float* __restrict__ qkv, int ld, int seq_len, int nseq, int H, int Hkv, const int8_t* __restrict__ kc,
     const int8_t* __restrict__ vc, const float* __restrict__ ks, const float* __restrict__ vs, int slot_base,
     int layer, int L, int P, float* __restrict__ out, float* __restrict__ out_absmax) {
   extern __shared__ __align__(1024) unsigned char apf_raw[];
@@ -849,26 +900,26 @@ __global__ void __launch_bounds__(kApfThreads, 1) attn_prefill_tc_kernel(
   float* xl = xmax + 2 * kApfSplit * 128;                      // [S][128] final l
   float* xsc = xl + kApfSplit * 128;                           // [128] row score scales
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kApfOffBar);
-  uint64_t* k_full = bar + 0;       // [2] fp16 K operand of tile j written to buffer j % 2
-  uint64_t* k_free = bar + 2;       // [2] S MMAs reading buffer j % 2 completed
+  uint64_t* k_full = bar + 0;       // [2] fp16 K operand of tile g written to buffer g % 2
+  uint64_t* k_free = bar + 2;       // [2] S MMAs reading buffer g % 2 completed
   uint64_t* v_full = bar + 6;       // fp16 V operand written
   uint64_t* v_free = bar + 7;       // P.V MMAs reading it completed
-  uint64_t* s_full = bar + 8;       // [2] S_j in TMEM
-  uint64_t* s_free = bar + 10;      // [2] the softmax warps have read S_j
-  uint64_t* p_full = bar + 12;      // [2] P_j written to buffer j % 2
-  uint64_t* o_full = bar + 14;      // [2] P_j.V_j in TMEM; P buffer j % 2 no longer read
+  uint64_t* s_full = bar + 8;       // [2] S_g in TMEM
+  uint64_t* s_free = bar + 10;      // [2] the softmax warps have read S_g
+  uint64_t* p_full = bar + 12;      // [2] P_g written to buffer g % 2
+  uint64_t* o_full = bar + 14;      // [2] P_g.V_g in TMEM; P buffer g % 2 no longer read
   uint64_t* xbar = bar + 16;        // [4] the softmax warps of rows 32 q .. exchanged values
-  uint64_t* q_full = bar + 20;      // Q operands and row scales written (warps 0-3)
+  uint64_t* q_full = bar + 20;      // an item's Q operands and row scales written (V converter warps)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 21);
 
-  const int qt = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);  // longest rows first
-  const int head = blockIdx.y, seq = blockIdx.z;
+  // Tiles are numbered g = 0, 1, .. across this CTA's items (every role
+  // walks the same items in the same order); all buffer indices and mbarrier
+  // phases follow g, so an item's first tiles wait on the previous item's
+  // last ones exactly as within an item.
+  const int n_qt = (seq_len + kApfRows - 1) / kApfRows;
+  const int items = n_qt * H * nseq;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int h = head / (H / Hkv);
   const int Dq = H * 64;
-  const int q0 = qt * kApfRows;
-  const int n_kt = qt + 1;  // key tiles 0..qt cover positions 0..q0 + 127
-  const size_t sidx = (static_cast<size_t>(slot_base + seq) * L + layer) * Hkv + h;
 
   if (tid == 0) {
     for (int i = 0; i < 8; ++i) mbar_init(bar + i, 1);
@@ -881,7 +932,7 @@ __global__ void __launch_bounds__(kApfThreads, 1) attn_prefill_tc_kernel(
       mbar_init(o_full + i, 1);
     }
     for (int i = 0; i < 4; ++i) mbar_init(xbar + i, 32 * kApfSplit);
-    mbar_init(q_full, 4);
+    mbar_init(q_full, kApfConvV);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == kApfWarpMma) tmem_alloc(tmem_slot, kApfTmemCols);
@@ -901,9 +952,8 @@ __global__ void __launch_bounds__(kApfThreads, 1) attn_prefill_tc_kernel(
       const uint64_t dk0 = smem_desc_sw128(smem_u32(sm + kApfOffK));
       const uint64_t dv = smem_desc_sw128_mn(smem_u32(sm + kApfOffV));
       const uint64_t dp = smem_desc_sw128(smem_u32(sm + kApfOffP));
-      bool ok = apf_wait(q_full, 0, 20u);
-      auto issue_qk = [&](int j) -> bool {
-        const int b = j & 1, u = j >> 1;
+      auto issue_qk = [&](int g) -> bool {
+        const int b = g & 1, u = g >> 1;
         if (!apf_wait(k_full + b, u & 1, 22u)) return false;
         if (u > 0 && !apf_wait(s_free + b, (u - 1) & 1, 23u)) return false;
         tc_fence_after();
@@ -918,10 +968,10 @@ __global__ void __launch_bounds__(kApfThreads, 1) attn_prefill_tc_kernel(
         mma_commit(k_free + b);
         return true;
       };
-      auto issue_pv = [&](int j) -> bool {
-        const int b = j & 1, u = j >> 1;
+      auto issue_pv = [&](int g) -> bool {
+        const int b = g & 1, u = g >> 1;
         if (!apf_wait(p_full + b, u & 1, 24u)) return false;
-        if (!apf_wait(v_full, j & 1, 25u)) return false;
+        if (!apf_wait(v_full, g & 1, 25u)) return false;
         tc_fence_after();
         const uint32_t d = tmem + 256u + static_cast<uint32_t>(64 * b);
         const uint64_t pbuf = dp + static_cast<uint64_t>(b * (kApfPBuf >> 4));
@@ -935,200 +985,208 @@ __global__ void __launch_bounds__(kApfThreads, 1) attn_prefill_tc_kernel(
         mma_commit(v_free);
         return true;
       };
-      if (ok) ok = issue_qk(0);
-      if (ok && n_kt > 1) ok = issue_qk(1);
-      for (int j = 0; j < n_kt && ok; ++j) {
-        if (j + 2 < n_kt) ok = issue_qk(j + 2);
-        if (ok) ok = issue_pv(j);
+      bool ok = true;
+      int g0 = 0, itc = 0;
+      for (int it = blockIdx.x; it < items && ok; it += gridDim.x, ++itc) {
+        const ApfItem w = apf_item(it, n_qt, H, Hkv, nseq, slot_base, L, layer);
+        const int n_kt = w.qt + 1;  // key tiles 0..qt cover positions 0..128 qt + 127
+        ok = apf_wait(q_full, itc & 1, 20u);
+        if (ok) ok = issue_qk(g0);
+        if (ok && n_kt > 1) ok = issue_qk(g0 + 1);
+        for (int j = 0; j < n_kt && ok; ++j) {
+          if (j + 2 < n_kt) ok = issue_qk(g0 + j + 2);
+          if (ok) ok = issue_pv(g0 + j);
+        }
+        g0 += n_kt;
       }
     }
   } else if (warp >= kApfWarpConvK) {
-    // K: tile j into buffer j % 2 once QK_{j-2} (its last reader) completed;
-    // V: tile j once PV_{j-1} completed. The tile's loads go first.
+    // K (S operand): tile g into buffer g % 2 once QK_{g-2} completed.
+    // V (P.V operand): tile g once PV_{g-1} completed; the V warps also
+    // prepare each item's Q rows (one per thread), the next item's once the
+    // softmax warps have read the current item's last S (so the current Q
+    // and row scales are no longer needed). Each tile's loads go first.
     const bool is_v = warp >= kApfWarpConvK + kApfConvK;
     const int T = 32 * (is_v ? kApfConvV : kApfConvK);
     const int ct = tid - 32 * (is_v ? kApfWarpConvK + kApfConvK : kApfWarpConvK);
-    const unsigned char* rows =
-        reinterpret_cast<const unsigned char*>(is_v ? vc : kc) + sidx * static_cast<size_t>(P) * 64;
-    for (int j = 0; j < n_kt; ++j) {
-      const int b = j & 1, u = j >> 1;
-      const int kv0 = j * kApfKeys;
-      ApfChunks c;
-      apf_load_rows(rows + static_cast<size_t>(kv0) * 64, ct, T, min(kApfKeys, P - kv0), c);
-      if (is_v) {
-        if (j > 0 && !apf_wait(v_free, (j - 1) & 1, 27u)) break;
-        apf_store_rows(sm + kApfOffV, ct, T, c);
-      } else {
-        if (u > 0 && !apf_wait(k_free + b, (u - 1) & 1, 26u)) break;
-        apf_store_rows(sm + kApfOffK + b * 16384, ct, T, c);
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(is_v ? v_full : k_full + b);
-    }
-  } else {
-    if (warp < 4) {
-      // row tid's query -> power-of-two scaled fp16 hi/lo operands; the
-      // row's sixteen 16-byte loads are all in flight before the first use
-      const int t = q0 + tid;
-      const float4* q4 = reinterpret_cast<const float4*>(
-          qkv + static_cast<size_t>(seq * seq_len + (t < seq_len ? t : 0)) * ld + head * 64);
-      float4 x[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) x[i] = t < seq_len ? __ldg(q4 + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      float mx = 0.0f;
-#pragma unroll
-      for (int i = 0; i < 16; ++i)
-        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(x[i].x), fabsf(x[i].y)), fmaxf(fabsf(x[i].z), fabsf(x[i].w))));
-      const float qs = pow2_scale(mx);
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint4 hi, lo;
-        split2_fast(x[2 * c].x * qs, x[2 * c].y * qs, hi.x, lo.x);
-        split2_fast(x[2 * c].z * qs, x[2 * c].w * qs, hi.y, lo.y);
-        split2_fast(x[2 * c + 1].x * qs, x[2 * c + 1].y * qs, hi.z, lo.z);
-        split2_fast(x[2 * c + 1].z * qs, x[2 * c + 1].w * qs, hi.w, lo.w);
-        const uint32_t off = sw128_offset(tid, c);
-        *reinterpret_cast<uint4*>(sm + kApfOffQHi + off) = hi;
-        *reinterpret_cast<uint4*>(sm + kApfOffQLo + off) = lo;
-      }
-      // (the K scale is applied by the softmax threads: sc2 = xsc * sK,
-      // the same single rounding of sK * log2 e as sK * 0.125 * log2 e / qs)
-      xsc[tid] = 0.125f * kLog2e / qs;
+    int g = 0;
+    bool ok = true;
+    if (is_v && static_cast<int>(blockIdx.x) < items) {
+      apf_prep_q_row(sm, xsc, qkv, ld, seq_len, apf_item(blockIdx.x, n_qt, H, Hkv, nseq, slot_base, L, layer), ct);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(q_full);
     }
+    for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
+      const ApfItem w = apf_item(it, n_qt, H, Hkv, nseq, slot_base, L, layer);
+      const int n_kt = w.qt + 1;
+      const unsigned char* rows =
+          reinterpret_cast<const unsigned char*>(is_v ? vc : kc) + w.sidx * static_cast<size_t>(P) * 64;
+      for (int j = 0; j < n_kt && ok; ++j, ++g) {
+        const int b = g & 1, u = g >> 1;
+        const int kv0 = j * kApfKeys;
+        ApfChunks c;
+        apf_load_rows(rows + static_cast<size_t>(kv0) * 64, ct, T, min(kApfKeys, P - kv0), c);
+        if (is_v) {
+          if (g > 0 && !(ok = apf_wait(v_free, (g - 1) & 1, 27u))) break;
+          apf_store_rows(sm + kApfOffV, ct, T, c);
+        } else {
+          if (u > 0 && !(ok = apf_wait(k_free + b, (u - 1) & 1, 26u))) break;
+          apf_store_rows(sm + kApfOffK + b * 16384, ct, T, c);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(is_v ? v_full : k_full + b);
+      }
+      const int next = it + static_cast<int>(gridDim.x);
+      if (is_v && ok && next < items) {
+        const int gl = g - 1;  // this item's last tile
+        if (!(ok = apf_wait(s_free + (gl & 1), (gl >> 1) & 1, 21u))) break;
+        apf_prep_q_row(sm, xsc, qkv, ld, seq_len, apf_item(next, n_qt, H, Hkv, nseq, slot_base, L, layer), ct);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(q_full);
+      }
+    }
+  } else {
     // softmax warps: row r, key slice ks_ (keys kApfSliceKeys ks_ ..), dims kApfSliceDims ks_ ..
     const int qq = warp & 3, ks_ = warp >> 2;
-    const int r = qq * 32 + lane, t = q0 + r;
+    const int r = qq * 32 + lane;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(qq * 32) << 16);
-    float m2 = -INFINITY, l = 0.0f;  // running max (log2 units), running sum of p * 2^14 (this slice)
-    float c_prev = 1.0f;             // correction of the previous tile (m_{j-2} -> m_{j-1})
-    uint32_t xph = 0;                // phases of xbar[qq] completed so far
+    uint32_t xph = 0;  // phases of xbar[qq] completed so far
     float o[kApfSliceDims];
-#pragma unroll
-    for (int i = 0; i < kApfSliceDims; ++i) o[i] = 0.0f;
-    auto fold = [&](int jj, float scale) -> bool {
-      // o += scale * (P_jj . V_jj) for this slice's dims
-      if (!apf_wait(o_full + (jj & 1), (jj >> 1) & 1, 30u)) return false;
+    auto fold = [&](int gg, float scale) -> bool {
+      // o += scale * (P_gg . V_gg) for this slice's dims
+      if (!apf_wait(o_full + (gg & 1), (gg >> 1) & 1, 30u)) return false;
       tc_fence_after();
 #pragma unroll
       for (int hh = 0; hh < kApfSliceDims / 16; ++hh) {
-        int w[16];
-        tmem_ld16(lane_base + 256u + static_cast<uint32_t>(64 * (jj & 1) + kApfSliceDims * ks_ + 16 * hh), w);
+        int w16[16];
+        tmem_ld16(lane_base + 256u + static_cast<uint32_t>(64 * (gg & 1) + kApfSliceDims * ks_ + 16 * hh), w16);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) o[16 * hh + i] = fmaf(__int_as_float(w[i]), scale, o[16 * hh + i]);
+        for (int i = 0; i < 16; ++i) o[16 * hh + i] = fmaf(__int_as_float(w16[i]), scale, o[16 * hh + i]);
       }
       return true;
     };
-    const float sk = __ldg(ks + sidx);
-    bool ok = apf_wait(q_full, 0, 28u);  // the row scales in xsc
-    const float sc2 = xsc[r] * sk;
-    for (int j = 0; j < n_kt && ok; ++j) {
-      const int b = j & 1, u = j >> 1;
-      if (!(ok = apf_wait(s_full + b, u & 1, 29u))) break;
-      tc_fence_after();
-      const bool diag = j == qt;
-      const int lim = t - j * kApfKeys - kApfSliceKeys * ks_;  // keys k > lim of this slice are masked
-      const uint32_t sb = lane_base + static_cast<uint32_t>(b * kApfKeys + kApfSliceKeys * ks_);
-      // row maximum of the raw scores (the scale is positive), 32 columns at
-      // a time in 8-way trees, then across the row's slices through shared
-      // memory (double-buffered by tile parity: a warp writes buffer b again
-      // only after every partner's arrival for tile j + 1, which follows its
-      // read of tile j)
-      float mraw = -INFINITY;
+    bool ok = true;
+    int g0 = 0, itc = 0;
+    for (int it = blockIdx.x; it < items && ok; it += gridDim.x, ++itc) {
+      const ApfItem w = apf_item(it, n_qt, H, Hkv, nseq, slot_base, L, layer);
+      const int qt = w.qt, n_kt = qt + 1;
+      const int t = qt * kApfRows + r;
+      const float sk = __ldg(ks + w.sidx);
+      if (!(ok = apf_wait(q_full, itc & 1, 28u))) break;  // the row scales in xsc
+      const float sc2 = xsc[r] * sk;
+      float m2 = -INFINITY, l = 0.0f;  // running max (log2 units), running sum of p * 2^14 (this slice)
+      float c_prev = 1.0f;             // correction of the previous tile (m_{j-2} -> m_{j-1})
 #pragma unroll
-      for (int cc = 0; cc < kApfSliceKeys / 32; ++cc) {
-        uint32_t v[32];
-        tmem_ld32(sb + 32 * cc, v);
-        if (diag) {
+      for (int i = 0; i < kApfSliceDims; ++i) o[i] = 0.0f;
+      for (int j = 0; j < n_kt && ok; ++j) {
+        const int g = g0 + j, b = g & 1, u = g >> 1;
+        if (!(ok = apf_wait(s_full + b, u & 1, 29u))) break;
+        tc_fence_after();
+        const bool diag = j == qt;
+        const int lim = t - j * kApfKeys - kApfSliceKeys * ks_;  // keys k > lim of this slice are masked
+        const uint32_t sb = lane_base + static_cast<uint32_t>(b * kApfKeys + kApfSliceKeys * ks_);
+        // row maximum of the raw scores (the scale is positive), 32 columns at
+        // a time in 8-way trees, then across the row's slices through shared
+        // memory (double-buffered by tile parity: a warp writes buffer b again
+        // only after every partner's arrival for tile g + 1, which follows its
+        // read of tile g)
+        float mraw = -INFINITY;
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (32 * cc + i > lim) v[i] = __float_as_uint(-INFINITY);
+        for (int cc = 0; cc < kApfSliceKeys / 32; ++cc) {
+          uint32_t v[32];
+          tmem_ld32(sb + 32 * cc, v);
+          if (diag) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (32 * cc + i > lim) v[i] = __float_as_uint(-INFINITY);
+          }
+          float mq[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            mq[i] = fmaxf(fmaxf(__uint_as_float(v[i]), __uint_as_float(v[i + 8])),
+                          fmaxf(__uint_as_float(v[i + 16]), __uint_as_float(v[i + 24])));
+          mraw = fmaxf(mraw, fmaxf(fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])),
+                                   fmaxf(fmaxf(mq[4], mq[5]), fmaxf(mq[6], mq[7]))));
         }
-        float mq[8];
+        xmax[(b * kApfSplit + ks_) * 128 + r] = mraw;
+        mbar_arrive(xbar + qq);
+        if (!(ok = apf_wait(xbar + qq, xph & 1, 32u))) break;
+        ++xph;
+        mraw = xmax[(b * kApfSplit) * 128 + r];
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          mq[i] = fmaxf(fmaxf(__uint_as_float(v[i]), __uint_as_float(v[i + 8])),
-                        fmaxf(__uint_as_float(v[i + 16]), __uint_as_float(v[i + 24])));
-        mraw = fmaxf(mraw, fmaxf(fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])),
-                                 fmaxf(fmaxf(mq[4], mq[5]), fmaxf(mq[6], mq[7]))));
-      }
-      xmax[(b * kApfSplit + ks_) * 128 + r] = mraw;
-      mbar_arrive(xbar + qq);
-      if (!(ok = apf_wait(xbar + qq, xph & 1, 32u))) break;
-      ++xph;
-      mraw = xmax[(b * kApfSplit) * 128 + r];
+        for (int k = 1; k < kApfSplit; ++k) mraw = fmaxf(mraw, xmax[(b * kApfSplit + k) * 128 + r]);
+        const float m_new = fmaxf(m2, mraw * sc2);
+        const float corr = ex2f(m2 - m_new);
+        m2 = m_new;
+        // o holds tiles <= j - 3 at max m_{j-1}; P_{j-2}.V_{j-2} is at m_{j-2}.
+        // Its completion also frees P buffer b for P_j (for j < 2 the previous
+        // item's final folds have waited for P_{g-2}.V_{g-2} already).
 #pragma unroll
-      for (int k = 1; k < kApfSplit; ++k) mraw = fmaxf(mraw, xmax[(b * kApfSplit + k) * 128 + r]);
-      const float m_new = fmaxf(m2, mraw * sc2);
-      const float corr = ex2f(m2 - m_new);
-      m2 = m_new;
-      // o holds tiles <= j - 3 at max m_{j-1}; P_{j-2}.V_{j-2} is at m_{j-2}.
-      // Its completion also frees P buffer b for P_j.
+        for (int i = 0; i < kApfSliceDims; ++i) o[i] *= corr;
+        if (j >= 2 && !(ok = fold(g - 2, c_prev * corr))) break;
+        c_prev = corr;
+        // p * 2^14 = 2^(s * sc2 - m + 14) (masked scores are -inf: p = 0) as
+        // fp16 hi + lo into this slice's chunks of P buffer b; l sums the p in
+        // an 8-way tree
+        const float off14 = 14.0f - m_new;
+        float lq[8];
 #pragma unroll
-      for (int i = 0; i < kApfSliceDims; ++i) o[i] *= corr;
-      if (j >= 2 && !(ok = fold(j - 2, c_prev * corr))) break;
-      c_prev = corr;
-      // p * 2^14 = 2^(s * sc2 - m + 14) (masked scores are -inf: p = 0) as
-      // fp16 hi + lo into this slice's chunks of P buffer b; l sums the p in
-      // an 8-way tree
-      const float off14 = 14.0f - m_new;
-      float lq[8];
+        for (int i = 0; i < 8; ++i) lq[i] = 0.0f;
+        unsigned char* pb = sm + kApfOffP + b * kApfPBuf;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) lq[i] = 0.0f;
-      unsigned char* pb = sm + kApfOffP + b * kApfPBuf;
+        for (int cc = 0; cc < kApfSliceKeys / 32; ++cc) {
+          uint32_t v[32];
+          tmem_ld32(sb + 32 * cc, v);
 #pragma unroll
-      for (int cc = 0; cc < kApfSliceKeys / 32; ++cc) {
-        uint32_t v[32];
-        tmem_ld32(sb + 32 * cc, v);
+          for (int i = 0; i < 32; ++i) {
+            const bool live = !diag || 32 * cc + i <= lim;
+            const float p = live ? ex2f(fmaf(__uint_as_float(v[i]), sc2, off14)) : 0.0f;
+            v[i] = __float_as_uint(p);
+            lq[i & 7] += p;
+          }
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const bool live = !diag || 32 * cc + i <= lim;
-          const float p = live ? ex2f(fmaf(__uint_as_float(v[i]), sc2, off14)) : 0.0f;
-          v[i] = __float_as_uint(p);
-          lq[i & 7] += p;
+          for (int gq = 0; gq < 4; ++gq) {
+            uint4 hi, lo;
+            split2_fast(__uint_as_float(v[8 * gq + 0]), __uint_as_float(v[8 * gq + 1]), hi.x, lo.x);
+            split2_fast(__uint_as_float(v[8 * gq + 2]), __uint_as_float(v[8 * gq + 3]), hi.y, lo.y);
+            split2_fast(__uint_as_float(v[8 * gq + 4]), __uint_as_float(v[8 * gq + 5]), hi.z, lo.z);
+            split2_fast(__uint_as_float(v[8 * gq + 6]), __uint_as_float(v[8 * gq + 7]), hi.w, lo.w);
+            const int key = kApfSliceKeys * ks_ + 32 * cc + 8 * gq;
+            const uint32_t off = static_cast<uint32_t>((key >> 6) * 16384) + sw128_offset(r, (key & 63) >> 3);
+            *reinterpret_cast<uint4*>(pb + off) = hi;
+            *reinterpret_cast<uint4*>(pb + 32768 + off) = lo;
+          }
         }
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          uint4 hi, lo;
-          split2_fast(__uint_as_float(v[8 * g + 0]), __uint_as_float(v[8 * g + 1]), hi.x, lo.x);
-          split2_fast(__uint_as_float(v[8 * g + 2]), __uint_as_float(v[8 * g + 3]), hi.y, lo.y);
-          split2_fast(__uint_as_float(v[8 * g + 4]), __uint_as_float(v[8 * g + 5]), hi.z, lo.z);
-          split2_fast(__uint_as_float(v[8 * g + 6]), __uint_as_float(v[8 * g + 7]), hi.w, lo.w);
-          const int key = kApfSliceKeys * ks_ + 32 * cc + 8 * g;
-          const uint32_t off = static_cast<uint32_t>((key >> 6) * 16384) + sw128_offset(r, (key & 63) >> 3);
-          *reinterpret_cast<uint4*>(pb + off) = hi;
-          *reinterpret_cast<uint4*>(pb + 32768 + off) = lo;
+        l = fmaf(l, corr, ((lq[0] + lq[1]) + (lq[2] + lq[3])) + ((lq[4] + lq[5]) + (lq[6] + lq[7])));
+        tc_fence_before();
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(s_free + b);
+          mbar_arrive(p_full + b);
         }
       }
-      l = fmaf(l, corr, ((lq[0] + lq[1]) + (lq[2] + lq[3])) + ((lq[4] + lq[5]) + (lq[6] + lq[7])));
-      tc_fence_before();
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(s_free + b);
-        mbar_arrive(p_full + b);
-      }
-    }
-    // the last two tiles' P.V: P_{J-1}.V_{J-1} at m_{J-1} (scaled by the last
-    // correction), P_J.V_J at the final maximum
-    const int J = n_kt - 1;
-    if (ok && J >= 1) ok = fold(J - 1, c_prev);
-    if (ok) ok = fold(J, 1.0f);
-    if (ok) {
+      if (!ok) break;
+      // the last two tiles' P.V: P_{J-1}.V_{J-1} at m_{J-1} (scaled by the last
+      // correction), P_J.V_J at the final maximum
+      const int gJ = g0 + n_kt - 1;
+      if (n_kt >= 2 && !(ok = fold(gJ - 1, c_prev))) break;
+      if (!(ok = fold(gJ, 1.0f))) break;
       // the row's l is the sum of its slices' (same running maximum)
       xl[ks_ * 128 + r] = l;
       mbar_arrive(xbar + qq);
-      const bool got = apf_wait(xbar + qq, xph & 1, 33u);
+      if (!(ok = apf_wait(xbar + qq, xph & 1, 33u))) break;
+      ++xph;
       float lt = xl[r];
 #pragma unroll
       for (int k = 1; k < kApfSplit; ++k) lt += xl[k * 128 + r];
       float local_max = 0.0f;
-      if (got && t < seq_len) {
-        const float inv = vs[sidx] / lt;
-        float* orow = out + static_cast<size_t>(seq * seq_len + t) * Dq + head * 64 + kApfSliceDims * ks_;
+      if (t < seq_len) {
+        const float inv = vs[w.sidx] / lt;
+        float* orow = out + static_cast<size_t>(w.seq * seq_len + t) * Dq + w.head * 64 + kApfSliceDims * ks_;
 #pragma unroll
         for (int d = 0; d < kApfSliceDims; d += 4) {
           const float4 y = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
@@ -1138,8 +1196,9 @@ __global__ void __launch_bounds__(kApfThreads, 1) attn_prefill_tc_kernel(
       }
       if (out_absmax) {
         local_max = warp_max(local_max);
-        if (lane == 0) atomic_max_nonneg(out_absmax + seq, local_max);
+        if (lane == 0) atomic_max_nonneg(out_absmax + w.seq, local_max);
       }
+      g0 += n_kt;
     }
   }
   tc_fence_before();
@@ -1157,9 +1216,10 @@ cudaError_t launch_attn_prefill(const float* qkv, int ld, int rows, int seq_len,
   const int nseq = rows / seq_len;
   if (use_apf_tc() && (reinterpret_cast<uintptr_t>(out) & 15u) == 0) {
     // (its float4 output stores need 16-byte aligned rows; Dq is a multiple of 64)
-    dim3 grid((seq_len + kApfRows - 1) / kApfRows, H, nseq);
-    attn_prefill_tc_kernel<<<grid, kApfThreads, kApfSmem, s>>>(qkv, ld, seq_len, H, Hkv, kc, vc, ks, vs,
-                                                                slot_base, layer, L, P, out, out_absmax);
+    // persistent: one CTA per SM walking the (query tile, head, sequence) items
+    const int items = ((seq_len + kApfRows - 1) / kApfRows) * H * nseq;
+    attn_prefill_tc_kernel<<<std::min(items, device_sm_count()), kApfThreads, kApfSmem, s>>>(
+        qkv, ld, seq_len, nseq, H, Hkv, kc, vc, ks, vs, slot_base, layer, L, P, out, out_absmax);
     return cudaGetLastError();
   }
   dim3 grid((seq_len + kPfQTile - 1) / kPfQTile, H, nseq);
