@@ -432,6 +432,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) attn_decode_kernel(AttnDecodeA
   }
   __syncthreads();
   if (n_act == 1) {
+    float omax = 0.0f;  // max |output| of this thread, for the row's absmax
     for (int i = tid; i < G * 64; i += kDecThreads) {
       const int gg = i >> 6, d = i & 63;
       float M = -INFINITY;
@@ -445,7 +446,13 @@ __global__ void __launch_bounds__(kDecThreads, 2) attn_decode_kernel(AttnDecodeA
         L += cw[1] * f;
         O += cw[2 + d] * f;
       }
-      a.out[static_cast<size_t>(m) * Dq + (h * G + gg) * 64 + d] = O / L * sV;
+      const float y = O / L * sV;
+      a.out[static_cast<size_t>(m) * Dq + (h * G + gg) * 64 + d] = y;
+      omax = fmaxf(omax, fabsf(y));
+    }
+    if (a.out_absmax) {
+      omax = warp_max(omax);
+      if (lane == 0) atomic_max_nonneg(a.out_absmax + m, omax);
     }
     return;
   }
@@ -481,6 +488,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) attn_decode_kernel(AttnDecodeA
   __threadfence();
   // ---- merge the splits (only the last CTA of this (row, kv head))
   const float* pall = a.part + (static_cast<size_t>(m) * a.Hkv + h) * a.splits * kAttnPartStride;
+  float omax = 0.0f;
   for (int i = tid; i < G * 64; i += kDecThreads) {
     const int gg = i >> 6, d = i & 63;
     float M = -INFINITY;
@@ -493,7 +501,13 @@ __global__ void __launch_bounds__(kDecThreads, 2) attn_decode_kernel(AttnDecodeA
       L += ps[1] * f;
       O += ps[2 + d] * f;
     }
-    a.out[static_cast<size_t>(m) * Dq + (h * G + gg) * 64 + d] = O / L * sV;
+    const float y = O / L * sV;
+    a.out[static_cast<size_t>(m) * Dq + (h * G + gg) * 64 + d] = y;
+    omax = fmaxf(omax, fabsf(y));
+  }
+  if (a.out_absmax) {
+    omax = warp_max(omax);
+    if (lane == 0) atomic_max_nonneg(a.out_absmax + m, omax);
   }
   if (tid == 0) a.counters[static_cast<size_t>(m) * a.Hkv + h] = 0u;
 }

@@ -102,6 +102,9 @@ struct DecodeBufs {
   float* logits = nullptr;  // [rows][V]
   int8_t* xq = nullptr;     // [rows][max(D, F)] int8 activations (tensor-core path)
   float* amax = nullptr;    // [rows] per-row absmax of the activation in xq
+  // [rows] per-row max |x| folded in by the producer's epilogue (attention
+  // output, SiLU*up) with atomics; zeroed by the RMSNorm kernel before it
+  float* amax_prod = nullptr;
   float* attn_part = nullptr;         // decode attention split partials
   unsigned int* attn_cnt = nullptr;   // [rows][Hkv] merge tickets
   // persistent single-sequence step (decode1.cu)
@@ -257,6 +260,7 @@ tl_status alloc_decode(tl_engine* e) {
   TL_TRY(dmalloc(&d.logits, static_cast<size_t>(B) * e->V));
   TL_TRY(dmalloc(&d.xq, static_cast<size_t>(B) * std::max(e->D, e->F)));
   TL_TRY(dmalloc(&d.amax, B));
+  TL_TRY(dmalloc(&d.amax_prod, B));
   TL_TRY(dmalloc(&d.attn_part, attn_part_floats(B, e->Hkv, e->P)));
   TL_TRY(dmalloc(&d.attn_cnt, static_cast<size_t>(B) * e->Hkv));
   TL_CU(cudaMemset(d.attn_cnt, 0, static_cast<size_t>(B) * e->Hkv * sizeof(unsigned int)));
@@ -321,7 +325,11 @@ tl_status tc_gemm(tl_engine* e, const int8_t* w, int N, const int8_t* x, int M, 
 
 // Batched decode step on the tensor cores (M >= kTcMinRows rows): per row
 // RMSNorm + INT8 quantization kernels feed tcgen05 GEMMs whose epilogues
-// dequantize, add the residual or apply SiLU*up.
+// dequantize, add the residual or apply SiLU*up. The attention kernel and
+// the SiLU*up epilogue fold each row's max |output| into d.amax_prod with
+// atomics, so the quantization of their outputs is elementwise over the
+// whole block; each RMSNorm kernel re-arms d.amax_prod (its last reader, the
+// GEMM two kernels back, has completed by then).
 tl_status enqueue_decode_step_tc(tl_engine* e, int M, bool finalize) {
   DecodeBufs& d = e->dec;
   cudaStream_t s = e->stream;
@@ -330,7 +338,7 @@ tl_status enqueue_decode_step_tc(tl_engine* e, int M, bool finalize) {
   TL_CU(launch_embed(e->embed, d.tokens, d.x, M, e->D, e->V, s, pdl));
   for (int l = 0; l < e->L; ++l) {
     const Layer& ly = e->layers[l];
-    TL_CU(launch_norm_quant_rows(d.x, ly.g1, eps, M, e->D, d.xq, d.amax, s, pdl));
+    TL_CU(launch_norm_quant_rows(d.x, ly.g1, eps, M, e->D, d.xq, d.amax, s, pdl, d.amax_prod));
     TcArgs q;
     q.epi = EPI_F32; q.w_scale = ly.sqkv; q.in_absmax = d.amax; q.rows_per_group = 1; q.out_f32 = d.qkv;
     TL_TRY(tc_gemm(e, ly.wqkv, e->Nqkv, d.xq, M, e->D, q, pdl));
@@ -339,20 +347,21 @@ tl_status enqueue_decode_step_tc(tl_engine* e, int M, bool finalize) {
     at.kc = e->kc; at.vc = e->vc; at.ks = e->ks; at.vs = e->vs;
     at.layer = l; at.L = e->L; at.H = e->H; at.Hkv = e->Hkv; at.P = e->P; at.M = M;
     at.cos = e->cosT; at.sin = e->sinT; at.out = d.att;
-    at.part = d.attn_part; at.counters = d.attn_cnt;
+    at.part = d.attn_part; at.counters = d.attn_cnt; at.out_absmax = d.amax_prod;
     TL_CU(launch_attn_decode(at, s, pdl));
-    TL_CU(launch_quant_rows(d.att, M, e->Dq, d.xq, d.amax, s, pdl));
+    TL_CU(launch_quant_known_rows(d.att, d.amax_prod, M, e->Dq, d.xq, s, pdl));
     TcArgs o;
-    o.epi = EPI_RESID; o.w_scale = ly.so; o.in_absmax = d.amax; o.rows_per_group = 1; o.out_f32 = d.x;
+    o.epi = EPI_RESID; o.w_scale = ly.so; o.in_absmax = d.amax_prod; o.rows_per_group = 1; o.out_f32 = d.x;
     o.resid = d.x;
     TL_TRY(tc_gemm(e, ly.wo, e->D, d.xq, M, e->Dq, o, pdl));
-    TL_CU(launch_norm_quant_rows(d.x, ly.g2, eps, M, e->D, d.xq, d.amax, s, pdl));
+    TL_CU(launch_norm_quant_rows(d.x, ly.g2, eps, M, e->D, d.xq, d.amax, s, pdl, d.amax_prod));
     TcArgs gu;
     gu.epi = EPI_SILU; gu.w_scale = ly.sgu; gu.in_absmax = d.amax; gu.rows_per_group = 1; gu.out_f32 = d.hid;
+    gu.out_absmax = d.amax_prod;
     TL_TRY(tc_gemm(e, ly.wgu, 2 * e->F, d.xq, M, e->D, gu, pdl));
-    TL_CU(launch_quant_rows(d.hid, M, e->F, d.xq, d.amax, s, pdl));
+    TL_CU(launch_quant_known_rows(d.hid, d.amax_prod, M, e->F, d.xq, s, pdl));
     TcArgs dn;
-    dn.epi = EPI_RESID; dn.w_scale = ly.sd; dn.in_absmax = d.amax; dn.rows_per_group = 1; dn.out_f32 = d.x;
+    dn.epi = EPI_RESID; dn.w_scale = ly.sd; dn.in_absmax = d.amax_prod; dn.rows_per_group = 1; dn.out_f32 = d.x;
     dn.resid = d.x;
     TL_TRY(tc_gemm(e, ly.wd, e->D, d.xq, M, e->F, dn, pdl));
   }
@@ -897,7 +906,7 @@ tl_status tl_destroy(tl_engine* e) {
   cudaFree(d.x); cudaFree(d.qkv); cudaFree(d.att); cudaFree(d.hid); cudaFree(d.tokens); cudaFree(d.pos);
   cudaFree(d.slots); cudaFree(d.active); cudaFree(d.count); cudaFree(d.stop); cudaFree(d.out_ids);
   cudaFree(d.run); cudaFree(d.argmax); cudaFree(d.am_key); cudaFree(d.am_partial); cudaFree(d.am_counter); cudaFree(d.logits);
-  cudaFree(d.xq); cudaFree(d.amax); cudaFree(d.attn_part); cudaFree(d.attn_cnt);
+  cudaFree(d.xq); cudaFree(d.amax); cudaFree(d.amax_prod); cudaFree(d.attn_part); cudaFree(d.attn_cnt);
   cudaFree(d.d1_layers); cudaFree(d.d1_part); cudaFree(d.d1_sync);
   PrefillBufs& p = e->pf;
   cudaFree(p.ids); cudaFree(p.x); cudaFree(p.h); cudaFree(p.qkv); cudaFree(p.att); cudaFree(p.hid);
@@ -1416,7 +1425,8 @@ tl_status tl_profile_decode_kernels(tl_engine* e, uint32_t n_seqs, uint32_t iter
           ce = launch_norm_quant_rows(d.x, ly.g1, eps, M, e->D, d.xq, d.amax, s, false);
           break;
         case 7:
-          ce = launch_quant_rows(d.hid, M, e->F, d.xq, d.amax, s, false);
+          ce = tc ? launch_quant_known_rows(d.hid, d.amax, M, e->F, d.xq, s, false)
+                  : launch_quant_rows(d.hid, M, e->F, d.xq, d.amax, s, false);
           break;
       }
       if (ce != cudaSuccess) {

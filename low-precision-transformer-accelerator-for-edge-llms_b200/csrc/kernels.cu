@@ -546,12 +546,13 @@ static cudaLaunchConfig_t row_cfg(int rows, int threads, size_t smem, cudaStream
 
 __global__ void __launch_bounds__(256) norm_quant_rows_kernel(const float* x, const float* gamma, float eps,
                                                               int D, NormPlan plan, int8_t* out_q,
-                                                              float* out_absmax) {
+                                                              float* out_absmax, float* zero_rows) {
   extern __shared__ __align__(16) unsigned char smem[];
   float* buf = reinterpret_cast<float*>(smem);
   RowScratchView rs = rs_view(buf + D, plan);
   const int r = blockIdx.x;
   pdl_wait();
+  if (threadIdx.x == 0 && zero_rows) zero_rows[r] = 0.0f;
   const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(r) * D);
   for (int i = threadIdx.x; i < D / 4; i += blockDim.x) reinterpret_cast<float4*>(buf)[i] = src[i];
   __syncthreads();
@@ -620,7 +621,7 @@ TL_DEV uint32_t quant_pack4(float4 v, float sf) {
 
 __global__ void __launch_bounds__(128) norm_quant_rows_d2048_kernel(const float* x, const float* gamma,
                                                                      float eps, int8_t* out_q,
-                                                                     float* out_absmax) {
+                                                                     float* out_absmax, float* zero_rows) {
   constexpr int D = 2048;
   __shared__ float red[2][4];
   const int r = blockIdx.x, t = threadIdx.x;
@@ -628,10 +629,13 @@ __global__ void __launch_bounds__(128) norm_quant_rows_d2048_kernel(const float*
   float gm[16], v[16];
 #pragma unroll
   for (int k = 0; k < 16; ++k) gm[k] = gamma[base + 8 * k];
+  // Only gamma (constant) is read before the wait, so the dependent GEMM may
+  // launch now and stream its weights while this kernel waits and runs.
+  pdl_launch_dependents();
   pdl_wait();
+  if (t == 0 && zero_rows) zero_rows[r] = 0.0f;
   d2048_norm_regs(x + static_cast<size_t>(r) * D, gm, eps, v, red[0]);
   const float m = d2048_absmax(v, red[1]);
-  pdl_launch_dependents();
   const float sf = static_cast<float>(quant_scale64(m));
   int8_t* dst = out_q + static_cast<size_t>(r) * D + base;
 #pragma unroll
@@ -713,6 +717,7 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rows_reg_kernel(const flo
   __shared__ float red[kQuantThreads / 32];
   const int r = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int n4 = K >> 2;
+  pdl_launch_dependents();  // nothing is read before the wait
   pdl_wait();
   const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(r) * K);
   float4 v[kQuantVec];
@@ -731,7 +736,6 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rows_reg_kernel(const flo
   m = red[0];
 #pragma unroll
   for (int w = 1; w < kQuantThreads / 32; ++w) m = fmaxf(m, red[w]);
-  pdl_launch_dependents();
   const float sf = static_cast<float>(quant_scale64(m));
   uint32_t* dst = reinterpret_cast<uint32_t*>(out_q + static_cast<size_t>(r) * K);
 #pragma unroll
@@ -743,16 +747,17 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rows_reg_kernel(const flo
 }
 
 cudaError_t launch_norm_quant_rows(const float* x, const float* gamma, float eps, int rows, int D,
-                                   int8_t* out_q, float* out_absmax, cudaStream_t s, bool pdl) {
+                                   int8_t* out_q, float* out_absmax, cudaStream_t s, bool pdl,
+                                   float* zero_rows) {
   NormPlan plan;
   if (!norm_plan(D, &plan) || D % 4) return cudaErrorInvalidValue;
   cudaLaunchAttribute attr[1];
   if (D == 2048 && plan.n_leaves == 16 && plan.leaf_len == 128) {
     cudaLaunchConfig_t cfg = row_cfg(rows, 128, 0, s, pdl, attr);
-    return cudaLaunchKernelEx(&cfg, norm_quant_rows_d2048_kernel, x, gamma, eps, out_q, out_absmax);
+    return cudaLaunchKernelEx(&cfg, norm_quant_rows_d2048_kernel, x, gamma, eps, out_q, out_absmax, zero_rows);
   }
   cudaLaunchConfig_t cfg = row_cfg(rows, 256, rmsnorm_rows_smem(D), s, pdl, attr);
-  return cudaLaunchKernelEx(&cfg, norm_quant_rows_kernel, x, gamma, eps, D, plan, out_q, out_absmax);
+  return cudaLaunchKernelEx(&cfg, norm_quant_rows_kernel, x, gamma, eps, D, plan, out_q, out_absmax, zero_rows);
 }
 
 __global__ void __launch_bounds__(256) quant_rows_kernel(const float* x, int K, int8_t* out_q, float* out_absmax) {
@@ -783,6 +788,35 @@ cudaError_t launch_quant_rows(const float* x, int rows, int K, int8_t* out_q, fl
   }
   cudaLaunchConfig_t cfg = row_cfg(rows, 256, 0, s, pdl, attr);
   return cudaLaunchKernelEx(&cfg, quant_rows_kernel, x, K, out_q, out_absmax);
+}
+
+// INT8 quantization of rows whose max |x| is already known (the producer
+// folded it into absmax[row] with atomics): elementwise, one float4 per
+// thread over the whole [rows][K] block, so the grid covers the SMs instead
+// of one CTA per row. Same scale and rounding as quant_rows_reg_kernel.
+constexpr int kQuantKnownThreads = 256;
+__global__ void __launch_bounds__(kQuantKnownThreads) quant_known_rows_kernel(const float* x, const float* absmax,
+                                                                            int rows, int K, int8_t* out_q) {
+  const int n4 = K >> 2;
+  const long long i = static_cast<long long>(blockIdx.x) * kQuantKnownThreads + threadIdx.x;
+  pdl_launch_dependents();  // nothing is read before the wait
+  pdl_wait();
+  if (i >= static_cast<long long>(rows) * n4) return;
+  const int r = static_cast<int>(i / n4);
+  const float4 v = reinterpret_cast<const float4*>(x)[i];
+  const float sf = static_cast<float>(quant_scale64(absmax[r]));
+  reinterpret_cast<uint32_t*>(out_q)[i] = quant_pack4(v, sf);
+}
+
+cudaError_t launch_quant_known_rows(const float* x, const float* absmax, int rows, int K, int8_t* out_q,
+                                    cudaStream_t s, bool pdl) {
+  if (K % 4 || rows <= 0) return cudaErrorInvalidValue;
+  const long long n4 = static_cast<long long>(rows) * (K / 4);
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg =
+      row_cfg(static_cast<int>((n4 + kQuantKnownThreads - 1) / kQuantKnownThreads), kQuantKnownThreads, 0, s, pdl,
+              attr);
+  return cudaLaunchKernelEx(&cfg, quant_known_rows_kernel, x, absmax, rows, K, out_q);
 }
 
 __global__ void __launch_bounds__(512) row_argmax_kernel(const float* logits, int V, int32_t* out) {

@@ -167,6 +167,7 @@ struct AttnDecodeArgs {
   float* part = nullptr;        // split partials, attn_part_floats(M, Hkv, P)
   unsigned int* counters = nullptr;  // [M][Hkv], zero on entry and on exit
   int splits = 0;               // set by the launcher
+  float* out_absmax = nullptr;  // [M] optional: atomic max of |out| per row (zero on entry)
 };
 constexpr int kAttnPartStride = 8 * 66;  // per split: 8 heads x (max, sum, 64 values)
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);
@@ -209,12 +210,18 @@ cudaError_t launch_attn_prefill(const float* qkv, int ld, int rows, int seq_len,
                                 float* out, float* out_absmax, cudaStream_t s);
 
 // ---- per-row (one sequence per row) activation prep for the batched path
-// out_q[r] = quantize(rmsnorm(x[r]) ), out_absmax[r] = max|rmsnorm(x[r])|
+// out_q[r] = quantize(rmsnorm(x[r]) ), out_absmax[r] = max|rmsnorm(x[r])|;
+// zero_rows[r] = 0 when given (re-arms an atomic-max buffer for a later
+// producer, after this kernel's dependency wait)
 cudaError_t launch_norm_quant_rows(const float* x, const float* gamma, float eps, int rows, int D,
-                                   int8_t* out_q, float* out_absmax, cudaStream_t s, bool pdl);
+                                   int8_t* out_q, float* out_absmax, cudaStream_t s, bool pdl,
+                                   float* zero_rows = nullptr);
 // out_q[r] = quantize(x[r]) with the row's own absmax
 cudaError_t launch_quant_rows(const float* x, int rows, int K, int8_t* out_q, float* out_absmax,
                               cudaStream_t s, bool pdl);
+// out_q[r] = quantize(x[r]) with a precomputed absmax[r] (K % 4 == 0)
+cudaError_t launch_quant_known_rows(const float* x, const float* absmax, int rows, int K, int8_t* out_q,
+                                    cudaStream_t s, bool pdl);
 // out[r] = argmax over logits[r][0..V) (lowest index on ties)
 cudaError_t launch_row_argmax(const float* logits, int rows, int V, int32_t* out, cudaStream_t s, bool pdl);
 
