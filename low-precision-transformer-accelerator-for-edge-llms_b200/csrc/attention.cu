@@ -205,9 +205,13 @@ __global__ void __launch_bounds__(kDecThreads, 2) attn_decode_kernel(AttnDecodeA
   const int g = lane >> 2, q4 = lane & 3;
   const int G = a.H / a.Hkv;
   const int Dq = a.H * 64;
-  pdl_wait();
+  // Before the dependency wait this kernel reads only state from earlier
+  // steps (positions, slots, frozen KV scales, cache rows < p): the QKV GEMM
+  // releases its dependents after its own wait, when every kernel before it
+  // has completed. The cache chunks stream in while that GEMM finishes.
   const int p = a.pos[m];
   if (p < 0 || p >= a.P) {
+    pdl_wait();
     if (sp == 0)
       for (int i = tid; i < G * 64; i += kDecThreads) a.out[static_cast<size_t>(m) * Dq + h * G * 64 + i] = 0.0f;
     return;
@@ -232,24 +236,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) attn_decode_kernel(AttnDecodeA
     for (int i = 0; i < 2 * kDecWarps; ++i) dec_mbar_init(bars + i);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  // ---- rotated queries of the group, one head per warp, power-of-two scaled
-  {
-    const int gg = warp;
-    float r0 = 0.0f, r1 = 0.0f;
-    if (gg < G) {
-      const float* qr = row + (h * G + gg) * 64;
-      const float q0 = qr[lane], q1 = qr[lane + 32];
-      r0 = __fadd_rn(__fmul_rn(q0, cs[lane]), __fmul_rn(-q1, sn[lane]));
-      r1 = __fadd_rn(__fmul_rn(q1, cs[lane + 32]), __fmul_rn(q0, sn[lane + 32]));
-    }
-    // power of two taking max |q| into [2^21, 2^22): 22-bit integer queries
-    const float qs = pow2_scale(warp_max(fmaxf(fabsf(r0), fabsf(r1)))) * 256.0f;
-    q_sm[gg * 64 + lane] = rintf(r0 * qs);
-    q_sm[gg * 64 + lane + 32] = rintf(r1 * qs);
-    if (lane == 0) q_scale[gg] = qs;
-  }
   __syncthreads();
-
   // ---- this warp's chunks and their bulk copies
   uint64_t* wbar = bars + 2 * warp;
   unsigned char* wslot = ring + warp * 2 * kDecSlot;
@@ -273,6 +260,24 @@ __global__ void __launch_bounds__(kDecThreads, 2) attn_decode_kernel(AttnDecodeA
   };
   if (lane == 0)
     for (int i = 0; i < min(2, nmine); ++i) issue(first + i * kDecWarps, i);
+  pdl_wait();
+  // ---- rotated queries of the group, one head per warp, power-of-two scaled
+  {
+    const int gg = warp;
+    float r0 = 0.0f, r1 = 0.0f;
+    if (gg < G) {
+      const float* qr = row + (h * G + gg) * 64;
+      const float q0 = qr[lane], q1 = qr[lane + 32];
+      r0 = __fadd_rn(__fmul_rn(q0, cs[lane]), __fmul_rn(-q1, sn[lane]));
+      r1 = __fadd_rn(__fmul_rn(q1, cs[lane + 32]), __fmul_rn(q0, sn[lane + 32]));
+    }
+    // power of two taking max |q| into [2^21, 2^22): 22-bit integer queries
+    const float qs = pow2_scale(warp_max(fmaxf(fabsf(r0), fabsf(r1)))) * 256.0f;
+    q_sm[gg * 64 + lane] = rintf(r0 * qs);
+    q_sm[gg * 64 + lane + 32] = rintf(r1 * qs);
+    if (lane == 0) q_scale[gg] = qs;
+  }
+  __syncthreads();
 
   // ---- Q digit fragments. k-step ks (32 of the 64 head dims) of thread q4:
   // k 4 q4 + {0..3} <-> dims 16 q4 + 8 ks + {0..3}, k 16 + 4 q4 + {0..3} <->
