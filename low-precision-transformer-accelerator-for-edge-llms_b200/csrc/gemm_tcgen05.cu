@@ -22,8 +22,9 @@
 // kernel is instantiated per tile width, epilogue and split count, so the
 // epilogue is straight-line code. With k_splits > 1 the CTAs of one tile
 // (a cluster of 1 x 1 x k_splits) each reduce a K range; the INT32 partials
-// are exchanged with bulk async copies between the CTAs' shared memories
-// and summed locally (integer addition: exact, order-free), each CTA running
+// are exchanged with bulk async copies between the CTAs' shared memories as
+// soon as each CTA's MMAs are done (no cluster-wide barrier) and summed
+// locally (integer addition: exact, order-free), each CTA running
 // the epilogue for 128 / k_splits of the tile's channels.
 //
 // No TMA multicast is used anywhere. Every mbarrier wait is bounded (about a
@@ -50,6 +51,12 @@ constexpr int kTcThreads = 128;
 constexpr int kTileN = 128;      // weight rows per CTA (MMA M)
 constexpr int kTileK = 128;      // bytes of K per stage (one 128-byte swizzle row)
 constexpr int kABytes = kTileN * kTileK;
+// Split-K receive area of one CTA, outside the operand ring: KS slices of
+// 128 / KS accumulator rows, each row BN + 4 int32 (the padding keeps 16-byte
+// accesses to consecutive rows bank-conflict free).
+__host__ __device__ constexpr uint32_t tc_recv_bytes(int bn, int ks) {
+  return ks > 1 ? static_cast<uint32_t>(kTileN * (bn + 4) * 4) : 0u;
+}
 
 // Bounded wait on the GEMM's error word.
 TL_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned code) {
@@ -173,7 +180,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   constexpr int kTmemCols = BN < 32 ? 32 : BN;
   constexpr bool kFloatEpi = EPI != EPI_I32 && EPI != EPI_REQ;
   const int stages = a.stages;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * kStage);
+  int* recv_area = reinterpret_cast<int*>(smem + stages * kStage);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * kStage + tc_recv_bytes(BN, KS));
   uint64_t* empty = full + stages;
   uint64_t* done = empty + stages;
   uint64_t* recv_bar = done + 1;  // split-K: peers' partial slices have landed
@@ -210,6 +218,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // split-K: this CTA's receive barrier is initialised; peers wait for this
+  // arrive before their first copy into this CTA
+  if constexpr (KS > 1) cluster_arrive_relaxed();
 
   bool ok = true;
   if (warp == 0 && lane == 0) {
@@ -337,18 +348,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else {
     // Split-K across the CTAs of one cluster (cluster dims 1 x 1 x KS): each
     // CTA parks its INT32 partial tile [128 n][BN m] (row stride BN + 4 ints)
-    // in its own shared memory (the operand ring is idle now). After one
-    // cluster barrier, CTA `rank` owns rows [rank*R, (rank+1)*R): every CTA
-    // pushes the rows each peer owns into that peer's receive area with bulk
-    // async copies (shared::cta -> shared::cluster), whose completion lands
-    // on the receiver's mbarrier; each CTA then sums its rows over the KS
-    // slices from its own shared memory and runs the epilogue for them.
-    // Integer addition: exact and order-free.
+    // in its own operand ring (idle once its MMAs are done). CTA `rank` owns
+    // rows [rank*R, (rank+1)*R): right away, with no cluster-wide barrier,
+    // every CTA pushes the rows each peer owns into that peer's receive area
+    // (separate from the peer's ring, so the peer may still be computing)
+    // with bulk async copies (shared::cta -> shared::cluster), whose
+    // completion lands on the receiver's mbarrier; each CTA then sums its
+    // rows over the KS slices from its own shared memory and runs the
+    // epilogue for them. Integer addition: exact and order-free.
     using SL = SplitSlice<BN, KS, EPI>;
     constexpr int PS = BN + 4;
     constexpr uint32_t kSliceBytes = SL::R * PS * 4;
     int* part = reinterpret_cast<int*>(smem);
-    int* recv = part + kTileN * PS;  // [KS][R][PS], slot p from CTA p
+    static_assert(2 * kStage >= kTileN * PS * 4, "two ring stages must hold the parked partial tile");
+    int* recv = recv_area;  // [KS][R][PS], slot p from CTA p
     const int nl = warp * 32 + lane;
     const int rank = static_cast<int>(cluster_rank());
     // this thread's slice and the residuals / constants it needs (issued now,
@@ -385,7 +398,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     // the bulk copies read `part` through the async proxy
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    cluster_sync();  // every partial is parked; every receive barrier is armed
+    __syncthreads();  // this CTA's partial is parked
+    cluster_wait();   // every peer has started (pairs with the arrive above)
     if (threadIdx.x == 0) {
       mbar_arrive_expect_tx(recv_bar, (KS - 1) * kSliceBytes);
       const uint32_t bar_local = smem_u32(recv_bar);
@@ -834,13 +848,14 @@ cudaError_t get_encode() {
 }
 
 template <int BN>
-size_t tc_smem(int stages) {
-  return static_cast<size_t>(stages) * (kABytes + BN * kTileK) + 1024 + 16 * (2 * stages + 3);
+size_t tc_smem(int stages, int ks) {
+  return static_cast<size_t>(stages) * (kABytes + BN * kTileK) + tc_recv_bytes(BN, ks) + 1024 +
+         16 * (2 * stages + 3);
 }
 
 template <int BN, int EPI, int KS>
 cudaError_t launch_tc_k(const TcPlan& p, const TcArgs& a, cudaStream_t s, bool pdl) {
-  const size_t smem = tc_smem<BN>(a.stages);
+  const size_t smem = tc_smem<BN>(a.stages, KS);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((a.N + kTileN - 1) / kTileN, (a.M + BN - 1) / BN, KS);
   cfg.blockDim = dim3(kTcThreads);
@@ -899,7 +914,7 @@ cudaError_t prepare_tc_k() {
     return cudaSuccess;
   } else {
     return cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(tc_smem<BN>(tc_max_stages(BN))));
+                                static_cast<int>(tc_smem<BN>(tc_max_stages(BN, KS), KS)));
   }
 }
 
@@ -928,9 +943,12 @@ cudaError_t prepare_tc_t() {
 // fit on an SM and the next kernel's CTAs can start under programmatic
 // dependent launch. Wide prefill tiles keep the ring at <= 100 KB as well:
 // with two CTAs per SM one CTA's epilogue runs under the other's main loop.
-int tc_max_stages(int bn) {
+// Split-K CTAs also hold the receive area: ring + area stay <= 108 KB, still
+// two CTAs per SM.
+int tc_max_stages(int bn, int ks) {
   const int stage = kABytes + bn * kTileK;
-  return std::max(2, std::min(4, (100 * 1024) / stage));
+  const int budget = ks > 1 ? 108 * 1024 - static_cast<int>(tc_recv_bytes(bn, ks)) : 100 * 1024;
+  return std::max(2, std::min(4, budget / stage));
 }
 
 int tc_pick_bn(int M) {
@@ -969,12 +987,8 @@ cudaError_t tc_make_plan(TcPlan* p, const int8_t* w_nk, int N, const int8_t* x, 
   while (p->bn <= 64 && ks < 8 && tiles * ks < want && 2 * ks <= nkb && tc_split_ok(p->bn, epi, 2 * ks)) ks *= 2;
   p->k_splits = ks;
   const int per = (nkb + ks - 1) / ks;
-  p->stages = std::max(2, std::min(tc_max_stages(p->bn), per));
-  // the split-K partial tile [128][bn + 4] int32 and the receive area of
-  // the same size are staged in the ring
-  while (ks > 1 && static_cast<size_t>(p->stages) * (kABytes + p->bn * kTileK) <
-                       2 * static_cast<size_t>(kTileN) * (p->bn + 4) * 4)
-    ++p->stages;
+  // (two stages always hold the parked split-K partial tile [128][bn + 4])
+  p->stages = std::max(2, std::min(tc_max_stages(p->bn, ks), per));
   p->M = M;
   p->N = N;
   p->K = K;

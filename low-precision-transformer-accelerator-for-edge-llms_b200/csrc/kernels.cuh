@@ -92,7 +92,7 @@ struct TcPlan {
 cudaError_t tc_make_plan(TcPlan* p, const int8_t* w_nk, int N, const int8_t* x, int M, int K, int num_sms, int epi);
 cudaError_t launch_gemm_tc(const TcPlan& p, const TcArgs& a, cudaStream_t s, bool pdl);
 cudaError_t prepare_tc();
-int tc_max_stages(int bn);
+int tc_max_stages(int bn, int ks = 1);
 int tc_pick_bn(int M);
 // Reads (and clears) the device error word of the tensor-core kernels: 0 ok,
 // else the code of the bounded wait that expired.

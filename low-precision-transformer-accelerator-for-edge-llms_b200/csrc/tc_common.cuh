@@ -149,6 +149,11 @@ TL_DEV void tmem_free(uint32_t taddr, uint32_t cols) {
 TL_DEV void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// Split cluster barrier: an arrive that orders nothing and a plain wait,
+// for "every CTA of the cluster has started (its shared memory and
+// mbarriers exist)" before the first access from another CTA.
+TL_DEV void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
+TL_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 TL_DEV uint32_t cluster_rank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
