@@ -66,6 +66,9 @@ constexpr int kD1Rec = 68;
 constexpr int kD1RecO = 4;
 constexpr int kD1XOwn = 64;  // residual rows owned per CTA (D <= 64 * CTAs)
 constexpr long long kD1Wait = 4000000000ll;      // ~2 s at 1.9 GHz
+// a.sync layout: word 0 the grid-barrier counter; from kD1Tickets one
+// attention ticket per (layer, kv head). All zero at launch.
+constexpr int kD1Tickets = 256;
 
 TL_DEV uint32_t d1_smem(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 TL_DEV bool d1_failed() { return *reinterpret_cast<volatile unsigned int*>(&g_d1_error) != 0u; }
@@ -460,6 +463,7 @@ TL_DEV void d1_rows(const D1Args& a, int mat, const int8_t* w, int r, int nr, do
 struct D1KvPiece {
   int4 k, v;
 };
+TL_DEV float4 d1_merge_qd(const D1Args& a, int layer, int qd, int nch);
 TL_DEV D1KvPiece d1_load_kv_piece(const D1Args& a, int layer, int h, int c) {
   D1KvPiece r{make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0)};
   const int tid = threadIdx.x;
@@ -477,7 +481,8 @@ TL_DEV D1KvPiece d1_load_kv_piece(const D1Args& a, int layer, int h, int c) {
   return r;
 }
 
-TL_DEV void d1_attention_item(const D1Args& a, int layer, int h, int c, const D1Smem& sm, const D1KvPiece& pre) {
+TL_DEV void d1_attention_item(const D1Args& a, int layer, int h, int c, int nch, const D1Smem& sm,
+                              const D1KvPiece& pre) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = a.H / a.Hkv;
   const int p = a.pos[0];
@@ -580,65 +585,72 @@ TL_DEV void d1_attention_item(const D1Args& a, int layer, int h, int c, const D1
     }
   }
   bar_cons();  // the scratch in xf is reused by the next item
+  // The item that finishes kv head h last merges the head's chunks into
+  // a.att once (instead of every CTA merging every head after the barrier).
+  // Ticket: the CTA barrier orders this CTA's partial stores before thread
+  // 0's fence and atomic; the winner fences again before reading the others'.
+  if (tid == 0) {
+    __threadfence();
+    const unsigned int t = atomicAdd(a.sync + kD1Tickets + layer * a.Hkv + h, 1u);
+    *sm.flag = t == static_cast<unsigned int>(nch - 1);
+    if (*sm.flag) __threadfence();
+  }
+  bar_cons();
+  if (*sm.flag) {
+    const int qd0 = h * G * 16;  // 16 four-dim groups per query head
+    for (int i = tid; i < G * 16; i += kD1ConsThreads)
+      reinterpret_cast<float4*>(a.att)[qd0 + i] = d1_merge_qd(a, layer, qd0 + i, nch);
+  }
+  bar_cons();  // sm.flag is reused by the next item
 }
 
-// The O projection's input, merged from the attention partials by every CTA
-// (identical arithmetic everywhere): for each query head and dimension the
-// chunks' (max, sum, P.V) are combined in chunk order, eight chunks per load
-// round, as att = (sum_c o_c e_c) / (sum_c l_c e_c) * sV with
-// e_c = exp(m_c - running max); then quantized into xq.
-TL_DEV void cons_merge_attn_quant(const D1Args& a, int layer, int nch, const D1Smem& sm) {
-  const int tid = threadIdx.x;
+// Attention output dims 4 qd .. 4 qd + 3 merged from the chunk partials of
+// their query head: the chunks' (max, sum, P.V) are combined in chunk order,
+// eight chunks per load round, as att = (sum_c o_c e_c) / (sum_c l_c e_c) *
+// sV with e_c = exp(m_c - running max). Partials written by other CTAs are
+// read from L2.
+TL_DEV float4 d1_merge_qd(const D1Args& a, int layer, int qd, int nch) {
   const int G = a.H / a.Hkv;
   const int maxch = (a.P + kD1AttnChunk - 1) / kD1AttnChunk;
-  float4 v[kD1RowVec];
-  const int n4 = a.Dq >> 2;
+  const int gq = (qd * 4) >> 6, d = (qd * 4) & 63;
+  const int h = gq / G, g = gq % G;
+  const float* rec = a.part + (static_cast<size_t>(h) * 8 + g) * maxch * kD1Rec;
+  float M = -INFINITY, L = 0.0f;
+  float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (int c0 = 0; c0 < nch; c0 += 8) {
+    float mv[8], lv[8];
+    float4 ov[8];
 #pragma unroll
-  for (int u = 0; u < kD1RowVec; ++u) {
-    const int qd = tid + u * kD1ConsThreads;
-    v[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    if (qd >= n4) continue;
-    const int gq = (qd * 4) >> 6, d = (qd * 4) & 63;
-    const int h = gq / G, g = gq % G;
-    const float* rec = a.part + (static_cast<size_t>(h) * 8 + g) * maxch * kD1Rec;
-    float M = -INFINITY, L = 0.0f;
-    float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    for (int c0 = 0; c0 < nch; c0 += 8) {
-      float mv[8], lv[8];
-      float4 ov[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float* r = rec + static_cast<size_t>(c0 + j) * kD1Rec;
-        const bool ok = c0 + j < nch;
-        mv[j] = ok ? __ldcg(r) : -INFINITY;
-        lv[j] = ok ? __ldcg(r + 1) : 0.0f;
-        ov[j] = ok ? __ldcg(reinterpret_cast<const float4*>(r + kD1RecO + d)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      }
-      float bm = M;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) bm = fmaxf(bm, mv[j]);
-      const float keep = expf(M - bm);  // 0 on the first batch (M = -inf)
-      L *= keep;
-      o.x *= keep;
-      o.y *= keep;
-      o.z *= keep;
-      o.w *= keep;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (c0 + j >= nch) continue;
-        const float f = expf(mv[j] - bm);
-        L += lv[j] * f;
-        o.x += ov[j].x * f;
-        o.y += ov[j].y * f;
-        o.z += ov[j].z * f;
-        o.w += ov[j].w * f;
-      }
-      M = bm;
+    for (int j = 0; j < 8; ++j) {
+      const float* r = rec + static_cast<size_t>(c0 + j) * kD1Rec;
+      const bool ok = c0 + j < nch;
+      mv[j] = ok ? __ldcg(r) : -INFINITY;
+      lv[j] = ok ? __ldcg(r + 1) : 0.0f;
+      ov[j] = ok ? __ldcg(reinterpret_cast<const float4*>(r + kD1RecO + d)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
-    const float sV = a.vs[(static_cast<size_t>(a.slot[0]) * a.L + layer) * a.Hkv + h];
-    v[u] = make_float4(o.x / L * sV, o.y / L * sV, o.z / L * sV, o.w / L * sV);
+    float bm = M;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) bm = fmaxf(bm, mv[j]);
+    const float keep = expf(M - bm);  // 0 on the first batch (M = -inf)
+    L *= keep;
+    o.x *= keep;
+    o.y *= keep;
+    o.z *= keep;
+    o.w *= keep;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (c0 + j >= nch) continue;
+      const float f = expf(mv[j] - bm);
+      L += lv[j] * f;
+      o.x += ov[j].x * f;
+      o.y += ov[j].y * f;
+      o.z += ov[j].z * f;
+      o.w += ov[j].w * f;
+    }
+    M = bm;
   }
-  cons_quant_regs(sm, v, a.Dq);
+  const float sV = a.vs[(static_cast<size_t>(a.slot[0]) * a.L + layer) * a.Hkv + h];
+  return make_float4(o.x / L * sV, o.y / L * sV, o.z / L * sV, o.w / L * sV);
 }
 
 __global__ void __launch_bounds__(kD1Threads, 1) decode1_kernel(D1Args a) {
@@ -750,10 +762,10 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode1_kernel(D1Args a) {
     d1_grid_wait(a.sync, target);
     for (int w = blockIdx.x; w < items; w += gridDim.x) {
       if (w != static_cast<int>(blockIdx.x)) pre = d1_load_kv_piece(a, l, w / nch, w % nch);
-      d1_attention_item(a, l, w / nch, w % nch, sm, pre);
+      d1_attention_item(a, l, w / nch, w % nch, nch, sm, pre);
     }
     d1_grid_sync(a.sync, target);
-    cons_merge_attn_quant(a, l, nch, sm);
+    cons_load_quant(sm, a.att, a.Dq, nullptr, a.eps, a.plan);  // merged by the heads' last items
     consume_matrix(ly.so, D1_O, a.D, a.Dq, false);
     d1_grid_sync(a.sync, target);
     if (fast_norm) cons_norm_quant_d2048(sm, a.x, ly.g2, a.eps);
@@ -793,6 +805,8 @@ bool decode1_supported(int D, int F, int Dq, int H, int Hkv, int P) {
          F % 16 == 0 && (D + device_sm_count() - 1) / device_sm_count() <= kD1XOwn && Dq % 16 == 0 &&
          decode1_smem(D, F, Dq) <= 227 * 1024;
 }
+
+size_t decode1_sync_words(int L, int Hkv) { return static_cast<size_t>(kD1Tickets) + static_cast<size_t>(L) * Hkv; }
 
 size_t decode1_part_floats(int Hkv, int P) {
   return static_cast<size_t>(Hkv) * 8 * ((P + kD1AttnChunk - 1) / kD1AttnChunk) * kD1Rec;

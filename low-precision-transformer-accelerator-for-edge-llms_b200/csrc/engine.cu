@@ -267,7 +267,7 @@ tl_status alloc_decode(tl_engine* e) {
   if (e->use_decode1) {
     TL_TRY(dmalloc(&d.d1_layers, e->L));
     TL_TRY(dmalloc(&d.d1_part, decode1_part_floats(e->Hkv, e->P)));
-    TL_TRY(dmalloc(&d.d1_sync, 256));  // grid barrier: one generation flag per CTA
+    TL_TRY(dmalloc(&d.d1_sync, decode1_sync_words(e->L, e->Hkv)));  // barrier counter + attention tickets
     std::vector<D1Layer> h(e->L);
     for (int l = 0; l < e->L; ++l) {
       const Layer& ly = e->layers[l];
@@ -401,7 +401,7 @@ tl_status enqueue_decode_step_d1(tl_engine* e, bool finalize) {
   a.x = d.x; a.qkv = d.qkv; a.att = d.att; a.hid = d.hid;
   a.token = d.tokens; a.pos = d.pos; a.slot = d.slots; a.active = d.active;
   a.part = d.d1_part; a.sync = d.d1_sync; a.am_key = d.am_key;
-  TL_CU(cudaMemsetAsync(d.d1_sync, 0, 256 * sizeof(unsigned int), s));
+  TL_CU(cudaMemsetAsync(d.d1_sync, 0, decode1_sync_words(e->L, e->Hkv) * sizeof(unsigned int), s));
   TL_CU(launch_decode1(a, device_sm_count(), s));
   if (finalize) {
     StepArgs st;

@@ -136,12 +136,14 @@ struct D1Args {
   const int* slot = nullptr;
   const int* active = nullptr;
   float* part = nullptr;               // decode1_part_floats(Hkv, P)
-  unsigned int* sync = nullptr;        // [256] grid barrier flags (one per CTA), zeroed before every launch
+  unsigned int* sync = nullptr;        // decode1_sync_words(L, Hkv): barrier counter + attention tickets, zeroed before every launch
   unsigned long long* am_key = nullptr;  // [1], zero
 };
 bool decode1_supported(int D, int F, int Dq, int H, int Hkv, int P);
 size_t decode1_smem(int D, int F, int Dq);
 size_t decode1_part_floats(int Hkv, int P);
+// words of D1Args::sync (grid-barrier counter + attention tickets), zeroed before every launch
+size_t decode1_sync_words(int L, int Hkv);
 cudaError_t decode1_prepare(int D, int F, int Dq);
 cudaError_t launch_decode1(const D1Args& a, int grid, cudaStream_t s);
 // Reads and clears the persistent step's error word; a nonzero code encodes
