@@ -921,6 +921,7 @@ TL_DEV void rope_pair(float a0, float a1, const float* cs, const float* sn, int 
   r1 = __fadd_rn(__fmul_rn(a1, cs[d + 32]), __fmul_rn(a0, sn[d + 32]));
 }
 constexpr int kKvRowsPerWarp = 8;
+constexpr int kRopeMaxH = 32;  // q heads a warp holds in registers (two per lane pair step)
 __global__ void __launch_bounds__(256) rope_stats_prefill_kernel(float* qkv, int ld, int rows, int seq_len, int H,
                                                                  int Hkv, const float* cos, const float* sin,
                                                                  float* kv_absmax) {
@@ -952,22 +953,49 @@ __global__ void __launch_bounds__(256) rope_stats_prefill_kernel(float* qkv, int
     const float* sn = sin + static_cast<size_t>(t) * 64;
     const float2 c0 = *reinterpret_cast<const float2*>(cs + 2 * j), c1 = *reinterpret_cast<const float2*>(cs + 2 * j + 32);
     const float2 s0 = *reinterpret_cast<const float2*>(sn + 2 * j), s1 = *reinterpret_cast<const float2*>(sn + 2 * j + 32);
-    for (int h = hsub; h < H; h += 2) {
-      float2* a = reinterpret_cast<float2*>(row + h * 64 + 2 * j);
-      float2* b = reinterpret_cast<float2*>(row + h * 64 + 2 * j + 32);
-      const float2 x = *a, y = *b;
-      *a = make_float2(__fadd_rn(__fmul_rn(x.x, c0.x), __fmul_rn(-y.x, s0.x)),
-                       __fadd_rn(__fmul_rn(x.y, c0.y), __fmul_rn(-y.y, s0.y)));
-      *b = make_float2(__fadd_rn(__fmul_rn(y.x, c1.x), __fmul_rn(x.x, s1.x)),
-                       __fadd_rn(__fmul_rn(y.y, c1.y), __fmul_rn(x.y, s1.y)));
+    // every load of the row (its q heads, k and v) is issued before the
+    // first store, so the row costs one memory round trip, not one per head
+    float2 xa[kRopeMaxH / 2], xb[kRopeMaxH / 2];
+#pragma unroll
+    for (int i = 0; i < kRopeMaxH / 2; ++i) {
+      const int h = hsub + 2 * i;
+      if (h < H) {
+        xa[i] = *reinterpret_cast<const float2*>(row + h * 64 + 2 * j);
+        xb[i] = *reinterpret_cast<const float2*>(row + h * 64 + 2 * j + 32);
+      }
     }
     const float* kv = row + H * 64;
-    for (int h = 0; h < Hkv; ++h) {
-      float k0, k1;
-      rope_pair(kv[h * 64 + lane], kv[h * 64 + lane + 32], cs, sn, lane, k0, k1);
-      const float* v = kv + (Hkv + h) * 64;
-      mk[h] = fmaxf(mk[h], fmaxf(fabsf(k0), fabsf(k1)));
-      mv[h] = fmaxf(mv[h], fmaxf(fabsf(v[lane]), fabsf(v[lane + 32])));
+    float ka[8], kb[8], va[8], vb[8];
+#pragma unroll
+    for (int h = 0; h < 8; ++h) {
+      if (h < Hkv) {
+        ka[h] = kv[h * 64 + lane];
+        kb[h] = kv[h * 64 + lane + 32];
+        va[h] = kv[(Hkv + h) * 64 + lane];
+        vb[h] = kv[(Hkv + h) * 64 + lane + 32];
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kRopeMaxH / 2; ++i) {
+      const int h = hsub + 2 * i;
+      if (h < H) {
+        const float2 x = xa[i], y = xb[i];
+        *reinterpret_cast<float2*>(row + h * 64 + 2 * j) =
+            make_float2(__fadd_rn(__fmul_rn(x.x, c0.x), __fmul_rn(-y.x, s0.x)),
+                        __fadd_rn(__fmul_rn(x.y, c0.y), __fmul_rn(-y.y, s0.y)));
+        *reinterpret_cast<float2*>(row + h * 64 + 2 * j + 32) =
+            make_float2(__fadd_rn(__fmul_rn(y.x, c1.x), __fmul_rn(x.x, s1.x)),
+                        __fadd_rn(__fmul_rn(y.y, c1.y), __fmul_rn(x.y, s1.y)));
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < 8; ++h) {
+      if (h < Hkv) {
+        float k0, k1;
+        rope_pair(ka[h], kb[h], cs, sn, lane, k0, k1);
+        mk[h] = fmaxf(mk[h], fmaxf(fabsf(k0), fabsf(k1)));
+        mv[h] = fmaxf(mv[h], fmaxf(fabsf(va[h]), fabsf(vb[h])));
+      }
     }
   }
   flush();
@@ -975,7 +1003,7 @@ __global__ void __launch_bounds__(256) rope_stats_prefill_kernel(float* qkv, int
 
 cudaError_t launch_rope_stats_prefill(float* qkv, int ld, int rows, int seq_len, int H, int Hkv, const float* cos,
                                       const float* sin, float* kv_absmax, cudaStream_t s) {
-  if (Hkv > 8 || (ld & 1)) return cudaErrorInvalidValue;
+  if (Hkv > 8 || H > kRopeMaxH || (ld & 1)) return cudaErrorInvalidValue;
   const int warps = (rows + kKvRowsPerWarp - 1) / kKvRowsPerWarp;
   rope_stats_prefill_kernel<<<(warps + 7) / 8, 256, 0, s>>>(qkv, ld, rows, seq_len, H, Hkv, cos, sin, kv_absmax);
   return cudaGetLastError();
