@@ -1021,15 +1021,29 @@ __global__ void __launch_bounds__(256) kv_write_prefill_kernel(const float* qkv,
   const float* row = qkv + static_cast<size_t>(r) * ld + H * 64;
   const float* cs = cos + static_cast<size_t>(t) * 64;
   const float* sn = sin + static_cast<size_t>(t) * 64;
-  for (int hh = 0; hh < 2 * Hkv; ++hh) {
+  // all of the row's k / v values and scales are loaded before the first
+  // store (the stores could alias them as far as the compiler knows)
+  float a0[16], a1[16], amax[16];
+#pragma unroll
+  for (int hh = 0; hh < 16; ++hh) {
+    if (hh < 2 * Hkv) {
+      const int kind = hh / Hkv, h = hh % Hkv;
+      a0[hh] = row[hh * 64 + lane];
+      a1[hh] = row[hh * 64 + lane + 32];
+      amax[hh] = kv_absmax[(seq * 2 + kind) * Hkv + h];
+    }
+  }
+#pragma unroll
+  for (int hh = 0; hh < 16; ++hh) {
+    if (hh >= 2 * Hkv) break;
     const int kind = hh / Hkv, h = hh % Hkv;  // 0 = K, 1 = V
-    const float sf = static_cast<float>(quant_scale64(kv_absmax[(seq * 2 + kind) * Hkv + h]));
-    float a0 = row[hh * 64 + lane], a1 = row[hh * 64 + lane + 32];
-    if (kind == 0) rope_pair(a0, a1, cs, sn, lane, a0, a1);
+    const float sf = static_cast<float>(quant_scale64(amax[hh]));
+    float b0 = a0[hh], b1 = a1[hh];
+    if (kind == 0) rope_pair(b0, b1, cs, sn, lane, b0, b1);
     const size_t sidx = (static_cast<size_t>(slot_base + seq) * L + layer) * Hkv + h;
     int8_t* dst = (kind == 0 ? kc : vc) + (sidx * P + t) * 64;
-    dst[lane] = static_cast<int8_t>(quantize_one(a0, sf));
-    dst[lane + 32] = static_cast<int8_t>(quantize_one(a1, sf));
+    dst[lane] = static_cast<int8_t>(quantize_one(b0, sf));
+    dst[lane + 32] = static_cast<int8_t>(quantize_one(b1, sf));
     if (t == 0 && lane == 0) (kind == 0 ? ks : vs)[sidx] = sf;
   }
 }
@@ -1037,6 +1051,7 @@ __global__ void __launch_bounds__(256) kv_write_prefill_kernel(const float* qkv,
 cudaError_t launch_kv_write_prefill(const float* qkv, int ld, int rows, int seq_len, int H, int Hkv, const float* cos,
                                     const float* sin, const float* kv_absmax, int8_t* kc, int8_t* vc, float* ks,
                                     float* vs, int slot_base, int layer, int L, int P, cudaStream_t s) {
+  if (Hkv > 8) return cudaErrorInvalidValue;
   kv_write_prefill_kernel<<<(rows + 7) / 8, 256, 0, s>>>(qkv, ld, rows, seq_len, H, Hkv, cos, sin, kv_absmax, kc, vc,
                                                           ks, vs, slot_base, layer, L, P);
   return cudaGetLastError();
