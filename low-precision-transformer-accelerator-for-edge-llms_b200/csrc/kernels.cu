@@ -921,7 +921,7 @@ TL_DEV void rope_pair(float a0, float a1, const float* cs, const float* sn, int 
   r1 = __fadd_rn(__fmul_rn(a1, cs[d + 32]), __fmul_rn(a0, sn[d + 32]));
 }
 constexpr int kKvRowsPerWarp = 8;
-constexpr int kRopeMaxH = 32;  // q heads a warp holds in registers (two per lane pair step)
+constexpr int kRopeMaxH = 32;  // q heads whose loads a warp keeps in flight at once
 __global__ void __launch_bounds__(256) rope_stats_prefill_kernel(float* qkv, int ld, int rows, int seq_len, int H,
                                                                  int Hkv, const float* cos, const float* sin,
                                                                  float* kv_absmax) {
@@ -953,17 +953,9 @@ __global__ void __launch_bounds__(256) rope_stats_prefill_kernel(float* qkv, int
     const float* sn = sin + static_cast<size_t>(t) * 64;
     const float2 c0 = *reinterpret_cast<const float2*>(cs + 2 * j), c1 = *reinterpret_cast<const float2*>(cs + 2 * j + 32);
     const float2 s0 = *reinterpret_cast<const float2*>(sn + 2 * j), s1 = *reinterpret_cast<const float2*>(sn + 2 * j + 32);
-    // every load of the row (its q heads, k and v) is issued before the
-    // first store, so the row costs one memory round trip, not one per head
-    float2 xa[kRopeMaxH / 2], xb[kRopeMaxH / 2];
-#pragma unroll
-    for (int i = 0; i < kRopeMaxH / 2; ++i) {
-      const int h = hsub + 2 * i;
-      if (h < H) {
-        xa[i] = *reinterpret_cast<const float2*>(row + h * 64 + 2 * j);
-        xb[i] = *reinterpret_cast<const float2*>(row + h * 64 + 2 * j + 32);
-      }
-    }
+    // every load of the row (up to kRopeMaxH q heads at a time, k and v) is
+    // issued before the first store, so the row costs one memory round trip,
+    // not one per head pair
     const float* kv = row + H * 64;
     float ka[8], kb[8], va[8], vb[8];
 #pragma unroll
@@ -975,10 +967,20 @@ __global__ void __launch_bounds__(256) rope_stats_prefill_kernel(float* qkv, int
         vb[h] = kv[(Hkv + h) * 64 + lane + 32];
       }
     }
+    for (int hb = 0; hb < H; hb += kRopeMaxH) {
+      float2 xa[kRopeMaxH / 2], xb[kRopeMaxH / 2];
 #pragma unroll
-    for (int i = 0; i < kRopeMaxH / 2; ++i) {
-      const int h = hsub + 2 * i;
-      if (h < H) {
+      for (int i = 0; i < kRopeMaxH / 2; ++i) {
+        const int h = hb + hsub + 2 * i;
+        if (h < H) {
+          xa[i] = *reinterpret_cast<const float2*>(row + h * 64 + 2 * j);
+          xb[i] = *reinterpret_cast<const float2*>(row + h * 64 + 2 * j + 32);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kRopeMaxH / 2; ++i) {
+        const int h = hb + hsub + 2 * i;
+        if (h >= H) continue;
         const float2 x = xa[i], y = xb[i];
         *reinterpret_cast<float2*>(row + h * 64 + 2 * j) =
             make_float2(__fadd_rn(__fmul_rn(x.x, c0.x), __fmul_rn(-y.x, s0.x)),
@@ -1003,7 +1005,7 @@ __global__ void __launch_bounds__(256) rope_stats_prefill_kernel(float* qkv, int
 
 cudaError_t launch_rope_stats_prefill(float* qkv, int ld, int rows, int seq_len, int H, int Hkv, const float* cos,
                                       const float* sin, float* kv_absmax, cudaStream_t s) {
-  if (Hkv > 8 || H > kRopeMaxH || (ld & 1)) return cudaErrorInvalidValue;
+  if (Hkv > 8 || (ld & 1)) return cudaErrorInvalidValue;
   const int warps = (rows + kKvRowsPerWarp - 1) / kKvRowsPerWarp;
   rope_stats_prefill_kernel<<<(warps + 7) / 8, 256, 0, s>>>(qkv, ld, rows, seq_len, H, Hkv, cos, sin, kv_absmax);
   return cudaGetLastError();
