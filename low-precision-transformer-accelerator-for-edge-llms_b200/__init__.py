@@ -11,6 +11,7 @@ ctypes binding and mirrors the reference's Python operator API.
 
 from . import replicas, shim  # noqa: F401
 from .shim import (  # noqa: F401
-    Engine, Linear, Layer, Model, TLError, forward_mixed, from_tinyllama_weights, load_library,
-    quantize_int8, quantize_weight, quantized_linear, rms_norm, rope_tables, tp_unique_id,
+    Engine, Linear, Layer, Model, TLError, checkpoint_config, forward_mixed, from_tinyllama_weights,
+    load_checkpoint_npz, load_library, quantize_int8, quantize_weight, quantized_linear, rms_norm, rope_tables,
+    tp_unique_id,
 )

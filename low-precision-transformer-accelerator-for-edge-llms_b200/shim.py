@@ -232,6 +232,56 @@ def from_tinyllama_weights(weights, layer_count: int | None = None, granularity:
                  quantize_weight(weights.lm_head_w(), granularity), layers)
 
 
+# meta_* keys of the reference's weight archive and the engine config keys
+# they fill (model/tinyllama.py:322-335 writes them, :205-217 reads them)
+_NPZ_META = (("hidden_size", int), ("intermediate_size", int), ("num_hidden_layers", int),
+             ("num_attention_heads", int), ("num_key_value_heads", int), ("head_dim", int),
+             ("vocab_size", int), ("max_position_embeddings", int), ("rms_norm_eps", float),
+             ("rope_theta", float))
+_NPZ_PROJ = ("q", "k", "v", "o", "gate", "up", "down")
+
+
+def checkpoint_config(arrays) -> dict:
+    """Engine config from the ``meta_*`` entries of a weight archive in the
+    reference's npz schema (``save_weights_from_hf``, model/tinyllama.py:292-382).
+    ``arrays`` is the opened archive (or any mapping of the same keys)."""
+    missing = [k for k, _ in _NPZ_META if f"meta_{k}" not in arrays]
+    if missing:
+        raise ValueError(f"not a TinyLlama weight archive: missing meta_{missing[0]}")
+    cfg = {k: conv(np.asarray(arrays[f"meta_{k}"]).item()) for k, conv in _NPZ_META}
+    if "meta_model_id" in arrays:
+        cfg["model_id"] = str(np.asarray(arrays["meta_model_id"]).item())
+    return cfg
+
+
+def load_checkpoint_npz(path, layer_count: int | None = None, granularity: str = "channel") -> Model:
+    """Read a weight archive written by the reference's ``save_weights_from_hf``
+    (model/tinyllama.py:292-382: float16 or float32 arrays, projections stored
+    ``[in, out]``, ``lm_head_w`` transposed to ``[hidden, vocab]``) and quantize
+    it for :meth:`Engine.load`: every projection and the LM head to INT8 with a
+    float64 scale per output channel (``granularity="channel"``, the hardware's
+    static scheme) or per tensor (``"tensor"``, the reference bridge's per-call
+    rule), norms and the embedding table as float32. The engine has no bias
+    path (TinyLlama has none): an archive with ``layer*_b`` arrays is refused.
+    ``layer_count`` keeps only the first layers."""
+    with np.load(path, allow_pickle=False) as arrays:
+        cfg = checkpoint_config(arrays)
+        biases = sorted(k for k in arrays.files if k.startswith("layer") and k.endswith("_b"))
+        if biases:
+            raise ValueError(f"projection biases are not supported by the engine ({biases[0]})")
+        n = cfg["num_hidden_layers"] if layer_count is None else int(layer_count)
+        if not 0 < n <= cfg["num_hidden_layers"]:
+            raise ValueError(f"layer_count {n} outside 1..{cfg['num_hidden_layers']}")
+        layers = []
+        for i in range(n):
+            projs = [quantize_weight(arrays[f"layer{i}_{p}_w"], granularity) for p in _NPZ_PROJ]
+            layers.append(Layer(*projs, input_norm=np.asarray(arrays[f"layer{i}_input_norm_w"], np.float32),
+                                post_norm=np.asarray(arrays[f"layer{i}_post_norm_w"], np.float32)))
+        cfg["num_hidden_layers"] = n
+        return Model(cfg, np.asarray(arrays["embed_w"], np.float32), np.asarray(arrays["final_norm_w"], np.float32),
+                     quantize_weight(arrays["lm_head_w"], granularity), layers)
+
+
 def rope_tables(n_pos: int, head_dim: int, theta: float) -> tuple[np.ndarray, np.ndarray]:
     """float32 RoPE tables with the reference's NumPy arithmetic
     (model/tinyllama.py:59-66), so the device sees identical cos/sin."""

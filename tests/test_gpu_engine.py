@@ -345,3 +345,27 @@ def test_reference_golden_first_token(pkg, gpu, golden):
     if top2[1] - top2[0] > FP_RTOL * abs(top2[1]):
         assert int(np.argmax(lg)) == int(d["recompute_tokens"][0])
     eng.close()
+
+
+def test_checkpoint_npz_generation(pkg, gpu, tmp_path):
+    """A float16 weight archive in the reference's npz schema
+    (model/tinyllama.py:292-382), read and quantized per output channel by
+    load_checkpoint_npz, drives the engine: each sequence's greedy ids follow
+    the oracle run on the oracle's quantization of the same arrays."""
+    arc = W.random_archive(41, 2, W.small_dims(), gamma_one=False)
+    arc = {k: (v.astype(np.float16) if k.startswith(("layer", "embed", "final", "lm_head")) else v)
+           for k, v in arc.items()}
+    path = tmp_path / "weights.npz"
+    np.savez(path, **arc)
+    model = pkg.load_checkpoint_npz(path)
+    qm = W.quantize_archive(arc, "channel")
+    eng = pkg.Engine(model.cfg, max_batch=4, max_prefill_tokens=4 * 8)
+    eng.load(model)
+    prompts = np.random.default_rng(42).integers(0, model.cfg["vocab_size"], (4, 8)).astype(np.uint32)
+    outs, sts = eng.generate_batch(prompts, 5)
+    assert pkg.shim.load_library().tl_device_error() == 0
+    for i in range(4):
+        ref, ref_logits, _ = oracle_generate(qm, list(prompts[i]), 5)
+        assert sts[i]["generated_count"] == 5
+        assert tokens_match_modulo_ties(outs[i], ref, ref_logits), (i, outs[i], ref)
+    eng.close()
