@@ -174,6 +174,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __shared__ double sw_sm[kTileN];
   __shared__ unsigned int amax_sm[BN];
   __shared__ unsigned long long key_sm[EPI == EPI_F32 ? BN : 1];
+  __shared__ int issued_sm;  // k-blocks whose TMA loads this CTA issued
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int kBBytes = BN * kTileK;
   constexpr int kStage = kABytes + kBBytes;
@@ -235,6 +236,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     pdl_wait();
     for (int i = 0; i < pre; ++i)
       tma_load_2d(smem + i * kStage + kABytes, &tm_x, (kb0 + i) * kTileK, m0, full + i);
+    int issued = pre;
     for (int kb = kb0 + pre, i = pre; kb < kb1 && ok; ++kb, ++i) {
       const int s = i % stages, round = i / stages;
       ok = mbar_wait(empty + s, (round - 1) & 1, 1u);
@@ -242,7 +244,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_arrive_expect_tx(full + s, kStage);
       tma_load_2d(smem + s * kStage, &tm_w, kb * kTileK, n0, full + s);
       tma_load_2d(smem + s * kStage + kABytes, &tm_x, kb * kTileK, m0, full + s);
+      issued = i + 1;
     }
+    issued_sm = issued;
   } else if (warp == 1 && lane == 0) {
     pdl_wait();
     constexpr uint32_t idesc = idesc_i8(kTileN, BN);
@@ -417,7 +421,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       asm volatile("cp.async.bulk.commit_group;" ::: "memory");
     }
-    const bool got = mbar_wait(recv_bar, 0, 4u);
+    bool got = mbar_wait(recv_bar, 0, 4u);
+    // a timed-out receive (error already recorded): give late pushes from
+    // peers one more bounded wait to land before this CTA moves on to exit
+    if (!got && threadIdx.x == 0) mbar_wait(recv_bar, 0, 4u);
     if (ready && got) {
 #pragma unroll
       for (int q = 0; q < SL::kQuads; ++q) {
@@ -466,6 +473,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     // this CTA's outgoing copies must have read `part` before it exits
     if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+  }
+  // After a failed wait anywhere (the error word is set) this CTA's own TMA
+  // loads may still be in flight into its ring (the producer or the MMA
+  // warp stopped early): wait, bounded, for the last phase issued on every
+  // stage so that no copy lands in shared memory after the CTA has exited.
+  // In a CTA without failure these phases have all completed already.
+  if (threadIdx.x == 0 && *reinterpret_cast<volatile unsigned int*>(&g_tc_error) != 0u) {
+    const int n = issued_sm;
+    for (int i = max(0, n - stages); i < n; ++i) mbar_wait(full + i % stages, (i / stages) & 1, 5u);
   }
   tc_fence_before();
   __syncthreads();

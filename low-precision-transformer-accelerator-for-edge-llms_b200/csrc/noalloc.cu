@@ -24,9 +24,13 @@ using namespace tl;
 namespace {
 
 constexpr int kMaxRows = TL_LMHEAD_NOALLOC_MAX_ROWS;  // rows of one call
-constexpr int kMaxCtas = 1024;                       // bound on the GEMV grid (one CTA per SM)
+constexpr int kMaxCtas = kGemvMaxGrid;               // bound on the GEMV grid (one CTA per SM)
 constexpr int kCandidates = kMaxCtas * kMaxRows;     // per-CTA, per-row argmax keys
 constexpr int kTicketWords = 32;                     // 256 bytes: the kernel's completion ticket
+// One row block (8 rows) means one ticket word; the candidates cover every
+// CTA the GEMV launcher may start for every row of a call.
+static_assert(kMaxRows <= 8, "the argmax kernel keeps one ticket per 8-row block");
+static_assert(kCandidates >= kGemvMaxGrid * kMaxRows, "candidate scratch smaller than the GEMV grid bound");
 
 // [0, kCandidates): packed (logit, token) keys; then the ticket counter.
 static __device__ __align__(256) unsigned long long g_lmhead_scratch[kCandidates + kTicketWords];
@@ -67,6 +71,7 @@ tl_status tl_lmhead_argmax_noalloc(const float* x, const float* gamma, float eps
     return TL_ERR_INVALID_ARGUMENT;
   NormPlan plan;
   if (!norm_plan(hidden, &plan)) return TL_ERR_INVALID_ARGUMENT;
+  if (gemv_argmax_partials(rows, vocab) > static_cast<size_t>(kCandidates)) return TL_ERR_OUT_OF_RANGE;
   if (prepare_kernels(hidden) != cudaSuccess) return TL_ERR_CUDA;
   void* base = nullptr;
   if (scratch_address(&base) != cudaSuccess) return TL_ERR_CUDA;
