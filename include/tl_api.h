@@ -215,6 +215,83 @@ TL_API tl_status tl_read_kv(tl_engine* eng, uint32_t slot, uint32_t layer, uint3
                      int8_t* k_out, int8_t* v_out, float* k_scale_out, float* v_scale_out);
 TL_API tl_status tl_get_position(tl_engine* eng, uint32_t slot, uint32_t* pos);
 
+/* Logits of EVERY prompt row, as forward_mixed returns them
+ * (model/tinyllama_gemm_int8.py:437-467 with quantize_lm_head: final RMSNorm
+ * of all n rows, one per-tensor INT8 scale over those rows, INT8 LM head on
+ * each row). Prefills slot 0 with ids[0..n) like tl_prefill_logits;
+ * logits_out (may be NULL) is host float32 [n][vocab]; hidden_out (may be
+ * NULL) receives the final RMSNorm output [n][hidden], the input of the LM
+ * head (:463). */
+TL_API tl_status tl_forward_logits(tl_engine* eng, const uint32_t* ids, uint32_t n, float* logits_out,
+                                   float* hidden_out);
+
+/* Per-layer capture of tl_decoder_layer: every pointer is an optional HOST
+ * destination (NULL skips it). Names follow the debug dictionaries of
+ * mixed_precision_decoder_layer (model/tinyllama_gemm_int8.py:136-281):
+ * *_input_q / *_acc are the `input_q` / `accum_int32` of each
+ * quantized_linear, *_input_absmax the max |x| whose /127 is `input_scale`.
+ * S = rows of the call, Dq = heads*64, Dkv = kv_heads*64, F = intermediate. */
+typedef struct tl_layer_capture {
+  float* attn_input;          /* [S][hidden]  RMSNorm(x, input_norm)      attn_input_fp */
+  int8_t* qkv_input_q;        /* [S][hidden]  INT8 input of q/k/v_proj */
+  float* qkv_input_absmax;    /* [1] */
+  int32_t* q_acc;             /* [S][Dq] */
+  int32_t* k_acc;             /* [S][Dkv] */
+  int32_t* v_acc;             /* [S][Dkv] */
+  float* q_proj;              /* [S][Dq]  dequantized, before RoPE        q_proj_fp */
+  float* k_proj;              /* [S][Dkv]                                k_proj_fp */
+  float* v_proj;              /* [S][Dkv]                                v_proj_fp */
+  float* scores;              /* [heads][S][S] Q.K^T/8, -1e9 above the diagonal  scores_fp */
+  float* probs;               /* [heads][S][S] softmax(scores)            weights_fp */
+  float* attended;            /* [S][Dq]  attention output                attended_fp */
+  int8_t* o_input_q;          /* [S][Dq] */
+  float* o_input_absmax;      /* [1] */
+  int32_t* o_acc;             /* [S][hidden] */
+  float* o_proj;              /* [S][hidden] dequantized o_proj output     attn out_fp */
+  float* x_after_attn;        /* [S][hidden]                              x_after_attn_fp */
+  float* ffn_input;           /* [S][hidden]  RMSNorm(x_after_attn, post_norm)  ffn_input_fp */
+  int8_t* gate_up_input_q;    /* [S][hidden] */
+  float* gate_up_input_absmax;/* [1] */
+  int32_t* gate_acc;          /* [S][F] */
+  int32_t* up_acc;            /* [S][F] */
+  float* gate_proj;           /* [S][F]                                   gate_proj_fp */
+  float* up_proj;             /* [S][F]                                   up_proj_fp */
+  float* hidden;              /* [S][F]   silu(gate) * up                 hidden_fp */
+  int8_t* down_input_q;       /* [S][F] */
+  float* down_input_absmax;   /* [1] */
+  int32_t* down_acc;          /* [S][hidden] */
+  float* down_proj;           /* [S][hidden] dequantized down_proj output  ffn out_fp */
+} tl_layer_capture;
+
+/* One decoder layer on caller-given activations (teacher forcing):
+ * mixed_precision_decoder_layer (model/tinyllama_gemm_int8.py:256-281) on the
+ * n rows of host float32 x [n][hidden] as one sequence at positions 0..n-1,
+ * run by the engine's prefill kernels for layer `layer`. K/V of those rows
+ * are calibrated and written into KV slot `slot` of that layer (INT8, the
+ * engine's cache). out (host [n][hidden], may be NULL) receives the layer
+ * output; cap (may be NULL) the intermediate tensors. The slot's position
+ * is not changed. TL_ERR_UNIMPLEMENTED on a tensor-parallel engine. */
+TL_API tl_status tl_decoder_layer(tl_engine* eng, uint32_t slot, uint32_t layer, const float* x, uint32_t n,
+                                  float* out, const tl_layer_capture* cap);
+
+/* One decoder layer of a batched DECODE step on caller-given activations
+ * (teacher forcing of the decode path, the KV-cached counterpart of
+ * mixed_precision_decoder_layer, model/tinyllama_gemm_int8.py:256-281): row r
+ * of host float32 x [n][hidden] is the new token at position positions[r] of
+ * the sequence held in KV slot slots[r], whose cache already holds positions
+ * 0..positions[r]-1 of this layer and their scales (a prefill of that slot).
+ * Runs the engine's batched decode kernels for layer `layer` (tcgen05 GEMMs,
+ * decode attention): the row's K/V is quantized with the frozen scales and
+ * appended at positions[r]; attention reads positions 0..positions[r].
+ * Each row is quantized on its own, so the *_input_absmax capture fields
+ * receive n floats; scores/probs must be NULL. n must be in
+ * [16, max_batch] (the tensor-core decode path) and the slots distinct.
+ * The batched decode rows' device state (positions, active flags) is left
+ * undefined: tl_generate_batch / tl_prefill_batch_device set it up again.
+ * TL_ERR_UNIMPLEMENTED on a tensor-parallel engine. */
+TL_API tl_status tl_decode_layer(tl_engine* eng, uint32_t layer, uint32_t n, const uint32_t* slots,
+                                 const uint32_t* positions, const float* x, float* out, const tl_layer_capture* cap);
+
 /* Device-resident decode step for benchmarks: runs `steps` captured decode
  * steps of the first n_seqs slots (greedy feedback on the device) and
  * returns without copying tokens to the host. */

@@ -11,7 +11,7 @@ ctypes binding and mirrors the reference's Python operator API.
 
 from . import replicas, shim  # noqa: F401
 from .shim import (  # noqa: F401
-    Engine, Linear, Layer, Model, TLError, checkpoint_config, forward_mixed, from_tinyllama_weights,
-    load_checkpoint_npz, load_library, quantize_int8, quantize_weight, quantized_linear, rms_norm, rope_tables,
-    tp_unique_id,
+    Engine, Linear, Layer, Model, TLError, check_model, checkpoint_config, forward_mixed, from_tinyllama_weights,
+    layer_debug, load_checkpoint_npz, load_library, mixed_precision_decoder_layer, quantize_int8, quantize_weight,
+    quantized_linear, rms_norm, rope_tables, tp_unique_id,
 )

@@ -204,6 +204,8 @@ struct tl_engine {
   size_t tp_rows = 0, tp_buf_bytes = 0;
   unsigned int tp_epoch = 0;
   bool use_decode1 = false;         // batch-1 steps run as one persistent kernel
+  float* logits_all = nullptr;      // [logits_all_rows][V]: tl_forward_logits
+  size_t logits_all_rows = 0;
 };
 
 namespace {
@@ -323,48 +325,188 @@ tl_status tc_gemm(tl_engine* e, const int8_t* w, int N, const int8_t* x, int M, 
   return TL_OK;
 }
 
-// Batched decode step on the tensor cores (M >= kTcMinRows rows): per row
-// RMSNorm + INT8 quantization kernels feed tcgen05 GEMMs whose epilogues
-// dequantize, add the residual or apply SiLU*up. The attention kernel and
-// the SiLU*up epilogue fold each row's max |output| into d.amax_prod with
-// atomics, so the quantization of their outputs is elementwise over the
-// whole block; each RMSNorm kernel re-arms d.amax_prod (its last reader, the
-// GEMM two kernels back, has completed by then).
+// Optional per-layer capture (tl_decoder_layer, tl_decode_layer): host destinations plus the
+// device scratch the extra INT32 / float projections write into. The capture
+// re-runs a projection with the raw INT32 (or float) epilogue on the same INT8
+// operands; integer MMAs are exact, so these are the accumulators the fused
+// epilogues consumed.
+struct LayerCap {
+  const tl_layer_capture* h = nullptr;
+  int32_t* i32 = nullptr;      // [R][max(Nqkv, 2F, D)]
+  float* f32 = nullptr;        // [R][2F]
+  float* scores = nullptr;     // [H][S][S] (when h->scores or h->probs)
+  float* probs = nullptr;
+  std::vector<int32_t> tmp_i;  // host staging for the interleaved gate/up rows
+  std::vector<float> tmp_f;
+};
+
+tl_status d2h(tl_engine* e, void* dst, const void* src, size_t bytes) {
+  if (!dst || !bytes) return TL_OK;
+  TL_CU(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, e->stream));
+  return TL_OK;
+}
+// columns [c0, c0 + w) of a device matrix [rows][ld] of 4-byte elements
+tl_status d2h_cols(tl_engine* e, void* dst, const void* src, int rows, int ld, int c0, int w) {
+  if (!dst) return TL_OK;
+  TL_CU(cudaMemcpy2DAsync(dst, static_cast<size_t>(w) * 4, static_cast<const char*>(src) + static_cast<size_t>(c0) * 4,
+                          static_cast<size_t>(ld) * 4, static_cast<size_t>(w) * 4, rows, cudaMemcpyDeviceToHost,
+                          e->stream));
+  return TL_OK;
+}
+
+// Raw INT32 (EPI_I32) or dequantized (EPI_F32) product of an INT8 input
+// already in xq, for the capture.
+tl_status capture_gemm(tl_engine* e, const int8_t* xq, const int8_t* w, const double* ws, int N, int K, int R, int S,
+                       const float* in_absmax, int epi, void* out) {
+  if (R >= kTcMinRows) {
+    TcPlan plan;
+    TL_CU(tc_make_plan(&plan, w, N, xq, R, K, device_sm_count(), epi));
+    TcArgs a;
+    a.epi = epi; a.w_scale = ws; a.in_absmax = in_absmax; a.rows_per_group = S;
+    if (epi == EPI_I32) a.out_i32 = static_cast<int32_t*>(out);
+    else a.out_f32 = static_cast<float*>(out);
+    TL_CU(launch_gemm_tc(plan, a, e->stream, false));
+    return TL_OK;
+  }
+  GemvArgs g;
+  g.x_q = xq; g.in_absmax = in_absmax; g.rows_per_group = S;
+  g.w = w; g.w_scale = ws; g.M = R; g.N = N; g.K = K;
+  if (epi == EPI_I32) g.out_i32 = static_cast<int32_t*>(out);
+  else g.out_f32 = static_cast<float*>(out);
+  TL_CU(launch_gemv(PRO_Q8, epi, g, e->stream, false));
+  return TL_OK;
+}
+
+// interleaved rows [R][2F] (column 2j = gate j, 2j+1 = up j) -> two host [R][F]
+template <typename T>
+tl_status split_gate_up(tl_engine* e, const T* dev, int R, int F, std::vector<T>& tmp, T* gate, T* up) {
+  if (!gate && !up) return TL_OK;
+  tmp.resize(static_cast<size_t>(R) * 2 * F);
+  TL_CU(cudaMemcpyAsync(tmp.data(), dev, tmp.size() * sizeof(T), cudaMemcpyDeviceToHost, e->stream));
+  TL_CU(cudaStreamSynchronize(e->stream));
+  for (size_t r = 0; r < static_cast<size_t>(R); ++r)
+    for (size_t j = 0; j < static_cast<size_t>(F); ++j) {
+      if (gate) gate[r * F + j] = tmp[(r * F + j) * 2];
+      if (up) up[r * F + j] = tmp[(r * F + j) * 2 + 1];
+    }
+  return TL_OK;
+}
+
+// Layer l of the batched decode step on the tensor cores (M >= kTcMinRows
+// rows): per row RMSNorm + INT8 quantization kernels feed tcgen05 GEMMs whose
+// epilogues dequantize, add the residual or apply SiLU*up. The attention
+// kernel and the SiLU*up epilogue fold each row's max |output| into
+// d.amax_prod with atomics, so the quantization of their outputs is
+// elementwise over the whole block; each RMSNorm kernel re-arms d.amax_prod
+// (its last reader, the GEMM two kernels back, has completed by then).
+// `cap` (tl_decode_layer) copies the intermediate tensors of the M rows out
+// as they are produced; it is never set inside stream capture.
+tl_status enqueue_decode_layer_tc(tl_engine* e, int l, int M, LayerCap* cap) {
+  DecodeBufs& d = e->dec;
+  cudaStream_t s = e->stream;
+  const bool pdl = e->use_pdl && !cap;
+  const float eps = e->cfg.rms_norm_eps;
+  const tl_layer_capture* hc = cap ? cap->h : nullptr;
+  const size_t rowsD = static_cast<size_t>(M) * e->D * sizeof(float);
+  const Layer& ly = e->layers[l];
+  if (hc && hc->attn_input) {
+    TL_CU(launch_rmsnorm_rows(d.x, ly.g1, eps, cap->f32, nullptr, M, e->D, 1, s));
+    TL_TRY(d2h(e, hc->attn_input, cap->f32, rowsD));
+  }
+  TL_CU(launch_norm_quant_rows(d.x, ly.g1, eps, M, e->D, d.xq, d.amax, s, pdl, d.amax_prod));
+  TcArgs q;
+  q.epi = EPI_F32; q.w_scale = ly.sqkv; q.in_absmax = d.amax; q.rows_per_group = 1; q.out_f32 = d.qkv;
+  TL_TRY(tc_gemm(e, ly.wqkv, e->Nqkv, d.xq, M, e->D, q, pdl));
+  if (hc) {
+    TL_TRY(d2h(e, hc->qkv_input_q, d.xq, static_cast<size_t>(M) * e->D));
+    TL_TRY(d2h(e, hc->qkv_input_absmax, d.amax, M * sizeof(float)));
+    TL_TRY(d2h_cols(e, hc->q_proj, d.qkv, M, e->Nqkv, 0, e->Dq));
+    TL_TRY(d2h_cols(e, hc->k_proj, d.qkv, M, e->Nqkv, e->Dq, e->Dkv));
+    TL_TRY(d2h_cols(e, hc->v_proj, d.qkv, M, e->Nqkv, e->Dq + e->Dkv, e->Dkv));
+    if (hc->q_acc || hc->k_acc || hc->v_acc) {
+      TL_TRY(capture_gemm(e, d.xq, ly.wqkv, ly.sqkv, e->Nqkv, e->D, M, 1, d.amax, EPI_I32, cap->i32));
+      TL_TRY(d2h_cols(e, hc->q_acc, cap->i32, M, e->Nqkv, 0, e->Dq));
+      TL_TRY(d2h_cols(e, hc->k_acc, cap->i32, M, e->Nqkv, e->Dq, e->Dkv));
+      TL_TRY(d2h_cols(e, hc->v_acc, cap->i32, M, e->Nqkv, e->Dq + e->Dkv, e->Dkv));
+    }
+  }
+  AttnDecodeArgs at;
+  at.qkv = d.qkv; at.ld = e->Nqkv; at.pos = d.pos; at.slot = d.slots; at.active = d.active;
+  at.kc = e->kc; at.vc = e->vc; at.ks = e->ks; at.vs = e->vs;
+  at.layer = l; at.L = e->L; at.H = e->H; at.Hkv = e->Hkv; at.P = e->P; at.M = M;
+  at.cos = e->cosT; at.sin = e->sinT; at.out = d.att;
+  at.part = d.attn_part; at.counters = d.attn_cnt; at.out_absmax = d.amax_prod;
+  TL_CU(launch_attn_decode(at, s, pdl));
+  TL_CU(launch_quant_known_rows(d.att, d.amax_prod, M, e->Dq, d.xq, s, pdl));
+  if (hc) {
+    TL_TRY(d2h(e, hc->attended, d.att, static_cast<size_t>(M) * e->Dq * sizeof(float)));
+    TL_TRY(d2h(e, hc->o_input_q, d.xq, static_cast<size_t>(M) * e->Dq));
+    TL_TRY(d2h(e, hc->o_input_absmax, d.amax_prod, M * sizeof(float)));
+    if (hc->o_acc) {
+      TL_TRY(capture_gemm(e, d.xq, ly.wo, ly.so, e->D, e->Dq, M, 1, d.amax_prod, EPI_I32, cap->i32));
+      TL_TRY(d2h(e, hc->o_acc, cap->i32, static_cast<size_t>(M) * e->D * 4));
+    }
+    if (hc->o_proj) {
+      TL_TRY(capture_gemm(e, d.xq, ly.wo, ly.so, e->D, e->Dq, M, 1, d.amax_prod, EPI_F32, cap->i32));
+      TL_TRY(d2h(e, hc->o_proj, cap->i32, static_cast<size_t>(M) * e->D * 4));
+    }
+  }
+  TcArgs o;
+  o.epi = EPI_RESID; o.w_scale = ly.so; o.in_absmax = d.amax_prod; o.rows_per_group = 1; o.out_f32 = d.x;
+  o.resid = d.x;
+  TL_TRY(tc_gemm(e, ly.wo, e->D, d.xq, M, e->Dq, o, pdl));
+  if (hc) TL_TRY(d2h(e, hc->x_after_attn, d.x, rowsD));
+  if (hc && hc->ffn_input) {
+    TL_CU(launch_rmsnorm_rows(d.x, ly.g2, eps, cap->f32, nullptr, M, e->D, 1, s));
+    TL_TRY(d2h(e, hc->ffn_input, cap->f32, rowsD));
+  }
+  TL_CU(launch_norm_quant_rows(d.x, ly.g2, eps, M, e->D, d.xq, d.amax, s, pdl, d.amax_prod));
+  TcArgs gu;
+  gu.epi = EPI_SILU; gu.w_scale = ly.sgu; gu.in_absmax = d.amax; gu.rows_per_group = 1; gu.out_f32 = d.hid;
+  gu.out_absmax = d.amax_prod;
+  TL_TRY(tc_gemm(e, ly.wgu, 2 * e->F, d.xq, M, e->D, gu, pdl));
+  if (hc) {
+    TL_TRY(d2h(e, hc->gate_up_input_q, d.xq, static_cast<size_t>(M) * e->D));
+    TL_TRY(d2h(e, hc->gate_up_input_absmax, d.amax, M * sizeof(float)));
+    if (hc->gate_acc || hc->up_acc) {
+      TL_TRY(capture_gemm(e, d.xq, ly.wgu, ly.sgu, 2 * e->F, e->D, M, 1, d.amax, EPI_I32, cap->i32));
+      TL_TRY(split_gate_up(e, cap->i32, M, e->F, cap->tmp_i, hc->gate_acc, hc->up_acc));
+    }
+    if (hc->gate_proj || hc->up_proj) {
+      TL_TRY(capture_gemm(e, d.xq, ly.wgu, ly.sgu, 2 * e->F, e->D, M, 1, d.amax, EPI_F32, cap->f32));
+      TL_TRY(split_gate_up(e, static_cast<const float*>(cap->f32), M, e->F, cap->tmp_f, hc->gate_proj,
+                           hc->up_proj));
+    }
+  }
+  TL_CU(launch_quant_known_rows(d.hid, d.amax_prod, M, e->F, d.xq, s, pdl));
+  if (hc) {
+    TL_TRY(d2h(e, hc->hidden, d.hid, static_cast<size_t>(M) * e->F * sizeof(float)));
+    TL_TRY(d2h(e, hc->down_input_q, d.xq, static_cast<size_t>(M) * e->F));
+    TL_TRY(d2h(e, hc->down_input_absmax, d.amax_prod, M * sizeof(float)));
+    if (hc->down_acc) {
+      TL_TRY(capture_gemm(e, d.xq, ly.wd, ly.sd, e->D, e->F, M, 1, d.amax_prod, EPI_I32, cap->i32));
+      TL_TRY(d2h(e, hc->down_acc, cap->i32, static_cast<size_t>(M) * e->D * 4));
+    }
+    if (hc->down_proj) {
+      TL_TRY(capture_gemm(e, d.xq, ly.wd, ly.sd, e->D, e->F, M, 1, d.amax_prod, EPI_F32, cap->i32));
+      TL_TRY(d2h(e, hc->down_proj, cap->i32, static_cast<size_t>(M) * e->D * 4));
+    }
+  }
+  TcArgs dn;
+  dn.epi = EPI_RESID; dn.w_scale = ly.sd; dn.in_absmax = d.amax_prod; dn.rows_per_group = 1; dn.out_f32 = d.x;
+  dn.resid = d.x;
+  TL_TRY(tc_gemm(e, ly.wd, e->D, d.xq, M, e->F, dn, pdl));
+  return TL_OK;
+}
+
+// Batched decode step on the tensor cores (M >= kTcMinRows rows).
 tl_status enqueue_decode_step_tc(tl_engine* e, int M, bool finalize) {
   DecodeBufs& d = e->dec;
   cudaStream_t s = e->stream;
   const bool pdl = e->use_pdl;
   const float eps = e->cfg.rms_norm_eps;
   TL_CU(launch_embed(e->embed, d.tokens, d.x, M, e->D, e->V, s, pdl));
-  for (int l = 0; l < e->L; ++l) {
-    const Layer& ly = e->layers[l];
-    TL_CU(launch_norm_quant_rows(d.x, ly.g1, eps, M, e->D, d.xq, d.amax, s, pdl, d.amax_prod));
-    TcArgs q;
-    q.epi = EPI_F32; q.w_scale = ly.sqkv; q.in_absmax = d.amax; q.rows_per_group = 1; q.out_f32 = d.qkv;
-    TL_TRY(tc_gemm(e, ly.wqkv, e->Nqkv, d.xq, M, e->D, q, pdl));
-    AttnDecodeArgs at;
-    at.qkv = d.qkv; at.ld = e->Nqkv; at.pos = d.pos; at.slot = d.slots; at.active = d.active;
-    at.kc = e->kc; at.vc = e->vc; at.ks = e->ks; at.vs = e->vs;
-    at.layer = l; at.L = e->L; at.H = e->H; at.Hkv = e->Hkv; at.P = e->P; at.M = M;
-    at.cos = e->cosT; at.sin = e->sinT; at.out = d.att;
-    at.part = d.attn_part; at.counters = d.attn_cnt; at.out_absmax = d.amax_prod;
-    TL_CU(launch_attn_decode(at, s, pdl));
-    TL_CU(launch_quant_known_rows(d.att, d.amax_prod, M, e->Dq, d.xq, s, pdl));
-    TcArgs o;
-    o.epi = EPI_RESID; o.w_scale = ly.so; o.in_absmax = d.amax_prod; o.rows_per_group = 1; o.out_f32 = d.x;
-    o.resid = d.x;
-    TL_TRY(tc_gemm(e, ly.wo, e->D, d.xq, M, e->Dq, o, pdl));
-    TL_CU(launch_norm_quant_rows(d.x, ly.g2, eps, M, e->D, d.xq, d.amax, s, pdl, d.amax_prod));
-    TcArgs gu;
-    gu.epi = EPI_SILU; gu.w_scale = ly.sgu; gu.in_absmax = d.amax; gu.rows_per_group = 1; gu.out_f32 = d.hid;
-    gu.out_absmax = d.amax_prod;
-    TL_TRY(tc_gemm(e, ly.wgu, 2 * e->F, d.xq, M, e->D, gu, pdl));
-    TL_CU(launch_quant_known_rows(d.hid, d.amax_prod, M, e->F, d.xq, s, pdl));
-    TcArgs dn;
-    dn.epi = EPI_RESID; dn.w_scale = ly.sd; dn.in_absmax = d.amax_prod; dn.rows_per_group = 1; dn.out_f32 = d.x;
-    dn.resid = d.x;
-    TL_TRY(tc_gemm(e, ly.wd, e->D, d.xq, M, e->F, dn, pdl));
-  }
+  for (int l = 0; l < e->L; ++l) TL_TRY(enqueue_decode_layer_tc(e, l, M, nullptr));
   TL_CU(launch_norm_quant_rows(d.x, e->gfinal, eps, M, e->D, d.xq, d.amax, s, pdl));
   // LM head with the greedy argmax fused into the epilogue (packed keys in
   // d.am_key, consumed and re-armed by step_finalize / keys_to_tokens); the
@@ -545,52 +687,131 @@ tl_status tp_exchange(tl_engine* e, const float* x, int Kl, int Kf, int R, int S
   return TL_OK;
 }
 
+// Layer l of a batched prefill: rows of n_seq sequences of S tokens each, in
+// place on pf.x; K/V into slots slot_base..slot_base+n_seq-1. `cap` (one
+// sequence only) copies the intermediate tensors out as they are produced.
+tl_status enqueue_prefill_layer(tl_engine* e, int l, int n_seq, int S, int slot_base, LayerCap* cap) {
+  PrefillBufs& p = e->pf;
+  cudaStream_t s = e->stream;
+  const bool tp = e->tp_world > 1;
+  const int R = n_seq * S;
+  const float eps = e->cfg.rms_norm_eps;
+  const tl_layer_capture* hc = cap ? cap->h : nullptr;
+  const size_t rowsD = static_cast<size_t>(R) * e->D * sizeof(float);
+  const Layer& ly = e->layers[l];
+  float* am = p.amax + static_cast<size_t>(l) * 4 * n_seq;
+  float* kva = p.kvamax + static_cast<size_t>(l) * n_seq * 2 * e->Hkv;
+  // attention block
+  if (hc && hc->attn_input) {
+    TL_CU(launch_rmsnorm_rows(p.x, ly.g1, eps, p.h, nullptr, R, e->D, S, s));
+    TL_TRY(d2h(e, hc->attn_input, p.h, rowsD));
+  }
+  TL_CU(launch_norm_quant_prefill(p.x, ly.g1, eps, R, e->D, S, p.inv, am, p.h, p.xq, s));
+  TL_TRY(prefill_gemm(e, p.xq, ly.wqkv, ly.sqkv, e->Nqkv, e->D, R, S, am, EPI_F32, p.qkv, nullptr, nullptr));
+  if (hc) {
+    TL_TRY(d2h(e, hc->qkv_input_q, p.xq, static_cast<size_t>(R) * e->D));
+    TL_TRY(d2h(e, hc->qkv_input_absmax, am, sizeof(float)));
+    TL_TRY(d2h_cols(e, hc->q_proj, p.qkv, R, e->Nqkv, 0, e->Dq));
+    TL_TRY(d2h_cols(e, hc->k_proj, p.qkv, R, e->Nqkv, e->Dq, e->Dkv));
+    TL_TRY(d2h_cols(e, hc->v_proj, p.qkv, R, e->Nqkv, e->Dq + e->Dkv, e->Dkv));
+    if (hc->q_acc || hc->k_acc || hc->v_acc) {
+      TL_TRY(capture_gemm(e, p.xq, ly.wqkv, ly.sqkv, e->Nqkv, e->D, R, S, am, EPI_I32, cap->i32));
+      TL_TRY(d2h_cols(e, hc->q_acc, cap->i32, R, e->Nqkv, 0, e->Dq));
+      TL_TRY(d2h_cols(e, hc->k_acc, cap->i32, R, e->Nqkv, e->Dq, e->Dkv));
+      TL_TRY(d2h_cols(e, hc->v_acc, cap->i32, R, e->Nqkv, e->Dq + e->Dkv, e->Dkv));
+    }
+  }
+  // RoPE of q in place, RoPE(k) and v maxima per (sequence, kv head), then the INT8 cache
+  TL_CU(launch_rope_stats_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->cosT, e->sinT, kva, s));
+  TL_CU(launch_kv_write_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->cosT, e->sinT, kva, e->kc, e->vc, e->ks,
+                                e->vs, slot_base, l, e->L, e->P, s));
+  if (cap && cap->scores) {
+    TL_CU(launch_attn_scores_debug(p.qkv, e->Nqkv, S, e->H, e->Hkv, e->kc, e->ks, slot_base, l, e->L, e->P,
+                                   cap->scores, cap->probs, s));
+    const size_t sb = static_cast<size_t>(e->H) * S * S * sizeof(float);
+    TL_TRY(d2h(e, hc->scores, cap->scores, sb));
+    TL_TRY(d2h(e, hc->probs, cap->probs, sb));
+  }
+  TL_CU(launch_attn_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->kc, e->vc, e->ks, e->vs, slot_base,
+                            l, e->L, e->P, p.att, am + n_seq, s));
+  const int8_t* xin = p.xq;
+  if (tp) {
+    TL_TRY(tp_allreduce_max(e, am + n_seq, n_seq));
+    TL_TRY(tp_exchange(e, p.att, e->Dq, e->Dq_full, R, S, am + n_seq, &xin));
+  } else {
+    TL_CU(launch_quantize_rows(p.att, am + n_seq, R, e->Dq, S, p.xq, s));
+  }
+  if (hc) {
+    TL_TRY(d2h(e, hc->attended, p.att, static_cast<size_t>(R) * e->Dq * sizeof(float)));
+    TL_TRY(d2h(e, hc->o_input_q, p.xq, static_cast<size_t>(R) * e->Dq));
+    TL_TRY(d2h(e, hc->o_input_absmax, am + n_seq, sizeof(float)));
+    if (hc->o_acc) {
+      TL_TRY(capture_gemm(e, p.xq, ly.wo, ly.so, e->D, e->Dq, R, S, am + n_seq, EPI_I32, cap->i32));
+      TL_TRY(d2h(e, hc->o_acc, cap->i32, static_cast<size_t>(R) * e->D * 4));
+    }
+    if (hc->o_proj) {
+      TL_TRY(capture_gemm(e, p.xq, ly.wo, ly.so, e->D, e->Dq, R, S, am + n_seq, EPI_F32, cap->i32));
+      TL_TRY(d2h(e, hc->o_proj, cap->i32, static_cast<size_t>(R) * e->D * 4));
+    }
+  }
+  TL_TRY(prefill_gemm(e, xin, ly.wo, ly.so, e->D, e->Dq_full, R, S, am + n_seq, EPI_RESID, p.x, p.x, nullptr));
+  if (hc) TL_TRY(d2h(e, hc->x_after_attn, p.x, rowsD));
+  // feed-forward block
+  if (hc && hc->ffn_input) {
+    TL_CU(launch_rmsnorm_rows(p.x, ly.g2, eps, p.h, nullptr, R, e->D, S, s));
+    TL_TRY(d2h(e, hc->ffn_input, p.h, rowsD));
+  }
+  TL_CU(launch_norm_quant_prefill(p.x, ly.g2, eps, R, e->D, S, p.inv, am + 2 * n_seq, p.h, p.xq, s));
+  TL_TRY(prefill_gemm(e, p.xq, ly.wgu, ly.sgu, 2 * e->F, e->D, R, S, am + 2 * n_seq, EPI_SILU, p.hid, nullptr,
+                      am + 3 * n_seq));
+  if (hc) {
+    TL_TRY(d2h(e, hc->gate_up_input_q, p.xq, static_cast<size_t>(R) * e->D));
+    TL_TRY(d2h(e, hc->gate_up_input_absmax, am + 2 * n_seq, sizeof(float)));
+    if (hc->gate_acc || hc->up_acc) {
+      TL_TRY(capture_gemm(e, p.xq, ly.wgu, ly.sgu, 2 * e->F, e->D, R, S, am + 2 * n_seq, EPI_I32, cap->i32));
+      TL_TRY(split_gate_up(e, cap->i32, R, e->F, cap->tmp_i, hc->gate_acc, hc->up_acc));
+    }
+    if (hc->gate_proj || hc->up_proj) {
+      TL_TRY(capture_gemm(e, p.xq, ly.wgu, ly.sgu, 2 * e->F, e->D, R, S, am + 2 * n_seq, EPI_F32, cap->f32));
+      TL_TRY(split_gate_up(e, static_cast<const float*>(cap->f32), R, e->F, cap->tmp_f, hc->gate_proj, hc->up_proj));
+    }
+  }
+  xin = p.xq;
+  if (tp) {
+    TL_TRY(tp_allreduce_max(e, am + 3 * n_seq, n_seq));
+    TL_TRY(tp_exchange(e, p.hid, e->F, e->F_full, R, S, am + 3 * n_seq, &xin));
+  } else {
+    TL_CU(launch_quantize_rows(p.hid, am + 3 * n_seq, R, e->F, S, p.xq, s));
+  }
+  if (hc) {
+    TL_TRY(d2h(e, hc->hidden, p.hid, static_cast<size_t>(R) * e->F * sizeof(float)));
+    TL_TRY(d2h(e, hc->down_input_q, p.xq, static_cast<size_t>(R) * e->F));
+    TL_TRY(d2h(e, hc->down_input_absmax, am + 3 * n_seq, sizeof(float)));
+    if (hc->down_acc) {
+      TL_TRY(capture_gemm(e, p.xq, ly.wd, ly.sd, e->D, e->F, R, S, am + 3 * n_seq, EPI_I32, cap->i32));
+      TL_TRY(d2h(e, hc->down_acc, cap->i32, static_cast<size_t>(R) * e->D * 4));
+    }
+    if (hc->down_proj) {
+      TL_TRY(capture_gemm(e, p.xq, ly.wd, ly.sd, e->D, e->F, R, S, am + 3 * n_seq, EPI_F32, cap->i32));
+      TL_TRY(d2h(e, hc->down_proj, cap->i32, static_cast<size_t>(R) * e->D * 4));
+    }
+  }
+  TL_TRY(prefill_gemm(e, xin, ly.wd, ly.sd, e->D, e->F_full, R, S, am + 3 * n_seq, EPI_RESID, p.x, p.x, nullptr));
+  return TL_OK;
+}
+
 // n_seq sequences of S tokens each, token ids already in pf.ids; slots
 // slot_base..slot_base+n_seq-1. Leaves the first greedy token of each
 // sequence in dec.argmax[0..n_seq) when `head` is set.
 tl_status enqueue_prefill(tl_engine* e, int n_seq, int S, int slot_base, bool head, float* logits) {
   PrefillBufs& p = e->pf;
   cudaStream_t s = e->stream;
-  const bool tp = e->tp_world > 1;
   const int R = n_seq * S;
   const float eps = e->cfg.rms_norm_eps;
   TL_CU(cudaMemsetAsync(p.amax, 0, (static_cast<size_t>(e->L) * 4 * n_seq + n_seq) * sizeof(float), s));
   TL_CU(cudaMemsetAsync(p.kvamax, 0, static_cast<size_t>(e->L) * n_seq * 2 * e->Hkv * sizeof(float), s));
   TL_CU(launch_embed(e->embed, p.ids, p.x, R, e->D, e->V, s, false));
-  for (int l = 0; l < e->L; ++l) {
-    const Layer& ly = e->layers[l];
-    float* am = p.amax + static_cast<size_t>(l) * 4 * n_seq;
-    float* kva = p.kvamax + static_cast<size_t>(l) * n_seq * 2 * e->Hkv;
-    // attention block
-    TL_CU(launch_norm_quant_prefill(p.x, ly.g1, eps, R, e->D, S, p.inv, am, p.h, p.xq, s));
-    TL_TRY(prefill_gemm(e, p.xq, ly.wqkv, ly.sqkv, e->Nqkv, e->D, R, S, am, EPI_F32, p.qkv, nullptr, nullptr));
-    // RoPE of q in place, RoPE(k) and v maxima per (sequence, kv head), then the INT8 cache
-    TL_CU(launch_rope_stats_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->cosT, e->sinT, kva, s));
-    TL_CU(launch_kv_write_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->cosT, e->sinT, kva, e->kc, e->vc, e->ks,
-                                  e->vs, slot_base, l, e->L, e->P, s));
-    TL_CU(launch_attn_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->kc, e->vc, e->ks, e->vs, slot_base,
-                              l, e->L, e->P, p.att, am + n_seq, s));
-    const int8_t* xin = p.xq;
-    if (tp) {
-      TL_TRY(tp_allreduce_max(e, am + n_seq, n_seq));
-      TL_TRY(tp_exchange(e, p.att, e->Dq, e->Dq_full, R, S, am + n_seq, &xin));
-    } else {
-      TL_CU(launch_quantize_rows(p.att, am + n_seq, R, e->Dq, S, p.xq, s));
-    }
-    TL_TRY(prefill_gemm(e, xin, ly.wo, ly.so, e->D, e->Dq_full, R, S, am + n_seq, EPI_RESID, p.x, p.x, nullptr));
-    // feed-forward block
-    TL_CU(launch_norm_quant_prefill(p.x, ly.g2, eps, R, e->D, S, p.inv, am + 2 * n_seq, p.h, p.xq, s));
-    TL_TRY(prefill_gemm(e, p.xq, ly.wgu, ly.sgu, 2 * e->F, e->D, R, S, am + 2 * n_seq, EPI_SILU, p.hid, nullptr,
-                        am + 3 * n_seq));
-    xin = p.xq;
-    if (tp) {
-      TL_TRY(tp_allreduce_max(e, am + 3 * n_seq, n_seq));
-      TL_TRY(tp_exchange(e, p.hid, e->F, e->F_full, R, S, am + 3 * n_seq, &xin));
-    } else {
-      TL_CU(launch_quantize_rows(p.hid, am + 3 * n_seq, R, e->F, S, p.xq, s));
-    }
-    TL_TRY(prefill_gemm(e, xin, ly.wd, ly.sd, e->D, e->F_full, R, S, am + 3 * n_seq, EPI_RESID, p.x, p.x, nullptr));
-  }
+  for (int l = 0; l < e->L; ++l) TL_TRY(enqueue_prefill_layer(e, l, n_seq, S, slot_base, nullptr));
   if (!head) return TL_OK;
   float* amf = p.amax + static_cast<size_t>(e->L) * 4 * n_seq;
   TL_CU(launch_rmsnorm_rows(p.x, e->gfinal, eps, p.h, amf, R, e->D, S, s));
@@ -911,6 +1132,7 @@ tl_status tl_destroy(tl_engine* e) {
   PrefillBufs& p = e->pf;
   cudaFree(p.ids); cudaFree(p.x); cudaFree(p.h); cudaFree(p.qkv); cudaFree(p.att); cudaFree(p.hid);
   cudaFree(p.xq); cudaFree(p.amax); cudaFree(p.kvamax); cudaFree(p.inv);
+  cudaFree(e->logits_all);
   if (e->h_pinned) cudaFreeHost(e->h_pinned);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
@@ -1218,6 +1440,138 @@ tl_status tl_prefill_logits(tl_engine* e, uint32_t slot, const uint32_t* ids, ui
   e->slot_pos[0] = static_cast<int>(n);
   e->slot_pending[0] = -1;
   return TL_OK;
+}
+
+tl_status tl_forward_logits(tl_engine* e, const uint32_t* ids, uint32_t n, float* logits_out, float* hidden_out) {
+  if (!e || !ids) return TL_ERR_INVALID_ARGUMENT;
+  if (!e->loaded) return TL_ERR_NOT_LOADED;
+  if (e->tp_world > 1) return TL_ERR_UNIMPLEMENTED;
+  TL_CU(cudaSetDevice(e->device));
+  TL_TRY(prefill_common(e, 1, ids, n, false, nullptr));
+  if (logits_out && e->logits_all_rows < n) {
+    cudaFree(e->logits_all);
+    e->logits_all = nullptr;
+    e->logits_all_rows = 0;
+    TL_TRY(dmalloc(&e->logits_all, static_cast<size_t>(n) * e->V));
+    e->logits_all_rows = n;
+  }
+  // final RMSNorm of every row, one INT8 scale over all rows (the absmax slot
+  // after the layers' four, zeroed by the prefill), LM head on every row
+  PrefillBufs& p = e->pf;
+  const int R = static_cast<int>(n);
+  float* amf = p.amax + static_cast<size_t>(e->L) * 4;
+  TL_CU(launch_rmsnorm_rows(p.x, e->gfinal, e->cfg.rms_norm_eps, p.h, amf, R, e->D, R, e->stream));
+  if (hidden_out) TL_TRY(d2h(e, hidden_out, p.h, static_cast<size_t>(n) * e->D * sizeof(float)));
+  if (logits_out) {
+    TL_CU(launch_quantize_rows(p.h, amf, R, e->D, R, p.xq, e->stream));
+    TL_TRY(prefill_gemm(e, p.xq, e->wlm, e->slm, e->V, e->D, R, R, amf, EPI_F32, e->logits_all, nullptr, nullptr));
+    TL_CU(cudaMemcpyAsync(logits_out, e->logits_all, static_cast<size_t>(n) * e->V * sizeof(float),
+                          cudaMemcpyDeviceToHost, e->stream));
+  }
+  TL_CU(cudaStreamSynchronize(e->stream));
+  TL_TRY(tl_device_error());
+  e->slot_pos[0] = static_cast<int>(n);
+  e->slot_pending[0] = -1;
+  return TL_OK;
+}
+
+tl_status tl_decoder_layer(tl_engine* e, uint32_t slot, uint32_t layer, const float* x, uint32_t n, float* out,
+                           const tl_layer_capture* cap) {
+  if (!e || !x) return TL_ERR_INVALID_ARGUMENT;
+  if (!e->loaded) return TL_ERR_NOT_LOADED;
+  if (e->tp_world > 1) return TL_ERR_UNIMPLEMENTED;
+  if (n == 0) return TL_ERR_BAD_DESCRIPTOR;
+  if (slot >= static_cast<uint32_t>(e->B) || layer >= static_cast<uint32_t>(e->L) || n > static_cast<uint32_t>(e->P))
+    return TL_ERR_OUT_OF_RANGE;
+  TL_CU(cudaSetDevice(e->device));
+  TL_TRY(ensure_prefill(e, n, 1));
+  PrefillBufs& p = e->pf;
+  const int S = static_cast<int>(n);
+  const size_t rowsD = static_cast<size_t>(n) * e->D * sizeof(float);
+  LayerCap lc;
+  lc.h = cap;
+  auto body = [&]() -> tl_status {
+    if (cap) {
+      const size_t wide = std::max<size_t>(std::max<size_t>(e->Nqkv, 2 * static_cast<size_t>(e->F)), e->D);
+      TL_TRY(dmalloc(&lc.i32, static_cast<size_t>(n) * wide));
+      if (cap->gate_proj || cap->up_proj) TL_TRY(dmalloc(&lc.f32, static_cast<size_t>(n) * 2 * e->F));
+      if (cap->scores || cap->probs) {
+        TL_TRY(dmalloc(&lc.scores, static_cast<size_t>(e->H) * n * n));
+        TL_TRY(dmalloc(&lc.probs, static_cast<size_t>(e->H) * n * n));
+      }
+    }
+    cudaStream_t s = e->stream;
+    float* am = p.amax + static_cast<size_t>(layer) * 4;
+    float* kva = p.kvamax + static_cast<size_t>(layer) * 2 * e->Hkv;
+    TL_CU(cudaMemsetAsync(am, 0, 4 * sizeof(float), s));
+    TL_CU(cudaMemsetAsync(kva, 0, 2 * e->Hkv * sizeof(float), s));
+    TL_CU(cudaMemcpyAsync(p.x, x, rowsD, cudaMemcpyHostToDevice, s));
+    TL_TRY(enqueue_prefill_layer(e, static_cast<int>(layer), 1, S, static_cast<int>(slot), cap ? &lc : nullptr));
+    if (out) TL_CU(cudaMemcpyAsync(out, p.x, rowsD, cudaMemcpyDeviceToHost, s));
+    TL_CU(cudaStreamSynchronize(s));
+    return tl_device_error();
+  };
+  const tl_status st = body();
+  cudaStreamSynchronize(e->stream);
+  cudaFree(lc.i32);
+  cudaFree(lc.f32);
+  cudaFree(lc.scores);
+  cudaFree(lc.probs);
+  return st;
+}
+
+tl_status tl_decode_layer(tl_engine* e, uint32_t layer, uint32_t n, const uint32_t* slots,
+                          const uint32_t* positions, const float* x, float* out, const tl_layer_capture* cap) {
+  if (!e || !x || !slots || !positions) return TL_ERR_INVALID_ARGUMENT;
+  if (!e->loaded) return TL_ERR_NOT_LOADED;
+  if (e->tp_world > 1) return TL_ERR_UNIMPLEMENTED;
+  if (cap && (cap->scores || cap->probs)) return TL_ERR_UNIMPLEMENTED;
+  if (n < static_cast<uint32_t>(kTcMinRows)) return TL_ERR_UNIMPLEMENTED;
+  if (n > static_cast<uint32_t>(e->B) || layer >= static_cast<uint32_t>(e->L)) return TL_ERR_OUT_OF_RANGE;
+  std::vector<char> seen(e->B, 0);
+  for (uint32_t r = 0; r < n; ++r) {
+    if (slots[r] >= static_cast<uint32_t>(e->B) || positions[r] >= static_cast<uint32_t>(e->P))
+      return TL_ERR_OUT_OF_RANGE;
+    if (seen[slots[r]]++) return TL_ERR_INVALID_ARGUMENT;
+  }
+  TL_CU(cudaSetDevice(e->device));
+  TL_TRY(ensure_pinned(e, 3 * static_cast<size_t>(n) + static_cast<size_t>(e->B)));
+  DecodeBufs& d = e->dec;
+  const int M = static_cast<int>(n);
+  const size_t rowsD = static_cast<size_t>(n) * e->D * sizeof(float);
+  LayerCap lc;
+  lc.h = cap;
+  auto body = [&]() -> tl_status {
+    if (cap) {
+      const size_t wide = std::max<size_t>(std::max<size_t>(e->Nqkv, 2 * static_cast<size_t>(e->F)), e->D);
+      TL_TRY(dmalloc(&lc.i32, static_cast<size_t>(n) * wide));
+      TL_TRY(dmalloc(&lc.f32, static_cast<size_t>(n) * 2 * e->F));
+    }
+    cudaStream_t s = e->stream;
+    int* h = e->h_pinned;
+    for (int r = 0; r < M; ++r) {
+      h[r] = static_cast<int>(slots[r]);
+      h[M + r] = static_cast<int>(positions[r]);
+      h[2 * M + r] = 1;
+    }
+    TL_CU(cudaMemcpyAsync(d.slots, h, M * sizeof(int), cudaMemcpyHostToDevice, s));
+    TL_CU(cudaMemcpyAsync(d.pos, h + M, M * sizeof(int), cudaMemcpyHostToDevice, s));
+    TL_CU(cudaMemcpyAsync(d.active, h + 2 * M, M * sizeof(int), cudaMemcpyHostToDevice, s));
+    TL_CU(cudaMemcpyAsync(d.x, x, rowsD, cudaMemcpyHostToDevice, s));
+    TL_TRY(enqueue_decode_layer_tc(e, static_cast<int>(layer), M, cap ? &lc : nullptr));
+    if (out) TL_CU(cudaMemcpyAsync(out, d.x, rowsD, cudaMemcpyDeviceToHost, s));
+    TL_CU(cudaStreamSynchronize(s));
+    return tl_device_error();
+  };
+  const tl_status st = body();
+  // the decode graphs read row m's cache from slot m
+  int* h = e->h_pinned + 3 * static_cast<size_t>(n);
+  for (int r = 0; r < e->B; ++r) h[r] = r;
+  cudaMemcpyAsync(d.slots, h, e->B * sizeof(int), cudaMemcpyHostToDevice, e->stream);
+  cudaStreamSynchronize(e->stream);
+  cudaFree(lc.i32);
+  cudaFree(lc.f32);
+  return st;
 }
 
 tl_status tl_decode_logits(tl_engine* e, uint32_t slot, uint32_t token, float* logits_out) {

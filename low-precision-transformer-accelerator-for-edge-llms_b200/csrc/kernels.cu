@@ -76,7 +76,6 @@ constexpr int kGemvThreads = 256;
 constexpr int kGemvWarps = kGemvThreads / 32;
 constexpr int kGemvRW = 2;   // weight rows per warp item
 constexpr int kGemvU = 4;    // 16-byte chunks per lane per row per item
-constexpr int kGemvMaxGrid = 1024;
 static int g_num_sms[64] = {0};
 
 
@@ -905,6 +904,62 @@ cudaError_t launch_quantize_rows(const float* x, const float* absmax_groups, int
     quantize_rows_vec_kernel<<<rows, kQuantThreads, 0, s>>>(x, absmax_groups, K, rows_per_group, out);
   else
     quantize_rows_kernel<<<rows, 256, 0, s>>>(x, absmax_groups, K, rows_per_group, out);
+  return cudaGetLastError();
+}
+
+// Debug capture of one sequence's attention (not on the generation path):
+// scores[h][i][j] = (q_i . K_j) * 1/8 with K_j the dequantized cache row
+// float32(k_q) * float32(s_K) (model/tinyllama_gemm_int8.py:156-159), -1e9
+// where j > i (the causal fill of :159), and probs = the max-shifted softmax
+// of each row (model/tinyllama.py:100-103). q comes from the rotated qkv rows.
+// Products are summed in double, so these match the reference's float64
+// scores to well below float32 resolution. One CTA per (query row, head).
+__global__ void __launch_bounds__(256) attn_scores_debug_kernel(const float* qkv, int ld, int S, int H, int Hkv,
+                                                                const int8_t* kc, const float* ks, int slot, int layer,
+                                                                int L, int P, float* scores, float* probs) {
+  __shared__ double red[8];
+  __shared__ float q[64];
+  const int i = blockIdx.x, h = blockIdx.y, t = threadIdx.x;
+  const int kvh = h / (H / Hkv);
+  if (t < 64) q[t] = qkv[static_cast<size_t>(i) * ld + h * 64 + t];
+  __syncthreads();
+  const size_t base = ((static_cast<size_t>(slot) * L + layer) * Hkv + kvh);
+  const int8_t* krows = kc + base * P * 64;
+  const float sk = ks[base];
+  float* srow = scores + (static_cast<size_t>(h) * S + i) * S;
+  float* prow = probs + (static_cast<size_t>(h) * S + i) * S;
+  double m = -1e300;
+  for (int j = t; j < S; j += blockDim.x) {
+    double sc = -1e9;
+    if (j <= i) {
+      double acc = 0.0;
+      for (int d = 0; d < 64; ++d)
+        acc += static_cast<double>(q[d]) * static_cast<double>(__fmul_rn(static_cast<float>(krows[j * 64 + d]), sk));
+      sc = acc * 0.125;
+    }
+    srow[j] = static_cast<float>(sc);
+    m = fmax(m, sc);
+  }
+  for (int o = 16; o; o >>= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((t & 31) == 0) red[t >> 5] = m;
+  __syncthreads();
+  m = red[0];
+  for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) m = fmax(m, red[w]);
+  __syncthreads();
+  double sum = 0.0;
+  for (int j = t; j < S; j += blockDim.x) sum += exp(static_cast<double>(srow[j]) - m);
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if ((t & 31) == 0) red[t >> 5] = sum;
+  __syncthreads();
+  sum = 0.0;
+  for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) sum += red[w];
+  for (int j = t; j < S; j += blockDim.x) prow[j] = static_cast<float>(exp(static_cast<double>(srow[j]) - m) / sum);
+}
+
+cudaError_t launch_attn_scores_debug(const float* qkv, int ld, int S, int H, int Hkv, const int8_t* kc, const float* ks,
+                                     int slot, int layer, int L, int P, float* scores, float* probs, cudaStream_t s) {
+  if (S <= 0 || H <= 0 || Hkv <= 0 || H % Hkv) return cudaErrorInvalidValue;
+  attn_scores_debug_kernel<<<dim3(S, H), 256, 0, s>>>(qkv, ld, S, H, Hkv, kc, ks, slot, layer, L, P, scores, probs);
   return cudaGetLastError();
 }
 

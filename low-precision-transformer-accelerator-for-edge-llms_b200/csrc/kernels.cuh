@@ -59,6 +59,10 @@ struct GemvArgs {
 // particular before stream capture, where attribute changes are not wanted).
 cudaError_t prepare_kernels(int max_k);
 
+// Upper bound on the GEMV grid (gridDim.x): the argmax epilogue keeps one
+// candidate per CTA and row, so its scratch is sized by this bound.
+constexpr int kGemvMaxGrid = 1024;
+
 // Picks the tile shape and launches; `pdl` enables programmatic dependent
 // launch (the kernel prefetches weights before waiting on its predecessor).
 cudaError_t launch_gemv(int pro, int epi, const GemvArgs& a, cudaStream_t s, bool pdl);
@@ -210,6 +214,11 @@ cudaError_t launch_attn_prefill(const float* qkv, int ld, int rows, int seq_len,
                                 const int8_t* kc, const int8_t* vc, const float* ks,
                                 const float* vs, int slot_base, int layer, int L, int P,
                                 float* out, float* out_absmax, cudaStream_t s);
+
+// Debug capture: scores / probabilities [H][S][S] of one prefilled sequence
+// (rotated q in qkv, K from cache slot `slot`), see kernels.cu.
+cudaError_t launch_attn_scores_debug(const float* qkv, int ld, int S, int H, int Hkv, const int8_t* kc, const float* ks,
+                                     int slot, int layer, int L, int P, float* scores, float* probs, cudaStream_t s);
 
 // ---- per-row (one sequence per row) activation prep for the batched path
 // out_q[r] = quantize(rmsnorm(x[r]) ), out_absmax[r] = max|rmsnorm(x[r])|;

@@ -11,7 +11,10 @@ error behaviour where the reference has one):
 * ``quantize_int8(t)``           model/tinyllama_gemm_int8.py:36-42
 * ``rms_norm(x, w, eps)``        model/tinyllama.py:45-50
 * ``forward_mixed(token_ids, weights, cos, sin, layer_count, quantize_lm_head)``
-  model/tinyllama_gemm_int8.py:437-467 (last row of logits; see its docstring)
+  model/tinyllama_gemm_int8.py:437-467 -> logits of every row, [S, vocab]
+* ``mixed_precision_decoder_layer(x, layer, cfg, cos, sin, capture_arrays)``
+  model/tinyllama_gemm_int8.py:256-281 -> ``(out, debug)`` with the
+  reference's nested debug keys (``Engine.decoder_layer`` for a loaded model)
 * ``Engine.generate`` / ``generate_batch``: run_generate
   (model/tinyllama_gemm_int8.py:629-685) with the RTL launch/stop contract
   (rtl/control/prefill_decode_controller.sv, stop_condition_unit.sv).
@@ -23,6 +26,7 @@ library is missing or no GPU is visible, calls raise.
 from __future__ import annotations
 
 import ctypes as C
+from collections import OrderedDict
 from dataclasses import dataclass, field
 from pathlib import Path
 
@@ -51,6 +55,7 @@ EXPORTS = (
     "tl_transpose_i8", "tl_quantize_int8",
     "tl_gemm_i8", "tl_gemm_i8_requant", "tl_quantized_linear", "tl_rmsnorm", "tl_lmhead_argmax",
     "tl_attn_decode", "tl_attn_prefill", "tl_lmhead_argmax_noalloc",
+    "tl_forward_logits", "tl_decoder_layer", "tl_decode_layer",
 )
 
 
@@ -91,6 +96,27 @@ class RunStatus(C.Structure):
 
     def as_dict(self) -> dict:
         return {f: getattr(self, f) for f, _ in self._fields_}
+
+
+# tl_layer_capture: (field, element dtype, shape key) in the C struct's order.
+# Shape keys: S rows, D hidden, Dq heads*64, Dkv kv_heads*64, F intermediate,
+# HSS heads x S x S, 1 one float.
+CAPTURE_FIELDS = (
+    ("attn_input", np.float32, "SD"), ("qkv_input_q", np.int8, "SD"), ("qkv_input_absmax", np.float32, "1"),
+    ("q_acc", np.int32, "SDq"), ("k_acc", np.int32, "SDkv"), ("v_acc", np.int32, "SDkv"),
+    ("q_proj", np.float32, "SDq"), ("k_proj", np.float32, "SDkv"), ("v_proj", np.float32, "SDkv"),
+    ("scores", np.float32, "HSS"), ("probs", np.float32, "HSS"), ("attended", np.float32, "SDq"),
+    ("o_input_q", np.int8, "SDq"), ("o_input_absmax", np.float32, "1"), ("o_acc", np.int32, "SD"),
+    ("o_proj", np.float32, "SD"), ("x_after_attn", np.float32, "SD"), ("ffn_input", np.float32, "SD"),
+    ("gate_up_input_q", np.int8, "SD"), ("gate_up_input_absmax", np.float32, "1"),
+    ("gate_acc", np.int32, "SF"), ("up_acc", np.int32, "SF"), ("gate_proj", np.float32, "SF"),
+    ("up_proj", np.float32, "SF"), ("hidden", np.float32, "SF"), ("down_input_q", np.int8, "SF"),
+    ("down_input_absmax", np.float32, "1"), ("down_acc", np.int32, "SD"), ("down_proj", np.float32, "SD"),
+)
+
+
+class LayerCapture(C.Structure):
+    _fields_ = [(name, C.c_void_p) for name, _, _ in CAPTURE_FIELDS]
 
 
 _LIB = None
@@ -142,6 +168,9 @@ def load_library(path: Path | str | None = None):
         "tl_attn_decode": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, vp]),
         "tl_attn_prefill": (i32, [vp, i32, i32, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, vp, vp]),
         "tl_lmhead_argmax_noalloc": (i32, [vp, vp, C.c_float, vp, vp, i32, i32, i32, vp, vp, vp]),
+        "tl_forward_logits": (i32, [vp, vp, u32, vp, vp]),
+        "tl_decoder_layer": (i32, [vp, u32, u32, vp, u32, vp, C.POINTER(LayerCapture)]),
+        "tl_decode_layer": (i32, [vp, u32, u32, vp, vp, vp, vp, C.POINTER(LayerCapture)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -272,6 +301,18 @@ def load_checkpoint_npz(path, layer_count: int | None = None, granularity: str =
         n = cfg["num_hidden_layers"] if layer_count is None else int(layer_count)
         if not 0 < n <= cfg["num_hidden_layers"]:
             raise ValueError(f"layer_count {n} outside 1..{cfg['num_hidden_layers']}")
+        shapes = model_shapes(cfg)
+        d, v = cfg["hidden_size"], cfg["vocab_size"]
+        expect = {"embed_w": (v, d), "final_norm_w": (d,), "lm_head_w": (d, v)}
+        for i in range(n):
+            expect.update({f"layer{i}_{p}_w": shapes[p] for p in _NPZ_PROJ})
+            expect[f"layer{i}_input_norm_w"] = (d,)
+            expect[f"layer{i}_post_norm_w"] = (d,)
+        for key, shape in expect.items():
+            if key not in arrays:
+                raise ValueError(f"weight archive has no {key}")
+            if tuple(arrays[key].shape) != shape:
+                raise ValueError(f"{key}: shape {tuple(arrays[key].shape)}, the meta_* entries imply {shape}")
         layers = []
         for i in range(n):
             projs = [quantize_weight(arrays[f"layer{i}_{p}_w"], granularity) for p in _NPZ_PROJ]
@@ -289,6 +330,50 @@ def rope_tables(n_pos: int, head_dim: int, theta: float) -> tuple[np.ndarray, np
     ang = np.outer(np.arange(n_pos, dtype=np.float32), inv_freq)
     ang = np.concatenate([ang, ang], axis=-1)
     return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+_CFG_KEYS = ("hidden_size", "intermediate_size", "num_hidden_layers", "num_attention_heads",
+             "num_key_value_heads", "head_dim", "vocab_size", "max_position_embeddings")
+
+
+def model_shapes(cfg: dict) -> dict:
+    """[in, out] of each projection for a config (reference layout, x @ W)."""
+    d, f = cfg["hidden_size"], cfg["intermediate_size"]
+    dq = cfg["num_attention_heads"] * cfg["head_dim"]
+    dkv = cfg["num_key_value_heads"] * cfg["head_dim"]
+    return {"q": (d, dq), "k": (d, dkv), "v": (d, dkv), "o": (dq, d), "gate": (d, f), "up": (d, f), "down": (f, d)}
+
+
+def check_model(model: Model, cfg: dict) -> None:
+    """Raise ValueError unless every array of ``model`` has the shape the
+    engine configuration ``cfg`` implies (and the model's own cfg agrees)."""
+    for k in _CFG_KEYS:
+        if int(model.cfg.get(k, -1)) != int(cfg[k]):
+            raise ValueError(f"model {k}={model.cfg.get(k)} but the engine was created with {cfg[k]}")
+    d, v = cfg["hidden_size"], cfg["vocab_size"]
+    if len(model.layers) != cfg["num_hidden_layers"]:
+        raise ValueError(f"model has {len(model.layers)} layers, engine expects {cfg['num_hidden_layers']}")
+
+    def lin(name, l, shape):
+        w = np.asarray(l.w)
+        if w.shape != shape or w.dtype != np.int8:
+            raise ValueError(f"{name}: weight {w.dtype} {w.shape}, expected int8 {shape}")
+        if np.asarray(l.scale).shape != (shape[1],):
+            raise ValueError(f"{name}: scale shape {np.asarray(l.scale).shape}, expected ({shape[1]},)")
+
+    def vec(name, a, shape):
+        if np.asarray(a).shape != shape:
+            raise ValueError(f"{name}: shape {np.asarray(a).shape}, expected {shape}")
+
+    shapes = model_shapes(cfg)
+    for i, ly in enumerate(model.layers):
+        for p in _NPZ_PROJ:
+            lin(f"layer{i}.{p}", getattr(ly, p), shapes[p])
+        vec(f"layer{i}.input_norm", ly.input_norm, (d,))
+        vec(f"layer{i}.post_norm", ly.post_norm, (d,))
+    vec("embed", model.embed, (v, d))
+    vec("final_norm", model.final_norm, (d,))
+    lin("lm_head", model.lm_head, (d, v))
 
 
 # --------------------------------------------------------------------------
@@ -352,6 +437,11 @@ class Engine:
 
     # ----------------------------------------------------------- weights
     def load(self, model: Model):
+        """Copy a quantized model into the engine. The model must have exactly
+        the engine's configuration (layer count, widths, vocabulary): the C
+        side reads each array with the sizes the engine was created with, so
+        every shape is checked here first and a mismatch raises ValueError."""
+        check_model(model, self.cfg)
         cfg = model.cfg
         cos, sin = rope_tables(cfg["max_position_embeddings"], cfg["head_dim"], cfg["rope_theta"])
         keep = [cos, sin]
@@ -413,6 +503,81 @@ class Engine:
         out = np.zeros(self.cfg["vocab_size"], dtype=np.float32)
         check(self.lib.tl_prefill_logits(self.h, 0, _ptr(ids), ids.size, _ptr(out)), "tl_prefill_logits")
         return out
+
+    def forward_logits(self, ids, hidden: bool = False):
+        """float32 logits of every prompt row, [len(ids), vocab] (tl_forward_logits:
+        forward_mixed's output, model/tinyllama_gemm_int8.py:437-467). Leaves
+        the prompt prefilled in slot 0. ``hidden=True`` returns instead the
+        final RMSNorm output [len(ids), hidden] (the LM head's input) and
+        skips the LM head."""
+        ids = np.ascontiguousarray(np.asarray(list(ids), dtype=np.uint32))
+        if hidden:
+            out = np.zeros((ids.size, self.cfg["hidden_size"]), dtype=np.float32)
+            args = (None, _ptr(out))
+        else:
+            out = np.zeros((ids.size, self.cfg["vocab_size"]), dtype=np.float32)
+            args = (_ptr(out), None)
+        check(self.lib.tl_forward_logits(self.h, _ptr(ids) if ids.size else None, ids.size, *args),
+              "tl_forward_logits")
+        return out
+
+    def _capture(self, capture, S: int, groups: int, windows: bool):
+        c = self.cfg
+        dims = {"S": S, "D": c["hidden_size"], "Dq": c["num_attention_heads"] * c["head_dim"],
+                "Dkv": c["num_key_value_heads"] * c["head_dim"], "F": c["intermediate_size"]}
+        if capture is True:
+            capture = [n for n, _, k in CAPTURE_FIELDS if k != "HSS"]
+        want = set(capture or ())
+        unknown = want - {n for n, _, _ in CAPTURE_FIELDS}
+        if unknown:
+            raise ValueError(f"unknown capture fields {sorted(unknown)}")
+        arrays, cap = {}, LayerCapture()
+        for name, dt, key in CAPTURE_FIELDS:
+            if name not in want:
+                continue
+            if key == "HSS" and not windows:
+                raise ValueError(f"{name}: score windows are captured by decoder_layer only")
+            shape = ((groups,) if key == "1" else (c["num_attention_heads"], S, S) if key == "HSS"
+                     else (S, dims[key[1:]]))
+            arrays[name] = np.zeros(shape, dtype=dt)
+            setattr(cap, name, _ptr(arrays[name]))
+        return arrays, (C.byref(cap) if want else None), cap
+
+    def decode_layer(self, layer: int, x, slots, positions, capture=None):
+        """One decoder layer of a batched decode step on caller-given rows
+        (tl_decode_layer): row r of ``x`` [n, hidden] is the token at
+        ``positions[r]`` of the sequence in KV slot ``slots[r]``; its K/V row
+        is appended there. n >= 16 (the tensor-core decode path). Returns
+        (out [n, hidden], capture dict; ``*_input_absmax`` one float per row)."""
+        xf = np.ascontiguousarray(np.asarray(x, dtype=np.float32))
+        n = xf.shape[0]
+        if xf.ndim != 2 or xf.shape[1] != self.cfg["hidden_size"]:
+            raise ValueError(f"x must be [n, {self.cfg['hidden_size']}], got {xf.shape}")
+        sl = np.ascontiguousarray(np.asarray(slots, dtype=np.uint32))
+        ps = np.ascontiguousarray(np.asarray(positions, dtype=np.uint32))
+        if sl.shape != (n,) or ps.shape != (n,):
+            raise ValueError("slots and positions need one entry per row")
+        arrays, ref, _keep = self._capture(capture, n, n, False)
+        out = np.zeros_like(xf)
+        check(self.lib.tl_decode_layer(self.h, layer, n, _ptr(sl), _ptr(ps), _ptr(xf), _ptr(out), ref),
+              "tl_decode_layer")
+        return out, arrays
+
+    def decoder_layer(self, layer: int, x, slot: int = 0, capture=None):
+        """One decoder layer of this engine on caller-given activations
+        (teacher forcing, tl_decoder_layer): ``x`` float32 [S, hidden] is one
+        sequence at positions 0..S-1; layer ``layer``'s K/V for those rows go
+        into KV slot ``slot``. ``capture`` names the intermediate tensors to
+        return (fields of ``CAPTURE_FIELDS``; ``True`` = all but the [H,S,S]
+        score and probability windows). Returns (out [S, hidden], dict)."""
+        xf = np.ascontiguousarray(np.asarray(x, dtype=np.float32))
+        if xf.ndim != 2 or xf.shape[1] != self.cfg["hidden_size"]:
+            raise ValueError(f"x must be [S, {self.cfg['hidden_size']}], got {xf.shape}")
+        S = xf.shape[0]
+        arrays, ref, _keep = self._capture(capture, S, 1, True)
+        out = np.zeros_like(xf)
+        check(self.lib.tl_decoder_layer(self.h, slot, layer, _ptr(xf), S, _ptr(out), ref), "tl_decoder_layer")
+        return out, arrays
 
     def decode_logits(self, token: int, slot: int = 0) -> np.ndarray:
         out = np.zeros(self.cfg["vocab_size"], dtype=np.float32)
@@ -552,26 +717,156 @@ def rms_norm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
     return out.cpu().numpy().reshape(shp)
 
 
-_ENGINE_CACHE: dict = {}
+_ENGINE_CACHE: "OrderedDict" = OrderedDict()
+_ENGINE_CACHE_MAX = 4
+
+
+def _cached_engine(key, owner, make_model, cfg: dict, max_prefill: int):
+    """Engine for a weights object (or a reference layer dict), reused while
+    the caller passes the same object: the cache holds a reference to
+    ``owner`` so its id cannot be reused while cached. The least recently used
+    of more than four engines is closed (each holds device memory)."""
+    hit = _ENGINE_CACHE.get(key)
+    if hit is not None and hit[0] is owner:
+        _ENGINE_CACHE.move_to_end(key)
+        return hit[1]
+    if hit is not None:
+        hit[1].close()
+        del _ENGINE_CACHE[key]
+    while len(_ENGINE_CACHE) >= _ENGINE_CACHE_MAX:
+        _, (_, old) = _ENGINE_CACHE.popitem(last=False)
+        old.close()
+    model = make_model()
+    eng = Engine(model.cfg, max_batch=1, max_prefill_tokens=max_prefill)
+    eng.load(model)
+    _ENGINE_CACHE[key] = (owner, eng)
+    return eng
 
 
 def forward_mixed(token_ids, weights, cos=None, sin=None, layer_count: int | None = None,
                   quantize_lm_head: bool = True) -> np.ndarray:
     """GPU ``forward_mixed`` (model/tinyllama_gemm_int8.py:437-467) for a
-    ``TinyLlamaWeights``-like object. Only the INT8 LM head is supported
-    (``quantize_lm_head=True``). Returns the logits of the LAST row as an
-    array of shape [1, vocab] -- the only row the reference's callers read
-    (``logits[-1]``, :671). ``cos``/``sin`` are accepted for signature
-    compatibility; the engine uses the same float32 tables."""
-    if not quantize_lm_head:
-        raise NotImplementedError("the engine's LM head is INT8 (quantize_lm_head=True)")
-    key = (id(weights), layer_count)
-    eng = _ENGINE_CACHE.get(key)
-    if eng is None:
-        model = from_tinyllama_weights(weights, layer_count)
-        eng = Engine(model.cfg, max_batch=1)
-        eng.load(model)
-        _ENGINE_CACHE[key] = eng
-    if len(token_ids) > eng.cfg["max_position_embeddings"]:
-        raise ValueError("Sequence length exceeds max_position_embeddings")
-    return eng.prefill_logits(token_ids)[None, :]
+    ``TinyLlamaWeights``-like object: logits of every row, float32 [S, vocab].
+    Weights are quantized per tensor, as the reference bridge does on every
+    call; attention reads the engine's INT8 KV cache (per-(layer, kv head)
+    scales calibrated on the prompt), the one place the engine's numerics
+    differ from the reference's float K/V. ``quantize_lm_head=False`` takes
+    the final RMSNorm output from the engine and multiplies it by the float
+    LM head on the GPU (float32, no TF32), as the reference's float branch
+    does. ``cos``/``sin`` are accepted for signature compatibility; the
+    engine builds the same float32 tables from the config."""
+    cfg = dict(weights.cfg)
+    n_layers = cfg["num_hidden_layers"] if layer_count is None else int(layer_count)
+    if not 0 < n_layers <= cfg["num_hidden_layers"]:
+        raise ValueError(f"--layers must be between 1 and {cfg['num_hidden_layers']}")
+    if len(token_ids) > cfg["max_position_embeddings"]:
+        raise ValueError(f"Sequence length {len(token_ids)} exceeds "
+                         f"max_position_embeddings={cfg['max_position_embeddings']}")
+    eng = _cached_engine(("model", id(weights), n_layers), weights,
+                         lambda: from_tinyllama_weights(weights, n_layers), cfg, cfg["max_position_embeddings"])
+    if quantize_lm_head:
+        return eng.forward_logits(token_ids)
+    torch = _torch()
+    hid = eng.forward_logits(token_ids, hidden=True)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        w = torch.from_numpy(np.ascontiguousarray(np.asarray(weights.lm_head_w(), np.float32))).cuda()
+        return (torch.from_numpy(hid).cuda() @ w).cpu().numpy().astype(np.float32)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def _linear_debug(capture_arrays, input_fp, input_q, absmax, w_fp, w_q, w_scale, acc, output_fp):
+    """``quantized_linear``'s debug dict (model/tinyllama_gemm_int8.py:74-86)."""
+    peak = float(absmax[0])
+    sx = 1.0 if peak == 0.0 else peak / 127.0
+    ws = np.asarray(w_scale, np.float64)
+    d = {"input_scale": np.array([sx], dtype=np.float32),
+         "weight_scale": (np.array([ws[0]], np.float32) if np.all(ws == ws[0]) else ws.astype(np.float32))}
+    if capture_arrays:
+        d.update({"input_fp": input_fp, "input_q": input_q, "weight_fp": w_fp, "weight_q": w_q,
+                  "accum_int32": acc, "output_fp": output_fp})
+    return d
+
+
+def layer_debug(cap: dict, capture_arrays: bool, weights: dict | None = None, quant: dict | None = None) -> dict:
+    """Arrange a :meth:`Engine.decoder_layer` capture as the debug dict of
+    ``mixed_precision_decoder_layer`` (model/tinyllama_gemm_int8.py:136-281):
+    ``attn``/``ffn`` sub-dicts with one ``quantized_linear`` dict per
+    projection plus the ``*_fp`` tensors. ``weights`` (float [in, out] by
+    projection name) and ``quant`` (Linear by name) fill ``weight_fp`` /
+    ``weight_q`` / ``weight_scale`` when given."""
+    weights, quant = weights or {}, quant or {}
+
+    def lin(name, inp, inq, am, acc, out):
+        q = quant.get(name)
+        return _linear_debug(capture_arrays, inp, inq, am, weights.get(name),
+                             None if q is None else q.w, [1.0] if q is None else q.scale, acc, out)
+
+    attn = {
+        "q_proj": lin("q", cap["attn_input"], cap["qkv_input_q"], cap["qkv_input_absmax"], cap["q_acc"], cap["q_proj"]),
+        "k_proj": lin("k", cap["attn_input"], cap["qkv_input_q"], cap["qkv_input_absmax"], cap["k_acc"], cap["k_proj"]),
+        "v_proj": lin("v", cap["attn_input"], cap["qkv_input_q"], cap["qkv_input_absmax"], cap["v_acc"], cap["v_proj"]),
+        "o_proj": lin("o", cap["attended"], cap["o_input_q"], cap["o_input_absmax"], cap["o_acc"], cap["o_proj"]),
+        "q_proj_fp": cap["q_proj"], "k_proj_fp": cap["k_proj"], "v_proj_fp": cap["v_proj"],
+    }
+    ffn = {
+        "gate_proj": lin("gate", cap["ffn_input"], cap["gate_up_input_q"], cap["gate_up_input_absmax"],
+                         cap["gate_acc"], cap["gate_proj"]),
+        "up_proj": lin("up", cap["ffn_input"], cap["gate_up_input_q"], cap["gate_up_input_absmax"],
+                       cap["up_acc"], cap["up_proj"]),
+        "down_proj": lin("down", cap["hidden"], cap["down_input_q"], cap["down_input_absmax"], cap["down_acc"],
+                         cap["down_proj"]),
+        "gate_proj_fp": cap["gate_proj"], "up_proj_fp": cap["up_proj"], "hidden_fp": cap["hidden"],
+    }
+    if capture_arrays:
+        attn.update({"scores_fp": cap.get("scores"), "weights_fp": cap.get("probs"),
+                     "attended_fp": cap["attended"], "out_fp": cap["o_proj"]})
+        ffn["out_fp"] = cap["down_proj"]
+        attn = {k: v for k, v in attn.items() if v is not None}
+    return {"attn_input_fp": cap["attn_input"], "x_after_attn_fp": cap["x_after_attn"],
+            "ffn_input_fp": cap["ffn_input"], "attn": attn, "ffn": ffn}
+
+
+def mixed_precision_decoder_layer(x, layer: dict, cfg: dict, cos=None, sin=None, capture_arrays: bool = False):
+    """GPU ``mixed_precision_decoder_layer`` (model/tinyllama_gemm_int8.py:256-281).
+
+    ``layer`` is the reference's layer dict (model/tinyllama.py:249-267:
+    float ``q_w`` .. ``down_w`` stored [in, out], ``*_b`` biases, the two
+    norm gains); ``x`` float32 [S, hidden] is one sequence at positions
+    0..S-1. The weights are quantized per tensor (the bridge's per-call rule,
+    :69) and the layer runs on the engine's prefill kernels; K and V go
+    through the engine's INT8 cache before attention. Returns ``(out,
+    debug)`` with the reference's debug keys; ``capture_arrays`` adds the
+    per-projection arrays (``input_q``, ``accum_int32``, ...), the [H, S, S]
+    score and probability windows and the block outputs. Biases are not
+    supported (TinyLlama has none)."""
+    for b in ("q_b", "k_b", "v_b", "o_b", "gate_b", "up_b", "down_b"):
+        if layer.get(b) is not None:
+            raise NotImplementedError(f"projection biases are not supported by the engine ({b})")
+    xf = np.asarray(x, dtype=np.float32)
+    c = {k: cfg[k] for k in ("hidden_size", "intermediate_size", "num_attention_heads", "num_key_value_heads",
+                             "head_dim", "max_position_embeddings", "rms_norm_eps", "rope_theta")}
+    c.update(num_hidden_layers=1, vocab_size=16)  # the layer engine never uses the embedding or LM head
+    if xf.shape[0] > c["max_position_embeddings"]:
+        raise ValueError(f"Sequence length {xf.shape[0]} exceeds max_position_embeddings={c['max_position_embeddings']}")
+
+    def make_model():
+        quant = {p: quantize_weight(layer[f"{p}_w"], "tensor") for p in _NPZ_PROJ}
+        ly = Layer(*(quant[p] for p in _NPZ_PROJ), input_norm=np.asarray(layer["input_norm_w"], np.float32),
+                   post_norm=np.asarray(layer["post_norm_w"], np.float32))
+        d = c["hidden_size"]
+        m = Model(dict(c), np.zeros((16, d), np.float32), np.ones(d, np.float32),
+                  Linear(np.zeros((d, 16), np.int8), np.ones(16)), [ly])
+        return m
+
+    eng = _cached_engine(("layer", id(layer)), layer, make_model, c, c["max_position_embeddings"])
+    want = [n for n, _, k in CAPTURE_FIELDS if capture_arrays or k != "HSS"]
+    out, cap = eng.decoder_layer(0, xf, capture=want)
+    quant = {p: quantize_weight(layer[f"{p}_w"], "tensor") for p in _NPZ_PROJ} if capture_arrays else None
+    wfp = {p: np.asarray(layer[f"{p}_w"], np.float32) for p in _NPZ_PROJ} if capture_arrays else None
+    debug = layer_debug(cap, capture_arrays, wfp, quant)
+    if capture_arrays:
+        debug["layer_out_fp"] = out
+    return out, debug

@@ -76,6 +76,42 @@ def int8_matmul(a_q: np.ndarray, b_q: np.ndarray) -> np.ndarray:
     return prod.astype(np.int32)
 
 
+class ExactMatmul:
+    """Exact INT8 x INT8 -> INT32 matmul for large models, faster than
+    :func:`int8_matmul` when the same weight matrices are used many times.
+
+    Each weight ``b_q`` [K, N] is converted once to float32 (kept while this
+    object lives) and the product is formed over K-chunks of at most 1024:
+    within a chunk every product and every partial sum is an integer of
+    magnitude <= 1024 * 127 * 127 < 2**24, so float32 BLAS is exact in any
+    summation order; the chunk results are summed in float64 (exact) and
+    returned as INT32, identical to ``x_q.astype(int32) @ w_q.astype(int32)``
+    (model/tinyllama_gemm_int8.py:70)."""
+
+    CHUNK = 1024
+
+    def __init__(self):
+        self._cache: dict = {}
+
+    def _chunks(self, b_q: np.ndarray):
+        hit = self._cache.get(id(b_q))
+        if hit is not None and hit[0] is b_q:
+            return hit[1]
+        k = b_q.shape[0]
+        parts = [np.asarray(b_q[i:i + self.CHUNK], dtype=np.float32) for i in range(0, k, self.CHUNK)]
+        self._cache[id(b_q)] = (b_q, parts)
+        return parts
+
+    def __call__(self, a_q: np.ndarray, b_q: np.ndarray) -> np.ndarray:
+        parts = self._chunks(b_q)
+        a = np.asarray(a_q, dtype=np.float32)
+        acc = None
+        for i, bp in enumerate(parts):
+            r = (a[:, i * self.CHUNK:i * self.CHUNK + bp.shape[0]] @ bp).astype(np.float64)
+            acc = r if acc is None else acc + r
+        return acc.astype(np.int32)
+
+
 def int8_matmul_reference_path(a_q: np.ndarray, b_q: np.ndarray) -> np.ndarray:
     """The reference's own INT32 NumPy matmul (non-BLAS, single thread),
     model/tinyllama_gemm_int8.py:70. Used only to time the CPU baseline."""
@@ -219,6 +255,44 @@ def attention_core(q_heads: np.ndarray, k_heads: np.ndarray, v_heads: np.ndarray
     return out.transpose(1, 0, 2).reshape(sq, n_heads * hd)
 
 
+def attention_core_f32(q_heads: np.ndarray, k_heads: np.ndarray, v_heads: np.ndarray,
+                       groups: int, attn_scale, causal: bool) -> np.ndarray:
+    """:func:`attention_core` with every step in float32 instead of the
+    reference's float64 (scores, mask, softmax, weighted sum). Not the
+    reference's numerics: it exists to measure how far the reference's own
+    INT8 pipeline moves when only the attention arithmetic changes by
+    float32 rounding (the sensitivity that end-to-end tolerances are set
+    against)."""
+    q = np.asarray(q_heads, np.float32)
+    k_rep = repeat_kv(np.asarray(k_heads, np.float32), groups)
+    v_rep = repeat_kv(np.asarray(v_heads, np.float32), groups)
+    scores = (q @ k_rep.transpose(0, 2, 1)) * np.float32(attn_scale)
+    if causal:
+        scores[:, ~causal_mask(scores.shape[-1])] = np.float32(MASK_FILL)
+    e = np.exp(scores - np.max(scores, axis=-1, keepdims=True))
+    probs = e / np.sum(e, axis=-1, keepdims=True)
+    out = probs @ v_rep
+    n_heads, sq, hd = q.shape
+    return out.transpose(1, 0, 2).reshape(sq, n_heads * hd)
+
+
+def attention_core_noisy(seed: int, rel: float = 2e-6):
+    """:func:`attention_core` whose output is perturbed by Gaussian noise of
+    ``rel`` x max|output| (fresh noise per call, seeded). Not the reference's
+    numerics: it models any implementation whose attention is within ``rel``
+    of the float64 reference (2e-6 is the accuracy the decode attention
+    tests hold the CUDA kernels to), to measure how far that moves the
+    reference's own INT8 pipeline end to end."""
+    rng = np.random.default_rng(seed)
+
+    def core(q_heads, k_heads, v_heads, groups, attn_scale, causal):
+        out = attention_core(q_heads, k_heads, v_heads, groups, attn_scale, causal)
+        peak = float(np.max(np.abs(out))) if out.size else 0.0
+        return out + rel * peak * rng.standard_normal(out.shape)
+
+    return core
+
+
 # ----------------------------------------------------------------------------
 # Decoder layer and full forward, reference semantics (no KV cache)
 # ----------------------------------------------------------------------------
@@ -255,6 +329,34 @@ def decoder_layer_mixed(x: np.ndarray, layer, cfg: dict, cos: np.ndarray, sin: n
     u, _, _, _ = linear_q(h2, layer.up.w_q, layer.up.scale, matmul)
     hid = silu(g) * u
     d, _, _, _ = linear_q(hid, layer.down.w_q, layer.down.scale, matmul)
+    return (x1 + d).astype(np.float32)
+
+
+def reference_decoder_layer(x: np.ndarray, layer: dict, cfg: dict, cos: np.ndarray,
+                            sin: np.ndarray) -> np.ndarray:
+    """The float32 decoder layer the reference compares the INT8 path with
+    (``reference_decoder_layer``, model/tinyllama_gemm_int8.py:228-253, over
+    ``reference_self_attention`` :91-133 and ``reference_feed_forward``
+    :185-202): the same blocks with ``x @ W`` float matmuls. ``layer`` is a
+    reference-schema dict of float [in, out] weights (``q_w`` ..) and norm
+    gains (``input_norm_w``, ``post_norm_w``); no biases."""
+    s = x.shape[0]
+    eps = cfg["rms_norm_eps"]
+    f32 = lambda a: np.asarray(a, dtype=np.float32)
+    h = rms_norm(x, layer["input_norm_w"], eps)
+    q = (h @ f32(layer["q_w"])).astype(np.float32)
+    k = (h @ f32(layer["k_w"])).astype(np.float32)
+    v = (h @ f32(layer["v_w"])).astype(np.float32)
+    qh = rope(split_heads(q, cfg["num_attention_heads"], cfg["head_dim"]), cos[:s], sin[:s])
+    kh = rope(split_heads(k, cfg["num_key_value_heads"], cfg["head_dim"]), cos[:s], sin[:s])
+    vh = split_heads(v, cfg["num_key_value_heads"], cfg["head_dim"])
+    att = attention_core(qh, kh, vh, cfg["num_key_value_groups"], cfg["attn_scale"], True)
+    o = (f32(att) @ f32(layer["o_w"])).astype(np.float32)
+    x1 = x + o
+    h2 = rms_norm(x1, layer["post_norm_w"], eps)
+    g = (h2 @ f32(layer["gate_w"])).astype(np.float32)
+    u = (h2 @ f32(layer["up_w"])).astype(np.float32)
+    d = ((silu(g) * u) @ f32(layer["down_w"])).astype(np.float32)
     return (x1 + d).astype(np.float32)
 
 

@@ -43,13 +43,23 @@ MODE_PREFILL, MODE_DECODE = 0, 1
 class KVGolden:
     """One sequence's engine state: position, INT8 (or float32) KV cache."""
 
-    def __init__(self, model, kv: str = "int8", matmul=G.int8_matmul):
+    def __init__(self, model, kv: str = "int8", matmul=G.int8_matmul, attention: str = "f64",
+                 noise_seed: int = 0):
+        """``attention="f32"`` swaps the reference's float64 attention for
+        :func:`oracle.golden.attention_core_f32`, ``attention="noisy"`` for
+        :func:`oracle.golden.attention_core_noisy` (seeded by ``noise_seed``);
+        both exist only to measure the pipeline's sensitivity."""
         if kv not in ("int8", "fp32"):
             raise ValueError("kv must be 'int8' or 'fp32'")
+        if attention not in ("f64", "f32", "noisy"):
+            raise ValueError("attention must be 'f64', 'f32' or 'noisy'")
         self.m = model
         self.cfg = model.cfg
         self.kv = kv
         self.matmul = matmul
+        self.attention = {"f64": G.attention_core, "f32": G.attention_core_f32}.get(attention)
+        if attention == "noisy":
+            self.attention = G.attention_core_noisy(noise_seed)
         c = self.cfg
         self.cos, self.sin = G.build_rope_cache(c["max_position_embeddings"], c["head_dim"],
                                                 c["rope_theta"])
@@ -126,7 +136,7 @@ class KVGolden:
         else:
             self._store_decode_kv(li, kh, vh, p0)
         kd, vd = self._read_kv(li, p0 + s)
-        att = G.attention_core(qh, kd, vd, c["num_key_value_groups"], c["attn_scale"], prefill)
+        att = self.attention(qh, kd, vd, c["num_key_value_groups"], c["attn_scale"], prefill)
         o, _, _, _ = G.linear_q(att, lay.o.w_q, lay.o.scale, mm)
         x1 = x + o
         h2 = G.rms_norm(x1, lay.post_norm, eps)
@@ -135,6 +145,68 @@ class KVGolden:
         hid = G.silu(g) * u
         d, _, _, _ = G.linear_q(hid, lay.down.w_q, lay.down.scale, mm)
         return (x1 + d).astype(np.float32)
+
+    def layer_capture(self, li: int, x: np.ndarray, p0: int = 0, prefill: bool = True) -> tuple[np.ndarray, dict]:
+        """Layer ``li`` on ``x`` recording the tensors the engine's
+        ``tl_decoder_layer`` / ``tl_decode_layer`` captures name: each
+        projection's INT8 input and its absmax, INT32 accumulators, the float
+        projections, the attention output and the block outputs. With
+        ``prefill`` ``x`` [S, hidden] is a prompt at positions 0..S-1 (K/V of
+        this layer calibrated and cached); otherwise ``x`` [1, hidden] is the
+        token at position ``p0`` (K/V quantized with the frozen scales and
+        appended). Follows :meth:`_layer` (and through it
+        model/tinyllama_gemm_int8.py:136-281)."""
+        c = self.cfg
+        lay = self.m.layers[li]
+        s = x.shape[0]
+        eps = c["rms_norm_eps"]
+        mm = self.matmul
+        cap = {}
+        h = G.rms_norm(x, lay.input_norm, eps)
+        xq, sx = G.quantize_int8(h)
+        cap.update(attn_input=h, qkv_input_q=xq, qkv_input_absmax=np.float32(np.max(np.abs(h))))
+        outs = {}
+        for name in ("q", "k", "v"):
+            ln = getattr(lay, name)
+            acc = mm(xq, ln.w_q)
+            outs[name] = G.dequantize_int32(acc, sx, ln.scale)
+            cap[f"{name}_acc"] = acc
+            cap[f"{name}_proj"] = outs[name]
+        qh = G.split_heads(outs["q"], c["num_attention_heads"], c["head_dim"])
+        kh = G.split_heads(outs["k"], c["num_key_value_heads"], c["head_dim"])
+        vh = G.split_heads(outs["v"], c["num_key_value_heads"], c["head_dim"])
+        qh = G.rope(qh, self.cos[p0:p0 + s], self.sin[p0:p0 + s])
+        kh = G.rope(kh, self.cos[p0:p0 + s], self.sin[p0:p0 + s])
+        if prefill:
+            self._store_prompt_kv(li, kh, vh)
+        else:
+            self._store_decode_kv(li, kh, vh, p0)
+        cap["q_rot"] = qh
+        kd, vd = self._read_kv(li, p0 + s)
+        att = self.attention(qh, kd, vd, c["num_key_value_groups"], c["attn_scale"], prefill)
+        aq, sa = G.quantize_int8(att)
+        acc = mm(aq, lay.o.w_q)
+        o = G.dequantize_int32(acc, sa, lay.o.scale)
+        cap.update(attended=att.astype(np.float32), o_input_q=aq, o_input_absmax=np.float32(np.max(np.abs(att))),
+                   o_acc=acc, o_proj=o)
+        x1 = x + o
+        h2 = G.rms_norm(x1, lay.post_norm, eps)
+        hq, sh = G.quantize_int8(h2)
+        cap.update(x_after_attn=x1, ffn_input=h2, gate_up_input_q=hq,
+                   gate_up_input_absmax=np.float32(np.max(np.abs(h2))))
+        for name in ("gate", "up"):
+            ln = getattr(lay, name)
+            acc = mm(hq, ln.w_q)
+            outs[name] = G.dequantize_int32(acc, sh, ln.scale)
+            cap[f"{name}_acc"] = acc
+            cap[f"{name}_proj"] = outs[name]
+        hid = G.silu(outs["gate"]) * outs["up"]
+        dq, sd = G.quantize_int8(hid)
+        acc = mm(dq, lay.down.w_q)
+        d = G.dequantize_int32(acc, sd, lay.down.scale)
+        cap.update(hidden=hid, down_input_q=dq, down_input_absmax=np.float32(np.max(np.abs(hid))),
+                   down_acc=acc, down_proj=d)
+        return (x1 + d).astype(np.float32), cap
 
     def _head(self, x: np.ndarray) -> np.ndarray:
         """Final RMSNorm over all rows, per-tensor quantization over all rows,

@@ -196,3 +196,64 @@ def small_dims(vocab: int = 512, hidden: int = 256, ffn: int = 704, heads: int =
             "num_attention_heads": heads, "num_key_value_heads": kv_heads, "head_dim": head_dim,
             "vocab_size": vocab, "max_position_embeddings": max_pos,
             "rms_norm_eps": 1e-5, "rope_theta": 10000.0}
+
+
+def random_qmodel(seed: int, n_layers: int, dims: dict | None = None, std: float = 0.02,
+                  granularity: str = "channel") -> QModel:
+    """A seeded random model drawn and quantized one matrix at a time, so a
+    full 22-layer TinyLlama (1.04e9 INT8 weights) never holds its float
+    weights at once: every matrix and the embedding table ~ N(0, std) in
+    float32, quantized per output channel (or per tensor), RMSNorm gains 1.
+    Same distribution as :func:`random_archive` followed by
+    :func:`quantize_archive` (a different random stream)."""
+    base = dict(TINYLLAMA if dims is None else dims)
+    base["num_hidden_layers"] = n_layers
+    cfg = full_cfg(base)
+    rng = np.random.default_rng(seed)
+    d, v = cfg["hidden_size"], cfg["vocab_size"]
+    shapes = proj_shapes(cfg)
+
+    def draw(shape):
+        return quantize_weight(rng.standard_normal(shape, dtype=np.float32) * np.float32(std), granularity)
+
+    layers = []
+    for _ in range(n_layers):
+        qs = {n: draw(shapes[n]) for n in PROJ_NAMES}
+        layers.append(QLayer(**qs, input_norm=np.ones(d, np.float32), post_norm=np.ones(d, np.float32)))
+    embed = (rng.standard_normal((v, d), dtype=np.float32) * np.float32(std)).astype(np.float32)
+    return QModel(cfg=cfg, embed=embed, final_norm=np.ones(d, np.float32), lm_head=draw((d, v)), layers=layers)
+
+
+class ArchiveWeights:
+    """In-memory stand-in for the reference's ``TinyLlamaWeights`` over an
+    archive dict from :func:`random_archive`: the same ``cfg`` keys and the
+    same accessors (``embed``, ``final_norm_w``, ``lm_head_w``, ``layer`` with
+    ``*_b`` entries None when absent, ``_array``), model/tinyllama.py:198-267,
+    without writing the archive to disk."""
+
+    def __init__(self, arc: dict):
+        self.data = arc
+        self.cfg = archive_cfg(arc)
+        self.cfg["model_id"] = str(np.asarray(arc.get("meta_model_id", "random")).item())
+
+    def _array(self, key: str) -> np.ndarray:
+        return np.asarray(self.data[key], dtype=np.float32)
+
+    def _optional_array(self, key: str):
+        return self._array(key) if key in self.data else None
+
+    def embed(self, token_ids) -> np.ndarray:
+        return self._array("embed_w")[token_ids]
+
+    def final_norm_w(self) -> np.ndarray:
+        return self._array("final_norm_w")
+
+    def lm_head_w(self) -> np.ndarray:
+        return self._array("lm_head_w")
+
+    def layer(self, idx: int) -> dict:
+        d = {f"{p}_w": self._array(f"layer{idx}_{p}_w") for p in PROJ_NAMES}
+        d.update({f"{p}_b": self._optional_array(f"layer{idx}_{p}_b") for p in PROJ_NAMES})
+        d["input_norm_w"] = self._array(f"layer{idx}_input_norm_w")
+        d["post_norm_w"] = self._array(f"layer{idx}_post_norm_w")
+        return d

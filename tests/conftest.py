@@ -45,3 +45,13 @@ def pkg():
 def golden():
     import numpy as np
     return {p.stem: np.load(p) for p in GOLDEN.glob("*.npz")}
+
+
+@pytest.fixture(scope="session")
+def tinyllama22():
+    """The full 22-layer TinyLlama with seeded random per-channel INT8
+    weights, and an exact INT8 matmul that caches its float32 weight copies,
+    shared by the full-size GPU tests (drawing the model takes ~30 s)."""
+    from oracle import golden as G
+    from oracle import weights as W
+    return W.random_qmodel(2025, 22), G.ExactMatmul()

@@ -64,3 +64,47 @@ def test_npz_rejects_biases_and_foreign_archives(pkg, tmp_path):
     plain = {"embed_w": np.zeros((4, 4), np.float16)}
     with pytest.raises(ValueError, match="meta_"):
         pkg.load_checkpoint_npz(_save(tmp_path, plain, "plain.npz"))
+
+
+def test_model_shape_checks(pkg):
+    """Engine.load validates the model against the engine's configuration
+    before the C side reads any array (shim.check_model): a layer-count,
+    width or transposed-weight mismatch raises ValueError."""
+    import dataclasses
+    from helpers import small_model, to_engine_model
+    qm = small_model(7, 2)
+    m = to_engine_model(pkg, qm)
+    cfg = dict(qm.cfg)
+    pkg.check_model(m, cfg)
+    short = dataclasses.replace(m, layers=m.layers[:1])
+    with pytest.raises(ValueError, match="layers"):
+        pkg.check_model(short, cfg)
+    with pytest.raises(ValueError, match="num_hidden_layers"):
+        pkg.check_model(m, dict(cfg, num_hidden_layers=3))
+    bad = dataclasses.replace(m, layers=list(m.layers))
+    ly = m.layers[0]
+    bad.layers[0] = dataclasses.replace(ly, q=pkg.Linear(np.ascontiguousarray(ly.q.w.T), ly.q.scale))
+    if ly.q.w.shape[0] != ly.q.w.shape[1]:
+        with pytest.raises(ValueError, match="layer0.q"):
+            pkg.check_model(bad, cfg)
+    bad.layers[0] = dataclasses.replace(ly, down=pkg.Linear(ly.down.w, ly.down.scale[:-1]))
+    with pytest.raises(ValueError, match="layer0.down: scale"):
+        pkg.check_model(bad, cfg)
+    with pytest.raises(ValueError, match="embed"):
+        pkg.check_model(dataclasses.replace(m, embed=m.embed[:-1]), cfg)
+
+
+def test_checkpoint_npz_shape_mismatch(pkg, tmp_path):
+    """An archive whose arrays disagree with its meta_* entries is refused
+    with ValueError instead of being read with the wrong sizes."""
+    arc = W.random_archive(3, 1, W.small_dims())
+    arc["layer0_k_w"] = arc["layer0_k_w"][:, :-64]
+    path = tmp_path / "bad.npz"
+    np.savez(path, **arc)
+    with pytest.raises(ValueError, match="layer0_k_w"):
+        pkg.load_checkpoint_npz(path)
+    arc = W.random_archive(3, 1, W.small_dims())
+    del arc["final_norm_w"]
+    np.savez(path, **arc)
+    with pytest.raises(ValueError, match="final_norm_w"):
+        pkg.load_checkpoint_npz(path)
