@@ -209,6 +209,43 @@ TL_API tl_status tl_abort(tl_engine* eng);
 TL_API tl_status tl_prefill_logits(tl_engine* eng, uint32_t slot, const uint32_t* ids, uint32_t n,
                             float* logits_out);
 TL_API tl_status tl_decode_logits(tl_engine* eng, uint32_t slot, uint32_t token, float* logits_out);
+
+/* Debug capture of one decode step (docs/design_decisions.txt B8, the
+ * layer-/step-scoped capture of rtl/compute/debug_capture_mux.sv): the
+ * fixed tensor set of layer `layer` plus the step's final hidden state,
+ * top-16 logits and chosen token, read back after the step completes. Every
+ * pointer is an optional HOST destination (NULL skips it); the scalar fields
+ * are always written. Dq = heads*64, Dkv = kv_heads*64, n = position + 1. */
+typedef struct tl_debug_record {
+  uint32_t position;          /* position of the fed token (its K/V row) */
+  uint32_t chosen_token;      /* greedy argmax (lowest id on ties) */
+  uint32_t top_ids[16];       /* the 16 largest logits, highest first (lower id first on ties) */
+  float top_logits[16];
+  float input_absmax[5];      /* max |x| of the INT8 inputs of q/k/v, o, gate/up, down and the
+                                 LM head (each quantization scale is absmax / 127) */
+  float* layer_input;         /* [hidden]    layer input activation */
+  int8_t* qkv_input_q;        /* [hidden]    quantized input of the q/k/v projections */
+  float* q_proj;              /* [Dq]        q, k, v before RoPE */
+  float* k_proj;              /* [Dkv] */
+  float* v_proj;              /* [Dkv] */
+  float* scores;              /* [heads][n]  attention-score window */
+  float* probs;               /* [heads][n]  post-softmax window */
+  int8_t* k_row;              /* [kv_heads][64] updated K-cache row */
+  int8_t* v_row;              /* [kv_heads][64] updated V-cache row */
+  float* k_scale;             /* [kv_heads]  their scales */
+  float* v_scale;             /* [kv_heads] */
+  float* attended;            /* [Dq]        attention output */
+  float* layer_output;        /* [hidden]    layer output activation */
+  float* final_hidden;        /* [hidden]    final RMSNorm output */
+} tl_debug_record;
+
+/* tl_decode_logits with the debug capture of layer `layer`: feeds `token`
+ * to slot `slot` at its current position (advancing it) on the per-kernel
+ * decode path, fills `rec`, and (if logits_out is not NULL) the float32
+ * logits [vocab]. The performance path (graph-captured steps) is untouched.
+ * TL_ERR_UNIMPLEMENTED on a tensor-parallel engine. */
+TL_API tl_status tl_decode_debug(tl_engine* eng, uint32_t slot, uint32_t token, uint32_t layer, tl_debug_record* rec,
+                                 float* logits_out);
 /* Copies one (slot, layer) of the INT8 KV cache to host: k/v [kv_heads][n_pos][head_dim],
  * scales [kv_heads]. */
 TL_API tl_status tl_read_kv(tl_engine* eng, uint32_t slot, uint32_t layer, uint32_t n_pos,

@@ -9,9 +9,10 @@ any module name. The compute lives in ``libtl_b200.so``; ``shim`` is its
 ctypes binding and mirrors the reference's Python operator API.
 """
 
-from . import replicas, shim  # noqa: F401
+from . import analysis, replicas, shim  # noqa: F401
 from .shim import (  # noqa: F401
     Engine, Linear, Layer, Model, TLError, check_model, checkpoint_config, forward_mixed, from_tinyllama_weights,
     layer_debug, load_checkpoint_npz, load_library, mixed_precision_decoder_layer, quantize_int8, quantize_weight,
     quantized_linear, rms_norm, rope_tables, tp_unique_id,
 )
+from .analysis import diff_stats, dump_debug, flatten_named_arrays, run_analysis  # noqa: F401

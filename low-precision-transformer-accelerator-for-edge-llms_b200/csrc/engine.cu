@@ -557,42 +557,102 @@ tl_status enqueue_decode_step_d1(tl_engine* e, bool finalize) {
   return TL_OK;
 }
 
-tl_status enqueue_decode_step(tl_engine* e, int M, float* logits, bool finalize) {
+// Step-scoped debug capture (tl_decode_debug): the fixed tensor set of the
+// hardware's debug contract for one layer of a batch-1 decode step, taken by
+// extra copies and by kernels that apply the same rules to the same inputs
+// (the GEMV's fused RMSNorm/quantize prologue does not materialize its INT8
+// row, so it is recomputed by the row kernel with the identical rule).
+struct DebugCap {
+  tl_debug_record* h = nullptr;
+  int layer = 0, slot = 0, pos = 0;
+  float* f32 = nullptr;     // [max(D, F)] scratch
+  int8_t* i8 = nullptr;     // [max(D, F)]
+  float* am = nullptr;      // [5] input absmax: qkv, o, gate/up, down, LM head
+  float* sc = nullptr;      // [H][pos + 1]
+  float* pr = nullptr;
+};
+
+// Layer l of the per-kernel decode step for rows 0..M-1 (M < kTcMinRows, or
+// teacher-forced logits): dp4a GEMVs with the RMSNorm/quantize prologue and
+// the dequant / residual / SiLU*up epilogues, decode attention in between.
+tl_status enqueue_decode_layer_gemv(tl_engine* e, int l, int M, DebugCap* dbg) {
+  DecodeBufs& d = e->dec;
+  cudaStream_t s = e->stream;
+  const bool pdl = e->use_pdl && !dbg;
+  const Layer& ly = e->layers[l];
+  const float eps = e->cfg.rms_norm_eps;
+  tl_debug_record* h = dbg && dbg->layer == l ? dbg->h : nullptr;
+  if (h) {
+    TL_TRY(d2h(e, h->layer_input, d.x, e->D * sizeof(float)));
+    TL_CU(launch_norm_quant_rows(d.x, ly.g1, eps, 1, e->D, dbg->i8, dbg->am, s, false));
+    TL_TRY(d2h(e, h->qkv_input_q, dbg->i8, e->D));
+  }
+  GemvArgs q;
+  q.x_f32 = d.x; q.gamma = ly.g1; q.eps = eps;
+  q.w = ly.wqkv; q.w_scale = ly.sqkv; q.M = M; q.N = e->Nqkv; q.K = e->D; q.out_f32 = d.qkv;
+  TL_CU(launch_gemv(PRO_NORM, EPI_F32, q, s, pdl));
+  if (h) {
+    TL_TRY(d2h(e, h->q_proj, d.qkv, e->Dq * sizeof(float)));
+    TL_TRY(d2h(e, h->k_proj, d.qkv + e->Dq, e->Dkv * sizeof(float)));
+    TL_TRY(d2h(e, h->v_proj, d.qkv + e->Dq + e->Dkv, e->Dkv * sizeof(float)));
+  }
+  AttnDecodeArgs at;
+  at.qkv = d.qkv; at.ld = e->Nqkv; at.pos = d.pos; at.slot = d.slots; at.active = d.active;
+  at.kc = e->kc; at.vc = e->vc; at.ks = e->ks; at.vs = e->vs;
+  at.layer = l; at.L = e->L; at.H = e->H; at.Hkv = e->Hkv; at.P = e->P; at.M = M;
+  at.cos = e->cosT; at.sin = e->sinT; at.out = d.att;
+  at.part = d.attn_part; at.counters = d.attn_cnt;
+  TL_CU(launch_attn_decode(at, s, pdl));
+  if (h) {
+    const size_t base = (static_cast<size_t>(dbg->slot) * e->L + l) * e->Hkv;
+    const size_t row = static_cast<size_t>(dbg->pos) * 64;
+    if (h->k_row)
+      TL_CU(cudaMemcpy2DAsync(h->k_row, 64, e->kc + base * e->P * 64 + row, static_cast<size_t>(e->P) * 64, 64,
+                              e->Hkv, cudaMemcpyDeviceToHost, s));
+    if (h->v_row)
+      TL_CU(cudaMemcpy2DAsync(h->v_row, 64, e->vc + base * e->P * 64 + row, static_cast<size_t>(e->P) * 64, 64,
+                              e->Hkv, cudaMemcpyDeviceToHost, s));
+    TL_TRY(d2h(e, h->k_scale, e->ks + base, e->Hkv * sizeof(float)));
+    TL_TRY(d2h(e, h->v_scale, e->vs + base, e->Hkv * sizeof(float)));
+    if (h->scores || h->probs) {
+      TL_CU(launch_attn_scores_debug(d.qkv, e->Nqkv, 1, dbg->pos + 1, dbg->pos, true, e->H, e->Hkv, e->kc, e->ks,
+                                     e->cosT, e->sinT, dbg->slot, l, e->L, e->P, dbg->sc, dbg->pr, s));
+      const size_t wb = static_cast<size_t>(e->H) * (dbg->pos + 1) * sizeof(float);
+      TL_TRY(d2h(e, h->scores, dbg->sc, wb));
+      TL_TRY(d2h(e, h->probs, dbg->pr, wb));
+    }
+    TL_TRY(d2h(e, h->attended, d.att, e->Dq * sizeof(float)));
+    TL_CU(launch_absmax_rows(d.att, 1, e->Dq, 1, dbg->am + 1, s));
+  }
+  GemvArgs o;
+  o.x_f32 = d.att; o.w = ly.wo; o.w_scale = ly.so; o.M = M; o.N = e->D; o.K = e->Dq;
+  o.out_f32 = d.x; o.resid = d.x;
+  TL_CU(launch_gemv(PRO_F32, EPI_RESID, o, s, pdl));
+  if (h) TL_CU(launch_norm_quant_rows(d.x, ly.g2, eps, 1, e->D, dbg->i8, dbg->am + 2, s, false));
+  GemvArgs gu;
+  gu.x_f32 = d.x; gu.gamma = ly.g2; gu.eps = eps;
+  gu.w = ly.wgu; gu.w_scale = ly.sgu; gu.M = M; gu.N = 2 * e->F; gu.K = e->D; gu.out_f32 = d.hid;
+  TL_CU(launch_gemv(PRO_NORM, EPI_SILU, gu, s, pdl));
+  if (h) TL_CU(launch_absmax_rows(d.hid, 1, e->F, 1, dbg->am + 3, s));
+  GemvArgs dn;
+  dn.x_f32 = d.hid; dn.w = ly.wd; dn.w_scale = ly.sd; dn.M = M; dn.N = e->D; dn.K = e->F;
+  dn.out_f32 = d.x; dn.resid = d.x;
+  TL_CU(launch_gemv(PRO_F32, EPI_RESID, dn, s, pdl));
+  if (h) TL_TRY(d2h(e, h->layer_output, d.x, e->D * sizeof(float)));
+  return TL_OK;
+}
+
+tl_status enqueue_decode_step(tl_engine* e, int M, float* logits, bool finalize, DebugCap* dbg = nullptr) {
   if (M >= kTcMinRows && !logits) return enqueue_decode_step_tc(e, M, finalize);
   if (M == 1 && !logits && e->use_decode1) return enqueue_decode_step_d1(e, finalize);
   DecodeBufs& d = e->dec;
   cudaStream_t s = e->stream;
-  const bool pdl = e->use_pdl;
+  const bool pdl = e->use_pdl && !dbg;
   TL_CU(launch_embed(e->embed, d.tokens, d.x, M, e->D, e->V, s, pdl));
-  for (int l = 0; l < e->L; ++l) {
-    const Layer& ly = e->layers[l];
-    GemvArgs q;
-    q.x_f32 = d.x; q.gamma = ly.g1; q.eps = e->cfg.rms_norm_eps;
-    q.w = ly.wqkv; q.w_scale = ly.sqkv; q.M = M; q.N = e->Nqkv; q.K = e->D; q.out_f32 = d.qkv;
-    TL_CU(launch_gemv(PRO_NORM, EPI_F32, q, s, pdl));
-
-    AttnDecodeArgs at;
-    at.qkv = d.qkv; at.ld = e->Nqkv; at.pos = d.pos; at.slot = d.slots; at.active = d.active;
-    at.kc = e->kc; at.vc = e->vc; at.ks = e->ks; at.vs = e->vs;
-    at.layer = l; at.L = e->L; at.H = e->H; at.Hkv = e->Hkv; at.P = e->P; at.M = M;
-    at.cos = e->cosT; at.sin = e->sinT; at.out = d.att;
-    at.part = d.attn_part; at.counters = d.attn_cnt;
-    TL_CU(launch_attn_decode(at, s, pdl));
-
-    GemvArgs o;
-    o.x_f32 = d.att; o.w = ly.wo; o.w_scale = ly.so; o.M = M; o.N = e->D; o.K = e->Dq;
-    o.out_f32 = d.x; o.resid = d.x;
-    TL_CU(launch_gemv(PRO_F32, EPI_RESID, o, s, pdl));
-
-    GemvArgs gu;
-    gu.x_f32 = d.x; gu.gamma = ly.g2; gu.eps = e->cfg.rms_norm_eps;
-    gu.w = ly.wgu; gu.w_scale = ly.sgu; gu.M = M; gu.N = 2 * e->F; gu.K = e->D; gu.out_f32 = d.hid;
-    TL_CU(launch_gemv(PRO_NORM, EPI_SILU, gu, s, pdl));
-
-    GemvArgs dn;
-    dn.x_f32 = d.hid; dn.w = ly.wd; dn.w_scale = ly.sd; dn.M = M; dn.N = e->D; dn.K = e->F;
-    dn.out_f32 = d.x; dn.resid = d.x;
-    TL_CU(launch_gemv(PRO_F32, EPI_RESID, dn, s, pdl));
+  for (int l = 0; l < e->L; ++l) TL_TRY(enqueue_decode_layer_gemv(e, l, M, dbg));
+  if (dbg) {
+    TL_CU(launch_rmsnorm_rows(d.x, e->gfinal, e->cfg.rms_norm_eps, dbg->f32, dbg->am + 4, 1, e->D, 1, s));
+    TL_TRY(d2h(e, dbg->h->final_hidden, dbg->f32, e->D * sizeof(float)));
   }
   GemvArgs lm;
   lm.x_f32 = d.x; lm.gamma = e->gfinal; lm.eps = e->cfg.rms_norm_eps;
@@ -726,8 +786,8 @@ tl_status enqueue_prefill_layer(tl_engine* e, int l, int n_seq, int S, int slot_
   TL_CU(launch_kv_write_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->cosT, e->sinT, kva, e->kc, e->vc, e->ks,
                                 e->vs, slot_base, l, e->L, e->P, s));
   if (cap && cap->scores) {
-    TL_CU(launch_attn_scores_debug(p.qkv, e->Nqkv, S, e->H, e->Hkv, e->kc, e->ks, slot_base, l, e->L, e->P,
-                                   cap->scores, cap->probs, s));
+    TL_CU(launch_attn_scores_debug(p.qkv, e->Nqkv, S, S, 0, false, e->H, e->Hkv, e->kc, e->ks, e->cosT, e->sinT,
+                                   slot_base, l, e->L, e->P, cap->scores, cap->probs, s));
     const size_t sb = static_cast<size_t>(e->H) * S * S * sizeof(float);
     TL_TRY(d2h(e, hc->scores, cap->scores, sb));
     TL_TRY(d2h(e, hc->probs, cap->probs, sb));
@@ -1597,6 +1657,72 @@ tl_status tl_decode_logits(tl_engine* e, uint32_t slot, uint32_t token, float* l
   TL_TRY(st);
   TL_CU(cudaMemcpyAsync(logits_out, d.logits, e->V * sizeof(float), cudaMemcpyDeviceToHost, e->stream));
   TL_CU(cudaStreamSynchronize(e->stream));
+  e->slot_pos[slot] = pos + 1;
+  e->slot_pending[slot] = -1;
+  return TL_OK;
+}
+
+tl_status tl_decode_debug(tl_engine* e, uint32_t slot, uint32_t token, uint32_t layer, tl_debug_record* rec,
+                          float* logits_out) {
+  if (e && e->tp_world > 1) return TL_ERR_UNIMPLEMENTED;
+  if (!e || !rec) return TL_ERR_INVALID_ARGUMENT;
+  if (!e->loaded) return TL_ERR_NOT_LOADED;
+  if (slot >= static_cast<uint32_t>(e->B) || layer >= static_cast<uint32_t>(e->L)) return TL_ERR_OUT_OF_RANGE;
+  TL_CU(cudaSetDevice(e->device));
+  const int pos = e->slot_pos[slot];
+  if (pos >= e->P) return TL_ERR_OUT_OF_RANGE;
+  if (!e->dec.logits) TL_TRY(dmalloc(&e->dec.logits, static_cast<size_t>(e->B) * e->V));
+  TL_TRY(ensure_pinned(e, 8));
+  DebugCap dc;
+  dc.h = rec;
+  dc.layer = static_cast<int>(layer);
+  dc.slot = static_cast<int>(slot);
+  dc.pos = pos;
+  DecodeBufs& d = e->dec;
+  cudaStream_t s = e->stream;
+  auto body = [&]() -> tl_status {
+    TL_TRY(dmalloc(&dc.f32, std::max(e->D, e->F)));
+    TL_TRY(dmalloc(&dc.i8, std::max(e->D, e->F)));
+    TL_TRY(dmalloc(&dc.am, 5));
+    TL_TRY(dmalloc(&dc.sc, static_cast<size_t>(e->H) * (pos + 1)));
+    TL_TRY(dmalloc(&dc.pr, static_cast<size_t>(e->H) * (pos + 1)));
+    TL_CU(cudaMemsetAsync(dc.am, 0, 5 * sizeof(float), s));
+    int* h = e->h_pinned;
+    h[0] = static_cast<int>(token); h[1] = pos; h[2] = 1; h[3] = static_cast<int>(slot);
+    TL_CU(cudaMemcpyAsync(d.tokens, h, sizeof(int), cudaMemcpyHostToDevice, s));
+    TL_CU(cudaMemcpyAsync(d.pos, h + 1, sizeof(int), cudaMemcpyHostToDevice, s));
+    TL_CU(cudaMemcpyAsync(d.active, h + 2, sizeof(int), cudaMemcpyHostToDevice, s));
+    TL_CU(cudaMemcpyAsync(d.slots, h + 3, sizeof(int), cudaMemcpyHostToDevice, s));
+    TL_TRY(enqueue_decode_step(e, 1, d.logits, false, &dc));
+    TL_TRY(d2h(e, rec->input_absmax, dc.am, 5 * sizeof(float)));
+    std::vector<float> lg(e->V);
+    TL_CU(cudaMemcpyAsync(lg.data(), d.logits, e->V * sizeof(float), cudaMemcpyDeviceToHost, s));
+    int32_t tok = 0;
+    TL_CU(cudaMemcpyAsync(&tok, d.argmax, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    TL_CU(cudaStreamSynchronize(s));
+    TL_TRY(tl_device_error());
+    // top-16 slice: highest logit first, lower id first on equal logits
+    std::vector<int> ids(e->V);
+    for (int i = 0; i < e->V; ++i) ids[i] = i;
+    const int k = std::min(16, e->V);
+    std::partial_sort(ids.begin(), ids.begin() + k, ids.end(),
+                      [&](int a, int b) { return lg[a] > lg[b] || (lg[a] == lg[b] && a < b); });
+    for (int i = 0; i < 16; ++i) {
+      rec->top_ids[i] = i < k ? static_cast<uint32_t>(ids[i]) : 0u;
+      rec->top_logits[i] = i < k ? lg[ids[i]] : 0.0f;
+    }
+    rec->position = static_cast<uint32_t>(pos);
+    rec->chosen_token = static_cast<uint32_t>(tok);
+    if (logits_out) std::memcpy(logits_out, lg.data(), lg.size() * sizeof(float));
+    return TL_OK;
+  };
+  const tl_status st = body();
+  int* h = e->h_pinned;
+  h[4] = 0;
+  cudaMemcpyAsync(d.slots, h + 4, sizeof(int), cudaMemcpyHostToDevice, s);
+  cudaStreamSynchronize(s);
+  cudaFree(dc.f32); cudaFree(dc.i8); cudaFree(dc.am); cudaFree(dc.sc); cudaFree(dc.pr);
+  if (st != TL_OK) return st;
   e->slot_pos[slot] = pos + 1;
   e->slot_pending[slot] = -1;
   return TL_OK;

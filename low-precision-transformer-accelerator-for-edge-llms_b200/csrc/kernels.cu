@@ -908,30 +908,50 @@ cudaError_t launch_quantize_rows(const float* x, const float* absmax_groups, int
 }
 
 // Debug capture of one sequence's attention (not on the generation path):
+// query row i (position pos0 + i) against keys 0..n_keys-1 of the cache:
 // scores[h][i][j] = (q_i . K_j) * 1/8 with K_j the dequantized cache row
 // float32(k_q) * float32(s_K) (model/tinyllama_gemm_int8.py:156-159), -1e9
-// where j > i (the causal fill of :159), and probs = the max-shifted softmax
-// of each row (model/tinyllama.py:100-103). q comes from the rotated qkv rows.
-// Products are summed in double, so these match the reference's float64
-// scores to well below float32 resolution. One CTA per (query row, head).
-__global__ void __launch_bounds__(256) attn_scores_debug_kernel(const float* qkv, int ld, int S, int H, int Hkv,
-                                                                const int8_t* kc, const float* ks, int slot, int layer,
-                                                                int L, int P, float* scores, float* probs) {
+// where j > pos0 + i (the causal fill of :159), and probs = the max-shifted
+// softmax of each row (model/tinyllama.py:100-103). With `rotate` the q rows
+// are pre-RoPE (decode) and are rotated here at their position with the
+// same float32 roundings as the attention kernels; otherwise they already
+// are (prefill). Products are summed in double, so these match the
+// reference's float64 scores to well below float32 resolution. One CTA per
+// (query row, head).
+__global__ void __launch_bounds__(256) attn_scores_debug_kernel(const float* qkv, int ld, int n_keys, int pos0,
+                                                                int rotate, int H, int Hkv, const int8_t* kc,
+                                                                const float* ks, const float* cosT, const float* sinT,
+                                                                int slot, int layer, int L, int P, float* scores,
+                                                                float* probs) {
   __shared__ double red[8];
   __shared__ float q[64];
-  const int i = blockIdx.x, h = blockIdx.y, t = threadIdx.x;
+  const int i = blockIdx.x, h = blockIdx.y, t = threadIdx.x, n_q = gridDim.x;
   const int kvh = h / (H / Hkv);
-  if (t < 64) q[t] = qkv[static_cast<size_t>(i) * ld + h * 64 + t];
+  const int pos = pos0 + i;
+  if (t < 32) {
+    const float* qr = qkv + static_cast<size_t>(i) * ld + h * 64;
+    float a = qr[t], b = qr[t + 32];
+    if (rotate) {
+      const float* cs = cosT + static_cast<size_t>(pos) * 64;
+      const float* sn = sinT + static_cast<size_t>(pos) * 64;
+      const float r0 = __fadd_rn(__fmul_rn(a, cs[t]), __fmul_rn(-b, sn[t]));
+      const float r1 = __fadd_rn(__fmul_rn(b, cs[t + 32]), __fmul_rn(a, sn[t + 32]));
+      a = r0;
+      b = r1;
+    }
+    q[t] = a;
+    q[t + 32] = b;
+  }
   __syncthreads();
   const size_t base = ((static_cast<size_t>(slot) * L + layer) * Hkv + kvh);
   const int8_t* krows = kc + base * P * 64;
   const float sk = ks[base];
-  float* srow = scores + (static_cast<size_t>(h) * S + i) * S;
-  float* prow = probs + (static_cast<size_t>(h) * S + i) * S;
+  float* srow = scores + (static_cast<size_t>(h) * n_q + i) * n_keys;
+  float* prow = probs + (static_cast<size_t>(h) * n_q + i) * n_keys;
   double m = -1e300;
-  for (int j = t; j < S; j += blockDim.x) {
+  for (int j = t; j < n_keys; j += blockDim.x) {
     double sc = -1e9;
-    if (j <= i) {
+    if (j <= pos) {
       double acc = 0.0;
       for (int d = 0; d < 64; ++d)
         acc += static_cast<double>(q[d]) * static_cast<double>(__fmul_rn(static_cast<float>(krows[j * 64 + d]), sk));
@@ -947,19 +967,22 @@ __global__ void __launch_bounds__(256) attn_scores_debug_kernel(const float* qkv
   for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) m = fmax(m, red[w]);
   __syncthreads();
   double sum = 0.0;
-  for (int j = t; j < S; j += blockDim.x) sum += exp(static_cast<double>(srow[j]) - m);
+  for (int j = t; j < n_keys; j += blockDim.x) sum += exp(static_cast<double>(srow[j]) - m);
   for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   if ((t & 31) == 0) red[t >> 5] = sum;
   __syncthreads();
   sum = 0.0;
   for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) sum += red[w];
-  for (int j = t; j < S; j += blockDim.x) prow[j] = static_cast<float>(exp(static_cast<double>(srow[j]) - m) / sum);
+  for (int j = t; j < n_keys; j += blockDim.x) prow[j] = static_cast<float>(exp(static_cast<double>(srow[j]) - m) / sum);
 }
 
-cudaError_t launch_attn_scores_debug(const float* qkv, int ld, int S, int H, int Hkv, const int8_t* kc, const float* ks,
+cudaError_t launch_attn_scores_debug(const float* qkv, int ld, int n_q, int n_keys, int pos0, bool rotate, int H,
+                                     int Hkv, const int8_t* kc, const float* ks, const float* cosT, const float* sinT,
                                      int slot, int layer, int L, int P, float* scores, float* probs, cudaStream_t s) {
-  if (S <= 0 || H <= 0 || Hkv <= 0 || H % Hkv) return cudaErrorInvalidValue;
-  attn_scores_debug_kernel<<<dim3(S, H), 256, 0, s>>>(qkv, ld, S, H, Hkv, kc, ks, slot, layer, L, P, scores, probs);
+  if (n_q <= 0 || n_keys <= 0 || H <= 0 || Hkv <= 0 || H % Hkv || pos0 < 0 || pos0 + n_q > P || n_keys > P)
+    return cudaErrorInvalidValue;
+  attn_scores_debug_kernel<<<dim3(n_q, H), 256, 0, s>>>(qkv, ld, n_keys, pos0, rotate ? 1 : 0, H, Hkv, kc, ks, cosT,
+                                                        sinT, slot, layer, L, P, scores, probs);
   return cudaGetLastError();
 }
 

@@ -215,9 +215,11 @@ cudaError_t launch_attn_prefill(const float* qkv, int ld, int rows, int seq_len,
                                 const float* vs, int slot_base, int layer, int L, int P,
                                 float* out, float* out_absmax, cudaStream_t s);
 
-// Debug capture: scores / probabilities [H][S][S] of one prefilled sequence
-// (rotated q in qkv, K from cache slot `slot`), see kernels.cu.
-cudaError_t launch_attn_scores_debug(const float* qkv, int ld, int S, int H, int Hkv, const int8_t* kc, const float* ks,
+// Debug capture: scores / probabilities [H][n_q][n_keys] of query rows at
+// positions pos0.. of one sequence against its cache (slot `slot`); q rows in
+// qkv, already rotated unless `rotate`. See kernels.cu.
+cudaError_t launch_attn_scores_debug(const float* qkv, int ld, int n_q, int n_keys, int pos0, bool rotate, int H,
+                                     int Hkv, const int8_t* kc, const float* ks, const float* cosT, const float* sinT,
                                      int slot, int layer, int L, int P, float* scores, float* probs, cudaStream_t s);
 
 // ---- per-row (one sequence per row) activation prep for the batched path

@@ -55,7 +55,7 @@ EXPORTS = (
     "tl_transpose_i8", "tl_quantize_int8",
     "tl_gemm_i8", "tl_gemm_i8_requant", "tl_quantized_linear", "tl_rmsnorm", "tl_lmhead_argmax",
     "tl_attn_decode", "tl_attn_prefill", "tl_lmhead_argmax_noalloc",
-    "tl_forward_logits", "tl_decoder_layer", "tl_decode_layer",
+    "tl_forward_logits", "tl_decoder_layer", "tl_decode_layer", "tl_decode_debug",
 )
 
 
@@ -119,6 +119,23 @@ class LayerCapture(C.Structure):
     _fields_ = [(name, C.c_void_p) for name, _, _ in CAPTURE_FIELDS]
 
 
+# tl_debug_record pointer fields: (name, dtype, shape key); D hidden, Dq, Dkv,
+# Hkv64 [kv_heads, 64], Hkv [kv_heads], Hn [heads, position + 1].
+DEBUG_FIELDS = (
+    ("layer_input", np.float32, "D"), ("qkv_input_q", np.int8, "D"), ("q_proj", np.float32, "Dq"),
+    ("k_proj", np.float32, "Dkv"), ("v_proj", np.float32, "Dkv"), ("scores", np.float32, "Hn"),
+    ("probs", np.float32, "Hn"), ("k_row", np.int8, "Hkv64"), ("v_row", np.int8, "Hkv64"),
+    ("k_scale", np.float32, "Hkv"), ("v_scale", np.float32, "Hkv"), ("attended", np.float32, "Dq"),
+    ("layer_output", np.float32, "D"), ("final_hidden", np.float32, "D"),
+)
+
+
+class DebugRecord(C.Structure):
+    _fields_ = [("position", C.c_uint32), ("chosen_token", C.c_uint32), ("top_ids", C.c_uint32 * 16),
+                ("top_logits", C.c_float * 16), ("input_absmax", C.c_float * 5)] + \
+               [(name, C.c_void_p) for name, _, _ in DEBUG_FIELDS]
+
+
 _LIB = None
 
 
@@ -171,6 +188,7 @@ def load_library(path: Path | str | None = None):
         "tl_forward_logits": (i32, [vp, vp, u32, vp, vp]),
         "tl_decoder_layer": (i32, [vp, u32, u32, vp, u32, vp, C.POINTER(LayerCapture)]),
         "tl_decode_layer": (i32, [vp, u32, u32, vp, vp, vp, vp, C.POINTER(LayerCapture)]),
+        "tl_decode_debug": (i32, [vp, u32, u32, u32, C.POINTER(DebugRecord), vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -578,6 +596,31 @@ class Engine:
         out = np.zeros_like(xf)
         check(self.lib.tl_decoder_layer(self.h, slot, layer, _ptr(xf), S, _ptr(out), ref), "tl_decoder_layer")
         return out, arrays
+
+    def decode_debug(self, token: int, layer: int, slot: int = 0, logits: bool = False) -> dict:
+        """One decode step of ``slot`` fed ``token`` with the debug capture of
+        layer ``layer`` (tl_decode_debug, the hardware's debug contract,
+        docs/design_decisions.txt B8): a dict of every record field (arrays as
+        numpy), plus ``logits`` [vocab] when asked."""
+        c = self.cfg
+        pos = self.position(slot)
+        hkv = c["num_key_value_heads"]
+        shapes = {"D": (c["hidden_size"],), "Dq": (c["num_attention_heads"] * c["head_dim"],),
+                  "Dkv": (hkv * c["head_dim"],), "Hn": (c["num_attention_heads"], pos + 1),
+                  "Hkv64": (hkv, 64), "Hkv": (hkv,)}
+        rec, out = DebugRecord(), {}
+        for name, dt, key in DEBUG_FIELDS:
+            out[name] = np.zeros(shapes[key], dtype=dt)
+            setattr(rec, name, _ptr(out[name]))
+        lg = np.zeros(c["vocab_size"], np.float32) if logits else None
+        check(self.lib.tl_decode_debug(self.h, slot, int(token), layer, C.byref(rec),
+                                       _ptr(lg) if lg is not None else None), "tl_decode_debug")
+        out.update(position=rec.position, chosen_token=rec.chosen_token,
+                   top_ids=np.array(rec.top_ids[:], np.int64), top_logits=np.array(rec.top_logits[:], np.float32),
+                   input_absmax=np.array(rec.input_absmax[:], np.float32))
+        if lg is not None:
+            out["logits"] = lg
+        return out
 
     def decode_logits(self, token: int, slot: int = 0) -> np.ndarray:
         out = np.zeros(self.cfg["vocab_size"], dtype=np.float32)

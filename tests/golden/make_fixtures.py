@@ -205,12 +205,44 @@ def make_contract(exporter, bridge):
     np.savez_compressed(HERE / "contract.npz", **out)
 
 
+def make_analysis(bridge, tmpdir: str):
+    """The reference's own accuracy report (run_analysis with --dump-layer,
+    model/tinyllama_gemm_int8.py:470-626) on a seeded 2-layer scaled model
+    and 11 token ids: its debug_arrays.npz (every array, under the
+    reference's flatten_named_arrays keys) and summary lines."""
+    import contextlib
+    import io
+    seed, layers = 31, 2
+    arc = W.random_archive(seed, layers, W.small_dims(), gamma_one=False)
+    path = save_archive(arc, tmpdir, "analysis.npz")
+    ids = [int(t) for t in np.random.default_rng(32).integers(0, 512, 11)]
+    dump = os.path.join(tmpdir, "analysis_dump")
+    with contextlib.redirect_stdout(io.StringIO()):
+        bridge.run_analysis(prompt=None, token_ids_arg=",".join(map(str, ids)), weights_path=path,
+                            layer_count=layers, dump_layer=0, dump_dir=dump, local_files_only=True, top_k=5,
+                            quantize_lm_head=True, cache_arrays=True)
+    with np.load(os.path.join(dump, "debug_arrays.npz")) as d:
+        # the weight copies (weight_fp / weight_q) follow from the seed; keep
+        # their names and shapes only
+        keys = sorted(d.files)
+        out = {f"dump__{k}": d[k] for k in keys if not k.endswith(("weight_fp", "weight_q"))}
+        out["dump_keys"] = np.array(keys)
+        out["dump_shapes"] = np.array([",".join(map(str, d[k].shape)) for k in keys])
+    summary = open(os.path.join(dump, "summary.txt"), encoding="utf-8").read().splitlines()
+    out.update(seed=np.int64(seed), layers=np.int64(layers), token_ids=np.array(ids, np.int64),
+               summary=np.array(summary))
+    np.savez_compressed(HERE / "analysis.npz", **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("TL_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("TL_REFERENCE_ROOT"),
+                    help="reference checkout (default: $TL_REFERENCE_ROOT)")
     ap.add_argument("--skip-config0", action="store_true")
     ap.add_argument("--config0-steps", type=int, default=3)
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set TL_REFERENCE_ROOT to the reference checkout")
     ref_root = Path(args.reference)
     ref, bridge, exporter = load_reference(ref_root)
     bridge.ref = ref
@@ -219,6 +251,7 @@ def main():
     make_contract(exporter, bridge)
     with tempfile.TemporaryDirectory() as tmp:
         make_small_model(ref, bridge, tmp)
+        make_analysis(bridge, tmp)
         if not args.skip_config0:
             make_config0(ref, bridge, tmp, args.config0_steps)
     print("fixtures written to", HERE)

@@ -185,3 +185,24 @@ def test_stop_priority_and_addresses():
     assert C.stop_decision(False, True, 5, 3, 0, 2) == (False, 0)
     assert C.kv_row_address(0x1000, 1, 2, 3) == 0x1000 + (((1 * 4 + 2) * 2048 + 3) << 6)
     assert C.status_word(False, True, False, True, 1, 0) == 0b1_1010
+
+
+def test_analysis_fixture_float_and_int8_layers(golden):
+    """The reference's run_analysis dump (tests/golden/analysis.npz, made by
+    the reference itself): the oracle's float32 layer and INT8 golden layer
+    reproduce its layer-0 arrays bit for bit, and its reported layer-0 MAE."""
+    from oracle import weights as W
+    d = golden["analysis"]
+    arc = W.random_archive(int(d["seed"]), int(d["layers"]), W.small_dims(), gamma_one=False)
+    w = W.ArchiveWeights(arc)
+    cfg = w.cfg
+    ids = [int(t) for t in d["token_ids"]]
+    cos, sin = G.build_rope_cache(cfg["max_position_embeddings"], cfg["head_dim"], cfg["rope_theta"])
+    x = w.embed(ids).astype(np.float32)
+    ref_out = G.reference_decoder_layer(x, w.layer(0), cfg, cos, sin)
+    np.testing.assert_array_equal(ref_out, d["dump__reference_layer_out_fp"])
+    qm = W.quantize_archive(arc, "tensor")
+    mix_out = G.decoder_layer_mixed(x, qm.layers[0], cfg, cos, sin)
+    np.testing.assert_array_equal(mix_out, d["dump__mixed_layer_out_fp"])
+    mae = float(np.abs(mix_out - ref_out).mean())
+    assert f"isolated MAE={mae:.6f}" in str(d["summary"][3])
