@@ -11,10 +11,18 @@ Sequences are independent, so N GPUs run N x 64 sequences with no collective:
 weak scaling.
 
 Also reported (rank 0 at N=1): bs1 decode (configs[2]: 128-token prompt, 256
-decode tokens), prefill of 8 x 2048 tokens (configs[4], 1 GPU), per-kernel
-device times with the HBM roofline of the dominant kernel, the end-to-end
-C-ABI number (host prompts in, host token ids out), and the CPU baseline (the
-oracle port of the reference's INT8 golden model on one host core).
+decode tokens), prefill of 8 x 2048 tokens (configs[4], 1 GPU, median of 5),
+per-kernel device times with the HBM roofline of the dominant kernel (its
+DRAM traffic read from the committed ncu summary), the configs[1] GEMM sweep
+(32 shapes, each against its HBM or INT8 tensor roofline), configs[0] on the
+GPU and the reference golden model's own configs[0] prefill timed on one
+host core, the end-to-end C-ABI number (host prompts in, host token ids
+out), and the CPU baseline (one step of the --impl reference arm: every host
+core decodes one token). At N = 2 and 4: the tensor-parallel prefill with
+both exchanges (row-split O/down + NCCL INT32 all-reduce, or replicated O/down
++ INT8 all-gather) and their bit identity with one GPU; at N > 1 the fixed
+64-sequence job split over the GPUs (strong scaling) beside the weak-scaling
+value.
 
 ``--impl reference`` times the reference's own CPU implementation of the path
 (the oracle port of model/tinyllama_gemm_int8.py, KV-cached) on all host cores.
@@ -45,8 +53,9 @@ TINYLLAMA = dict(hidden_size=2048, intermediate_size=5632, num_hidden_layers=22,
                  num_key_value_heads=4, head_dim=64, vocab_size=32000, max_position_embeddings=2048,
                  rms_norm_eps=1e-5, rope_theta=10000.0)
 FALLBACK_HBM_GBS = 6650.0
-# DRAM bytes (read + write) of one gate/up launch at 64 rows, measured by ncu
-GATE_UP_DRAM_BYTES = 23364864
+# ncu summary of the roofline kernel: its `traffic_bytes_per_launch:` line is
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch at 64 rows
+ROOFLINE_PROFILE = ROOT / "profiles" / "gemm_tc_kernel_decode64.md"
 METRIC = "decode tok/s @bs64 (TinyLlama-1.1B INT8, 22 layers, 512-token prompts, 512 greedy tokens)"
 
 
@@ -66,6 +75,17 @@ def load_pkg():
     sys.modules["lpta_b200"] = mod
     spec.loader.exec_module(mod)
     return mod
+
+
+def profile_traffic(path: Path):
+    """``traffic_bytes_per_launch: N`` from a committed ncu summary, or None."""
+    try:
+        for line in path.read_text().splitlines():
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":", 1)[1].strip().replace(",", ""))
+    except OSError:
+        pass
+    return None
 
 
 def peaks():
@@ -163,20 +183,8 @@ def oracle_decoder(qm, ctx: int, seed: int):
     return o
 
 
-def cpu_baseline_sample(tokens: int = 2, ctx: int = 768):
-    qm = random_qmodel(22, 5)
-    o = oracle_decoder(qm, ctx, 6)
-    t0 = time.perf_counter()
-    for i in range(tokens):
-        o.decode(100 + i)
-    dt = time.perf_counter() - t0
-    return {"value": tokens / dt, "unit": "tok/s", "cores": 1, "kind": "port",
-            "sample": f"{tokens} decode tokens of one sequence at context {ctx}, 22 layers, INT8 KV, "
-                      "reference INT32 NumPy matmul path (oracle/kv_golden.py); batching does not "
-                      "amortise the non-BLAS int32 matmul, so bs64 costs 64x per step"}
-
-
 _REF_QM = None
+REF_CTX = 768
 
 
 def _ref_worker(args):
@@ -187,26 +195,60 @@ def _ref_worker(args):
     return time.perf_counter() - t0
 
 
-def run_reference(a, rank, world):
-    if rank != 0:
-        return
+def reference_rate(steps: int, warmup: int):
+    """The reference's CPU algorithm on every host core: per step, one process
+    per core decodes one token of its own sequence at context REF_CTX (the
+    KV-cached oracle port of the reference INT8 golden model with its INT32
+    NumPy matmul). Forks its pool, so it must run before any CUDA call.
+    Returns (tok/s, seconds, cores)."""
     import multiprocessing as mp
     global _REF_QM
     cores = os.cpu_count() or 1
-    _REF_QM = random_qmodel(22, 5)   # shared copy-on-write by the forked workers (no GPU here)
-    ctx = 768
-    ctx_pool = mp.get_context("fork").Pool(cores)
+    _REF_QM = random_qmodel(22, 5)   # shared copy-on-write by the forked workers
+    pool = mp.get_context("fork").Pool(cores)
     try:
-        for _ in range(a.warmup):
-            ctx_pool.map(_ref_worker, [(i, ctx) for i in range(cores)])
+        for _ in range(warmup):
+            pool.map(_ref_worker, [(i, REF_CTX) for i in range(cores)])
         t0 = time.perf_counter()
-        for _ in range(a.steps):
-            ctx_pool.map(_ref_worker, [(i, ctx) for i in range(cores)])
+        for _ in range(steps):
+            pool.map(_ref_worker, [(i, REF_CTX) for i in range(cores)])
         dt = time.perf_counter() - t0
     finally:
-        ctx_pool.close()
-        ctx_pool.join()
-    value = cores * a.steps / dt
+        pool.close()
+        pool.join()
+    return cores * steps / dt, dt, cores
+
+
+def cpu_baseline_sample():
+    value, dt, cores = reference_rate(1, 0)
+    return {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"one step: {cores} processes each decode one token of their own sequence at context "
+                      f"{REF_CTX}, 22 layers, INT8 KV, oracle port of the reference INT8 golden model with its "
+                      "INT32 NumPy matmul (the --impl reference arm's method, one step)"}
+
+
+def cpu_golden_config0():
+    """configs[0] on the host: the reference golden model itself (forward_mixed
+    recompute, restated bit for bit in oracle/golden.py, with the reference's
+    INT32 NumPy matmul, one core) for the 32-token prefill of one full-size
+    layer with per-channel INT8 weights: seconds per forward and tok/s."""
+    from oracle import golden as G
+    from oracle import weights as W
+    qm = W.quantize_archive(W.random_archive(0, 1), "channel")
+    cos, sin = G.build_rope_cache(2048, 64, 10000.0)
+    ids = [int(t) for t in np.random.default_rng(1).integers(0, 32000, 32)]
+    t0 = time.perf_counter()
+    G.forward_mixed(ids, qm, cos, sin, matmul=G.int8_matmul_reference_path)
+    dt = time.perf_counter() - t0
+    return {"workload": "configs[0]: 1 layer, 32-token prefill (forward_mixed recompute), per-channel INT8",
+            "seconds": dt, "value": 32 / dt, "unit": "tok/s", "cores": 1, "kind": "port"}
+
+
+def run_reference(a, rank, world):
+    if rank != 0:
+        return
+    value, dt, cores = reference_rate(a.steps, a.warmup)
+    ctx = REF_CTX
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1000 * dt / a.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
@@ -221,40 +263,80 @@ def run_reference(a, rank, world):
 
 
 # ------------------------------------------------------------------ ours
+def _digest(*arrays) -> str:
+    import hashlib
+    h = hashlib.sha256()
+    for x in arrays:
+        h.update(np.ascontiguousarray(x).tobytes())
+    return h.hexdigest()[:16]
+
+
 def tp_prefill_bench(pkg, group, rank, world, local_rank):
     """configs[4] on `world` GPUs: one 8 x 2048-token prefill split by KV head
-    (tl_tp_create, NCCL INT32 all-reduces after O and down), CUDA events on
-    every rank, max over ranks. Random weights of the same seed on every rank
-    (each draws its slice of one model)."""
+    (tl_tp_create_ex), timed with CUDA events on every rank (median of 5
+    calls, max over ranks), for both exchanges: O and down row-split with an
+    NCCL INT32 all-reduce of the partial sums ("allreduce"), and O and down
+    replicated with their INT8 inputs all-gathered by NVLink peer stores
+    ("allgather"). Random weights of the same seed on every rank (each draws
+    its slice of one model). Bit identity: every rank prefills one 2048-token
+    prompt and reports digests of its logits and its kv heads' layer-21 INT8
+    cache bytes; rank 0 recomputes both on one GPU."""
     import torch
     import torch.distributed as dist
-    box = [pkg.tp_unique_id() if rank == 0 else None]
-    dist.broadcast_object_list(box, src=0)
-    eng = pkg.Engine(TINYLLAMA, max_batch=8, device=local_rank, max_prefill_tokens=8 * 2048,
-                     tp_rank=rank, tp_world=world, tp_id=box[0])
-    eng.init_random(1234)
     p8 = np.random.default_rng(7).integers(0, 32000, (8, 2048)).astype(np.uint32)
-    stream = torch.cuda.ExternalStream(eng.stream_handle())
-    eng.prefill_batch_device(p8)  # warm-up (same collective sequence on every rank)
-    eng.synchronize()
-    times = []
-    for _ in range(3):
-        group.barrier()
-        h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        h0.record(stream)
-        eng.prefill_batch_device(p8)
-        h1.record(stream)
-        h1.synchronize()
-        times.append(group.max(h0.elapsed_time(h1)))
-    eng.close()
-    ms = float(np.median(times))
-    return {"workload": "configs[4]: 8 x 2048-token prompts, 22 layers, tensor parallel by KV head",
-            "world": world, "value": 8 * 2048 / (ms / 1e3), "unit": "tok/s", "ms": ms,
-            "collectives": "per layer: 2 x all-reduce max (one float per sequence), then the INT8 O and down inputs all-gathered by peer stores over NVLink (quantize_scatter_kernel)"}
+    out = {"workload": "configs[4]: 8 x 2048-token prompts, 22 layers, tensor parallel by KV head",
+           "world": world, "unit": "tok/s", "per_exchange": {}}
+    digests = {}
+    for exchange in ("allreduce", "allgather"):
+        box = [pkg.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        eng = pkg.Engine(TINYLLAMA, max_batch=8, device=local_rank, max_prefill_tokens=8 * 2048,
+                         tp_rank=rank, tp_world=world, tp_id=box[0], tp_exchange=exchange)
+        eng.init_random(1234)
+        stream = torch.cuda.ExternalStream(eng.stream_handle())
+        eng.prefill_batch_device(p8)  # warm-up (same collective sequence on every rank)
+        eng.synchronize()
+        times = []
+        for _ in range(5):
+            group.barrier()
+            h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            h0.record(stream)
+            eng.prefill_batch_device(p8)
+            h1.record(stream)
+            h1.synchronize()
+            times.append(group.max(h0.elapsed_time(h1)))
+        logits = eng.prefill_logits(p8[0])
+        k21 = eng.read_kv(21, 2048)[0]
+        eng.close()
+        mine = (_digest(logits), _digest(k21))
+        every = [None] * world
+        dist.all_gather_object(every, mine)
+        digests[exchange] = every
+        ms = float(np.median(times))
+        out["per_exchange"][exchange] = {"ms": ms, "value": 8 * 2048 / (ms / 1e3)}
+    if rank == 0:
+        one = pkg.Engine(TINYLLAMA, max_batch=1, device=local_rank, max_prefill_tokens=2048)
+        one.init_random(1234)
+        logits = one.prefill_logits(p8[0])
+        k21 = one.read_kv(21, 2048)[0]
+        one.close()
+        hr = k21.shape[0] // world
+        want = [(_digest(logits), _digest(k21[r * hr:(r + 1) * hr])) for r in range(world)]
+        for exchange in digests:
+            out["per_exchange"][exchange]["bit_identical"] = digests[exchange] == want
+    best = min(out["per_exchange"], key=lambda k: out["per_exchange"][k]["ms"])
+    out.update(exchange=best, ms=out["per_exchange"][best]["ms"], value=out["per_exchange"][best]["value"],
+               bit_identical=all(v.get("bit_identical", False) for v in out["per_exchange"].values())
+               if rank == 0 else None)
+    return out
 
 
 def run_ours(a, rank, world, local_rank):
     import torch
+    extras = rank == 0 and world == 1 and not a.no_extras
+    # CPU legs first: their process pool forks, which must happen before CUDA
+    cpu = cpu_baseline_sample() if extras else None
+    golden0 = cpu_golden_config0() if extras else None
     torch.cuda.set_device(local_rank)
     pkg = load_pkg()
     from lpta_b200 import replicas
@@ -320,7 +402,9 @@ def run_ours(a, rank, world, local_rank):
             "gpu_launches": int((per_step_kernels * T + 1) * a.steps),
             "clocks": clk.summary()}
 
-    if rank == 0 and world == 1 and not a.no_extras:
+    if world > 1 and not a.no_extras:
+        line["strong_scaling"] = strong_scaling(eng, group, world, prompts, S, T, a.steps, stream, torch)
+    if extras:
         kern = eng.profile_decode_kernels(B, 44)
         names = ["qkv", "attn", "o", "gate_up", "down", "lm_head", "norm_quant_rows", "quant_rows"]
         D, F, V = 2048, 5632, 32000
@@ -331,9 +415,10 @@ def run_ours(a, rank, world, local_rank):
         achieved = bytes_gu / (gu_ms / 1e3) / 1e9
         line["roofline"] = {"bound": "hbm", "kernel": "tcgen05 gate/up GEMM + SiLU*up (M=64)", "achieved": achieved,
                             "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                            # dram__bytes_read.sum + dram__bytes_write.sum of this launch from
-                            # the ncu capture in profiles/gemm_tc_kernel_decode64.md
-                            "traffic": GATE_UP_DRAM_BYTES,
+                            # dram__bytes_read.sum + dram__bytes_write.sum of one launch,
+                            # from the ncu capture summarised in ROOFLINE_PROFILE
+                            "traffic": profile_traffic(ROOFLINE_PROFILE),
+                            "traffic_source": str(ROOFLINE_PROFILE.relative_to(ROOT)),
                             "peak_kind": peak_kind,
                             "algorithmic_bytes": bytes_gu}
         line["kernels_ms"] = {n: float(v) for n, v in zip(names, kern)}
@@ -361,26 +446,136 @@ def run_ours(a, rank, world, local_rank):
         p8 = rng.integers(0, 32000, (8, 2048)).astype(np.uint32)
         eng.prefill_batch_device(p8)
         eng.synchronize()
-        h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        h0.record(stream)
-        eng.prefill_batch_device(p8)
-        h1.record(stream)
-        h1.synchronize()
-        pf_ms = h0.elapsed_time(h1)
+        pf_times = []
+        for _ in range(5):
+            h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            h0.record(stream)
+            eng.prefill_batch_device(p8)
+            h1.record(stream)
+            h1.synchronize()
+            pf_times.append(h0.elapsed_time(h1))
+        pf_ms = float(np.median(pf_times))
         line["prefill"] = {"workload": "configs[4]: 8 x 2048-token prompts, 22 layers, 1 GPU",
-                           "value": 8 * 2048 / (pf_ms / 1e3), "unit": "tok/s", "ms": pf_ms}
+                           "value": 8 * 2048 / (pf_ms / 1e3), "unit": "tok/s", "ms": pf_ms,
+                           "timing": "median of 5 calls, CUDA events on the engine stream"}
         i8 = int8_gemm_rate(pkg, torch)
         # prefill ops (config 4): linear 3.175e13 + causal attention 3.025e12 + LM head 1.05e9
         pf_ops = 3.175e13 + 3.025e12 + 1.05e9
         line["prefill"]["tensor_frac_of_cublaslt_int8"] = pf_ops / (pf_ms / 1e3) / 1e12 / i8["cublaslt_tops"]
         line["int8_gemm"] = i8
-        line["cpu_baseline"] = cpu_baseline_sample()
+        line["gemm_sweep"] = gemm_sweep(pkg, torch, hbm, i8["cublaslt_tops"])
+        line["config0"] = config0_gpu(pkg, torch)
+        line["config0"]["cpu_golden"] = golden0
+        line["cpu_baseline"] = cpu
     eng.close()
     if world in (2, 4) and not a.no_extras:
         line["tp_prefill"] = tp_prefill_bench(pkg, group, rank, world, local_rank)
     group.close()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+# HBM roofline of the fixed 64-sequence job split over N GPUs (every GPU
+# streams all 1.0365 GB of weights per step, plus its sequences' KV reads at
+# the mean context 767.5: 11,264 B x 768.5 per sequence)
+def strong_roofline(world: int) -> float:
+    w, kv = 1036.5e6, 11264 * 768.5
+    return (w + 64 * kv) / (w + 64 * kv / world)
+
+
+def strong_scaling(eng, group, world, prompts, S, T, steps, stream, torch):
+    """The fixed configs[3] job (64 sequences) split over `world` GPUs:
+    64 / world sequences per GPU, same prompts / decode length, CUDA events,
+    max over ranks; reported beside the weak-scaling `value`."""
+    b = 64 // world
+    eng.prefill_batch_device(prompts[:b])
+    eng.synchronize()
+    for _ in range(2):
+        eng.decode_rewind(b, S)
+        eng.decode_steps_device(b, T)
+    eng.synchronize()
+    group.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        eng.decode_rewind(b, S)
+        eng.decode_steps_device(b, T)
+    e1.record(stream)
+    e1.synchronize()
+    ms = group.max(e0.elapsed_time(e1))
+    return {"global_batch": 64, "per_gpu": b, "value": 64 * T * steps / (ms / 1e3), "unit": "tok/s",
+            "ms_per_step": ms / steps, "roofline_speedup_vs_1gpu": strong_roofline(world),
+            "note": "weights are replicated and streamed by every GPU each step, so the fixed job's HBM "
+                    "roofline speed-up is (W + KV_64) / (W + KV_64/N), not N"}
+
+
+def gemm_sweep(pkg, torch, hbm_gbs: float, int8_tops: float, iters: int = 10) -> list:
+    """the 32-shape shared-GEMM sweep through tl_gemm_i8_requant
+    (INT8 x INT8 -> INT32, per-tensor Q16.16 requantize to INT8), each launch
+    timed alone with CUDA events after a 256 MB L2 flush. M in {1, 32} is
+    bounded by HBM (algorithmic bytes M*K + K*N + M*N against the measured
+    copy bandwidth), M in {512, 4096} by the INT8 tensor pipe (2*M*N*K against
+    cuBLASLt's INT8 rate measured in the same run)."""
+    lib = pkg.shim.load_library()
+    s = torch.cuda.current_stream()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(11)
+    scale = torch.tensor([int(0.003 * 65536)], dtype=torch.int32, device="cuda")
+    out = []
+    for M in (1, 32, 512, 4096):
+        for K in (2048, 5632):
+            for N in (256, 2048, 5632, 32000):
+                a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda", generator=g)
+                w = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda", generator=g)
+                y = torch.empty((M, N), dtype=torch.int8, device="cuda")
+
+                def launch():
+                    pkg.shim.check(lib.tl_gemm_i8_requant(a.data_ptr(), w.data_ptr(), scale.data_ptr(), 0, 0,
+                                                          y.data_ptr(), M, N, K, s.cuda_stream), "requant")
+                launch()
+                t = []
+                for _ in range(iters):
+                    flush.fill_(1)
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(s)
+                    launch()
+                    e1.record(s)
+                    e1.synchronize()
+                    t.append(e0.elapsed_time(e1))
+                ms = float(np.median(t))
+                byts, ops = M * K + K * N + M * N, 2.0 * M * N * K
+                row = {"M": M, "K": K, "N": N, "us": ms * 1e3}
+                if M <= 32:
+                    row.update(bound="hbm", gbs=byts / (ms / 1e3) / 1e9, frac=byts / (ms / 1e3) / 1e9 / hbm_gbs)
+                else:
+                    row.update(bound="tensor", tops=ops / (ms / 1e3) / 1e12,
+                               frac=ops / (ms / 1e3) / 1e12 / int8_tops)
+                out.append(row)
+    return out
+
+
+def config0_gpu(pkg, torch) -> dict:
+    """configs[0] on the GPU: one full-size layer (random per-channel INT8
+    weights drawn on the device), 32-token prefill then 16 greedy decode
+    steps through tl_generate (host ids in and out), CUDA events."""
+    cfg = dict(TINYLLAMA, num_hidden_layers=1)
+    eng = pkg.Engine(cfg, max_batch=1, max_prefill_tokens=64)
+    eng.init_random(7)
+    ids = [int(t) for t in np.random.default_rng(1).integers(0, 32000, 32)]
+    stream = torch.cuda.ExternalStream(eng.stream_handle())
+    eng.generate(ids, 17)
+    t = []
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        eng.generate(ids, 17)
+        e1.record(stream)
+        e1.synchronize()
+        t.append(e0.elapsed_time(e1))
+    eng.close()
+    ms = float(np.median(t))
+    return {"workload": "configs[0]: 1 layer, 32-token prefill + 16 decode steps, batch 1", "ms": ms,
+            "tokens_per_s": 17 / (ms / 1e3)}
 
 
 def int8_gemm_rate(pkg, torch, n: int = 8192, iters: int = 10) -> dict:

@@ -148,13 +148,20 @@ TL_API tl_status tl_destroy(tl_engine* eng);
  * engine per GPU. The reference's prefill is the recompute forward_mixed
  * (model/tinyllama_gemm_int8.py:432-467); its TP-2/4 split is by KV head:
  * rank r holds kv heads [r Hkv/world, (r+1) Hkv/world) and their query
- * heads and the matching columns of Q/K/V and gate/up, with O, down,
- * RMSNorm, embedding and LM head replicated. The O and down inputs are
- * quantized with group-wide scales (NCCL all-reduce max) and all-gathered as
- * INT8 by peer stores over NVLink (CUDA-IPC mappings set up here; one
- * process per GPU), so the logits are bit-identical to one GPU's. world
- * (<= 4) must divide num_kv_heads and intermediate_size / 16; a prefill call
- * may hold at most max_prefill_tokens rows.
+ * heads and the matching columns of Q/K/V and gate/up; RMSNorm, embedding
+ * and LM head are replicated. The O and down inputs are quantized with
+ * group-wide per-sequence scales (NCCL all-reduce max). Two exchanges:
+ *  TL_TP_ALLREDUCE  O and down are row-split (rank r holds the input rows of
+ *                   its heads / its FFN columns); each rank's partial INT32
+ *                   accumulators are summed by an NCCL all-reduce over
+ *                   NVLink before the dequant + residual epilogue;
+ *  TL_TP_ALLGATHER  O and down are replicated; each rank's INT8 input block
+ *                   is written into every rank's full-width input by peer
+ *                   stores over NVLink (CUDA-IPC mappings set up here).
+ * Integer sums are exact and order-free, so with either exchange the logits
+ * are bit-identical to one GPU's. world (<= 4) must divide num_kv_heads and
+ * intermediate_size / 16; a prefill call may hold at most
+ * max_prefill_tokens rows.
  * tl_tp_unique_id: rank 0 draws the group id; the host hands the same
  * TL_TP_ID_BYTES bytes to every rank's tl_tp_create (all ranks must call it
  * concurrently: it blocks until the group is complete). tl_load_weights on
@@ -168,9 +175,17 @@ TL_API tl_status tl_destroy(tl_engine* eng);
  * run time; TL_ERR_NCCL when it is missing or a collective fails;
  * TL_ERR_TIMEOUT (tl_synchronize) when a peer's activations do not arrive. */
 #define TL_TP_ID_BYTES 128
+enum { TL_TP_ALLREDUCE = 0, TL_TP_ALLGATHER = 1 };
+/* The default is the faster exchange measured on B200 pairs: at TP-2 on the
+ * 8 x 2048 prefill the INT8 all-gather moves 16 + 46 MB per layer and rank
+ * against 2 x 134 MB of INT32 partial sums for the all-reduce. */
+#define TL_TP_DEFAULT TL_TP_ALLGATHER
 TL_API tl_status tl_tp_unique_id(uint8_t* id_out);
+/* tl_tp_create_ex with exchange TL_TP_DEFAULT. */
 TL_API tl_status tl_tp_create(const tl_config* cfg, int32_t device, int32_t rank, int32_t world, const uint8_t* id,
                               tl_engine** out);
+TL_API tl_status tl_tp_create_ex(const tl_config* cfg, int32_t device, int32_t rank, int32_t world, const uint8_t* id,
+                                 int32_t exchange, tl_engine** out);
 /* Copies (and lays out) the host weights into the engine's device arena. */
 TL_API tl_status tl_load_weights(tl_engine* eng, const tl_weights_view* w);
 /* Random INT8 weights drawn on the device (benchmarks of the full model

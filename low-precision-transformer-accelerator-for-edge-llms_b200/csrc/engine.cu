@@ -193,7 +193,13 @@ struct tl_engine {
   // tensor parallelism (prefill only): H, Hkv, Dq, Dkv, Nqkv and F above are
   // this rank's shares; cfg keeps the model's global sizes
   int tp_rank = 0, tp_world = 1;
-  int Dq_full = 0, F_full = 0;      // the model's O / down input widths (O and down are replicated)
+  int Dq_full = 0, F_full = 0;      // the model's O / down input widths
+  // O / down input widths this rank holds: the full widths when O and down
+  // are replicated (single GPU, TL_TP_ALLGATHER), this rank's row blocks
+  // Dq / F when they are row-split (TL_TP_ALLREDUCE)
+  int Dq_in = 0, F_in = 0;
+  int tp_exchange = TL_TP_ALLREDUCE;
+  int32_t* tp_acc = nullptr;        // [tp_rows][D] partial INT32 accumulators (TL_TP_ALLREDUCE)
   ncclComm_t comm = nullptr;
   // INT8 exchange buffers of the tensor-parallel prefill: two [tp_rows][max(Dq_full, F_full)]
   // matrices (exchange k uses k % 2) and `world` flag words per rank, in one
@@ -698,19 +704,21 @@ tl_status get_graph(tl_engine* e, int M, cudaGraphExec_t* out) {
 // sequence of S tokens): tcgen05 for R >= kTcMinRows rows, else the dp4a
 // GEMV.
 tl_status prefill_gemm(tl_engine* e, const int8_t* xq, const int8_t* w, const double* ws, int N, int K, int R, int S,
-                       const float* in_absmax, int epi, float* out, const float* resid, float* out_absmax) {
+                       const float* in_absmax, int epi, float* out, const float* resid, float* out_absmax,
+                       int32_t* out_i32 = nullptr) {
   if (R >= kTcMinRows) {
     TcPlan plan;
     TL_CU(tc_make_plan(&plan, w, N, xq, R, K, device_sm_count(), epi));
     TcArgs a;
     a.epi = epi; a.w_scale = ws; a.in_absmax = in_absmax; a.rows_per_group = S; a.out_f32 = out;
-    a.resid = resid; a.out_absmax = out_absmax;
+    a.resid = resid; a.out_absmax = out_absmax; a.out_i32 = out_i32;
     TL_CU(launch_gemm_tc(plan, a, e->stream, false));
     return TL_OK;
   }
   GemvArgs g;
   g.x_q = xq; g.in_absmax = in_absmax; g.rows_per_group = S;
   g.w = w; g.w_scale = ws; g.M = R; g.N = N; g.K = K; g.out_f32 = out; g.resid = resid; g.out_absmax = out_absmax;
+  g.out_i32 = out_i32;
   TL_CU(launch_gemv(PRO_Q8, epi, g, e->stream, false));
   return TL_OK;
 }
@@ -718,6 +726,22 @@ tl_status prefill_gemm(tl_engine* e, const int8_t* xq, const int8_t* w, const do
 // Tensor parallel: max over ranks of per-sequence activation maxima (in place)
 tl_status tp_allreduce_max(tl_engine* e, float* v, int n) {
   TL_NCCL(nccl_api().all_reduce(v, v, static_cast<size_t>(n), ncclFloat32, ncclMax, e->comm, e->stream));
+  return TL_OK;
+}
+
+// Tensor parallel, row-split O / down (TL_TP_ALLREDUCE): this rank's INT8
+// input block xq [R][K_local] (quantized with the group-wide scale) times its
+// row block of W (device W^T [D][K_local]) gives partial INT32 accumulators;
+// an NCCL all-reduce sums them over the ranks (integer addition: exact and
+// order-free) and the dequant + residual epilogue runs on the full sums, so
+// every rank holds the one-GPU result bit for bit.
+tl_status tp_rowsplit_resid(tl_engine* e, const int8_t* xq, const int8_t* w, const double* ws, int K_local, int R, int S,
+                            const float* in_absmax, float* x) {
+  if (static_cast<size_t>(R) > e->tp_rows) return TL_ERR_OUT_OF_RANGE;
+  TL_TRY(prefill_gemm(e, xq, w, ws, e->D, K_local, R, S, in_absmax, EPI_I32, nullptr, nullptr, nullptr, e->tp_acc));
+  TL_NCCL(nccl_api().all_reduce(e->tp_acc, e->tp_acc, static_cast<size_t>(R) * e->D, ncclInt32, ncclSum, e->comm,
+                                e->stream));
+  TL_CU(launch_dequant_resid(e->tp_acc, in_absmax, S, 0, ws, x, R, e->D, e->stream));
   return TL_OK;
 }
 
@@ -795,8 +819,9 @@ tl_status enqueue_prefill_layer(tl_engine* e, int l, int n_seq, int S, int slot_
   TL_CU(launch_attn_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->kc, e->vc, e->ks, e->vs, slot_base,
                             l, e->L, e->P, p.att, am + n_seq, s));
   const int8_t* xin = p.xq;
-  if (tp) {
-    TL_TRY(tp_allreduce_max(e, am + n_seq, n_seq));
+  const bool rowsplit = tp && e->tp_exchange == TL_TP_ALLREDUCE;
+  if (tp) TL_TRY(tp_allreduce_max(e, am + n_seq, n_seq));
+  if (tp && !rowsplit) {
     TL_TRY(tp_exchange(e, p.att, e->Dq, e->Dq_full, R, S, am + n_seq, &xin));
   } else {
     TL_CU(launch_quantize_rows(p.att, am + n_seq, R, e->Dq, S, p.xq, s));
@@ -814,7 +839,8 @@ tl_status enqueue_prefill_layer(tl_engine* e, int l, int n_seq, int S, int slot_
       TL_TRY(d2h(e, hc->o_proj, cap->i32, static_cast<size_t>(R) * e->D * 4));
     }
   }
-  TL_TRY(prefill_gemm(e, xin, ly.wo, ly.so, e->D, e->Dq_full, R, S, am + n_seq, EPI_RESID, p.x, p.x, nullptr));
+  if (rowsplit) TL_TRY(tp_rowsplit_resid(e, xin, ly.wo, ly.so, e->Dq, R, S, am + n_seq, p.x));
+  else TL_TRY(prefill_gemm(e, xin, ly.wo, ly.so, e->D, e->Dq_full, R, S, am + n_seq, EPI_RESID, p.x, p.x, nullptr));
   if (hc) TL_TRY(d2h(e, hc->x_after_attn, p.x, rowsD));
   // feed-forward block
   if (hc && hc->ffn_input) {
@@ -837,8 +863,8 @@ tl_status enqueue_prefill_layer(tl_engine* e, int l, int n_seq, int S, int slot_
     }
   }
   xin = p.xq;
-  if (tp) {
-    TL_TRY(tp_allreduce_max(e, am + 3 * n_seq, n_seq));
+  if (tp) TL_TRY(tp_allreduce_max(e, am + 3 * n_seq, n_seq));
+  if (tp && !rowsplit) {
     TL_TRY(tp_exchange(e, p.hid, e->F, e->F_full, R, S, am + 3 * n_seq, &xin));
   } else {
     TL_CU(launch_quantize_rows(p.hid, am + 3 * n_seq, R, e->F, S, p.xq, s));
@@ -856,7 +882,8 @@ tl_status enqueue_prefill_layer(tl_engine* e, int l, int n_seq, int S, int slot_
       TL_TRY(d2h(e, hc->down_proj, cap->i32, static_cast<size_t>(R) * e->D * 4));
     }
   }
-  TL_TRY(prefill_gemm(e, xin, ly.wd, ly.sd, e->D, e->F_full, R, S, am + 3 * n_seq, EPI_RESID, p.x, p.x, nullptr));
+  if (rowsplit) TL_TRY(tp_rowsplit_resid(e, xin, ly.wd, ly.sd, e->F, R, S, am + 3 * n_seq, p.x));
+  else TL_TRY(prefill_gemm(e, xin, ly.wd, ly.sd, e->D, e->F_full, R, S, am + 3 * n_seq, EPI_RESID, p.x, p.x, nullptr));
   return TL_OK;
 }
 
@@ -1061,7 +1088,7 @@ tl_status tp_setup_exchange(tl_engine* e, size_t rows) {
 // Engine for rank `rank` of a tensor-parallel group of `world` GPUs (world 1:
 // the whole model on one GPU). `id` is the NCCL group id (world > 1 only).
 tl_status create_engine(const tl_config* cfg, int32_t device, int rank, int world, const ncclUniqueId* id,
-                        tl_engine** out) {
+                        int exchange, tl_engine** out) {
   if (!out) return TL_ERR_INVALID_ARGUMENT;
   *out = nullptr;
   TL_TRY(check_cfg(cfg));
@@ -1078,6 +1105,10 @@ tl_status create_engine(const tl_config* cfg, int32_t device, int rank, int worl
   e->Hkv = cfg->num_kv_heads / world;
   e->Dq = e->H * 64; e->Dkv = e->Hkv * 64; e->Nqkv = e->Dq + 2 * e->Dkv; e->V = cfg->vocab_size;
   e->Dq_full = cfg->num_heads * 64; e->F_full = cfg->intermediate_size;
+  e->tp_exchange = exchange;
+  const bool rowsplit = world > 1 && exchange == TL_TP_ALLREDUCE;
+  e->Dq_in = rowsplit ? e->Dq : e->Dq_full;
+  e->F_in = rowsplit ? e->F : e->F_full;
   e->L = cfg->num_layers; e->P = cfg->max_positions; e->B = cfg->max_batch;
   auto fail = [&](tl_status s) { tl_destroy(e); return s; };
   if (world > 1) {
@@ -1100,11 +1131,11 @@ tl_status create_engine(const tl_config* cfg, int32_t device, int rank, int worl
     tl_status s;
     if ((s = dmalloc(&ly.wqkv, static_cast<size_t>(e->Nqkv) * e->D)) != TL_OK) return fail(s);
     if ((s = dmalloc(&ly.sqkv, e->Nqkv)) != TL_OK) return fail(s);
-    if ((s = dmalloc(&ly.wo, static_cast<size_t>(e->D) * e->Dq_full)) != TL_OK) return fail(s);
+    if ((s = dmalloc(&ly.wo, static_cast<size_t>(e->D) * e->Dq_in)) != TL_OK) return fail(s);
     if ((s = dmalloc(&ly.so, e->D)) != TL_OK) return fail(s);
     if ((s = dmalloc(&ly.wgu, static_cast<size_t>(2) * e->F * e->D)) != TL_OK) return fail(s);
     if ((s = dmalloc(&ly.sgu, 2 * e->F)) != TL_OK) return fail(s);
-    if ((s = dmalloc(&ly.wd, static_cast<size_t>(e->D) * e->F_full)) != TL_OK) return fail(s);
+    if ((s = dmalloc(&ly.wd, static_cast<size_t>(e->D) * e->F_in)) != TL_OK) return fail(s);
     if ((s = dmalloc(&ly.sd, e->D)) != TL_OK) return fail(s);
     if ((s = dmalloc(&ly.g1, e->D)) != TL_OK) return fail(s);
     if ((s = dmalloc(&ly.g2, e->D)) != TL_OK) return fail(s);
@@ -1135,14 +1166,19 @@ tl_status create_engine(const tl_config* cfg, int32_t device, int rank, int worl
   // TL_DISABLE_PDL=1 launches every kernel without programmatic dependent
   // launch (plain stream order); a debugging aid, off by default.
   if (const char* v = std::getenv("TL_DISABLE_PDL")) e->use_pdl = !(v[0] == '1');
-  if (world > 1 && (s = tp_setup_exchange(e, pf_rows)) != TL_OK) return fail(s);
+  if (rowsplit) {
+    e->tp_rows = pf_rows;
+    if ((s = dmalloc(&e->tp_acc, pf_rows * e->D)) != TL_OK) return fail(s);
+  } else if (world > 1 && (s = tp_setup_exchange(e, pf_rows)) != TL_OK) {
+    return fail(s);
+  }
   *out = e;
   return TL_OK;
 }
 }  // namespace
 
 tl_status tl_create(const tl_config* cfg, int32_t device, tl_engine** out) {
-  return create_engine(cfg, device, 0, 1, nullptr, out);
+  return create_engine(cfg, device, 0, 1, nullptr, TL_TP_ALLREDUCE, out);
 }
 
 tl_status tl_tp_unique_id(uint8_t* id_out) {
@@ -1160,10 +1196,16 @@ tl_status tl_tp_unique_id(uint8_t* id_out) {
 
 tl_status tl_tp_create(const tl_config* cfg, int32_t device, int32_t rank, int32_t world, const uint8_t* id,
                        tl_engine** out) {
+  return tl_tp_create_ex(cfg, device, rank, world, id, TL_TP_DEFAULT, out);
+}
+
+tl_status tl_tp_create_ex(const tl_config* cfg, int32_t device, int32_t rank, int32_t world, const uint8_t* id,
+                          int32_t exchange, tl_engine** out) {
   if (!id || world < 2) return TL_ERR_INVALID_ARGUMENT;
+  if (exchange != TL_TP_ALLREDUCE && exchange != TL_TP_ALLGATHER) return TL_ERR_INVALID_ARGUMENT;
   ncclUniqueId uid;
   std::memcpy(&uid, id, sizeof(uid));
-  return create_engine(cfg, device, rank, world, &uid, out);
+  return create_engine(cfg, device, rank, world, &uid, exchange, out);
 }
 
 tl_status tl_destroy(tl_engine* e) {
@@ -1175,6 +1217,7 @@ tl_status tl_destroy(tl_engine* e) {
     if (e->tp_peer[q] && e->tp_peer[q] != e->tp_base) cudaIpcCloseMemHandle(e->tp_peer[q]);
   cudaFree(e->tp_base);
   cudaFree(e->tp_done);
+  cudaFree(e->tp_acc);
   if (e->comm) nccl_api().comm_destroy(e->comm);
   e->comm = nullptr;
   for (auto& ly : e->layers) {
@@ -1270,7 +1313,10 @@ tl_status tl_load_weights(tl_engine* e, const tl_weights_view* w) {
       TL_CU(cudaMemcpyAsync(ly.sqkv, lv.q.scale, Dq * sizeof(double), cudaMemcpyHostToDevice, e->stream));
       TL_CU(cudaMemcpyAsync(ly.sqkv + Dq, lv.k.scale, Dkv * sizeof(double), cudaMemcpyHostToDevice, e->stream));
       TL_CU(cudaMemcpyAsync(ly.sqkv + Dq + Dkv, lv.v.scale, Dkv * sizeof(double), cudaMemcpyHostToDevice, e->stream));
-      TL_TRY(upload_transposed(e, tmp, lv.o.w, e->Dq_full, D, ly.wo));
+      // O and down: the whole matrix, or this rank's row block (input
+      // features) when they are row-split -- contiguous rows of W[in][out]
+      const size_t o_row0 = e->Dq_in == e->Dq_full ? 0 : static_cast<size_t>(e->tp_rank) * e->Dq_in;
+      TL_TRY(upload_transposed(e, tmp, lv.o.w + o_row0 * D, e->Dq_in, D, ly.wo));
       TL_CU(cudaMemcpyAsync(ly.so, lv.o.scale, D * sizeof(double), cudaMemcpyHostToDevice, e->stream));
       TL_CU(cudaMemcpyAsync(tmp, lv.gate.w, static_cast<size_t>(D) * F, cudaMemcpyHostToDevice, e->stream));
       TL_CU(cudaMemcpyAsync(tmp + static_cast<size_t>(D) * F, lv.up.w, static_cast<size_t>(D) * F,
@@ -1283,7 +1329,8 @@ tl_status tl_load_weights(tl_engine* e, const tl_weights_view* w) {
       }
       TL_CU(cudaMemcpyAsync(ly.sgu, sgu.data(), sgu.size() * sizeof(double), cudaMemcpyHostToDevice, e->stream));
       TL_CU(cudaStreamSynchronize(e->stream));  // sgu is a host temporary
-      TL_TRY(upload_transposed(e, tmp, lv.down.w, e->F_full, D, ly.wd));
+      const size_t d_row0 = e->F_in == e->F_full ? 0 : static_cast<size_t>(e->tp_rank) * e->F_in;
+      TL_TRY(upload_transposed(e, tmp, lv.down.w + d_row0 * D, e->F_in, D, ly.wd));
       TL_CU(cudaMemcpyAsync(ly.sd, lv.down.scale, D * sizeof(double), cudaMemcpyHostToDevice, e->stream));
       TL_CU(cudaMemcpyAsync(ly.g1, lv.input_norm, D * sizeof(float), cudaMemcpyHostToDevice, e->stream));
       TL_CU(cudaMemcpyAsync(ly.g2, lv.post_norm, D * sizeof(float), cudaMemcpyHostToDevice, e->stream));
@@ -1337,9 +1384,9 @@ tl_status tl_init_random_weights(tl_engine* e, uint64_t seed) {
                                  kqkv, s));
     TL_CU(launch_random_i8_block(ly.wqkv + static_cast<size_t>(e->Dq + e->Dkv) * e->D, e->Dkv, e->D,
                                  Dqg + Dkvg + r * e->Dkv, 0, D, kqkv, s));
-    TL_CU(launch_random_i8_block(ly.wo, e->D, e->Dq_full, 0, 0, Dqg, ++k, s));
+    TL_CU(launch_random_i8_block(ly.wo, e->D, e->Dq_in, 0, e->Dq_in == e->Dq_full ? 0 : r * e->Dq_in, Dqg, ++k, s));
     TL_CU(launch_random_i8_block(ly.wgu, 2 * e->F, e->D, 2 * r * e->F, 0, D, ++k, s));
-    TL_CU(launch_random_i8_block(ly.wd, e->D, e->F_full, 0, 0, Fg, ++k, s));
+    TL_CU(launch_random_i8_block(ly.wd, e->D, e->F_in, 0, e->F_in == e->F_full ? 0 : r * e->F_in, Fg, ++k, s));
     TL_CU(launch_fill_f64(ly.sqkv, e->Nqkv, wscale, s));
     TL_CU(launch_fill_f64(ly.so, e->D, wscale, s));
     TL_CU(launch_fill_f64(ly.sgu, 2 * e->F, wscale, s));

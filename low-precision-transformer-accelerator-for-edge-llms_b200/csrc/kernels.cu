@@ -1353,6 +1353,40 @@ cudaError_t launch_tp_wait(const unsigned int* flags, int world, int rank, unsig
   return cudaGetLastError();
 }
 
+// Tensor-parallel prefill, row-split O / down: after the INT32 all-reduce
+// of the ranks' partial accumulators, out = resid + float32(acc) *
+// float32(s_x * s_w[n]) -- the single-GPU EPI_RESID epilogue's exact
+// arithmetic (dequant of model/tinyllama_gemm_int8.py:45-46, then the
+// residual add of :266,270), so the result is bit-identical to one GPU's.
+// Four elements per thread (N % 4 == 0).
+__global__ void __launch_bounds__(256) dequant_resid_kernel(const int32_t* __restrict__ acc,
+                                                            const float* __restrict__ in_absmax, int rows_per_group,
+                                                            int row0, const double* __restrict__ w_scale, float* out,
+                                                            size_t n4, int N) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t e0 = i * 4;
+    const int m = row0 + static_cast<int>(e0 / N), n = static_cast<int>(e0 % N);
+    const double sx = quant_scale64(in_absmax[m / rows_per_group]);
+    const int4 a = reinterpret_cast<const int4*>(acc)[i];
+    float4 r = reinterpret_cast<const float4*>(out)[i];
+    r.x = __fadd_rn(r.x, dequant(a.x, sx, w_scale[n]));
+    r.y = __fadd_rn(r.y, dequant(a.y, sx, w_scale[n + 1]));
+    r.z = __fadd_rn(r.z, dequant(a.z, sx, w_scale[n + 2]));
+    r.w = __fadd_rn(r.w, dequant(a.w, sx, w_scale[n + 3]));
+    reinterpret_cast<float4*>(out)[i] = r;
+  }
+}
+
+cudaError_t launch_dequant_resid(const int32_t* acc, const float* in_absmax, int rows_per_group, int row0,
+                                 const double* w_scale, float* out, int rows, int N, cudaStream_t s) {
+  if (N % 4 || rows <= 0) return cudaErrorInvalidValue;
+  const size_t n4 = static_cast<size_t>(rows) * N / 4;
+  const int grid = static_cast<int>(std::min<size_t>((n4 + 255) / 256, static_cast<size_t>(device_sm_count()) * 8));
+  dequant_resid_kernel<<<grid, 256, 0, s>>>(acc, in_absmax, rows_per_group, row0, w_scale, out, n4, N);
+  return cudaGetLastError();
+}
+
 cudaError_t tp_read_error(unsigned int* code) {
   cudaError_t e = cudaMemcpyFromSymbol(code, g_tp_error, sizeof(unsigned int));
   if (e != cudaSuccess || !*code) return e;

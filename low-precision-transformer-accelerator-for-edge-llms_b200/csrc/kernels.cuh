@@ -281,6 +281,11 @@ cudaError_t launch_quantize_scatter(const float* x, const float* absmax, int row
                                     int col0, const TpScatter& t, unsigned int* done, unsigned int epoch,
                                     cudaStream_t s);
 cudaError_t launch_tp_wait(const unsigned int* flags, int world, int rank, unsigned int epoch, cudaStream_t s);
+// out[m][n] += float32(acc[m][n]) * float32(s_x(row0 + m) * w_scale[n]),
+// the EPI_RESID arithmetic, after the row-split tensor-parallel all-reduce
+// (acc and out point at row row0; s_x from in_absmax[(row0 + m) / rows_per_group]).
+cudaError_t launch_dequant_resid(const int32_t* acc, const float* in_absmax, int rows_per_group, int row0,
+                                 const double* w_scale, float* out, int rows, int N, cudaStream_t s);
 cudaError_t tp_read_error(unsigned int* code);
 // random int8 sub-block [rows][cols] of a global [*][src_cols] matrix whose
 // element (i, j) is hash(seed, i * src_cols + j), at (src_row0, src_col0)

@@ -47,7 +47,8 @@ MODE_PREFILL, MODE_DECODE = 0, 1
 
 # Every symbol the header declares (checked by the CPU tests).
 EXPORTS = (
-    "tl_status_string", "tl_version", "tl_create", "tl_destroy", "tl_tp_unique_id", "tl_tp_create", "tl_load_weights",
+    "tl_status_string", "tl_version", "tl_create", "tl_destroy", "tl_tp_unique_id", "tl_tp_create", "tl_tp_create_ex",
+    "tl_load_weights",
     "tl_init_random_weights", "tl_generate", "tl_generate_batch", "tl_abort",
     "tl_prefill_logits", "tl_decode_logits", "tl_read_kv", "tl_get_position",
     "tl_decode_steps_device", "tl_prefill_batch_device", "tl_decode_rewind", "tl_synchronize",
@@ -157,6 +158,7 @@ def load_library(path: Path | str | None = None):
         "tl_destroy": (i32, [vp]),
         "tl_tp_unique_id": (i32, [vp]),
         "tl_tp_create": (i32, [C.POINTER(Config), i32, i32, i32, vp, C.POINTER(vp)]),
+        "tl_tp_create_ex": (i32, [C.POINTER(Config), i32, i32, i32, vp, i32, C.POINTER(vp)]),
         "tl_load_weights": (i32, [vp, C.POINTER(WeightsView)]),
         "tl_init_random_weights": (i32, [vp, u64]),
         "tl_generate": (i32, [vp, vp, u32, u32, u32, u32, vp, u32, C.POINTER(RunStatus)]),
@@ -415,10 +417,13 @@ class Engine:
 
     def __init__(self, cfg: dict, max_batch: int = 1, device: int = 0,
                  max_prefill_tokens: int | None = None, tp_rank: int = 0, tp_world: int = 1,
-                 tp_id: bytes | None = None):
+                 tp_id: bytes | None = None, tp_exchange: str = "allgather"):
         """``tp_world > 1`` makes rank ``tp_rank`` of a tensor-parallel
-        prefill group (tl_tp_create); every rank passes the same ``tp_id``
-        from :func:`tp_unique_id` and all ranks construct concurrently."""
+        prefill group (tl_tp_create_ex); every rank passes the same ``tp_id``
+        from :func:`tp_unique_id` and all ranks construct concurrently.
+        ``tp_exchange``: ``"allreduce"`` (O and down row-split, NCCL INT32
+        all-reduce) or ``"allgather"`` (O and down replicated, INT8 inputs
+        all-gathered by NVLink peer stores)."""
         self.lib = load_library()
         self.cfg = dict(cfg)
         c = Config(hidden_size=cfg["hidden_size"], intermediate_size=cfg["intermediate_size"],
@@ -432,9 +437,12 @@ class Engine:
         if tp_world > 1:
             if tp_id is None or len(tp_id) != TP_ID_BYTES:
                 raise ValueError("tensor-parallel engines need the group's tp_unique_id() bytes")
+            modes = {"allreduce": 0, "allgather": 1}
+            if tp_exchange not in modes:
+                raise ValueError(f"tp_exchange must be one of {sorted(modes)}")
             idbuf = (C.c_uint8 * TP_ID_BYTES).from_buffer_copy(tp_id)
-            check(self.lib.tl_tp_create(C.byref(c), device, tp_rank, tp_world, C.addressof(idbuf), C.byref(h)),
-                  "tl_tp_create")
+            check(self.lib.tl_tp_create_ex(C.byref(c), device, tp_rank, tp_world, C.addressof(idbuf),
+                                           modes[tp_exchange], C.byref(h)), "tl_tp_create_ex")
         else:
             check(self.lib.tl_create(C.byref(c), device, C.byref(h)), "tl_create")
         self.h = h

@@ -43,13 +43,16 @@ def decode_shard_rank(rank: int, world: int, port: int, n_global: int, max_new: 
         group.close()
 
 
-def tp_prefill_rank(rank: int, world: int, port: int, seed: int, prompt: list, out_q):
+def tp_prefill_rank(rank: int, world: int, port: int, seed: int, prompt: list, out_q, exchange: str = "allgather"):
     """One rank of the tensor-parallel prefill decomposition the engine runs
-    (tl_tp_create), restated over the oracle's NumPy blocks with gloo
+    (tl_tp_create_ex), restated over the oracle's NumPy blocks with gloo
     collectives: kv heads [r*hr, (r+1)*hr) and their query heads, Q/K/V and
     gate/up column slices; per-sequence activation maxima combined with
-    all-reduce MAX, each rank's column block of the O (down) input quantized
-    with that scale and all-gathered as INT8, O and down applied whole."""
+    all-reduce MAX and each rank's column block of the O (down) input
+    quantized with that scale. ``allgather``: the INT8 blocks all-gathered, O
+    and down applied whole. ``allreduce``: each rank multiplies its block by
+    its row block of O (down), the INT32 partial sums are all-reduced (SUM)
+    and dequantized."""
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
     import torch
@@ -107,16 +110,22 @@ def tp_prefill_rank(rank: int, world: int, port: int, seed: int, prompt: list, o
             att = G.attention_core(qh, kd, vd, grp, c["attn_scale"], True)
             peak = allreduce(np.array([np.max(np.abs(att))], np.float32), dist.ReduceOp.MAX)[0]
             sx = 1.0 if peak == 0.0 else float(peak) / 127.0
-            att_q = allgather_cols(G.quantize_with_scale(att, sx))
-            x1 = x + G.dequantize_int32(G.int8_matmul(att_q, lay.o.w_q), sx, lay.o.scale)
+            if exchange == "allgather":
+                acc = G.int8_matmul(allgather_cols(G.quantize_with_scale(att, sx)), lay.o.w_q)
+            else:
+                acc = allreduce(G.int8_matmul(G.quantize_with_scale(att, sx), lay.o.w_q[qcols]), dist.ReduceOp.SUM)
+            x1 = x + G.dequantize_int32(acc, sx, lay.o.scale)
             h2 = G.rms_norm(x1, lay.post_norm, eps)
             g, _, _, _ = G.linear_q(h2, lay.gate.w_q[:, fcols], lay.gate.scale[fcols])
             u, _, _, _ = G.linear_q(h2, lay.up.w_q[:, fcols], lay.up.scale[fcols])
             hid = G.silu(g) * u
             peak = allreduce(np.array([np.max(np.abs(hid))], np.float32), dist.ReduceOp.MAX)[0]
             sh = 1.0 if peak == 0.0 else float(peak) / 127.0
-            hid_q = allgather_cols(G.quantize_with_scale(hid, sh))
-            x = (x1 + G.dequantize_int32(G.int8_matmul(hid_q, lay.down.w_q), sh, lay.down.scale)).astype(np.float32)
+            if exchange == "allgather":
+                acc = G.int8_matmul(allgather_cols(G.quantize_with_scale(hid, sh)), lay.down.w_q)
+            else:
+                acc = allreduce(G.int8_matmul(G.quantize_with_scale(hid, sh), lay.down.w_q[fcols]), dist.ReduceOp.SUM)
+            x = (x1 + G.dequantize_int32(acc, sh, lay.down.scale)).astype(np.float32)
         hn = G.rms_norm(x, qm.final_norm, eps)
         xq, sxh = G.quantize_int8(hn)
         logits = G.dequantize_int32(G.int8_matmul(xq[-1:], qm.lm_head.w_q), sxh, qm.lm_head.scale)[0]
@@ -125,7 +134,7 @@ def tp_prefill_rank(rank: int, world: int, port: int, seed: int, prompt: list, o
         group.close()
 
 
-def gpu_tp_prefill_rank(rank: int, world: int, tp_id: bytes, prompt: list, out_q):
+def gpu_tp_prefill_rank(rank: int, world: int, tp_id: bytes, prompt: list, out_q, exchange: str = "allgather"):
     """One GPU rank of the engine's tensor-parallel prefill (tl_tp_create):
     small oracle model loaded from the full host view, then TinyLlama-size
     random weights; rank 0 also runs the single-GPU engine on the same
@@ -138,14 +147,14 @@ def gpu_tp_prefill_rank(rank: int, world: int, tp_id: bytes, prompt: list, out_q
     qm = small_model(seed=9, layers=2, granularity="channel")
     res = {}
     eng = pkg.Engine(qm.cfg, max_batch=2, device=rank, max_prefill_tokens=256, tp_rank=rank, tp_world=world,
-                     tp_id=tp_id[0])
+                     tp_id=tp_id[0], tp_exchange=exchange)
     eng.load(to_engine_model(pkg, qm))
     res["small_logits"] = eng.prefill_logits(prompt)
     res["small_k"] = eng.read_kv(1, len(prompt))[0]
     eng.close()
     big = W.full_cfg(dict(W.TINYLLAMA, num_hidden_layers=22))
     eng = pkg.Engine(big, max_batch=2, device=rank, max_prefill_tokens=512, tp_rank=rank, tp_world=world,
-                     tp_id=tp_id[1])
+                     tp_id=tp_id[1], tp_exchange=exchange)
     eng.init_random(77)
     res["big_logits"] = eng.prefill_logits(prompt * 12)
     res["big_k"] = eng.read_kv(21, len(prompt) * 12)[0]

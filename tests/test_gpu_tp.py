@@ -1,4 +1,4 @@
-"""Tensor-parallel prefill on 2 GPUs (tl_tp_create): logits and the rank's
+"""Tensor-parallel prefill on 2 GPUs (tl_tp_create_ex, both exchanges): logits and the rank's
 INT8 KV-cache bytes must be bit-identical to the single-GPU engine on the
 same weights -- a small model from the oracle's archive (loaded through the
 full host view, sliced by the engine) and TinyLlama-size random weights
@@ -17,7 +17,8 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 
-def test_tp2_prefill_bit_identical_to_one_gpu(pkg):
+@pytest.mark.parametrize("exchange", ["allreduce", "allgather"])
+def test_tp2_prefill_bit_identical_to_one_gpu(pkg, exchange):
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     world = 2
@@ -25,7 +26,7 @@ def test_tp2_prefill_bit_identical_to_one_gpu(pkg):
     prompt = [int(t) for t in np.random.default_rng(10).integers(0, 512, 23)]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=gpu_tp_prefill_rank, args=(r, world, ids, prompt, q)) for r in range(world)]
+    procs = [ctx.Process(target=gpu_tp_prefill_rank, args=(r, world, ids, prompt, q, exchange)) for r in range(world)]
     for p in procs:
         p.start()
     try:

@@ -1,10 +1,12 @@
 """Tensor-parallel prefill decomposition on CPU ranks over gloo (world 2).
 
-The engine's TP-2/4 prefill (tl_tp_create) splits by KV head with INT32
-all-reduces after O and down and activation-maximum all-reduces before their
-input quantization. Restated over the oracle's blocks, every rank's logits
-and its kv heads' INT8 cache bytes must equal the single-process oracle's
-bit for bit."""
+The engine's TP-2/4 prefill (tl_tp_create_ex) splits by KV head, combines
+the activation maxima before the O and down input quantization with an
+all-reduce max, and either all-reduces the INT32 partial sums of row-split O
+and down (``allreduce``) or all-gathers their INT8 inputs (``allgather``).
+Restated over the oracle's blocks, every rank's logits and its kv heads'
+INT8 cache bytes must equal the single-process oracle's bit for bit, with
+either exchange."""
 
 from __future__ import annotations
 
@@ -12,6 +14,7 @@ import multiprocessing as mp
 import socket
 
 import numpy as np
+import pytest
 
 from dist_workers import tp_prefill_rank
 from helpers import small_model
@@ -24,13 +27,14 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def test_tp2_prefill_equals_single_process():
+@pytest.mark.parametrize("exchange", ["allreduce", "allgather"])
+def test_tp2_prefill_equals_single_process(exchange):
     world, seed = 2, 9
     prompt = [int(t) for t in np.random.default_rng(10).integers(0, 512, 23)]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=tp_prefill_rank, args=(r, world, port, seed, prompt, q)) for r in range(world)]
+    procs = [ctx.Process(target=tp_prefill_rank, args=(r, world, port, seed, prompt, q, exchange)) for r in range(world)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=240) for _ in range(world)], key=lambda t: t[0])
