@@ -13,6 +13,7 @@ from . import analysis, replicas, shim  # noqa: F401
 from .shim import (  # noqa: F401
     Engine, Linear, Layer, Model, TLError, check_model, checkpoint_config, forward_mixed, from_tinyllama_weights,
     layer_debug, load_checkpoint_npz, load_library, mixed_precision_decoder_layer, quantize_int8, quantize_weight,
-    quantized_linear, rms_norm, rope_tables, tp_unique_id,
+    quantized_linear, rms_norm, rope_tables, tp_unique_id, contract_rmsnorm, contract_silu, contract_softmax,
+    contract_rope, residual_add_i32,
 )
 from .analysis import diff_stats, dump_debug, flatten_named_arrays, run_analysis  # noqa: F401

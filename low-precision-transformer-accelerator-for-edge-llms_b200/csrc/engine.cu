@@ -1876,8 +1876,12 @@ tl_status tl_profile_decode_kernels(tl_engine* e, uint32_t n_seqs, uint32_t iter
     for (uint32_t it = 0; it < iters; ++it) {
       const int l = static_cast<int>(it % e->L);
       const Layer& ly = e->layers[l];
-      if (kind == 5) TL_CU(cudaMemsetAsync(flush, it & 0xff, flush_bytes, s));
-      TL_CU(cudaEventRecord(ev[2 * it], s));
+      // kinds 0-4, 6, 7: one event pair around all iters back-to-back launches
+      // (layers cycled, so weights come from HBM); the LM head (one matrix) is
+      // timed per launch with an L2 flush outside each interval
+      const bool per_launch = kind == 5;
+      if (per_launch) TL_CU(cudaMemsetAsync(flush, it & 0xff, flush_bytes, s));
+      if (per_launch || it == 0) TL_CU(cudaEventRecord(ev[2 * it], s));
       cudaError_t ce = cudaSuccess;
       tl_status ts = TL_OK;
       GemvArgs g;
@@ -1965,15 +1969,21 @@ tl_status tl_profile_decode_kernels(tl_engine* e, uint32_t n_seqs, uint32_t iter
         result = ts;
         break;
       }
-      TL_CU(cudaEventRecord(ev[2 * it + 1], s));
+      if (per_launch || it + 1 == iters) TL_CU(cudaEventRecord(ev[2 * it + 1], s));
     }
     if (result != TL_OK) break;
     TL_CU(cudaStreamSynchronize(s));
     double tot = 0.0;
-    for (uint32_t it = 0; it < iters; ++it) {
+    if (kind == 5) {
+      for (uint32_t it = 0; it < iters; ++it) {
+        float ms = 0.f;
+        TL_CU(cudaEventElapsedTime(&ms, ev[2 * it], ev[2 * it + 1]));
+        tot += ms;
+      }
+    } else {
       float ms = 0.f;
-      TL_CU(cudaEventElapsedTime(&ms, ev[2 * it], ev[2 * it + 1]));
-      tot += ms;
+      TL_CU(cudaEventElapsedTime(&ms, ev[0], ev[2 * (iters - 1) + 1]));
+      tot = ms;
     }
     avg_ms_out[kind] = static_cast<float>(tot / iters);
   }

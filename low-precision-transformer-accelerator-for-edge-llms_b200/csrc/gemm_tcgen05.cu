@@ -119,31 +119,32 @@ TL_DEV float tc_store(const TcArgs& a, int n, int m, int acc, float y, float par
 // final pair exchange. Returns the warp maximum of token
 // 8 b4 + 4 b3 + 2 b2 + b1 (bits of the lane index), held by both lanes of
 // each even/odd pair: 16 64-bit shuffles instead of 16 full reductions.
-TL_DEV unsigned long long warp_key_max16(const unsigned long long* k, int lane, int& token) {
-  unsigned long long a8[8], a4[4], a2[2];
+template <typename T>
+TL_DEV T warp_max16(const T* k, int lane, int& token) {
+  T a8[8], a4[4], a2[2];
   const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const unsigned long long keep = b4 ? k[i + 8] : k[i], send = b4 ? k[i] : k[i + 8];
-    const unsigned long long r = __shfl_xor_sync(0xffffffffu, send, 16);
+    const T keep = b4 ? k[i + 8] : k[i], send = b4 ? k[i] : k[i + 8];
+    const T r = __shfl_xor_sync(0xffffffffu, send, 16);
     a8[i] = keep > r ? keep : r;
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const unsigned long long keep = b3 ? a8[i + 4] : a8[i], send = b3 ? a8[i] : a8[i + 4];
-    const unsigned long long r = __shfl_xor_sync(0xffffffffu, send, 8);
+    const T keep = b3 ? a8[i + 4] : a8[i], send = b3 ? a8[i] : a8[i + 4];
+    const T r = __shfl_xor_sync(0xffffffffu, send, 8);
     a4[i] = keep > r ? keep : r;
   }
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
-    const unsigned long long keep = b2 ? a4[i + 2] : a4[i], send = b2 ? a4[i] : a4[i + 2];
-    const unsigned long long r = __shfl_xor_sync(0xffffffffu, send, 4);
+    const T keep = b2 ? a4[i + 2] : a4[i], send = b2 ? a4[i] : a4[i + 2];
+    const T r = __shfl_xor_sync(0xffffffffu, send, 4);
     a2[i] = keep > r ? keep : r;
   }
-  const unsigned long long keep = b1 ? a2[1] : a2[0], send = b1 ? a2[0] : a2[1];
-  const unsigned long long r = __shfl_xor_sync(0xffffffffu, send, 2);
-  unsigned long long m = keep > r ? keep : r;
-  const unsigned long long o = __shfl_xor_sync(0xffffffffu, m, 1);
+  const T keep = b1 ? a2[1] : a2[0], send = b1 ? a2[0] : a2[1];
+  const T r = __shfl_xor_sync(0xffffffffu, send, 2);
+  T m = keep > r ? keep : r;
+  const T o = __shfl_xor_sync(0xffffffffu, m, 1);
   m = m > o ? m : o;
   token = (b4 ? 8 : 0) + (b3 ? 4 : 0) + (b2 ? 2 : 0) + (b1 ? 1 : 0);
   return m;
@@ -323,26 +324,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // and lands with one shared atomic per warp instead of one per element
         const bool one_group = has_amax && mc / a.rows_per_group == (mc + 15) / a.rows_per_group;
         float chunk_max = 0.0f;
+        uint32_t mag_bits[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int m = mc + j;
           const float y = kFloatEpi ? dequant(v[j], sx_sm[c * 16 + j], cc.sw) : 0.0f;
           const float partner = EPI == EPI_SILU ? __shfl_xor_sync(0xffffffffu, y, 1) : 0.0f;
           key[j] = 0ull;
+          mag_bits[j] = 0u;
           if (n_ok && m < a.M) {
             const float mag = tc_store<EPI>(a, n, m, v[j], y, partner, rcur[j], cc);
             if (one_group) chunk_max = fmaxf(chunk_max, mag);
-            else if (has_amax) atomicMax(amax_sm + c * 16 + j, __float_as_uint(mag));
+            mag_bits[j] = __float_as_uint(mag);  // non-negative: bit order is value order
             if (EPI == EPI_F32) key[j] = argmax_key(y, n);
           }
         }
         if (one_group) {
           chunk_max = warp_max(chunk_max);
           if (lane == 0) atomicMax(amax_sm + c * 16, __float_as_uint(chunk_max));
+        } else if (has_amax) {
+          // one row max per token: reduced across the warp's 32 channels
+          // first (transposed butterfly), then one shared atomic per token
+          // and warp instead of 32
+          int tok;
+          const uint32_t mm = warp_max16(mag_bits, lane, tok);
+          if ((lane & 1) == 0 && mm) atomicMax(amax_sm + c * 16 + tok, mm);
         }
         if (EPI == EPI_F32 && has_key) {
           int tok;
-          const unsigned long long km = warp_key_max16(key, lane, tok);
+          const unsigned long long km = warp_max16(key, lane, tok);
           if ((lane & 1) == 0 && km) atomicMax(key_sm + c * 16 + tok, km);
         }
 #pragma unroll

@@ -1423,4 +1423,201 @@ cudaError_t launch_rows_rewind(int* pos, int* active, int* count, int* stop, int
   return cudaGetLastError();
 }
 
+// ============================================== contract mode (Q16.16 wrappers)
+// The hardware's fixed-point wrappers around its nonlinear blocks
+// (rtl/nonlinear/*_wrapper.sv, model/export_fpga_vectors.py:874-927,
+// 1522-1990): INT8 in, Q16.16 core values, INT8 out by a Q16.16 scale.
+TL_DEV float q16_to_float(int32_t raw) {  // float32(raw / 65536), the division in double
+  return static_cast<float>(static_cast<double>(raw) / 65536.0);
+}
+TL_DEV int32_t float_to_q16(float v) {     // round half to even of v * 65536, saturated
+  const long long r = __double2ll_rn(static_cast<double>(v) * 65536.0);
+  return static_cast<int32_t>(r > 2147483647ll ? 2147483647ll : (r < -2147483648ll ? -2147483648ll : r));
+}
+TL_DEV int32_t mul_i32_wrap(int32_t a, int32_t b) {  // int32 product modulo 2^32 (NumPy int32)
+  return static_cast<int32_t>(static_cast<uint32_t>(a) * static_cast<uint32_t>(b));
+}
+// Q16.16 value / Q16.16 scale, half to even on the remainder, clamped
+TL_DEV int8_t quant_fixed_q16(int32_t v, uint32_t scale, bool nonneg) {
+  const unsigned long long den = scale ? scale : 1u;
+  const unsigned long long mag = v < 0 ? static_cast<unsigned long long>(-static_cast<long long>(v))
+                                       : static_cast<unsigned long long>(v);
+  unsigned long long q = mag / den;
+  const unsigned long long r = mag - q * den;
+  if (2 * r > den || (2 * r == den && (q & 1))) ++q;
+  long long sgn = v < 0 ? -static_cast<long long>(q) : static_cast<long long>(q);
+  const long long lo = nonneg ? 0 : -127;
+  sgn = sgn < lo ? lo : (sgn > 127 ? 127 : sgn);
+  return static_cast<int8_t>(sgn);
+}
+// |t| >> 16 rounded half to even, sign restored (the RTL's Q16.16 rounding)
+TL_DEV long long round_shift16(long long t) {
+  const unsigned long long mag = t < 0 ? static_cast<unsigned long long>(-t) : static_cast<unsigned long long>(t);
+  unsigned long long q = mag >> 16;
+  const unsigned long long rem = mag & 0xffffu;
+  if (rem > 0x8000u || (rem == 0x8000u && (q & 1))) ++q;
+  return t < 0 ? -static_cast<long long>(q) : static_cast<long long>(q);
+}
+
+// RMSNorm wrapper: one CTA per row; the float32 RMSNorm in NumPy's order.
+__global__ void __launch_bounds__(256) contract_rmsnorm_kernel(const int8_t* xq, int D, uint32_t in_scale,
+                                                               const int32_t* gamma_q16, float eps, uint32_t out_scale,
+                                                               NormPlan plan, int8_t* yq, int32_t* y16) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* buf = reinterpret_cast<float*>(smem);
+  float* g = buf + D;
+  RowScratchView rs = rs_view(g + D, plan);
+  const size_t r = blockIdx.x;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    buf[i] = q16_to_float(mul_i32_wrap(xq[r * D + i], static_cast<int32_t>(in_scale)));
+    g[i] = q16_to_float(gamma_q16[i]);
+  }
+  __syncthreads();
+  block_rmsnorm(buf, D, g, eps, plan, rs);
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    const int32_t v = float_to_q16(buf[i]);
+    if (y16) y16[r * D + i] = v;
+    yq[r * D + i] = quant_fixed_q16(v, out_scale, false);
+  }
+}
+
+cudaError_t launch_contract_rmsnorm(const int8_t* xq, int rows, int D, uint32_t in_scale, const int32_t* gamma_q16,
+                                    float eps, uint32_t out_scale, int8_t* yq, int32_t* y16, cudaStream_t s) {
+  NormPlan plan;
+  if (rows <= 0 || !norm_plan(D, &plan)) return cudaErrorInvalidValue;
+  const size_t smem = 8 * static_cast<size_t>(D) + 4 * rs_floats(plan) + 16;
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(contract_rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  contract_rmsnorm_kernel<<<rows, 256, smem, s>>>(xq, D, in_scale, gamma_q16, eps, out_scale, plan, yq, y16);
+  return cudaGetLastError();
+}
+
+// SiLU wrapper, elementwise.
+__global__ void contract_silu_kernel(const int8_t* xq, long long n, uint32_t in_scale, uint32_t out_scale, int8_t* yq,
+                                     int32_t* y16) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float x = q16_to_float(mul_i32_wrap(xq[i], static_cast<int32_t>(in_scale)));
+    const float c = fminf(fmaxf(x, -60.0f), 60.0f);
+    const float y = __fdiv_rn(x, __fadd_rn(1.0f, expf(-c)));
+    const int32_t v = float_to_q16(y);
+    if (y16) y16[i] = v;
+    yq[i] = quant_fixed_q16(v, out_scale, false);
+  }
+}
+
+cudaError_t launch_contract_silu(const int8_t* xq, long long n, uint32_t in_scale, uint32_t out_scale, int8_t* yq,
+                                 int32_t* y16, cudaStream_t s) {
+  if (n <= 0) return cudaErrorInvalidValue;
+  const int grid = static_cast<int>(std::min<long long>((n + 255) / 256, device_sm_count() * 8ll));
+  contract_silu_kernel<<<grid, 256, 0, s>>>(xq, n, in_scale, out_scale, yq, y16);
+  return cudaGetLastError();
+}
+
+// Softmax wrapper: one warp per row of <= 128 scores. Scores times the
+// Q16.16 scale saturate to int32; the float32 softmax sums in NumPy's order
+// (8 strided accumulators, then ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)), then
+// the tail); probabilities to Q16.16, then p * 127 >> 16 (the 1/127 scale).
+__global__ void __launch_bounds__(128) contract_softmax_kernel(const int32_t* scores, int rows, int cols,
+                                                               uint32_t scale, int8_t* pq, int32_t* p16) {
+  __shared__ float e_sm[4][128];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * 4 + warp;
+  if (r >= rows) return;
+  float x[4];
+  float m = -INFINITY;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int c = lane + 32 * u;
+    x[u] = -INFINITY;
+    if (c < cols) {
+      long long t = static_cast<long long>(scores[static_cast<size_t>(r) * cols + c]) * static_cast<long long>(scale);
+      t = t > 2147483647ll ? 2147483647ll : (t < -2147483648ll ? -2147483648ll : t);
+      x[u] = q16_to_float(static_cast<int32_t>(t));
+      m = fmaxf(m, x[u]);
+    }
+  }
+  m = warp_max(m);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int c = lane + 32 * u;
+    if (c < cols) e_sm[warp][c] = expf(__fsub_rn(x[u], m));
+  }
+  __syncwarp();
+  float sum = 0.0f;
+  if (lane == 0) {
+    const float* e = e_sm[warp];
+    if (cols < 8) {
+      for (int c = 0; c < cols; ++c) sum = __fadd_rn(sum, e[c]);
+    } else {
+      float acc[8];
+      for (int j = 0; j < 8; ++j) acc[j] = e[j];
+      const int full = cols - cols % 8;
+      for (int b = 8; b < full; b += 8)
+        for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(acc[j], e[b + j]);
+      sum = __fadd_rn(__fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3])),
+                      __fadd_rn(__fadd_rn(acc[4], acc[5]), __fadd_rn(acc[6], acc[7])));
+      for (int c = full; c < cols; ++c) sum = __fadd_rn(sum, e[c]);
+    }
+  }
+  sum = __shfl_sync(0xffffffffu, sum, 0);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int c = lane + 32 * u;
+    if (c >= cols) continue;
+    const int32_t v = float_to_q16(__fdiv_rn(e_sm[warp][c], sum));
+    const long long q = round_shift16(static_cast<long long>(v) * 127);
+    const size_t o = static_cast<size_t>(r) * cols + c;
+    if (p16) p16[o] = v;
+    pq[o] = static_cast<int8_t>(q < 0 ? 0 : (q > 127 ? 127 : q));
+  }
+}
+
+cudaError_t launch_contract_softmax(const int32_t* scores, int rows, int cols, uint32_t scale, int8_t* pq, int32_t* p16,
+                                    cudaStream_t s) {
+  if (rows <= 0 || cols <= 0 || cols > 128) return cudaErrorInvalidValue;
+  contract_softmax_kernel<<<(rows + 3) / 4, 128, 0, s>>>(scores, rows, cols, scale, pq, p16);
+  return cudaGetLastError();
+}
+
+// Q16.16 RoPE of INT8 rows [rows][64] with per-row tables: lower half
+// x*cos - x[d+32]*sin, upper half x*cos + x[d-32]*sin, rounded to INT8
+// (rtl/compute/rope_unit.sv:73-127, model/export_fpga_vectors.py:684-732).
+__global__ void contract_rope_kernel(const int8_t* x, const int32_t* cs, const int32_t* sn, long long n, int8_t* out) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long row = i >> 6;
+    const int d = static_cast<int>(i & 63);
+    const long long xv = x[i], pv = x[(row << 6) + (d < 32 ? d + 32 : d - 32)];
+    const long long t = d < 32 ? xv * cs[i] - pv * sn[i] : xv * cs[i] + pv * sn[i];
+    const long long q = round_shift16(t);
+    out[i] = static_cast<int8_t>(q < -127 ? -127 : (q > 127 ? 127 : q));
+  }
+}
+
+cudaError_t launch_contract_rope(const int8_t* x, const int32_t* cs, const int32_t* sn, int rows, int8_t* out,
+                                 cudaStream_t s) {
+  if (rows <= 0) return cudaErrorInvalidValue;
+  const long long n = static_cast<long long>(rows) * 64;
+  const int grid = static_cast<int>(std::min<long long>((n + 255) / 256, device_sm_count() * 8ll));
+  contract_rope_kernel<<<grid, 256, 0, s>>>(x, cs, sn, n, out);
+  return cudaGetLastError();
+}
+
+// Unsaturated INT32 residual add (rtl/compute/residual_add.sv:92-96): modulo 2^32.
+__global__ void residual_add_i32_kernel(const int32_t* a, const int32_t* b, int32_t* out, long long n) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    out[i] = static_cast<int32_t>(static_cast<uint32_t>(a[i]) + static_cast<uint32_t>(b[i]));
+}
+
+cudaError_t launch_residual_add_i32(const int32_t* a, const int32_t* b, int32_t* out, long long n, cudaStream_t s) {
+  if (n <= 0) return cudaErrorInvalidValue;
+  const int grid = static_cast<int>(std::min<long long>((n + 255) / 256, device_sm_count() * 8ll));
+  residual_add_i32_kernel<<<grid, 256, 0, s>>>(a, b, out, n);
+  return cudaGetLastError();
+}
+
 }  // namespace tl

@@ -295,4 +295,15 @@ cudaError_t launch_random_i8_block(int8_t* dst, int rows, int cols, long long sr
 cudaError_t launch_rows_rewind(int* pos, int* active, int* count, int* stop, int M, int position,
                                cudaStream_t s);
 
+// ---- contract mode: the hardware's Q16.16 wrappers (kernels.cu)
+cudaError_t launch_contract_rmsnorm(const int8_t* xq, int rows, int D, uint32_t in_scale, const int32_t* gamma_q16,
+                                    float eps, uint32_t out_scale, int8_t* yq, int32_t* y16, cudaStream_t s);
+cudaError_t launch_contract_silu(const int8_t* xq, long long n, uint32_t in_scale, uint32_t out_scale, int8_t* yq,
+                                 int32_t* y16, cudaStream_t s);
+cudaError_t launch_contract_softmax(const int32_t* scores, int rows, int cols, uint32_t scale, int8_t* pq, int32_t* p16,
+                                    cudaStream_t s);
+cudaError_t launch_contract_rope(const int8_t* x, const int32_t* cs, const int32_t* sn, int rows, int8_t* out,
+                                 cudaStream_t s);
+cudaError_t launch_residual_add_i32(const int32_t* a, const int32_t* b, int32_t* out, long long n, cudaStream_t s);
+
 }  // namespace tl

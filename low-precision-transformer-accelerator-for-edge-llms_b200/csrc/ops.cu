@@ -225,4 +225,38 @@ tl_status tl_attn_prefill(const float* qkv, int32_t seq_len, int32_t n_seqs, con
                                 static_cast<cudaStream_t>(stream)));
 }
 
+tl_status tl_contract_rmsnorm(const int8_t* x_q, int32_t rows, int32_t cols, uint32_t in_scale_q16,
+                              const int32_t* gamma_q16, float eps, uint32_t out_scale_q16, int8_t* y_q,
+                              int32_t* y_q16, void* stream) {
+  if (!x_q || !gamma_q16 || !y_q || rows <= 0 || cols <= 0) return TL_ERR_INVALID_ARGUMENT;
+  return cu(launch_contract_rmsnorm(x_q, rows, cols, in_scale_q16, gamma_q16, eps, out_scale_q16, y_q, y_q16,
+                                    static_cast<cudaStream_t>(stream)));
+}
+
+tl_status tl_contract_silu(const int8_t* x_q, int64_t n, uint32_t in_scale_q16, uint32_t out_scale_q16, int8_t* y_q,
+                           int32_t* y_q16, void* stream) {
+  if (!x_q || !y_q || n <= 0) return TL_ERR_INVALID_ARGUMENT;
+  return cu(launch_contract_silu(x_q, n, in_scale_q16, out_scale_q16, y_q, y_q16, static_cast<cudaStream_t>(stream)));
+}
+
+tl_status tl_contract_softmax(const int32_t* scores, int32_t rows, int32_t cols, uint32_t score_scale_q16,
+                              int8_t* prob_q, int32_t* prob_q16, void* stream) {
+  if (!scores || !prob_q || rows <= 0 || cols <= 0) return TL_ERR_INVALID_ARGUMENT;
+  if (cols > 128) return TL_ERR_OUT_OF_RANGE;
+  return cu(launch_contract_softmax(scores, rows, cols, score_scale_q16, prob_q, prob_q16,
+                                    static_cast<cudaStream_t>(stream)));
+}
+
+tl_status tl_contract_rope(const int8_t* x_q, const int32_t* cos_q16, const int32_t* sin_q16, int32_t rows,
+                           int8_t* out, void* stream) {
+  if (!x_q || !cos_q16 || !sin_q16 || !out || rows <= 0) return TL_ERR_INVALID_ARGUMENT;
+  return cu(launch_contract_rope(x_q, cos_q16, sin_q16, rows, out, static_cast<cudaStream_t>(stream)));
+}
+
+tl_status tl_residual_add_i32(const int32_t* residual_q16, const int32_t* update_q16, int32_t* out, int64_t n,
+                              void* stream) {
+  if (!residual_q16 || !update_q16 || !out || n <= 0) return TL_ERR_INVALID_ARGUMENT;
+  return cu(launch_residual_add_i32(residual_q16, update_q16, out, n, static_cast<cudaStream_t>(stream)));
+}
+
 }  // extern "C"

@@ -57,6 +57,7 @@ EXPORTS = (
     "tl_gemm_i8", "tl_gemm_i8_requant", "tl_quantized_linear", "tl_rmsnorm", "tl_lmhead_argmax",
     "tl_attn_decode", "tl_attn_prefill", "tl_lmhead_argmax_noalloc",
     "tl_forward_logits", "tl_decoder_layer", "tl_decode_layer", "tl_decode_debug",
+    "tl_contract_rmsnorm", "tl_contract_silu", "tl_contract_softmax", "tl_contract_rope", "tl_residual_add_i32",
 )
 
 
@@ -191,6 +192,11 @@ def load_library(path: Path | str | None = None):
         "tl_decoder_layer": (i32, [vp, u32, u32, vp, u32, vp, C.POINTER(LayerCapture)]),
         "tl_decode_layer": (i32, [vp, u32, u32, vp, vp, vp, vp, C.POINTER(LayerCapture)]),
         "tl_decode_debug": (i32, [vp, u32, u32, u32, C.POINTER(DebugRecord), vp]),
+        "tl_contract_rmsnorm": (i32, [vp, i32, i32, u32, vp, C.c_float, u32, vp, vp, vp]),
+        "tl_contract_silu": (i32, [vp, C.c_int64, u32, u32, vp, vp, vp]),
+        "tl_contract_softmax": (i32, [vp, i32, i32, u32, vp, vp, vp]),
+        "tl_contract_rope": (i32, [vp, vp, vp, i32, vp, vp]),
+        "tl_residual_add_i32": (i32, [vp, vp, vp, C.c_int64, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -921,3 +927,75 @@ def mixed_precision_decoder_layer(x, layer: dict, cfg: dict, cos=None, sin=None,
     if capture_arrays:
         debug["layer_out_fp"] = out
     return out, debug
+
+
+# --------------------------------------------------------------------------
+# Contract mode: the hardware's Q16.16 wrappers (host arrays in and out)
+# --------------------------------------------------------------------------
+def _dev(torch, a, dtype):
+    return torch.from_numpy(np.ascontiguousarray(np.asarray(a, dtype=dtype))).cuda()
+
+
+def contract_rmsnorm(x_q, in_scale_q16: int, gamma_q16, eps: float, out_scale_q16: int):
+    """RMSNorm wrapper (rtl/nonlinear/rmsnorm_wrapper.sv): INT8 rows [R, D] ->
+    (y_q16 int32, y_q int8), see tl_contract_rmsnorm."""
+    torch = _torch()
+    lib = load_library()
+    x = _dev(torch, x_q, np.int8)
+    rows, cols = x.shape
+    yq = torch.empty_like(x)
+    y16 = torch.empty((rows, cols), dtype=torch.int32, device="cuda")
+    g = _dev(torch, gamma_q16, np.int32)  # held: a temporary's memory would be reused before the launch
+    check(lib.tl_contract_rmsnorm(x.data_ptr(), rows, cols, int(in_scale_q16), g.data_ptr(), float(eps),
+                                  int(out_scale_q16), yq.data_ptr(), y16.data_ptr(), _stream(torch)),
+          "tl_contract_rmsnorm")
+    return y16.cpu().numpy(), yq.cpu().numpy()
+
+
+def contract_silu(x_q, in_scale_q16: int, out_scale_q16: int):
+    """SiLU wrapper (rtl/nonlinear/silu_wrapper.sv): -> (y_q16, y_q)."""
+    torch = _torch()
+    lib = load_library()
+    x = _dev(torch, x_q, np.int8)
+    yq = torch.empty_like(x)
+    y16 = torch.empty(x.shape, dtype=torch.int32, device="cuda")
+    check(lib.tl_contract_silu(x.data_ptr(), x.numel(), int(in_scale_q16), int(out_scale_q16), yq.data_ptr(),
+                               y16.data_ptr(), _stream(torch)), "tl_contract_silu")
+    return y16.cpu().numpy(), yq.cpu().numpy()
+
+
+def contract_softmax(scores, score_scale_q16: int):
+    """Softmax wrapper (rtl/nonlinear/softmax_wrapper.sv): INT32 scores
+    [R, C <= 128] -> (prob_q16, prob_q) with the 1/127 probability scale."""
+    torch = _torch()
+    lib = load_library()
+    sc = _dev(torch, scores, np.int32)
+    rows, cols = sc.shape
+    pq = torch.empty((rows, cols), dtype=torch.int8, device="cuda")
+    p16 = torch.empty((rows, cols), dtype=torch.int32, device="cuda")
+    check(lib.tl_contract_softmax(sc.data_ptr(), rows, cols, int(score_scale_q16), pq.data_ptr(), p16.data_ptr(),
+                                  _stream(torch)), "tl_contract_softmax")
+    return p16.cpu().numpy(), pq.cpu().numpy()
+
+
+def contract_rope(x_q, cos_q16, sin_q16):
+    """Q16.16 RoPE of INT8 rows [R, 64] with per-row tables (rope_unit.sv)."""
+    torch = _torch()
+    lib = load_library()
+    x = _dev(torch, x_q, np.int8)
+    out = torch.empty_like(x)
+    cs, sn = _dev(torch, cos_q16, np.int32), _dev(torch, sin_q16, np.int32)  # held until the launch
+    check(lib.tl_contract_rope(x.data_ptr(), cs.data_ptr(), sn.data_ptr(), x.shape[0], out.data_ptr(),
+                               _stream(torch)), "tl_contract_rope")
+    return out.cpu().numpy()
+
+
+def residual_add_i32(residual_q16, update_q16):
+    """Unsaturated INT32 residual add (residual_add.sv:92-96)."""
+    torch = _torch()
+    lib = load_library()
+    a, b = _dev(torch, residual_q16, np.int32), _dev(torch, update_q16, np.int32)
+    out = torch.empty_like(a)
+    check(lib.tl_residual_add_i32(a.data_ptr(), b.data_ptr(), out.data_ptr(), a.numel(), _stream(torch)),
+          "tl_residual_add_i32")
+    return out.cpu().numpy()

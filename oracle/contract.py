@@ -124,3 +124,82 @@ def status_word(busy: bool, done: bool, error: bool, stop_valid: bool, stop_reas
     (rtl/common/tinyllama_pkg.sv:159-166)."""
     return (int(busy) | (int(done) << 1) | (int(error) << 2) | (int(stop_valid) << 3)
             | ((stop_reason & 0x7) << 4) | ((error_code & 0xF) << 8))
+
+
+# ----------------------------------------------------------------------------
+# Fixed-point wrapper chain of the nonlinear blocks (contract mode)
+# ----------------------------------------------------------------------------
+def float_from_q16_16(raw) -> np.ndarray:
+    """float32(raw / 65536) with the division in float64
+    (model/export_fpga_vectors.py:191-192)."""
+    return (np.asarray(raw, dtype=np.int64).astype(np.float64) / float(Q16_ONE)).astype(np.float32)
+
+
+def q16_16_signed_array(values) -> np.ndarray:
+    """Elementwise :func:`q16_16_signed_from_float` (Python round, half to
+    even, of value * 65536; saturated to int32)."""
+    v = np.asarray(values, dtype=np.float64) * float(Q16_ONE)
+    return np.clip(np.rint(v), -(1 << 31), (1 << 31) - 1).astype(np.int32)
+
+
+def quantize_fixed_by_scale_q16(values_q16, scale_q16, nonnegative_only: bool = False) -> np.ndarray:
+    """Q16.16 values divided by a Q16.16 scale, rounded half to even on the
+    integer remainder, clamped to [-127, 127] (or [0, 127])
+    (quantize_fixed_tile_by_scale_q16, model/export_fpga_vectors.py:900-927)."""
+    den = int(scale_q16) if int(scale_q16) != 0 else 1
+    v = np.asarray(values_q16, dtype=np.int64)
+    mag = np.abs(v)
+    q, r = mag // den, mag % den
+    up = (2 * r > den) | ((2 * r == den) & ((q & 1) == 1))
+    s = np.where(v < 0, -(q + up), q + up)
+    lo = 0 if nonnegative_only else -127
+    return np.clip(s, lo, 127).astype(np.int8)
+
+
+def rmsnorm_contract(x_q, in_scale_q16, gamma_q16, eps: float, out_scale_q16):
+    """RMSNorm wrapper (build_rmsnorm_case, model/export_fpga_vectors.py:1705-1728,
+    rtl/nonlinear/rmsnorm_wrapper.sv): INT8 x times the Q16.16 input scale,
+    the float32 RMSNorm of model/tinyllama.py:45-50 on the dequantized core
+    values, Q16.16 result, INT8 output by the Q16.16 output scale. Returns
+    (y_q16 int32, y_q int8, y_fp float32)."""
+    from . import golden as G
+    x_core = np.asarray(x_q, dtype=np.int32) * np.int32(in_scale_q16)
+    y_fp = G.rms_norm(float_from_q16_16(x_core), float_from_q16_16(gamma_q16), eps)
+    y_q16 = q16_16_signed_array(y_fp)
+    return y_q16, quantize_fixed_by_scale_q16(y_q16, out_scale_q16), y_fp
+
+
+def silu_contract(x_q, in_scale_q16, out_scale_q16):
+    """SiLU wrapper (build_silu_case, model/export_fpga_vectors.py:1896-1910,
+    rtl/nonlinear/silu_wrapper.sv). Returns (y_q16, y_q, y_fp)."""
+    from . import golden as G
+    x_core = np.asarray(x_q, dtype=np.int32) * np.int32(in_scale_q16)
+    y_fp = G.silu(float_from_q16_16(x_core))
+    y_q16 = q16_16_signed_array(y_fp)
+    return y_q16, quantize_fixed_by_scale_q16(y_q16, out_scale_q16), y_fp
+
+
+def softmax_contract(scores_i32, score_scale_q16):
+    """Softmax wrapper (build_softmax_case, model/export_fpga_vectors.py:1808-1829,
+    rtl/nonlinear/softmax_wrapper.sv:23): INT32 scores times the Q16.16 score
+    scale with 32-bit saturation (mul_int32_by_scale_q16, :894-896), float32
+    max-shifted softmax of each row (model/tinyllama.py:100-103), Q16.16
+    probabilities, INT8 probabilities p * 127 >> 16 rounded half to even and
+    clamped to [0, 127] (quantize_probability_q16_tile, :874-888), i.e. the
+    1/127 probability scale. Returns (prob_q16, prob_q, prob_fp)."""
+    from . import golden as G
+    core = np.clip(np.asarray(scores_i32, np.int64) * np.int64(score_scale_q16), -(1 << 31), (1 << 31) - 1)
+    fp = float_from_q16_16(core)
+    prob = np.stack([G.softmax(r) for r in fp]) if fp.ndim == 2 else G.softmax(fp)
+    prob_q16 = q16_16_signed_array(prob)
+    p = prob_q16.astype(np.int64) * 127
+    r = _round_shift16_half_even(np.abs(p))
+    prob_q = np.clip(np.where(p < 0, -r, r), 0, 127).astype(np.int8)
+    return prob_q16, prob_q, prob.astype(np.float32)
+
+
+def residual_add_i32(residual_q16, update_q16) -> np.ndarray:
+    """Unsaturated INT32 residual add, wrapping modulo 2**32
+    (rtl/compute/residual_add.sv:92-96; build_residual_add_case,
+    model/export_fpga_vectors.py:1522-1540)."""
+    return (np.asarray(residual_q16, np.int64) + np.asarray(update_q16, np.int64)).astype(np.int32)

@@ -234,6 +234,79 @@ def make_analysis(bridge, tmpdir: str):
     np.savez_compressed(HERE / "analysis.npz", **out)
 
 
+def _unpack_row_major(packed: np.ndarray, rows: int, cols: int, lane: int = 32) -> np.ndarray:
+    """Inverse of the exporter's pack_feature_row_major_i32 (chunk-major rows of 32 lanes)."""
+    chunks = (cols + lane - 1) // lane
+    return np.asarray(packed).reshape(chunks, rows, lane).transpose(1, 0, 2).reshape(rows, chunks * lane)[:, :cols]
+
+
+def make_contract_mode(exporter, bridge, ref, tmpdir: str):
+    """The exporter's own fixed-point wrapper cases (phase 5 RMSNorm, softmax,
+    SiLU; phase 6 residual add; model/export_fpga_vectors.py:1522-1990) on
+    seeded synthetic inputs, written to a temporary output root and stored
+    unpacked with the exact Q16.16 scales the exporter derives."""
+    root = Path(tmpdir) / "contract_mode"
+    rng = np.random.default_rng(555)
+    man: list = []
+    q16 = exporter.q16_16_from_float
+    out = {}
+    eps = 1e-5
+    # RMSNorm: a 16-row prefill tile and a 1-row decode row
+    for mode, rows in (("prefill", 16), ("decode", 1)):
+        x = (rng.standard_normal((rows, 2048)) * 0.8).astype(np.float32)
+        gamma = (1.0 + 0.1 * rng.standard_normal(2048)).astype(np.float32)
+        exporter.build_rmsnorm_case(runtime_mode=mode, layer_id=0, block_name="rmsnorm1", block_id=2, x_fp=x,
+                                    gamma_fp=gamma, eps=eps, output_root=root, manifest_entries=man)
+        x_q, s_in = bridge.quantize_int8(x)
+        s_out = bridge.quantize_int8(ref.rms_norm(x_q.astype(np.float32) * s_in, gamma, eps))[1]
+        d = np.load(root / "phase5" / f"phase5_{mode}_layer0_rmsnorm1.npz")
+        np.testing.assert_array_equal(d["x_q"], x_q)
+        out.update({f"rms_{mode}_x_q": x_q, f"rms_{mode}_in_q16": np.uint32(q16(s_in)),
+                    f"rms_{mode}_gamma_q16": np.vectorize(exporter.q16_16_signed_from_float, otypes=[np.int32])(gamma),
+                    f"rms_{mode}_out_q16": np.uint32(q16(s_out)), f"rms_{mode}_y_fp": d["y_fp"],
+                    f"rms_{mode}_y_q": d["y_q"], f"rms_{mode}_y_q16": _unpack_row_major(d["core_y_chunks"], rows, 2048)})
+    out["rms_eps"] = np.float32(eps)
+    # softmax: 8 query rows x 64 keys of INT32 scores, masked like the exporter's tiles
+    for mode, qrows, kcols in (("prefill", 8, 50), ("decode", 1, 64)):
+        score = np.full((exporter.SCORE_ROWS_PER_CHUNK, exporter.SCORE_K_TILE), exporter.MASK_NEG_INF, dtype=np.int32)
+        score[:qrows, :kcols] = rng.integers(-60000, 60000, (qrows, kcols), dtype=np.int32)
+        scale = float(rng.uniform(2e-5, 8e-5))
+        exporter.build_softmax_case(runtime_mode=mode, layer_id=0, q_head_id=0, kv_head_id=0, query_pos_base=0,
+                                    key_pos_base=0, query_row_count=qrows, key_col_count_active=kcols,
+                                    score_masked_tile=score, score_scale=scale, output_root=root, manifest_entries=man)
+        d = np.load(root / "phase5" / f"phase5_{mode}_layer0_softmax_q0_kv0_qb0_kb0.npz")
+        out.update({f"sm_{mode}_score": score, f"sm_{mode}_scale_q16": np.uint32(q16(scale)),
+                    f"sm_{mode}_prob_fp": d["prob_fp"], f"sm_{mode}_prob_q": d["prob_q"],
+                    f"sm_{mode}_prob_q16": np.asarray(d["core_prob_chunks"]).reshape(8, 64),
+                    f"sm_{mode}_rows": np.int64(qrows)})
+    # SiLU on the first 32 columns of a gate projection
+    for mode, rows in (("prefill", 16), ("decode", 1)):
+        g = (rng.standard_normal((rows, 5632)) * 1.5).astype(np.float32)
+        sl = slice(0, rows)
+        exporter.build_silu_case(runtime_mode=mode, layer_id=0, x_fp_full=g, row_slice=sl, output_root=root,
+                                 manifest_entries=man)
+        x_q_full, s_in = bridge.quantize_int8(g)
+        s_in_q16 = q16(s_in)
+        x_deq = np.vectorize(exporter.float_from_q16_16, otypes=[np.float32])(
+            exporter.mul_int8_by_scale_q16(x_q_full, s_in_q16).astype(np.int32))
+        s_out_q16 = q16(bridge.quantize_int8(ref.silu(x_deq))[1])
+        d = np.load(root / "phase5" / f"phase5_{mode}_layer0_silu_gate_m0.npz")
+        np.testing.assert_array_equal(d["x_q"], x_q_full[sl, :32])
+        out.update({f"silu_{mode}_x_q": d["x_q"], f"silu_{mode}_in_q16": np.uint32(s_in_q16),
+                    f"silu_{mode}_out_q16": np.uint32(s_out_q16), f"silu_{mode}_y_fp": d["y_fp"],
+                    f"silu_{mode}_y_q": d["y_q"], f"silu_{mode}_y_q16": _unpack_row_major(d["core_y_chunks"], rows, 32)})
+    # residual add (unsaturated INT32), including sums that wrap
+    res = (rng.standard_normal((16, 2048)) * 3.0).astype(np.float32)
+    upd = (rng.standard_normal((16, 2048)) * 3.0).astype(np.float32)
+    exporter.build_residual_add_case(runtime_mode="prefill", layer_id=0, block_name="residual1", block_id=9,
+                                     residual_fp_full=res, update_fp_full=upd, row_slice=slice(0, 16),
+                                     output_root=root, manifest_entries=man)
+    d = np.load(root / "phase6" / "phase6_prefill_layer0_residual1_m0.npz")
+    out.update(res_a=np.asarray(d["residual_q16"]).reshape(-1)[:512], res_b=np.asarray(d["update_q16"]).reshape(-1)[:512],
+               res_sum=np.asarray(d["sum_q16"]).reshape(-1)[:512])
+    np.savez_compressed(HERE / "contract_mode.npz", **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("TL_REFERENCE_ROOT"),
@@ -252,6 +325,7 @@ def main():
     with tempfile.TemporaryDirectory() as tmp:
         make_small_model(ref, bridge, tmp)
         make_analysis(bridge, tmp)
+        make_contract_mode(exporter, bridge, ref, tmp)
         if not args.skip_config0:
             make_config0(ref, bridge, tmp, args.config0_steps)
     print("fixtures written to", HERE)

@@ -206,3 +206,31 @@ def test_analysis_fixture_float_and_int8_layers(golden):
     np.testing.assert_array_equal(mix_out, d["dump__mixed_layer_out_fp"])
     mae = float(np.abs(mix_out - ref_out).mean())
     assert f"isolated MAE={mae:.6f}" in str(d["summary"][3])
+
+
+def test_contract_mode_wrappers_match_exporter(golden):
+    """oracle/contract.py's fixed-point wrapper chain reproduces the
+    exporter's own RMSNorm / SiLU / softmax / residual-add cases
+    (tests/golden/contract_mode.npz, written by the exporter's build_*_case
+    functions) bit for bit."""
+    from oracle import contract as K
+    d = golden["contract_mode"]
+    for m in ("prefill", "decode"):
+        y16, yq, yfp = K.rmsnorm_contract(d[f"rms_{m}_x_q"], d[f"rms_{m}_in_q16"], d[f"rms_{m}_gamma_q16"],
+                                          float(d["rms_eps"]), d[f"rms_{m}_out_q16"])
+        np.testing.assert_array_equal(yfp, d[f"rms_{m}_y_fp"])
+        np.testing.assert_array_equal(y16, d[f"rms_{m}_y_q16"])
+        np.testing.assert_array_equal(yq, d[f"rms_{m}_y_q"])
+        y16, yq, yfp = K.silu_contract(d[f"silu_{m}_x_q"], d[f"silu_{m}_in_q16"], d[f"silu_{m}_out_q16"])
+        np.testing.assert_array_equal(yfp, d[f"silu_{m}_y_fp"])
+        np.testing.assert_array_equal(y16, d[f"silu_{m}_y_q16"])
+        np.testing.assert_array_equal(yq, d[f"silu_{m}_y_q"])
+        n = int(d[f"sm_{m}_rows"])
+        p16, pq, pfp = K.softmax_contract(d[f"sm_{m}_score"][:n], d[f"sm_{m}_scale_q16"])
+        np.testing.assert_array_equal(pfp, d[f"sm_{m}_prob_fp"][:n])
+        np.testing.assert_array_equal(p16, d[f"sm_{m}_prob_q16"][:n])
+        np.testing.assert_array_equal(pq, d[f"sm_{m}_prob_q"][:n])
+    np.testing.assert_array_equal(K.residual_add_i32(d["res_a"], d["res_b"]), d["res_sum"])
+    big = np.array([2**31 - 5, -2**31 + 3], np.int64)
+    np.testing.assert_array_equal(K.residual_add_i32(big.astype(np.int32), np.array([10, -10], np.int32)),
+                                  np.array([-2**31 + 5, 2**31 - 7], np.int64).astype(np.int32))
