@@ -408,12 +408,16 @@ def run_ours(a, rank, world, local_rank):
         kern = eng.profile_decode_kernels(B, 44)
         names = ["qkv", "attn", "o", "gate_up", "down", "lm_head", "norm_quant_rows", "quant_rows"]
         D, F, V = 2048, 5632, 32000
-        # algorithmic bytes of one gate/up launch at M=B: INT8 weights + fp64
-        # scales + INT8 activations in + fp32 SiLU*up out
+        # algorithmic bytes of the gate/up product of all B rows: INT8 weights +
+        # fp64 scales + INT8 activations in + fp32 SiLU*up out. The step runs it
+        # as two concurrent launches of B/2 rows (two row groups), and
+        # kern[3] times that pair, so the weights count once.
         bytes_gu = 2 * F * D + 2 * F * 8 + B * D + B * F * 4
         gu_ms = float(kern[3])
         achieved = bytes_gu / (gu_ms / 1e3) / 1e9
-        line["roofline"] = {"bound": "hbm", "kernel": "tcgen05 gate/up GEMM + SiLU*up (M=64)", "achieved": achieved,
+        groups = eng.decode_row_groups(B)
+        line["roofline"] = {"bound": "hbm", "kernel": f"tcgen05 gate/up GEMM + SiLU*up, {B} rows as {groups} concurrent "
+                                                      f"launches of {B // groups} rows", "achieved": achieved,
                             "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                             # dram__bytes_read.sum + dram__bytes_write.sum of one launch,
                             # from the ncu capture summarised in ROOFLINE_PROFILE

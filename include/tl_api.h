@@ -356,12 +356,15 @@ TL_API tl_status tl_prefill_batch_device(tl_engine* eng, uint32_t n_seqs, const 
  * span from one prefilled prompt state. Enqueued on the engine stream. */
 TL_API tl_status tl_decode_rewind(tl_engine* eng, uint32_t n_seqs, uint32_t position);
 TL_API tl_status tl_synchronize(tl_engine* eng);
-/* Times each decode-step kernel kind in isolation on the engine stream with
- * CUDA events: [0] QKV projection, [1] attention (+RoPE), [2] O projection +
+/* Times each decode-step kernel kind in isolation with CUDA events on the
+ * engine stream: [0] QKV projection, [1] attention (+RoPE), [2] O projection +
  * residual, [3] gate/up + SiLU*up, [4] down + residual, [5] LM head + argmax,
  * [6] RMSNorm+quantize rows, [7] quantize rows. For n_seqs < 16 the
  * projections are the dp4a GEMVs with the RMSNorm/quantize prologue fused
- * ([6], [7] = 0); for n_seqs >= 16 they are the tcgen05 GEMMs. Each kind runs
+ * ([6], [7] = 0); for n_seqs >= 16 they are the tcgen05 GEMMs, launched as
+ * the decode step launches them: once per row group (two concurrent groups
+ * of n_seqs / 2 rows on two streams for n_seqs >= 32, each group's launches
+ * back to back on its stream), so a time covers all n_seqs rows. Each kind runs
  * `iters` back-to-back launches (no programmatic dependent launch) between
  * one event pair, layers cycled so weights come from HBM as in a real step;
  * the average includes each launch's start-up. The LM head (one matrix) is
@@ -372,6 +375,10 @@ TL_API tl_status tl_profile_decode_kernels(tl_engine* eng, uint32_t n_seqs, uint
                                            float* avg_ms_out);
 /* Number of kernels one decode step of n_seqs rows launches. */
 TL_API int32_t tl_decode_step_kernel_count_rows(tl_engine* eng, uint32_t n_seqs);
+/* Number of concurrent row groups (streams) a decode step of n_seqs rows
+ * runs: 2 for n_seqs >= 32 (TL_DECODE_GROUPS=n overrides, up to 4), else 1;
+ * 0 for a NULL engine. */
+TL_API int32_t tl_decode_row_groups(tl_engine* eng, uint32_t n_seqs);
 /* Number of kernels one decode step launches (for launch accounting). */
 TL_API int32_t tl_decode_step_kernel_count(tl_engine* eng);
 TL_API void* tl_engine_stream(tl_engine* eng);

@@ -1283,7 +1283,8 @@ cudaError_t launch_attn_decode(const AttnDecodeArgs& a0, cudaStream_t s, bool pd
   AttnDecodeArgs a = a0;
   const int G = a.H / a.Hkv;
   if (G < 1 || G > 8 || a.H % a.Hkv || !a.part || !a.counters) return cudaErrorInvalidValue;
-  a.splits = attn_splits(a.M, a.Hkv, a.P);
+  // (a larger split_rows never raises the count: part holds attn_part_floats(M, ...))
+  a.splits = attn_splits(std::max(a.M, a.split_rows), a.Hkv, a.P);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.Hkv, a.M, a.splits);
   cfg.blockDim = dim3(kDecThreads);

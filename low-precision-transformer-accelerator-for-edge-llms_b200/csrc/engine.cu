@@ -173,6 +173,17 @@ struct tl_engine {
   tl_config cfg{};
   int device = 0;
   cudaStream_t stream = nullptr;
+  // The batched decode step runs its rows as independent groups, group i > 0
+  // on side[i - 1] (parallel branches of the step graph). Every kernel of the
+  // step is latency-bound at 64 rows, so two groups of 32 rows in lockstep
+  // keep twice the CTAs in flight, and the second group's weight tiles
+  // mostly come from L2 behind the first's (1.047 vs 1.124 ms per 64-row
+  // step; 3 and 4 groups: 1.161 and 1.336 ms; group 1 started one to seven
+  // kernels behind group 0: 1.07-1.11 ms). TL_DECODE_GROUPS=n overrides.
+  static constexpr int kMaxGroups = 4;
+  cudaStream_t side[kMaxGroups - 1] = {};
+  cudaEvent_t ev_fork = nullptr, ev_join[kMaxGroups - 1] = {};
+  int decode_groups = 2;
   int D = 0, F = 0, H = 0, Hkv = 0, Dq = 0, Dkv = 0, Nqkv = 0, V = 0, L = 0, P = 0, B = 0;
   std::vector<Layer> layers;
   float *embed = nullptr, *gfinal = nullptr, *cosT = nullptr, *sinT = nullptr;
@@ -269,7 +280,7 @@ tl_status alloc_decode(tl_engine* e) {
   TL_TRY(dmalloc(&d.xq, static_cast<size_t>(B) * std::max(e->D, e->F)));
   TL_TRY(dmalloc(&d.amax, B));
   TL_TRY(dmalloc(&d.amax_prod, B));
-  TL_TRY(dmalloc(&d.attn_part, attn_part_floats(B, e->Hkv, e->P)));
+  TL_TRY(dmalloc(&d.attn_part, tl_engine::kMaxGroups * attn_part_floats(B, e->Hkv, e->P)));  // a region per row group
   TL_TRY(dmalloc(&d.attn_cnt, static_cast<size_t>(B) * e->Hkv));
   TL_CU(cudaMemset(d.attn_cnt, 0, static_cast<size_t>(B) * e->Hkv * sizeof(unsigned int)));
   if (e->use_decode1) {
@@ -324,10 +335,10 @@ void invalidate_graphs(tl_engine* e) {
 // One tcgen05 GEMM: out = epi(X[M][K] . W^T[N][K]); plan (tensor maps, tile,
 // split-K) made on the host, so this is also safe inside stream capture.
 tl_status tc_gemm(tl_engine* e, const int8_t* w, int N, const int8_t* x, int M, int K, const TcArgs& args,
-                  bool pdl) {
+                  bool pdl, cudaStream_t s = nullptr) {
   TcPlan p;
   TL_CU(tc_make_plan(&p, w, N, x, M, K, device_sm_count(), args.epi));
-  TL_CU(launch_gemm_tc(p, args, e->stream, pdl));
+  TL_CU(launch_gemm_tc(p, args, s ? s : e->stream, pdl));
   return TL_OK;
 }
 
@@ -398,6 +409,20 @@ tl_status split_gate_up(tl_engine* e, const T* dev, int R, int F, std::vector<T>
   return TL_OK;
 }
 
+// Rows [r0, r0 + M) of the batched decode step, enqueued on stream `s`; the
+// per-row buffers are addressed from row r0, the attention split partials
+// live in the group's own region `attn_part`, and the attention split count
+// is sized for `split_rows` rows (the whole step, when groups run
+// concurrently). `pdl_entry` = false launches the group's first kernel
+// without programmatic serialization (it follows an event, not a kernel).
+struct RowGroup {
+  int r0 = 0, M = 0;
+  cudaStream_t s = nullptr;
+  float* attn_part = nullptr;
+  int split_rows = 0;
+  bool pdl_entry = true;
+};
+
 // Layer l of the batched decode step on the tensor cores (M >= kTcMinRows
 // rows): per row RMSNorm + INT8 quantization kernels feed tcgen05 GEMMs whose
 // epilogues dequantize, add the residual or apply SiLU*up. The attention
@@ -407,127 +432,172 @@ tl_status split_gate_up(tl_engine* e, const T* dev, int R, int F, std::vector<T>
 // (its last reader, the GEMM two kernels back, has completed by then).
 // `cap` (tl_decode_layer) copies the intermediate tensors of the M rows out
 // as they are produced; it is never set inside stream capture.
-tl_status enqueue_decode_layer_tc(tl_engine* e, int l, int M, LayerCap* cap) {
+tl_status enqueue_decode_layer_tc(tl_engine* e, int l, const RowGroup& g, LayerCap* cap) {
   DecodeBufs& d = e->dec;
-  cudaStream_t s = e->stream;
+  cudaStream_t s = g.s;
+  const int M = g.M;
+  const size_t r0 = static_cast<size_t>(g.r0);
   const bool pdl = e->use_pdl && !cap;
   const float eps = e->cfg.rms_norm_eps;
   const tl_layer_capture* hc = cap ? cap->h : nullptr;
   const size_t rowsD = static_cast<size_t>(M) * e->D * sizeof(float);
   const Layer& ly = e->layers[l];
+  float* x = d.x + r0 * e->D;
+  float* qkv = d.qkv + r0 * e->Nqkv;
+  float* att = d.att + r0 * e->Dq;
+  float* hid = d.hid + r0 * e->F;
+  int8_t* xq = d.xq + r0 * std::max(e->D, e->F);
+  float* amax = d.amax + r0;
+  float* amax_prod = d.amax_prod + r0;
   if (hc && hc->attn_input) {
-    TL_CU(launch_rmsnorm_rows(d.x, ly.g1, eps, cap->f32, nullptr, M, e->D, 1, s));
+    TL_CU(launch_rmsnorm_rows(x, ly.g1, eps, cap->f32, nullptr, M, e->D, 1, s));
     TL_TRY(d2h(e, hc->attn_input, cap->f32, rowsD));
   }
-  TL_CU(launch_norm_quant_rows(d.x, ly.g1, eps, M, e->D, d.xq, d.amax, s, pdl, d.amax_prod));
+  TL_CU(launch_norm_quant_rows(x, ly.g1, eps, M, e->D, xq, amax, s, pdl && (l > 0 || g.pdl_entry), amax_prod));
   TcArgs q;
-  q.epi = EPI_F32; q.w_scale = ly.sqkv; q.in_absmax = d.amax; q.rows_per_group = 1; q.out_f32 = d.qkv;
-  TL_TRY(tc_gemm(e, ly.wqkv, e->Nqkv, d.xq, M, e->D, q, pdl));
+  q.epi = EPI_F32; q.w_scale = ly.sqkv; q.in_absmax = amax; q.rows_per_group = 1; q.out_f32 = qkv;
+  TL_TRY(tc_gemm(e, ly.wqkv, e->Nqkv, xq, M, e->D, q, pdl, s));
   if (hc) {
-    TL_TRY(d2h(e, hc->qkv_input_q, d.xq, static_cast<size_t>(M) * e->D));
-    TL_TRY(d2h(e, hc->qkv_input_absmax, d.amax, M * sizeof(float)));
-    TL_TRY(d2h_cols(e, hc->q_proj, d.qkv, M, e->Nqkv, 0, e->Dq));
-    TL_TRY(d2h_cols(e, hc->k_proj, d.qkv, M, e->Nqkv, e->Dq, e->Dkv));
-    TL_TRY(d2h_cols(e, hc->v_proj, d.qkv, M, e->Nqkv, e->Dq + e->Dkv, e->Dkv));
+    TL_TRY(d2h(e, hc->qkv_input_q, xq, static_cast<size_t>(M) * e->D));
+    TL_TRY(d2h(e, hc->qkv_input_absmax, amax, M * sizeof(float)));
+    TL_TRY(d2h_cols(e, hc->q_proj, qkv, M, e->Nqkv, 0, e->Dq));
+    TL_TRY(d2h_cols(e, hc->k_proj, qkv, M, e->Nqkv, e->Dq, e->Dkv));
+    TL_TRY(d2h_cols(e, hc->v_proj, qkv, M, e->Nqkv, e->Dq + e->Dkv, e->Dkv));
     if (hc->q_acc || hc->k_acc || hc->v_acc) {
-      TL_TRY(capture_gemm(e, d.xq, ly.wqkv, ly.sqkv, e->Nqkv, e->D, M, 1, d.amax, EPI_I32, cap->i32));
+      TL_TRY(capture_gemm(e, xq, ly.wqkv, ly.sqkv, e->Nqkv, e->D, M, 1, amax, EPI_I32, cap->i32));
       TL_TRY(d2h_cols(e, hc->q_acc, cap->i32, M, e->Nqkv, 0, e->Dq));
       TL_TRY(d2h_cols(e, hc->k_acc, cap->i32, M, e->Nqkv, e->Dq, e->Dkv));
       TL_TRY(d2h_cols(e, hc->v_acc, cap->i32, M, e->Nqkv, e->Dq + e->Dkv, e->Dkv));
     }
   }
   AttnDecodeArgs at;
-  at.qkv = d.qkv; at.ld = e->Nqkv; at.pos = d.pos; at.slot = d.slots; at.active = d.active;
+  at.qkv = qkv; at.ld = e->Nqkv; at.pos = d.pos + r0; at.slot = d.slots + r0; at.active = d.active + r0;
   at.kc = e->kc; at.vc = e->vc; at.ks = e->ks; at.vs = e->vs;
   at.layer = l; at.L = e->L; at.H = e->H; at.Hkv = e->Hkv; at.P = e->P; at.M = M;
-  at.cos = e->cosT; at.sin = e->sinT; at.out = d.att;
-  at.part = d.attn_part; at.counters = d.attn_cnt; at.out_absmax = d.amax_prod;
+  at.cos = e->cosT; at.sin = e->sinT; at.out = att;
+  at.part = g.attn_part; at.counters = d.attn_cnt + r0 * e->Hkv; at.out_absmax = amax_prod;
+  at.split_rows = g.split_rows;
   TL_CU(launch_attn_decode(at, s, pdl));
-  TL_CU(launch_quant_known_rows(d.att, d.amax_prod, M, e->Dq, d.xq, s, pdl));
+  TL_CU(launch_quant_known_rows(att, amax_prod, M, e->Dq, xq, s, pdl));
   if (hc) {
-    TL_TRY(d2h(e, hc->attended, d.att, static_cast<size_t>(M) * e->Dq * sizeof(float)));
-    TL_TRY(d2h(e, hc->o_input_q, d.xq, static_cast<size_t>(M) * e->Dq));
-    TL_TRY(d2h(e, hc->o_input_absmax, d.amax_prod, M * sizeof(float)));
+    TL_TRY(d2h(e, hc->attended, att, static_cast<size_t>(M) * e->Dq * sizeof(float)));
+    TL_TRY(d2h(e, hc->o_input_q, xq, static_cast<size_t>(M) * e->Dq));
+    TL_TRY(d2h(e, hc->o_input_absmax, amax_prod, M * sizeof(float)));
     if (hc->o_acc) {
-      TL_TRY(capture_gemm(e, d.xq, ly.wo, ly.so, e->D, e->Dq, M, 1, d.amax_prod, EPI_I32, cap->i32));
+      TL_TRY(capture_gemm(e, xq, ly.wo, ly.so, e->D, e->Dq, M, 1, amax_prod, EPI_I32, cap->i32));
       TL_TRY(d2h(e, hc->o_acc, cap->i32, static_cast<size_t>(M) * e->D * 4));
     }
     if (hc->o_proj) {
-      TL_TRY(capture_gemm(e, d.xq, ly.wo, ly.so, e->D, e->Dq, M, 1, d.amax_prod, EPI_F32, cap->i32));
+      TL_TRY(capture_gemm(e, xq, ly.wo, ly.so, e->D, e->Dq, M, 1, amax_prod, EPI_F32, cap->i32));
       TL_TRY(d2h(e, hc->o_proj, cap->i32, static_cast<size_t>(M) * e->D * 4));
     }
   }
   TcArgs o;
-  o.epi = EPI_RESID; o.w_scale = ly.so; o.in_absmax = d.amax_prod; o.rows_per_group = 1; o.out_f32 = d.x;
-  o.resid = d.x;
-  TL_TRY(tc_gemm(e, ly.wo, e->D, d.xq, M, e->Dq, o, pdl));
-  if (hc) TL_TRY(d2h(e, hc->x_after_attn, d.x, rowsD));
+  o.epi = EPI_RESID; o.w_scale = ly.so; o.in_absmax = amax_prod; o.rows_per_group = 1; o.out_f32 = x;
+  o.resid = x;
+  TL_TRY(tc_gemm(e, ly.wo, e->D, xq, M, e->Dq, o, pdl, s));
+  if (hc) TL_TRY(d2h(e, hc->x_after_attn, x, rowsD));
   if (hc && hc->ffn_input) {
-    TL_CU(launch_rmsnorm_rows(d.x, ly.g2, eps, cap->f32, nullptr, M, e->D, 1, s));
+    TL_CU(launch_rmsnorm_rows(x, ly.g2, eps, cap->f32, nullptr, M, e->D, 1, s));
     TL_TRY(d2h(e, hc->ffn_input, cap->f32, rowsD));
   }
-  TL_CU(launch_norm_quant_rows(d.x, ly.g2, eps, M, e->D, d.xq, d.amax, s, pdl, d.amax_prod));
+  TL_CU(launch_norm_quant_rows(x, ly.g2, eps, M, e->D, xq, amax, s, pdl, amax_prod));
   TcArgs gu;
-  gu.epi = EPI_SILU; gu.w_scale = ly.sgu; gu.in_absmax = d.amax; gu.rows_per_group = 1; gu.out_f32 = d.hid;
-  gu.out_absmax = d.amax_prod;
-  TL_TRY(tc_gemm(e, ly.wgu, 2 * e->F, d.xq, M, e->D, gu, pdl));
+  gu.epi = EPI_SILU; gu.w_scale = ly.sgu; gu.in_absmax = amax; gu.rows_per_group = 1; gu.out_f32 = hid;
+  gu.out_absmax = amax_prod;
+  TL_TRY(tc_gemm(e, ly.wgu, 2 * e->F, xq, M, e->D, gu, pdl, s));
   if (hc) {
-    TL_TRY(d2h(e, hc->gate_up_input_q, d.xq, static_cast<size_t>(M) * e->D));
-    TL_TRY(d2h(e, hc->gate_up_input_absmax, d.amax, M * sizeof(float)));
+    TL_TRY(d2h(e, hc->gate_up_input_q, xq, static_cast<size_t>(M) * e->D));
+    TL_TRY(d2h(e, hc->gate_up_input_absmax, amax, M * sizeof(float)));
     if (hc->gate_acc || hc->up_acc) {
-      TL_TRY(capture_gemm(e, d.xq, ly.wgu, ly.sgu, 2 * e->F, e->D, M, 1, d.amax, EPI_I32, cap->i32));
+      TL_TRY(capture_gemm(e, xq, ly.wgu, ly.sgu, 2 * e->F, e->D, M, 1, amax, EPI_I32, cap->i32));
       TL_TRY(split_gate_up(e, cap->i32, M, e->F, cap->tmp_i, hc->gate_acc, hc->up_acc));
     }
     if (hc->gate_proj || hc->up_proj) {
-      TL_TRY(capture_gemm(e, d.xq, ly.wgu, ly.sgu, 2 * e->F, e->D, M, 1, d.amax, EPI_F32, cap->f32));
+      TL_TRY(capture_gemm(e, xq, ly.wgu, ly.sgu, 2 * e->F, e->D, M, 1, amax, EPI_F32, cap->f32));
       TL_TRY(split_gate_up(e, static_cast<const float*>(cap->f32), M, e->F, cap->tmp_f, hc->gate_proj,
                            hc->up_proj));
     }
   }
-  TL_CU(launch_quant_known_rows(d.hid, d.amax_prod, M, e->F, d.xq, s, pdl));
+  TL_CU(launch_quant_known_rows(hid, amax_prod, M, e->F, xq, s, pdl));
   if (hc) {
-    TL_TRY(d2h(e, hc->hidden, d.hid, static_cast<size_t>(M) * e->F * sizeof(float)));
-    TL_TRY(d2h(e, hc->down_input_q, d.xq, static_cast<size_t>(M) * e->F));
-    TL_TRY(d2h(e, hc->down_input_absmax, d.amax_prod, M * sizeof(float)));
+    TL_TRY(d2h(e, hc->hidden, hid, static_cast<size_t>(M) * e->F * sizeof(float)));
+    TL_TRY(d2h(e, hc->down_input_q, xq, static_cast<size_t>(M) * e->F));
+    TL_TRY(d2h(e, hc->down_input_absmax, amax_prod, M * sizeof(float)));
     if (hc->down_acc) {
-      TL_TRY(capture_gemm(e, d.xq, ly.wd, ly.sd, e->D, e->F, M, 1, d.amax_prod, EPI_I32, cap->i32));
+      TL_TRY(capture_gemm(e, xq, ly.wd, ly.sd, e->D, e->F, M, 1, amax_prod, EPI_I32, cap->i32));
       TL_TRY(d2h(e, hc->down_acc, cap->i32, static_cast<size_t>(M) * e->D * 4));
     }
     if (hc->down_proj) {
-      TL_TRY(capture_gemm(e, d.xq, ly.wd, ly.sd, e->D, e->F, M, 1, d.amax_prod, EPI_F32, cap->i32));
+      TL_TRY(capture_gemm(e, xq, ly.wd, ly.sd, e->D, e->F, M, 1, amax_prod, EPI_F32, cap->i32));
       TL_TRY(d2h(e, hc->down_proj, cap->i32, static_cast<size_t>(M) * e->D * 4));
     }
   }
   TcArgs dn;
-  dn.epi = EPI_RESID; dn.w_scale = ly.sd; dn.in_absmax = d.amax_prod; dn.rows_per_group = 1; dn.out_f32 = d.x;
-  dn.resid = d.x;
-  TL_TRY(tc_gemm(e, ly.wd, e->D, d.xq, M, e->F, dn, pdl));
+  dn.epi = EPI_RESID; dn.w_scale = ly.sd; dn.in_absmax = amax_prod; dn.rows_per_group = 1; dn.out_f32 = x;
+  dn.resid = x;
+  TL_TRY(tc_gemm(e, ly.wd, e->D, xq, M, e->F, dn, pdl, s));
   return TL_OK;
 }
 
-// Batched decode step on the tensor cores (M >= kTcMinRows rows).
+// Row groups of a batched decode step of M rows: up to decode_groups
+// concurrent groups of about equal size, each of at least kTcMinRows rows
+// (one group on the engine stream when M is smaller).
+int decode_row_groups(const tl_engine* e, int M, RowGroup* g) {
+  const size_t region = attn_part_floats(e->B, e->Hkv, e->P);
+  const int ng = std::max(1, std::min(e->decode_groups, M / kTcMinRows));
+  int r = 0;
+  for (int i = 0; i < ng; ++i) {
+    const int rows = (M - r) / (ng - i);
+    g[i].r0 = r; g[i].M = rows; g[i].s = i == 0 ? e->stream : e->side[i - 1];
+    g[i].attn_part = e->dec.attn_part + i * region; g[i].split_rows = M; g[i].pdl_entry = i == 0;
+    r += rows;
+  }
+  return ng;
+}
+
+// Batched decode step on the tensor cores (M >= kTcMinRows rows): embedding
+// on the engine stream, then each row group's layers, final RMSNorm and
+// LM head (fused argmax) on its own stream, joined before the finalize.
 tl_status enqueue_decode_step_tc(tl_engine* e, int M, bool finalize) {
   DecodeBufs& d = e->dec;
   cudaStream_t s = e->stream;
   const bool pdl = e->use_pdl;
   const float eps = e->cfg.rms_norm_eps;
   TL_CU(launch_embed(e->embed, d.tokens, d.x, M, e->D, e->V, s, pdl));
-  for (int l = 0; l < e->L; ++l) TL_TRY(enqueue_decode_layer_tc(e, l, M, nullptr));
-  TL_CU(launch_norm_quant_rows(d.x, e->gfinal, eps, M, e->D, d.xq, d.amax, s, pdl));
-  // LM head with the greedy argmax fused into the epilogue (packed keys in
-  // d.am_key, consumed and re-armed by step_finalize / keys_to_tokens); the
-  // logits themselves are not written
-  TcArgs lm;
-  lm.epi = EPI_F32; lm.w_scale = e->slm; lm.in_absmax = d.amax; lm.rows_per_group = 1; lm.out_f32 = nullptr;
-  lm.am_key = d.am_key;
-  TL_TRY(tc_gemm(e, e->wlm, e->V, d.xq, M, e->D, lm, pdl));
+  RowGroup grp[tl_engine::kMaxGroups];
+  const int ng = decode_row_groups(e, M, grp);
+  if (ng > 1) {
+    TL_CU(cudaEventRecord(e->ev_fork, s));
+    for (int i = 1; i < ng; ++i) TL_CU(cudaStreamWaitEvent(grp[i].s, e->ev_fork, 0));
+  }
+  for (int l = 0; l < e->L; ++l)
+    for (int i = 0; i < ng; ++i) TL_TRY(enqueue_decode_layer_tc(e, l, grp[i], nullptr));
+  for (int i = 0; i < ng; ++i) {
+    const RowGroup& g = grp[i];
+    const size_t r0 = static_cast<size_t>(g.r0);
+    int8_t* xq = d.xq + r0 * std::max(e->D, e->F);
+    TL_CU(launch_norm_quant_rows(d.x + r0 * e->D, e->gfinal, eps, g.M, e->D, xq, d.amax + r0, g.s, pdl));
+    // LM head with the greedy argmax fused into the epilogue (packed keys in
+    // d.am_key, consumed and re-armed by step_finalize / keys_to_tokens); the
+    // logits themselves are not written
+    TcArgs lm;
+    lm.epi = EPI_F32; lm.w_scale = e->slm; lm.in_absmax = d.amax + r0; lm.rows_per_group = 1; lm.out_f32 = nullptr;
+    lm.am_key = d.am_key + r0;
+    TL_TRY(tc_gemm(e, e->wlm, e->V, xq, g.M, e->D, lm, pdl, g.s));
+  }
+  for (int i = 1; i < ng; ++i) {
+    TL_CU(cudaEventRecord(e->ev_join[i - 1], grp[i].s));
+    TL_CU(cudaStreamWaitEvent(s, e->ev_join[i - 1], 0));
+  }
+  const bool pdl_tail = pdl && ng == 1;  // after the join the predecessor is an event
   if (!finalize) TL_CU(launch_keys_to_tokens(d.am_key, d.argmax, M, s));
   if (finalize) {
     StepArgs st;
     st.M = M; st.am_key = d.am_key; st.tokens = d.tokens; st.pos = d.pos; st.active = d.active;
     st.count = d.count; st.stop = d.stop; st.out_ids = d.out_ids; st.out_stride = e->P;
     st.run = d.run; st.P = e->P;
-    TL_CU(launch_step_finalize(st, s, pdl));
+    TL_CU(launch_step_finalize(st, s, pdl_tail));
   }
   return TL_OK;
 }
@@ -1125,7 +1195,14 @@ tl_status create_engine(const tl_config* cfg, int32_t device, int rank, int worl
   }
   cudaError_t ce = prepare_kernels(std::max(e->F, e->D));
   if (ce == cudaSuccess) ce = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
+  for (int i = 0; i < tl_engine::kMaxGroups - 1 && ce == cudaSuccess; ++i) {
+    ce = cudaStreamCreateWithFlags(&e->side[i], cudaStreamNonBlocking);
+    if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&e->ev_join[i], cudaEventDisableTiming);
+  }
+  if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&e->ev_fork, cudaEventDisableTiming);
   if (ce != cudaSuccess) { g_last_error = cudaGetErrorString(ce); return fail(TL_ERR_CUDA); }
+  if (const char* v = std::getenv("TL_DECODE_GROUPS"))
+    e->decode_groups = std::max(1, std::min(tl_engine::kMaxGroups, std::atoi(v)));
   e->layers.resize(e->L);
   for (auto& ly : e->layers) {
     tl_status s;
@@ -1238,6 +1315,11 @@ tl_status tl_destroy(tl_engine* e) {
   cudaFree(e->logits_all);
   if (e->h_pinned) cudaFreeHost(e->h_pinned);
   if (e->stream) cudaStreamDestroy(e->stream);
+  for (int i = 0; i < tl_engine::kMaxGroups - 1; ++i) {
+    if (e->side[i]) cudaStreamDestroy(e->side[i]);
+    if (e->ev_join[i]) cudaEventDestroy(e->ev_join[i]);
+  }
+  if (e->ev_fork) cudaEventDestroy(e->ev_fork);
   delete e;
   return TL_OK;
 }
@@ -1665,7 +1747,9 @@ tl_status tl_decode_layer(tl_engine* e, uint32_t layer, uint32_t n, const uint32
     TL_CU(cudaMemcpyAsync(d.pos, h + M, M * sizeof(int), cudaMemcpyHostToDevice, s));
     TL_CU(cudaMemcpyAsync(d.active, h + 2 * M, M * sizeof(int), cudaMemcpyHostToDevice, s));
     TL_CU(cudaMemcpyAsync(d.x, x, rowsD, cudaMemcpyHostToDevice, s));
-    TL_TRY(enqueue_decode_layer_tc(e, static_cast<int>(layer), M, cap ? &lc : nullptr));
+    RowGroup g;
+    g.M = M; g.s = s; g.attn_part = d.attn_part; g.split_rows = M;
+    TL_TRY(enqueue_decode_layer_tc(e, static_cast<int>(layer), g, cap ? &lc : nullptr));
     if (out) TL_CU(cudaMemcpyAsync(out, d.x, rowsD, cudaMemcpyDeviceToHost, s));
     TL_CU(cudaStreamSynchronize(s));
     return tl_device_error();
@@ -1861,6 +1945,15 @@ tl_status tl_profile_decode_kernels(tl_engine* e, uint32_t n_seqs, uint32_t iter
   const bool tc = M >= kTcMinRows;
   DecodeBufs& d = e->dec;
   cudaStream_t s = e->stream;
+  // each kind is launched as the step launches it: once per row group, the
+  // groups concurrently on their streams (one group below kTcMinRows rows)
+  RowGroup grp[tl_engine::kMaxGroups];
+  int ng = 1;
+  if (tc) {
+    ng = decode_row_groups(e, M, grp);
+  } else {
+    grp[0].M = M; grp[0].s = s; grp[0].attn_part = d.attn_part; grp[0].split_rows = M;
+  }
   const size_t flush_bytes = 256ull << 20;
   void* flush = nullptr;
   TL_CU(cudaMallocAsync(&flush, flush_bytes, s));
@@ -1868,6 +1961,7 @@ tl_status tl_profile_decode_kernels(tl_engine* e, uint32_t n_seqs, uint32_t iter
   for (auto& x : ev) TL_CU(cudaEventCreate(&x));
   tl_status result = TL_OK;
   const float eps = e->cfg.rms_norm_eps;
+  const size_t xq_ld = static_cast<size_t>(std::max(e->D, e->F));
   for (int kind = 0; kind < 8 && result == TL_OK; ++kind) {
     if (!tc && kind >= 6) {
       avg_ms_out[kind] = 0.0f;
@@ -1882,94 +1976,115 @@ tl_status tl_profile_decode_kernels(tl_engine* e, uint32_t n_seqs, uint32_t iter
       const bool per_launch = kind == 5;
       if (per_launch) TL_CU(cudaMemsetAsync(flush, it & 0xff, flush_bytes, s));
       if (per_launch || it == 0) TL_CU(cudaEventRecord(ev[2 * it], s));
-      cudaError_t ce = cudaSuccess;
-      tl_status ts = TL_OK;
-      GemvArgs g;
-      g.M = M;
-      g.eps = eps;
-      TcArgs t;
-      t.in_absmax = d.amax;
-      t.rows_per_group = 1;
-      switch (kind) {
-        case 0:
-          if (tc) {
-            t.epi = EPI_F32; t.w_scale = ly.sqkv; t.out_f32 = d.qkv;
-            ts = tc_gemm(e, ly.wqkv, e->Nqkv, d.xq, M, e->D, t, false);
-          } else {
-            g.x_f32 = d.x; g.gamma = ly.g1; g.w = ly.wqkv; g.w_scale = ly.sqkv; g.N = e->Nqkv; g.K = e->D;
-            g.out_f32 = d.qkv;
-            ce = launch_gemv(PRO_NORM, EPI_F32, g, s, false);
+      // the groups fork once per timed interval: per launch for the LM head,
+      // around all iters back-to-back launches of each group otherwise
+      const bool fork = per_launch || it == 0, join = per_launch || it + 1 == iters;
+      if (ng > 1 && fork) {
+        TL_CU(cudaEventRecord(e->ev_fork, s));
+        for (int i = 1; i < ng; ++i) TL_CU(cudaStreamWaitEvent(grp[i].s, e->ev_fork, 0));
+      }
+      for (int gi = 0; gi < ng && result == TL_OK; ++gi) {
+        const RowGroup& rg = grp[gi];
+        const size_t r0 = static_cast<size_t>(rg.r0);
+        const int Mg = rg.M;
+        cudaStream_t gs = rg.s;
+        float* x = d.x + r0 * e->D;
+        float* qkv = d.qkv + r0 * e->Nqkv;
+        float* att = d.att + r0 * e->Dq;
+        float* hid = d.hid + r0 * e->F;
+        int8_t* xq = d.xq + r0 * xq_ld;
+        float* amax = d.amax + r0;
+        cudaError_t ce = cudaSuccess;
+        tl_status ts = TL_OK;
+        GemvArgs g;
+        g.M = Mg;
+        g.eps = eps;
+        TcArgs t;
+        t.in_absmax = amax;
+        t.rows_per_group = 1;
+        switch (kind) {
+          case 0:
+            if (tc) {
+              t.epi = EPI_F32; t.w_scale = ly.sqkv; t.out_f32 = qkv;
+              ts = tc_gemm(e, ly.wqkv, e->Nqkv, xq, Mg, e->D, t, false, gs);
+            } else {
+              g.x_f32 = x; g.gamma = ly.g1; g.w = ly.wqkv; g.w_scale = ly.sqkv; g.N = e->Nqkv; g.K = e->D;
+              g.out_f32 = qkv;
+              ce = launch_gemv(PRO_NORM, EPI_F32, g, gs, false);
+            }
+            break;
+          case 1: {
+            AttnDecodeArgs at;
+            at.qkv = qkv; at.ld = e->Nqkv; at.pos = d.pos + r0; at.slot = d.slots + r0;
+            at.kc = e->kc; at.vc = e->vc; at.ks = e->ks; at.vs = e->vs; at.layer = l; at.L = e->L;
+            at.H = e->H; at.Hkv = e->Hkv; at.P = e->P; at.M = Mg; at.cos = e->cosT; at.sin = e->sinT;
+            at.out = att;
+            at.part = rg.attn_part; at.counters = d.attn_cnt + r0 * e->Hkv; at.split_rows = rg.split_rows;
+            at.active = d.stop + r0;  // stop[] is 0 for running rows: read side only, no KV append
+            ce = launch_attn_decode(at, gs, false);
+            break;
           }
-          break;
-        case 1: {
-          AttnDecodeArgs at;
-          at.qkv = d.qkv; at.ld = e->Nqkv; at.pos = d.pos; at.slot = d.slots;
-          at.kc = e->kc; at.vc = e->vc; at.ks = e->ks; at.vs = e->vs; at.layer = l; at.L = e->L;
-          at.H = e->H; at.Hkv = e->Hkv; at.P = e->P; at.M = M; at.cos = e->cosT; at.sin = e->sinT;
-          at.out = d.att;
-          at.part = d.attn_part; at.counters = d.attn_cnt;
-          at.active = d.stop;  // stop[] is 0 for running rows: read side only, no KV append
-          ce = launch_attn_decode(at, s, false);
-          break;
+          case 2:
+            if (tc) {
+              t.epi = EPI_RESID; t.w_scale = ly.so; t.out_f32 = hid; t.resid = hid;
+              ts = tc_gemm(e, ly.wo, e->D, xq, Mg, e->Dq, t, false, gs);
+            } else {
+              g.x_f32 = att; g.w = ly.wo; g.w_scale = ly.so; g.N = e->D; g.K = e->Dq; g.out_f32 = hid;
+              g.resid = hid;
+              ce = launch_gemv(PRO_F32, EPI_RESID, g, gs, false);
+            }
+            break;
+          case 3:
+            if (tc) {
+              t.epi = EPI_SILU; t.w_scale = ly.sgu; t.out_f32 = hid;
+              ts = tc_gemm(e, ly.wgu, 2 * e->F, xq, Mg, e->D, t, false, gs);
+            } else {
+              g.x_f32 = x; g.gamma = ly.g2; g.w = ly.wgu; g.w_scale = ly.sgu; g.N = 2 * e->F; g.K = e->D;
+              g.out_f32 = hid;
+              ce = launch_gemv(PRO_NORM, EPI_SILU, g, gs, false);
+            }
+            break;
+          case 4:
+            if (tc) {
+              t.epi = EPI_RESID; t.w_scale = ly.sd; t.out_f32 = att; t.resid = att;
+              ts = tc_gemm(e, ly.wd, e->D, xq, Mg, e->F, t, false, gs);
+            } else {
+              g.x_f32 = hid; g.w = ly.wd; g.w_scale = ly.sd; g.N = e->D; g.K = e->F; g.out_f32 = att;
+              g.resid = att;
+              ce = launch_gemv(PRO_F32, EPI_RESID, g, gs, false);
+            }
+            break;
+          case 5:
+            if (tc) {
+              t.epi = EPI_F32; t.w_scale = e->slm; t.out_f32 = nullptr; t.am_key = d.am_key + r0;
+              ts = tc_gemm(e, e->wlm, e->V, xq, Mg, e->D, t, false, gs);
+            } else {
+              g.x_f32 = x; g.gamma = e->gfinal; g.w = e->wlm; g.w_scale = e->slm; g.N = e->V; g.K = e->D;
+              g.am_partial = d.am_partial; g.am_counter = d.am_counter; g.am_token = d.argmax;
+              ce = launch_gemv(PRO_NORM, EPI_ARGMAX, g, gs, false);
+            }
+            break;
+          case 6:
+            ce = launch_norm_quant_rows(x, ly.g1, eps, Mg, e->D, xq, amax, gs, false);
+            break;
+          case 7:
+            ce = tc ? launch_quant_known_rows(hid, amax, Mg, e->F, xq, gs, false)
+                    : launch_quant_rows(hid, Mg, e->F, xq, amax, gs, false);
+            break;
         }
-        case 2:
-          if (tc) {
-            t.epi = EPI_RESID; t.w_scale = ly.so; t.out_f32 = d.hid; t.resid = d.hid;
-            ts = tc_gemm(e, ly.wo, e->D, d.xq, M, e->Dq, t, false);
-          } else {
-            g.x_f32 = d.att; g.w = ly.wo; g.w_scale = ly.so; g.N = e->D; g.K = e->Dq; g.out_f32 = d.hid;
-            g.resid = d.hid;
-            ce = launch_gemv(PRO_F32, EPI_RESID, g, s, false);
-          }
-          break;
-        case 3:
-          if (tc) {
-            t.epi = EPI_SILU; t.w_scale = ly.sgu; t.out_f32 = d.hid;
-            ts = tc_gemm(e, ly.wgu, 2 * e->F, d.xq, M, e->D, t, false);
-          } else {
-            g.x_f32 = d.x; g.gamma = ly.g2; g.w = ly.wgu; g.w_scale = ly.sgu; g.N = 2 * e->F; g.K = e->D;
-            g.out_f32 = d.hid;
-            ce = launch_gemv(PRO_NORM, EPI_SILU, g, s, false);
-          }
-          break;
-        case 4:
-          if (tc) {
-            t.epi = EPI_RESID; t.w_scale = ly.sd; t.out_f32 = d.att; t.resid = d.att;
-            ts = tc_gemm(e, ly.wd, e->D, d.xq, M, e->F, t, false);
-          } else {
-            g.x_f32 = d.hid; g.w = ly.wd; g.w_scale = ly.sd; g.N = e->D; g.K = e->F; g.out_f32 = d.att;
-            g.resid = d.att;
-            ce = launch_gemv(PRO_F32, EPI_RESID, g, s, false);
-          }
-          break;
-        case 5:
-          if (tc) {
-            t.epi = EPI_F32; t.w_scale = e->slm; t.out_f32 = nullptr; t.am_key = d.am_key;
-            ts = tc_gemm(e, e->wlm, e->V, d.xq, M, e->D, t, false);
-          } else {
-            g.x_f32 = d.x; g.gamma = e->gfinal; g.w = e->wlm; g.w_scale = e->slm; g.N = e->V; g.K = e->D;
-            g.am_partial = d.am_partial; g.am_counter = d.am_counter; g.am_token = d.argmax;
-            ce = launch_gemv(PRO_NORM, EPI_ARGMAX, g, s, false);
-          }
-          break;
-        case 6:
-          ce = launch_norm_quant_rows(d.x, ly.g1, eps, M, e->D, d.xq, d.amax, s, false);
-          break;
-        case 7:
-          ce = tc ? launch_quant_known_rows(d.hid, d.amax, M, e->F, d.xq, s, false)
-                  : launch_quant_rows(d.hid, M, e->F, d.xq, d.amax, s, false);
-          break;
+        if (ce != cudaSuccess) {
+          g_last_error = cudaGetErrorString(ce);
+          result = TL_ERR_CUDA;
+        } else if (ts != TL_OK) {
+          result = ts;
+        }
       }
-      if (ce != cudaSuccess) {
-        g_last_error = cudaGetErrorString(ce);
-        result = TL_ERR_CUDA;
-        break;
+      for (int i = 1; i < ng && (join || result != TL_OK); ++i) {
+        TL_CU(cudaEventRecord(e->ev_join[i - 1], grp[i].s));
+        TL_CU(cudaStreamWaitEvent(s, e->ev_join[i - 1], 0));
       }
-      if (ts != TL_OK) {
-        result = ts;
-        break;
-      }
-      if (per_launch || it + 1 == iters) TL_CU(cudaEventRecord(ev[2 * it + 1], s));
+      if (result != TL_OK) break;
+      if (join) TL_CU(cudaEventRecord(ev[2 * it + 1], s));
     }
     if (result != TL_OK) break;
     TL_CU(cudaStreamSynchronize(s));
@@ -1988,6 +2103,8 @@ tl_status tl_profile_decode_kernels(tl_engine* e, uint32_t n_seqs, uint32_t iter
     avg_ms_out[kind] = static_cast<float>(tot / iters);
   }
   for (auto& x : ev) cudaEventDestroy(x);
+  cudaStreamSynchronize(s);
+  for (int i = 1; i < ng; ++i) cudaStreamSynchronize(grp[i].s);
   cudaFreeAsync(flush, s);
   // the LM-head timing accumulated argmax keys: re-arm them for the next step
   if (tc) cudaMemsetAsync(d.am_key, 0, static_cast<size_t>(e->B) * sizeof(unsigned long long), s);
@@ -1999,10 +2116,21 @@ int32_t tl_decode_step_kernel_count(tl_engine* e) { return tl_decode_step_kernel
 
 int32_t tl_decode_step_kernel_count_rows(tl_engine* e, uint32_t n_seqs) {
   if (!e) return 0;
-  // embed, 9 per layer, final norm, LM head with fused argmax, finalize
-  if (static_cast<int>(n_seqs) >= kTcMinRows) return 1 + 9 * e->L + 3;
+  // embed, per row group 9 per layer + final norm + LM head with fused
+  // argmax, finalize
+  if (static_cast<int>(n_seqs) >= kTcMinRows) {
+    RowGroup g[tl_engine::kMaxGroups];
+    return 1 + decode_row_groups(e, static_cast<int>(n_seqs), g) * (9 * e->L + 2) + 1;
+  }
   if (n_seqs == 1 && e->use_decode1) return 2;  // persistent step + finalize
   return 1 + 5 * e->L + 2;
+}
+
+int32_t tl_decode_row_groups(tl_engine* e, uint32_t n_seqs) {
+  if (!e) return 0;
+  if (static_cast<int>(n_seqs) < kTcMinRows) return 1;
+  RowGroup g[tl_engine::kMaxGroups];
+  return decode_row_groups(e, static_cast<int>(n_seqs), g);
 }
 
 void* tl_engine_stream(tl_engine* e) { return e ? static_cast<void*>(e->stream) : nullptr; }

@@ -174,6 +174,7 @@ struct AttnDecodeArgs {
   unsigned int* counters = nullptr;  // [M][Hkv], zero on entry and on exit
   int splits = 0;               // set by the launcher
   float* out_absmax = nullptr;  // [M] optional: atomic max of |out| per row (zero on entry)
+  int split_rows = 0;           // rows the context split count is sized for (0: M)
 };
 constexpr int kAttnPartStride = 8 * 66;  // per split: 8 heads x (max, sum, 64 values)
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);

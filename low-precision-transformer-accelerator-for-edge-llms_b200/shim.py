@@ -52,7 +52,7 @@ EXPORTS = (
     "tl_init_random_weights", "tl_generate", "tl_generate_batch", "tl_abort",
     "tl_prefill_logits", "tl_decode_logits", "tl_read_kv", "tl_get_position",
     "tl_decode_steps_device", "tl_prefill_batch_device", "tl_decode_rewind", "tl_synchronize",
-    "tl_decode_step_kernel_count", "tl_decode_step_kernel_count_rows", "tl_engine_stream", "tl_profile_decode_kernels", "tl_device_error",
+    "tl_decode_step_kernel_count", "tl_decode_step_kernel_count_rows", "tl_decode_row_groups", "tl_engine_stream", "tl_profile_decode_kernels", "tl_device_error",
     "tl_transpose_i8", "tl_quantize_int8",
     "tl_gemm_i8", "tl_gemm_i8_requant", "tl_quantized_linear", "tl_rmsnorm", "tl_lmhead_argmax",
     "tl_attn_decode", "tl_attn_prefill", "tl_lmhead_argmax_noalloc",
@@ -175,6 +175,7 @@ def load_library(path: Path | str | None = None):
         "tl_synchronize": (i32, [vp]),
         "tl_decode_step_kernel_count": (i32, [vp]),
         "tl_decode_step_kernel_count_rows": (i32, [vp, u32]),
+        "tl_decode_row_groups": (i32, [vp, u32]),
         "tl_engine_stream": (vp, [vp]),
         "tl_profile_decode_kernels": (i32, [vp, u32, u32, vp]),
         "tl_device_error": (i32, []),
@@ -687,6 +688,10 @@ class Engine:
 
     def decode_step_kernel_count(self, n_seqs: int = 1) -> int:
         return int(self.lib.tl_decode_step_kernel_count_rows(self.h, n_seqs))
+
+    def decode_row_groups(self, n_seqs: int) -> int:
+        """Concurrent row groups (streams) of a decode step of n_seqs rows."""
+        return int(self.lib.tl_decode_row_groups(self.h, n_seqs))
 
 
 # --------------------------------------------------------------------------

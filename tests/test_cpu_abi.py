@@ -41,6 +41,7 @@ def test_null_arguments_are_errors_not_crashes(pkg):
     assert lib.tl_destroy(None) == 0
     assert lib.tl_abort(None) == 16
     assert lib.tl_decode_step_kernel_count(None) == 0
+    assert lib.tl_decode_row_groups(None, 64) == 0
 
 
 def test_bad_config_rejected(pkg):
