@@ -518,22 +518,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // CTAs in flight share token tiles in L2). Roles: warp 0 lane 0 streams A/B
 // k-blocks through a 4-stage ring (48 KB a stage) across tile boundaries;
 // warp 1 lane 0 issues the MMAs of tile i into TMEM accumulator i % 2 (two
-// 256-column buffers, all 512 columns); warps 2..13 drain accumulator i % 2
+// 256-column buffers, all 512 columns); warps 2.. drain accumulator i % 2
 // while tile i + 1 accumulates in the other, so the epilogue runs under the
 // main loop instead of after it. Epilogue warp w reads TMEM lanes
 // 32 (w % 4) .. + 31 (the lanes its warp rank may access) and token chunks
-// [16 p / 3, 16 (p + 1) / 3) of 16 tokens, p = (w - 2) / 4 (three warps per
-// lane quarter). Handshakes: acc_full[b] (MMA commit -> epilogue),
-// acc_empty[b] (12 epilogue-warp arrivals -> MMA).
-constexpr int kPEpiWarps = 12;
-constexpr int kPParts = kPEpiWarps / 4;  // epilogue warps per TMEM lane quarter
-constexpr int kPThreads = 32 * (2 + kPEpiWarps);
+// [16 p / P, 16 (p + 1) / P) of 16 tokens, p = (w - 2) / 4, with P epilogue
+// warps per lane quarter. Handshakes: acc_full[b] (MMA commit -> epilogue),
+// acc_empty[b] (one arrival per epilogue warp -> MMA).
+// Epilogue warps per epilogue kind: 16 (four per TMEM lane quarter, four
+// 16-token chunks each) keep the SiLU*up and float epilogues ahead of the
+// MMAs (prefill 8 x 2048: 39.6 vs 40.9 ms with 12); the residual epilogue
+// keeps 12, where 16 would spill its prefetched residual registers.
+template <int EPI>
+__host__ __device__ constexpr int tcp_epi_warps() { return EPI == EPI_RESID ? 12 : 16; }
+template <int EPI>
+__host__ __device__ constexpr int tcp_threads() { return 32 * (2 + tcp_epi_warps<EPI>()); }
 constexpr int kPBN = 256;
 constexpr int kPStages = 4;
 constexpr int kPStage = kABytes + kPBN * kTileK;
 
 template <int EPI>
-__global__ void __launch_bounds__(kPThreads, 1)
+__global__ void __launch_bounds__(tcp_threads<EPI>(), 1)
     gemm_tcp_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, TcArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -556,7 +561,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(acc_full + b, 1);
-      mbar_init(acc_empty + b, kPEpiWarps);
+      mbar_init(acc_empty + b, tcp_epi_warps<EPI>());
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_w)) : "memory");
@@ -629,7 +634,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
     // epilogue warps
     const int q = warp & 3;
     const int part = (warp - 2) >> 2;
-    const int c0 = part * 16 / kPParts, c1 = (part + 1) * 16 / kPParts;  // this warp's 16-token chunks
+    constexpr int kParts = tcp_epi_warps<EPI>() / 4;  // epilogue warps per TMEM lane quarter
+    const int c0 = part * 16 / kParts, c1 = (part + 1) * 16 / kParts;  // this warp's 16-token chunks
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(c0 * 16);
     const bool has_amax = kFloatEpi && a.out_absmax != nullptr;
     pdl_wait();  // token scales and residuals come from the previous kernel
@@ -813,7 +819,7 @@ cudaError_t launch_tcp_e(const TcPlan& p, const TcArgs& a, cudaStream_t s, bool 
   const int tiles = ((a.N + kTileN - 1) / kTileN) * ((a.M + kPBN - 1) / kPBN);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(std::min(tiles, device_sm_count()));
-  cfg.blockDim = dim3(kPThreads);
+  cfg.blockDim = dim3(tcp_threads<EPI>());
   cfg.dynamicSmemBytes = tcp_smem();
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
