@@ -1225,6 +1225,324 @@ __global__ void __launch_bounds__(kApfThreads, 1) attn_prefill_tc_kernel(
   if (warp == kApfWarpMma) tmem_free(tmem, kApfTmemCols);
 }
 
+
+// ---------------------------------------------- prefill, two q-tile streams
+// Causal prefill attention with K / V as fp16 rows in global memory (written
+// once per layer by the cache-write kernel: the INT8 values, exact) and two
+// independent work streams per CTA that share the SM's tensor core: while
+// one stream's softmax warps turn S into P, the other stream's MMAs run.
+// Stream s of CTA b takes the CTA's work items b + (2k + s) * gridDim.x
+// (longest query tiles first). Per stream: one load warp (lane 0 issues the
+// TMA loads of the K and V tiles, double-buffered), one MMA warp (lane 0
+// issues S = (Q_hi + Q_lo) . K^T and O = (P_hi + P_lo) . V) and four softmax
+// warps, one thread per query row over all 128 keys of a tile (so no row
+// maximum is exchanged between threads). P is written back into the TMEM
+// columns of S (hi and lo halves of each 16-key group side by side) and read
+// from there as the A operand of P.V; the next tile's S is issued only once
+// that P.V has completed. P.V of tile g accumulates fresh in O buffer g % 2
+// and is folded into the softmax thread's registers two tiles later, with
+// the online-softmax correction (as in attn_prefill_tc_kernel). Numerics are
+// those of attn_prefill_tc_kernel: fp16 hi + lo halves of the power-of-two
+// scaled query and of the probabilities (~22 significant bits), fp32
+// accumulation, base-2 softmax.
+//
+// TMEM per stream s (columns 256 s ..): S / P [0, 128), O buffers [128, 192)
+// and [192, 256). Shared memory per stream (96 KB): Q hi, Q lo (16 KB each,
+// SW128 K-major), K tiles x 2, V tiles x 2 (16 KB each, TMA SW128 boxes).
+constexpr int kPpRows = 128, kPpKeys = 128;
+constexpr int kPpWarps = 12;  // per stream: load, MMA; then 4 + 4 softmax warps (warps 4-7, 8-11)
+constexpr int kPpThreads = 32 * kPpWarps;
+constexpr int kPpStreamBytes = 98304;
+constexpr int kPpOffQHi = 0, kPpOffQLo = 16384, kPpOffK = 32768, kPpOffV = 65536;
+constexpr int kPpOffBar = 2 * kPpStreamBytes;
+constexpr int kPpBarsPerStream = 11;
+constexpr size_t kPpSmem = kPpOffBar + 2 * kPpBarsPerStream * 8 + 16 + 1024;
+
+// TL_DISABLE_PP_ATTN_PREFILL=1 keeps prefill attention on attn_prefill_tc_kernel (A/B).
+bool use_apf_pp() {
+  static const bool disabled = [] {
+    const char* v = std::getenv("TL_DISABLE_PP_ATTN_PREFILL");
+    return v && v[0] == '1';
+  }();
+  return !disabled;
+}
+
+struct PpBars {
+  uint64_t *q_full, *kv_full, *kv_free, *s_full, *p_full, *o_full, *o_free;
+};
+TL_DEV PpBars pp_bars(unsigned char* sm, int s) {
+  uint64_t* b = reinterpret_cast<uint64_t*>(sm + kPpOffBar) + s * kPpBarsPerStream;
+  return PpBars{b, b + 1, b + 3, b + 5, b + 6, b + 7, b + 9};
+}
+// Query row `row` of item w, power-of-two scaled, into the stream's fp16 hi /
+// lo operand rows; returns the row's score scale without the K scale.
+TL_DEV float pp_prep_q_row(unsigned char* qs, const float* qkv, int ld, int seq_len, const ApfItem& w, int row) {
+  const int t = w.qt * kPpRows + row;
+  const float4* q4 = reinterpret_cast<const float4*>(
+      qkv + static_cast<size_t>(w.seq * seq_len + (t < seq_len ? t : 0)) * ld + w.head * 64);
+  float4 x[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) x[i] = t < seq_len ? __ldg(q4 + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  float mx = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(x[i].x), fabsf(x[i].y)), fmaxf(fabsf(x[i].z), fabsf(x[i].w))));
+  const float qsc = pow2_scale(mx);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint4 hi, lo;
+    split2_fast(x[2 * c].x * qsc, x[2 * c].y * qsc, hi.x, lo.x);
+    split2_fast(x[2 * c].z * qsc, x[2 * c].w * qsc, hi.y, lo.y);
+    split2_fast(x[2 * c + 1].x * qsc, x[2 * c + 1].y * qsc, hi.z, lo.z);
+    split2_fast(x[2 * c + 1].z * qsc, x[2 * c + 1].w * qsc, hi.w, lo.w);
+    const uint32_t off = sw128_offset(row, c);
+    *reinterpret_cast<uint4*>(qs + kPpOffQHi + off) = hi;
+    *reinterpret_cast<uint4*>(qs + kPpOffQLo + off) = lo;
+  }
+  return 0.125f * kLog2e / qsc;
+}
+
+__global__ void __launch_bounds__(kPpThreads, 1) attn_prefill_pp_kernel(
+    const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v, const float* __restrict__ qkv,
+    int ld, int seq_len, int nseq, int H, int Hkv, const float* __restrict__ ks, const float* __restrict__ vs,
+    int slot_base, int layer, int L, float* __restrict__ out, float* __restrict__ out_absmax) {
+  extern __shared__ __align__(1024) unsigned char pp_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(pp_raw) + 1023) & ~uintptr_t(1023));
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kPpOffBar + 2 * kPpBarsPerStream * 8);
+  const int n_qt = (seq_len + kPpRows - 1) / kPpRows;
+  const int items = n_qt * H * nseq;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int Dq = H * 64, G = H / Hkv;
+
+  if (tid == 0) {
+    for (int s = 0; s < 2; ++s) {
+      const PpBars b = pp_bars(sm, s);
+      mbar_init(b.q_full, 4);
+      mbar_init(b.s_full, 1);
+      mbar_init(b.p_full, 4);
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(b.kv_full + i, 1);
+        mbar_init(b.kv_free + i, 1);
+        mbar_init(b.o_full + i, 1);
+        mbar_init(b.o_free + i, 4);
+      }
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_k)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_v)) : "memory");
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int s = warp < 4 ? (warp >> 1) : (warp >> 3);  // this warp's stream
+  unsigned char* ss = sm + s * kPpStreamBytes;
+  const PpBars bb = pp_bars(sm, s);
+  const uint32_t tm_s = tmem + 256u * static_cast<uint32_t>(s);
+  const int stride = static_cast<int>(gridDim.x);
+  // k-th work item of this stream (>= items: none)
+  auto item_of = [&](int k) { return static_cast<int>(blockIdx.x) + (2 * k + s) * stride; };
+
+  if (warp < 4 && (warp & 1) == 0) {
+    // ---- load warp: K and V tiles of every key tile, double-buffered
+    if (lane == 0) {
+      int g = 0;
+      bool ok = true;
+      for (int k = 0; ok && item_of(k) < items; ++k) {
+        const ApfItem w = apf_item(item_of(k), n_qt, H, Hkv, nseq, slot_base, L, layer);
+        const int row0 = (w.seq * Hkv + w.head / G) * seq_len;
+        for (int j = 0; j <= w.qt && ok; ++j, ++g) {
+          const int b = g & 1;
+          if (g >= 2 && !(ok = apf_wait(bb.kv_free + b, ((g - 2) >> 1) & 1, 40u))) break;
+          mbar_arrive_expect_tx(bb.kv_full + b, 2u * 16384u);
+          tma_load_2d(ss + kPpOffK + b * 16384, &tm_k, 0, row0 + j * kPpKeys, bb.kv_full + b);
+          tma_load_2d(ss + kPpOffV + b * 16384, &tm_v, 0, row0 + j * kPpKeys, bb.kv_full + b);
+        }
+      }
+      // after a failed wait anywhere, the copies issued last get a bounded
+      // chance to land before the CTA exits
+      if (*reinterpret_cast<volatile unsigned int*>(&g_apf_error) != 0u)
+        for (int i = g >= 2 ? g - 2 : 0; i < g; ++i) (void)apf_wait(bb.kv_full + (i & 1), (i >> 1) & 1, 41u);
+    }
+  } else if (warp < 4) {
+    // ---- MMA warp
+    if (lane == 0) {
+      constexpr uint32_t id_s = idesc_f16(kPpRows, kPpKeys);
+      constexpr uint32_t id_o = idesc_f16(kPpRows, 64) | (1u << 16);  // B (V) MN-major
+      const uint64_t dqh = smem_desc_sw128(smem_u32(ss + kPpOffQHi));
+      const uint64_t dql = smem_desc_sw128(smem_u32(ss + kPpOffQLo));
+      const uint64_t dk0 = smem_desc_sw128(smem_u32(ss + kPpOffK));
+      const uint64_t dv0 = smem_desc_sw128_mn(smem_u32(ss + kPpOffV));
+      int g = 0;
+      bool ok = true;
+      for (int k = 0; ok && item_of(k) < items; ++k) {
+        const ApfItem w = apf_item(item_of(k), n_qt, H, Hkv, nseq, slot_base, L, layer);
+        if (!(ok = apf_wait(bb.q_full, k & 1, 42u))) break;
+        for (int j = 0; j <= w.qt && ok; ++j, ++g) {
+          const int b = g & 1;
+          if (!(ok = apf_wait(bb.kv_full + b, (g >> 1) & 1, 43u))) break;
+          // S / P columns are free once the previous tile's P.V has completed
+          if (g >= 1 && !(ok = apf_wait(bb.o_full + ((g - 1) & 1), ((g - 1) >> 1) & 1, 44u))) break;
+          tc_fence_after();
+          const uint64_t dk = dk0 + static_cast<uint64_t>(b * 1024);  // + 16 KB
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            mma_f16(tm_s, dqh + 2 * kk, dk + 2 * kk, id_s, kk > 0 ? 1u : 0u);
+            mma_f16(tm_s, dql + 2 * kk, dk + 2 * kk, id_s, 1u);
+          }
+          mma_commit(bb.s_full);
+          if (!(ok = apf_wait(bb.p_full, g & 1, 45u))) break;
+          if (g >= 2 && !(ok = apf_wait(bb.o_free + b, ((g - 2) >> 1) & 1, 46u))) break;
+          tc_fence_after();
+          const uint32_t d_o = tm_s + 128u + 64u * static_cast<uint32_t>(b);
+          const uint64_t dv = dv0 + static_cast<uint64_t>(b * 1024);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            // keys 16 kk .. + 15: P hi at columns 16 kk .. + 7, lo at 16 kk + 8 .. + 15
+            const uint32_t a = tm_s + 16u * static_cast<uint32_t>(kk);
+            mma_f16_ts(d_o, a, dv + kk * 128, id_o, kk > 0 ? 1u : 0u);
+            mma_f16_ts(d_o, a + 8u, dv + kk * 128, id_o, 1u);
+          }
+          mma_commit(bb.o_full + b);
+          mma_commit(bb.kv_free + b);
+        }
+      }
+    }
+  } else {
+    // ---- softmax warps: thread = query row r of the stream's tile, all 128 keys
+    const int qq = warp & 3;
+    const int r = qq * 32 + lane;
+    const uint32_t lane_base = tm_s + (static_cast<uint32_t>(qq * 32) << 16);
+    float o[64];
+    // o += scale * (P_gg . V_gg), then O buffer gg % 2 may be overwritten
+    auto fold = [&](int gg, float scale) -> bool {
+      if (!apf_wait(bb.o_full + (gg & 1), (gg >> 1) & 1, 47u)) return false;
+      tc_fence_after();
+#pragma unroll
+      for (int hh = 0; hh < 4; ++hh) {
+        int w16[16];
+        tmem_ld16(lane_base + 128u + 64u * static_cast<uint32_t>(gg & 1) + 16u * hh, w16);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[16 * hh + i] = fmaf(__int_as_float(w16[i]), scale, o[16 * hh + i]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bb.o_free + (gg & 1));
+      return true;
+    };
+    int g = 0;
+    bool ok = true;
+    for (int k = 0; ok && item_of(k) < items; ++k) {
+      const ApfItem w = apf_item(item_of(k), n_qt, H, Hkv, nseq, slot_base, L, layer);
+      const int qt = w.qt;
+      const int t = qt * kPpRows + r;
+      // this item's query rows (every S MMA of the previous item has completed:
+      // its last S was awaited below)
+      const float xs = pp_prep_q_row(ss, qkv, ld, seq_len, w, r);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bb.q_full);
+      const float sc2 = xs * __ldg(ks + w.sidx);
+      float m2 = -INFINITY, l = 0.0f;  // running max (log2 units), running sum of p * 2^14
+      float c_prev = 1.0f;             // correction of the previous tile (m_{j-2} -> m_{j-1})
+#pragma unroll
+      for (int i = 0; i < 64; ++i) o[i] = 0.0f;
+      for (int j = 0; j <= qt && ok; ++j, ++g) {
+        if (!(ok = apf_wait(bb.s_full, g & 1, 48u))) break;
+        tc_fence_after();
+        const bool diag = j == qt;
+        const int lim = t - j * kPpKeys;  // keys k > lim are masked (diagonal tile only)
+        float mraw = -INFINITY;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t v[32];
+          tmem_ld32(lane_base + 32u * cc, v);
+          if (diag) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (32 * cc + i > lim) v[i] = __float_as_uint(-INFINITY);
+          }
+          float mq[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            mq[i] = fmaxf(fmaxf(__uint_as_float(v[i]), __uint_as_float(v[i + 8])),
+                          fmaxf(__uint_as_float(v[i + 16]), __uint_as_float(v[i + 24])));
+          mraw = fmaxf(mraw, fmaxf(fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])),
+                                   fmaxf(fmaxf(mq[4], mq[5]), fmaxf(mq[6], mq[7]))));
+        }
+        const float m_new = fmaxf(m2, mraw * sc2);
+        const float corr = ex2f(m2 - m_new);
+        m2 = m_new;
+        // o holds tiles <= j - 3 at max m_{j-1}; P_{j-2}.V_{j-2} is at m_{j-2}
+#pragma unroll
+        for (int i = 0; i < 64; ++i) o[i] *= corr;
+        if (j >= 2 && !(ok = fold(g - 2, c_prev * corr))) break;
+        c_prev = corr;
+        // p * 2^14 = 2^(s * sc2 - m + 14) (masked keys: p = 0) as fp16 hi + lo
+        // back into the S columns just read: keys 16 h .. + 15 (S columns
+        // 16 h .. + 15) become 8 hi words at column 16 h and 8 lo words at
+        // column 16 h + 8
+        const float off14 = 14.0f - m_new;
+        float lq[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) lq[i] = 0.0f;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            const uint32_t col = 32u * cc + 16u * hf;
+            int vi[16];
+            tmem_ld16(lane_base + col, vi);
+            float p[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int key = 32 * cc + 16 * hf + i;
+              const bool live = !diag || key <= lim;
+              p[i] = live ? ex2f(fmaf(__int_as_float(vi[i]), sc2, off14)) : 0.0f;
+              lq[i & 7] += p[i];
+            }
+            uint32_t hi[8], lo[8];
+#pragma unroll
+            for (int q2 = 0; q2 < 8; ++q2) split2_fast(p[2 * q2], p[2 * q2 + 1], hi[q2], lo[q2]);
+            tmem_st8(lane_base + col, hi);
+            tmem_st8(lane_base + col + 8u, lo);
+          }
+        }
+        l = fmaf(l, corr, ((lq[0] + lq[1]) + (lq[2] + lq[3])) + ((lq[4] + lq[5]) + (lq[6] + lq[7])));
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bb.p_full);
+      }
+      if (!ok) break;
+      // the last two tiles' P.V: P_{J-1}.V_{J-1} at m_{J-1} (scaled by the
+      // last correction), P_J.V_J at the final maximum
+      const int gJ = g - 1;
+      if (qt >= 1 && !(ok = fold(gJ - 1, c_prev))) break;
+      if (!(ok = fold(gJ, 1.0f))) break;
+      float local_max = 0.0f;
+      if (t < seq_len) {
+        const float inv = vs[w.sidx] / l;
+        float4* orow = reinterpret_cast<float4*>(out + static_cast<size_t>(w.seq * seq_len + t) * Dq + w.head * 64);
+#pragma unroll
+        for (int d = 0; d < 64; d += 4) {
+          const float4 y = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
+          orow[d / 4] = y;
+          local_max = fmaxf(local_max, fmaxf(fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w))));
+        }
+      }
+      if (out_absmax) {
+        local_max = warp_max(local_max);
+        if (lane == 0) atomic_max_nonneg(out_absmax + w.seq, local_max);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_free(tmem, 512);
+}
+
 }  // namespace
 
 cudaError_t launch_attn_prefill(const float* qkv, int ld, int rows, int seq_len, int H, int Hkv,
@@ -1247,6 +1565,26 @@ cudaError_t launch_attn_prefill(const float* qkv, int ld, int rows, int seq_len,
   return cudaGetLastError();
 }
 
+cudaError_t launch_attn_prefill_kvh(const float* qkv, int ld, int rows, int seq_len, int H, int Hkv,
+                                    const uint16_t* kh, const uint16_t* vh, const float* ks, const float* vs,
+                                    int slot_base, int layer, int L, float* out, float* out_absmax, cudaStream_t s) {
+  if (!use_apf_pp() || (reinterpret_cast<uintptr_t>(out) & 15u)) return cudaErrorNotSupported;
+  // (the query rows are read as float4: 16-byte aligned rows)
+  if (seq_len <= 0 || rows % seq_len || H % Hkv || (ld & 3) || (reinterpret_cast<uintptr_t>(qkv) & 15u) || !kh || !vh)
+    return cudaErrorInvalidValue;
+  const int nseq = rows / seq_len;
+  CUtensorMap tk, tv;
+  const long long krows = static_cast<long long>(nseq) * Hkv * seq_len;
+  cudaError_t e = tc_encode_f16_rows64(&tk, kh, krows);
+  if (e != cudaSuccess) return e;
+  if ((e = tc_encode_f16_rows64(&tv, vh, krows)) != cudaSuccess) return e;
+  const int items = ((seq_len + kPpRows - 1) / kPpRows) * H * nseq;
+  const int grid = std::min(device_sm_count(), (items + 1) / 2);
+  attn_prefill_pp_kernel<<<grid, kPpThreads, kPpSmem, s>>>(tk, tv, qkv, ld, seq_len, nseq, H, Hkv, ks, vs, slot_base,
+                                                           layer, L, out, out_absmax);
+  return cudaGetLastError();
+}
+
 // CTAs per (row, kv head): at most two resident CTAs per SM in one wave
 // (no split once the (row, kv head) pairs alone fill the GPU), each split
 // keeping at least two 32-position chunks of the longest context. The
@@ -1263,8 +1601,11 @@ cudaError_t attn_prepare() {
   cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(kDecSmem));
   if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(attn_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(kApfSmem));
+  e = cudaFuncSetAttribute(attn_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(kApfSmem));
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(attn_prefill_pp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(kPpSmem));
 }
 
 cudaError_t attn_read_error(unsigned int* code) {

@@ -126,6 +126,9 @@ struct PrefillBufs {
   int8_t* xq = nullptr;
   float* amax = nullptr;     // [L][4][n_seq] + [n_seq] (final norm)
   float* kvamax = nullptr;   // [L][n_seq][2][Hkv]
+  // this layer's K / V as fp16 rows [(seq * Hkv + h) * S + t][64] (the INT8
+  // cache values, exact): the attention's TMA operand rows
+  uint16_t *kh = nullptr, *vh = nullptr;
 };
 
 // NCCL entry points, resolved at run time from libnccl.so.2 (the copy a host
@@ -311,6 +314,7 @@ tl_status ensure_prefill(tl_engine* e, size_t rows, int n_seq) {
   n_seq = std::max(n_seq, p.n_seq_cap);
   cudaFree(p.ids); cudaFree(p.x); cudaFree(p.h); cudaFree(p.qkv); cudaFree(p.att);
   cudaFree(p.hid); cudaFree(p.xq); cudaFree(p.amax); cudaFree(p.kvamax); cudaFree(p.inv);
+  cudaFree(p.kh); cudaFree(p.vh);
   p = PrefillBufs{};
   TL_TRY(dmalloc(&p.ids, rows));
   TL_TRY(dmalloc(&p.x, rows * e->D));
@@ -322,6 +326,8 @@ tl_status ensure_prefill(tl_engine* e, size_t rows, int n_seq) {
   TL_TRY(dmalloc(&p.xq, rows * std::max(e->F, e->D)));
   TL_TRY(dmalloc(&p.amax, static_cast<size_t>(e->L) * 4 * n_seq + n_seq));
   TL_TRY(dmalloc(&p.kvamax, static_cast<size_t>(e->L) * n_seq * 2 * e->Hkv));
+  TL_TRY(dmalloc(&p.kh, rows * e->Dkv));
+  TL_TRY(dmalloc(&p.vh, rows * e->Dkv));
   p.rows = rows;
   p.n_seq_cap = n_seq;
   return TL_OK;
@@ -878,7 +884,7 @@ tl_status enqueue_prefill_layer(tl_engine* e, int l, int n_seq, int S, int slot_
   // RoPE of q in place, RoPE(k) and v maxima per (sequence, kv head), then the INT8 cache
   TL_CU(launch_rope_stats_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->cosT, e->sinT, kva, s));
   TL_CU(launch_kv_write_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->cosT, e->sinT, kva, e->kc, e->vc, e->ks,
-                                e->vs, slot_base, l, e->L, e->P, s));
+                                e->vs, slot_base, l, e->L, e->P, s, p.kh, p.vh));
   if (cap && cap->scores) {
     TL_CU(launch_attn_scores_debug(p.qkv, e->Nqkv, S, S, 0, false, e->H, e->Hkv, e->kc, e->ks, e->cosT, e->sinT,
                                    slot_base, l, e->L, e->P, cap->scores, cap->probs, s));
@@ -886,8 +892,16 @@ tl_status enqueue_prefill_layer(tl_engine* e, int l, int n_seq, int S, int slot_
     TL_TRY(d2h(e, hc->scores, cap->scores, sb));
     TL_TRY(d2h(e, hc->probs, cap->probs, sb));
   }
-  TL_CU(launch_attn_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->kc, e->vc, e->ks, e->vs, slot_base,
-                            l, e->L, e->P, p.att, am + n_seq, s));
+  {
+    // two-stream tcgen05 attention over the fp16 rows; the INT8-cache kernel
+    // when it is disabled or the output is not 16-byte aligned
+    cudaError_t ae = launch_attn_prefill_kvh(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, p.kh, p.vh, e->ks, e->vs, slot_base,
+                                             l, e->L, p.att, am + n_seq, s);
+    if (ae == cudaErrorNotSupported)
+      ae = launch_attn_prefill(p.qkv, e->Nqkv, R, S, e->H, e->Hkv, e->kc, e->vc, e->ks, e->vs, slot_base, l, e->L,
+                               e->P, p.att, am + n_seq, s);
+    TL_CU(ae);
+  }
   const int8_t* xin = p.xq;
   const bool rowsplit = tp && e->tp_exchange == TL_TP_ALLREDUCE;
   if (tp) TL_TRY(tp_allreduce_max(e, am + n_seq, n_seq));
@@ -1311,7 +1325,7 @@ tl_status tl_destroy(tl_engine* e) {
   cudaFree(d.d1_layers); cudaFree(d.d1_part); cudaFree(d.d1_sync);
   PrefillBufs& p = e->pf;
   cudaFree(p.ids); cudaFree(p.x); cudaFree(p.h); cudaFree(p.qkv); cudaFree(p.att); cudaFree(p.hid);
-  cudaFree(p.xq); cudaFree(p.amax); cudaFree(p.kvamax); cudaFree(p.inv);
+  cudaFree(p.xq); cudaFree(p.amax); cudaFree(p.kvamax); cudaFree(p.inv); cudaFree(p.kh); cudaFree(p.vh);
   cudaFree(e->logits_all);
   if (e->h_pinned) cudaFreeHost(e->h_pinned);
   if (e->stream) cudaStreamDestroy(e->stream);

@@ -11,6 +11,8 @@
 //  (decode attention on tensor cores lives in attention.cu)
 //  * prefill helpers: RMSNorm rows, quantize rows, RoPE + KV calibration, KV
 //    write, causal attention.
+#include <cuda_fp16.h>
+
 #include <algorithm>
 #include <cfloat>
 #include <cmath>
@@ -1093,7 +1095,7 @@ __global__ void __launch_bounds__(256) kv_write_prefill_kernel(const float* qkv,
                                                                int Hkv, const float* cos, const float* sin,
                                                                const float* kv_absmax, int8_t* kc, int8_t* vc,
                                                                float* ks, float* vs, int slot_base, int layer, int L,
-                                                               int P) {
+                                                               int P, uint16_t* kh, uint16_t* vh) {
   const int lane = threadIdx.x & 31;
   const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (r >= rows) return;
@@ -1122,18 +1124,25 @@ __global__ void __launch_bounds__(256) kv_write_prefill_kernel(const float* qkv,
     if (kind == 0) rope_pair(b0, b1, cs, sn, lane, b0, b1);
     const size_t sidx = (static_cast<size_t>(slot_base + seq) * L + layer) * Hkv + h;
     int8_t* dst = (kind == 0 ? kc : vc) + (sidx * P + t) * 64;
-    dst[lane] = static_cast<int8_t>(quantize_one(b0, sf));
-    dst[lane + 32] = static_cast<int8_t>(quantize_one(b1, sf));
+    const int q0 = quantize_one(b0, sf), q1 = quantize_one(b1, sf);
+    dst[lane] = static_cast<int8_t>(q0);
+    dst[lane + 32] = static_cast<int8_t>(q1);
+    if (kh) {
+      uint16_t* hd = (kind == 0 ? kh : vh) + (static_cast<size_t>(seq * Hkv + h) * seq_len + t) * 64;
+      hd[lane] = __half_as_ushort(__int2half_rn(q0));
+      hd[lane + 32] = __half_as_ushort(__int2half_rn(q1));
+    }
     if (t == 0 && lane == 0) (kind == 0 ? ks : vs)[sidx] = sf;
   }
 }
 
 cudaError_t launch_kv_write_prefill(const float* qkv, int ld, int rows, int seq_len, int H, int Hkv, const float* cos,
                                     const float* sin, const float* kv_absmax, int8_t* kc, int8_t* vc, float* ks,
-                                    float* vs, int slot_base, int layer, int L, int P, cudaStream_t s) {
-  if (Hkv > 8) return cudaErrorInvalidValue;
+                                    float* vs, int slot_base, int layer, int L, int P, cudaStream_t s,
+                                    uint16_t* kh, uint16_t* vh) {
+  if (Hkv > 8 || (!kh) != (!vh)) return cudaErrorInvalidValue;
   kv_write_prefill_kernel<<<(rows + 7) / 8, 256, 0, s>>>(qkv, ld, rows, seq_len, H, Hkv, cos, sin, kv_absmax, kc, vc,
-                                                          ks, vs, slot_base, layer, L, P);
+                                                          ks, vs, slot_base, layer, L, P, kh, vh);
   return cudaGetLastError();
 }
 

@@ -94,6 +94,8 @@ struct TcPlan {
 };
 // Encodes the two operand tensor maps and picks tile/split/stage counts.
 cudaError_t tc_make_plan(TcPlan* p, const int8_t* w_nk, int N, const int8_t* x, int M, int K, int num_sms, int epi);
+// Tensor map of a [rows][64] fp16 matrix in 128-row SW128 boxes.
+cudaError_t tc_encode_f16_rows64(CUtensorMap* tm, const void* base, long long rows);
 cudaError_t launch_gemm_tc(const TcPlan& p, const TcArgs& a, cudaStream_t s, bool pdl);
 cudaError_t prepare_tc();
 int tc_max_stages(int bn, int ks = 1);
@@ -204,17 +206,27 @@ cudaError_t launch_absmax_rows(const float* x, int rows, int K, int rows_per_gro
 // positions 0..seq_len-1): rope_stats rotates q in place and folds max
 // |RoPE(k)| and max |v| per (sequence, kv head) into kv_absmax (zero on
 // entry, [seq][2][Hkv]); kv_write recomputes RoPE(k) and stores K and V
-// quantized with those scales (and the scales).
+// quantized with those scales (and the scales). With kh / vh, kv_write also
+// stores the same INT8 K / V values as fp16 bits (exact) in rows
+// [(seq * Hkv + h) * seq_len + t][64], the operand rows of
+// launch_attn_prefill_kvh.
 cudaError_t launch_rope_stats_prefill(float* qkv, int ld, int rows, int seq_len, int H, int Hkv, const float* cos,
                                       const float* sin, float* kv_absmax, cudaStream_t s);
 cudaError_t launch_kv_write_prefill(const float* qkv, int ld, int rows, int seq_len, int H, int Hkv, const float* cos,
                                     const float* sin, const float* kv_absmax, int8_t* kc, int8_t* vc, float* ks,
-                                    float* vs, int slot_base, int layer, int L, int P, cudaStream_t s);
+                                    float* vs, int slot_base, int layer, int L, int P, cudaStream_t s,
+                                    uint16_t* kh = nullptr, uint16_t* vh = nullptr);
 // Causal attention of a prefilled batch: q from qkv (rotated), K/V from cache.
 cudaError_t launch_attn_prefill(const float* qkv, int ld, int rows, int seq_len, int H, int Hkv,
                                 const int8_t* kc, const int8_t* vc, const float* ks,
                                 const float* vs, int slot_base, int layer, int L, int P,
                                 float* out, float* out_absmax, cudaStream_t s);
+// The same attention reading K / V from the fp16 rows kv_write stored (kh,
+// vh) through TMA; cudaErrorNotSupported when it is disabled
+// (TL_DISABLE_PP_ATTN_PREFILL=1) or the output rows are not 16-byte aligned.
+cudaError_t launch_attn_prefill_kvh(const float* qkv, int ld, int rows, int seq_len, int H, int Hkv,
+                                    const uint16_t* kh, const uint16_t* vh, const float* ks, const float* vs,
+                                    int slot_base, int layer, int L, float* out, float* out_absmax, cudaStream_t s);
 
 // Debug capture: scores / probabilities [H][n_q][n_keys] of query rows at
 // positions pos0.. of one sequence against its cache (slot `slot`); q rows in
