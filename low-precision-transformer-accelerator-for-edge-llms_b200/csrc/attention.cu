@@ -1229,33 +1229,35 @@ __global__ void __launch_bounds__(kApfThreads, 1) attn_prefill_tc_kernel(
 // ---------------------------------------------- prefill, two q-tile streams
 // Causal prefill attention with K / V as fp16 rows in global memory (written
 // once per layer by the cache-write kernel: the INT8 values, exact) and two
-// independent work streams per CTA that share the SM's tensor core: while
-// one stream's softmax warps turn S into P, the other stream's MMAs run.
-// Stream s of CTA b takes the CTA's work items b + (2k + s) * gridDim.x
-// (longest query tiles first). Per stream: one load warp (lane 0 issues the
-// TMA loads of the K and V tiles, double-buffered), one MMA warp (lane 0
-// issues S = (Q_hi + Q_lo) . K^T and O = (P_hi + P_lo) . V) and four softmax
-// warps, one thread per query row over all 128 keys of a tile (so no row
-// maximum is exchanged between threads). P is written back into the TMEM
-// columns of S (hi and lo halves of each 16-key group side by side) and read
-// from there as the A operand of P.V; the next tile's S is issued only once
-// that P.V has completed. P.V of tile g accumulates fresh in O buffer g % 2
-// and is folded into the softmax thread's registers two tiles later, with
-// the online-softmax correction (as in attn_prefill_tc_kernel). Numerics are
-// those of attn_prefill_tc_kernel: fp16 hi + lo halves of the power-of-two
-// scaled query and of the probabilities (~22 significant bits), fp32
-// accumulation, base-2 softmax.
+// independent work streams per CTA that share the SM's tensor core. Stream s
+// of CTA b takes the CTA's work items b + (2k + s) * gridDim.x (longest query
+// tiles first). Per stream: one load warp (lane 0 issues the TMA loads of the
+// 64-key K and V tiles, each double-buffered and released separately: K once
+// its S is computed, V once its P.V is), one MMA warp (lane 0 issues
+// S = (Q_hi + Q_lo) . K^T and O = (P_hi + P_lo) . V) and four softmax warps,
+// one thread per query row (so no row maximum is exchanged between threads).
+// S is double-buffered in TMEM: S_{g+2} is issued as soon as P_g.V_g has
+// completed, while the softmax threads work on S_{g+1}. P is written back
+// into the TMEM columns of its S (hi and lo halves of each 16-key group side
+// by side) and read from there as the A operand of P.V. P_g.V_g accumulates
+// fresh in O buffer g % 2 and is folded into the softmax thread's registers
+// two tiles later with the online-softmax correction (as in
+// attn_prefill_tc_kernel). Numerics are those of attn_prefill_tc_kernel:
+// fp16 hi + lo halves of the power-of-two scaled query and of the
+// probabilities (~22 significant bits), fp32 accumulation, base-2 softmax.
 //
-// TMEM per stream s (columns 256 s ..): S / P [0, 128), O buffers [128, 192)
-// and [192, 256). Shared memory per stream (96 KB): Q hi, Q lo (16 KB each,
-// SW128 K-major), K tiles x 2, V tiles x 2 (16 KB each, TMA SW128 boxes).
-constexpr int kPpRows = 128, kPpKeys = 128;
+// TMEM per stream s (columns 256 s ..): S / P buffers [0, 64) and [64, 128),
+// O buffers [128, 192) and [192, 256). Shared memory per stream (64 KB): Q hi,
+// Q lo (16 KB each, SW128 K-major), K tiles x 2, V tiles x 2 (8 KB each, TMA
+// SW128 boxes of 64 rows).
+constexpr int kPpRows = 128, kPpKeys = 64;
 constexpr int kPpWarps = 12;  // per stream: load, MMA; then 4 + 4 softmax warps (warps 4-7, 8-11)
 constexpr int kPpThreads = 32 * kPpWarps;
-constexpr int kPpStreamBytes = 98304;
-constexpr int kPpOffQHi = 0, kPpOffQLo = 16384, kPpOffK = 32768, kPpOffV = 65536;
+constexpr int kPpStreamBytes = 65536;
+constexpr int kPpTile = kPpKeys * 128;  // bytes of one K or V tile
+constexpr int kPpOffQHi = 0, kPpOffQLo = 16384, kPpOffK = 32768, kPpOffV = 32768 + 2 * kPpTile;
 constexpr int kPpOffBar = 2 * kPpStreamBytes;
-constexpr int kPpBarsPerStream = 11;
+constexpr int kPpBarsPerStream = 16;
 constexpr size_t kPpSmem = kPpOffBar + 2 * kPpBarsPerStream * 8 + 16 + 1024;
 
 // TL_DISABLE_PP_ATTN_PREFILL=1 keeps prefill attention on attn_prefill_tc_kernel (A/B).
@@ -1268,11 +1270,11 @@ bool use_apf_pp() {
 }
 
 struct PpBars {
-  uint64_t *q_full, *kv_full, *kv_free, *s_full, *p_full, *o_full, *o_free;
+  uint64_t *q_full, *k_full, *k_free, *v_full, *v_free, *s_full, *p_full, *o_full, *o_free;
 };
 TL_DEV PpBars pp_bars(unsigned char* sm, int s) {
   uint64_t* b = reinterpret_cast<uint64_t*>(sm + kPpOffBar) + s * kPpBarsPerStream;
-  return PpBars{b, b + 1, b + 3, b + 5, b + 6, b + 7, b + 9};
+  return PpBars{b, b + 1, b + 3, b + 5, b + 7, b + 9, b + 11, b + 12, b + 14};
 }
 // Query row `row` of item w, power-of-two scaled, into the stream's fp16 hi /
 // lo operand rows; returns the row's score scale without the K scale.
@@ -1302,6 +1304,68 @@ TL_DEV float pp_prep_q_row(unsigned char* qs, const float* qkv, int ld, int seq_
   return 0.125f * kLog2e / qsc;
 }
 
+// Row maximum of the tile's 64 raw scores in TMEM (keys > lim masked when
+// MASK: the tiles on the diagonal), 16 columns per load with the next load
+// in flight.
+template <bool MASK>
+TL_DEV float pp_row_max(uint32_t base, int lim) {
+  int a[16], b[16];
+  float m = -INFINITY;
+  tmem_ld16_nw(base, a);
+  tmem_ld_wait16(a);
+#pragma unroll
+  for (int h = 0; h < kPpKeys / 16; ++h) {
+    if (h + 1 < kPpKeys / 16) tmem_ld16_nw(base + 16u * (h + 1), b);
+    float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float x = (MASK && 16 * h + i > lim) ? -INFINITY : __int_as_float(a[i]);
+      mq[i & 3] = fmaxf(mq[i & 3], x);
+    }
+    m = fmaxf(m, fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])));
+    if (h + 1 < kPpKeys / 16) {
+      tmem_ld_wait16(b);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) a[i] = b[i];
+    }
+  }
+  return m;
+}
+// p * 2^14 = 2^(s * sc2 + off14) of the tile's 64 scores (masked keys: 0),
+// written back over the S columns just read as fp16 hi + lo (keys 16 h ..
+// + 15: 8 hi words at column 16 h, 8 lo words at 16 h + 8); returns the sum
+// of the p (8-way tree). Loads pipelined one ahead as in pp_row_max.
+template <bool MASK>
+TL_DEV float pp_exp_store(uint32_t base, int lim, float sc2, float off14) {
+  int a[16], b[16];
+  float lq[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) lq[i] = 0.0f;
+  tmem_ld16_nw(base, a);
+  tmem_ld_wait16(a);
+#pragma unroll
+  for (int h = 0; h < kPpKeys / 16; ++h) {
+    if (h + 1 < kPpKeys / 16) tmem_ld16_nw(base + 16u * (h + 1), b);
+    float p[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      p[i] = (MASK && 16 * h + i > lim) ? 0.0f : ex2f(fmaf(__int_as_float(a[i]), sc2, off14));
+      lq[i & 7] += p[i];
+    }
+    uint32_t hi[8], lo[8];
+#pragma unroll
+    for (int q2 = 0; q2 < 8; ++q2) split2_fast(p[2 * q2], p[2 * q2 + 1], hi[q2], lo[q2]);
+    tmem_st8(base + 16u * h, hi);
+    tmem_st8(base + 16u * h + 8u, lo);
+    if (h + 1 < kPpKeys / 16) {
+      tmem_ld_wait16(b);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) a[i] = b[i];
+    }
+  }
+  return ((lq[0] + lq[1]) + (lq[2] + lq[3])) + ((lq[4] + lq[5]) + (lq[6] + lq[7]));
+}
+
 __global__ void __launch_bounds__(kPpThreads, 1) attn_prefill_pp_kernel(
     const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v, const float* __restrict__ qkv,
     int ld, int seq_len, int nseq, int H, int Hkv, const float* __restrict__ ks, const float* __restrict__ vs,
@@ -1318,11 +1382,13 @@ __global__ void __launch_bounds__(kPpThreads, 1) attn_prefill_pp_kernel(
     for (int s = 0; s < 2; ++s) {
       const PpBars b = pp_bars(sm, s);
       mbar_init(b.q_full, 4);
-      mbar_init(b.s_full, 1);
       mbar_init(b.p_full, 4);
       for (int i = 0; i < 2; ++i) {
-        mbar_init(b.kv_full + i, 1);
-        mbar_init(b.kv_free + i, 1);
+        mbar_init(b.k_full + i, 1);
+        mbar_init(b.k_free + i, 1);
+        mbar_init(b.v_full + i, 1);
+        mbar_init(b.v_free + i, 1);
+        mbar_init(b.s_full + i, 1);
         mbar_init(b.o_full + i, 1);
         mbar_init(b.o_free + i, 4);
       }
@@ -1341,29 +1407,37 @@ __global__ void __launch_bounds__(kPpThreads, 1) attn_prefill_pp_kernel(
   const PpBars bb = pp_bars(sm, s);
   const uint32_t tm_s = tmem + 256u * static_cast<uint32_t>(s);
   const int stride = static_cast<int>(gridDim.x);
-  // k-th work item of this stream (>= items: none)
+  // k-th work item of this stream (>= items: none); key tiles of query tile qt
   auto item_of = [&](int k) { return static_cast<int>(blockIdx.x) + (2 * k + s) * stride; };
+  auto tiles_of = [&](int qt) { return 2 * qt + 2; };
 
   if (warp < 4 && (warp & 1) == 0) {
-    // ---- load warp: K and V tiles of every key tile, double-buffered
+    // ---- load warp: K tile g + 2 once S_g is computed, V tile g + 2 once P_g.V_g is
     if (lane == 0) {
       int g = 0;
       bool ok = true;
       for (int k = 0; ok && item_of(k) < items; ++k) {
         const ApfItem w = apf_item(item_of(k), n_qt, H, Hkv, nseq, slot_base, L, layer);
         const int row0 = (w.seq * Hkv + w.head / G) * seq_len;
-        for (int j = 0; j <= w.qt && ok; ++j, ++g) {
+        const int n_kt = tiles_of(w.qt);
+        for (int j = 0; j < n_kt && ok; ++j, ++g) {
           const int b = g & 1;
-          if (g >= 2 && !(ok = apf_wait(bb.kv_free + b, ((g - 2) >> 1) & 1, 40u))) break;
-          mbar_arrive_expect_tx(bb.kv_full + b, 2u * 16384u);
-          tma_load_2d(ss + kPpOffK + b * 16384, &tm_k, 0, row0 + j * kPpKeys, bb.kv_full + b);
-          tma_load_2d(ss + kPpOffV + b * 16384, &tm_v, 0, row0 + j * kPpKeys, bb.kv_full + b);
+          const uint32_t ph = ((g - 2) >> 1) & 1;
+          if (g >= 2 && !(ok = apf_wait(bb.k_free + b, ph, 40u))) break;
+          mbar_arrive_expect_tx(bb.k_full + b, static_cast<uint32_t>(kPpTile));
+          tma_load_2d(ss + kPpOffK + b * kPpTile, &tm_k, 0, row0 + j * kPpKeys, bb.k_full + b);
+          if (g >= 2 && !(ok = apf_wait(bb.v_free + b, ph, 39u))) break;
+          mbar_arrive_expect_tx(bb.v_full + b, static_cast<uint32_t>(kPpTile));
+          tma_load_2d(ss + kPpOffV + b * kPpTile, &tm_v, 0, row0 + j * kPpKeys, bb.v_full + b);
         }
       }
       // after a failed wait anywhere, the copies issued last get a bounded
       // chance to land before the CTA exits
       if (*reinterpret_cast<volatile unsigned int*>(&g_apf_error) != 0u)
-        for (int i = g >= 2 ? g - 2 : 0; i < g; ++i) (void)apf_wait(bb.kv_full + (i & 1), (i >> 1) & 1, 41u);
+        for (int i = g >= 2 ? g - 2 : 0; i < g; ++i) {
+          (void)apf_wait(bb.k_full + (i & 1), (i >> 1) & 1, 41u);
+          (void)apf_wait(bb.v_full + (i & 1), (i >> 1) & 1, 41u);
+        }
     }
   } else if (warp < 4) {
     // ---- MMA warp
@@ -1374,43 +1448,56 @@ __global__ void __launch_bounds__(kPpThreads, 1) attn_prefill_pp_kernel(
       const uint64_t dql = smem_desc_sw128(smem_u32(ss + kPpOffQLo));
       const uint64_t dk0 = smem_desc_sw128(smem_u32(ss + kPpOffK));
       const uint64_t dv0 = smem_desc_sw128_mn(smem_u32(ss + kPpOffV));
+      // S_gg into S buffer gg % 2, once K tile gg is in and P_{gg-2}.V_{gg-2}
+      // (the buffer's previous P) has completed
+      auto issue_qk = [&](int gg) -> bool {
+        const int b = gg & 1;
+        if (!apf_wait(bb.k_full + b, (gg >> 1) & 1, 43u)) return false;
+        if (gg >= 2 && !apf_wait(bb.o_full + b, ((gg - 2) >> 1) & 1, 44u)) return false;
+        tc_fence_after();
+        const uint32_t d = tm_s + 64u * static_cast<uint32_t>(b);
+        const uint64_t dk = dk0 + static_cast<uint64_t>(b * (kPpTile >> 4));
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          mma_f16(d, dqh + 2 * kk, dk + 2 * kk, id_s, kk > 0 ? 1u : 0u);
+          mma_f16(d, dql + 2 * kk, dk + 2 * kk, id_s, 1u);
+        }
+        mma_commit(bb.s_full + b);
+        mma_commit(bb.k_free + b);
+        return true;
+      };
       int g = 0;
       bool ok = true;
       for (int k = 0; ok && item_of(k) < items; ++k) {
         const ApfItem w = apf_item(item_of(k), n_qt, H, Hkv, nseq, slot_base, L, layer);
+        const int n_kt = tiles_of(w.qt);
         if (!(ok = apf_wait(bb.q_full, k & 1, 42u))) break;
-        for (int j = 0; j <= w.qt && ok; ++j, ++g) {
-          const int b = g & 1;
-          if (!(ok = apf_wait(bb.kv_full + b, (g >> 1) & 1, 43u))) break;
-          // S / P columns are free once the previous tile's P.V has completed
-          if (g >= 1 && !(ok = apf_wait(bb.o_full + ((g - 1) & 1), ((g - 1) >> 1) & 1, 44u))) break;
+        ok = issue_qk(g) && issue_qk(g + 1);
+        for (int j = 0; j < n_kt && ok; ++j) {
+          const int gg = g + j, b = gg & 1;
+          if (!(ok = apf_wait(bb.p_full, gg & 1, 45u))) break;
+          if (!(ok = apf_wait(bb.v_full + b, (gg >> 1) & 1, 38u))) break;
+          if (gg >= 2 && !(ok = apf_wait(bb.o_free + b, ((gg - 2) >> 1) & 1, 46u))) break;
           tc_fence_after();
-          const uint64_t dk = dk0 + static_cast<uint64_t>(b * 1024);  // + 16 KB
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            mma_f16(tm_s, dqh + 2 * kk, dk + 2 * kk, id_s, kk > 0 ? 1u : 0u);
-            mma_f16(tm_s, dql + 2 * kk, dk + 2 * kk, id_s, 1u);
-          }
-          mma_commit(bb.s_full);
-          if (!(ok = apf_wait(bb.p_full, g & 1, 45u))) break;
-          if (g >= 2 && !(ok = apf_wait(bb.o_free + b, ((g - 2) >> 1) & 1, 46u))) break;
-          tc_fence_after();
+          const uint32_t sp = tm_s + 64u * static_cast<uint32_t>(b);
           const uint32_t d_o = tm_s + 128u + 64u * static_cast<uint32_t>(b);
-          const uint64_t dv = dv0 + static_cast<uint64_t>(b * 1024);
+          const uint64_t dv = dv0 + static_cast<uint64_t>(b * (kPpTile >> 4));
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
+          for (int kk = 0; kk < kPpKeys / 16; ++kk) {
             // keys 16 kk .. + 15: P hi at columns 16 kk .. + 7, lo at 16 kk + 8 .. + 15
-            const uint32_t a = tm_s + 16u * static_cast<uint32_t>(kk);
+            const uint32_t a = sp + 16u * static_cast<uint32_t>(kk);
             mma_f16_ts(d_o, a, dv + kk * 128, id_o, kk > 0 ? 1u : 0u);
             mma_f16_ts(d_o, a + 8u, dv + kk * 128, id_o, 1u);
           }
           mma_commit(bb.o_full + b);
-          mma_commit(bb.kv_free + b);
+          mma_commit(bb.v_free + b);
+          if (j + 2 < n_kt) ok = issue_qk(gg + 2);
         }
+        g += n_kt;
       }
     }
   } else {
-    // ---- softmax warps: thread = query row r of the stream's tile, all 128 keys
+    // ---- softmax warps: thread = query row r of the stream's tile
     const int qq = warp & 3;
     const int r = qq * 32 + lane;
     const uint32_t lane_base = tm_s + (static_cast<uint32_t>(qq * 32) << 16);
@@ -1419,12 +1506,19 @@ __global__ void __launch_bounds__(kPpThreads, 1) attn_prefill_pp_kernel(
     auto fold = [&](int gg, float scale) -> bool {
       if (!apf_wait(bb.o_full + (gg & 1), (gg >> 1) & 1, 47u)) return false;
       tc_fence_after();
+      const uint32_t ob = lane_base + 128u + 64u * static_cast<uint32_t>(gg & 1);
 #pragma unroll
-      for (int hh = 0; hh < 4; ++hh) {
-        int w16[16];
-        tmem_ld16(lane_base + 128u + 64u * static_cast<uint32_t>(gg & 1) + 16u * hh, w16);
+      for (int hh = 0; hh < 4; hh += 2) {
+        int w0[16], w1[16];
+        tmem_ld16_nw(ob + 16u * hh, w0);
+        tmem_ld16_nw(ob + 16u * (hh + 1), w1);
+        tmem_ld_wait16(w0);
+        tmem_ld_wait16(w1);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) o[16 * hh + i] = fmaf(__int_as_float(w16[i]), scale, o[16 * hh + i]);
+        for (int i = 0; i < 16; ++i) {
+          o[16 * hh + i] = fmaf(__int_as_float(w0[i]), scale, o[16 * hh + i]);
+          o[16 * hh + 16 + i] = fmaf(__int_as_float(w1[i]), scale, o[16 * hh + 16 + i]);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -1435,7 +1529,7 @@ __global__ void __launch_bounds__(kPpThreads, 1) attn_prefill_pp_kernel(
     bool ok = true;
     for (int k = 0; ok && item_of(k) < items; ++k) {
       const ApfItem w = apf_item(item_of(k), n_qt, H, Hkv, nseq, slot_base, L, layer);
-      const int qt = w.qt;
+      const int qt = w.qt, n_kt = tiles_of(qt);
       const int t = qt * kPpRows + r;
       // this item's query rows (every S MMA of the previous item has completed:
       // its last S was awaited below)
@@ -1448,68 +1542,27 @@ __global__ void __launch_bounds__(kPpThreads, 1) attn_prefill_pp_kernel(
       float c_prev = 1.0f;             // correction of the previous tile (m_{j-2} -> m_{j-1})
 #pragma unroll
       for (int i = 0; i < 64; ++i) o[i] = 0.0f;
-      for (int j = 0; j <= qt && ok; ++j, ++g) {
-        if (!(ok = apf_wait(bb.s_full, g & 1, 48u))) break;
+      for (int j = 0; j < n_kt && ok; ++j) {
+        const int gg = g + j, b = gg & 1;
+        if (!(ok = apf_wait(bb.s_full + b, (gg >> 1) & 1, 48u))) break;
         tc_fence_after();
-        const bool diag = j == qt;
-        const int lim = t - j * kPpKeys;  // keys k > lim are masked (diagonal tile only)
-        float mraw = -INFINITY;
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          uint32_t v[32];
-          tmem_ld32(lane_base + 32u * cc, v);
-          if (diag) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (32 * cc + i > lim) v[i] = __float_as_uint(-INFINITY);
-          }
-          float mq[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            mq[i] = fmaxf(fmaxf(__uint_as_float(v[i]), __uint_as_float(v[i + 8])),
-                          fmaxf(__uint_as_float(v[i + 16]), __uint_as_float(v[i + 24])));
-          mraw = fmaxf(mraw, fmaxf(fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])),
-                                   fmaxf(fmaxf(mq[4], mq[5]), fmaxf(mq[6], mq[7]))));
-        }
-        const float m_new = fmaxf(m2, mraw * sc2);
+        const uint32_t sb = lane_base + 64u * static_cast<uint32_t>(b);
+        const bool diag = j >= 2 * qt;       // key tiles that reach past row 128 qt
+        const int lim = t - j * kPpKeys;      // keys k > lim of the tile are masked
+        const float mraw = diag ? pp_row_max<true>(sb, lim) : pp_row_max<false>(sb, lim);
+        const float m_new = fmaxf(m2, mraw * sc2);  // a fully masked tile keeps m2
         const float corr = ex2f(m2 - m_new);
         m2 = m_new;
         // o holds tiles <= j - 3 at max m_{j-1}; P_{j-2}.V_{j-2} is at m_{j-2}
+        if (__any_sync(0xffffffffu, corr != 1.0f)) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) o[i] *= corr;
-        if (j >= 2 && !(ok = fold(g - 2, c_prev * corr))) break;
-        c_prev = corr;
-        // p * 2^14 = 2^(s * sc2 - m + 14) (masked keys: p = 0) as fp16 hi + lo
-        // back into the S columns just read: keys 16 h .. + 15 (S columns
-        // 16 h .. + 15) become 8 hi words at column 16 h and 8 lo words at
-        // column 16 h + 8
-        const float off14 = 14.0f - m_new;
-        float lq[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) lq[i] = 0.0f;
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-#pragma unroll
-          for (int hf = 0; hf < 2; ++hf) {
-            const uint32_t col = 32u * cc + 16u * hf;
-            int vi[16];
-            tmem_ld16(lane_base + col, vi);
-            float p[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int key = 32 * cc + 16 * hf + i;
-              const bool live = !diag || key <= lim;
-              p[i] = live ? ex2f(fmaf(__int_as_float(vi[i]), sc2, off14)) : 0.0f;
-              lq[i & 7] += p[i];
-            }
-            uint32_t hi[8], lo[8];
-#pragma unroll
-            for (int q2 = 0; q2 < 8; ++q2) split2_fast(p[2 * q2], p[2 * q2 + 1], hi[q2], lo[q2]);
-            tmem_st8(lane_base + col, hi);
-            tmem_st8(lane_base + col + 8u, lo);
-          }
+          for (int i = 0; i < 64; ++i) o[i] *= corr;
         }
-        l = fmaf(l, corr, ((lq[0] + lq[1]) + (lq[2] + lq[3])) + ((lq[4] + lq[5]) + (lq[6] + lq[7])));
+        if (j >= 2 && !(ok = fold(gg - 2, c_prev * corr))) break;
+        c_prev = corr;
+        const float off14 = 14.0f - m_new;
+        const float psum = diag ? pp_exp_store<true>(sb, lim, sc2, off14) : pp_exp_store<false>(sb, lim, sc2, off14);
+        l = fmaf(l, corr, psum);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
@@ -1518,8 +1571,8 @@ __global__ void __launch_bounds__(kPpThreads, 1) attn_prefill_pp_kernel(
       if (!ok) break;
       // the last two tiles' P.V: P_{J-1}.V_{J-1} at m_{J-1} (scaled by the
       // last correction), P_J.V_J at the final maximum
-      const int gJ = g - 1;
-      if (qt >= 1 && !(ok = fold(gJ - 1, c_prev))) break;
+      const int gJ = g + n_kt - 1;
+      if (!(ok = fold(gJ - 1, c_prev))) break;
       if (!(ok = fold(gJ, 1.0f))) break;
       float local_max = 0.0f;
       if (t < seq_len) {
@@ -1536,6 +1589,7 @@ __global__ void __launch_bounds__(kPpThreads, 1) attn_prefill_pp_kernel(
         local_max = warp_max(local_max);
         if (lane == 0) atomic_max_nonneg(out_absmax + w.seq, local_max);
       }
+      g += n_kt;
     }
   }
   tc_fence_before();
@@ -1568,16 +1622,17 @@ cudaError_t launch_attn_prefill(const float* qkv, int ld, int rows, int seq_len,
 cudaError_t launch_attn_prefill_kvh(const float* qkv, int ld, int rows, int seq_len, int H, int Hkv,
                                     const uint16_t* kh, const uint16_t* vh, const float* ks, const float* vs,
                                     int slot_base, int layer, int L, float* out, float* out_absmax, cudaStream_t s) {
-  if (!use_apf_pp() || (reinterpret_cast<uintptr_t>(out) & 15u)) return cudaErrorNotSupported;
+  // (TL_DISABLE_TC_ATTN_PREFILL=1 selects the mma.sync kernel for every prefill)
+  if (!use_apf_pp() || !use_apf_tc() || (reinterpret_cast<uintptr_t>(out) & 15u)) return cudaErrorNotSupported;
   // (the query rows are read as float4: 16-byte aligned rows)
   if (seq_len <= 0 || rows % seq_len || H % Hkv || (ld & 3) || (reinterpret_cast<uintptr_t>(qkv) & 15u) || !kh || !vh)
     return cudaErrorInvalidValue;
   const int nseq = rows / seq_len;
   CUtensorMap tk, tv;
   const long long krows = static_cast<long long>(nseq) * Hkv * seq_len;
-  cudaError_t e = tc_encode_f16_rows64(&tk, kh, krows);
+  cudaError_t e = tc_encode_f16_rows64(&tk, kh, krows, kPpKeys);
   if (e != cudaSuccess) return e;
-  if ((e = tc_encode_f16_rows64(&tv, vh, krows)) != cudaSuccess) return e;
+  if ((e = tc_encode_f16_rows64(&tv, vh, krows, kPpKeys)) != cudaSuccess) return e;
   const int items = ((seq_len + kPpRows - 1) / kPpRows) * H * nseq;
   const int grid = std::min(device_sm_count(), (items + 1) / 2);
   attn_prefill_pp_kernel<<<grid, kPpThreads, kPpSmem, s>>>(tk, tv, qkv, ld, seq_len, nseq, H, Hkv, ks, vs, slot_base,

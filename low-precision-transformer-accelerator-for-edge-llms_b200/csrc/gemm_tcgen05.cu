@@ -1004,17 +1004,18 @@ cudaError_t tc_encode_operand(CUtensorMap* tm, const int8_t* base, int rows, int
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-// fp16 rows of 64 values (128 bytes) -> 128-row boxes with the 128-byte
-// swizzle: a box lands in shared memory as a K-major (or, read the other
-// way, MN-major) SW128 operand tile, byte (row r, 16-byte chunk c) at
+// fp16 rows of 64 values (128 bytes) -> boxes of box_rows rows with the
+// 128-byte swizzle: a box lands in shared memory as a K-major (or, read the
+// other way, MN-major) SW128 operand tile, byte (row r, 16-byte chunk c) at
 // r * 128 + ((c ^ (r & 7)) << 4). Rows past `rows` read as zero.
-cudaError_t tc_encode_f16_rows64(CUtensorMap* tm, const void* base, long long rows) {
+cudaError_t tc_encode_f16_rows64(CUtensorMap* tm, const void* base, long long rows, int box_rows) {
   cudaError_t e = get_encode();
   if (e != cudaSuccess) return e;
-  if ((reinterpret_cast<uintptr_t>(base) & 15u) || rows <= 0) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) || rows <= 0 || box_rows < 8 || box_rows > 256 || box_rows % 8)
+    return cudaErrorInvalidValue;
   cuuint64_t dims[2] = {64, static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {128};
-  cuuint32_t box[2] = {64, 128};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

@@ -94,8 +94,8 @@ struct TcPlan {
 };
 // Encodes the two operand tensor maps and picks tile/split/stage counts.
 cudaError_t tc_make_plan(TcPlan* p, const int8_t* w_nk, int N, const int8_t* x, int M, int K, int num_sms, int epi);
-// Tensor map of a [rows][64] fp16 matrix in 128-row SW128 boxes.
-cudaError_t tc_encode_f16_rows64(CUtensorMap* tm, const void* base, long long rows);
+// Tensor map of a [rows][64] fp16 matrix in SW128 boxes of box_rows rows.
+cudaError_t tc_encode_f16_rows64(CUtensorMap* tm, const void* base, long long rows, int box_rows);
 cudaError_t launch_gemm_tc(const TcPlan& p, const TcArgs& a, cudaStream_t s, bool pdl);
 cudaError_t prepare_tc();
 int tc_max_stages(int bn, int ks = 1);
@@ -223,7 +223,8 @@ cudaError_t launch_attn_prefill(const float* qkv, int ld, int rows, int seq_len,
                                 float* out, float* out_absmax, cudaStream_t s);
 // The same attention reading K / V from the fp16 rows kv_write stored (kh,
 // vh) through TMA; cudaErrorNotSupported when it is disabled
-// (TL_DISABLE_PP_ATTN_PREFILL=1) or the output rows are not 16-byte aligned.
+// (TL_DISABLE_PP_ATTN_PREFILL=1 or TL_DISABLE_TC_ATTN_PREFILL=1) or the
+// output rows are not 16-byte aligned.
 cudaError_t launch_attn_prefill_kvh(const float* qkv, int ld, int rows, int seq_len, int H, int Hkv,
                                     const uint16_t* kh, const uint16_t* vh, const float* ks, const float* vs,
                                     int slot_base, int layer, int L, float* out, float* out_absmax, cudaStream_t s);
