@@ -419,8 +419,9 @@ def run_ours(a, rank, world, local_rank):
         line["roofline"] = {"bound": "hbm", "kernel": f"tcgen05 gate/up GEMM + SiLU*up, {B} rows as {groups} concurrent "
                                                       f"launches of {B // groups} rows", "achieved": achieved,
                             "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                            # dram__bytes_read.sum + dram__bytes_write.sum of one launch,
-                            # from the ncu capture summarised in ROOFLINE_PROFILE
+                            # dram__bytes_read.sum + dram__bytes_write.sum of the step's
+                            # gate/up launch pair, from the ncu capture summarised in
+                            # ROOFLINE_PROFILE
                             "traffic": profile_traffic(ROOFLINE_PROFILE),
                             "traffic_source": str(ROOFLINE_PROFILE.relative_to(ROOT)),
                             "peak_kind": peak_kind,
