@@ -364,7 +364,8 @@ TL_API tl_status tl_synchronize(tl_engine* eng);
  * ([6], [7] = 0); for n_seqs >= 16 they are the tcgen05 GEMMs, launched as
  * the decode step launches them: once per row group (two concurrent groups
  * of n_seqs / 2 rows on two streams for n_seqs >= 32, each group's launches
- * back to back on its stream), so a time covers all n_seqs rows. Each kind runs
+ * back to back on its stream; the LM head once over all rows), so a time
+ * covers all n_seqs rows. Each kind runs
  * `iters` back-to-back launches (no programmatic dependent launch) between
  * one event pair, layers cycled so weights come from HBM as in a real step;
  * the average includes each launch's start-up. The LM head (one matrix) is

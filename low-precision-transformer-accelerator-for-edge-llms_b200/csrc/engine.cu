@@ -101,6 +101,7 @@ struct DecodeBufs {
   unsigned int* am_counter = nullptr;
   float* logits = nullptr;  // [rows][V]
   int8_t* xq = nullptr;     // [rows][max(D, F)] int8 activations (tensor-core path)
+  int8_t* xq_lm = nullptr;  // [rows][D] the LM head's int8 input, written by every row group
   float* amax = nullptr;    // [rows] per-row absmax of the activation in xq
   // [rows] per-row max |x| folded in by the producer's epilogue (attention
   // output, SiLU*up) with atomics; zeroed by the RMSNorm kernel before it
@@ -281,6 +282,7 @@ tl_status alloc_decode(tl_engine* e) {
   TL_TRY(dmalloc(&d.am_counter, gemv_argmax_row_blocks(B) + 1));
   TL_TRY(dmalloc(&d.logits, static_cast<size_t>(B) * e->V));
   TL_TRY(dmalloc(&d.xq, static_cast<size_t>(B) * std::max(e->D, e->F)));
+  TL_TRY(dmalloc(&d.xq_lm, static_cast<size_t>(B) * e->D));
   TL_TRY(dmalloc(&d.amax, B));
   TL_TRY(dmalloc(&d.amax_prod, B));
   TL_TRY(dmalloc(&d.attn_part, tl_engine::kMaxGroups * attn_part_floats(B, e->Hkv, e->P)));  // a region per row group
@@ -563,8 +565,10 @@ int decode_row_groups(const tl_engine* e, int M, RowGroup* g) {
 }
 
 // Batched decode step on the tensor cores (M >= kTcMinRows rows): embedding
-// on the engine stream, then each row group's layers, final RMSNorm and
-// LM head (fused argmax) on its own stream, joined before the finalize.
+// on the engine stream, then each row group's layers and final RMSNorm on its
+// own stream, joined before one LM head (fused argmax) over all rows and the
+// finalize (one 64-row LM head launch: 250 CTAs, against 2 x 250 for two
+// 32-row ones).
 tl_status enqueue_decode_step_tc(tl_engine* e, int M, bool finalize) {
   DecodeBufs& d = e->dec;
   cudaStream_t s = e->stream;
@@ -582,28 +586,28 @@ tl_status enqueue_decode_step_tc(tl_engine* e, int M, bool finalize) {
   for (int i = 0; i < ng; ++i) {
     const RowGroup& g = grp[i];
     const size_t r0 = static_cast<size_t>(g.r0);
-    int8_t* xq = d.xq + r0 * std::max(e->D, e->F);
-    TL_CU(launch_norm_quant_rows(d.x + r0 * e->D, e->gfinal, eps, g.M, e->D, xq, d.amax + r0, g.s, pdl));
-    // LM head with the greedy argmax fused into the epilogue (packed keys in
-    // d.am_key, consumed and re-armed by step_finalize / keys_to_tokens); the
-    // logits themselves are not written
-    TcArgs lm;
-    lm.epi = EPI_F32; lm.w_scale = e->slm; lm.in_absmax = d.amax + r0; lm.rows_per_group = 1; lm.out_f32 = nullptr;
-    lm.am_key = d.am_key + r0;
-    TL_TRY(tc_gemm(e, e->wlm, e->V, xq, g.M, e->D, lm, pdl, g.s));
+    TL_CU(launch_norm_quant_rows(d.x + r0 * e->D, e->gfinal, eps, g.M, e->D, d.xq_lm + r0 * e->D, d.amax + r0, g.s,
+                                 pdl));
   }
   for (int i = 1; i < ng; ++i) {
     TL_CU(cudaEventRecord(e->ev_join[i - 1], grp[i].s));
     TL_CU(cudaStreamWaitEvent(s, e->ev_join[i - 1], 0));
   }
-  const bool pdl_tail = pdl && ng == 1;  // after the join the predecessor is an event
+  // LM head with the greedy argmax fused into the epilogue (packed keys in
+  // d.am_key, consumed and re-armed by step_finalize / keys_to_tokens); the
+  // logits themselves are not written. After the join its predecessor is an
+  // event, so it launches without programmatic serialization.
+  TcArgs lm;
+  lm.epi = EPI_F32; lm.w_scale = e->slm; lm.in_absmax = d.amax; lm.rows_per_group = 1; lm.out_f32 = nullptr;
+  lm.am_key = d.am_key;
+  TL_TRY(tc_gemm(e, e->wlm, e->V, d.xq_lm, M, e->D, lm, pdl && ng == 1, s));
   if (!finalize) TL_CU(launch_keys_to_tokens(d.am_key, d.argmax, M, s));
   if (finalize) {
     StepArgs st;
     st.M = M; st.am_key = d.am_key; st.tokens = d.tokens; st.pos = d.pos; st.active = d.active;
     st.count = d.count; st.stop = d.stop; st.out_ids = d.out_ids; st.out_stride = e->P;
     st.run = d.run; st.P = e->P;
-    TL_CU(launch_step_finalize(st, s, pdl_tail));
+    TL_CU(launch_step_finalize(st, s, pdl));
   }
   return TL_OK;
 }
@@ -1321,7 +1325,7 @@ tl_status tl_destroy(tl_engine* e) {
   cudaFree(d.x); cudaFree(d.qkv); cudaFree(d.att); cudaFree(d.hid); cudaFree(d.tokens); cudaFree(d.pos);
   cudaFree(d.slots); cudaFree(d.active); cudaFree(d.count); cudaFree(d.stop); cudaFree(d.out_ids);
   cudaFree(d.run); cudaFree(d.argmax); cudaFree(d.am_key); cudaFree(d.am_partial); cudaFree(d.am_counter); cudaFree(d.logits);
-  cudaFree(d.xq); cudaFree(d.amax); cudaFree(d.amax_prod); cudaFree(d.attn_part); cudaFree(d.attn_cnt);
+  cudaFree(d.xq); cudaFree(d.xq_lm); cudaFree(d.amax); cudaFree(d.amax_prod); cudaFree(d.attn_part); cudaFree(d.attn_cnt);
   cudaFree(d.d1_layers); cudaFree(d.d1_part); cudaFree(d.d1_sync);
   PrefillBufs& p = e->pf;
   cudaFree(p.ids); cudaFree(p.x); cudaFree(p.h); cudaFree(p.qkv); cudaFree(p.att); cudaFree(p.hid);
@@ -1990,15 +1994,18 @@ tl_status tl_profile_decode_kernels(tl_engine* e, uint32_t n_seqs, uint32_t iter
       const bool per_launch = kind == 5;
       if (per_launch) TL_CU(cudaMemsetAsync(flush, it & 0xff, flush_bytes, s));
       if (per_launch || it == 0) TL_CU(cudaEventRecord(ev[2 * it], s));
-      // the groups fork once per timed interval: per launch for the LM head,
-      // around all iters back-to-back launches of each group otherwise
-      const bool fork = per_launch || it == 0, join = per_launch || it + 1 == iters;
-      if (ng > 1 && fork) {
+      // the groups fork once per timed interval, around all iters back-to-back
+      // launches of each group; the LM head runs once over all rows, as in the step
+      const int ngk = kind == 5 ? 1 : ng;
+      RowGroup all;
+      all.M = M; all.s = s; all.attn_part = d.attn_part; all.split_rows = M;
+      const bool fork = it == 0, join = it + 1 == iters;
+      if (ngk > 1 && fork) {
         TL_CU(cudaEventRecord(e->ev_fork, s));
-        for (int i = 1; i < ng; ++i) TL_CU(cudaStreamWaitEvent(grp[i].s, e->ev_fork, 0));
+        for (int i = 1; i < ngk; ++i) TL_CU(cudaStreamWaitEvent(grp[i].s, e->ev_fork, 0));
       }
-      for (int gi = 0; gi < ng && result == TL_OK; ++gi) {
-        const RowGroup& rg = grp[gi];
+      for (int gi = 0; gi < ngk && result == TL_OK; ++gi) {
+        const RowGroup& rg = kind == 5 ? all : grp[gi];
         const size_t r0 = static_cast<size_t>(rg.r0);
         const int Mg = rg.M;
         cudaStream_t gs = rg.s;
@@ -2093,12 +2100,12 @@ tl_status tl_profile_decode_kernels(tl_engine* e, uint32_t n_seqs, uint32_t iter
           result = ts;
         }
       }
-      for (int i = 1; i < ng && (join || result != TL_OK); ++i) {
+      for (int i = 1; i < ngk && (join || result != TL_OK); ++i) {
         TL_CU(cudaEventRecord(e->ev_join[i - 1], grp[i].s));
         TL_CU(cudaStreamWaitEvent(s, e->ev_join[i - 1], 0));
       }
       if (result != TL_OK) break;
-      if (join) TL_CU(cudaEventRecord(ev[2 * it + 1], s));
+      if (per_launch || join) TL_CU(cudaEventRecord(ev[2 * it + 1], s));
     }
     if (result != TL_OK) break;
     TL_CU(cudaStreamSynchronize(s));
@@ -2130,11 +2137,11 @@ int32_t tl_decode_step_kernel_count(tl_engine* e) { return tl_decode_step_kernel
 
 int32_t tl_decode_step_kernel_count_rows(tl_engine* e, uint32_t n_seqs) {
   if (!e) return 0;
-  // embed, per row group 9 per layer + final norm + LM head with fused
+  // embed, per row group 9 per layer + final norm, LM head with fused
   // argmax, finalize
   if (static_cast<int>(n_seqs) >= kTcMinRows) {
     RowGroup g[tl_engine::kMaxGroups];
-    return 1 + decode_row_groups(e, static_cast<int>(n_seqs), g) * (9 * e->L + 2) + 1;
+    return 1 + decode_row_groups(e, static_cast<int>(n_seqs), g) * (9 * e->L + 1) + 2;
   }
   if (n_seqs == 1 && e->use_decode1) return 2;  // persistent step + finalize
   return 1 + 5 * e->L + 2;
