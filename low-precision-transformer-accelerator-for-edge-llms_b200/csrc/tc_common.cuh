@@ -143,15 +143,8 @@ TL_DEV void tmem_ld32(uint32_t taddr, uint32_t* v) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// 16 consecutive columns of this thread's TMEM lane <- v (asynchronous:
+// 8 consecutive columns of this thread's TMEM lane <- v (asynchronous:
 // tmem_st_wait() before another thread or the tensor core may read them).
-TL_DEV void tmem_st16(uint32_t taddr, const uint32_t* v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
-      ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
-        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-      : "memory");
-}
 TL_DEV void tmem_st8(uint32_t taddr, const uint32_t* v) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
                ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
@@ -159,8 +152,8 @@ TL_DEV void tmem_st8(uint32_t taddr, const uint32_t* v) {
 }
 TL_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// The same loads without the wait: the registers are valid only after
-// tmem_ld_wait(), which waits for every load this thread has in flight.
+// The 16-column load without the wait: the registers are valid only after
+// tmem_ld_wait16 on them (which waits for every load this thread has in flight).
 TL_DEV void tmem_ld16_nw(uint32_t taddr, int* v) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -168,7 +161,6 @@ TL_DEV void tmem_ld16_nw(uint32_t taddr, int* v) {
         "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
       : "r"(taddr));
 }
-TL_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // tcgen05.wait::ld that also names the 16 registers of a load issued with
 // tmem_ld16_nw, so that no use of them can be scheduled before the wait.
 TL_DEV void tmem_ld_wait16(int* v) {
