@@ -77,6 +77,21 @@ TL_DEV int quantize_one(float x, float scale_f32) {
   q = fminf(fmaxf(q, -127.0f), 127.0f);
   return static_cast<int>(q);
 }
+// quantize_one without a division per element: inv = __fdiv_rn(1, scale)
+// (correctly rounded) is computed once per group. a = x * inv lies within
+// 2^-23 |x / scale| <= 1.6e-5 of x / scale for |x / scale| < 128, and
+// fl(x / scale) within 7.7e-6 of it, so rint(a) = rint(fl(x / scale)) unless
+// a is within 1e-4 of a half-integer, where the division decides; |a| >= 128
+// rounds past 127 either way. The result equals quantize_one for every x.
+TL_DEV int quantize_one_inv(float x, float scale_f32, float inv) {
+  const float a = __fmul_rn(x, inv);
+  if (fabsf(a) >= 128.0f) return a < 0.0f ? -127 : 127;
+  float q = rintf(a);
+  if (fabsf(a - q) > 0.4999f) q = rintf(__fdiv_rn(x, scale_f32));
+  q = fminf(fmaxf(q, -127.0f), 127.0f);
+  return static_cast<int>(q);
+}
+TL_DEV float quant_inv(float scale_f32) { return __fdiv_rn(1.0f, scale_f32); }
 // dequantize_int32 (model/tinyllama_gemm_int8.py:45-46) with a float64
 // product of the two scales rounded to float32 once.
 TL_DEV float dequant(int acc, double sx, double sw) {

@@ -619,6 +619,16 @@ TL_DEV uint32_t quant_pack4(float4 v, float sf) {
          ((static_cast<uint32_t>(quantize_one(v.z, sf)) & 0xffu) << 16) |
          ((static_cast<uint32_t>(quantize_one(v.w, sf)) & 0xffu) << 24);
 }
+// the same four results from quantize_one_inv (inv = quant_inv(sf)): for
+// the throughput-bound prefill passes; in the latency-bound decode row
+// kernels the one serial reciprocal costs more than the divisions it saves
+// (64-row step 1.070-1.087 vs 1.053-1.057 ms)
+TL_DEV uint32_t quant_pack4_inv(float4 v, float sf, float inv) {
+  return (static_cast<uint32_t>(quantize_one_inv(v.x, sf, inv)) & 0xffu) |
+         ((static_cast<uint32_t>(quantize_one_inv(v.y, sf, inv)) & 0xffu) << 8) |
+         ((static_cast<uint32_t>(quantize_one_inv(v.z, sf, inv)) & 0xffu) << 16) |
+         ((static_cast<uint32_t>(quantize_one_inv(v.w, sf, inv)) & 0xffu) << 24);
+}
 
 __global__ void __launch_bounds__(128) norm_quant_rows_d2048_kernel(const float* x, const float* gamma,
                                                                      float eps, int8_t* out_q,
@@ -678,7 +688,7 @@ __global__ void __launch_bounds__(128) norm_quant_apply_d2048_kernel(const float
 #pragma unroll
   for (int i = 0; i < 4; ++i) v[i] = src[t + 128 * i];
   const float iv = inv[r];
-  const float sf = static_cast<float>(quant_scale64(absmax[r / rows_per_group]));
+  const float sf = static_cast<float>(quant_scale64(absmax[r / rows_per_group])), rsf = quant_inv(sf);
   const float4* g4 = reinterpret_cast<const float4*>(gamma);
   uint32_t* dst = reinterpret_cast<uint32_t*>(out_q + static_cast<size_t>(r) * D);
 #pragma unroll
@@ -689,7 +699,7 @@ __global__ void __launch_bounds__(128) norm_quant_apply_d2048_kernel(const float
     y.y = __fmul_rn(__fmul_rn(v[i].y, iv), g.y);
     y.z = __fmul_rn(__fmul_rn(v[i].z, iv), g.z);
     y.w = __fmul_rn(__fmul_rn(v[i].w, iv), g.w);
-    dst[t + 128 * i] = quant_pack4(y, sf);
+    dst[t + 128 * i] = quant_pack4_inv(y, sf, rsf);
   }
 }
 
@@ -891,12 +901,12 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_rows_vec_kernel(const 
     const int c = t + i * kQuantThreads;
     v[i] = c < n4 ? src[c] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   }
-  const float sf = static_cast<float>(quant_scale64(absmax[r / rows_per_group]));
+  const float sf = static_cast<float>(quant_scale64(absmax[r / rows_per_group])), inv = quant_inv(sf);
   uint32_t* dst = reinterpret_cast<uint32_t*>(out + static_cast<size_t>(r) * K);
 #pragma unroll
   for (int i = 0; i < kQuantVec; ++i) {
     const int c = t + i * kQuantThreads;
-    if (c < n4) dst[c] = quant_pack4(v[i], sf);
+    if (c < n4) dst[c] = quant_pack4_inv(v[i], sf, inv);
   }
 }
 
@@ -1314,11 +1324,11 @@ __global__ void __launch_bounds__(256) quantize_scatter_kernel(const float* x, c
                                                                int Kf, int col0, TpScatter t, unsigned int* done,
                                                                unsigned int epoch) {
   const int r = blockIdx.x;
-  const float sf = static_cast<float>(quant_scale64(absmax[r / rpg]));
+  const float sf = static_cast<float>(quant_scale64(absmax[r / rpg])), inv = quant_inv(sf);
   const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(r) * Kl);
   const size_t off = static_cast<size_t>(r) * Kf + col0;
   for (int c = threadIdx.x; c < Kl / 4; c += blockDim.x) {
-    const uint32_t q = quant_pack4(src[c], sf);
+    const uint32_t q = quant_pack4_inv(src[c], sf, inv);
     for (int d = 0; d < t.ndst; ++d) reinterpret_cast<uint32_t*>(t.dst[d] + off)[c] = q;
   }
   __syncthreads();

@@ -110,6 +110,24 @@ def test_quantize_int8_bit_exact(lib, pkg, golden):
         assert (1.0 if peak == 0.0 else peak / 127.0) == float(d[f"{key}_scale"]), key
 
 
+def test_quantize_int8_adversarial_quotients(lib, pkg):
+    """The kernels' division-free quantizer (x times the reciprocal scale,
+    the division only within 1e-4 of a rounding boundary) against the
+    oracle on quotients exactly at k + 1/2, one ulp either side and at the
+    +-127.5 clamp edge (tests/test_quantize_rule.py restates the rule)."""
+    from test_quantize_rule import adversarial
+    rng = np.random.default_rng(5)
+    for amax in (np.float32(3.0e-3), np.float32(0.7), np.float32(17.0), np.float32(2.5e3)):
+        x = adversarial(rng, amax)
+        x = np.concatenate([x, np.zeros((-x.size) % 4, np.float32)])[None, :]
+        q = torch.empty(x.shape, dtype=torch.int8, device="cuda")
+        am = torch.empty(1, dtype=torch.float32, device="cuda")
+        pkg.shim.check(lib.tl_quantize_int8(dev(x).data_ptr(), 1, x.shape[1], 1, q.data_ptr(), am.data_ptr(),
+                                            stream()), "quantize")
+        want, _ = G.quantize_int8(x)
+        np.testing.assert_array_equal(q.cpu().numpy(), want, err_msg=str(amax))
+
+
 def test_quantized_linear_matches_reference_fixture(pkg, golden, lib):
     d = golden["quant_cases"]
     for i in range(4):
