@@ -363,7 +363,7 @@ TL_API tl_status tl_synchronize(tl_engine* eng);
  * projections are the dp4a GEMVs with the RMSNorm/quantize prologue fused
  * ([6], [7] = 0); for n_seqs >= 16 they are the tcgen05 GEMMs, launched as
  * the decode step launches them: once per row group (two concurrent groups
- * of n_seqs / 2 rows on two streams for n_seqs >= 32, each group's launches
+ * of n_seqs / 2 rows on two streams for n_seqs >= 48, each group's launches
  * back to back on its stream; the LM head once over all rows), so a time
  * covers all n_seqs rows. Each kind runs
  * `iters` back-to-back launches (no programmatic dependent launch) between
@@ -377,8 +377,8 @@ TL_API tl_status tl_profile_decode_kernels(tl_engine* eng, uint32_t n_seqs, uint
 /* Number of kernels one decode step of n_seqs rows launches. */
 TL_API int32_t tl_decode_step_kernel_count_rows(tl_engine* eng, uint32_t n_seqs);
 /* Number of concurrent row groups (streams) a decode step of n_seqs rows
- * runs: 2 for n_seqs >= 32 (TL_DECODE_GROUPS=n overrides, up to 4), else 1;
- * 0 for a NULL engine. */
+ * runs: 2 for n_seqs >= 48 (groups of at least 24 rows; TL_DECODE_GROUPS=n
+ * sets the most, up to 4), else 1; 0 for a NULL engine. */
 TL_API int32_t tl_decode_row_groups(tl_engine* eng, uint32_t n_seqs);
 /* Number of kernels one decode step launches (for launch accounting). */
 TL_API int32_t tl_decode_step_kernel_count(tl_engine* eng);

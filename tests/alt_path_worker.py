@@ -6,8 +6,8 @@ full-width TinyLlama layer:
   against the oracle on the engine's own inputs (tests/layer_checks.py), and
   the production prefill's hidden state equal to that chain's bit for bit;
 * prefill logits, batch-1 generation (the persistent decode kernel, or the
-  per-kernel GEMV path with TL_DISABLE_DECODE1=1) and a 32-row batched
-  generation (tcgen05 decode, two concurrent row groups of 16 rows unless
+  per-kernel GEMV path with TL_DISABLE_DECODE1=1) and a 48-row batched
+  generation (tcgen05 decode, two concurrent row groups of 24 rows unless
   TL_DECODE_GROUPS=1) against the oracle within the sensitivity
   bound of helpers.oracle_run; layer-0 K/V bytes exact.
 """
@@ -32,7 +32,7 @@ from oracle.kv_golden import KVGolden  # noqa: E402
 
 def run(pkg, qm, tag):
     rng = np.random.default_rng(3)
-    eng = pkg.Engine(qm.cfg, max_batch=32, max_prefill_tokens=32 * 16 + 300)
+    eng = pkg.Engine(qm.cfg, max_batch=48, max_prefill_tokens=48 * 16 + 300)
     eng.load(to_engine_model(pkg, qm))
     prompt = [int(t) for t in rng.integers(0, qm.cfg["vocab_size"], 300)]
     ora = KVGolden(qm, kv="int8", matmul=G.ExactMatmul())
@@ -54,10 +54,10 @@ def run(pkg, qm, tag):
     assert np.array_equal(k, ora.k_cache[0, :, :300]) and np.array_equal(v, ora.v_cache[0, :, :300]), tag
     toks, st = eng.generate(prompt, 6)
     assert st["generated_count"] == 6 and tokens_match_modulo_ties(toks, ref, ref_logits, bounds), (tag, toks, ref)
-    prompts = rng.integers(0, qm.cfg["vocab_size"], (32, 16)).astype(np.uint32)
+    prompts = rng.integers(0, qm.cfg["vocab_size"], (48, 16)).astype(np.uint32)
     outs, sts = eng.generate_batch(prompts, 4)
     assert pkg.shim.load_library().tl_device_error() == 0, tag
-    for i in (0, 15, 16, 31):  # first and last row of each row group
+    for i in (0, 23, 24, 47):  # first and last row of each row group
         r, rl, b, _ = oracle_run(qm, [int(t) for t in prompts[i]], 4)
         assert tokens_match_modulo_ties(outs[i], r, rl, b), (tag, i, outs[i], r)
     eng.close()

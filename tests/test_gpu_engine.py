@@ -128,19 +128,19 @@ def test_batched_tensor_core_path(pkg, gpu):
 
 
 def test_uneven_row_groups(pkg, gpu):
-    """33 sequences: the decode step runs them as two concurrent row groups of
-    16 and 17 rows (two streams, one LM head over all 33); the first and last
+    """49 sequences: the decode step runs them as two concurrent row groups of
+    24 and 25 rows (two streams, one LM head over all 49); the first and last
     sequence of each group must follow its own oracle; so must a 16-row
     batch, which runs as one group."""
     qm = small_model(13, 2)
-    eng = pkg.Engine(qm.cfg, max_batch=33, max_prefill_tokens=33 * 6)
+    eng = pkg.Engine(qm.cfg, max_batch=49, max_prefill_tokens=49 * 6)
     eng.load(to_engine_model(pkg, qm))
-    assert eng.decode_row_groups(33) == 2 and eng.decode_row_groups(16) == 1
+    assert eng.decode_row_groups(49) == 2 and eng.decode_row_groups(47) == 1 and eng.decode_row_groups(16) == 1
     rng = np.random.default_rng(14)
-    prompts = rng.integers(0, qm.cfg["vocab_size"], (33, 6)).astype(np.uint32)
+    prompts = rng.integers(0, qm.cfg["vocab_size"], (49, 6)).astype(np.uint32)
     outs, sts = eng.generate_batch(prompts, 5)
     assert pkg.shim.load_library().tl_device_error() == 0
-    for i in (0, 15, 16, 32):
+    for i in (0, 23, 24, 48):
         ref, ref_logits, _ = oracle_generate(qm, list(prompts[i]), 5)
         assert sts[i]["stop_reason"] == 2 and sts[i]["generated_count"] == 5
         assert tokens_match_modulo_ties(outs[i], ref, ref_logits), (i, outs[i], ref)
