@@ -188,6 +188,13 @@ struct tl_engine {
   cudaStream_t side[kMaxGroups - 1] = {};
   cudaEvent_t ev_fork = nullptr, ev_join[kMaxGroups - 1] = {};
   int decode_groups = 2;
+  // Batched decode steps of at least this many rows run on the tcgen05 GEMMs,
+  // which stream every weight once per step whatever the row count below a
+  // 32-token tile; smaller batches (from 2 rows) take the dp4a GEMV path.
+  // Measured on B200 at context 512..1023: 8 rows 3.34 ms per step on the
+  // GEMV path, 16 rows 0.91 ms on the tensor cores. TL_DECODE_TC_MIN_ROWS=n
+  // overrides (2..16; 16 keeps every batch below 16 rows on the GEMV path).
+  int decode_tc_min_rows = 4;
   int D = 0, F = 0, H = 0, Hkv = 0, Dq = 0, Dkv = 0, Nqkv = 0, V = 0, L = 0, P = 0, B = 0;
   std::vector<Layer> layers;
   float *embed = nullptr, *gfinal = nullptr, *cosT = nullptr, *sinT = nullptr;
@@ -431,8 +438,8 @@ struct RowGroup {
   bool pdl_entry = true;
 };
 
-// Layer l of the batched decode step on the tensor cores (M >= kTcMinRows
-// rows): per row RMSNorm + INT8 quantization kernels feed tcgen05 GEMMs whose
+// Layer l of the batched decode step on the tensor cores (M >=
+// decode_tc_min_rows rows): per row RMSNorm + INT8 quantization kernels feed tcgen05 GEMMs whose
 // epilogues dequantize, add the residual or apply SiLU*up. The attention
 // kernel and the SiLU*up epilogue fold each row's max |output| into
 // d.amax_prod with atomics, so the quantization of their outputs is
@@ -568,7 +575,7 @@ int decode_row_groups(const tl_engine* e, int M, RowGroup* g) {
   return ng;
 }
 
-// Batched decode step on the tensor cores (M >= kTcMinRows rows): embedding
+// Batched decode step on the tensor cores (M >= decode_tc_min_rows): embedding
 // on the engine stream, then each row group's layers and final RMSNorm on its
 // own stream, joined before one LM head (fused argmax) over all rows and the
 // finalize (one 64-row LM head launch: 250 CTAs, against 2 x 250 for two
@@ -662,8 +669,8 @@ struct DebugCap {
   float* pr = nullptr;
 };
 
-// Layer l of the per-kernel decode step for rows 0..M-1 (M < kTcMinRows, or
-// teacher-forced logits): dp4a GEMVs with the RMSNorm/quantize prologue and
+// Layer l of the per-kernel decode step for rows 0..M-1 (2 <= M <
+// decode_tc_min_rows, batch 1 without decode1_kernel, or teacher-forced logits): dp4a GEMVs with the RMSNorm/quantize prologue and
 // the dequant / residual / SiLU*up epilogues, decode attention in between.
 tl_status enqueue_decode_layer_gemv(tl_engine* e, int l, int M, DebugCap* dbg) {
   DecodeBufs& d = e->dec;
@@ -733,7 +740,7 @@ tl_status enqueue_decode_layer_gemv(tl_engine* e, int l, int M, DebugCap* dbg) {
 }
 
 tl_status enqueue_decode_step(tl_engine* e, int M, float* logits, bool finalize, DebugCap* dbg = nullptr) {
-  if (M >= kTcMinRows && !logits) return enqueue_decode_step_tc(e, M, finalize);
+  if (M >= e->decode_tc_min_rows && !logits) return enqueue_decode_step_tc(e, M, finalize);
   if (M == 1 && !logits && e->use_decode1) return enqueue_decode_step_d1(e, finalize);
   DecodeBufs& d = e->dec;
   cudaStream_t s = e->stream;
@@ -1225,6 +1232,8 @@ tl_status create_engine(const tl_config* cfg, int32_t device, int rank, int worl
   if (ce != cudaSuccess) { g_last_error = cudaGetErrorString(ce); return fail(TL_ERR_CUDA); }
   if (const char* v = std::getenv("TL_DECODE_GROUPS"))
     e->decode_groups = std::max(1, std::min(tl_engine::kMaxGroups, std::atoi(v)));
+  if (const char* v = std::getenv("TL_DECODE_TC_MIN_ROWS"))
+    e->decode_tc_min_rows = std::max(2, std::min(kTcMinRows, std::atoi(v)));
   e->layers.resize(e->L);
   for (auto& ly : e->layers) {
     tl_status s;
@@ -1964,11 +1973,11 @@ tl_status tl_profile_decode_kernels(tl_engine* e, uint32_t n_seqs, uint32_t iter
   if (n_seqs == 0 || n_seqs > static_cast<uint32_t>(e->B)) return TL_ERR_OUT_OF_RANGE;
   TL_CU(cudaSetDevice(e->device));
   const int M = static_cast<int>(n_seqs);
-  const bool tc = M >= kTcMinRows;
+  const bool tc = M >= e->decode_tc_min_rows;
   DecodeBufs& d = e->dec;
   cudaStream_t s = e->stream;
   // each kind is launched as the step launches it: once per row group, the
-  // groups concurrently on their streams (one group below kTcMinRows rows)
+  // groups concurrently on their streams (one group below 48 rows)
   RowGroup grp[tl_engine::kMaxGroups];
   int ng = 1;
   if (tc) {
@@ -2143,7 +2152,7 @@ int32_t tl_decode_step_kernel_count_rows(tl_engine* e, uint32_t n_seqs) {
   if (!e) return 0;
   // embed, per row group 9 per layer + final norm, LM head with fused
   // argmax, finalize
-  if (static_cast<int>(n_seqs) >= kTcMinRows) {
+  if (static_cast<int>(n_seqs) >= e->decode_tc_min_rows) {
     RowGroup g[tl_engine::kMaxGroups];
     return 1 + decode_row_groups(e, static_cast<int>(n_seqs), g) * (9 * e->L + 1) + 2;
   }
@@ -2153,7 +2162,7 @@ int32_t tl_decode_step_kernel_count_rows(tl_engine* e, uint32_t n_seqs) {
 
 int32_t tl_decode_row_groups(tl_engine* e, uint32_t n_seqs) {
   if (!e) return 0;
-  if (static_cast<int>(n_seqs) < kTcMinRows) return 1;
+  if (static_cast<int>(n_seqs) < e->decode_tc_min_rows) return 1;
   RowGroup g[tl_engine::kMaxGroups];
   return decode_row_groups(e, static_cast<int>(n_seqs), g);
 }

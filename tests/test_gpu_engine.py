@@ -151,6 +151,26 @@ def test_uneven_row_groups(pkg, gpu):
     eng.close()
 
 
+def test_small_batches_on_tensor_cores(pkg, gpu):
+    """4, 8 and 15 sequences: batched decode steps of 4 or more rows run on
+    the tcgen05 GEMMs with most of each 32-token tile empty (the same kernels
+    as the large batches); the first and last sequence of each batch must
+    follow its own oracle; 3 sequences stay on the GEMV path."""
+    qm = small_model(17, 2)
+    eng = pkg.Engine(qm.cfg, max_batch=15, max_prefill_tokens=15 * 6)
+    eng.load(to_engine_model(pkg, qm))
+    rng = np.random.default_rng(18)
+    prompts = rng.integers(0, qm.cfg["vocab_size"], (15, 6)).astype(np.uint32)
+    for n in (3, 4, 8, 15):
+        outs, sts = eng.generate_batch(prompts[:n], 5)
+        assert pkg.shim.load_library().tl_device_error() == 0
+        for i in (0, n - 1):
+            ref, ref_logits, _ = oracle_generate(qm, list(prompts[i]), 5)
+            assert sts[i]["stop_reason"] == 2 and sts[i]["generated_count"] == 5
+            assert tokens_match_modulo_ties(outs[i], ref, ref_logits), (n, i, outs[i], ref)
+    eng.close()
+
+
 def test_batched_decode_full_width(pkg, gpu):
     """TinyLlama widths (hidden 2048, FFN 5632, 32/4 heads; 1 layer, vocab
     2048) at 16 sequences: the batched decode step runs its tcgen05 GEMMs and
