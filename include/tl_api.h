@@ -359,9 +359,9 @@ TL_API tl_status tl_synchronize(tl_engine* eng);
 /* Times each decode-step kernel kind in isolation with CUDA events on the
  * engine stream: [0] QKV projection, [1] attention (+RoPE), [2] O projection +
  * residual, [3] gate/up + SiLU*up, [4] down + residual, [5] LM head + argmax,
- * [6] RMSNorm+quantize rows, [7] quantize rows. For n_seqs < 4 the
+ * [6] RMSNorm+quantize rows, [7] quantize rows. For n_seqs = 1 the
  * projections are the dp4a GEMVs with the RMSNorm/quantize prologue fused
- * ([6], [7] = 0); for n_seqs >= 4 they are the tcgen05 GEMMs, launched as
+ * ([6], [7] = 0); for n_seqs >= 2 they are the tcgen05 GEMMs, launched as
  * the decode step launches them: once per row group (two concurrent groups
  * of n_seqs / 2 rows on two streams for n_seqs >= 48, each group's launches
  * back to back on its stream; the LM head once over all rows), so a time

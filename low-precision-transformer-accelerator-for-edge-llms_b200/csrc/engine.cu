@@ -190,11 +190,12 @@ struct tl_engine {
   int decode_groups = 2;
   // Batched decode steps of at least this many rows run on the tcgen05 GEMMs,
   // which stream every weight once per step whatever the row count below a
-  // 32-token tile; smaller batches (from 2 rows) take the dp4a GEMV path.
-  // Measured on B200 at context 512..1023: 8 rows 3.34 ms per step on the
-  // GEMV path, 16 rows 0.91 ms on the tensor cores. TL_DECODE_TC_MIN_ROWS=n
-  // overrides (2..16; 16 keeps every batch below 16 rows on the GEMV path).
-  int decode_tc_min_rows = 4;
+  // 32-token tile; batch 1 runs decode1_kernel (or, without it, the dp4a
+  // GEMV path). Measured on B200 at context 512..1023, per step on the GEMV
+  // path / on the tensor cores: 2 rows 1.397 / 0.941 ms, 4 rows 2.046 /
+  // 0.927 ms, 8 rows 3.34 / 0.913 ms. TL_DECODE_TC_MIN_ROWS=n overrides
+  // (2..16; 16 keeps every batch below 16 rows on the GEMV path).
+  int decode_tc_min_rows = 2;
   int D = 0, F = 0, H = 0, Hkv = 0, Dq = 0, Dkv = 0, Nqkv = 0, V = 0, L = 0, P = 0, B = 0;
   std::vector<Layer> layers;
   float *embed = nullptr, *gfinal = nullptr, *cosT = nullptr, *sinT = nullptr;
@@ -669,7 +670,7 @@ struct DebugCap {
   float* pr = nullptr;
 };
 
-// Layer l of the per-kernel decode step for rows 0..M-1 (2 <= M <
+// Layer l of the per-kernel decode step for rows 0..M-1 (M <
 // decode_tc_min_rows, batch 1 without decode1_kernel, or teacher-forced logits): dp4a GEMVs with the RMSNorm/quantize prologue and
 // the dequant / residual / SiLU*up epilogues, decode attention in between.
 tl_status enqueue_decode_layer_gemv(tl_engine* e, int l, int M, DebugCap* dbg) {

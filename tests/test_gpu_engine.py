@@ -152,10 +152,10 @@ def test_uneven_row_groups(pkg, gpu):
 
 
 def test_small_batches_on_tensor_cores(pkg, gpu):
-    """4, 8 and 15 sequences: batched decode steps of 4 or more rows run on
-    the tcgen05 GEMMs with most of each 32-token tile empty (the same kernels
-    as the large batches); the first and last sequence of each batch must
-    follow its own oracle; 3 sequences stay on the GEMV path."""
+    """3, 4, 8 and 15 sequences: batched decode steps of 2 or more rows run
+    on the tcgen05 GEMMs with most of each 32-token tile empty (the same
+    kernels as the large batches); the first and last sequence of each batch
+    must follow its own oracle."""
     qm = small_model(17, 2)
     eng = pkg.Engine(qm.cfg, max_batch=15, max_prefill_tokens=15 * 6)
     eng.load(to_engine_model(pkg, qm))
