@@ -440,9 +440,10 @@ struct RowGroup {
 };
 
 // Layer l of the batched decode step on the tensor cores (M >=
-// decode_tc_min_rows rows): per row RMSNorm + INT8 quantization kernels feed tcgen05 GEMMs whose
-// epilogues dequantize, add the residual or apply SiLU*up. The attention
-// kernel and the SiLU*up epilogue fold each row's max |output| into
+// decode_tc_min_rows rows): per row RMSNorm + INT8 quantization kernels feed
+// tcgen05 GEMMs whose epilogues dequantize, add the residual or apply
+// SiLU*up. The attention kernel and the SiLU*up epilogue fold each row's max
+// |output| into
 // d.amax_prod with atomics, so the quantization of their outputs is
 // elementwise over the whole block; each RMSNorm kernel re-arms d.amax_prod
 // (its last reader, the GEMM two kernels back, has completed by then).
@@ -671,8 +672,9 @@ struct DebugCap {
 };
 
 // Layer l of the per-kernel decode step for rows 0..M-1 (M <
-// decode_tc_min_rows, batch 1 without decode1_kernel, or teacher-forced logits): dp4a GEMVs with the RMSNorm/quantize prologue and
-// the dequant / residual / SiLU*up epilogues, decode attention in between.
+// decode_tc_min_rows, batch 1 without decode1_kernel, or teacher-forced
+// logits): dp4a GEMVs with the RMSNorm/quantize prologue and the dequant /
+// residual / SiLU*up epilogues, decode attention in between.
 tl_status enqueue_decode_layer_gemv(tl_engine* e, int l, int M, DebugCap* dbg) {
   DecodeBufs& d = e->dec;
   cudaStream_t s = e->stream;
